@@ -1,0 +1,109 @@
+#!/usr/bin/env bash
+# Builds oracle/_ref/libpb_refpins.so: the reference's OWN CPU functions for
+# this path, compiled from the reference sources where they lie. TEST
+# INFRASTRUCTURE ONLY (it pins the oracle restatement; nothing ships it).
+#
+# No reference source is copied into this repository: each function is cut
+# out of its file by line range at build time and piped straight into the
+# compiler (stdin), followed by a few exported wrappers written here.
+#
+#   pq1_host.c:14-24, 78-121    pq1_h2f, pq1_split_repack, pq1_gemv_cpu (non-ternary)
+#   fwd35_ref.c:42-43, 46-72    fbits/bitsf, f16f, ff16
+#   fwd35_ref.c:333-344         Q8 / q8(): the Q8_0 activation quantizer
+#   pq1_parity.c:13-23          mk_q8k: the parity gate's seeded Q8_K generator
+#   pq1_parity.c:119-147        rms_ser / rms_ref: RMS + Q8_K quantizer chain
+#   q8_gemv_cpu.c (whole file)  gemv_q8 / quant_row (main renamed away)
+#   lfm3_nanode.cu:4598-4603    cpu_f2bf / cpu_bf2f
+#   lfm3_nanode.cu:4658-4684    cpuchk_run's scalar leaf-order transcription
+#
+# Needs the reference checkout (default /root/reference, override with
+# PB_REFERENCE_ROOT). Without it this script does nothing and exits 0.
+set -euo pipefail
+here="$(cd "$(dirname "$0")" && pwd)"
+REF="${PB_REFERENCE_ROOT:-/root/reference}"
+out="$here/_ref"
+if [ ! -d "$REF/pulsar_arm" ]; then
+  echo "build_ref: no reference tree at $REF; skipping"; exit 0
+fi
+CC=/usr/bin/gcc; [ -x "$CC" ] || CC=gcc
+CXX=/usr/bin/g++; [ -x "$CXX" ] || CXX=g++
+mkdir -p "$out"
+B2="$REF/pulsar_arm/bonsai2"
+CFL="-O2 -fPIC -ffp-contract=off -fopenmp -w"
+
+# --- A: bonsai2 host functions (C) ------------------------------------------
+{
+  printf '#include <stdint.h>\n#include <string.h>\n#include <stdlib.h>\n#include <math.h>\n#include <stddef.h>\n'
+  sed -n '14,24p'   "$B2/pq1_host.c"
+  sed -n '78,121p'  "$B2/pq1_host.c"
+  sed -n '42,43p'   "$B2/fwd35_ref.c"
+  sed -n '46,72p'   "$B2/fwd35_ref.c"
+  sed -n '333,344p' "$B2/fwd35_ref.c"
+  sed -n '13,23p'   "$B2/pq1_parity.c"
+  sed -n '119,147p' "$B2/pq1_parity.c"
+  cat <<'EOF'
+/* ---- exported wrappers (this repository's code) ---- */
+float pbref_h2f(uint16_t h) { return pq1_h2f(h); }
+void pbref_q1_repack(const uint8_t* q1, int rows, int K, uint32_t* wb, uint16_t* sc) { pq1_split_repack(q1, rows, K, wb, sc); }
+void pbref_q1_gemv(int rows, int K, const uint32_t* wb, const uint16_t* sc, const uint8_t* xq, float* y) { pq1_gemv_cpu(rows, K, wb, sc, xq, y); }
+uint16_t pbref_ff16(float f) { return ff16(f); }
+float pbref_f16f(uint16_t h) { return f16f(h); }
+void pbref_q80_quant(const float* x, int n, int8_t* q, float* d) { Q8 o = { q, d }; q8(x, n, &o); }
+void pbref_mk_q8k(uint8_t* xq, int K, unsigned seed) { mk_q8k(xq, K, seed); }
+void pbref_rms_q8k(float* x, const float* r, const float* w, int n, uint8_t* xq) { rms_ref(x, r, w, n, xq); }
+/* the parity gate's weight generator (pq1_parity.c:750-758, restated) */
+void pbref_parity_q1_weights(uint8_t* q1, int rows, int K) {
+  const int nb = K / 128; const size_t q1b = (size_t)rows * nb * 18;
+  srand(31337);
+  for (size_t i = 0; i < q1b; i++) q1[i] = (uint8_t)(rand() & 0xFF);
+  for (int r = 0; r < rows; r++)
+    for (int b = 0; b < nb; b++) {
+      uint16_t h = (uint16_t)(0x2800 + (rand() % 0x1000));
+      memcpy(q1 + ((size_t)r * nb + b) * 18, &h, 2);
+    }
+}
+EOF
+} | "$CC" $CFL -x c -c -o "$out/pins_bonsai.o" -
+
+# --- B: the x86/C CPU Q8 GEMV, whole file, main renamed ----------------------
+{
+  printf '#define main pbref_q8_gemv_cpu_main\n#include "%s"\n#undef main\n' "$REF/.auto/lfm3/q8_gemv_cpu.c"
+  cat <<'EOF'
+void pbref_gemv_q8(const signed char* q, const float* s, const float* x, float* y, int N, int K) { gemv_q8(q, s, x, y, N, K); }
+void pbref_quant_row(const float* w, int K, signed char* q, float* s) { quant_row(w, K, q, s); }
+EOF
+} | "$CC" $CFL -x c -c -o "$out/pins_q8cpu.o" -
+
+# --- C: cpuchk_run's scalar transcription of the tiled leaf order (C++) ------
+{
+  printf '#include <cstdint>\n#include <cstring>\n#include <cmath>\n#include <vector>\n'
+  sed -n '4598,4603p' "$REF/pulsar_arm/asm/lfm3_nanode.cu"
+  cat <<'EOF'
+struct PbChk { long outs = 0, bad = 0; };
+/* codes/scales row-major [N][K], [N][K/32] fp32; x bf16 [Tn][K]; y bf16 [Tn][N]
+ * (the values under test). Tiles the last R rows the way lfm3_nanode.cu:4510-4521
+ * does, then runs the reference's own loop; returns the bitwise-differ count. */
+extern "C" long pbref_cpuchk(const int8_t* codes, const float* scales, const uint16_t* xb,
+                             const uint16_t* yb, int N, int K, int Tn, int R) {
+  const int nb = K / 32, r0 = N - R;
+  const size_t tq = (size_t)nb * 64 * 16;
+  std::vector<int8_t> hq((size_t)(R / 32) * tq);
+  std::vector<float> hs((size_t)(R / 32) * nb * 32);
+  for (int rr = 0; rr < R; rr++)
+    for (int b = 0; b < nb; b++) {
+      std::memcpy(&hq[(size_t)(rr >> 5) * tq + ((size_t)b * 64 + (rr & 31)) * 16], codes + (size_t)(r0 + rr) * K + b * 32, 16);
+      std::memcpy(&hq[(size_t)(rr >> 5) * tq + ((size_t)b * 64 + 32 + (rr & 31)) * 16], codes + (size_t)(r0 + rr) * K + b * 32 + 16, 16);
+      hs[(size_t)(rr >> 5) * nb * 32 + (size_t)b * 32 + (rr & 31)] = scales[(size_t)(r0 + rr) * nb + b];
+    }
+  std::vector<float> xf((size_t)Tn * K);
+  for (size_t i = 0; i < xf.size(); i++) xf[i] = cpu_bf2f(xb[i]);
+  std::vector<uint16_t> hy(yb, yb + (size_t)Tn * N);
+  PbChk c;
+EOF
+  sed -n '4658,4684p' "$REF/pulsar_arm/asm/lfm3_nanode.cu"
+  printf '  return c.bad;\n}\n'
+} | "$CXX" -O2 -fPIC -ffp-contract=off -w -x c++ -c -o "$out/pins_cpuchk.o" -
+
+"$CXX" -shared -fopenmp -o "$out/libpb_refpins.so" "$out/pins_bonsai.o" "$out/pins_q8cpu.o" "$out/pins_cpuchk.o" -lm
+rm -f "$out"/pins_*.o
+echo "build_ref: built $out/libpb_refpins.so"

@@ -1,0 +1,237 @@
+"""ctypes front end for the CPU oracle (oracle/_build/libpb_oracle.so) and for
+the reference-compiled pins (oracle/_ref/libpb_refpins.so).
+
+TEST INFRASTRUCTURE ONLY: tests/, __graft_entry__.smoke() and bench.py's CPU
+baseline arm import this module as the checker. The product never does.
+"""
+import ctypes as C
+import os
+import subprocess
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(HERE, "_build", "libpb_oracle.so")
+REF_PATH = os.path.join(HERE, "_ref", "libpb_refpins.so")
+
+_lib = None
+_ref = None
+
+
+def build():
+    """Compile the oracle (and, where the reference tree exists, its pins)."""
+    subprocess.check_call(["make", "-s", "-C", HERE])
+    subprocess.check_call(["bash", os.path.join(HERE, "build_ref.sh")])
+
+
+def _p(a):
+    return a.ctypes.data_as(C.c_void_p)
+
+
+class _Cfg(C.Structure):
+    _fields_ = [(n, C.c_int) for n in ("hidden", "inter", "n_layers", "n_heads", "n_kv",
+                                       "head_dim", "vocab", "conv_w", "max_ctx",
+                                       "sliding_window")] + \
+               [(n, C.c_float) for n in ("rope_theta", "rope_partial", "norm_eps")]
+
+
+def lib():
+    global _lib
+    if _lib is None:
+        if not os.path.exists(LIB_PATH):
+            subprocess.check_call(["make", "-s", "-C", HERE])
+        L = C.CDLL(LIB_PATH)
+        vp, i, f = C.c_void_p, C.c_int, C.c_float
+        L.pbo_f2bf.restype = C.c_uint16; L.pbo_f2bf.argtypes = [f]
+        L.pbo_bf2f.restype = f; L.pbo_bf2f.argtypes = [C.c_uint16]
+        L.pbo_f2h.restype = C.c_uint16; L.pbo_f2h.argtypes = [f]
+        L.pbo_h2f.restype = f; L.pbo_h2f.argtypes = [C.c_uint16]
+        L.pbo_expf.restype = f; L.pbo_expf.argtypes = [f]
+        L.pbo_q8_kchunk.restype = i; L.pbo_q8_kchunk.argtypes = [i]
+        L.pbo_q8f_gemv.argtypes = [vp, vp, i, i, vp, vp]
+        L.pbo_q8f_gemm.argtypes = [vp, vp, i, i, i, vp, vp]
+        L.pbo_q80_quant_act.argtypes = [vp, i, vp, vp]
+        L.pbo_q80_gemv.argtypes = [vp, vp, i, i, vp, vp, vp, vp]
+        L.pbo_q1_repack.argtypes = [vp, i, i, vp, vp]
+        L.pbo_q8k_quant.argtypes = [vp, i, vp]
+        L.pbo_q1_gemv.argtypes = [i, i, vp, vp, vp, vp, vp]
+        L.pbo_q1_rms_q8k.argtypes = [vp, vp, vp, i, f, vp, vp]
+        L.pbo_rmsnorm.argtypes = [vp, vp, vp, i, f]
+        L.pbo_headnorm.argtypes = [vp, vp, i, i, f]
+        L.pbo_rope_invf.argtypes = [vp, f, i, f]
+        L.pbo_rope_cs.argtypes = [vp, i, i, vp, vp]
+        L.pbo_rope.argtypes = [vp, i, i, i, vp, vp]
+        L.pbo_attn_head.argtypes = [vp, vp, vp, i, i, i, i, i, f, C.c_uint16, i, vp]
+        L.pbo_argmax.restype = i; L.pbo_argmax.argtypes = [vp, i]
+        L.pbo_model_new.restype = vp; L.pbo_model_new.argtypes = [C.POINTER(_Cfg), vp]
+        L.pbo_model_free.argtypes = [vp]
+        L.pbo_model_set_q8.argtypes = [vp, i, i, vp, vp, i, i]
+        L.pbo_model_set_f32.argtypes = [vp, i, i, vp]
+        L.pbo_state_new.restype = vp; L.pbo_state_new.argtypes = [vp]
+        L.pbo_state_free.argtypes = [vp]
+        L.pbo_decode.restype = i; L.pbo_decode.argtypes = [vp, vp, i, i, vp, vp]
+        L.pbo_state_kv.restype = vp; L.pbo_state_kv.argtypes = [vp, i, i]
+        L.pbo_state_ring.restype = vp; L.pbo_state_ring.argtypes = [vp, i]
+        L.pbo_threads.restype = i
+        _lib = L
+    return _lib
+
+
+def ref():
+    """The reference's own functions, or None when they were not built here."""
+    global _ref
+    if _ref is None and os.path.exists(REF_PATH):
+        R = C.CDLL(REF_PATH)
+        vp, i = C.c_void_p, C.c_int
+        R.pbref_h2f.restype = C.c_float; R.pbref_h2f.argtypes = [C.c_uint16]
+        R.pbref_ff16.restype = C.c_uint16; R.pbref_ff16.argtypes = [C.c_float]
+        R.pbref_f16f.restype = C.c_float; R.pbref_f16f.argtypes = [C.c_uint16]
+        R.pbref_q1_repack.argtypes = [vp, i, i, vp, vp]
+        R.pbref_q1_gemv.argtypes = [i, i, vp, vp, vp, vp]
+        R.pbref_q80_quant.argtypes = [vp, i, vp, vp]
+        R.pbref_mk_q8k.argtypes = [vp, i, C.c_uint]
+        R.pbref_rms_q8k.argtypes = [vp, vp, vp, i, vp]
+        R.pbref_parity_q1_weights.argtypes = [vp, i, i]
+        R.pbref_gemv_q8.argtypes = [vp, vp, vp, vp, i, i]
+        R.pbref_quant_row.argtypes = [vp, i, vp, vp]
+        R.pbref_cpuchk.restype = C.c_long
+        R.pbref_cpuchk.argtypes = [vp, vp, vp, vp, i, i, i, i]
+        _ref = R
+    return _ref
+
+
+# ---------------------------------------------------------------- helpers ---
+def f2bf(a):
+    """vectorised lfm3_nanode.cu:116-121 (numpy; matches pbo_f2bf bit for bit)."""
+    u = np.ascontiguousarray(a, dtype=np.float32).view(np.uint32)
+    special = ((u >> 23) & 0xFF) == 0xFF
+    r = ((u + np.uint32(0x7FFF) + ((u >> 16) & 1)) >> 16).astype(np.uint16)
+    return np.where(special, (u >> 16).astype(np.uint16), r)
+
+
+def bf2f(h):
+    return (np.asarray(h, dtype=np.uint16).astype(np.uint32) << 16).view(np.float32)
+
+
+def q8f_gemv(codes, scales_f32, x_bf16):
+    N, K = codes.shape
+    T = 1 if x_bf16.ndim == 1 else x_bf16.shape[0]
+    y = np.zeros((T, N), np.float32)
+    lib().pbo_q8f_gemm(_p(codes), _p(scales_f32), N, K, T, _p(np.ascontiguousarray(x_bf16)), _p(y))
+    return y[0] if x_bf16.ndim == 1 else y
+
+
+def q80_quant_act(x):
+    K = x.shape[0]
+    qx = np.zeros(K, np.int8); dx = np.zeros(K // 32, np.uint16)
+    lib().pbo_q80_quant_act(_p(np.ascontiguousarray(x, np.float32)), K, _p(qx), _p(dx))
+    return qx, dx
+
+
+def q80_gemv(codes, dw_h, qx, dx_h):
+    N, K = codes.shape
+    isum = np.zeros((N, K // 32), np.int32); y = np.zeros(N, np.float32)
+    lib().pbo_q80_gemv(_p(codes), _p(dw_h), N, K, _p(qx), _p(dx_h), _p(isum), _p(y))
+    return isum, y
+
+
+def q1_repack(q1, rows, K):
+    wb = np.zeros((rows, K // 32), np.uint32); sc = np.zeros((rows, K // 128), np.uint16)
+    lib().pbo_q1_repack(_p(q1), rows, K, _p(wb), _p(sc))
+    return wb, sc
+
+
+def q8k_quant(x):
+    K = x.shape[0]
+    xq = np.zeros((K // 256) * 292, np.uint8)
+    lib().pbo_q8k_quant(_p(np.ascontiguousarray(x, np.float32)), K, _p(xq))
+    return xq
+
+
+def q1_rms_q8k(x, w, r=None, eps=1e-6):
+    x = np.array(x, np.float32)
+    n = x.shape[0]
+    y = np.zeros(n, np.float32); xq = np.zeros((n // 256) * 292, np.uint8)
+    lib().pbo_q1_rms_q8k(_p(x), _p(np.ascontiguousarray(r, np.float32)) if r is not None else None,
+                         _p(np.ascontiguousarray(w, np.float32)), n, eps, _p(y), _p(xq))
+    return x, y, xq
+
+
+def q1_gemv(wb, sc, xq, K):
+    rows = wb.shape[0]
+    isum = np.zeros((rows, K // 128), np.int32); y = np.zeros(rows, np.float32)
+    lib().pbo_q1_gemv(rows, K, _p(wb), _p(sc), _p(xq), _p(isum), _p(y))
+    return isum, y
+
+
+def h2f_all():
+    return np.array([lib().pbo_h2f(h) for h in range(65536)], np.float32)
+
+
+class Model:
+    """Oracle decode over numpy weights held by `weights` (a dict shaped like
+    pulsar_b200.synth.make_weights)."""
+
+    SLOTS_Q8 = {"q": 0, "k": 1, "v": 2, "gate": 3, "o": 4, "in_proj": 5, "out_proj": 6,
+                "w1": 7, "w3": 8, "w2": 9}
+    SLOTS_F = {"op_norm": 0, "post_op_norm": 1, "ffn_norm": 2, "post_ffn_norm": 3,
+               "q_norm": 4, "k_norm": 5, "taps": 6}
+
+    def __init__(self, cfg, weights):
+        L = lib()
+        self.cfg = cfg
+        self._keep = []
+        c = _Cfg(cfg["hidden"], cfg["inter"], cfg["n_layers"], cfg["n_heads"], cfg["n_kv"],
+                 cfg["head_dim"], cfg["vocab"], cfg["conv_w"], cfg["max_ctx"],
+                 cfg.get("sliding_window", 0), cfg["rope_theta"], cfg["rope_partial"],
+                 cfg["norm_eps"])
+        isa = np.array([1 if t != "conv" else 0 for t in cfg["layer_types"]], np.int32)
+        self._keep.append(isa)
+        self.m = L.pbo_model_new(C.byref(c), _p(isa))
+        for li, lw in enumerate(weights["layers"]):
+            for name, slot in self.SLOTS_Q8.items():
+                if name in lw:
+                    codes, sc16 = lw[name]
+                    s32 = np.ascontiguousarray(h2f_vec(sc16))
+                    self._keep += [codes, s32]
+                    L.pbo_model_set_q8(self.m, li, slot, _p(codes), _p(s32), codes.shape[0], codes.shape[1])
+            for name, slot in self.SLOTS_F.items():
+                if name in lw:
+                    a = np.ascontiguousarray(lw[name], np.float32)
+                    self._keep.append(a)
+                    L.pbo_model_set_f32(self.m, li, slot, _p(a))
+        codes, sc16 = weights["embed"]
+        s32 = np.ascontiguousarray(h2f_vec(sc16))
+        self._keep += [codes, s32]
+        L.pbo_model_set_q8(self.m, -1, 0, _p(codes), _p(s32), codes.shape[0], codes.shape[1])
+        fn = np.ascontiguousarray(weights["final_norm"], np.float32)
+        self._keep.append(fn)
+        L.pbo_model_set_f32(self.m, -1, 0, _p(fn))
+        self.s = L.pbo_state_new(self.m)
+
+    def reset(self):
+        lib().pbo_state_free(self.s)
+        self.s = lib().pbo_state_new(self.m)
+
+    def decode(self, token, pos, want_logits=False):
+        lg = np.zeros(self.cfg["vocab"], np.float32) if want_logits else None
+        x = np.zeros(self.cfg["hidden"], np.uint16)
+        tid = lib().pbo_decode(self.m, self.s, int(token), int(pos), _p(lg) if lg is not None else None, _p(x))
+        return tid, lg, x
+
+    def kv(self, layer, which, n):
+        c = self.cfg
+        ptr = lib().pbo_state_kv(self.s, layer, which)
+        return np.ctypeslib.as_array(C.cast(ptr, C.POINTER(C.c_uint16)), shape=(n * c["n_kv"] * c["head_dim"],)).copy()
+
+    def __del__(self):
+        try:
+            lib().pbo_state_free(self.s)
+            lib().pbo_model_free(self.m)
+        except Exception:
+            pass
+
+
+def h2f_vec(h):
+    """exact fp16 -> fp32 widening (numpy's float16 conversion is exact)."""
+    return np.asarray(h, np.uint16).view(np.float16).astype(np.float32)

@@ -1,0 +1,565 @@
+/* pb_oracle.c -- CPU restatement of PULSAR-ASM's quantized weight-streaming
+ * hot path. TEST INFRASTRUCTURE, NOT PRODUCT: see pb_oracle.h.
+ *
+ * Reference files (paths relative to the PULSAR-ASM project root):
+ *   LFM3 engine      pulsar_arm/asm/lfm3_nanode.cu
+ *   Q8_0 activation  pulsar_arm/bonsai2/fwd35_ref.c
+ *   Q1_0 host ref    pulsar_arm/bonsai2/pq1_host.c
+ *   Q8_K quantizer   pulsar_arm/bonsai2/fwd8.c, pulsar_arm/bonsai2/pq1_parity.c
+ *
+ * Deterministic replacements for device intrinsics (the CUDA product uses the
+ * same ones, so results agree bit for bit):
+ *   rsqrtf(v)        -> 1.0f / sqrtf(v), both correctly rounded (the reference's
+ *                       MUFU rsqrtf is an approximation with no CPU twin)
+ *   expf(x)          -> pbo_expf: Cody-Waite reduction x = n*ln2 + r with a
+ *                       two-constant ln2 split, e^r by its degree-7 Taylor
+ *                       polynomial in Horner form with fused multiply-adds,
+ *                       then an exact scale by 2^n. Max error about 1 ulp.
+ *   cosf/sinf(ang)   -> (float)cos((double)ang), (float)sin((double)ang),
+ *                       evaluated on the host; the product precomputes the
+ *                       same table on the host and uploads it.
+ *   argmax ties      -> the lowest index wins.
+ */
+#include "pb_oracle.h"
+#include <math.h>
+#include <string.h>
+#include <stdlib.h>
+#ifdef _OPENMP
+#include <omp.h>
+#endif
+
+static inline uint32_t fbits(float f) { uint32_t u; memcpy(&u, &f, 4); return u; }
+static inline float bitsf(uint32_t u) { float f; memcpy(&f, &u, 4); return f; }
+
+int pbo_threads(void) {
+#ifdef _OPENMP
+  return omp_get_max_threads();
+#else
+  return 1;
+#endif
+}
+
+/* ------------------------------------------------------------ scalars ---- */
+/* lfm3_nanode.cu:116-121: round to nearest even, inf/nan keep their top bits. */
+uint16_t pbo_f2bf(float v) {
+  const uint32_t u = fbits(v);
+  if (((u >> 23) & 0xffu) == 0xffu) return (uint16_t)(u >> 16);
+  return (uint16_t)((u + 0x7fffu + ((u >> 16) & 1u)) >> 16);
+}
+float pbo_bf2f(uint16_t h) { return bitsf((uint32_t)h << 16); }
+
+/* IEEE binary16, round to nearest even (the rounding pq1_host.c:386-391 and
+ * fwd35_ref.c:55-70 perform). */
+uint16_t pbo_f2h(float v) {
+  const uint32_t u = fbits(v);
+  const uint16_t sign = (uint16_t)((u >> 16) & 0x8000u);
+  const uint32_t a = u & 0x7fffffffu;
+  if (a >= 0x7f800000u) return sign | (a > 0x7f800000u ? 0x7e00u : 0x7c00u);
+  if (a >= 0x477ff000u) return sign | 0x7c00u;            /* >= 65520 -> inf */
+  if (a < 0x38800000u) {                                  /* half subnormal or 0 */
+    const float r = rintf(bitsf(a) * 16777216.0f);        /* exact scale by 2^24 */
+    return sign | (uint16_t)r;                            /* 1024 -> min normal */
+  }
+  const uint32_t m = a + 0xfffu + ((a >> 13) & 1u) - (112u << 23);
+  return sign | (uint16_t)(m >> 13);
+}
+/* exact widening, pq1_host.c:14-24 */
+float pbo_h2f(uint16_t h) {
+  const uint32_t s = (uint32_t)(h & 0x8000u) << 16, e = (h >> 10) & 0x1fu, m = h & 0x3ffu;
+  if (e == 0) { const float f = (float)m * 5.9604644775390625e-8f; return s ? -f : f; }
+  if (e == 31) return bitsf(s | 0x7f800000u | (m << 13));
+  return bitsf(s | ((e + 112u) << 23) | (m << 13));
+}
+
+/* e^x: x = n*ln2 + r, |r| <= ln2/2 (Cody & Waite, "Software Manual for the
+ * Elementary Functions", 1980: argument reduction with ln2 split into a short
+ * high part and a low correction); e^r from its Taylor series to r^7 (the
+ * truncation error r^8/8! < 6e-9 relative); 2^n applied by exponent
+ * arithmetic in at most two exact-or-once-rounded multiplies. */
+float pbo_expf(float x) {
+  if (x != x) return x;
+  if (x > 88.72283935546875f) return INFINITY;
+  if (x < -103.97207708399179f) return 0.0f;
+  const float n = rintf(x * 1.44269502162933349609375f);
+  float r = fmaf(n, -0.693145751953125f, x);
+  r = fmaf(n, -1.428606765330187e-06f, r);
+  float p = 1.98412701138295233249664306640625e-4f;       /* 1/7! */
+  p = fmaf(p, r, 1.38888892251998186111450195312500e-3f);  /* 1/6! */
+  p = fmaf(p, r, 8.33333376795053482055664062500000e-3f);  /* 1/5! */
+  p = fmaf(p, r, 4.16666679084300994873046875000000e-2f);  /* 1/4! */
+  p = fmaf(p, r, 1.66666671633720397949218750000000e-1f);  /* 1/3! */
+  p = fmaf(p, r, 0.5f);
+  p = fmaf(p, r, 1.0f);
+  p = fmaf(p, r, 1.0f);
+  int k = (int)n;
+  if (k > 127) { p = p * 2.0f; k -= 1; }
+  if (k < -126) { p = p * bitsf((uint32_t)(k + 64 + 127) << 23); return p * 5.42101086242752217003726400434970855712890625e-20f; }
+  return p * bitsf((uint32_t)(k + 127) << 23);
+}
+
+static float pairwise(float* s, int E) {   /* ((s0+s1)+(s2+s3))+... levels */
+  for (int w = E; w > 1; w >>= 1)
+    for (int i = 0; i < w / 2; i++) s[i] = s[2 * i] + s[2 * i + 1];
+  return s[0];
+}
+static float tree_down(float* v, int n) {  /* __shfl_down_sync tree over n lanes */
+  for (int o = n / 2; o > 0; o >>= 1)
+    for (int l = 0; l < o; l++) v[l] = v[l] + v[l + o];
+  return v[0];
+}
+
+/* -------------------------------------------------------- Q8 float path -- */
+/* pick(): lfm3_nanode.cu:1763-1768 (KCHUNK 2048 when it divides K, 512 for
+ * K == 512, else the whole row). The chunk count fixes the combine order. */
+int pbo_q8_kchunk(int K) {
+  if (K >= 2048 && K % 2048 == 0) return 2048;
+  if (K == 512) return 512;
+  return K;
+}
+
+/* One (row, chunk): lane l chains blocks b = l, l+32, ... with
+ * dot_b = fma(code_j, x_j, dot) over j ascending and acc = fma(s_b, dot_b, acc)
+ * (q8_partial<bf16,FMA=true>, lfm3_nanode.cu:270-323), then the shuffle-down
+ * tree 16..1 (:326-327). Identical to q8_partial_TLb's 5-bit bit-reversed
+ * binary-counter combine (:4045-4123) and to cpuchk_run (:4658-4684). */
+static float q8f_chunk(const int8_t* qr, const float* sr, const float* x, int nbc) {
+  float v[32];
+  for (int l = 0; l < 32; l++) {
+    float acc = 0.0f;
+    for (int b = l; b < nbc; b += 32) {
+      const int8_t* c = qr + (size_t)b * 32;
+      const float* xb = x + (size_t)b * 32;
+      float dot = 0.0f;
+      for (int j = 0; j < 32; j++) dot = fmaf((float)c[j], xb[j], dot);
+      acc = fmaf(sr[b], dot, acc);
+    }
+    v[l] = acc;
+  }
+  return tree_down(v, 32);
+}
+
+/* chunk partials summed ascending from 0 (k_combine_bf / k_combine_f,
+ * lfm3_nanode.cu:336-374); the caller rounds to bf16 where the reference does. */
+void pbo_q8f_gemm(const int8_t* codes, const float* scales, int N, int K, int T,
+                  const uint16_t* x_bf16, float* y) {
+  const int KC = pbo_q8_kchunk(K), nch = K / KC, nbc = KC / 32, nb = K / 32;
+  float* xf = (float*)malloc((size_t)T * K * sizeof(float));
+  for (size_t i = 0; i < (size_t)T * K; i++) xf[i] = pbo_bf2f(x_bf16[i]);
+#pragma omp parallel for schedule(static)
+  for (int n = 0; n < N; n++) {
+    const int8_t* qr = codes + (size_t)n * K;
+    const float* sr = scales + (size_t)n * nb;
+    for (int t = 0; t < T; t++) {
+      float acc = 0.0f;
+      for (int c = 0; c < nch; c++)
+        acc = acc + q8f_chunk(qr + (size_t)c * KC, sr + (size_t)c * nbc,
+                              xf + (size_t)t * K + (size_t)c * KC, nbc);
+      y[(size_t)t * N + n] = acc;
+    }
+  }
+  free(xf);
+}
+void pbo_q8f_gemv(const int8_t* codes, const float* scales, int N, int K,
+                  const uint16_t* x_bf16, float* y) {
+  pbo_q8f_gemm(codes, scales, N, K, 1, x_bf16, y);
+}
+
+/* ----------------------------------------------------- Q8_0 integer path -- */
+/* fwd35_ref.c:332-343 (the AVX quantize_row_q8_0 form): d = amax/127 stored
+ * as fp16; q = rint(x * 127/amax), 0 when amax == 0. */
+void pbo_q80_quant_act(const float* x, int K, int8_t* qx, uint16_t* dx_h) {
+  for (int b = 0; b < K / 32; b++) {
+    float amax = 0.0f;
+    for (int j = 0; j < 32; j++) amax = fmaxf(amax, fabsf(x[32 * b + j]));
+    const float d = amax / 127.0f;
+    dx_h[b] = pbo_f2h(d);
+    const float id = amax != 0.0f ? 127.0f / amax : 0.0f;
+    for (int j = 0; j < 32; j++) qx[32 * b + j] = (int8_t)rintf(x[32 * b + j] * id);
+  }
+}
+/* exact int32 block dot, then the fold acc += (dw*dx)*(float)isum in block
+ * order with no contraction (pattern of pq1_host.c:112-116 and ggml's generic
+ * Q8_0 x Q8_0 dot). */
+void pbo_q80_gemv(const int8_t* codes, const uint16_t* dw_h, int N, int K,
+                  const int8_t* qx, const uint16_t* dx_h, int32_t* isum, float* y) {
+  const int nb = K / 32;
+#pragma omp parallel for schedule(static)
+  for (int n = 0; n < N; n++) {
+    float acc = 0.0f;
+    for (int b = 0; b < nb; b++) {
+      const int8_t* c = codes + (size_t)n * K + (size_t)b * 32;
+      int32_t s = 0;
+      for (int j = 0; j < 32; j++) s += (int32_t)c[j] * (int32_t)qx[32 * b + j];
+      if (isum) isum[(size_t)n * nb + b] = s;
+      acc = acc + (pbo_h2f(dw_h[(size_t)n * nb + b]) * pbo_h2f(dx_h[b])) * (float)s;
+    }
+    y[n] = acc;
+  }
+}
+
+/* ---------------------------------------------------------- Q1_0 x Q8_K -- */
+/* pq1_host.c:77-97 (non-ternary build): 18-byte blocks -> 16 sign bytes per
+ * 128 weights (LSB-first, bit 1 = +1) and the fp16 scale verbatim. */
+void pbo_q1_repack(const uint8_t* q1, int rows, int K, uint32_t* w_bits, uint16_t* w_scales) {
+  const int nb = K / 128;
+  for (int r = 0; r < rows; r++) {
+    const uint8_t* row = q1 + (size_t)r * nb * 18;
+    for (int b = 0; b < nb; b++) {
+      memcpy(w_bits + (size_t)r * (K / 32) + b * 4, row + b * 18 + 2, 16);
+      memcpy(w_scales + (size_t)r * nb + b, row + b * 18, 2);
+    }
+  }
+}
+/* Q8_K quantizer: fwd8.c:67-139 as pq1_parity.c:131-148 states it in scalar
+ * form (the NEON multiply-add is contracted to one fma by GCC there): amax and
+ * the value `mx` at the first index reaching it; iscale = -127/mx;
+ * q = min(127, nearest_int(fma(x, iscale, 1.5*2^23))); d = 1/iscale; int16
+ * bsums of 16-value groups. An all-zero block is all zero bytes. */
+void pbo_q8k_quant(const float* x, int K, uint8_t* xq) {
+  for (int b = 0; b < K / 256; b++) {
+    const float* xb = x + (size_t)b * 256;
+    uint8_t* qb = xq + (size_t)b * 292;
+    float amax = 0.0f, mx = 0.0f;
+    for (int j = 0; j < 256; j++)
+      if (fabsf(xb[j]) > amax) { amax = fabsf(xb[j]); mx = xb[j]; }
+    if (!amax) { memset(qb, 0, 292); continue; }
+    const float iscale = -127.f / mx;
+    int8_t* qs = (int8_t*)(qb + 4);
+    for (int j = 0; j < 256; j++) {
+      const float v = fmaf(xb[j], iscale, 12582912.f);
+      int32_t q = (int32_t)(fbits(v) & 0x007fffffu) - 0x00400000;
+      qs[j] = (int8_t)(q < 127 ? q : 127);
+    }
+    for (int g = 0; g < 16; g++) {
+      int s = 0;
+      for (int j = 0; j < 16; j++) s += qs[16 * g + j];
+      const int16_t s16 = (int16_t)s;
+      memcpy(qb + 260 + 2 * g, &s16, 2);
+    }
+    const float d = 1.0f / iscale;
+    memcpy(qb, &d, 4);
+  }
+}
+/* pq1_host.c:14-24 widens -0 to +0 (the only difference from pbo_h2f). */
+static float q1_h2f(uint16_t h) { return (h == 0x8000u) ? 0.0f : pbo_h2f(h); }
+/* RMS + Q8_K chain of the Q1 engine: fwd8.c:312-317 / pq1_parity.c:124-147:
+ * x += r (optional); s = serial double fma sum of squares; sc = 1/sqrtf(float(s/n)
+ * + eps); y = (x*sc)*w; then the Q8_K quantizer above. */
+void pbo_q1_rms_q8k(float* x, const float* r, const float* w, int n, float eps, float* y,
+                    uint8_t* xq) {
+  if (r) for (int i = 0; i < n; i++) x[i] = x[i] + r[i];
+  double s = 0;
+  for (int i = 0; i < n; i++) s = fma((double)x[i], (double)x[i], s);
+  const float sc = 1.0f / sqrtf((float)(s / n) + eps);
+  for (int i = 0; i < n; i++) y[i] = (x[i] * sc) * w[i];
+  if (xq) pbo_q8k_quant(y, n, xq);
+}
+/* pq1_host.c:99-120: isum = sum(bit ? +q : -q) exact; acc += (ws*db)*(float)isum
+ * in group order, no contraction. */
+void pbo_q1_gemv(int rows, int K, const uint32_t* w_bits, const uint16_t* w_scales,
+                 const uint8_t* xq, int32_t* isum, float* y) {
+  const int nb = K / 128;
+#pragma omp parallel for schedule(static)
+  for (int r = 0; r < rows; r++) {
+    const uint32_t* wb = w_bits + (size_t)r * (K / 32);
+    float acc = 0.0f;
+    for (int b = 0; b < nb; b++) {
+      const uint8_t* qb = xq + (size_t)(b >> 1) * 292;
+      float db; memcpy(&db, qb, 4);
+      const int8_t* qs = (const int8_t*)(qb + 4 + (b & 1) * 128);
+      const float ws = q1_h2f(w_scales[(size_t)r * nb + b]);
+      const uint32_t* w4 = wb + b * 4;
+      int32_t s = 0;
+      for (int i = 0; i < 128; i++) s += (((w4[i >> 5] >> (i & 31)) & 1u) ? 1 : -1) * (int32_t)qs[i];
+      if (isum) isum[(size_t)r * nb + b] = s;
+      acc = acc + (ws * db) * (float)s;
+    }
+    y[r] = acc;
+  }
+}
+
+/* ---------------------------------------------------------- layer math --- */
+/* rmsnorm_body, lfm3_nanode.cu:383-440, 256 threads with H/256 consecutive
+ * elements each: squares summed pairwise, warp shuffle-down tree, 8 warp
+ * partials ascending; y = bf16(w * bf16(x*rs)). */
+void pbo_rmsnorm(const uint16_t* x, const float* w, uint16_t* y, int H, float eps) {
+  const int E = H / 256;
+  float part[256], ss[64], wsum[8];
+  for (int t = 0; t < 256; t++) {
+    for (int j = 0; j < E; j++) { const float v = pbo_bf2f(x[t * E + j]); ss[j] = v * v; }
+    part[t] = pairwise(ss, E);
+  }
+  for (int wi = 0; wi < 8; wi++) wsum[wi] = tree_down(part + 32 * wi, 32);
+  float tot = wsum[0];
+  for (int i = 1; i < 8; i++) tot = tot + wsum[i];
+  const float rs = 1.0f / sqrtf(tot * (1.0f / (float)H) + eps);
+  for (int i = 0; i < H; i++) {
+    const float r = pbo_bf2f(pbo_f2bf(pbo_bf2f(x[i]) * rs));
+    y[i] = pbo_f2bf(w[i] * r);
+  }
+}
+/* k_headnorm, lfm3_nanode.cu:460-479: 32 lanes x hd/32 dims, pairwise then
+ * "+ 0", shuffle-down tree, same rounding as rmsnorm. In place. */
+void pbo_headnorm(uint16_t* x, const float* w, int nheads, int hd, float eps) {
+  const int E = hd / 32;
+  for (int h = 0; h < nheads; h++) {
+    uint16_t* xr = x + (size_t)h * hd;
+    float v32[32], ss[8];
+    for (int l = 0; l < 32; l++) {
+      for (int j = 0; j < E; j++) { const float v = pbo_bf2f(xr[l * E + j]); ss[j] = v * v; }
+      v32[l] = pairwise(ss, E) + 0.0f;
+    }
+    const float s = tree_down(v32, 32);
+    const float rs = 1.0f / sqrtf(s * (1.0f / (float)hd) + eps);
+    for (int i = 0; i < hd; i++) {
+      const float r = pbo_bf2f(pbo_f2bf(pbo_bf2f(xr[i]) * rs));
+      xr[i] = pbo_f2bf(w[i] * r);
+    }
+  }
+}
+/* build_invf, lfm3_nanode.cu:3719-3723: the first (int)(partial*hd)/2
+ * frequencies follow the full head_dim progression, the rest are 0. */
+void pbo_rope_invf(float* invf, float base, int hd, float partial) {
+  const int angles = (int)((double)partial * hd) / 2;
+  for (int i = 0; i < hd / 2; i++)
+    invf[i] = (i < angles) ? 1.0f / powf(base, (float)(2 * i) / (float)hd) : 0.0f;
+}
+void pbo_rope_cs(const float* invf, int pos, int half, float* c, float* s) {
+  for (int i = 0; i < half; i++) {
+    const float ang = (float)pos * invf[i];
+    c[i] = (float)cos((double)ang);
+    s[i] = (float)sin((double)ang);
+  }
+}
+/* k_rope, lfm3_nanode.cu:483-498: NeoX rotate-half on (i, i+hd/2) for
+ * i < half, fp32 products, one bf16 round per output. */
+void pbo_rope(uint16_t* x, int nheads, int hd, int half, const float* c, const float* s) {
+  for (int h = 0; h < nheads; h++) {
+    uint16_t* xr = x + (size_t)h * hd;
+    for (int i = 0; i < half; i++) {
+      const float lo = pbo_bf2f(xr[i]), hi = pbo_bf2f(xr[i + hd / 2]);
+      xr[i] = pbo_f2bf(lo * c[i] + (-hi) * s[i]);
+      xr[i + hd / 2] = pbo_f2bf(hi * c[i] + lo * s[i]);
+    }
+  }
+}
+
+/* k_attn_head, lfm3_nanode.cu:503-602, over an fp16 cache [ctx][nkv][hd]:
+ *  score(p) = (32-lane shuffle-down tree of per-lane chains over hd/32 dims,
+ *             ((0 + q0k0) + q1k1) + ...) * scaling
+ *  max over the window (order free); e = expf(s - m);
+ *  sum = per-thread strided chains (i = tid, tid+256, ...), warp trees, then
+ *        the 8-lane shuffle-down tree ((w0+w4)+(w2+w6))+((w1+w5)+(w3+w7));
+ *  out_d = pairwise tree over 8 segment chains (p = seg, seg+8, ...) of
+ *          (e_p * (1/sum)) * v_p,d, rounded to bf16;
+ *  optional sigmoid gate (k_sigmoid_gate, :852-864): bf16(out * 1/(1+e^-g)). */
+void pbo_attn_head(const uint16_t* q, const uint16_t* kc, const uint16_t* vc, int kvh,
+                   int nkv, int hd, int npos, int win, float scaling, uint16_t gate,
+                   int use_gate, uint16_t* out) {
+  const int E = hd / 32;
+  const int lo = (win > 0 && npos > win) ? npos - win : 0;
+  const int np = npos - lo;
+  float* sl = (float*)malloc((size_t)np * sizeof(float));
+  float qf[256];
+  for (int i = 0; i < hd; i++) qf[i] = pbo_bf2f(q[i]);
+  for (int p = 0; p < np; p++) {
+    const uint16_t* kr = kc + ((size_t)(lo + p) * nkv + kvh) * hd;
+    float v32[32];
+    for (int l = 0; l < 32; l++) {
+      float s = 0.0f;
+      for (int j = 0; j < E; j++) s = s + qf[l * E + j] * pbo_h2f(kr[l * E + j]);
+      v32[l] = s;
+    }
+    sl[p] = tree_down(v32, 32) * scaling;
+  }
+  float m = -1e30f;
+  for (int p = 0; p < np; p++) m = fmaxf(m, sl[p]);
+  float th[256];
+  for (int t = 0; t < 256; t++) th[t] = 0.0f;
+  for (int i = 0; i < np; i++) { sl[i] = pbo_expf(sl[i] + (-m)); th[i & 255] = th[i & 255] + sl[i]; }
+  float wsum[8];
+  for (int w = 0; w < 8; w++) wsum[w] = tree_down(th + 32 * w, 32);
+  const float inv = 1.0f / tree_down(wsum, 8);
+  float sig = 0.0f;
+  if (use_gate) sig = 1.0f / (1.0f + pbo_expf(-pbo_bf2f(gate)));
+  for (int d = 0; d < hd; d++) {
+    float seg[8];
+    for (int sg = 0; sg < 8; sg++) {
+      float acc = 0.0f;
+      for (int p = sg; p < np; p += 8) {
+        const float w = sl[p] * inv;
+        acc = acc + w * pbo_h2f(vc[((size_t)(lo + p) * nkv + kvh) * hd + d]);
+      }
+      seg[sg] = acc;
+    }
+    uint16_t o = pbo_f2bf(pairwise(seg, 8));
+    if (use_gate) o = pbo_f2bf(pbo_bf2f(o) * sig);
+    out[d] = o;
+  }
+  free(sl);
+}
+
+/* greedy argmax; ties go to the lowest index (the reference's k_argmax,
+ * lfm3_nanode.cu:942-964, resolves ties by its reduction tree instead). */
+int pbo_argmax(const float* v, int n) {
+  int bi = 0;
+  for (int i = 1; i < n; i++) if (v[i] > v[bi]) bi = i;
+  return bi;
+}
+
+/* ------------------------------------------------------- decode step ---- */
+typedef struct { const int8_t* c; const float* s; int N, K; } q8t;
+struct pbo_model {
+  pbo_cfg cfg;
+  int* is_attn;
+  q8t (*q)[PBO_NQ8];
+  const float* (*f)[PBO_NF32];
+  q8t emb;
+  const float* final_norm;
+  float* invf;
+};
+struct pbo_state {
+  int n_layers;
+  uint16_t** kc; uint16_t** vc; uint16_t** ring;
+  uint16_t* x;
+};
+
+pbo_model* pbo_model_new(const pbo_cfg* cfg, const int* layer_is_attn) {
+  pbo_model* m = (pbo_model*)calloc(1, sizeof *m);
+  m->cfg = *cfg;
+  m->is_attn = (int*)malloc(sizeof(int) * cfg->n_layers);
+  memcpy(m->is_attn, layer_is_attn, sizeof(int) * cfg->n_layers);
+  m->q = calloc((size_t)cfg->n_layers, sizeof *m->q);
+  m->f = calloc((size_t)cfg->n_layers, sizeof *m->f);
+  m->invf = (float*)malloc(sizeof(float) * cfg->head_dim / 2);
+  pbo_rope_invf(m->invf, cfg->rope_theta, cfg->head_dim, cfg->rope_partial);
+  return m;
+}
+void pbo_model_free(pbo_model* m) {
+  if (!m) return;
+  free(m->is_attn); free(m->q); free(m->f); free(m->invf); free(m);
+}
+void pbo_model_set_q8(pbo_model* m, int layer, int slot, const int8_t* codes,
+                      const float* scales, int N, int K) {
+  q8t t = {codes, scales, N, K};
+  if (layer < 0) m->emb = t; else m->q[layer][slot] = t;
+}
+void pbo_model_set_f32(pbo_model* m, int layer, int slot, const float* p) {
+  if (layer < 0) m->final_norm = p; else m->f[layer][slot] = p;
+}
+pbo_state* pbo_state_new(const pbo_model* m) {
+  const pbo_cfg* c = &m->cfg;
+  pbo_state* s = (pbo_state*)calloc(1, sizeof *s);
+  s->n_layers = c->n_layers;
+  s->kc = calloc((size_t)c->n_layers, sizeof(uint16_t*));
+  s->vc = calloc((size_t)c->n_layers, sizeof(uint16_t*));
+  s->ring = calloc((size_t)c->n_layers, sizeof(uint16_t*));
+  for (int L = 0; L < c->n_layers; L++) {
+    if (m->is_attn[L]) {
+      const size_t n = (size_t)c->max_ctx * c->n_kv * c->head_dim;
+      s->kc[L] = calloc(n, 2); s->vc[L] = calloc(n, 2);
+    } else {
+      s->ring[L] = calloc((size_t)c->conv_w * c->hidden, 2);
+    }
+  }
+  s->x = calloc((size_t)c->hidden, 2);
+  return s;
+}
+void pbo_state_free(pbo_state* s) {
+  if (!s) return;
+  for (int L = 0; L < s->n_layers; L++) { free(s->kc[L]); free(s->vc[L]); free(s->ring[L]); }
+  free(s->x);
+  free(s->kc); free(s->vc); free(s->ring);
+  free(s);
+}
+const uint16_t* pbo_state_kv(const pbo_state* s, int layer, int which) {
+  return which ? s->vc[layer] : s->kc[layer];
+}
+const uint16_t* pbo_state_ring(const pbo_state* s, int layer) { return s->ring[layer]; }
+
+static void gemv_bf(const q8t* t, const uint16_t* x, uint16_t* y) {
+  float* yf = (float*)malloc(sizeof(float) * t->N);
+  pbo_q8f_gemv(t->c, t->s, t->N, t->K, x, yf);
+  for (int i = 0; i < t->N; i++) y[i] = pbo_f2bf(yf[i]);
+  free(yf);
+}
+
+/* layer_body, lfm3_nanode.cu:3739-3856 (sandwich norms, conv or attention
+ * mixer, SwiGLU FFN), with the conv width and head geometry taken from cfg. */
+int pbo_decode(const pbo_model* m, pbo_state* s, int token, int pos, float* logits,
+               uint16_t* x_out) {
+  const pbo_cfg* c = &m->cfg;
+  const int H = c->hidden, F = c->inter, NH = c->n_heads, NKV = c->n_kv, HD = c->head_dim;
+  const int W = c->conv_w;
+  uint16_t* x = s->x;
+  uint16_t *h1 = malloc(2 * (size_t)H), *h2 = malloc(2 * (size_t)(F > 3 * H ? F : 3 * H));
+  uint16_t *h3 = malloc(2 * (size_t)F), *bx = malloc(2 * (size_t)3 * H);
+  uint16_t *qb = malloc(2 * (size_t)NH * HD), *kb = malloc(2 * (size_t)NKV * HD);
+  uint16_t *vb = malloc(2 * (size_t)NKV * HD), *gb = malloc(2 * (size_t)NH);
+  uint16_t *at = malloc(2 * (size_t)NH * HD), *ab = malloc(2 * (size_t)F);
+  const int half = (int)((double)c->rope_partial * HD) / 2;
+  float* cs = malloc(sizeof(float) * (HD / 2 + 1)); float* sn = malloc(sizeof(float) * (HD / 2 + 1));
+  /* embedding row: bf16(code * scale), k_dequant_row (:138-142) */
+  for (int i = 0; i < H; i++)
+    x[i] = pbo_f2bf((float)m->emb.c[(size_t)token * H + i] * m->emb.s[(size_t)token * (H / 32) + i / 32]);
+  for (int L = 0; L < c->n_layers; L++) {
+    const q8t* T = m->q[L];
+    const float* const* fw = m->f[L];
+    pbo_rmsnorm(x, fw[PBO_OPN], h1, H, c->norm_eps);
+    if (m->is_attn[L]) {
+      gemv_bf(&T[PBO_Q], h1, qb); gemv_bf(&T[PBO_K], h1, kb);
+      gemv_bf(&T[PBO_V], h1, vb); gemv_bf(&T[PBO_GATE], h1, gb);
+      pbo_headnorm(qb, fw[PBO_QN], NH, HD, c->norm_eps);
+      pbo_headnorm(kb, fw[PBO_KN], NKV, HD, c->norm_eps);
+      pbo_rope_cs(m->invf, pos, half, cs, sn);
+      pbo_rope(qb, NH, HD, half, cs, sn);
+      pbo_rope(kb, NKV, HD, half, cs, sn);
+      for (int i = 0; i < NKV * HD; i++) {
+        s->kc[L][(size_t)pos * NKV * HD + i] = pbo_f2h(pbo_bf2f(kb[i]));
+        s->vc[L][(size_t)pos * NKV * HD + i] = pbo_f2h(pbo_bf2f(vb[i]));
+      }
+      const float scaling = 1.0f / sqrtf((float)HD);
+      for (int h = 0; h < NH; h++)
+        pbo_attn_head(qb + (size_t)h * HD, s->kc[L], s->vc[L], h / (NH / NKV), NKV, HD, pos + 1,
+                      c->sliding_window, scaling, gb[h], 1, at + (size_t)h * HD);
+      gemv_bf(&T[PBO_O], at, h2);
+    } else {
+      gemv_bf(&T[PBO_IN], h1, bx);
+      uint16_t* ring = s->ring[L];
+      for (int k = 0; k + 1 < W; k++) memcpy(ring + (size_t)k * H, ring + (size_t)(k + 1) * H, 2 * (size_t)H);
+      for (int i = 0; i < H; i++)                       /* B * x, k_mul_bf (:811-815) */
+        ring[(size_t)(W - 1) * H + i] = pbo_f2bf(pbo_bf2f(bx[i]) * pbo_bf2f(bx[2 * H + i]));
+      const float* taps = fw[PBO_TAPS];
+      for (int i = 0; i < H; i++) {                     /* k_conv7 (:901-911), C * y */
+        float acc = 0.0f;
+        for (int k = 0; k < W; k++) acc = acc + taps[(size_t)i * W + k] * pbo_bf2f(ring[(size_t)k * H + i]);
+        const uint16_t cy = pbo_f2bf(acc);
+        h3[i] = pbo_f2bf(pbo_bf2f(bx[H + i]) * pbo_bf2f(cy));
+      }
+      gemv_bf(&T[PBO_OUT], h3, h2);
+    }
+    pbo_rmsnorm(h2, fw[PBO_POSTOPN], h3, H, c->norm_eps);
+    for (int i = 0; i < H; i++) x[i] = pbo_f2bf(pbo_bf2f(x[i]) + pbo_bf2f(h3[i]));
+    pbo_rmsnorm(x, fw[PBO_FFNN], h1, H, c->norm_eps);
+    gemv_bf(&T[PBO_W1], h1, ab);
+    gemv_bf(&T[PBO_W3], h1, h3);
+    for (int i = 0; i < F; i++) {                       /* k_silu_mul_bf (:821-829) */
+      const float a = pbo_bf2f(ab[i]);
+      const float sg = 1.0f / (1.0f + pbo_expf(-a));
+      ab[i] = pbo_f2bf((a * sg) * pbo_bf2f(h3[i]));
+    }
+    gemv_bf(&T[PBO_W2], ab, h2);
+    pbo_rmsnorm(h2, fw[PBO_POSTFFNN], h3, H, c->norm_eps);
+    for (int i = 0; i < H; i++) x[i] = pbo_f2bf(pbo_bf2f(x[i]) + pbo_bf2f(h3[i]));
+  }
+  /* embedding_norm, then the tied head in fp32 (gemv_f + k_combine_f) */
+  pbo_rmsnorm(x, m->final_norm, h1, H, c->norm_eps);
+  float* lg = logits ? logits : (float*)malloc(sizeof(float) * c->vocab);
+  pbo_q8f_gemv(m->emb.c, m->emb.s, c->vocab, H, h1, lg);
+  const int id = pbo_argmax(lg, c->vocab);
+  if (x_out) memcpy(x_out, x, 2 * (size_t)H);
+  if (!logits) free(lg);
+  free(h1); free(h2); free(h3); free(bx); free(qb); free(kb); free(vb); free(gb); free(at); free(ab);
+  free(cs); free(sn);
+  return id;
+}

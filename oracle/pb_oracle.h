@@ -1,0 +1,107 @@
+/* pb_oracle.h -- CPU restatement of PULSAR-ASM's quantized weight-streaming
+ * hot path. TEST INFRASTRUCTURE ONLY: this library is the checker that the
+ * CUDA product is compared against. Only tests/, __graft_entry__.smoke() and
+ * bench.py's CPU-baseline arm may load it; the product never links it.
+ *
+ * Every function names the reference file:line whose arithmetic it restates
+ * (paths are relative to the PULSAR-ASM project root). Built with
+ * -ffp-contract=off so every fmaf() below is the one written and no other
+ * multiply/add pair is fused, as the reference's own host code insists
+ * (.auto/lfm3/q8_gemv_cpu.c:10-16).
+ *
+ * Where the reference uses device intrinsics that have no bit-identical CPU
+ * counterpart (rsqrtf, expf, cosf/sinf on the GPU), this oracle and the CUDA
+ * product both use the deterministic replacements listed in pb_oracle.c's
+ * header comment, so the two agree bit for bit.
+ */
+#ifndef PB_ORACLE_H
+#define PB_ORACLE_H
+#include <stdint.h>
+#include <stddef.h>
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---- scalar numerics ---------------------------------------------------- */
+uint16_t pbo_f2bf(float v);          /* lfm3_nanode.cu:116-121 (RNE, inf/nan pass-through) */
+float pbo_bf2f(uint16_t h);
+uint16_t pbo_f2h(float v);           /* IEEE binary16, round to nearest even */
+float pbo_h2f(uint16_t h);           /* exact widening (pq1_host.c:14-24) */
+float pbo_expf(float x);             /* Cody-Waite + degree-7 Taylor, see pb_oracle.c */
+
+/* ---- Q8 float path (LFM3 REF_FLOAT): bf16 x, fp32 FMA, reference tree ---- */
+int pbo_q8_kchunk(int K);            /* pick(): lfm3_nanode.cu:1763-1768 */
+/* y[n] = ((0 + p_0) + p_1) + ... over K-chunks; p_c = 32-leaf shuffle tree of
+ * lane chains (lfm3_nanode.cu:222-343). scales are fp32 (fp16 callers widen). */
+void pbo_q8f_gemv(const int8_t* codes, const float* scales, int N, int K,
+                  const uint16_t* x_bf16, float* y);
+/* T positions, position-major x [T][K], y [T][N] (pf_gemv_T values). */
+void pbo_q8f_gemm(const int8_t* codes, const float* scales, int N, int K, int T,
+                  const uint16_t* x_bf16, float* y);
+
+/* ---- Q8_0 x Q8_0 integer path --------------------------------------------- */
+/* Activation quantizer per 32-block (fwd35_ref.c:332-343). */
+void pbo_q80_quant_act(const float* x, int K, int8_t* qx, uint16_t* dx_h);
+/* isum[n][b] exact int32; y[n] = sum_b (dw*dx)*(float)isum in block order. */
+void pbo_q80_gemv(const int8_t* codes, const uint16_t* dw_h, int N, int K,
+                  const int8_t* qx, const uint16_t* dx_h, int32_t* isum, float* y);
+
+/* ---- Q1_0 x Q8_K ---------------------------------------------------------- */
+void pbo_q1_repack(const uint8_t* q1, int rows, int K, uint32_t* w_bits, uint16_t* w_scales);
+void pbo_q8k_quant(const float* x, int K, uint8_t* xq);  /* 292 B per 256 values */
+void pbo_q1_rms_q8k(float* x, const float* r, const float* w, int n, float eps, float* y,
+                    uint8_t* xq);
+void pbo_q1_gemv(int rows, int K, const uint32_t* w_bits, const uint16_t* w_scales,
+                 const uint8_t* xq, int32_t* isum, float* y);
+
+/* ---- layer pieces (bf16 activations stored as uint16) --------------------- */
+void pbo_rmsnorm(const uint16_t* x, const float* w, uint16_t* y, int H, float eps);
+void pbo_headnorm(uint16_t* x, const float* w, int nheads, int hd, float eps);
+void pbo_rope_invf(float* invf, float base, int hd, float partial);
+void pbo_rope_cs(const float* invf, int pos, int half, float* c, float* s);
+void pbo_rope(uint16_t* x, int nheads, int hd, int half, const float* c, const float* s);
+void pbo_attn_head(const uint16_t* q, const uint16_t* kc, const uint16_t* vc, int kvh,
+                   int nkv, int hd, int npos, int win, float scaling, uint16_t gate,
+                   int use_gate, uint16_t* out);
+int pbo_argmax(const float* v, int n);
+
+/* ---- whole LFM3-style decode step ----------------------------------------- */
+typedef struct {
+  int hidden, inter, n_layers, n_heads, n_kv, head_dim, vocab, conv_w, max_ctx;
+  int sliding_window;          /* 0 = full attention */
+  float rope_theta, rope_partial, norm_eps;
+} pbo_cfg;
+
+enum {  /* tensor slots per layer */
+  PBO_Q = 0, PBO_K, PBO_V, PBO_GATE, PBO_O, PBO_IN, PBO_OUT, PBO_W1, PBO_W3, PBO_W2,
+  PBO_NQ8
+};
+enum {  /* fp32 slots per layer */
+  PBO_OPN = 0, PBO_POSTOPN, PBO_FFNN, PBO_POSTFFNN, PBO_QN, PBO_KN, PBO_TAPS, PBO_NF32
+};
+
+typedef struct pbo_model pbo_model;
+typedef struct pbo_state pbo_state;
+
+pbo_model* pbo_model_new(const pbo_cfg* cfg, const int* layer_is_attn);
+void pbo_model_free(pbo_model* m);
+void pbo_model_set_q8(pbo_model* m, int layer, int slot, const int8_t* codes,
+                      const float* scales, int N, int K);
+void pbo_model_set_f32(pbo_model* m, int layer, int slot, const float* p);
+/* layer -1: the tied embedding / head (Q8) and the final norm (fp32). */
+pbo_state* pbo_state_new(const pbo_model* m);
+void pbo_state_free(pbo_state* s);
+/* one token at position pos; returns the greedy id. logits (fp32 [vocab])
+ * and the final residual x (bf16 [hidden]) are optional outputs. */
+int pbo_decode(const pbo_model* m, pbo_state* s, int token, int pos, float* logits,
+               uint16_t* x_out);
+/* expose state for checks: K/V cache row (fp16) and conv ring (bf16) */
+const uint16_t* pbo_state_kv(const pbo_state* s, int layer, int which);
+const uint16_t* pbo_state_ring(const pbo_state* s, int layer);
+
+int pbo_threads(void);
+
+#ifdef __cplusplus
+}
+#endif
+#endif
