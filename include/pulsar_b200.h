@@ -1,0 +1,157 @@
+/* pulsar_b200.h -- C ABI of the B200 (sm_100a) quantized weight-streaming path.
+ *
+ * Drop-in boundary for PULSAR-ASM's decode hot path. Reference interfaces each
+ * entry point replaces are cited as file:line relative to the PULSAR-ASM root.
+ *
+ * Conventions
+ *  - Every function returns int: 0 (PB_OK) or a negative PB_E* code. No exits,
+ *    no printing; pb_last_error() returns the message of the calling thread's
+ *    last failure.
+ *  - Pointers named d_* are device pointers (cudaMalloc'd or equivalent) on the
+ *    current device; h_* are host pointers. `stream` is a cudaStream_t passed as
+ *    void* so that this header needs no CUDA include (NULL = legacy stream).
+ *  - bf16 activations are passed as uint16_t bit patterns, fp16 as uint16_t.
+ *  - The caller owns activations, outputs and streams; the library owns packed
+ *    weights (pb_q8 / pb_q1 tensors), models and states.
+ *  - Calls on one object are not thread-safe; distinct objects may be used
+ *    from different host threads and streams.
+ */
+#ifndef PULSAR_B200_H
+#define PULSAR_B200_H
+#include <stddef.h>
+#include <stdint.h>
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define PB_OK 0
+#define PB_EINVAL (-1)    /* bad argument or shape */
+#define PB_ENOMEM (-2)    /* device or host allocation failed */
+#define PB_ECUDA (-3)     /* a CUDA call or launch failed */
+#define PB_EIO (-4)       /* open/read failure or short read */
+#define PB_ECRC (-5)      /* per-tensor CRC mismatch */
+#define PB_EFORMAT (-6)   /* bad magic, malformed header or record */
+#define PB_ENOTSUP (-8)   /* shape/dtype this build does not implement */
+
+#define PB_DT_BF16 0
+#define PB_DT_F32 1
+#define PB_DT_F16 2
+
+int pb_version(void);
+int pb_last_error(char* buf, size_t n);
+/* number of this library's kernel launches issued so far by the calling process */
+uint64_t pb_launch_count(void);
+
+/* ------------------------------------------------------------------ Q8 ---- *
+ * Q8 tensor: int8 codes [N][K] row-major plus one scale per 32-code block,
+ * fp16 (Q8_0, PB_DT_F16) or fp32 (.lfm3q8 dtype 1, PB_DT_F32). pb_q8_pack
+ * copies it into the library's streaming layout (16-byte granules ordered so
+ * that each warp load instruction is one contiguous 512-byte segment).
+ * Replaces the loader's tiler, lfm3_nanode.cu:1359-1375 / :4510-4521.        */
+typedef struct pb_q8 pb_q8;
+int pb_q8_pack(const int8_t* codes, const void* scales, int scale_dtype, int N, int K,
+               int src_on_device, void* stream, pb_q8** out);
+int pb_q8_free(pb_q8* w);
+int pb_q8_shape(const pb_q8* w, int* N, int* K);
+/* y = W x, REF_FLOAT numerics: bf16 x, fp32 FMA chains in the reference's
+ * 32-leaf tree order, K-chunks of 2048 summed ascending, output rounded to
+ * bf16 (y_dtype PB_DT_BF16, the Linear) or kept fp32 (PB_DT_F32, the head).
+ * Replaces gemv() lfm3_nanode.cu:1916-1966 (q8_partial + k_combine_bf) and
+ * gemv_f() :3634-3664 (q8_partial + k_combine_f).                            */
+int pb_q8_gemv(const pb_q8* w, const uint16_t* d_x, void* d_y, int y_dtype, void* stream);
+/* T positions, x [T][K] position-major, y [T][N]: the values of the chunked
+ * prefill pf_gemv_T (lfm3_nanode.cu:4840-4968), bit-identical per position.  */
+int pb_q8_gemm(const pb_q8* w, int T, const uint16_t* d_x, void* d_y, int y_dtype,
+               void* stream);
+
+/* Q8_0 x Q8_0 integer path. x (fp32) is quantised per 32-block to int8 codes
+ * and fp16 scales (fwd35_ref.c:332-343); y[n] = sum_b (dw*dx)*(float)isum_b in
+ * block order where isum_b is the exact int32 block dot (pq1_host.c:112-116
+ * pattern). d_isum ([N][K/32] int32) is optional.                            */
+int pb_q80_quantize(const float* d_x, int K, int8_t* d_qx, uint16_t* d_dx, void* stream);
+int pb_q80_gemv(const pb_q8* w, const int8_t* d_qx, const uint16_t* d_dx, float* d_y,
+                int32_t* d_isum, void* stream);
+
+/* ------------------------------------------------------------------ Q1 ---- *
+ * Q1_0: 18-byte blocks per 128 weights along K, fp16 scale then 16 bytes of
+ * LSB-first sign bits, bit 1 => +1 (pq1_wrap.h:24-35).                        */
+typedef struct pb_q1 pb_q1;
+/* replaces pq1_split_repack + arena upload (pq1_host.c:78-97,
+ * pq1_fwd8_glue.c:562-620) */
+int pb_q1_pack(const uint8_t* blocks, int rows, int K, int src_on_device, void* stream,
+               pb_q1** out);
+int pb_q1_free(pb_q1* w);
+/* Q8_K activation quantiser, 292 bytes per 256 values (fwd8.c:67-139) */
+int pb_q8k_quantize(const float* d_x, int K, uint8_t* d_xq, void* stream);
+/* y = W xq: per 128-group exact int32 sum, acc += (ws*db)*(float)isum in group
+ * order (pq1_gemv_cpu, pq1_host.c:99-120; device form pq1_gemv_hs,
+ * pq1_swar_sm53.cu:924-1175). d_isum ([rows][K/128]) is optional.           */
+int pb_q1_gemv(const pb_q1* w, const uint8_t* d_xq, float* d_y, int32_t* d_isum, void* stream);
+
+/* The Bonsai engine's host ABI, same signatures and conventions
+ * (pq1_fwd8_shim.h:12-23): host Q1_0 weights w (also the cache key, packed
+ * and uploaded on first use), host Q8_K activation xq, host fp32 output y;
+ * x is unused. The batch form returns 0 when it ran, nonzero when the caller
+ * must fall back to the per-tensor call.                                     */
+void pq1_pq1_compat_gemv(int rows, int cols, const unsigned char* w, const float* x, float* y,
+                         const unsigned char* xq);
+int pq1_pq1_compat_gemv_batch(const unsigned char* const* w, const int* rows, int n, int cols,
+                              float* const* ys, const unsigned char* xq);
+
+/* --------------------------------------------------------------- model ---- *
+ * An LFM3-style backbone loaded from an .lfm3q8 blob (magic "LFM3Q8\1\0",
+ * u32 header length, JSON header with cfg and tensor table, payloads; per
+ * tensor CRC32). Tensor dtypes: 1 = Q8 codes + fp32 scales, 2 = fp32,
+ * 3 = bf16 (rejected by this build: PB_ENOTSUP), 8 = Q8_0 codes + fp16
+ * scales. Replaces load_blob
+ * (lfm3_nanode.cu:1404-1733).                                                */
+typedef struct pb_model pb_model;
+typedef struct pb_state pb_state;
+typedef struct {
+  int hidden, inter, n_layers, n_heads, n_kv, head_dim, vocab, conv_w;
+  int n_attn, sliding_window;
+  float rope_theta, rope_partial, norm_eps;
+  uint64_t weight_bytes;       /* bytes of weights streamed per decode token */
+} pb_model_info;
+/* device < 0: validate only (header, shapes, every payload CRC) without touching
+ * a GPU; returns the status and leaves *out NULL. */
+int pb_open(const char* blob_path, int device, pb_model** out);
+int pb_close(pb_model* m);
+int pb_model_get_info(const pb_model* m, pb_model_info* info);
+/* index of a tensor by its blob name, or PB_EINVAL */
+int pb_tensor_id(const pb_model* m, const char* name);
+/* KV cache (fp16, [layer][max_ctx][n_kv][head_dim]) and conv rings, zeroed */
+int pb_state_create(pb_model* m, int max_ctx, pb_state** out);
+int pb_state_destroy(pb_state* s);
+int pb_state_reset(pb_state* s, void* stream);
+/* one T=1 layer on the device residual x (bf16 [hidden], updated in place):
+ * layer_body, lfm3_nanode.cu:3739-3856 */
+int pb_layer_step(pb_model* m, pb_state* s, int layer, int pos, uint16_t* d_x, void* stream);
+/* one token: embedding row, every layer, final norm, tied head, greedy id.
+ * h_out_id (host, optional) receives the id after the call synchronises
+ * `stream`; d_logits (fp32 [vocab], optional) receives the logits. */
+int pb_decode_token(pb_model* m, pb_state* s, int token, int pos, int* h_out_id,
+                    float* d_logits, void* stream);
+/* n greedy steps on the device: step i feeds the previous id (the first feeds
+ * `token`), at positions pos0..pos0+n-1, one CUDA graph launch per token,
+ * no host round trip; d_ids (int32 [n]) receives the generated ids. */
+int pb_decode_greedy(pb_model* m, pb_state* s, int token, int pos0, int n, int* d_ids,
+                     void* stream);
+/* teacher-forced prompt: step i feeds d_tokens[i] (device int32 [n]) at
+ * position pos0+i, one graph launch per token, no host round trip; d_ids
+ * (optional, int32 [n]) receives the greedy prediction after each token.
+ * The prompt feed of the reference's step loop (lfm3_nanode.cu:5828-6030). */
+int pb_decode_prompt(pb_model* m, pb_state* s, const int* d_tokens, int n, int pos0, int* d_ids,
+                     void* stream);
+/* kernels one decode token launches (the CUDA graph's node count) */
+int pb_decode_kernels_per_token(pb_state* s);
+/* measurement hook: mean ms of one of the decode step's fused GEMV kernels
+ * launched alone (which: 0 first GEMV, 1 o/out_proj, 2 w1|w3, 3 w2, 4 head),
+ * cycling over the layers' distinct weights, and its algorithmic bytes */
+int pb_time_step_kernel(pb_model* m, pb_state* s, int which, int iters, float* ms, double* bytes,
+                        void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif

@@ -233,5 +233,9 @@ class Model:
 
 
 def h2f_vec(h):
-    """exact fp16 -> fp32 widening (numpy's float16 conversion is exact)."""
-    return np.asarray(h, np.uint16).view(np.float16).astype(np.float32)
+    """exact fp16 -> fp32 widening (numpy's float16 conversion is exact); accepts
+    float16 arrays or their uint16 bit patterns."""
+    h = np.asarray(h)
+    if h.dtype == np.uint16:
+        h = h.view(np.float16)
+    return h.astype(np.float32)

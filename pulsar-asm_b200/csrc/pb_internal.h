@@ -1,0 +1,70 @@
+// pb_internal.h -- host-side declarations shared by the library's translation
+// units (not part of the public ABI; include/pulsar_b200.h is).
+#pragma once
+#include <cstdint>
+#include <cstddef>
+#include <cuda_runtime.h>
+#include "../../include/pulsar_b200.h"
+
+// thread-local last error (pb_last_error) and a process-wide launch counter
+int pb_set_error(int code, const char* fmt, ...);
+void pb_count_launch(uint64_t n = 1);
+// while set on this thread, pb_count_launch ignores launches (graph capture)
+void pb_set_capturing(bool on);
+
+#define PB_TRY_CUDA(expr)                                                        \
+  do {                                                                           \
+    cudaError_t e__ = (expr);                                                    \
+    if (e__ != cudaSuccess)                                                      \
+      return pb_set_error(PB_ECUDA, "%s: %s (%s:%d)", #expr, cudaGetErrorString(e__), \
+                          __FILE__, __LINE__);                                   \
+  } while (0)
+
+// after a <<<>>> launch: count it and surface launch-configuration errors
+#define PB_LAUNCHED(name)                                                        \
+  do {                                                                           \
+    cudaError_t e__ = cudaGetLastError();                                        \
+    if (e__ != cudaSuccess)                                                      \
+      return pb_set_error(PB_ECUDA, "launch %s: %s", name, cudaGetErrorString(e__)); \
+    pb_count_launch();                                                           \
+  } while (0)
+
+// Q8 tensor layouts
+enum { PB_Q8_ROWMAJOR = 0, PB_Q8_STREAM = 1 };
+
+struct pb_q8 {
+  int N = 0, K = 0;
+  int sdt = PB_DT_F16;       // scale dtype: PB_DT_F16 or PB_DT_F32
+  int layout = PB_Q8_ROWMAJOR;
+  int nch = 1;               // 2048-code chunks per row (stream layout)
+  int8_t* codes = nullptr;   // device
+  void* scales = nullptr;    // device
+  bool owner = true;         // false: views into a model arena
+};
+
+struct pb_q1 {
+  int rows = 0, K = 0;
+  uint32_t* bits = nullptr;      // device, stream layout (see pb_q1.cu)
+  uint16_t* scales = nullptr;    // device
+  bool owner = true;
+};
+
+// streaming layout: 2048-code chunks, needs K % 2048 == 0 and chunks | 8
+inline bool pb_q8_stream_ok(int K) {
+  if (K % 2048) return false;
+  const int n = K / 2048;
+  return n == 1 || n == 2 || n == 4 || n == 8;
+}
+inline size_t pb_q8_scale_bytes(int N, int K, int sdt) {
+  return (size_t)N * (K / 32) * (sdt == PB_DT_F32 ? 4 : 2);
+}
+
+// pack src_rows row-major rows into caller-provided storage at destination
+// rows r*rmul + radd (the model arena merges and interleaves tensors this way)
+int pb_q8_pack_into(pb_q8* w, const int8_t* d_codes, const void* d_scales, cudaStream_t st,
+                    int src_rows, int rmul, int radd);
+
+// launch helpers used by the model's step (pdl: programmatic dependent launch)
+int pb_q8_gemv_launch(const pb_q8* w, const uint16_t* d_x, void* d_y, int y_dtype,
+                      cudaStream_t st);
+int pb_num_sms();

@@ -1,0 +1,1450 @@
+// pb_model.cu -- the LFM3-style backbone on sm_100a: .lfm3q8 loader, fused
+// decode-step kernels, whole-token CUDA graphs and the model C ABI.
+//
+// One decode token (layer_body, lfm3_nanode.cu:3739-3856, for every layer;
+// then the embedding norm, the tied head and greedy argmax) runs as 4 kernels
+// per conv layer, 5 per attention layer and 1 for the head. Everything that is
+// not a weight stream is fused into the GEMV that consumes it:
+//   [embed | residual add + post-norm] + operator_norm -> in_proj / q|k|v|gate
+//   headnorm + RoPE + fp16 KV append + attention + sigmoid gate   (k_attn)
+//   B*x, conv ring, taps, C*y                                      -> out_proj
+//   post_operator_norm + residual add + ffn_norm                   -> w1|w3
+//   SiLU(w1)*w3 in the w1|w3 epilogue (their rows are interleaved)
+//   post_ffn_norm + residual add + embedding_norm -> head -> argmax -> next id
+// Each fused prologue is computed redundantly by every CTA (it is a few KB of
+// L2 reads) so that no extra grid-wide dependency is needed. Kernels launch
+// with programmatic dependent launch: a kernel starts while its predecessor
+// drains, bulk-prefetches its own weight slice into L2, and only then waits
+// for the predecessor's results (griddepcontrol.wait).
+#include "pb_common.cuh"
+#include "pb_internal.h"
+#include "pb_json.h"
+#include <zlib.h>
+#include <cmath>
+#include <cstdio>
+#include <cstring>
+#include <string>
+#include <vector>
+
+namespace {
+
+constexpr int PRO_PLAIN = 0, PRO_ADDNORM = 1, PRO_EMBED = 2, PRO_CONV = 3;
+constexpr int EPI_BF16 = 0, EPI_SILU = 1, EPI_ARGMAX = 2;
+constexpr int MAX_CTA = 1024;
+
+// device control block of a state
+struct Ctl {
+  int token;          // input id of the step; the head writes the greedy id here
+  int pos;            // position of the step; the head advances it
+  int step;           // greedy step counter (index into ids)
+  unsigned counter;   // argmax last-CTA counter
+  int* ids;           // optional output: the greedy id of every step
+  const int* prompt;  // optional teacher-forced inputs: step i+1 feeds prompt[i+1]
+  int n_prompt;
+  int _pad;
+  float slot_val[MAX_CTA];
+  int slot_idx[MAX_CTA];
+};
+
+struct StepArgs {
+  // weight stream
+  const uint4* codes;
+  const void* scales;
+  int N;
+  // prologue
+  int pro;
+  int K;               // GEMV input length
+  int H;               // hidden size (prologue vectors)
+  float eps;
+  const bf16_t* xin;   // PLAIN: x [K]; ADDNORM: residual [H]; CONV: in_proj output [3H]
+  const bf16_t* hin;   // ADDNORM: vector to post-normalise and add (null: none)
+  const float* wpost;  // ADDNORM: its norm weight
+  const float* wnorm;  // norm giving x from the residual (null: x = residual)
+  bf16_t* rout;        // residual written by CTA 0 (null: not written)
+  const uint4* emb_codes;   // EMBED: tied table, stream layout
+  const void* emb_scales;
+  int emb_nch;
+  int emb_f32;         // EMBED: scales are fp32 pairs (else fp16 pairs)
+  bf16_t* ring;        // CONV: [W][H], slot = position mod W
+  const float* taps;   // CONV: [H][W]
+  int convw;
+  Ctl* ctl;
+  // epilogue
+  void* y;
+};
+
+// ---------------------------------------------------------------- prologue
+// RMSNorm over v (fp32 values of bf16 numbers, in shared memory) with the
+// reference's order (rmsnorm_body, lfm3_nanode.cu:383-440): thread t owns the
+// E = H/256 consecutive values [E t, E t + E), squares summed pairwise, warp
+// shuffle-down tree, the 8 warp partials ascending; rs = 1/sqrt(mean + eps)
+// correctly rounded; out = bf16(w * bf16(v * rs)).
+// sx (the GEMV input) is stored padded, one spare float per 32, so that lane
+// l reading its 32 consecutive values (index 32 l + j) hits bank (l + j) % 32.
+__device__ __forceinline__ int padx(int i) { return i + (i >> 5); }
+
+template <int E>
+__device__ void block_rmsnorm(const float* v, const float* __restrict__ w, float* out, int H,
+                              float eps, float* red, int opad) {
+  const int t = threadIdx.x;
+  float ss[E];
+#pragma unroll
+  for (int j = 0; j < E; j++) ss[j] = __fmul_rn(v[t * E + j], v[t * E + j]);
+#pragma unroll
+  for (int width = E; width > 1; width >>= 1)
+#pragma unroll
+    for (int i = 0; i < width / 2; i++) ss[i] = __fadd_rn(ss[2 * i], ss[2 * i + 1]);
+  float s = pb_warp_tree(ss[0]);
+  if ((t & 31) == 0) red[t >> 5] = s;
+  __syncthreads();
+  float tot = red[0];
+#pragma unroll
+  for (int i = 1; i < 8; i++) tot = __fadd_rn(tot, red[i]);
+  const float rs = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fmul_rn(tot, __fdiv_rn(1.0f, (float)H)), eps)));
+#pragma unroll
+  for (int j = 0; j < E; j++) {
+    const int i = t * E + j;
+    out[opad ? padx(i) : i] = pb_bf2f(pb_f2bf(__fmul_rn(w[i], pb_bf2f(pb_f2bf(__fmul_rn(v[i], rs))))));
+  }
+  __syncthreads();   // red is reused by the next call; out is complete
+}
+
+__device__ void rmsnorm_dispatch(const float* v, const float* w, float* out, int H, float eps,
+                                 float* red, int opad) {
+  switch (H >> 8) {
+    case 1: block_rmsnorm<1>(v, w, out, H, eps, red, opad); break;
+    case 2: block_rmsnorm<2>(v, w, out, H, eps, red, opad); break;
+    case 4: block_rmsnorm<4>(v, w, out, H, eps, red, opad); break;
+    case 8: block_rmsnorm<8>(v, w, out, H, eps, red, opad); break;
+    case 16: block_rmsnorm<16>(v, w, out, H, eps, red, opad); break;
+    default: break;
+  }
+}
+
+// Computes the GEMV input x (fp32 values of bf16 numbers) into sx, padded
+// (element i at padx(i)); sx must not overlap sa/sb.
+// Scratch sa/sb hold H floats each. Requires blockDim.x == 256.
+__device__ void step_prologue(const StepArgs& a, float* sx, float* sa, float* sb, float* red) {
+  const int t = threadIdx.x, H = a.H;
+  if (a.pro == PRO_PLAIN) {
+    for (int i = t; i < a.K; i += 256) sx[padx(i)] = pb_bf2f(a.xin[i]);
+    __syncthreads();
+    return;
+  }
+  if (a.pro == PRO_CONV) {
+    // lfm3_nanode.cu:3790-3818: bx = bf16(B*x) enters the ring as the newest
+    // slot; y = sum_k taps[i][k] * ring_k (oldest first); out = bf16(C * bf16(y)).
+    const int pos = a.ctl->pos, W = a.convw;
+    for (int i = t; i < H; i += 256) {
+      const float B = pb_bf2f(a.xin[i]), C = pb_bf2f(a.xin[H + i]), X = pb_bf2f(a.xin[2 * H + i]);
+      const bf16_t bx = pb_f2bf(__fmul_rn(B, X));
+      if (blockIdx.x == 0) a.ring[(size_t)(pos % W) * H + i] = bx;
+      float acc = 0.0f;
+      for (int k = 0; k < W; k++) {
+        const int p = pos - (W - 1) + k;
+        const float r = (k == W - 1) ? pb_bf2f(bx) : pb_bf2f(a.ring[(size_t)(((p % W) + W) % W) * H + i]);
+        acc = __fadd_rn(acc, __fmul_rn(a.taps[(size_t)i * W + k], r));
+      }
+      sx[padx(i)] = pb_bf2f(pb_f2bf(__fmul_rn(C, pb_bf2f(pb_f2bf(acc)))));
+    }
+    __syncthreads();
+    return;
+  }
+  // residual into sa
+  if (a.pro == PRO_EMBED) {
+    // k_dequant_row (lfm3_nanode.cu:138-142): bf16(code * scale), row = token
+    const int tok = a.ctl->token;
+    const int nch = a.emb_nch;
+    const int8_t* cb = reinterpret_cast<const int8_t*>(a.emb_codes);
+    for (int i = t; i < H; i += 256) {
+      const int b = i >> 5, j = i & 31, c = b >> 6, bb = b & 63, l = bb & 31, half = bb >> 5;
+      const size_t seg = (size_t)tok * nch + c;
+      const int gi = (half * 2 + (j >> 4)) * 32 + l;
+      const float code = (float)cb[(seg * 128 + gi) * 16 + (j & 15)];
+      const float s = a.emb_f32 ? reinterpret_cast<const float*>(a.emb_scales)[(seg * 32 + l) * 2 + half]
+                                : pb_h2f(reinterpret_cast<const unsigned short*>(a.emb_scales)[(seg * 32 + l) * 2 + half]);
+      sa[i] = pb_bf2f(pb_f2bf(__fmul_rn(code, s)));
+    }
+    __syncthreads();
+  } else {
+    for (int i = t; i < H; i += 256) sa[i] = pb_bf2f(a.xin[i]);
+    if (a.hin) {
+      for (int i = t; i < H; i += 256) sb[i] = pb_bf2f(a.hin[i]);
+      __syncthreads();
+      rmsnorm_dispatch(sb, a.wpost, sb, H, a.eps, red, 0);    // in place: each thread owns its values
+      for (int i = t; i < H; i += 256) sa[i] = pb_bf2f(pb_f2bf(__fadd_rn(sa[i], sb[i])));
+    }
+    __syncthreads();
+  }
+  if (a.rout && blockIdx.x == 0)
+    for (int i = t; i < H; i += 256) a.rout[i] = pb_f2bf(sa[i]);
+  if (a.wnorm) rmsnorm_dispatch(sa, a.wnorm, sx, H, a.eps, red, 1);
+  else {
+    for (int i = t; i < H; i += 256) sx[padx(i)] = sa[i];
+    __syncthreads();
+  }
+}
+
+
+// ------------------------------------------------------------ step GEMV
+// The streaming GEMV of pb_q8.cu (same granule layout, same leaf chains and
+// trees) with a fused prologue and epilogue. CTA b owns a contiguous range of
+// row blocks, prefetches that slice of codes and scales into L2 before it
+// waits on its predecessor, then streams it.
+template <bool F32S>
+struct SPair;
+template <>
+struct SPair<false> {
+  static PB_DEV void load(const void* base, size_t idx, float& lo, float& hi) {
+    const unsigned w = pb_ldg_stream32(reinterpret_cast<const unsigned*>(base) + idx);
+    lo = pb_h2f((unsigned short)(w & 0xffffu));
+    hi = pb_h2f((unsigned short)(w >> 16));
+  }
+  static constexpr int BYTES = 4;
+};
+template <>
+struct SPair<true> {
+  static PB_DEV void load(const void* base, size_t idx, float& lo, float& hi) {
+    const uint2 w = pb_ldg_stream64(reinterpret_cast<const uint2*>(base) + idx);
+    lo = __uint_as_float(w.x);
+    hi = __uint_as_float(w.y);
+  }
+  static constexpr int BYTES = 8;
+};
+
+PB_DEV float s_dot16(const uint4 g, const float* xr, float dot) {
+  const unsigned ws[4] = {g.x, g.y, g.z, g.w};
+#pragma unroll
+  for (int k = 0; k < 4; k++) {
+    const unsigned ub = ws[k] ^ 0x80808080u;
+#pragma unroll
+    for (int j = 0; j < 4; j++) dot = __fmaf_rn(pb_code(ub, j), xr[4 * k + j], dot);
+  }
+  return dot;
+}
+PB_DEV float s_leaf(const uint4 (&q)[4], float slo, float shi, const float (&xr)[64]) {
+  float d0 = s_dot16(q[0], xr, 0.0f);
+  d0 = s_dot16(q[1], xr + 16, d0);
+  const float acc = __fmaf_rn(slo, d0, 0.0f);
+  float d1 = s_dot16(q[2], xr + 32, 0.0f);
+  d1 = s_dot16(q[3], xr + 48, d1);
+  return __fmaf_rn(shi, d1, acc);
+}
+
+PB_DEV void l2_prefetch(const void* p, size_t bytes) {
+  const char* c = reinterpret_cast<const char*>(p);
+  // 16-byte aligned start and size for cp.async.bulk.prefetch
+  const uintptr_t a0 = ((uintptr_t)c + 15) & ~(uintptr_t)15;
+  const uintptr_t a1 = ((uintptr_t)c + bytes) & ~(uintptr_t)15;
+  for (uintptr_t a = a0; a < a1; a += 32768) {
+    const unsigned n = (unsigned)((a1 - a) < 32768 ? (a1 - a) : 32768);
+    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(a), "r"(n) : "memory");
+  }
+}
+
+template <int NCH, bool F32S, int EPI>
+__global__ void __launch_bounds__(256, 2) k_step(StepArgs a) {
+  constexpr int U = 2, G = 8 / NCH, RB = G * U;
+  extern __shared__ __align__(16) float smem[];
+  float* sx = smem;                          // K + K/32 (padded)
+  float* sa = sx + a.K + (a.K >> 5);         // H
+  float* sb = sa + a.H;                      // H
+  __shared__ float red[8];
+  __shared__ float part[2][RB][NCH];
+  __shared__ float bestv[8];
+  __shared__ int besti[8];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int c = warp % NCH, g = warp / NCH;
+  const int nrb = (a.N + RB - 1) / RB;
+  const int rb0 = (int)(((long long)blockIdx.x * nrb) / gridDim.x);
+  const int rb1 = (int)(((long long)(blockIdx.x + 1) * nrb) / gridDim.x);
+  if (threadIdx.x == 0 && rb1 > rb0) {
+    const int r0 = rb0 * RB, r1 = min(rb1 * RB, a.N);
+    l2_prefetch(reinterpret_cast<const char*>(a.codes) + (size_t)r0 * NCH * 2048, (size_t)(r1 - r0) * NCH * 2048);
+    l2_prefetch(reinterpret_cast<const char*>(a.scales) + (size_t)r0 * NCH * 32 * SPair<F32S>::BYTES,
+                (size_t)(r1 - r0) * NCH * 32 * SPair<F32S>::BYTES);
+  }
+  pb_grid_launch_dependents();
+  pb_grid_wait();
+  step_prologue(a, sx, sa, sb, red);
+  float xr[64];
+  {
+    const float* x0 = sx + (c * 64 + lane) * 33;          // block c*64 + lane, padded
+    const float* x1 = sx + (c * 64 + 32 + lane) * 33;     // block c*64 + 32 + lane
+#pragma unroll
+    for (int j = 0; j < 32; j++) { xr[j] = x0[j]; xr[32 + j] = x1[j]; }
+  }
+  float bv = -INFINITY;
+  int bi = 0x7fffffff;
+  int it = 0;
+  for (int rb = rb0; rb < rb1; rb++, it ^= 1) {
+    const int row0 = rb * RB + g * U;
+    uint4 q[U][4];
+    float slo[U], shi[U];
+#pragma unroll
+    for (int u = 0; u < U; u++) {
+      const int row = row0 + u;
+      if (row < a.N) {
+        const size_t seg = (size_t)row * NCH + c;
+        const uint4* base = a.codes + seg * 128 + lane;
+#pragma unroll
+        for (int h = 0; h < 4; h++) q[u][h] = pb_ldg_stream(base + 32 * h);
+        SPair<F32S>::load(a.scales, seg * 32 + lane, slo[u], shi[u]);
+      } else {
+#pragma unroll
+        for (int h = 0; h < 4; h++) q[u][h] = make_uint4(0, 0, 0, 0);
+        slo[u] = shi[u] = 0.0f;
+      }
+    }
+    float v[U];
+#pragma unroll
+    for (int u = 0; u < U; u++) v[u] = pb_warp_tree(s_leaf(q[u], slo[u], shi[u], xr));
+    if (NCH == 1) {
+      if (lane == 0) {
+        if (EPI == EPI_SILU) {
+          // rows 2i (w1) and 2i+1 (w3): k_silu_mul_bf, lfm3_nanode.cu:821-829
+          if (row0 + 1 < a.N) {
+            const float av = pb_bf2f(pb_f2bf(__fadd_rn(0.0f, v[0])));
+            const float bw = pb_bf2f(pb_f2bf(__fadd_rn(0.0f, v[1])));
+            reinterpret_cast<bf16_t*>(a.y)[row0 >> 1] =
+                pb_f2bf(__fmul_rn(__fmul_rn(av, pb_sigmoid(av)), bw));
+          }
+        } else {
+#pragma unroll
+          for (int u = 0; u < U; u++) {
+            const int row = row0 + u;
+            if (row < a.N) {
+              const float o = __fadd_rn(0.0f, v[u]);
+              if (EPI == EPI_ARGMAX) {
+                reinterpret_cast<float*>(a.y)[row] = o;
+                if (o > bv || (o == bv && row < bi)) { bv = o; bi = row; }
+              } else {
+                reinterpret_cast<bf16_t*>(a.y)[row] = pb_f2bf(o);
+              }
+            }
+          }
+        }
+      }
+    } else {
+      if (lane == 0)
+#pragma unroll
+        for (int u = 0; u < U; u++) part[it][g * U + u][c] = v[u];
+      __syncthreads();
+      if (threadIdx.x < RB) {
+        const int row = rb * RB + threadIdx.x;
+        float acc = 0.0f;
+#pragma unroll
+        for (int cc = 0; cc < NCH; cc++) acc = __fadd_rn(acc, part[it][threadIdx.x][cc]);
+        if (EPI == EPI_SILU) {
+          if ((threadIdx.x & 1) == 0 && row + 1 < a.N) {
+            float acc1 = 0.0f;
+#pragma unroll
+            for (int cc = 0; cc < NCH; cc++) acc1 = __fadd_rn(acc1, part[it][threadIdx.x + 1][cc]);
+            const float av = pb_bf2f(pb_f2bf(acc)), bw = pb_bf2f(pb_f2bf(acc1));
+            reinterpret_cast<bf16_t*>(a.y)[row >> 1] = pb_f2bf(__fmul_rn(__fmul_rn(av, pb_sigmoid(av)), bw));
+          }
+        } else if (row < a.N) {
+          if (EPI == EPI_ARGMAX) {
+            reinterpret_cast<float*>(a.y)[row] = acc;
+            if (acc > bv || (acc == bv && row < bi)) { bv = acc; bi = row; }
+          } else {
+            reinterpret_cast<bf16_t*>(a.y)[row] = pb_f2bf(acc);
+          }
+        }
+      }
+    }
+  }
+  if (EPI == EPI_ARGMAX) {
+    // greedy argmax, ties to the lowest index: per-thread best -> warp -> CTA
+    // slot; the last CTA to finish reduces the slots and publishes the id.
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const float ov = __shfl_down_sync(0xffffffffu, bv, o);
+      const int oi = __shfl_down_sync(0xffffffffu, bi, o);
+      if (ov > bv || (ov == bv && oi < bi)) { bv = ov; bi = oi; }
+    }
+    if (lane == 0) { bestv[warp] = bv; besti[warp] = bi; }
+    __syncthreads();
+    __shared__ int am_last;
+    if (threadIdx.x == 0) {
+      float b = bestv[0]; int ix = besti[0];
+      for (int w = 1; w < 8; w++)
+        if (bestv[w] > b || (bestv[w] == b && besti[w] < ix)) { b = bestv[w]; ix = besti[w]; }
+      a.ctl->slot_val[blockIdx.x] = b;
+      a.ctl->slot_idx[blockIdx.x] = ix;
+      __threadfence();
+      const unsigned prev = atomicAdd(&a.ctl->counter, 1u);
+      am_last = prev == gridDim.x - 1;
+    }
+    __syncthreads();
+    if (am_last && threadIdx.x == 0) {
+      __threadfence();
+      volatile float* sv = a.ctl->slot_val;
+      volatile int* si = a.ctl->slot_idx;
+      float b = sv[0]; int ix = si[0];
+      for (int k = 1; k < (int)gridDim.x; k++) {
+        const float ov = sv[k]; const int oi = si[k];
+        if (ov > b || (ov == b && oi < ix)) { b = ov; ix = oi; }
+      }
+      const int step = a.ctl->step;
+      a.ctl->token = (step + 1 < a.ctl->n_prompt) ? a.ctl->prompt[step + 1] : ix;
+      if (a.ctl->ids) a.ctl->ids[step] = ix;
+      a.ctl->step = step + 1;
+      a.ctl->pos += 1;
+      a.ctl->counter = 0;
+    }
+  }
+}
+
+// ------------------------------------------------------------- attention
+struct AttnArgs {
+  const bf16_t* qkvg;      // [NH*HD | NKV*HD | NKV*HD | NH]
+  const float* qnorm;      // [HD]
+  const float* knorm;      // [HD]
+  const float* rope_cos;   // [max_ctx][half]
+  const float* rope_sin;
+  unsigned short* kc;      // fp16 [max_ctx][NKV][HD]
+  unsigned short* vc;
+  bf16_t* out;             // [NH*HD] gated attention output
+  Ctl* ctl;
+  int nh, nkv, half, win, max_ctx;
+  float scaling, eps;
+};
+
+// per-head RMSNorm (k_headnorm, lfm3_nanode.cu:460-479) + NeoX RoPE
+// (k_rope, :483-498) by one warp; result (fp32 of bf16) into o[HD]
+template <int E>
+__device__ void head_norm_rope(const bf16_t* __restrict__ x, const float* __restrict__ w,
+                               const float* cs, const float* sn, int half, float eps, float* o) {
+  const int lane = threadIdx.x & 31;
+  constexpr int HD = 32 * E;
+  float v[E], ss[E];
+#pragma unroll
+  for (int j = 0; j < E; j++) { v[j] = pb_bf2f(x[lane * E + j]); ss[j] = __fmul_rn(v[j], v[j]); }
+#pragma unroll
+  for (int width = E; width > 1; width >>= 1)
+#pragma unroll
+    for (int i = 0; i < width / 2; i++) ss[i] = __fadd_rn(ss[2 * i], ss[2 * i + 1]);
+  float s = pb_warp_tree(__fadd_rn(ss[0], 0.0f));
+  s = __shfl_sync(0xffffffffu, s, 0);
+  const float rs = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fmul_rn(s, __fdiv_rn(1.0f, (float)HD)), eps)));
+#pragma unroll
+  for (int j = 0; j < E; j++) {
+    const int i = lane * E + j;
+    o[i] = pb_bf2f(pb_f2bf(__fmul_rn(w[i], pb_bf2f(pb_f2bf(__fmul_rn(v[j], rs))))));
+  }
+  __syncwarp();
+  float lo_n[E], hi_n[E];
+#pragma unroll
+  for (int j = 0; j < E; j++) {
+    const int i = lane * E + j;   // i < HD/2 covers the pairs when i < half
+    if (i < half) {
+      const float lo = o[i], hi = o[i + HD / 2];
+      lo_n[j] = pb_bf2f(pb_f2bf(__fadd_rn(__fmul_rn(lo, cs[i]), __fmul_rn(-hi, sn[i]))));
+      hi_n[j] = pb_bf2f(pb_f2bf(__fadd_rn(__fmul_rn(hi, cs[i]), __fmul_rn(lo, sn[i]))));
+    }
+  }
+  __syncwarp();
+#pragma unroll
+  for (int j = 0; j < E; j++) {
+    const int i = lane * E + j;
+    if (i < half) { o[i] = lo_n[j]; o[i + HD / 2] = hi_n[j]; }
+  }
+  __syncwarp();
+}
+
+// k_attn_head (lfm3_nanode.cu:503-602) for one q head over the fp16 cache,
+// with the q/k prologue and the sigmoid gate (k_sigmoid_gate, :852-864) fused.
+// The current position's k/v are used from shared memory (the CTA of the
+// group's first q head also appends them to the cache), so no CTA reads a
+// cache row another CTA of this launch writes.
+template <int E>
+__global__ void __launch_bounds__(256) k_attn(AttnArgs a) {
+  constexpr int HD = 32 * E;
+  extern __shared__ __align__(16) float sl[];     // scores [max_ctx]
+  __shared__ float qv[HD], kv[HD], vv[HD];
+  __shared__ float red[8];
+  __shared__ float segred[8][HD];
+  const int h = blockIdx.x, t = threadIdx.x, lane = t & 31, wid = t >> 5;
+  const int grp = a.nh / a.nkv, kvh = h / grp;
+  pb_grid_launch_dependents();
+  pb_grid_wait();
+  const int pos = a.ctl->pos;
+  const int npos = pos + 1;
+  const int lo = (a.win > 0 && npos > a.win) ? npos - a.win : 0;
+  const int np = npos - lo;
+  const float* cs = a.rope_cos + (size_t)pos * a.half;
+  const float* sn = a.rope_sin + (size_t)pos * a.half;
+  const size_t qoff = 0, koff = (size_t)a.nh * HD, voff = koff + (size_t)a.nkv * HD,
+               goff = voff + (size_t)a.nkv * HD;
+  if (wid == 0) head_norm_rope<E>(a.qkvg + qoff + (size_t)h * HD, a.qnorm, cs, sn, a.half, a.eps, qv);
+  if (wid == 1) {
+    head_norm_rope<E>(a.qkvg + koff + (size_t)kvh * HD, a.knorm, cs, sn, a.half, a.eps, kv);
+#pragma unroll
+    for (int j = 0; j < E; j++) {
+      const int i = lane * E + j;
+      const unsigned short k16 = pb_f2h(kv[i]);
+      kv[i] = pb_h2f(k16);
+      if (h % grp == 0) a.kc[((size_t)pos * a.nkv + kvh) * HD + i] = k16;
+    }
+  }
+  if (wid == 2) {
+#pragma unroll
+    for (int j = 0; j < E; j++) {
+      const int i = lane * E + j;
+      const unsigned short v16 = pb_f2h(pb_bf2f(a.qkvg[voff + (size_t)kvh * HD + i]));
+      vv[i] = pb_h2f(v16);
+      if (h % grp == 0) a.vc[((size_t)pos * a.nkv + kvh) * HD + i] = v16;
+    }
+  }
+  __syncthreads();
+  // scores: position p by warp (p - lo) % 8, lane chains over its E dims
+  float ql[E];
+#pragma unroll
+  for (int j = 0; j < E; j++) ql[j] = qv[lane * E + j];
+  for (int p = lo + wid; p < npos; p += 8) {
+    float kl[E];
+    if (p == pos) {
+#pragma unroll
+      for (int j = 0; j < E; j++) kl[j] = kv[lane * E + j];
+    } else {
+      const unsigned short* kr = a.kc + ((size_t)p * a.nkv + kvh) * HD + lane * E;
+#pragma unroll
+      for (int j = 0; j < E; j++) kl[j] = pb_h2f(kr[j]);
+    }
+    float s = 0.0f;
+#pragma unroll
+    for (int j = 0; j < E; j++) s = __fadd_rn(s, __fmul_rn(ql[j], kl[j]));
+    s = pb_warp_tree(s);
+    if (lane == 0) sl[p - lo] = __fmul_rn(s, a.scaling);
+  }
+  __syncthreads();
+  float mx = -1e30f;
+  for (int i = t; i < np; i += 256) mx = fmaxf(mx, sl[i]);
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_down_sync(0xffffffffu, mx, o));
+  if (lane == 0) red[wid] = mx;
+  __syncthreads();
+  float m = red[0];
+#pragma unroll
+  for (int i = 1; i < 8; i++) m = fmaxf(m, red[i]);
+  __syncthreads();
+  float sum = 0.0f;
+  for (int i = t; i < np; i += 256) {
+    const float e = pb_expf(__fadd_rn(sl[i], -m));
+    sl[i] = e;
+    sum = __fadd_rn(sum, e);
+  }
+  sum = pb_warp_tree(sum);
+  if (lane == 0) red[wid] = sum;
+  __syncthreads();
+  // 8-lane shuffle-down tree: ((r0+r4)+(r2+r6))+((r1+r5)+(r3+r7))
+  const float tot = __fadd_rn(__fadd_rn(__fadd_rn(red[0], red[4]), __fadd_rn(red[2], red[6])),
+                              __fadd_rn(__fadd_rn(red[1], red[5]), __fadd_rn(red[3], red[7])));
+  const float inv = __fdiv_rn(1.0f, tot);
+  // P.V: segment = warp, lane owns dims lane*E .. +E
+  float acc[E];
+#pragma unroll
+  for (int j = 0; j < E; j++) acc[j] = 0.0f;
+  for (int p = wid; p < np; p += 8) {
+    const float w = __fmul_rn(sl[p], inv);
+    const int ap = lo + p;
+    float vl[E];
+    if (ap == pos) {
+#pragma unroll
+      for (int j = 0; j < E; j++) vl[j] = vv[lane * E + j];
+    } else {
+      const unsigned short* vr = a.vc + ((size_t)ap * a.nkv + kvh) * HD + lane * E;
+#pragma unroll
+      for (int j = 0; j < E; j++) vl[j] = pb_h2f(vr[j]);
+    }
+#pragma unroll
+    for (int j = 0; j < E; j++) acc[j] = __fadd_rn(acc[j], __fmul_rn(w, vl[j]));
+  }
+#pragma unroll
+  for (int j = 0; j < E; j++) segred[wid][lane * E + j] = acc[j];
+  __syncthreads();
+  if (t < HD) {
+    const float o = __fadd_rn(__fadd_rn(__fadd_rn(segred[0][t], segred[1][t]), __fadd_rn(segred[2][t], segred[3][t])),
+                              __fadd_rn(__fadd_rn(segred[4][t], segred[5][t]), __fadd_rn(segred[6][t], segred[7][t])));
+    const float sg = pb_sigmoid(pb_bf2f(a.qkvg[goff + h]));
+    a.out[(size_t)h * HD + t] = pb_f2bf(__fmul_rn(pb_bf2f(pb_f2bf(o)), sg));
+  }
+}
+
+// residual tail for the standalone layer step: x = R + bf16(rms(h, w))
+__global__ void __launch_bounds__(256) k_tail(StepArgs a) {
+  extern __shared__ __align__(16) float smem[];
+  __shared__ float red[8];
+  pb_grid_launch_dependents();
+  pb_grid_wait();
+  float* sx = smem;
+  float* sa = sx + a.K + (a.K >> 5);
+  step_prologue(a, sx, sa, sa + a.H, red);
+}
+
+// ----------------------------------------------------------- host model
+struct Layer {
+  bool attn = false;
+  pb_q8 first;           // q|k|v|gate or in_proj
+  pb_q8 mix;             // o_proj or out_proj
+  pb_q8 w13;             // w1 row i at 2i, w3 row i at 2i+1
+  pb_q8 w2;
+  float* op_norm = nullptr; float* post_op_norm = nullptr;
+  float* ffn_norm = nullptr; float* post_ffn_norm = nullptr;
+  float* q_norm = nullptr; float* k_norm = nullptr;
+  float* taps = nullptr;
+  int attn_idx = -1, conv_idx = -1;
+};
+
+struct Tensor {
+  std::string name;
+  int dtype = -1;
+  std::vector<long long> ne;
+  size_t off = 0, nc = 0, ns = 0;
+  uint32_t crc = 0;
+};
+
+}  // namespace
+
+struct pb_model {
+  int device = 0;
+  int H = 0, F = 0, L = 0, NH = 0, NKV = 0, HD = 0, V = 0, W = 3, n_attn = 0, win = 0;
+  float theta = 1e6f, partial = 1.0f, eps = 1e-5f;
+  int sdt = PB_DT_F16;
+  std::vector<Layer> layers;
+  pb_q8 head;
+  float* final_norm = nullptr;
+  char* arena = nullptr;
+  size_t arena_bytes = 0;
+  std::vector<Tensor> table;
+  std::vector<float> invf;
+  uint64_t weight_bytes = 0;
+  bool decode_ok = true;     // every decode tensor in the streaming layout
+};
+
+struct pb_state {
+  pb_model* m = nullptr;
+  int max_ctx = 0;
+  unsigned short* kv = nullptr;   // [n_attn][2][max_ctx][NKV][HD]
+  bf16_t* ring = nullptr;         // [n_conv][W][H]
+  float* rope_cos = nullptr;      // [max_ctx][half]
+  float* rope_sin = nullptr;
+  bf16_t* res[3] = {nullptr, nullptr, nullptr};
+  bf16_t* h_first = nullptr;      // q|k|v|gate or in_proj output
+  bf16_t* h_attn = nullptr;
+  bf16_t* h_mix = nullptr;
+  bf16_t* h_u = nullptr;
+  bf16_t* h_w2 = nullptr;
+  float* logits = nullptr;
+  Ctl* ctl = nullptr;
+  Ctl* h_ctl = nullptr;           // pinned host mirror for token/pos uploads
+  char* mem = nullptr;
+  size_t mem_bytes = 0;
+  cudaGraph_t graph = nullptr;
+  cudaGraphExec_t exec = nullptr;
+  cudaStream_t graph_stream = nullptr;
+  int graph_res = 0;              // residual buffer holding the final residual
+  uint64_t graph_launches = 0;    // kernels per graph replay
+};
+
+namespace {
+
+size_t align256(size_t x) { return (x + 255) & ~(size_t)255; }
+
+int half_rot(const pb_model* m) { return (int)((double)m->partial * m->HD) / 2; }
+
+// ---- launches ---------------------------------------------------------------
+size_t step_smem(int K, int H) { return (size_t)(K + K / 32 + 2 * H) * sizeof(float); }
+
+template <int NCH, bool F32S, int EPI>
+int launch_step_t(const StepArgs& a, cudaStream_t st, bool pdl) {
+  const size_t smem = step_smem(a.K, a.H);
+  static bool set = false;
+  if (!set) {
+    cudaFuncSetAttribute(k_step<NCH, F32S, EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize, 96 * 1024);
+    set = true;
+  }
+  if (smem > 96 * 1024) return pb_set_error(PB_ENOTSUP, "step: K=%d H=%d needs too much shared memory", a.K, a.H);
+  constexpr int RB = (8 / NCH) * 2;
+  const int nrb = (a.N + RB - 1) / RB;
+  int grid = pb_num_sms();
+  if (grid > nrb) grid = nrb;
+  if (EPI == EPI_ARGMAX && grid > MAX_CTA) grid = MAX_CTA;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(256);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl ? 1 : 0;
+  cudaError_t e = cudaLaunchKernelEx(&cfg, k_step<NCH, F32S, EPI>, a);
+  if (e != cudaSuccess) return pb_set_error(PB_ECUDA, "launch k_step: %s", cudaGetErrorString(e));
+  pb_count_launch();
+  return PB_OK;
+}
+
+template <bool F32S, int EPI>
+int launch_step_n(int nch, const StepArgs& a, cudaStream_t st, bool pdl) {
+  switch (nch) {
+    case 1: return launch_step_t<1, F32S, EPI>(a, st, pdl);
+    case 2: return launch_step_t<2, F32S, EPI>(a, st, pdl);
+    case 4: return launch_step_t<4, F32S, EPI>(a, st, pdl);
+    case 8: return launch_step_t<8, F32S, EPI>(a, st, pdl);
+  }
+  return pb_set_error(PB_ENOTSUP, "step: %d chunks", nch);
+}
+
+int launch_step(const pb_q8& w, int epi, StepArgs a, cudaStream_t st, bool pdl) {
+  a.codes = reinterpret_cast<const uint4*>(w.codes);
+  a.scales = w.scales;
+  a.N = w.N;
+  a.K = w.K;
+  const bool f = w.sdt == PB_DT_F32;
+  if (epi == EPI_BF16) return f ? launch_step_n<true, EPI_BF16>(w.nch, a, st, pdl) : launch_step_n<false, EPI_BF16>(w.nch, a, st, pdl);
+  if (epi == EPI_SILU) return f ? launch_step_n<true, EPI_SILU>(w.nch, a, st, pdl) : launch_step_n<false, EPI_SILU>(w.nch, a, st, pdl);
+  return f ? launch_step_n<true, EPI_ARGMAX>(w.nch, a, st, pdl) : launch_step_n<false, EPI_ARGMAX>(w.nch, a, st, pdl);
+}
+
+int launch_attn(const pb_model* m, pb_state* s, int layer, cudaStream_t st, bool pdl) {
+  const Layer& Ly = m->layers[layer];
+  AttnArgs a;
+  a.qkvg = s->h_first;
+  a.qnorm = Ly.q_norm;
+  a.knorm = Ly.k_norm;
+  a.rope_cos = s->rope_cos;
+  a.rope_sin = s->rope_sin;
+  const size_t per = (size_t)s->max_ctx * m->NKV * m->HD;
+  a.kc = s->kv + (size_t)Ly.attn_idx * 2 * per;
+  a.vc = a.kc + per;
+  a.out = s->h_attn;
+  a.ctl = s->ctl;
+  a.nh = m->NH; a.nkv = m->NKV; a.half = half_rot(m); a.win = m->win; a.max_ctx = s->max_ctx;
+  a.scaling = 1.0f / sqrtf((float)m->HD);
+  a.eps = m->eps;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(m->NH);
+  cfg.blockDim = dim3(256);
+  cfg.dynamicSmemBytes = (size_t)s->max_ctx * sizeof(float);
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl ? 1 : 0;
+  cudaError_t e;
+  switch (m->HD) {
+    case 32: cudaFuncSetAttribute(k_attn<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, 160 * 1024);
+             e = cudaLaunchKernelEx(&cfg, k_attn<1>, a); break;
+    case 64: cudaFuncSetAttribute(k_attn<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, 160 * 1024);
+             e = cudaLaunchKernelEx(&cfg, k_attn<2>, a); break;
+    case 128: cudaFuncSetAttribute(k_attn<4>, cudaFuncAttributeMaxDynamicSharedMemorySize, 160 * 1024);
+              e = cudaLaunchKernelEx(&cfg, k_attn<4>, a); break;
+    default: return pb_set_error(PB_ENOTSUP, "attention head_dim %d", m->HD);
+  }
+  if (e != cudaSuccess) return pb_set_error(PB_ECUDA, "launch k_attn: %s", cudaGetErrorString(e));
+  pb_count_launch();
+  return PB_OK;
+}
+
+StepArgs base_args(const pb_model* m, pb_state* s) {
+  StepArgs a = {};
+  a.H = m->H;
+  a.eps = m->eps;
+  a.ctl = s->ctl;
+  a.convw = m->W;
+  return a;
+}
+
+// Enqueue one layer. `cur` is the residual buffer index holding x on entry;
+// on exit it names the buffer holding the layer's pre-FFN residual (the
+// post-FFN add is folded into whoever consumes h_w2 next).
+// first_mode: PRO_EMBED (layer 0 of a token), PRO_ADDNORM with hin = h_w2
+// (layer L > 0 of a token) or PRO_ADDNORM with hin = null (standalone step).
+int enqueue_layer(const pb_model* m, pb_state* s, int L, int& cur, int first_mode, bool add_prev,
+                  const bf16_t* x_in, cudaStream_t st, bool pdl, uint64_t& nk) {
+  const Layer& Ly = m->layers[L];
+  int rc;
+  StepArgs a = base_args(m, s);
+  a.pro = first_mode;
+  a.wnorm = Ly.op_norm;
+  a.y = s->h_first;
+  if (first_mode == PRO_EMBED) {
+    a.emb_codes = reinterpret_cast<const uint4*>(m->head.codes);
+    a.emb_scales = m->head.scales;
+    a.emb_nch = m->head.nch;
+    a.emb_f32 = m->head.sdt == PB_DT_F32;
+    a.rout = s->res[cur];
+  } else {
+    a.xin = x_in ? x_in : s->res[cur];
+    if (add_prev) {
+      a.hin = s->h_w2;
+      a.wpost = m->layers[L - 1].post_ffn_norm;
+      a.rout = s->res[cur ^ 1];
+      cur ^= 1;
+    }
+  }
+  if ((rc = launch_step(Ly.first, EPI_BF16, a, st, pdl))) return rc;
+  nk++;
+  if (Ly.attn) {
+    if ((rc = launch_attn(m, s, L, st, pdl))) return rc;
+    nk++;
+    StepArgs b = base_args(m, s);
+    b.pro = PRO_PLAIN;
+    b.xin = s->h_attn;
+    b.y = s->h_mix;
+    if ((rc = launch_step(Ly.mix, EPI_BF16, b, st, pdl))) return rc;
+    nk++;
+  } else {
+    StepArgs b = base_args(m, s);
+    b.pro = PRO_CONV;
+    b.xin = s->h_first;
+    b.ring = s->ring + (size_t)Ly.conv_idx * m->W * m->H;
+    b.taps = Ly.taps;
+    b.y = s->h_mix;
+    if ((rc = launch_step(Ly.mix, EPI_BF16, b, st, pdl))) return rc;
+    nk++;
+  }
+  // post_operator_norm + residual + ffn_norm -> w1|w3 (+ SiLU*mul)
+  StepArgs c = base_args(m, s);
+  c.pro = PRO_ADDNORM;
+  c.xin = (first_mode != PRO_EMBED && !add_prev && x_in) ? x_in : s->res[cur];
+  c.hin = s->h_mix;
+  c.wpost = Ly.post_op_norm;
+  c.wnorm = Ly.ffn_norm;
+  c.rout = s->res[cur ^ 1];
+  cur ^= 1;
+  c.y = s->h_u;
+  if ((rc = launch_step(Ly.w13, EPI_SILU, c, st, pdl))) return rc;
+  nk++;
+  StepArgs d = base_args(m, s);
+  d.pro = PRO_PLAIN;
+  d.xin = s->h_u;
+  d.y = s->h_w2;
+  if ((rc = launch_step(Ly.w2, EPI_BF16, d, st, pdl))) return rc;
+  nk++;
+  return PB_OK;
+}
+
+int enqueue_token(const pb_model* m, pb_state* s, cudaStream_t st, bool pdl, int& final_res, uint64_t& nk) {
+  int cur = 0;
+  int rc;
+  for (int L = 0; L < m->L; L++) {
+    if ((rc = enqueue_layer(m, s, L, cur, L == 0 ? PRO_EMBED : PRO_ADDNORM, L > 0, nullptr, st, pdl, nk))) return rc;
+  }
+  StepArgs h = base_args(m, s);
+  h.pro = PRO_ADDNORM;
+  h.xin = s->res[cur];
+  h.hin = s->h_w2;
+  h.wpost = m->layers[m->L - 1].post_ffn_norm;
+  h.wnorm = m->final_norm;
+  h.rout = s->res[cur ^ 1];
+  final_res = cur ^ 1;
+  h.y = s->logits;
+  if ((rc = launch_step(m->head, EPI_ARGMAX, h, st, pdl))) return rc;
+  nk++;
+  return PB_OK;
+}
+
+int build_graph(pb_state* s) {
+  if (s->exec) return PB_OK;
+  pb_model* m = s->m;
+  if (!s->graph_stream) PB_TRY_CUDA(cudaStreamCreateWithFlags(&s->graph_stream, cudaStreamNonBlocking));
+  cudaStream_t st = s->graph_stream;
+  PB_TRY_CUDA(cudaStreamBeginCapture(st, cudaStreamCaptureModeThreadLocal));
+  uint64_t nk = 0;
+  int fr = 0;
+  pb_set_capturing(true);     // captured launches are counted when the graph runs
+  int rc = enqueue_token(m, s, st, true, fr, nk);
+  pb_set_capturing(false);
+  cudaGraph_t g = nullptr;
+  cudaError_t e = cudaStreamEndCapture(st, &g);
+  if (rc) { if (g) cudaGraphDestroy(g); return rc; }
+  if (e != cudaSuccess) return pb_set_error(PB_ECUDA, "graph capture: %s", cudaGetErrorString(e));
+  cudaGraphExec_t ex = nullptr;
+  e = cudaGraphInstantiate(&ex, g, 0);
+  if (e != cudaSuccess) { cudaGraphDestroy(g); return pb_set_error(PB_ECUDA, "graph instantiate: %s", cudaGetErrorString(e)); }
+  s->graph = g;
+  s->exec = ex;
+  s->graph_res = fr;
+  s->graph_launches = nk;
+  return PB_OK;
+}
+
+// ---- loader -----------------------------------------------------------------
+int read_all(FILE* f, void* dst, size_t n) {
+  return fread(dst, 1, n, f) == n ? PB_OK : PB_EIO;
+}
+
+const Tensor* find(const pb_model* m, const std::string& name) {
+  for (auto& t : m->table) if (t.name == name) return &t;
+  return nullptr;
+}
+
+std::string lname(int L, const char* suf) {
+  char b[160];
+  snprintf(b, sizeof b, "lfm.model.layers.%d.%s", L, suf);
+  return b;
+}
+
+}  // namespace
+
+// ============================================================== C ABI
+extern "C" int pb_open(const char* path, int device, pb_model** out) {
+  if (!path || !out) return pb_set_error(PB_EINVAL, "pb_open: null argument");
+  *out = nullptr;
+  FILE* f = fopen(path, "rb");
+  if (!f) return pb_set_error(PB_EIO, "pb_open: cannot open %s", path);
+  char magic[8];
+  uint32_t hl = 0;
+  if (fread(magic, 1, 8, f) != 8 || memcmp(magic, "LFM3Q8\x01\x00", 8) != 0) {
+    fclose(f);
+    return pb_set_error(PB_EFORMAT, "pb_open: bad magic in %s", path);
+  }
+  if (fread(&hl, 4, 1, f) != 1 || hl == 0 || hl > (1u << 30)) {
+    fclose(f);
+    return pb_set_error(PB_EFORMAT, "pb_open: bad header length");
+  }
+  std::string js(hl, '\0');
+  if (read_all(f, &js[0], hl)) { fclose(f); return pb_set_error(PB_EIO, "pb_open: short header"); }
+  const size_t base = 8 + 4 + (size_t)hl;
+  pbjson::Value root;
+  pbjson::Parser P(js.data(), js.size());
+  if (!P.parse(root) || root.kind != pbjson::Value::OBJ) {
+    fclose(f);
+    return pb_set_error(PB_EFORMAT, "pb_open: header JSON: %s", P.error());
+  }
+  const pbjson::Value* cfg = root.get("cfg");
+  const pbjson::Value* table = root.get("table");
+  if (!cfg || cfg->kind != pbjson::Value::OBJ || !table || table->kind != pbjson::Value::ARR) {
+    fclose(f);
+    return pb_set_error(PB_EFORMAT, "pb_open: header lacks cfg/table");
+  }
+  pb_model* m = new pb_model();
+  m->device = device;
+  auto cint = [&](const char* k, long long d) { const pbjson::Value* v = cfg->get(k); return v ? v->as_int(d) : d; };
+  auto cnum = [&](const char* k, double d) { const pbjson::Value* v = cfg->get(k); return v ? v->as_num(d) : d; };
+  m->H = (int)cint("hidden_size", 0);
+  m->F = (int)cint("intermediate_size", cint("block_ff_dim", 0));
+  m->L = (int)cint("num_hidden_layers", 0);
+  m->NH = (int)cint("num_attention_heads", 0);
+  m->NKV = (int)cint("num_key_value_heads", m->NH);
+  m->HD = (int)cint("head_dim", m->NH ? m->H / m->NH : 0);
+  m->V = (int)cint("vocab_size", 0);
+  m->W = (int)cint("conv_L_cache", 3);
+  m->win = (int)cint("sliding_window_decode", 0);
+  m->theta = (float)cnum("rope_theta", 1e6);
+  m->partial = (float)cnum("partial_rotary_factor", 1.0);
+  m->eps = (float)cnum("norm_eps", 1e-5);
+  const pbjson::Value* lt = cfg->get("layer_types");
+  auto bad = [&](int code, const char* msg) { fclose(f); delete m; return pb_set_error(code, "pb_open: %s", msg); };
+  if (m->H <= 0 || m->F <= 0 || m->L <= 0 || m->NH <= 0 || m->NKV <= 0 || m->HD <= 0 || m->V <= 0 || m->W <= 0)
+    return bad(PB_EFORMAT, "cfg lacks a positive hidden/intermediate/layers/heads/vocab/conv size");
+  if (!lt || lt->kind != pbjson::Value::ARR || (int)lt->arr.size() != m->L)
+    return bad(PB_EFORMAT, "cfg.layer_types must list every layer");
+  if (m->NH % m->NKV) return bad(PB_EFORMAT, "heads not a multiple of kv heads");
+  if (m->H % 256 || m->H > 4096) return bad(PB_ENOTSUP, "hidden size must be a multiple of 256 up to 4096");
+  // table
+  for (auto& rv : table->arr) {
+    Tensor t;
+    const pbjson::Value* nm = rv.get("name");
+    const pbjson::Value* ne = rv.get("ne");
+    if (!nm || nm->kind != pbjson::Value::STR || !ne || ne->kind != pbjson::Value::ARR)
+      return bad(PB_EFORMAT, "record without name/ne");
+    t.name = nm->str;
+    for (auto& d : ne->arr) t.ne.push_back(d.as_int(-1));
+    const pbjson::Value *dt = rv.get("dtype"), *of = rv.get("off"), *nc = rv.get("ncodes"), *ns = rv.get("nscales"), *cr = rv.get("crc");
+    if (!dt || !of || !nc || !cr) return bad(PB_EFORMAT, "record lacks dtype/off/ncodes/crc");
+    t.dtype = (int)dt->as_int(-1);
+    t.off = (size_t)of->as_int(0);
+    t.nc = (size_t)nc->as_int(0);
+    t.ns = ns ? (size_t)ns->as_int(0) : 0;
+    t.crc = (uint32_t)cr->as_int(0);
+    if (t.dtype == 1 || t.dtype == 8) {
+      if (t.ne.size() != 2 || t.ne[0] <= 0 || t.ne[1] <= 0 || t.ne[1] % 32)
+        return bad(PB_EFORMAT, ("Q8 tensor with bad shape: " + t.name).c_str());
+      const size_t want_s = (size_t)t.ne[0] * (t.ne[1] / 32) * (t.dtype == 1 ? 4 : 2);
+      if (t.nc != (size_t)t.ne[0] * t.ne[1] || t.ns != want_s)
+        return bad(PB_EFORMAT, ("Q8 tensor with inconsistent sizes: " + t.name).c_str());
+    } else if (t.dtype == 2) {
+      size_t n = 1;
+      for (auto d : t.ne) n *= (size_t)d;
+      if (t.nc != n * 4) return bad(PB_EFORMAT, ("f32 tensor with inconsistent size: " + t.name).c_str());
+    } else {
+      return bad(PB_ENOTSUP, ("tensor dtype not supported by this build: " + t.name).c_str());
+    }
+    m->table.push_back(t);
+  }
+  // layer types and per-layer tensors
+  m->layers.resize(m->L);
+  int sdt = -1;
+  auto q8shape = [&](const std::string& n, int& N, int& K) -> const Tensor* {
+    const Tensor* t = find(m, n);
+    if (!t || (t->dtype != 1 && t->dtype != 8)) return nullptr;
+    N = (int)t->ne[0]; K = (int)t->ne[1];
+    const int d = t->dtype == 1 ? PB_DT_F32 : PB_DT_F16;
+    if (sdt < 0) sdt = d;
+    else if (sdt != d) return nullptr;
+    return t;
+  };
+  int n_attn = 0, n_conv = 0;
+  for (int L = 0; L < m->L; L++) {
+    const pbjson::Value& v = lt->arr[L];
+    if (v.kind != pbjson::Value::STR) return bad(PB_EFORMAT, "layer_types entries must be strings");
+    m->layers[L].attn = v.str != "conv";
+    if (m->layers[L].attn) m->layers[L].attn_idx = n_attn++;
+    else m->layers[L].conv_idx = n_conv++;
+  }
+  m->n_attn = n_attn;
+  // arena plan
+  struct Piece { std::string name; pb_q8* dst; int rmul, radd; };
+  std::vector<Piece> q8pieces;
+  struct FPiece { std::string name; float** dst; size_t n; };
+  std::vector<FPiece> fpieces;
+  size_t need = 0;
+  auto plan_q8 = [&](pb_q8& w, int N, int K) {
+    w.N = N; w.K = K; w.owner = false;
+    w.layout = pb_q8_stream_ok(K) ? PB_Q8_STREAM : PB_Q8_ROWMAJOR;
+    w.nch = w.layout == PB_Q8_STREAM ? K / 2048 : 1;
+    need += align256((size_t)N * K);
+    need += align256((size_t)N * (K / 32) * 4);
+    if (w.layout != PB_Q8_STREAM) m->decode_ok = false;
+  };
+  const int H = m->H, F = m->F, NH = m->NH, NKV = m->NKV, HD = m->HD, W = m->W;
+  for (int L = 0; L < m->L; L++) {
+    Layer& Ly = m->layers[L];
+    int N, K;
+    if (Ly.attn) {
+      const char* nm[4] = {"self_attn.q_proj.weight", "self_attn.k_proj.weight", "self_attn.v_proj.weight",
+                           "self_attn.gate_proj.weight"};
+      const int want[4] = {NH * HD, NKV * HD, NKV * HD, NH};
+      int off = 0;
+      for (int i = 0; i < 4; i++) {
+        if (!q8shape(lname(L, nm[i]), N, K) || N != want[i] || K != H) return bad(PB_EFORMAT, (lname(L, nm[i]) + " missing or misshapen").c_str());
+      }
+      plan_q8(Ly.first, NH * HD + 2 * NKV * HD + NH, H);
+      for (int i = 0; i < 4; i++) { q8pieces.push_back({lname(L, nm[i]), &Ly.first, 1, off}); off += want[i]; }
+      if (!q8shape(lname(L, "self_attn.o_proj.weight"), N, K) || N != H || K != NH * HD) return bad(PB_EFORMAT, "o_proj missing or misshapen");
+      plan_q8(Ly.mix, H, NH * HD);
+      q8pieces.push_back({lname(L, "self_attn.o_proj.weight"), &Ly.mix, 1, 0});
+      fpieces.push_back({lname(L, "self_attn.q_norm.weight"), &Ly.q_norm, (size_t)HD});
+      fpieces.push_back({lname(L, "self_attn.k_norm.weight"), &Ly.k_norm, (size_t)HD});
+    } else {
+      if (!q8shape(lname(L, "conv.in_proj.weight"), N, K) || N != 3 * H || K != H) return bad(PB_EFORMAT, "in_proj missing or misshapen");
+      plan_q8(Ly.first, 3 * H, H);
+      q8pieces.push_back({lname(L, "conv.in_proj.weight"), &Ly.first, 1, 0});
+      if (!q8shape(lname(L, "conv.out_proj.weight"), N, K) || N != H || K != H) return bad(PB_EFORMAT, "out_proj missing or misshapen");
+      plan_q8(Ly.mix, H, H);
+      q8pieces.push_back({lname(L, "conv.out_proj.weight"), &Ly.mix, 1, 0});
+      fpieces.push_back({lname(L, "conv.conv.weight"), &Ly.taps, (size_t)H * W});
+    }
+    if (!q8shape(lname(L, "feed_forward.w1.weight"), N, K) || N != F || K != H) return bad(PB_EFORMAT, "w1 missing or misshapen");
+    if (!q8shape(lname(L, "feed_forward.w3.weight"), N, K) || N != F || K != H) return bad(PB_EFORMAT, "w3 missing or misshapen");
+    plan_q8(Ly.w13, 2 * F, H);
+    q8pieces.push_back({lname(L, "feed_forward.w1.weight"), &Ly.w13, 2, 0});
+    q8pieces.push_back({lname(L, "feed_forward.w3.weight"), &Ly.w13, 2, 1});
+    if (!q8shape(lname(L, "feed_forward.w2.weight"), N, K) || N != H || K != F) return bad(PB_EFORMAT, "w2 missing or misshapen");
+    plan_q8(Ly.w2, H, F);
+    q8pieces.push_back({lname(L, "feed_forward.w2.weight"), &Ly.w2, 1, 0});
+    fpieces.push_back({lname(L, "operator_norm.weight"), &Ly.op_norm, (size_t)H});
+    fpieces.push_back({lname(L, "post_operator_norm.weight"), &Ly.post_op_norm, (size_t)H});
+    fpieces.push_back({lname(L, "ffn_norm.weight"), &Ly.ffn_norm, (size_t)H});
+    fpieces.push_back({lname(L, "post_ffn_norm.weight"), &Ly.post_ffn_norm, (size_t)H});
+  }
+  {
+    int N, K;
+    if (!q8shape("lfm.model.embed_tokens.weight", N, K) || N != m->V || K != H) return bad(PB_EFORMAT, "embed_tokens missing or misshapen");
+    plan_q8(m->head, m->V, H);
+    q8pieces.push_back({"lfm.model.embed_tokens.weight", &m->head, 1, 0});
+    fpieces.push_back({"lfm.model.embedding_norm.weight", &m->final_norm, (size_t)H});
+  }
+  for (auto& fp : fpieces) {
+    const Tensor* t = find(m, fp.name);
+    if (!t || t->dtype != 2 || t->nc != fp.n * 4) return bad(PB_EFORMAT, (fp.name + " missing or misshapen").c_str());
+    need += align256(fp.n * 4);
+  }
+  m->sdt = sdt < 0 ? PB_DT_F16 : sdt;
+  if (device < 0) {
+    // validate only: every payload's size and CRC, no GPU touched
+    std::vector<char> buf;
+    for (auto& t : m->table) {
+      buf.resize(t.nc + t.ns);
+      if (fseeko(f, (off_t)(base + t.off), SEEK_SET) != 0 || read_all(f, buf.data(), buf.size()))
+        return bad(PB_EIO, ("short read in " + t.name).c_str());
+      const uint32_t c = (uint32_t)crc32(0L, reinterpret_cast<const Bytef*>(buf.data()), (uInt)buf.size());
+      if (c != t.crc) return bad(PB_ECRC, ("CRC mismatch in " + t.name).c_str());
+    }
+    fclose(f);
+    delete m;
+    return PB_OK;
+  }
+  if (cudaSetDevice(device) != cudaSuccess) {
+    cudaGetLastError();
+    return bad(PB_ECUDA, "cudaSetDevice failed");
+  }
+  // allocate
+  if (cudaMalloc(&m->arena, need) != cudaSuccess) {
+    cudaGetLastError();
+    return bad(PB_ENOMEM, "cannot allocate the weight arena");
+  }
+  m->arena_bytes = need;
+  size_t cursor = 0;
+  std::vector<pb_q8*> assigned;
+  auto assign = [&](pb_q8* w) {
+    for (auto* p : assigned) if (p == w) return;
+    w->sdt = m->sdt;
+    w->codes = reinterpret_cast<int8_t*>(m->arena + cursor);
+    cursor += align256((size_t)w->N * w->K);
+    w->scales = m->arena + cursor;
+    cursor += align256((size_t)w->N * (w->K / 32) * 4);
+    assigned.push_back(w);
+  };
+  for (auto& p : q8pieces) assign(p.dst);
+  for (auto& fp : fpieces) {
+    *fp.dst = reinterpret_cast<float*>(m->arena + cursor);
+    cursor += align256(fp.n * 4);
+  }
+  // stream the payloads: read, CRC, upload, pack
+  size_t maxb = 0;
+  for (auto& t : m->table) maxb = std::max(maxb, t.nc + t.ns);
+  char* host = nullptr;
+  char* stage = nullptr;
+  cudaStream_t st = nullptr;
+  int rc = PB_OK;
+  if (cudaMallocHost(&host, maxb) != cudaSuccess || cudaMalloc(&stage, maxb) != cudaSuccess ||
+      cudaStreamCreateWithFlags(&st, cudaStreamNonBlocking) != cudaSuccess) {
+    cudaGetLastError();
+    rc = pb_set_error(PB_ENOMEM, "pb_open: staging buffers");
+  }
+  auto load = [&](const Tensor* t) -> int {
+    if (fseeko(f, (off_t)(base + t->off), SEEK_SET) != 0) return pb_set_error(PB_EIO, "seek %s", t->name.c_str());
+    if (cudaStreamSynchronize(st) != cudaSuccess) return pb_set_error(PB_ECUDA, "upload sync");
+    if (read_all(f, host, t->nc + t->ns)) return pb_set_error(PB_EIO, "short read in %s", t->name.c_str());
+    const uint32_t c = (uint32_t)crc32(0L, reinterpret_cast<const Bytef*>(host), (uInt)(t->nc + t->ns));
+    if (c != t->crc) return pb_set_error(PB_ECRC, "CRC mismatch in %s: file %08x, table %08x", t->name.c_str(), c, t->crc);
+    PB_TRY_CUDA(cudaMemcpyAsync(stage, host, t->nc + t->ns, cudaMemcpyHostToDevice, st));
+    return PB_OK;
+  };
+  for (size_t i = 0; rc == PB_OK && i < q8pieces.size(); i++) {
+    const Tensor* t = find(m, q8pieces[i].name);
+    if ((rc = load(t)) != PB_OK) break;
+    rc = pb_q8_pack_into(q8pieces[i].dst, reinterpret_cast<int8_t*>(stage), stage + t->nc, st,
+                         (int)t->ne[0], q8pieces[i].rmul, q8pieces[i].radd);
+    m->weight_bytes += t->nc + (size_t)t->ne[0] * (t->ne[1] / 32) * (m->sdt == PB_DT_F32 ? 4 : 2);
+  }
+  for (size_t i = 0; rc == PB_OK && i < fpieces.size(); i++) {
+    const Tensor* t = find(m, fpieces[i].name);
+    if ((rc = load(t)) != PB_OK) break;
+    if (cudaMemcpyAsync(*fpieces[i].dst, stage, t->nc, cudaMemcpyDeviceToDevice, st) != cudaSuccess)
+      rc = pb_set_error(PB_ECUDA, "upload %s", t->name.c_str());
+    m->weight_bytes += t->nc;
+  }
+  if (rc == PB_OK && cudaStreamSynchronize(st) != cudaSuccess)
+    rc = pb_set_error(PB_ECUDA, "pb_open: %s", cudaGetErrorString(cudaGetLastError()));
+  if (host) cudaFreeHost(host);
+  if (stage) cudaFree(stage);
+  if (st) cudaStreamDestroy(st);
+  fclose(f);
+  if (rc != PB_OK) { cudaFree(m->arena); delete m; return rc; }
+  m->invf.resize(m->HD / 2);
+  {
+    const int angles = (int)((double)m->partial * m->HD) / 2;
+    for (int i = 0; i < m->HD / 2; i++)
+      m->invf[i] = (i < angles) ? 1.0f / powf(m->theta, (float)(2 * i) / (float)m->HD) : 0.0f;
+  }
+  *out = m;
+  return PB_OK;
+}
+
+extern "C" int pb_close(pb_model* m) {
+  if (!m) return PB_OK;
+  cudaFree(m->arena);
+  delete m;
+  return PB_OK;
+}
+
+extern "C" int pb_model_get_info(const pb_model* m, pb_model_info* info) {
+  if (!m || !info) return pb_set_error(PB_EINVAL, "pb_model_get_info: null argument");
+  info->hidden = m->H; info->inter = m->F; info->n_layers = m->L; info->n_heads = m->NH;
+  info->n_kv = m->NKV; info->head_dim = m->HD; info->vocab = m->V; info->conv_w = m->W;
+  info->n_attn = m->n_attn; info->sliding_window = m->win;
+  info->rope_theta = m->theta; info->rope_partial = m->partial; info->norm_eps = m->eps;
+  info->weight_bytes = m->weight_bytes;
+  return PB_OK;
+}
+
+extern "C" int pb_tensor_id(const pb_model* m, const char* name) {
+  if (!m || !name) return pb_set_error(PB_EINVAL, "pb_tensor_id: null argument");
+  for (size_t i = 0; i < m->table.size(); i++)
+    if (m->table[i].name == name) return (int)i;
+  return pb_set_error(PB_EINVAL, "pb_tensor_id: no tensor %s", name);
+}
+
+extern "C" int pb_state_create(pb_model* m, int max_ctx, pb_state** out) {
+  if (!m || !out || max_ctx <= 0) return pb_set_error(PB_EINVAL, "pb_state_create: bad argument");
+  *out = nullptr;
+  if (!m->decode_ok) return pb_set_error(PB_ENOTSUP, "decode needs every matrix K to be a multiple of 2048");
+  if ((size_t)max_ctx * 4 > 160 * 1024) return pb_set_error(PB_ENOTSUP, "max_ctx %d too large", max_ctx);
+  PB_TRY_CUDA(cudaSetDevice(m->device));
+  pb_state* s = new pb_state();
+  s->m = m;
+  s->max_ctx = max_ctx;
+  const int H = m->H, n_conv = m->L - m->n_attn, half = half_rot(m);
+  const size_t kvb = (size_t)m->n_attn * 2 * max_ctx * m->NKV * m->HD * 2;
+  const size_t ringb = (size_t)n_conv * m->W * H * 2;
+  const size_t ropeb = (size_t)max_ctx * (half > 0 ? half : 1) * 4;
+  const size_t firstn = std::max((size_t)3 * H, (size_t)m->NH * m->HD + 2 * (size_t)m->NKV * m->HD + m->NH);
+  size_t sizes[] = {kvb, ringb, ropeb, ropeb, (size_t)H * 2, (size_t)H * 2, (size_t)H * 2, firstn * 2,
+                    (size_t)m->NH * m->HD * 2, (size_t)H * 2, (size_t)m->F * 2, (size_t)H * 2,
+                    (size_t)m->V * 4, sizeof(Ctl)};
+  size_t tot = 0;
+  for (size_t x : sizes) tot += align256(x);
+  if (cudaMalloc(&s->mem, tot) != cudaSuccess) { cudaGetLastError(); delete s; return pb_set_error(PB_ENOMEM, "pb_state_create: %zu bytes", tot); }
+  s->mem_bytes = tot;
+  char* p = s->mem;
+  void** slots[] = {(void**)&s->kv, (void**)&s->ring, (void**)&s->rope_cos, (void**)&s->rope_sin,
+                    (void**)&s->res[0], (void**)&s->res[1], (void**)&s->res[2], (void**)&s->h_first,
+                    (void**)&s->h_attn, (void**)&s->h_mix, (void**)&s->h_u, (void**)&s->h_w2,
+                    (void**)&s->logits, (void**)&s->ctl};
+  for (size_t i = 0; i < sizeof(sizes) / sizeof(sizes[0]); i++) { *slots[i] = p; p += align256(sizes[i]); }
+  if (cudaMallocHost(&s->h_ctl, sizeof(Ctl)) != cudaSuccess) {
+    cudaGetLastError(); cudaFree(s->mem); delete s;
+    return pb_set_error(PB_ENOMEM, "pb_state_create: pinned control block");
+  }
+  // RoPE table on the host: angle (float)pos * invf[i] in fp32 (lfm3_nanode.cu:492),
+  // cos/sin evaluated in double and rounded once to float
+  std::vector<float> hc((size_t)max_ctx * (half > 0 ? half : 1)), hs(hc.size());
+  for (int pos = 0; pos < max_ctx; pos++)
+    for (int i = 0; i < half; i++) {
+      const float ang = (float)pos * m->invf[i];
+      hc[(size_t)pos * half + i] = (float)cos((double)ang);
+      hs[(size_t)pos * half + i] = (float)sin((double)ang);
+    }
+  if (cudaMemcpy(s->rope_cos, hc.data(), hc.size() * 4, cudaMemcpyHostToDevice) != cudaSuccess ||
+      cudaMemcpy(s->rope_sin, hs.data(), hs.size() * 4, cudaMemcpyHostToDevice) != cudaSuccess) {
+    cudaFreeHost(s->h_ctl); cudaFree(s->mem); delete s;
+    return pb_set_error(PB_ECUDA, "pb_state_create: rope upload");
+  }
+  int rc = pb_state_reset(s, nullptr);
+  if (rc == PB_OK && cudaDeviceSynchronize() != cudaSuccess) rc = pb_set_error(PB_ECUDA, "pb_state_create: sync");
+  if (rc) { cudaFreeHost(s->h_ctl); cudaFree(s->mem); delete s; return rc; }
+  *out = s;
+  return PB_OK;
+}
+
+extern "C" int pb_state_destroy(pb_state* s) {
+  if (!s) return PB_OK;
+  if (s->exec) cudaGraphExecDestroy(s->exec);
+  if (s->graph) cudaGraphDestroy(s->graph);
+  if (s->graph_stream) cudaStreamDestroy(s->graph_stream);
+  cudaFreeHost(s->h_ctl);
+  cudaFree(s->mem);
+  delete s;
+  return PB_OK;
+}
+
+extern "C" int pb_state_reset(pb_state* s, void* stream) {
+  if (!s) return pb_set_error(PB_EINVAL, "pb_state_reset: null state");
+  cudaStream_t st = (cudaStream_t)stream;
+  const pb_model* m = s->m;
+  const size_t kvb = (size_t)m->n_attn * 2 * s->max_ctx * m->NKV * m->HD * 2;
+  const size_t ringb = (size_t)(m->L - m->n_attn) * m->W * m->H * 2;
+  if (kvb) PB_TRY_CUDA(cudaMemsetAsync(s->kv, 0, kvb, st));
+  if (ringb) PB_TRY_CUDA(cudaMemsetAsync(s->ring, 0, ringb, st));
+  PB_TRY_CUDA(cudaMemsetAsync(s->ctl, 0, sizeof(Ctl), st));
+  return PB_OK;
+}
+
+static int set_ctl(pb_state* s, int token, int pos, int* ids, cudaStream_t st,
+                   const int* prompt = nullptr, int n_prompt = 0) {
+  // the previous upload from this pinned block must have landed first
+  PB_TRY_CUDA(cudaStreamSynchronize(st));
+  s->h_ctl->token = token;
+  s->h_ctl->pos = pos;
+  s->h_ctl->step = 0;
+  s->h_ctl->counter = 0;
+  s->h_ctl->ids = ids;
+  s->h_ctl->prompt = prompt;
+  s->h_ctl->n_prompt = n_prompt;
+  PB_TRY_CUDA(cudaMemcpyAsync(s->ctl, s->h_ctl, offsetof(Ctl, slot_val), cudaMemcpyHostToDevice, st));
+  return PB_OK;
+}
+
+extern "C" int pb_layer_step(pb_model* m, pb_state* s, int layer, int pos, uint16_t* d_x, void* stream) {
+  if (!m || !s || !d_x || layer < 0 || layer >= m->L || pos < 0 || pos >= s->max_ctx)
+    return pb_set_error(PB_EINVAL, "pb_layer_step: bad argument");
+  cudaStream_t st = (cudaStream_t)stream;
+  int rc = set_ctl(s, 0, pos, nullptr, st);
+  if (rc) return rc;
+  // residual in d_x; the layer writes its pre-FFN residual into res[1] (cur
+  // flips 0 -> 1) and the tail adds the FFN branch back into d_x
+  int cur = 0;
+  uint64_t nk = 0;
+  if ((rc = enqueue_layer(m, s, layer, cur, PRO_ADDNORM, false, d_x, st, false, nk))) return rc;
+  StepArgs a = base_args(m, s);
+  a.pro = PRO_ADDNORM;
+  a.xin = s->res[cur];
+  a.hin = s->h_w2;
+  a.wpost = m->layers[layer].post_ffn_norm;
+  a.wnorm = nullptr;
+  a.rout = d_x;
+  a.K = m->H;
+  k_tail<<<1, 256, step_smem(m->H, m->H), st>>>(a);
+  PB_LAUNCHED("k_tail");
+  return PB_OK;
+}
+
+extern "C" int pb_decode_token(pb_model* m, pb_state* s, int token, int pos, int* h_out_id,
+                               float* d_logits, void* stream) {
+  if (!m || !s || token < 0 || token >= m->V || pos < 0 || pos >= s->max_ctx)
+    return pb_set_error(PB_EINVAL, "pb_decode_token: bad argument");
+  cudaStream_t st = (cudaStream_t)stream;
+  int rc = build_graph(s);
+  if (rc) return rc;
+  if ((rc = set_ctl(s, token, pos, nullptr, st))) return rc;
+  PB_TRY_CUDA(cudaGraphLaunch(s->exec, st));
+  pb_count_launch(s->graph_launches);
+  if (d_logits) PB_TRY_CUDA(cudaMemcpyAsync(d_logits, s->logits, (size_t)m->V * 4, cudaMemcpyDeviceToDevice, st));
+  if (h_out_id) {
+    PB_TRY_CUDA(cudaMemcpyAsync(&s->h_ctl->token, &s->ctl->token, sizeof(int), cudaMemcpyDeviceToHost, st));
+    PB_TRY_CUDA(cudaStreamSynchronize(st));
+    *h_out_id = s->h_ctl->token;
+  }
+  return PB_OK;
+}
+
+extern "C" int pb_decode_greedy(pb_model* m, pb_state* s, int token, int pos0, int n, int* d_ids,
+                                void* stream) {
+  if (!m || !s || token < 0 || token >= m->V || pos0 < 0 || n <= 0 || pos0 + n > s->max_ctx)
+    return pb_set_error(PB_EINVAL, "pb_decode_greedy: bad argument");
+  cudaStream_t st = (cudaStream_t)stream;
+  int rc = build_graph(s);
+  if (rc) return rc;
+  if ((rc = set_ctl(s, token, pos0, d_ids, st))) return rc;
+  for (int i = 0; i < n; i++) {
+    PB_TRY_CUDA(cudaGraphLaunch(s->exec, st));
+    pb_count_launch(s->graph_launches);
+  }
+  return PB_OK;
+}
+
+// test/inspection helpers (not in the public header): device pointers of a
+// state's buffers so that tests can compare intermediate state
+extern "C" int pb_state_debug(pb_state* s, int which, void** ptr, size_t* bytes) {
+  if (!s || !ptr) return PB_EINVAL;
+  const pb_model* m = s->m;
+  switch (which) {
+    case 0: *ptr = s->kv; if (bytes) *bytes = (size_t)m->n_attn * 2 * s->max_ctx * m->NKV * m->HD * 2; return PB_OK;
+    case 1: *ptr = s->ring; if (bytes) *bytes = (size_t)(m->L - m->n_attn) * m->W * m->H * 2; return PB_OK;
+    case 2: *ptr = s->res[s->graph_res]; if (bytes) *bytes = (size_t)m->H * 2; return PB_OK;
+    case 3: *ptr = s->logits; if (bytes) *bytes = (size_t)m->V * 4; return PB_OK;
+    case 4: *ptr = &s->ctl->pos; if (bytes) *bytes = 4; return PB_OK;
+  }
+  return PB_EINVAL;
+}
+
+extern "C" int pb_decode_prompt(pb_model* m, pb_state* s, const int* d_tokens, int n, int pos0,
+                                int* d_ids, void* stream) {
+  if (!m || !s || !d_tokens || n <= 0 || pos0 < 0 || pos0 + n > s->max_ctx)
+    return pb_set_error(PB_EINVAL, "pb_decode_prompt: bad argument");
+  cudaStream_t st = (cudaStream_t)stream;
+  int rc = build_graph(s);
+  if (rc) return rc;
+  int first = 0;
+  PB_TRY_CUDA(cudaMemcpy(&first, d_tokens, sizeof(int), cudaMemcpyDeviceToHost));
+  if (first < 0 || first >= m->V) return pb_set_error(PB_EINVAL, "pb_decode_prompt: token %d", first);
+  if ((rc = set_ctl(s, first, pos0, d_ids, st, d_tokens, n))) return rc;
+  for (int i = 0; i < n; i++) {
+    PB_TRY_CUDA(cudaGraphLaunch(s->exec, st));
+    pb_count_launch(s->graph_launches);
+  }
+  return PB_OK;
+}
+
+extern "C" int pb_decode_kernels_per_token(pb_state* s) {
+  if (!s) return pb_set_error(PB_EINVAL, "null state");
+  int rc = build_graph(s);
+  return rc ? rc : (int)s->graph_launches;
+}
+
+// Times one of the decode step's fused GEMV kernels alone: `which` 0 = the
+// layer's first GEMV (q|k|v|gate or in_proj), 1 = o_proj/out_proj, 2 = w1|w3,
+// 3 = w2, 4 = the head. Launches cycle over every layer that has the tensor
+// (distinct weights, more bytes than L2), `iters` launches between two events
+// on `stream`; returns the mean ms per launch and the algorithmic bytes of one
+// launch (codes + scales of its matrix).
+extern "C" int pb_time_step_kernel(pb_model* m, pb_state* s, int which, int iters, float* ms,
+                                   double* bytes, void* stream) {
+  if (!m || !s || !ms || iters <= 0 || which < 0 || which > 4) return pb_set_error(PB_EINVAL, "pb_time_step_kernel");
+  cudaStream_t st = (cudaStream_t)stream;
+  std::vector<const pb_q8*> ws;
+  std::vector<int> layer;
+  for (int L = 0; L < m->L; L++) {
+    const Layer& Ly = m->layers[L];
+    if (which == 0) { ws.push_back(&Ly.first); layer.push_back(L); }
+    if (which == 1) { ws.push_back(&Ly.mix); layer.push_back(L); }
+    if (which == 2) { ws.push_back(&Ly.w13); layer.push_back(L); }
+    if (which == 3) { ws.push_back(&Ly.w2); layer.push_back(L); }
+  }
+  if (which == 4) { ws.push_back(&m->head); layer.push_back(m->L - 1); }
+  // uniform shape subset: the most common shape among the candidates
+  const pb_q8* ref = ws[0];
+  std::vector<const pb_q8*> sel;
+  std::vector<int> sl;
+  for (size_t i = 0; i < ws.size(); i++)
+    if (ws[i]->N == ref->N && ws[i]->K == ref->K) { sel.push_back(ws[i]); sl.push_back(layer[i]); }
+  cudaEvent_t e0, e1;
+  PB_TRY_CUDA(cudaEventCreate(&e0));
+  PB_TRY_CUDA(cudaEventCreate(&e1));
+  auto one = [&](int i) -> int {
+    const pb_q8* w = sel[i % sel.size()];
+    const Layer& Ly = m->layers[sl[i % sl.size()]];
+    StepArgs a = base_args(m, s);
+    int epi = EPI_BF16;
+    if (which == 2) {
+      a.pro = PRO_ADDNORM; a.xin = s->res[0]; a.hin = s->h_mix; a.wpost = Ly.post_op_norm;
+      a.wnorm = Ly.ffn_norm; a.y = s->h_u; epi = EPI_SILU;
+    } else if (which == 4) {
+      a.pro = PRO_ADDNORM; a.xin = s->res[0]; a.hin = s->h_w2; a.wpost = Ly.post_ffn_norm;
+      a.wnorm = m->final_norm; a.y = s->logits; epi = EPI_ARGMAX;
+    } else if (which == 3) {
+      a.pro = PRO_PLAIN; a.xin = s->h_u; a.y = s->h_w2;
+    } else if (which == 1) {
+      a.pro = PRO_PLAIN; a.xin = s->h_attn; a.y = s->h_mix;     // same stream cost either mixer
+    } else {
+      a.pro = PRO_ADDNORM; a.xin = s->res[0]; a.hin = s->h_w2; a.wpost = Ly.post_ffn_norm;
+      a.wnorm = Ly.op_norm; a.y = s->h_first;
+    }
+    return launch_step(*w, epi, a, st, true);
+  };
+  int rc = PB_OK;
+  for (int i = 0; i < 3 && rc == PB_OK; i++) rc = one(i);         // warm-up
+  if (rc == PB_OK) rc = cudaEventRecord(e0, st) == cudaSuccess ? PB_OK : PB_ECUDA;
+  for (int i = 0; i < iters && rc == PB_OK; i++) rc = one(i);
+  if (rc == PB_OK && cudaEventRecord(e1, st) != cudaSuccess) rc = PB_ECUDA;
+  if (rc == PB_OK && cudaEventSynchronize(e1) != cudaSuccess) rc = pb_set_error(PB_ECUDA, "timing sync");
+  float t = 0;
+  if (rc == PB_OK) cudaEventElapsedTime(&t, e0, e1);
+  cudaEventDestroy(e0);
+  cudaEventDestroy(e1);
+  if (rc) return rc;
+  *ms = t / iters;
+  if (bytes) *bytes = (double)ref->N * ref->K + (double)ref->N * (ref->K / 32) * (ref->sdt == PB_DT_F32 ? 4 : 2);
+  return PB_OK;
+}
+
+namespace {
+__global__ void k_test_expf(const float* x, float* y, int n) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i < n) y[i] = pb_expf(x[i]);
+}
+}  // namespace
+// test hook: the device e^x over n values (not part of the public ABI)
+extern "C" int pb_test_expf(const float* d_x, float* d_y, int n, void* stream) {
+  k_test_expf<<<(n + 255) / 256, 256, 0, (cudaStream_t)stream>>>(d_x, d_y, n);
+  PB_LAUNCHED("k_test_expf");
+  return PB_OK;
+}

@@ -1,0 +1,324 @@
+// pb_q1.cu -- Q1_0 x Q8_K weight streaming on sm_100a, the Q8_K activation
+// quantiser, and the Bonsai engine's host compat entry points.
+//
+// Arithmetic (pq1_host.c:99-120): per 128-weight group g of a row,
+//   isum_g = sum_i (bit_i ? +q_i : -q_i)          exact int32
+//   acc    = acc + (ws_g * db) * (float)isum_g      group order, no contraction
+// with ws_g the group's fp16 scale (widened; -0 widens to +0 as pq1_h2f does)
+// and db the Q8_K block scale of the 256 activations holding the group.
+//
+// Device form: isum_g = 2 P_g - A_g with A_g = sum_i q_i (from the activations
+// alone) and P_g = sum_{bit_i = 1} q_i. P_g is computed with dp4a on 0/1 byte
+// masks: for a 32-bit word w of weight bits, (w >> k) & 0x01010101 selects the
+// weights at bit positions k, k+8, k+16, k+24, so the 32 activations of that
+// word are staged in shared memory pre-permuted as words
+// (q_k, q_{k+8}, q_{k+16}, q_{k+24}), k = 0..7.
+#include "pb_common.cuh"
+#include "pb_internal.h"
+#include <cstdio>
+#include <cstring>
+#include <map>
+#include <mutex>
+#include <tuple>
+#include <vector>
+
+// --------------------------------------------------------------- packing
+// 18-byte blocks (fp16 scale, 16 sign bytes) -> bits [rows][K/32] u32 and
+// scales [rows][K/128] fp16 (pq1_split_repack, pq1_host.c:78-97).
+__global__ void k_q1_pack(const uint8_t* __restrict__ src, uint32_t* __restrict__ bits,
+                          uint16_t* __restrict__ scales, int rows, int K) {
+  const int nb = K / 128;
+  const size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x;   // one block
+  if (i >= (size_t)rows * nb) return;
+  const uint8_t* b = src + i * 18;
+  scales[i] = (uint16_t)(b[0] | (b[1] << 8));
+#pragma unroll
+  for (int w = 0; w < 4; w++)
+    bits[i * 4 + w] = (uint32_t)b[2 + 4 * w] | ((uint32_t)b[3 + 4 * w] << 8) |
+                      ((uint32_t)b[4 + 4 * w] << 16) | ((uint32_t)b[5 + 4 * w] << 24);
+}
+
+// ------------------------------------------------------- Q8_K quantiser
+// fwd8.c:67-139 as stated in scalar form by pq1_parity.c:131-147: amax and the
+// value at the FIRST index reaching it, iscale = -127/mx, q = min(127,
+// nearest_int(fma(x, iscale, 1.5*2^23))), d = 1/iscale, int16 bsums per 16.
+// One CTA (256 threads) per 256-value block.
+__global__ void __launch_bounds__(256) k_q8k_quantize(const float* __restrict__ x,
+                                                      uint8_t* __restrict__ xq) {
+  const int b = blockIdx.x, t = threadIdx.x, lane = t & 31, wid = t >> 5;
+  const float v = x[(size_t)b * 256 + t];
+  float a = fabsf(v);
+  int idx = t;
+  // (max |x|, first index) reduction
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const float oa = __shfl_down_sync(0xffffffffu, a, o);
+    const int oi = __shfl_down_sync(0xffffffffu, idx, o);
+    if (oa > a || (oa == a && oi < idx)) { a = oa; idx = oi; }
+  }
+  __shared__ float sa[8];
+  __shared__ int si[8];
+  __shared__ float smx;
+  __shared__ int sidx;
+  if (lane == 0) { sa[wid] = a; si[wid] = idx; }
+  __syncthreads();
+  if (t == 0) {
+    float ba = sa[0]; int bi = si[0];
+    for (int w = 1; w < 8; w++) if (sa[w] > ba) { ba = sa[w]; bi = si[w]; }
+    smx = ba; sidx = bi;
+  }
+  __syncthreads();
+  uint8_t* qb = xq + (size_t)b * 292;
+  const float amax = smx;
+  if (amax == 0.0f) {   // whole block zero: d, qs and bsums all zero bytes
+    for (int i = t; i < 292; i += 256) qb[i] = 0;
+    return;
+  }
+  const float mx = x[(size_t)b * 256 + sidx];
+  const float iscale = __fdiv_rn(-127.0f, mx);
+  const float f = __fmaf_rn(v, iscale, 12582912.0f);
+  int q = (int)(__float_as_uint(f) & 0x007fffffu) - 0x00400000;
+  q = q < 127 ? q : 127;
+  qb[4 + t] = (uint8_t)(int8_t)q;
+  // bsums: 16 consecutive values = half a warp
+  int s = q;
+#pragma unroll
+  for (int o = 8; o > 0; o >>= 1) s += __shfl_down_sync(0xffffffffu, s, o, 16);
+  if ((lane & 15) == 0) {
+    const int16_t s16 = (int16_t)s;
+    const int g = t >> 4;
+    qb[260 + 2 * g] = (uint8_t)(s16 & 0xff);
+    qb[261 + 2 * g] = (uint8_t)((uint16_t)s16 >> 8);
+  }
+  if (t == 0) {
+    const float d = __fdiv_rn(1.0f, iscale);
+    const unsigned u = __float_as_uint(d);
+    qb[0] = u & 0xff; qb[1] = (u >> 8) & 0xff; qb[2] = (u >> 16) & 0xff; qb[3] = u >> 24;
+  }
+}
+
+// ------------------------------------------------------------ Q1 GEMV
+// One warp per row, lane l owns groups l, l+32, ...; products
+// (ws*db)*(float)isum go to a per-warp row buffer and lane 0 folds them in
+// group order. Activations staged once per CTA, permuted as described above,
+// 528 bytes per group (512 + 16 of padding so that lanes on consecutive
+// groups hit distinct banks).
+#define PB_Q1_GSTRIDE 528
+__global__ void __launch_bounds__(256)
+k_q1_gemv(const uint4* __restrict__ bits, const uint16_t* __restrict__ wsc,
+          const uint8_t* __restrict__ xq, float* __restrict__ y, int32_t* __restrict__ isum,
+          int rows, int K) {
+  extern __shared__ __align__(16) unsigned char smem[];
+  const int ng = K / 128;
+  unsigned char* act = smem;                                         // ng * 528
+  int* asum = reinterpret_cast<int*>(smem + (size_t)ng * PB_Q1_GSTRIDE);   // ng
+  float* dbs = reinterpret_cast<float*>(asum + ng);                 // ng (db per group)
+  float* prod = dbs + ng;                                           // 8 warps x ng
+  // stage: thread per (group, word-of-32, k)
+  for (int i = threadIdx.x; i < ng * 32; i += blockDim.x) {
+    const int g = i >> 5, j = (i >> 3) & 3, k = i & 7;
+    const int8_t* qs = reinterpret_cast<const int8_t*>(xq + (size_t)(g >> 1) * 292 + 4 + (g & 1) * 128 + j * 32);
+    const uint32_t w = (uint32_t)(uint8_t)qs[k] | ((uint32_t)(uint8_t)qs[k + 8] << 8) |
+                       ((uint32_t)(uint8_t)qs[k + 16] << 16) | ((uint32_t)(uint8_t)qs[k + 24] << 24);
+    reinterpret_cast<uint32_t*>(act + (size_t)g * PB_Q1_GSTRIDE)[j * 8 + k] = w;
+  }
+  for (int g = threadIdx.x; g < ng; g += blockDim.x) {
+    const int8_t* qs = reinterpret_cast<const int8_t*>(xq + (size_t)(g >> 1) * 292 + 4 + (g & 1) * 128);
+    int s = 0;
+    for (int i = 0; i < 128; i++) s += qs[i];
+    asum[g] = s;
+    float db;
+    memcpy(&db, xq + (size_t)(g >> 1) * 292, 4);
+    dbs[g] = db;
+  }
+  __syncthreads();
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  float* pw = prod + warp * ng;
+  for (int row = blockIdx.x * 8 + warp; row < rows; row += gridDim.x * 8) {
+    for (int g = lane; g < ng; g += 32) {
+      const uint4 wv = pb_ldg_stream(bits + (size_t)row * ng + g);
+      const unsigned short hs = wsc[(size_t)row * ng + g];
+      const uint4* av = reinterpret_cast<const uint4*>(act + (size_t)g * PB_Q1_GSTRIDE);
+      const unsigned ws[4] = {wv.x, wv.y, wv.z, wv.w};
+      int P = 0;
+#pragma unroll
+      for (int j = 0; j < 4; j++) {
+        const uint4 a0 = av[2 * j], a1 = av[2 * j + 1];
+        const unsigned aw[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
+#pragma unroll
+        for (int k = 0; k < 8; k++) P = __dp4a((int)((ws[j] >> k) & 0x01010101u), (int)aw[k], P);
+      }
+      const int s = 2 * P - asum[g];
+      if (isum) isum[(size_t)row * ng + g] = s;
+      const float wsf = hs == 0x8000u ? 0.0f : pb_h2f(hs);
+      pw[g] = __fmul_rn(__fmul_rn(wsf, dbs[g]), __int2float_rn(s));
+    }
+    __syncwarp();
+    if (lane == 0) {
+      float acc = 0.0f;
+      for (int g = 0; g < ng; g++) acc = __fadd_rn(acc, pw[g]);
+      y[row] = acc;
+    }
+    __syncwarp();
+  }
+}
+
+static size_t q1_smem(int K) {
+  const int ng = K / 128;
+  return (size_t)ng * PB_Q1_GSTRIDE + (size_t)ng * 4 * 2 + (size_t)8 * ng * 4;
+}
+
+static int q1_gemv_launch(const pb_q1* w, const uint8_t* d_xq, float* d_y, int32_t* d_isum,
+                          cudaStream_t st) {
+  const size_t smem = q1_smem(w->K);
+  if (smem > 220 * 1024) return pb_set_error(PB_ENOTSUP, "pb_q1_gemv: K=%d too large", w->K);
+  static bool attr = false;
+  if (!attr) {
+    cudaFuncSetAttribute(k_q1_gemv, cudaFuncAttributeMaxDynamicSharedMemorySize, 220 * 1024);
+    attr = true;
+  }
+  int grid = 2 * pb_num_sms();
+  if (grid * 8 > w->rows) grid = (w->rows + 7) / 8;
+  k_q1_gemv<<<grid, 256, smem, st>>>(reinterpret_cast<const uint4*>(w->bits), w->scales, d_xq,
+                                    d_y, d_isum, w->rows, w->K);
+  PB_LAUNCHED("k_q1_gemv");
+  return PB_OK;
+}
+
+// ---------------------------------------------------------------- C ABI
+extern "C" int pb_q1_pack(const uint8_t* blocks, int rows, int K, int src_on_device, void* stream,
+                          pb_q1** out) {
+  if (!out || !blocks) return pb_set_error(PB_EINVAL, "pb_q1_pack: null argument");
+  *out = nullptr;
+  if (rows <= 0 || K <= 0 || K % 256) return pb_set_error(PB_EINVAL, "pb_q1_pack: bad shape %dx%d", rows, K);
+  cudaStream_t st = (cudaStream_t)stream;
+  const size_t nblk = (size_t)rows * (K / 128), src_bytes = nblk * 18;
+  pb_q1* w = new pb_q1();
+  w->rows = rows; w->K = K;
+  if (cudaMalloc(&w->bits, nblk * 16) != cudaSuccess || cudaMalloc(&w->scales, nblk * 2) != cudaSuccess) {
+    cudaGetLastError();
+    cudaFree(w->bits); cudaFree(w->scales); delete w;
+    return pb_set_error(PB_ENOMEM, "pb_q1_pack: cannot allocate");
+  }
+  const uint8_t* src = blocks;
+  uint8_t* tmp = nullptr;
+  int rc = PB_OK;
+  if (!src_on_device) {
+    if (cudaMalloc(&tmp, src_bytes) != cudaSuccess) { cudaGetLastError(); rc = pb_set_error(PB_ENOMEM, "pb_q1_pack: staging"); }
+    else if (cudaMemcpyAsync(tmp, blocks, src_bytes, cudaMemcpyHostToDevice, st) != cudaSuccess)
+      rc = pb_set_error(PB_ECUDA, "pb_q1_pack: upload");
+    src = tmp;
+  }
+  if (rc == PB_OK) {
+    k_q1_pack<<<(unsigned)((nblk + 255) / 256), 256, 0, st>>>(src, w->bits, w->scales, rows, K);
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) rc = pb_set_error(PB_ECUDA, "launch k_q1_pack: %s", cudaGetErrorString(e));
+    else pb_count_launch();
+  }
+  if (rc == PB_OK && cudaStreamSynchronize(st) != cudaSuccess)
+    rc = pb_set_error(PB_ECUDA, "pb_q1_pack: %s", cudaGetErrorString(cudaGetLastError()));
+  cudaFree(tmp);
+  if (rc != PB_OK) { cudaFree(w->bits); cudaFree(w->scales); delete w; return rc; }
+  *out = w;
+  return PB_OK;
+}
+
+extern "C" int pb_q1_free(pb_q1* w) {
+  if (!w) return PB_OK;
+  if (w->owner) { cudaFree(w->bits); cudaFree(w->scales); }
+  delete w;
+  return PB_OK;
+}
+
+extern "C" int pb_q8k_quantize(const float* d_x, int K, uint8_t* d_xq, void* stream) {
+  if (!d_x || !d_xq || K <= 0 || K % 256) return pb_set_error(PB_EINVAL, "pb_q8k_quantize: bad argument");
+  k_q8k_quantize<<<K / 256, 256, 0, (cudaStream_t)stream>>>(d_x, d_xq);
+  PB_LAUNCHED("k_q8k_quantize");
+  return PB_OK;
+}
+
+extern "C" int pb_q1_gemv(const pb_q1* w, const uint8_t* d_xq, float* d_y, int32_t* d_isum, void* stream) {
+  if (!w || !d_xq || !d_y) return pb_set_error(PB_EINVAL, "pb_q1_gemv: null argument");
+  return q1_gemv_launch(w, d_xq, d_y, d_isum, (cudaStream_t)stream);
+}
+
+// ------------------------------------------------ host compat (Bonsai ABI)
+// pq1_fwd8_shim.h:12-23 / pq1_fwd8_glue.c:549-620: the host weight pointer
+// (with its shape) is the cache key; the first call packs and uploads it.
+namespace {
+struct Compat {
+  std::mutex mu;
+  std::map<std::tuple<const void*, int, int>, pb_q1*> cache;
+  cudaStream_t st = nullptr;
+  uint8_t* d_xq = nullptr; size_t xq_cap = 0;
+  float* d_y = nullptr; size_t y_cap = 0;
+  float* h_y = nullptr;
+};
+Compat& compat() { static Compat c; return c; }
+
+int compat_ensure(Compat& c, size_t xq_bytes, size_t y_elems) {
+  if (!c.st && cudaStreamCreateWithFlags(&c.st, cudaStreamNonBlocking) != cudaSuccess)
+    return pb_set_error(PB_ECUDA, "compat: stream");
+  if (xq_bytes > c.xq_cap) {
+    cudaFree(c.d_xq); c.d_xq = nullptr; c.xq_cap = 0;
+    if (cudaMalloc(&c.d_xq, xq_bytes) != cudaSuccess) return pb_set_error(PB_ENOMEM, "compat: xq");
+    c.xq_cap = xq_bytes;
+  }
+  if (y_elems > c.y_cap) {
+    cudaFree(c.d_y); cudaFreeHost(c.h_y); c.d_y = nullptr; c.h_y = nullptr; c.y_cap = 0;
+    if (cudaMalloc(&c.d_y, y_elems * 4) != cudaSuccess || cudaMallocHost(&c.h_y, y_elems * 4) != cudaSuccess)
+      return pb_set_error(PB_ENOMEM, "compat: y");
+    c.y_cap = y_elems;
+  }
+  return PB_OK;
+}
+pb_q1* compat_tensor(Compat& c, const unsigned char* w, int rows, int cols) {
+  auto key = std::make_tuple((const void*)w, rows, cols);
+  auto it = c.cache.find(key);
+  if (it != c.cache.end()) return it->second;
+  pb_q1* t = nullptr;
+  if (pb_q1_pack(w, rows, cols, 0, c.st, &t) != PB_OK) return nullptr;
+  c.cache[key] = t;
+  return t;
+}
+}  // namespace
+
+extern "C" int pq1_pq1_compat_gemv_batch(const unsigned char* const* w, const int* rows, int n, int cols,
+                                         float* const* ys, const unsigned char* xq) {
+  if (!w || !rows || !ys || !xq || n <= 0 || cols <= 0 || cols % 256) return PB_EINVAL;
+  Compat& c = compat();
+  std::lock_guard<std::mutex> lk(c.mu);
+  size_t tot = 0;
+  for (int i = 0; i < n; i++) tot += (size_t)rows[i];
+  const size_t xqb = (size_t)(cols / 256) * 292;
+  if (compat_ensure(c, xqb, tot) != PB_OK) return PB_ECUDA;
+  std::vector<pb_q1*> ts((size_t)n);
+  for (int i = 0; i < n; i++) {
+    ts[i] = compat_tensor(c, w[i], rows[i], cols);
+    if (!ts[i]) return PB_ENOMEM;
+  }
+  if (cudaMemcpyAsync(c.d_xq, xq, xqb, cudaMemcpyHostToDevice, c.st) != cudaSuccess) return PB_ECUDA;
+  size_t off = 0;
+  for (int i = 0; i < n; i++) {
+    if (q1_gemv_launch(ts[i], c.d_xq, c.d_y + off, nullptr, c.st) != PB_OK) return PB_ECUDA;
+    off += (size_t)rows[i];
+  }
+  if (cudaMemcpyAsync(c.h_y, c.d_y, tot * 4, cudaMemcpyDeviceToHost, c.st) != cudaSuccess) return PB_ECUDA;
+  if (cudaStreamSynchronize(c.st) != cudaSuccess) return PB_ECUDA;
+  off = 0;
+  for (int i = 0; i < n; i++) { memcpy(ys[i], c.h_y + off, (size_t)rows[i] * 4); off += (size_t)rows[i]; }
+  return PB_OK;
+}
+
+extern "C" void pq1_pq1_compat_gemv(int rows, int cols, const unsigned char* w, const float* x, float* y,
+                                    const unsigned char* xq) {
+  (void)x;
+  const unsigned char* const ws[1] = {w};
+  const int rs[1] = {rows};
+  float* const yv[1] = {y};
+  if (pq1_pq1_compat_gemv_batch(ws, rs, 1, cols, yv, xq) != PB_OK) {
+    // The reference's compat entry has no status; a failure leaves y as NaN
+    // so that a caller comparing results cannot mistake it for an answer.
+    for (int i = 0; i < rows; i++) y[i] = __builtin_nanf("");
+  }
+}

@@ -1,0 +1,490 @@
+// pb_q8.cu -- Q8 weight streaming on sm_100a: packing, the REF_FLOAT GEMV /
+// GEMM (bf16 activations, fp32 FMA chains in the reference's reduction order)
+// and the Q8_0 x Q8_0 integer GEMV.
+//
+// Reduction order (lfm3_nanode.cu:222-343, the order the reference's shipped
+// q8_partial<bf16,FMA=true> and q8_partial_TLb produce): per row and 2048-code
+// chunk, leaf l (l = 0..31) is the chain over blocks b = l, l+32, ... of
+// acc = fma(s_b, dot_b, acc), dot_b = fma(code_j, x_j, dot) over j = 0..31;
+// the 32 leaves combine by the shuffle-down tree (16, 8, 4, 2, 1); chunk
+// partials are summed ascending from 0; the Linear output is bf16(that sum).
+//
+// Streaming layout (PB_Q8_STREAM, K % 2048 == 0): the codes of (row, chunk)
+// form one 2048-byte segment of 128 16-byte granules; granule h*32 + l holds
+// codes [16(h&1), 16(h&1)+16) of block l + 32(h>>1). Lane l of a warp reads
+// granules l, 32+l, 64+l, 96+l -- each warp load instruction is one contiguous
+// 512-byte run -- and owns exactly leaf l. Scales of a segment are 32 pairs
+// (s_l, s_{l+32}), one 4-byte (fp16) or 8-byte (fp32) load per lane.
+#include "pb_common.cuh"
+#include "pb_internal.h"
+#include <cstdio>
+#include <cstdlib>
+#include <cstring>
+
+// ------------------------------------------------------------------ packing
+// Source rows r = 0..R-1 (row-major) land at destination row r*rmul + radd,
+// which lets the loader merge tensors (q|k|v|gate) and interleave w1/w3 rows.
+__global__ void k_q8_pack_codes(const uint4* __restrict__ src, uint4* __restrict__ dst,
+                                int R, int K, int rmul, int radd) {
+  // one thread per source granule of the destination order
+  const int nch = K / 2048;
+  const size_t total = (size_t)R * nch * 128;
+  const size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= total) return;
+  const size_t seg = i >> 7;
+  const int gi = (int)(i & 127), h = gi >> 5, l = gi & 31;
+  const size_t row = seg / nch;
+  const int c = (int)(seg - row * nch);
+  const int blk = c * 64 + l + 32 * (h >> 1);
+  const size_t drow = row * rmul + radd;
+  dst[(drow * nch + c) * 128 + gi] = src[(row * (size_t)K + (size_t)blk * 32 + 16 * (h & 1)) >> 4];
+}
+template <typename ST>
+__global__ void k_q8_pack_scales(const ST* __restrict__ src, ST* __restrict__ dst, int R, int K,
+                                 int rmul, int radd) {
+  const int nch = K / 2048, nb = K / 32;
+  const size_t total = (size_t)R * nch * 32;
+  const size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= total) return;
+  const size_t seg = i >> 5;
+  const int l = (int)(i & 31);
+  const size_t row = seg / nch;
+  const int c = (int)(seg - row * nch);
+  const size_t d = ((row * rmul + radd) * nch + c) * 32 + l;
+  dst[2 * d] = src[row * nb + c * 64 + l];
+  dst[2 * d + 1] = src[row * nb + c * 64 + l + 32];
+}
+
+// ------------------------------------------------------ fast streaming GEMV
+// CTA = 8 warps = G = 8/NCH row groups x NCH chunk warps. Warp (g, c) keeps the
+// 64 x values of its leaf for chunk c in registers for the whole kernel and
+// walks U rows per iteration; with NCH > 1 the chunk partials meet in shared
+// memory and one thread per row adds them in chunk order.
+template <bool F32S>
+struct ScalePair;
+template <>
+struct ScalePair<false> {
+  typedef unsigned T;
+  static PB_DEV void load(const void* base, size_t idx, float& lo, float& hi) {
+    const unsigned w = pb_ldg_stream32(reinterpret_cast<const unsigned*>(base) + idx);
+    lo = pb_h2f((unsigned short)(w & 0xffffu));
+    hi = pb_h2f((unsigned short)(w >> 16));
+  }
+};
+template <>
+struct ScalePair<true> {
+  static PB_DEV void load(const void* base, size_t idx, float& lo, float& hi) {
+    const uint2 w = pb_ldg_stream64(reinterpret_cast<const uint2*>(base) + idx);
+    lo = __uint_as_float(w.x);
+    hi = __uint_as_float(w.y);
+  }
+};
+
+PB_DEV void pb_load_x64(const bf16_t* __restrict__ xc, int lane, float (&xr)[64]) {
+  // xr[0..31] = x[32*lane .. +31], xr[32..63] = x[1024 + 32*lane .. +31]
+#pragma unroll
+  for (int half = 0; half < 2; half++) {
+    const uint4* p = reinterpret_cast<const uint4*>(xc + half * 1024 + lane * 32);
+#pragma unroll
+    for (int v = 0; v < 4; v++) {
+      const uint4 w = p[v];
+      const unsigned ws[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+      for (int k = 0; k < 4; k++) {
+        xr[half * 32 + v * 8 + 2 * k] = pb_lo2f(ws[k]);
+        xr[half * 32 + v * 8 + 2 * k + 1] = pb_hi2f(ws[k]);
+      }
+    }
+  }
+}
+
+// 16 codes of one granule against 16 x values, continuing the chain `dot`
+PB_DEV float pb_dot16(const uint4 g, const float* xr, float dot) {
+  const unsigned ws[4] = {g.x, g.y, g.z, g.w};
+#pragma unroll
+  for (int k = 0; k < 4; k++) {
+    const unsigned ub = ws[k] ^ 0x80808080u;
+#pragma unroll
+    for (int j = 0; j < 4; j++) dot = __fmaf_rn(pb_code(ub, j), xr[4 * k + j], dot);
+  }
+  return dot;
+}
+
+// one row's leaf value for this lane: blocks l and l+32 of the chunk
+PB_DEV float pb_leaf(const uint4 (&q)[4], float slo, float shi, const float (&xr)[64]) {
+  float d0 = pb_dot16(q[0], xr, 0.0f);
+  d0 = pb_dot16(q[1], xr + 16, d0);
+  float acc = __fmaf_rn(slo, d0, 0.0f);
+  float d1 = pb_dot16(q[2], xr + 32, 0.0f);
+  d1 = pb_dot16(q[3], xr + 48, d1);
+  return __fmaf_rn(shi, d1, acc);
+}
+
+template <int NCH, int U, bool F32S, bool OUTF32>
+__global__ void __launch_bounds__(256, 2)
+k_q8f_stream(const uint4* __restrict__ codes, const void* __restrict__ scales,
+             const bf16_t* __restrict__ x, void* __restrict__ y, int N) {
+  constexpr int G = 8 / NCH, RB = G * U;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int c = warp % NCH, g = warp / NCH;
+  __shared__ float part[2][RB][NCH];
+  float xr[64];
+  pb_load_x64(x + c * 2048, lane, xr);
+  int it = 0;
+  for (int rb = blockIdx.x; rb * RB < N; rb += gridDim.x, it ^= 1) {
+    const int row0 = rb * RB + g * U;
+    uint4 q[U][4];
+    float slo[U], shi[U];
+#pragma unroll
+    for (int u = 0; u < U; u++) {
+      const int row = row0 + u;
+      if (row < N) {
+        const size_t seg = (size_t)row * NCH + c;
+        const uint4* base = codes + seg * 128 + lane;
+#pragma unroll
+        for (int h = 0; h < 4; h++) q[u][h] = pb_ldg_stream(base + 32 * h);
+        ScalePair<F32S>::load(scales, seg * 32 + lane, slo[u], shi[u]);
+      } else {
+#pragma unroll
+        for (int h = 0; h < 4; h++) q[u][h] = make_uint4(0, 0, 0, 0);
+        slo[u] = shi[u] = 0.0f;
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < U; u++) {
+      const float v = pb_warp_tree(pb_leaf(q[u], slo[u], shi[u], xr));
+      const int row = row0 + u;
+      if (NCH == 1) {
+        if (lane == 0 && row < N) {
+          if (OUTF32) reinterpret_cast<float*>(y)[row] = __fadd_rn(0.0f, v);
+          else reinterpret_cast<bf16_t*>(y)[row] = pb_f2bf(__fadd_rn(0.0f, v));
+        }
+      } else if (lane == 0) {
+        part[it][g * U + u][c] = v;
+      }
+    }
+    if (NCH > 1) {
+      __syncthreads();
+      if (threadIdx.x < RB) {
+        const int row = rb * RB + threadIdx.x;
+        if (row < N) {
+          float acc = 0.0f;
+#pragma unroll
+          for (int cc = 0; cc < NCH; cc++) acc = __fadd_rn(acc, part[it][threadIdx.x][cc]);
+          if (OUTF32) reinterpret_cast<float*>(y)[row] = acc;
+          else reinterpret_cast<bf16_t*>(y)[row] = pb_f2bf(acc);
+        }
+      }
+    }
+  }
+}
+
+// ---------------------------------------------------- general (row-major) path
+// Any K % 32 == 0 and T positions: one warp per row, positions in groups of 4,
+// the same leaf chains and trees, chunks per pick(). x is read through L2.
+__global__ void __launch_bounds__(256)
+k_q8f_general(const int8_t* __restrict__ codes, const void* __restrict__ scales, int f32s,
+              const bf16_t* __restrict__ x, void* __restrict__ y, int outf32, int N, int K,
+              int T, int KC) {
+  const int lane = threadIdx.x & 31;
+  const int row = blockIdx.x * 8 + (threadIdx.x >> 5);
+  if (row >= N) return;
+  const int nb = K / 32, nch = K / KC, nbc = KC / 32;
+  const int8_t* qr = codes + (size_t)row * K;
+  for (int t0 = 0; t0 < T; t0 += 4) {
+    float tot[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+    for (int c = 0; c < nch; c++) {
+      float acc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+      for (int b = lane; b < nbc; b += 32) {
+        const int blk = c * nbc + b;
+        const float s = f32s ? reinterpret_cast<const float*>(scales)[(size_t)row * nb + blk]
+                             : pb_h2f(reinterpret_cast<const unsigned short*>(scales)[(size_t)row * nb + blk]);
+        const int8_t* cb = qr + (size_t)blk * 32;
+#pragma unroll
+        for (int p = 0; p < 4; p++) {
+          if (t0 + p < T) {
+            const bf16_t* xb = x + (size_t)(t0 + p) * K + (size_t)blk * 32;
+            float dot = 0.0f;
+            for (int j = 0; j < 32; j++) dot = __fmaf_rn((float)cb[j], pb_bf2f(xb[j]), dot);
+            acc[p] = __fmaf_rn(s, dot, acc[p]);
+          }
+        }
+      }
+#pragma unroll
+      for (int p = 0; p < 4; p++) tot[p] = __fadd_rn(tot[p], pb_warp_tree(acc[p]));
+    }
+    if (lane == 0)
+#pragma unroll
+      for (int p = 0; p < 4; p++) {
+        const int t = t0 + p;
+        if (t < T) {
+          if (outf32) reinterpret_cast<float*>(y)[(size_t)t * N + row] = tot[p];
+          else reinterpret_cast<bf16_t*>(y)[(size_t)t * N + row] = pb_f2bf(tot[p]);
+        }
+      }
+  }
+}
+
+// --------------------------------------------------------- Q8_0 integer path
+// fwd35_ref.c:332-343: one warp per 32-block.
+__global__ void k_q80_quantize(const float* __restrict__ x, int K, int8_t* __restrict__ qx,
+                               unsigned short* __restrict__ dx) {
+  const int b = blockIdx.x * 8 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
+  if (b >= K / 32) return;
+  const float v = x[b * 32 + lane];
+  float amax = fabsf(v);
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+  const float d = __fdiv_rn(amax, 127.0f);
+  const float id = amax != 0.0f ? __fdiv_rn(127.0f, amax) : 0.0f;
+  qx[b * 32 + lane] = (int8_t)rintf(__fmul_rn(v, id));
+  if (lane == 0) dx[b] = pb_f2h(d);
+}
+
+// Streaming layout; one warp per row (all chunks). Lane l owns blocks l and
+// l+32 of each chunk: exact int32 block dots by dp4a, products
+// (dw*dx)*(float)isum into a per-warp row buffer, then lane 0 folds the row in
+// block order (no contraction), the reference's serial accumulation.
+template <bool F32S>
+__global__ void __launch_bounds__(256)
+k_q80_stream(const uint4* __restrict__ codes, const void* __restrict__ scales,
+             const int8_t* __restrict__ qx, const unsigned short* __restrict__ dx,
+             float* __restrict__ y, int32_t* __restrict__ isum, int N, int K) {
+  extern __shared__ __align__(16) unsigned char smem[];
+  const int nch = K / 2048, nb = K / 32;
+  int8_t* sq = reinterpret_cast<int8_t*>(smem);                       // K bytes
+  float* sdx = reinterpret_cast<float*>(smem + K);                    // nb floats
+  float* prod = sdx + nb;                                             // 8 warps x nb
+  for (int i = threadIdx.x; i < K / 16; i += blockDim.x)
+    reinterpret_cast<uint4*>(sq)[i] = reinterpret_cast<const uint4*>(qx)[i];
+  for (int i = threadIdx.x; i < nb; i += blockDim.x) sdx[i] = pb_h2f(dx[i]);
+  __syncthreads();
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  float* pw = prod + warp * nb;
+  for (int row = blockIdx.x * 8 + warp; row < N; row += gridDim.x * 8) {
+    for (int c = 0; c < nch; c++) {
+      const size_t seg = (size_t)row * nch + c;
+      const uint4* base = codes + seg * 128 + lane;
+      uint4 q[4];
+#pragma unroll
+      for (int h = 0; h < 4; h++) q[h] = pb_ldg_stream(base + 32 * h);
+      float slo, shi;
+      ScalePair<F32S>::load(scales, seg * 32 + lane, slo, shi);
+#pragma unroll
+      for (int half = 0; half < 2; half++) {
+        const int blk = c * 64 + lane + 32 * half;
+        const uint4* xq = reinterpret_cast<const uint4*>(sq + blk * 32);
+        const uint4 x0 = xq[0], x1 = xq[1];
+        const uint4 w0 = q[2 * half], w1 = q[2 * half + 1];
+        int s = 0;
+        s = __dp4a((int)w0.x, (int)x0.x, s); s = __dp4a((int)w0.y, (int)x0.y, s);
+        s = __dp4a((int)w0.z, (int)x0.z, s); s = __dp4a((int)w0.w, (int)x0.w, s);
+        s = __dp4a((int)w1.x, (int)x1.x, s); s = __dp4a((int)w1.y, (int)x1.y, s);
+        s = __dp4a((int)w1.z, (int)x1.z, s); s = __dp4a((int)w1.w, (int)x1.w, s);
+        if (isum) isum[(size_t)row * nb + blk] = s;
+        const float dw = half ? shi : slo;
+        pw[blk] = __fmul_rn(__fmul_rn(dw, sdx[blk]), __int2float_rn(s));
+      }
+    }
+    __syncwarp();
+    if (lane == 0) {
+      float acc = 0.0f;
+      for (int b = 0; b < nb; b++) acc = __fadd_rn(acc, pw[b]);
+      y[row] = acc;
+    }
+    __syncwarp();
+  }
+}
+
+// =============================================================== host side
+static int g_nsm = 0;
+int pb_num_sms() {
+  if (!g_nsm) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&g_nsm, cudaDevAttrMultiProcessorCount, dev);
+    if (g_nsm <= 0) g_nsm = 148;
+  }
+  return g_nsm;
+}
+
+int pb_q8_pack_into(pb_q8* w, const int8_t* d_codes, const void* d_scales, cudaStream_t st,
+                    int src_rows, int rmul, int radd) {
+  const int K = w->K, R = src_rows;
+  if (R <= 0 || (size_t)(R - 1) * rmul + radd >= (size_t)w->N)
+    return pb_set_error(PB_EINVAL, "pack: rows %d x%d +%d exceed %d", R, rmul, radd, w->N);
+  const size_t sbr = (size_t)(K / 32) * (w->sdt == PB_DT_F32 ? 4 : 2);   // scale bytes per row
+  if (w->layout == PB_Q8_ROWMAJOR) {
+    if (rmul == 1) {
+      PB_TRY_CUDA(cudaMemcpyAsync(w->codes + (size_t)radd * K, d_codes, (size_t)R * K, cudaMemcpyDeviceToDevice, st));
+      PB_TRY_CUDA(cudaMemcpyAsync((char*)w->scales + (size_t)radd * sbr, d_scales, (size_t)R * sbr,
+                                  cudaMemcpyDeviceToDevice, st));
+    } else {
+      PB_TRY_CUDA(cudaMemcpy2DAsync(w->codes + (size_t)radd * K, (size_t)rmul * K, d_codes, K, K, R,
+                                    cudaMemcpyDeviceToDevice, st));
+      PB_TRY_CUDA(cudaMemcpy2DAsync((char*)w->scales + (size_t)radd * sbr, (size_t)rmul * sbr, d_scales,
+                                    sbr, sbr, R, cudaMemcpyDeviceToDevice, st));
+    }
+    return PB_OK;
+  }
+  const size_t ng = (size_t)R * (K / 2048) * 128;
+  k_q8_pack_codes<<<(unsigned)((ng + 255) / 256), 256, 0, st>>>(
+      reinterpret_cast<const uint4*>(d_codes), reinterpret_cast<uint4*>(w->codes), R, K, rmul, radd);
+  PB_LAUNCHED("k_q8_pack_codes");
+  const size_t ns = (size_t)R * (K / 2048) * 32;
+  if (w->sdt == PB_DT_F32)
+    k_q8_pack_scales<float><<<(unsigned)((ns + 255) / 256), 256, 0, st>>>(
+        reinterpret_cast<const float*>(d_scales), reinterpret_cast<float*>(w->scales), R, K, rmul, radd);
+  else
+    k_q8_pack_scales<unsigned short><<<(unsigned)((ns + 255) / 256), 256, 0, st>>>(
+        reinterpret_cast<const unsigned short*>(d_scales),
+        reinterpret_cast<unsigned short*>(w->scales), R, K, rmul, radd);
+  PB_LAUNCHED("k_q8_pack_scales");
+  return PB_OK;
+}
+
+template <int NCH, int U>
+static int launch_stream(const pb_q8* w, const uint16_t* x, void* y, int outf32, cudaStream_t st) {
+  constexpr int RB = (8 / NCH) * U;
+  const int nrb = (w->N + RB - 1) / RB;
+  int grid = 2 * pb_num_sms();
+  if (grid > nrb) grid = nrb;
+  const uint4* q = reinterpret_cast<const uint4*>(w->codes);
+  const bool f32s = w->sdt == PB_DT_F32;
+  if (f32s && outf32) k_q8f_stream<NCH, U, true, true><<<grid, 256, 0, st>>>(q, w->scales, x, y, w->N);
+  else if (f32s) k_q8f_stream<NCH, U, true, false><<<grid, 256, 0, st>>>(q, w->scales, x, y, w->N);
+  else if (outf32) k_q8f_stream<NCH, U, false, true><<<grid, 256, 0, st>>>(q, w->scales, x, y, w->N);
+  else k_q8f_stream<NCH, U, false, false><<<grid, 256, 0, st>>>(q, w->scales, x, y, w->N);
+  PB_LAUNCHED("k_q8f_stream");
+  return PB_OK;
+}
+
+int pb_q8_gemv_launch(const pb_q8* w, const uint16_t* d_x, void* d_y, int y_dtype, cudaStream_t st) {
+  const int outf32 = y_dtype == PB_DT_F32;
+  if (w->layout == PB_Q8_STREAM) {
+    switch (w->nch) {
+      case 1: return launch_stream<1, 2>(w, d_x, d_y, outf32, st);
+      case 2: return launch_stream<2, 2>(w, d_x, d_y, outf32, st);
+      case 4: return launch_stream<4, 2>(w, d_x, d_y, outf32, st);
+      case 8: return launch_stream<8, 2>(w, d_x, d_y, outf32, st);
+      default: return pb_set_error(PB_EINVAL, "stream layout with %d chunks", w->nch);
+    }
+  }
+  k_q8f_general<<<(w->N + 7) / 8, 256, 0, st>>>(w->codes, w->scales, w->sdt == PB_DT_F32, d_x,
+                                                d_y, outf32, w->N, w->K, 1, w->K >= 2048 && w->K % 2048 == 0 ? 2048 : (w->K == 512 ? 512 : w->K));
+  PB_LAUNCHED("k_q8f_general");
+  return PB_OK;
+}
+
+// ---------------------------------------------------------------- C ABI
+extern "C" int pb_q8_pack(const int8_t* codes, const void* scales, int scale_dtype, int N, int K,
+                          int src_on_device, void* stream, pb_q8** out) {
+  if (!out || !codes || !scales) return pb_set_error(PB_EINVAL, "pb_q8_pack: null argument");
+  *out = nullptr;
+  if (N <= 0 || K <= 0 || K % 32) return pb_set_error(PB_EINVAL, "pb_q8_pack: bad shape %dx%d", N, K);
+  if (scale_dtype != PB_DT_F16 && scale_dtype != PB_DT_F32)
+    return pb_set_error(PB_EINVAL, "pb_q8_pack: scale dtype %d", scale_dtype);
+  cudaStream_t st = (cudaStream_t)stream;
+  pb_q8* w = new pb_q8();
+  w->N = N; w->K = K; w->sdt = scale_dtype;
+  w->layout = pb_q8_stream_ok(K) ? PB_Q8_STREAM : PB_Q8_ROWMAJOR;
+  w->nch = w->layout == PB_Q8_STREAM ? K / 2048 : 1;
+  const size_t cb = (size_t)N * K, sb = pb_q8_scale_bytes(N, K, scale_dtype);
+  if (cudaMalloc(&w->codes, cb) != cudaSuccess || cudaMalloc(&w->scales, sb) != cudaSuccess) {
+    cudaGetLastError();
+    cudaFree(w->codes); cudaFree(w->scales); delete w;
+    return pb_set_error(PB_ENOMEM, "pb_q8_pack: cannot allocate %zu bytes", cb + sb);
+  }
+  int rc = PB_OK;
+  int8_t* tc = nullptr; void* ts = nullptr;
+  if (src_on_device) {
+    rc = pb_q8_pack_into(w, codes, scales, st, N, 1, 0);
+  } else {
+    if (cudaMalloc(&tc, cb) != cudaSuccess || cudaMalloc(&ts, sb) != cudaSuccess) {
+      cudaGetLastError();
+      rc = pb_set_error(PB_ENOMEM, "pb_q8_pack: staging");
+    } else if (cudaMemcpyAsync(tc, codes, cb, cudaMemcpyHostToDevice, st) != cudaSuccess ||
+               cudaMemcpyAsync(ts, scales, sb, cudaMemcpyHostToDevice, st) != cudaSuccess) {
+      rc = pb_set_error(PB_ECUDA, "pb_q8_pack: upload failed");
+    } else {
+      rc = pb_q8_pack_into(w, tc, ts, st, N, 1, 0);
+    }
+  }
+  if (rc == PB_OK && cudaStreamSynchronize(st) != cudaSuccess)
+    rc = pb_set_error(PB_ECUDA, "pb_q8_pack: %s", cudaGetErrorString(cudaGetLastError()));
+  cudaFree(tc); cudaFree(ts);
+  if (rc != PB_OK) { cudaFree(w->codes); cudaFree(w->scales); delete w; return rc; }
+  *out = w;
+  return PB_OK;
+}
+
+extern "C" int pb_q8_free(pb_q8* w) {
+  if (!w) return PB_OK;
+  if (w->owner) { cudaFree(w->codes); cudaFree(w->scales); }
+  delete w;
+  return PB_OK;
+}
+
+extern "C" int pb_q8_shape(const pb_q8* w, int* N, int* K) {
+  if (!w) return pb_set_error(PB_EINVAL, "pb_q8_shape: null tensor");
+  if (N) *N = w->N;
+  if (K) *K = w->K;
+  return PB_OK;
+}
+
+extern "C" int pb_q8_gemv(const pb_q8* w, const uint16_t* d_x, void* d_y, int y_dtype, void* stream) {
+  if (!w || !d_x || !d_y) return pb_set_error(PB_EINVAL, "pb_q8_gemv: null argument");
+  if (y_dtype != PB_DT_BF16 && y_dtype != PB_DT_F32) return pb_set_error(PB_EINVAL, "pb_q8_gemv: y dtype");
+  if (((uintptr_t)d_x & 15) != 0) return pb_set_error(PB_EINVAL, "pb_q8_gemv: x must be 16-byte aligned");
+  return pb_q8_gemv_launch(w, d_x, d_y, y_dtype, (cudaStream_t)stream);
+}
+
+extern "C" int pb_q8_gemm(const pb_q8* w, int T, const uint16_t* d_x, void* d_y, int y_dtype,
+                          void* stream) {
+  if (!w || !d_x || !d_y || T <= 0) return pb_set_error(PB_EINVAL, "pb_q8_gemm: bad argument");
+  if (y_dtype != PB_DT_BF16 && y_dtype != PB_DT_F32) return pb_set_error(PB_EINVAL, "pb_q8_gemm: y dtype");
+  cudaStream_t st = (cudaStream_t)stream;
+  if (w->layout == PB_Q8_STREAM) {
+    // positions one at a time through the streaming kernel: same values
+    for (int t = 0; t < T; t++) {
+      const size_t ob = (size_t)t * w->N * (y_dtype == PB_DT_F32 ? 4 : 2);
+      int rc = pb_q8_gemv_launch(w, d_x + (size_t)t * w->K, (char*)d_y + ob, y_dtype, st);
+      if (rc) return rc;
+    }
+    return PB_OK;
+  }
+  const int KC = w->K >= 2048 && w->K % 2048 == 0 ? 2048 : (w->K == 512 ? 512 : w->K);
+  k_q8f_general<<<(w->N + 7) / 8, 256, 0, st>>>(w->codes, w->scales, w->sdt == PB_DT_F32, d_x, d_y,
+                                                y_dtype == PB_DT_F32, w->N, w->K, T, KC);
+  PB_LAUNCHED("k_q8f_general");
+  return PB_OK;
+}
+
+extern "C" int pb_q80_quantize(const float* d_x, int K, int8_t* d_qx, uint16_t* d_dx, void* stream) {
+  if (!d_x || !d_qx || !d_dx || K <= 0 || K % 32) return pb_set_error(PB_EINVAL, "pb_q80_quantize: bad argument");
+  k_q80_quantize<<<(K / 32 + 7) / 8, 256, 0, (cudaStream_t)stream>>>(d_x, K, d_qx, d_dx);
+  PB_LAUNCHED("k_q80_quantize");
+  return PB_OK;
+}
+
+extern "C" int pb_q80_gemv(const pb_q8* w, const int8_t* d_qx, const uint16_t* d_dx, float* d_y,
+                           int32_t* d_isum, void* stream) {
+  if (!w || !d_qx || !d_dx || !d_y) return pb_set_error(PB_EINVAL, "pb_q80_gemv: null argument");
+  if (w->layout != PB_Q8_STREAM) return pb_set_error(PB_ENOTSUP, "pb_q80_gemv: needs K %% 2048 == 0 (K=%d)", w->K);
+  if (((uintptr_t)d_qx & 15) != 0) return pb_set_error(PB_EINVAL, "pb_q80_gemv: qx must be 16-byte aligned");
+  const size_t smem = (size_t)w->K + (size_t)(w->K / 32) * 4 * 9;
+  if (smem > 200 * 1024) return pb_set_error(PB_ENOTSUP, "pb_q80_gemv: K=%d too large", w->K);
+  int grid = 2 * pb_num_sms();
+  if (grid * 8 > w->N) grid = (w->N + 7) / 8;
+  cudaStream_t st = (cudaStream_t)stream;
+  const uint4* q = reinterpret_cast<const uint4*>(w->codes);
+  if (w->sdt == PB_DT_F32) {
+    cudaFuncSetAttribute(k_q80_stream<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    k_q80_stream<true><<<grid, 256, smem, st>>>(q, w->scales, d_qx, d_dx, d_y, d_isum, w->N, w->K);
+  } else {
+    cudaFuncSetAttribute(k_q80_stream<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    k_q80_stream<false><<<grid, 256, smem, st>>>(q, w->scales, d_qx, d_dx, d_y, d_isum, w->N, w->K);
+  }
+  PB_LAUNCHED("k_q80_stream");
+  return PB_OK;
+}

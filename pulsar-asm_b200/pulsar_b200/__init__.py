@@ -1,0 +1,339 @@
+"""Python host side of the B200 quantized weight-streaming path.
+
+A thin ctypes layer over the C ABI in include/pulsar_b200.h (built as
+pulsar-asm_b200/lib/libpulsar_b200.so). Device buffers are torch CUDA tensors
+(PyTorch is used for device memory and streams only); every computation runs in
+the library's own sm_100a kernels. There is no CPU fallback: if the library is
+missing, importing the wrapper classes raises.
+
+The interface mirrors the reference engine's entry points:
+  Q8Tensor.gemv      <- gemv() / gemv_f()      lfm3_nanode.cu:1916-1966, :3634-3664
+  Q8Tensor.gemm      <- pf_gemv_T()            lfm3_nanode.cu:4840-4968
+  Q1Tensor.gemv      <- pq1 GEMV launchers     pq1_swar_sm53.cu:1129-1175
+  Model.open         <- load_blob()            lfm3_nanode.cu:1404-1733
+  Model.layer_step   <- layer_body()           lfm3_nanode.cu:3739-3856
+  Model.decode_token <- the step loop's token  lfm3_nanode.cu:5828-6300
+"""
+import ctypes as C
+import os
+import subprocess
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+PKG = os.path.dirname(HERE)
+LIB_PATH = os.path.join(PKG, "lib", "libpulsar_b200.so")
+HEADER = os.path.join(os.path.dirname(PKG), "include", "pulsar_b200.h")
+
+PB_OK = 0
+PB_DT_BF16, PB_DT_F32, PB_DT_F16 = 0, 1, 2
+ERRORS = {-1: "PB_EINVAL", -2: "PB_ENOMEM", -3: "PB_ECUDA", -4: "PB_EIO", -5: "PB_ECRC",
+          -6: "PB_EFORMAT", -8: "PB_ENOTSUP"}
+
+_lib = None
+
+
+class PBError(RuntimeError):
+    def __init__(self, code, msg):
+        super().__init__("%s (%d): %s" % (ERRORS.get(code, "?"), code, msg))
+        self.code = code
+
+
+def build(force=False):
+    """Compile the CUDA library in-tree (sm_100a)."""
+    args = ["make", "-s", "-C", PKG]
+    if force:
+        subprocess.check_call(["make", "-s", "-C", PKG, "clean"])
+    subprocess.check_call(args)
+
+
+class _Info(C.Structure):
+    _fields_ = [(n, C.c_int) for n in ("hidden", "inter", "n_layers", "n_heads", "n_kv",
+                                       "head_dim", "vocab", "conv_w", "n_attn",
+                                       "sliding_window")] + \
+               [(n, C.c_float) for n in ("rope_theta", "rope_partial", "norm_eps")] + \
+               [("weight_bytes", C.c_uint64)]
+
+
+def lib():
+    """Load libpulsar_b200.so (raises if it was not built)."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    if not os.path.exists(LIB_PATH):
+        raise OSError("libpulsar_b200.so not built (%s); run pulsar_b200.build()" % LIB_PATH)
+    L = C.CDLL(LIB_PATH)
+    vp, i, u64, sz = C.c_void_p, C.c_int, C.c_uint64, C.c_size_t
+    pvp = C.POINTER(C.c_void_p)
+    L.pb_version.restype = i
+    L.pb_last_error.argtypes = [C.c_char_p, sz]
+    L.pb_launch_count.restype = u64
+    L.pb_q8_pack.argtypes = [vp, vp, i, i, i, i, vp, pvp]
+    L.pb_q8_free.argtypes = [vp]
+    L.pb_q8_shape.argtypes = [vp, C.POINTER(i), C.POINTER(i)]
+    L.pb_q8_gemv.argtypes = [vp, vp, vp, i, vp]
+    L.pb_q8_gemm.argtypes = [vp, i, vp, vp, i, vp]
+    L.pb_q80_quantize.argtypes = [vp, i, vp, vp, vp]
+    L.pb_q80_gemv.argtypes = [vp, vp, vp, vp, vp, vp]
+    L.pb_q1_pack.argtypes = [vp, i, i, i, vp, pvp]
+    L.pb_q1_free.argtypes = [vp]
+    L.pb_q8k_quantize.argtypes = [vp, i, vp, vp]
+    L.pb_q1_gemv.argtypes = [vp, vp, vp, vp, vp]
+    L.pq1_pq1_compat_gemv.restype = None
+    L.pq1_pq1_compat_gemv.argtypes = [i, i, vp, vp, vp, vp]
+    L.pq1_pq1_compat_gemv_batch.argtypes = [C.POINTER(vp), C.POINTER(i), i, i, C.POINTER(vp), vp]
+    L.pb_open.argtypes = [C.c_char_p, i, pvp]
+    L.pb_close.argtypes = [vp]
+    L.pb_model_get_info.argtypes = [vp, C.POINTER(_Info)]
+    L.pb_tensor_id.argtypes = [vp, C.c_char_p]
+    L.pb_state_create.argtypes = [vp, i, pvp]
+    L.pb_state_destroy.argtypes = [vp]
+    L.pb_state_reset.argtypes = [vp, vp]
+    L.pb_layer_step.argtypes = [vp, vp, i, i, vp, vp]
+    L.pb_decode_token.argtypes = [vp, vp, i, i, C.POINTER(i), vp, vp]
+    L.pb_decode_greedy.argtypes = [vp, vp, i, i, i, vp, vp]
+    L.pb_state_debug.argtypes = [vp, i, pvp, C.POINTER(sz)]
+    L.pb_decode_prompt.argtypes = [vp, vp, vp, i, i, vp, vp]
+    L.pb_decode_kernels_per_token.argtypes = [vp]
+    L.pb_time_step_kernel.argtypes = [vp, vp, i, i, C.POINTER(C.c_float), C.POINTER(C.c_double), vp]
+    L.pb_test_expf.argtypes = [vp, vp, i, vp]
+    _lib = L
+    return L
+
+
+def last_error():
+    buf = C.create_string_buffer(512)
+    lib().pb_last_error(buf, 512)
+    return buf.value.decode(errors="replace")
+
+
+def check(rc):
+    if rc != PB_OK:
+        raise PBError(rc, last_error())
+    return rc
+
+
+def launch_count():
+    return int(lib().pb_launch_count())
+
+
+def _ptr(t):
+    """device pointer of a torch tensor (or None)."""
+    return None if t is None else C.c_void_p(t.data_ptr())
+
+
+def _stream(stream=None):
+    import torch
+    s = stream if stream is not None else torch.cuda.current_stream()
+    return C.c_void_p(s.cuda_stream)
+
+
+class Q8Tensor:
+    """A packed Q8 weight matrix on the device (int8 codes + per-32 scales)."""
+
+    def __init__(self, codes, scales, stream=None):
+        """codes: int8 [N, K]; scales: fp16 (Q8_0) or fp32 (.lfm3q8 dtype 1)
+        [N, K/32]; torch CUDA tensors or numpy arrays (host)."""
+        import torch
+        L = lib()
+        N, K = codes.shape
+        if isinstance(codes, torch.Tensor):
+            sdt = PB_DT_F32 if scales.dtype == torch.float32 else PB_DT_F16
+            on_dev = 1 if codes.is_cuda else 0
+            cp, sp = C.c_void_p(codes.data_ptr()), C.c_void_p(scales.data_ptr())
+        else:
+            import numpy as np
+            sdt = PB_DT_F32 if scales.dtype == np.float32 else PB_DT_F16
+            on_dev = 0
+            codes = np.ascontiguousarray(codes)
+            scales = np.ascontiguousarray(scales)
+            cp, sp = codes.ctypes.data_as(C.c_void_p), scales.ctypes.data_as(C.c_void_p)
+        h = C.c_void_p()
+        check(L.pb_q8_pack(cp, sp, sdt, N, K, on_dev, _stream(stream), C.byref(h)))
+        self.h, self.N, self.K = h, N, K
+
+    def gemv(self, x, y, stream=None):
+        """x: bf16 [K] (device); y: bf16 or fp32 [N] (device)."""
+        import torch
+        dt = PB_DT_F32 if y.dtype == torch.float32 else PB_DT_BF16
+        check(lib().pb_q8_gemv(self.h, _ptr(x), _ptr(y), dt, _stream(stream)))
+
+    def gemm(self, x, y, stream=None):
+        """x: bf16 [T, K]; y: bf16 or fp32 [T, N]."""
+        import torch
+        dt = PB_DT_F32 if y.dtype == torch.float32 else PB_DT_BF16
+        check(lib().pb_q8_gemm(self.h, x.shape[0], _ptr(x), _ptr(y), dt, _stream(stream)))
+
+    def gemv_int(self, qx, dx, y, isum=None, stream=None):
+        check(lib().pb_q80_gemv(self.h, _ptr(qx), _ptr(dx), _ptr(y), _ptr(isum), _stream(stream)))
+
+    def __del__(self):
+        try:
+            if self.h:
+                lib().pb_q8_free(self.h)
+                self.h = None
+        except Exception:
+            pass
+
+
+def q80_quantize(x, qx, dx, stream=None):
+    check(lib().pb_q80_quantize(_ptr(x), x.shape[0], _ptr(qx), _ptr(dx), _stream(stream)))
+
+
+def q8k_quantize(x, xq, stream=None):
+    check(lib().pb_q8k_quantize(_ptr(x), x.shape[0], _ptr(xq), _stream(stream)))
+
+
+class Q1Tensor:
+    """A packed Q1_0 matrix (18-byte blocks per 128 weights) on the device."""
+
+    def __init__(self, blocks, rows, K, stream=None):
+        import torch
+        if isinstance(blocks, torch.Tensor):
+            on_dev = 1 if blocks.is_cuda else 0
+            bp = C.c_void_p(blocks.data_ptr())
+        else:
+            import numpy as np
+            blocks = np.ascontiguousarray(blocks)
+            on_dev = 0
+            bp = blocks.ctypes.data_as(C.c_void_p)
+        h = C.c_void_p()
+        check(lib().pb_q1_pack(bp, rows, K, on_dev, _stream(stream), C.byref(h)))
+        self.h, self.rows, self.K = h, rows, K
+
+    def gemv(self, xq, y, isum=None, stream=None):
+        check(lib().pb_q1_gemv(self.h, _ptr(xq), _ptr(y), _ptr(isum), _stream(stream)))
+
+    def __del__(self):
+        try:
+            if self.h:
+                lib().pb_q1_free(self.h)
+                self.h = None
+        except Exception:
+            pass
+
+
+def device_expf(x, y, stream=None):
+    """test hook: the kernels' e^x on a device fp32 tensor."""
+    check(lib().pb_test_expf(_ptr(x), _ptr(y), x.numel(), _stream(stream)))
+
+
+def compat_gemv(rows, cols, w, xq, y):
+    """pq1_pq1_compat_gemv on host numpy arrays (w: Q1_0 bytes, xq: Q8_K bytes)."""
+    lib().pq1_pq1_compat_gemv(rows, cols, w.ctypes.data_as(C.c_void_p), None,
+                              y.ctypes.data_as(C.c_void_p), xq.ctypes.data_as(C.c_void_p))
+
+
+class Model:
+    """An LFM3-style backbone loaded from an .lfm3q8 blob."""
+
+    def __init__(self, path, device=0):
+        h = C.c_void_p()
+        check(lib().pb_open(path.encode(), device, C.byref(h)))
+        self.h = h
+        info = _Info()
+        check(lib().pb_model_get_info(h, C.byref(info)))
+        self.info = {k: getattr(info, k) for k, _ in _Info._fields_}
+
+    def tensor_id(self, name):
+        r = lib().pb_tensor_id(self.h, name.encode())
+        if r < 0:
+            raise PBError(r, last_error())
+        return r
+
+    def new_state(self, max_ctx):
+        return State(self, max_ctx)
+
+    def close(self):
+        if self.h:
+            lib().pb_close(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+class State:
+    """KV cache (fp16), conv rings and per-sequence control block."""
+
+    def __init__(self, model, max_ctx):
+        h = C.c_void_p()
+        check(lib().pb_state_create(model.h, max_ctx, C.byref(h)))
+        self.h, self.model, self.max_ctx = h, model, max_ctx
+
+    def reset(self, stream=None):
+        check(lib().pb_state_reset(self.h, _stream(stream)))
+
+    def layer_step(self, layer, pos, x, stream=None):
+        check(lib().pb_layer_step(self.model.h, self.h, layer, pos, _ptr(x), _stream(stream)))
+
+    def decode_token(self, token, pos, logits=None, stream=None):
+        out = C.c_int(-1)
+        check(lib().pb_decode_token(self.model.h, self.h, int(token), int(pos), C.byref(out),
+                                    _ptr(logits), _stream(stream)))
+        return out.value
+
+    def decode_token_async(self, token, pos, stream=None):
+        check(lib().pb_decode_token(self.model.h, self.h, int(token), int(pos), None, None,
+                                    _stream(stream)))
+
+    def decode_greedy(self, token, pos0, n, ids, stream=None):
+        check(lib().pb_decode_greedy(self.model.h, self.h, int(token), int(pos0), int(n),
+                                     _ptr(ids), _stream(stream)))
+
+    def decode_prompt(self, tokens, pos0, ids=None, stream=None):
+        """tokens: device int32 [n]; ids (optional device int32 [n])."""
+        check(lib().pb_decode_prompt(self.model.h, self.h, _ptr(tokens), tokens.numel(), int(pos0),
+                                     _ptr(ids), _stream(stream)))
+
+    def kernels_per_token(self):
+        r = lib().pb_decode_kernels_per_token(self.h)
+        if r < 0:
+            raise PBError(r, last_error())
+        return r
+
+    def time_step_kernel(self, which, iters, stream=None):
+        ms, nb = C.c_float(), C.c_double()
+        check(lib().pb_time_step_kernel(self.model.h, self.h, which, iters, C.byref(ms), C.byref(nb),
+                                        _stream(stream)))
+        return ms.value, nb.value
+
+    def debug_ptr(self, which):
+        p = C.c_void_p()
+        n = C.c_size_t()
+        check(lib().pb_state_debug(self.h, which, C.byref(p), C.byref(n)))
+        return p.value, n.value
+
+    def debug_tensor(self, which, dtype):
+        """copy of an internal buffer (0 kv, 1 rings, 2 final residual, 3 logits)."""
+        import torch
+        p, n = self.debug_ptr(which)
+        esz = torch.tensor([], dtype=dtype).element_size()
+        out = torch.empty(n // esz, dtype=dtype, device="cuda")
+        torch.cuda.synchronize()
+        out.view(torch.uint8).copy_(_view_device(p, n))
+        return out
+
+    def destroy(self):
+        if self.h:
+            lib().pb_state_destroy(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.destroy()
+        except Exception:
+            pass
+
+
+def _view_device(ptr, nbytes):
+    """A torch uint8 view of raw device memory owned by the library."""
+    import torch
+
+    class _A:
+        pass
+    a = _A()
+    a.__cuda_array_interface__ = {"shape": (nbytes,), "typestr": "|u1", "data": (ptr, False),
+                                  "version": 3, "strides": None}
+    return torch.as_tensor(a, device="cuda")

@@ -1,0 +1,130 @@
+"""Seeded synthetic models and inputs with the shapes and value distributions of
+the benchmark configurations (no checkpoint or dataset is available offline):
+Q8_0 codes uniform integers in [-127, 127]; fp16 scales |N(0,1)| * 0.01; norm
+weights 1 + 0.05 N(0,1); conv taps 0.5 N(0,1); Q1_0 signs uniform, fp16 scales
+|N(0,1)| * 0.02.
+"""
+import numpy as np
+
+from . import blob
+
+LFM3_CFG1 = dict(hidden=2048, inter=8192, n_layers=24, n_heads=32, n_kv=8, head_dim=64,
+                 vocab=65536, conv_w=3, rope_theta=1e6, rope_partial=1.0, norm_eps=1e-5,
+                 sliding_window=0, attn_layers=(2, 6, 10, 14, 18, 22))
+
+# small model for parity tests: same kernels (K multiple of 2048), quick oracle
+LFM3_TINY = dict(hidden=2048, inter=2048, n_layers=4, n_heads=32, n_kv=8, head_dim=64,
+                 vocab=4096, conv_w=3, rope_theta=1e6, rope_partial=1.0, norm_eps=1e-5,
+                 sliding_window=0, attn_layers=(1, 3))
+
+
+def layer_types(c):
+    return ["full_attention" if i in c["attn_layers"] else "conv" for i in range(c["n_layers"])]
+
+
+def hf_cfg(c):
+    """the blob header's cfg object (HF-style keys the loader reads)."""
+    return dict(hidden_size=c["hidden"], intermediate_size=c["inter"],
+                num_hidden_layers=c["n_layers"], num_attention_heads=c["n_heads"],
+                num_key_value_heads=c["n_kv"], head_dim=c["head_dim"], vocab_size=c["vocab"],
+                conv_L_cache=c["conv_w"], rope_theta=c["rope_theta"],
+                partial_rotary_factor=c["rope_partial"], norm_eps=c["norm_eps"],
+                layer_types=layer_types(c))
+
+
+def oracle_cfg(c, max_ctx):
+    d = dict(c)
+    d["max_ctx"] = max_ctx
+    d["layer_types"] = layer_types(c)
+    return d
+
+
+def q8(rng, N, K, scale=0.01):
+    codes = rng.integers(-127, 128, size=(N, K), dtype=np.int8)
+    sc = (np.abs(rng.standard_normal((N, K // 32), dtype=np.float32)) * np.float32(scale)).astype(np.float16)
+    return codes, sc
+
+
+def make_weights(c, seed=1234):
+    rng = np.random.default_rng(seed)
+    H, F, NH, NKV, HD, W = c["hidden"], c["inter"], c["n_heads"], c["n_kv"], c["head_dim"], c["conv_w"]
+
+    def norm(n):
+        return (1.0 + 0.05 * rng.standard_normal(n)).astype(np.float32)
+
+    layers = []
+    for L in range(c["n_layers"]):
+        d = {}
+        if L in c["attn_layers"]:
+            d["q"] = q8(rng, NH * HD, H)
+            d["k"] = q8(rng, NKV * HD, H)
+            d["v"] = q8(rng, NKV * HD, H)
+            d["gate"] = q8(rng, NH, H)
+            d["o"] = q8(rng, H, NH * HD)
+            d["q_norm"] = norm(HD)
+            d["k_norm"] = norm(HD)
+        else:
+            d["in_proj"] = q8(rng, 3 * H, H)
+            d["out_proj"] = q8(rng, H, H)
+            d["taps"] = (0.5 * rng.standard_normal((H, W))).astype(np.float32)
+        d["w1"] = q8(rng, F, H)
+        d["w3"] = q8(rng, F, H)
+        d["w2"] = q8(rng, H, F)
+        for k in ("op_norm", "post_op_norm", "ffn_norm", "post_ffn_norm"):
+            d[k] = norm(H)
+        layers.append(d)
+    return dict(layers=layers, embed=q8(rng, c["vocab"], H), final_norm=norm(H))
+
+
+NAMES_Q8 = {"q": "self_attn.q_proj", "k": "self_attn.k_proj", "v": "self_attn.v_proj",
+            "gate": "self_attn.gate_proj", "o": "self_attn.o_proj", "in_proj": "conv.in_proj",
+            "out_proj": "conv.out_proj", "w1": "feed_forward.w1", "w3": "feed_forward.w3",
+            "w2": "feed_forward.w2"}
+NAMES_F = {"q_norm": "self_attn.q_norm", "k_norm": "self_attn.k_norm", "op_norm": "operator_norm",
+           "post_op_norm": "post_operator_norm", "ffn_norm": "ffn_norm",
+           "post_ffn_norm": "post_ffn_norm"}
+
+
+def write_model(path, c, w, fp32_scales=False):
+    ts = []
+    for L, d in enumerate(w["layers"]):
+        p = "lfm.model.layers.%d." % L
+        for k, nm in NAMES_Q8.items():
+            if k in d:
+                codes, sc = d[k]
+                ts.append((p + nm + ".weight", "q8", (codes, sc.astype(np.float32) if fp32_scales else sc)))
+        for k, nm in NAMES_F.items():
+            if k in d:
+                ts.append((p + nm + ".weight", "f32", d[k]))
+        if "taps" in d:
+            ts.append((p + "conv.conv.weight", "f32", d["taps"].reshape(c["hidden"], 1, c["conv_w"])))
+    codes, sc = w["embed"]
+    ts.append(("lfm.model.embed_tokens.weight", "q8", (codes, sc.astype(np.float32) if fp32_scales else sc)))
+    ts.append(("lfm.model.embedding_norm.weight", "f32", w["final_norm"]))
+    return blob.write_blob(path, hf_cfg(c), ts)
+
+
+def weight_bytes_per_token(c, fp32_scales=False):
+    """algorithmic bytes one decode token streams: every Q8 tensor (codes +
+    scales), every fp32 vector, one embedding row."""
+    H, F, NH, NKV, HD, V, W = (c["hidden"], c["inter"], c["n_heads"], c["n_kv"], c["head_dim"],
+                               c["vocab"], c["conv_w"])
+    sb = 4 if fp32_scales else 2
+
+    def q(N, K):
+        return N * K + N * (K // 32) * sb
+    tot = 0
+    for L in range(c["n_layers"]):
+        if L in c["attn_layers"]:
+            tot += q(NH * HD, H) + 2 * q(NKV * HD, H) + q(NH, H) + q(H, NH * HD) + 2 * HD * 4
+        else:
+            tot += q(3 * H, H) + q(H, H) + H * W * 4
+        tot += 2 * q(F, H) + q(H, F) + 4 * H * 4
+    tot += q(V, H) + H * 4 + H + (H // 32) * sb
+    return tot
+
+
+def kv_bytes_per_token(c, ctx):
+    """fp16 K and V read by the attention layers at context ctx."""
+    n_attn = len(c["attn_layers"])
+    return n_attn * 2 * ctx * c["n_kv"] * c["head_dim"] * 2
