@@ -143,6 +143,18 @@ int pb_decode_greedy(pb_model* m, pb_state* s, int token, int pos0, int n, int* 
  * The prompt feed of the reference's step loop (lfm3_nanode.cu:5828-6030). */
 int pb_decode_prompt(pb_model* m, pb_state* s, const int* d_tokens, int n, int pos0, int* d_ids,
                      void* stream);
+/* pb_layer_step for callers that cannot allocate device memory (a runtime
+ * that owns every allocation through its own pool, or code that must not
+ * allocate after start-up). This entry point has no counterpart in the
+ * reference. It calls no cudaMalloc/cudaFree and no allocating routine: the
+ * layer's intermediate activations live in one static device array of at most
+ * 512 KB per GPU (held by every GPU that loads the library until exit); models
+ * needing more scratch get PB_EINVAL. The first call on a device looks up that
+ * array's device address (make it before any stream capture). All calls share
+ * the array, so calls that overlap on the GPU race: serialise them on one
+ * stream. Results are identical to pb_layer_step's. */
+int pb_layer_step_noalloc(pb_model* m, pb_state* s, int layer, int pos, uint16_t* d_x,
+                          void* stream);
 /* kernels one decode token launches (the CUDA graph's node count) */
 int pb_decode_kernels_per_token(pb_state* s);
 /* measurement hook: mean ms of one of the decode step's fused GEMV kernels

@@ -25,6 +25,8 @@
 #include <cstring>
 #include <string>
 #include <vector>
+#include <algorithm>
+#include <mutex>
 
 namespace {
 
@@ -1446,5 +1448,135 @@ __global__ void k_test_expf(const float* x, float* y, int n) {
 extern "C" int pb_test_expf(const float* d_x, float* d_y, int n, void* stream) {
   k_test_expf<<<(n + 255) / 256, 256, 0, (cudaStream_t)stream>>>(d_x, d_y, n);
   PB_LAUNCHED("k_test_expf");
+  return PB_OK;
+}
+
+// ============================================ layer step without allocation
+// Some callers cannot call cudaMalloc at all: a host runtime that owns every
+// allocation through its own pool or arena, code running where allocation is
+// forbidden after start-up, or a caller that must not grow device memory in a
+// latency-critical loop. pb_layer_step_noalloc gives them the layer step with
+// its intermediate activations (the q|k|v|gate or in_proj output, the
+// attention output, the mixer output, SiLU(w1)*w3, the w2 output, a residual
+// and the control block) in one file-scope device array instead of buffers
+// that pb_state_create allocated. The model (weights) and the state (KV cache,
+// conv rings, RoPE table) are still the caller's existing objects.
+namespace {
+constexpr size_t PB_NOALLOC_SCRATCH_BYTES = 512 * 1024;   // the stated maximum
+__device__ __align__(256) unsigned char g_noalloc_scratch[PB_NOALLOC_SCRATCH_BYTES];
+
+constexpr int PB_MAX_DEVICES = 64;
+std::mutex g_noalloc_mu;
+void* g_noalloc_ptr[PB_MAX_DEVICES] = {};
+
+__global__ void k_noalloc_set_ctl(Ctl* ctl, int pos) {
+  ctl->token = 0;
+  ctl->pos = pos;
+  ctl->step = 0;
+  ctl->counter = 0;
+  ctl->ids = nullptr;
+  ctl->prompt = nullptr;
+  ctl->n_prompt = 0;
+}
+
+struct NoAllocBufs {
+  bf16_t *res1, *h_first, *h_attn, *h_mix, *h_u, *h_w2;
+  Ctl* ctl;
+};
+
+size_t noalloc_bytes(const pb_model* m) {
+  const size_t firstn = std::max((size_t)3 * m->H, (size_t)m->NH * m->HD + 2 * (size_t)m->NKV * m->HD + m->NH);
+  return align256((size_t)m->H * 2) + align256(firstn * 2) + align256((size_t)m->NH * m->HD * 2) +
+         align256((size_t)m->H * 2) + align256((size_t)m->F * 2) + align256((size_t)m->H * 2) +
+         align256(sizeof(Ctl));
+}
+}  // namespace
+
+extern "C" int pb_layer_step_noalloc(pb_model* m, pb_state* s, int layer, int pos, uint16_t* d_x,
+                                     void* stream) {
+  if (!m || !s || !d_x || layer < 0 || layer >= m->L || pos < 0 || pos >= s->max_ctx)
+    return pb_set_error(PB_EINVAL, "pb_layer_step_noalloc: bad argument");
+  const size_t need = noalloc_bytes(m);
+  if (need > PB_NOALLOC_SCRATCH_BYTES)
+    return pb_set_error(PB_EINVAL, "pb_layer_step_noalloc: this model needs %zu bytes of scratch, "
+                        "more than the static %zu", need, PB_NOALLOC_SCRATCH_BYTES);
+  int dev = 0;
+  PB_TRY_CUDA(cudaGetDevice(&dev));
+  if (dev < 0 || dev >= PB_MAX_DEVICES) return pb_set_error(PB_EINVAL, "pb_layer_step_noalloc: device %d", dev);
+  void* base = nullptr;
+  {
+    // set-up, once per device with that device current: the array's device
+    // address (its name in host code is only a stand-in, not an address)
+    std::lock_guard<std::mutex> lk(g_noalloc_mu);
+    if (!g_noalloc_ptr[dev]) {
+      void* p = nullptr;
+      cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+      if (e != cudaSuccess || !p)
+        return pb_set_error(PB_ECUDA, "pb_layer_step_noalloc: cudaGetSymbolAddress: %s", cudaGetErrorString(e));
+      g_noalloc_ptr[dev] = p;
+    }
+    base = g_noalloc_ptr[dev];
+  }
+  char* p = reinterpret_cast<char*>(base);
+  NoAllocBufs b;
+  const size_t firstn = std::max((size_t)3 * m->H, (size_t)m->NH * m->HD + 2 * (size_t)m->NKV * m->HD + m->NH);
+  b.res1 = reinterpret_cast<bf16_t*>(p); p += align256((size_t)m->H * 2);
+  b.h_first = reinterpret_cast<bf16_t*>(p); p += align256(firstn * 2);
+  b.h_attn = reinterpret_cast<bf16_t*>(p); p += align256((size_t)m->NH * m->HD * 2);
+  b.h_mix = reinterpret_cast<bf16_t*>(p); p += align256((size_t)m->H * 2);
+  b.h_u = reinterpret_cast<bf16_t*>(p); p += align256((size_t)m->F * 2);
+  b.h_w2 = reinterpret_cast<bf16_t*>(p); p += align256((size_t)m->H * 2);
+  b.ctl = reinterpret_cast<Ctl*>(p);
+  cudaStream_t st = (cudaStream_t)stream;
+  // the previous call's control block is stale: every field it reads is set here
+  k_noalloc_set_ctl<<<1, 1, 0, st>>>(b.ctl, pos);
+  PB_LAUNCHED("k_noalloc_set_ctl");
+  const Layer& Ly = m->layers[layer];
+  int rc;
+  auto args = [&]() { StepArgs a = {}; a.H = m->H; a.eps = m->eps; a.ctl = b.ctl; a.convw = m->W; return a; };
+  StepArgs a = args();
+  a.pro = PRO_ADDNORM; a.xin = d_x; a.wnorm = Ly.op_norm; a.y = b.h_first;
+  if ((rc = launch_step(Ly.first, EPI_BF16, a, st, false))) return rc;
+  if (Ly.attn) {
+    AttnArgs t;
+    t.qkvg = b.h_first; t.qnorm = Ly.q_norm; t.knorm = Ly.k_norm;
+    t.rope_cos = s->rope_cos; t.rope_sin = s->rope_sin;
+    const size_t per = (size_t)s->max_ctx * m->NKV * m->HD;
+    t.kc = s->kv + (size_t)Ly.attn_idx * 2 * per; t.vc = t.kc + per;
+    t.out = b.h_attn; t.ctl = b.ctl;
+    t.nh = m->NH; t.nkv = m->NKV; t.half = half_rot(m); t.win = m->win; t.max_ctx = s->max_ctx;
+    t.scaling = 1.0f / sqrtf((float)m->HD); t.eps = m->eps;
+    const size_t sm = (size_t)s->max_ctx * sizeof(float);
+    switch (m->HD) {
+      case 32: cudaFuncSetAttribute(k_attn<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, 160 * 1024);
+               k_attn<1><<<m->NH, 256, sm, st>>>(t); break;
+      case 64: cudaFuncSetAttribute(k_attn<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, 160 * 1024);
+               k_attn<2><<<m->NH, 256, sm, st>>>(t); break;
+      case 128: cudaFuncSetAttribute(k_attn<4>, cudaFuncAttributeMaxDynamicSharedMemorySize, 160 * 1024);
+                k_attn<4><<<m->NH, 256, sm, st>>>(t); break;
+      default: return pb_set_error(PB_ENOTSUP, "attention head_dim %d", m->HD);
+    }
+    PB_LAUNCHED("k_attn");
+    StepArgs o = args();
+    o.pro = PRO_PLAIN; o.xin = b.h_attn; o.y = b.h_mix;
+    if ((rc = launch_step(Ly.mix, EPI_BF16, o, st, false))) return rc;
+  } else {
+    StepArgs o = args();
+    o.pro = PRO_CONV; o.xin = b.h_first; o.ring = s->ring + (size_t)Ly.conv_idx * m->W * m->H;
+    o.taps = Ly.taps; o.y = b.h_mix;
+    if ((rc = launch_step(Ly.mix, EPI_BF16, o, st, false))) return rc;
+  }
+  StepArgs c = args();
+  c.pro = PRO_ADDNORM; c.xin = d_x; c.hin = b.h_mix; c.wpost = Ly.post_op_norm; c.wnorm = Ly.ffn_norm;
+  c.rout = b.res1; c.y = b.h_u;
+  if ((rc = launch_step(Ly.w13, EPI_SILU, c, st, false))) return rc;
+  StepArgs d = args();
+  d.pro = PRO_PLAIN; d.xin = b.h_u; d.y = b.h_w2;
+  if ((rc = launch_step(Ly.w2, EPI_BF16, d, st, false))) return rc;
+  StepArgs e = args();
+  e.pro = PRO_ADDNORM; e.xin = b.res1; e.hin = b.h_w2; e.wpost = Ly.post_ffn_norm; e.wnorm = nullptr;
+  e.rout = d_x; e.K = m->H;
+  k_tail<<<1, 256, step_smem(m->H, m->H), st>>>(e);
+  PB_LAUNCHED("k_tail");
   return PB_OK;
 }

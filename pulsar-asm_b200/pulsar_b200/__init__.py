@@ -95,6 +95,7 @@ def lib():
     L.pb_decode_kernels_per_token.argtypes = [vp]
     L.pb_time_step_kernel.argtypes = [vp, vp, i, i, C.POINTER(C.c_float), C.POINTER(C.c_double), vp]
     L.pb_test_expf.argtypes = [vp, vp, i, vp]
+    L.pb_layer_step_noalloc.argtypes = [vp, vp, i, i, vp, vp]
     _lib = L
     return L
 
@@ -267,6 +268,11 @@ class State:
 
     def layer_step(self, layer, pos, x, stream=None):
         check(lib().pb_layer_step(self.model.h, self.h, layer, pos, _ptr(x), _stream(stream)))
+
+    def layer_step_noalloc(self, layer, pos, x, stream=None):
+        """the layer step with its scratch in a static device array: for callers
+        that cannot allocate device memory (same results as layer_step)."""
+        check(lib().pb_layer_step_noalloc(self.model.h, self.h, layer, pos, _ptr(x), _stream(stream)))
 
     def decode_token(self, token, pos, logits=None, stream=None):
         out = C.c_int(-1)
