@@ -40,6 +40,8 @@ def parse():
     ap.add_argument("--cpu-seconds", type=float, default=15.0)
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--blob", default=os.environ.get("PB_BENCH_BLOB", "/tmp/pb_cfg1.lfm3q8"))
+    ap.add_argument("--layers", type=int, default=0,
+                    help="profiling only: a shallower model of the same shapes (0 = the 24-layer cfg1)")
     return ap.parse_args()
 
 
@@ -114,9 +116,17 @@ class Clocks:
                 "reasons": sorted(reasons), "samples": len(sm)}
 
 
-def make_blob(path):
+def bench_cfg(layers):
     from pulsar_b200 import synth
-    c = synth.LFM3_CFG1
+    c = dict(synth.LFM3_CFG1)
+    if layers:
+        c["n_layers"] = layers
+        c["attn_layers"] = tuple(L for L in c["attn_layers"] if L < layers) or (layers - 1,)
+    return c
+
+
+def make_blob(path, c):
+    from pulsar_b200 import synth
     if os.path.exists(path) and os.path.exists(path + ".ok"):
         return c, None
     w = synth.make_weights(c, seed=SEED)
@@ -191,10 +201,11 @@ def main():
     dist.init(timeout_s=900)
     if not os.path.exists(pb.LIB_PATH):
         pb.build()
-    blob = args.blob
-    c, weights = synth.LFM3_CFG1, None
+    c = bench_cfg(args.layers)
+    blob = args.blob if not args.layers else args.blob.replace(".lfm3q8", "_L%d.lfm3q8" % args.layers)
+    weights = None
     if rank == 0:
-        c, weights = make_blob(blob)
+        c, weights = make_blob(blob, c)
     dist.barrier()
     model = pb.Model(blob, device=local)
     max_ctx = args.ctx + args.warmup + 2 * args.steps + 8
@@ -243,37 +254,46 @@ def main():
         e3.record(stream)
         e3.synchronize()
         ms_e2e = dist.max_over_ranks(e2.elapsed_time(e3), device="cuda")
-        # dominant kernel alone: the w1|w3 GEMV (34.6 MB per launch) cycling
-        # over the 24 layers' distinct weights (830 MB > L2)
+        # per-kernel path, for reference: the fused w1|w3 GEMV kernel alone
+        # (34.6 MB per launch) cycling over the 24 layers' distinct weights
         k_ms, k_bytes = st.time_step_kernel(2, 96, stream=stream)
-        head_ms, head_bytes = st.time_step_kernel(4, 8, stream=stream)
         kpt = st.kernels_per_token()
     tokens = args.steps * world
     value = tokens / (ms_max / 1000.0)
     peak, peak_kind = measured_peaks()
-    achieved = k_bytes / (k_ms / 1000.0) / 1e9
     wb = model.info["weight_bytes"]
-    kvb = synth.kv_bytes_per_token(c, args.ctx + args.warmup + args.steps // 2)
+    ctx_mid = args.ctx + args.warmup + args.steps // 2
+    kvb = synth.kv_bytes_per_token(c, ctx_mid)
+    step_s = ms / 1000.0 / args.steps
+    persistent = kpt == 1
+    if persistent:
+        # the decode kernel: one cooperative launch for the K timed tokens; its
+        # algorithmic bytes are every token's weights plus the KV it reads
+        achieved = (wb + kvb) / step_s / 1e9
+        rk = {"kernel": "k_decode (persistent, warp-specialised: TMA bulk weight stream + fused phases)",
+              "bytes_per_launch": (wb + kvb) * args.steps, "ms_per_launch": ms,
+              "bytes_per_token": wb + kvb}
+    else:
+        achieved = k_bytes / (k_ms / 1000.0) / 1e9
+        rk = {"kernel": "k_step<1,fp16 scales,SiLU epilogue> (w1|w3 GEMV, 16384x2048)",
+              "bytes_per_launch": k_bytes, "ms_per_launch": k_ms}
     line = {"metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms_max / args.steps, "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "fp32", "data": "synthetic",
             "config": {"workload": WORKLOAD, "ctx": args.ctx, "seqs_per_gpu": 1,
                        "weights": "Q8_0 int8 codes + fp16 scales per 32, activations bf16",
                        "l2": "inputs larger than L2 (1.8 GB of weights per token)",
-                       "parallelism": "sequence split, one replica per GPU (dp%d)" % world},
+                       "parallelism": "sequence split, one replica per GPU (dp%d)" % world,
+                       "decode_path": "persistent" if persistent else "graph"},
             "e2e": {"value": e2e_steps * world / (ms_e2e / 1000.0), "unit": "tok/s",
                     "h2d_bytes_per_step": 40, "d2h_bytes_per_step": 4},
             "gpu_launches": launches,
             "kernels_per_token": kpt,
-            "step_hbm_gbs": (wb + kvb) / (ms_max / args.steps / 1000.0) / 1e9,
-            "step_roofline_frac": (wb + kvb) / (ms_max / args.steps / 1000.0) / 1e9 / peak,
-            "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
-                         "frac": achieved / peak, "traffic": ncu_traffic(),
-                         "kernel": "k_step<1,fp16 scales,SiLU epilogue> (w1|w3 GEMV, 16384x2048)",
-                         "bytes_per_launch": k_bytes, "ms_per_launch": k_ms,
-                         "peak_source": "%s hbm_gbs (MEASURED_PEAKS.json)" % peak_kind if peak_kind == "measured"
-                         else "fallback 6.65 TB/s",
-                         "head_gbs": head_bytes / (head_ms / 1000.0) / 1e9},
+            "roofline": dict({"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
+                              "frac": achieved / peak, "traffic": ncu_traffic(),
+                              "peak_source": "measured hbm_gbs (MEASURED_PEAKS.json)" if peak_kind == "measured"
+                              else "fallback 6.65 TB/s"}, **rk),
+            "step_kernel_gbs": k_bytes / (k_ms / 1000.0) / 1e9,
             "clocks": clk.summary()}
     if rank == 0 and world == 1 and not args.no_cpu:
         tps, cores, n, _ = cpu_baseline(c, weights, args.ctx, args.cpu_seconds)

@@ -155,7 +155,11 @@ int pb_decode_prompt(pb_model* m, pb_state* s, const int* d_tokens, int n, int p
  * stream. Results are identical to pb_layer_step's. */
 int pb_layer_step_noalloc(pb_model* m, pb_state* s, int layer, int pos, uint16_t* d_x,
                           void* stream);
-/* kernels one decode token launches (the CUDA graph's node count) */
+/* synchronise `stream` and report a decode failure recorded on the device
+ * (a bounded wait inside the decode kernel that gave up): PB_OK or PB_ECUDA */
+int pb_state_status(pb_state* s, void* stream);
+/* kernel launches per decode token: 1 on the persistent path (one launch
+ * decodes any number of tokens), the CUDA graph's node count otherwise */
 int pb_decode_kernels_per_token(pb_state* s);
 /* measurement hook: mean ms of one of the decode step's fused GEMV kernels
  * launched alone (which: 0 first GEMV, 1 o/out_proj, 2 w1|w3, 3 w2, 4 head),

@@ -1,0 +1,410 @@
+// pb_decode.cuh -- the persistent decode kernel: every phase of a token (each
+// fused GEMV, each attention layer, the greedy argmax), for any number of
+// tokens, in ONE cooperative launch with one CTA per SM.
+//
+// Each CTA is warp-specialised:
+//  * warp 8 (the producer) streams the CTA's row slice of every GEMV of every
+//    token, in order, through a ring of DS shared-memory stages with 1-D TMA
+//    bulk copies (cp.async.bulk ... mbarrier::complete_tx). Weights never
+//    depend on activations, so the producer never waits for a phase: while the
+//    consumers sit in a grid barrier, compute a prologue or run attention, HBM
+//    keeps streaming the next GEMV's weights into the ring.
+//  * warps 0-7 (the consumers) run the phases: wait until every CTA finished
+//    the previous phase (a global arrival counter), compute the fused prologue
+//    (the same code as the per-kernel path, pb_step.cuh), then consume stages:
+//    two 2048-code segments per warp per stage, in the reference's reduction
+//    order, with the FMA chains of a lane's two blocks (l and l+32) packed into
+//    one fma.rn.f32x2 (each half is an IEEE fma, so the values are unchanged).
+// All spin waits are bounded: on a timeout the kernel records an error code,
+// the producer waits (bounded) for its copies in flight, and every thread
+// returns; the host reports the error.
+#pragma once
+#include "pb_step.cuh"
+
+namespace {
+
+constexpr int PH_GEMV = 0, PH_ATTN = 1, PH_ARGMAX = 2;
+constexpr int DSEGS = 16;                      // 2048-byte segments per stage
+constexpr int STAGE_CODES = DSEGS * 2048;      // 32 KB
+constexpr unsigned PB_WAIT_LIMIT = 1u << 24;   // polls before a wait gives up
+
+struct Phase {
+  int kind, nch, epi, _pad;
+  StepArgs a;     // GEMV: weights, prologue, epilogue
+  AttnArgs at;    // ATTN
+};
+
+struct DecodeArgs {
+  const Phase* phases;
+  int nphase;
+  int ntok;
+  Ctl* ctl;
+  unsigned* bar;       // phase arrival counter (zeroed before the launch)
+  int* err;            // 0, or the code of the wait that gave up
+  int xregion;         // floats of the activation region in shared memory
+  int nh;              // attention heads = CTAs that run an attention phase
+  int ds;              // ring stages
+};
+
+template <bool F32S>
+struct DGeo {
+  static constexpr int SB = F32S ? 8 : 4;                  // bytes per scale pair
+  static constexpr int STAGE_SCALES = DSEGS * 32 * SB;
+  static constexpr int STAGE = STAGE_CODES + STAGE_SCALES;
+};
+
+PB_DEV uint32_t smem_u32(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
+PB_DEV void mbar_init(uint64_t* b, unsigned count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(b)), "r"(count) : "memory");
+}
+PB_DEV void mbar_expect_tx(uint64_t* b, unsigned bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(b)), "r"(bytes) : "memory");
+}
+PB_DEV void mbar_arrive(uint64_t* b) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(b)) : "memory");
+}
+PB_DEV bool mbar_try(uint64_t* b, unsigned parity) {
+  uint32_t ok;
+  asm volatile("{ .reg .pred p; mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2; selp.u32 %0, 1, 0, p; }"
+               : "=r"(ok) : "r"(smem_u32(b)), "r"(parity) : "memory");
+  return ok != 0;
+}
+PB_DEV bool mbar_wait(uint64_t* b, unsigned parity, volatile int* abort_flag) {
+  for (unsigned i = 0; i < PB_WAIT_LIMIT; i++) {
+    if (mbar_try(b, parity)) return true;
+    if ((i & 255) == 255 && *abort_flag) return false;
+    if (i > 64) __nanosleep(32);
+  }
+  return false;
+}
+PB_DEV void bulk_g2s(void* dst, const void* src, unsigned bytes, uint64_t* bar) {
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
+               ::"r"(smem_u32(dst)), "l"(src), "r"(bytes), "r"(smem_u32(bar)) : "memory");
+}
+PB_DEV bool grid_wait(const unsigned* bar, unsigned target) {
+  for (unsigned i = 0; i < PB_WAIT_LIMIT; i++) {
+    unsigned v;
+    asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(bar) : "memory");
+    if (v >= target) return true;
+    if (i > 16) __nanosleep(20);
+  }
+  return false;
+}
+PB_DEV void grid_arrive(unsigned* bar) {
+  asm volatile("red.release.gpu.global.add.u32 [%0], 1;" ::"l"(bar) : "memory");
+}
+
+// packed fp32 pairs
+typedef unsigned long long f2x;
+PB_DEV f2x pk(float a, float b) {
+  f2x r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(a), "f"(b));
+  return r;
+}
+PB_DEV f2x pku(unsigned a, unsigned b) {
+  f2x r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "r"(a), "r"(b));
+  return r;
+}
+PB_DEV void upk(f2x v, float& a, float& b) { asm("mov.b64 {%0, %1}, %2;" : "=f"(a), "=f"(b) : "l"(v)); }
+PB_DEV f2x fma2(f2x a, f2x b, f2x c) {
+  f2x d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+  return d;
+}
+PB_DEV f2x add2(f2x a, f2x b) {
+  f2x d;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+
+// the two chains of lane l (block l in the low half, block l+32 in the high
+// half) over one pair of 16-code granules, continuing d
+PB_DEV f2x dot16x2(uint4 ga, uint4 gb, const f2x* xr, f2x d) {
+  const unsigned wa[4] = {ga.x, ga.y, ga.z, ga.w}, wb[4] = {gb.x, gb.y, gb.z, gb.w};
+  const f2x bias = pk(-8388736.0f, -8388736.0f);
+#pragma unroll
+  for (int k = 0; k < 4; k++) {
+    const unsigned ua = wa[k] ^ 0x80808080u, ub = wb[k] ^ 0x80808080u;
+#pragma unroll
+    for (int j = 0; j < 4; j++) {
+      const f2x c = add2(pku(__byte_perm(ua, 0x4B000000u, 0x7440u + j), __byte_perm(ub, 0x4B000000u, 0x7440u + j)), bias);
+      d = fma2(c, xr[4 * k + j], d);
+    }
+  }
+  return d;
+}
+PB_DEV float leaf2(const uint4 (&q)[4], float slo, float shi, const f2x (&xr)[32]) {
+  f2x d = pk(0.0f, 0.0f);
+  d = dot16x2(q[0], q[2], xr, d);
+  d = dot16x2(q[1], q[3], xr + 16, d);
+  float d0, d1;
+  upk(d, d0, d1);
+  return __fmaf_rn(shi, d1, __fmaf_rn(slo, d0, 0.0f));
+}
+
+PB_DEV void row_range(int N, int RB, int& r0, int& r1) {
+  const int nrb = (N + RB - 1) / RB;
+  const int rb0 = (int)(((long long)blockIdx.x * nrb) / gridDim.x);
+  const int rb1 = (int)(((long long)(blockIdx.x + 1) * nrb) / gridDim.x);
+  r0 = rb0 * RB;
+  r1 = min(rb1 * RB, N);
+}
+
+template <bool F32S>
+__device__ void producer(const DecodeArgs& d, unsigned char* ring, uint64_t* full, uint64_t* empty,
+                         volatile int* abort_flag) {
+  typedef DGeo<F32S> Gm;
+  unsigned it = 0;
+  bool ok = true;
+  for (int tok = 0; tok < d.ntok && ok; tok++) {
+    for (int p = 0; p < d.nphase && ok; p++) {
+      const Phase& ph = d.phases[p];
+      if (ph.kind != PH_GEMV) continue;
+      const int nch = ph.nch, RB = DSEGS / nch;
+      int r0, r1;
+      row_range(ph.a.N, RB, r0, r1);
+      const char* codes = reinterpret_cast<const char*>(ph.a.codes);
+      const char* sc = reinterpret_cast<const char*>(ph.a.scales);
+      for (int r = r0; r < r1; r += RB) {
+        const unsigned slot = it % d.ds, round = it / d.ds;
+        if (!mbar_wait(&empty[slot], (round & 1) ^ 1, abort_flag)) { ok = false; break; }
+        const int nr = min(RB, r1 - r);
+        const unsigned bc = (unsigned)nr * nch * 2048, bs = (unsigned)nr * nch * 32 * Gm::SB;
+        mbar_expect_tx(&full[slot], bc + bs);
+        bulk_g2s(ring + (size_t)slot * Gm::STAGE, codes + (size_t)r * nch * 2048, bc, &full[slot]);
+        bulk_g2s(ring + (size_t)slot * Gm::STAGE + STAGE_CODES, sc + (size_t)r * nch * 32 * Gm::SB, bs, &full[slot]);
+        it++;
+      }
+    }
+  }
+  if (!ok) {
+    atomicCAS(d.err, 0, 1);
+    *abort_flag = 1;
+  }
+  // never leave with copies in flight: the latest issued round of every slot
+  // must have landed (bounded wait)
+  for (unsigned s = it > (unsigned)d.ds ? it - d.ds : 0; s < it; s++) {
+    const unsigned slot = s % d.ds, round = s / d.ds;
+    unsigned i = 0;
+    while (!mbar_try(&full[slot], round & 1) && i < PB_WAIT_LIMIT) { i++; if (i > 64) __nanosleep(32); }
+  }
+}
+
+constexpr int PSLOTS = 8;   // > ring stages: a partial slot is never reused while read
+
+// One GEMV phase on the consumer warps. Warp (g, c) owns rows 2g, 2g+1 of
+// every stage in chunk c. With several chunks per row the chunk partials meet
+// in shared memory; the warp whose arrival completes a row pair (a shared
+// atomic counter) adds them in chunk order and writes the outputs, so no CTA
+// barrier sits in the stage loop. A wait that gives up breaks out of the loop
+// and the phase still ends with the same barriers as on the other warps.
+template <bool F32S, int EPI>
+__device__ void gemv_phase(const DecodeArgs& d, const Phase& ph, unsigned char* ring, float* xreg,
+                           uint64_t* full, uint64_t* empty, unsigned& it, float* red,
+                           float (*part)[DSEGS][8], int (*cnt)[8], float* bestv, int* besti,
+                           volatile int* abort_flag) {
+  typedef DGeo<F32S> Gm;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (threadIdx.x < PSLOTS * 8) (&cnt[0][0])[threadIdx.x] = 0;
+  float* sx = xreg;
+  step_prologue<1>(ph.a, sx, red);      // ends with a consumer barrier
+  // the few fields the stage loop needs, read once into registers (the loop's
+  // global stores would otherwise force the compiler to re-read them)
+  void* const yout = ph.a.y;
+  const int Nrows = ph.a.N;
+  Ctl* const ctl = ph.a.ctl;
+  const int nch = ph.nch, RB = DSEGS / nch;
+  const int c = warp % nch, g = warp / nch;
+  const int ds = d.ds;
+  f2x xr[32];
+  {
+    const float* x0 = sx + (c * 64 + lane) * 33;
+    const float* x1 = sx + (c * 64 + 32 + lane) * 33;
+#pragma unroll
+    for (int j = 0; j < 32; j++) xr[j] = pk(x0[j], x1[j]);
+  }
+  int r0, r1;
+  row_range(Nrows, RB, r0, r1);
+  float bv = -INFINITY;
+  int bi = 0x7fffffff;
+  for (int r = r0; r < r1; r += RB) {
+    const unsigned slot = it % ds, round = it / ds;
+    const unsigned ps = it % PSLOTS;
+    it++;
+    if (!mbar_wait(&full[slot], round & 1, abort_flag)) {
+      *abort_flag = 1;
+      atomicCAS(d.err, 0, 2);
+      break;
+    }
+    const unsigned char* st = ring + (size_t)slot * Gm::STAGE;
+    uint4 q[2][4];
+    float slo[2], shi[2];
+#pragma unroll
+    for (int u = 0; u < 2; u++) {
+      const int rel = g * 2 + u;
+      const int seg = rel * nch + c;
+      if (r + rel < r1) {
+        const uint4* gp = reinterpret_cast<const uint4*>(st + (size_t)seg * 2048) + lane;
+#pragma unroll
+        for (int h = 0; h < 4; h++) q[u][h] = gp[32 * h];
+        if (F32S) {
+          const float2 s2 = reinterpret_cast<const float2*>(st + STAGE_CODES)[seg * 32 + lane];
+          slo[u] = s2.x; shi[u] = s2.y;
+        } else {
+          const unsigned w = reinterpret_cast<const unsigned*>(st + STAGE_CODES)[seg * 32 + lane];
+          slo[u] = pb_h2f((unsigned short)(w & 0xffffu));
+          shi[u] = pb_h2f((unsigned short)(w >> 16));
+        }
+      } else {
+#pragma unroll
+        for (int h = 0; h < 4; h++) q[u][h] = make_uint4(0, 0, 0, 0);
+        slo[u] = shi[u] = 0.0f;
+      }
+    }
+    float v[2];
+#pragma unroll
+    for (int u = 0; u < 2; u++) v[u] = pb_warp_tree(leaf2(q[u], slo[u], shi[u], xr));
+    // the stage's data are consumed (the tree depends on every loaded value):
+    // hand the slot back to the producer
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&empty[slot]);
+    const int row0 = r + g * 2;
+    if (row0 >= r1 || lane != 0) continue;
+    float o0, o1;
+    if (nch == 1) {
+      o0 = __fadd_rn(0.0f, v[0]);
+      o1 = __fadd_rn(0.0f, v[1]);
+    } else {
+      part[ps][g * 2][c] = v[0];
+      part[ps][g * 2 + 1][c] = v[1];
+      __threadfence_block();
+      const int old = atomicAdd(&cnt[ps][g], 1);
+      if (old != nch - 1) continue;                  // not the last chunk of this row pair
+      __threadfence_block();
+      o0 = 0.0f;
+      o1 = 0.0f;
+      for (int cc = 0; cc < nch; cc++) {
+        o0 = __fadd_rn(o0, part[ps][g * 2][cc]);
+        o1 = __fadd_rn(o1, part[ps][g * 2 + 1][cc]);
+      }
+    }
+    if (EPI == EPI_SILU) {
+      // rows 2i (w1) and 2i+1 (w3): k_silu_mul_bf, lfm3_nanode.cu:821-829
+      if (row0 + 1 < r1) {
+        const float av = pb_bf2f(pb_f2bf(o0)), bw = pb_bf2f(pb_f2bf(o1));
+        reinterpret_cast<bf16_t*>(yout)[row0 >> 1] = pb_f2bf(__fmul_rn(__fmul_rn(av, pb_sigmoid(av)), bw));
+      }
+    } else if (EPI == EPI_ARGMAX) {
+      reinterpret_cast<float*>(yout)[row0] = o0;
+      if (o0 > bv || (o0 == bv && row0 < bi)) { bv = o0; bi = row0; }
+      if (row0 + 1 < r1) {
+        reinterpret_cast<float*>(yout)[row0 + 1] = o1;
+        if (o1 > bv || (o1 == bv && row0 + 1 < bi)) { bv = o1; bi = row0 + 1; }
+      }
+    } else {
+      reinterpret_cast<bf16_t*>(yout)[row0] = pb_f2bf(o0);
+      if (row0 + 1 < r1) reinterpret_cast<bf16_t*>(yout)[row0 + 1] = pb_f2bf(o1);
+    }
+  }
+  if (EPI == EPI_ARGMAX) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const float ov = __shfl_down_sync(0xffffffffu, bv, o);
+      const int oi = __shfl_down_sync(0xffffffffu, bi, o);
+      if (ov > bv || (ov == bv && oi < bi)) { bv = ov; bi = oi; }
+    }
+    if (lane == 0) { bestv[warp] = bv; besti[warp] = bi; }
+    csync<1>();
+    if (threadIdx.x == 0) {
+      float b = bestv[0];
+      int ix = besti[0];
+      for (int w = 1; w < 8; w++)
+        if (bestv[w] > b || (bestv[w] == b && besti[w] < ix)) { b = bestv[w]; ix = besti[w]; }
+      ctl->slot_val[blockIdx.x] = b;
+      ctl->slot_idx[blockIdx.x] = ix;
+    }
+  }
+}
+
+// greedy id from the per-CTA maxima (ties to the lowest index); the next
+// input is the prompt's next token while a prompt is being fed
+__device__ void argmax_phase(const DecodeArgs& d) {
+  Ctl* ctl = d.ctl;
+  float b = __ldcg(&ctl->slot_val[0]);
+  int ix = __ldcg(&ctl->slot_idx[0]);
+  for (int k = 1; k < (int)gridDim.x; k++) {
+    const float ov = __ldcg(&ctl->slot_val[k]);
+    const int oi = __ldcg(&ctl->slot_idx[k]);
+    if (ov > b || (ov == b && oi < ix)) { b = ov; ix = oi; }
+  }
+  const int step = __ldcg(&ctl->step);
+  const int np = __ldcg(&ctl->n_prompt);
+  ctl->token = (step + 1 < np) ? __ldcg(ctl->prompt + step + 1) : ix;
+  if (ctl->ids) ctl->ids[step] = ix;
+  ctl->step = step + 1;
+  ctl->pos = __ldcg(&ctl->pos) + 1;
+}
+
+template <bool F32S, int E>
+__global__ void __launch_bounds__(288, 1) k_decode(DecodeArgs d) {
+  typedef DGeo<F32S> Gm;
+  constexpr int HD = 32 * E;
+  extern __shared__ __align__(128) unsigned char dsm[];
+  unsigned char* ring = dsm;
+  float* xreg = reinterpret_cast<float*>(dsm + (size_t)d.ds * Gm::STAGE);
+  uint64_t* full = reinterpret_cast<uint64_t*>(xreg + ((d.xregion + 1) & ~1));
+  uint64_t* empty = full + d.ds;
+  __shared__ float red[16];
+  __shared__ float part[PSLOTS][DSEGS][8];
+  __shared__ int cnt[PSLOTS][8];
+  __shared__ float bestv[8];
+  __shared__ int besti[8];
+  __shared__ float qv[HD], kv[HD], vv[HD];
+  __shared__ float segred[8 * HD];
+  __shared__ int abort_flag;
+  const int warp = threadIdx.x >> 5;
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < d.ds; i++) { mbar_init(&full[i], 1); mbar_init(&empty[i], 8); }
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    abort_flag = 0;
+  }
+  __syncthreads();
+  if (warp == 8) {
+    if ((threadIdx.x & 31) == 0) producer<F32S>(d, ring, full, empty, &abort_flag);
+    return;
+  }
+  const unsigned G = gridDim.x;
+  unsigned it = 0;
+  for (int tok = 0; tok < d.ntok; tok++) {
+    for (int p = 0; p < d.nphase; p++) {
+      const unsigned q = (unsigned)(tok * d.nphase + p);
+      if (q > 0) {
+        if (threadIdx.x == 0 && !abort_flag && !grid_wait(d.bar, G * q)) { abort_flag = 1; atomicCAS(d.err, 0, 3); }
+        csync<1>();
+      }
+      if (abort_flag) return;        // every consumer thread leaves here together
+      const Phase& ph = d.phases[p];
+      if (ph.kind == PH_GEMV) {
+        if (ph.epi == EPI_SILU)
+          gemv_phase<F32S, EPI_SILU>(d, ph, ring, xreg, full, empty, it, red, part, cnt, bestv, besti, &abort_flag);
+        else if (ph.epi == EPI_ARGMAX)
+          gemv_phase<F32S, EPI_ARGMAX>(d, ph, ring, xreg, full, empty, it, red, part, cnt, bestv, besti, &abort_flag);
+        else
+          gemv_phase<F32S, EPI_BF16>(d, ph, ring, xreg, full, empty, it, red, part, cnt, bestv, besti, &abort_flag);
+      } else if (ph.kind == PH_ATTN) {
+        if ((int)blockIdx.x < d.nh) attn_body<E, 1>(ph.at, blockIdx.x, xreg, qv, kv, vv, segred, red);
+      } else {
+        if (blockIdx.x == 0 && threadIdx.x == 0) argmax_phase(d);
+      }
+      // every consumer thread's writes of this phase are issued: publish them
+      csync<1>();
+      if (threadIdx.x == 0) {
+        __threadfence();
+        grid_arrive(d.bar);
+      }
+    }
+  }
+}
+
+}  // namespace

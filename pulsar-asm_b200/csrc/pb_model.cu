@@ -19,6 +19,8 @@
 #include "pb_common.cuh"
 #include "pb_internal.h"
 #include "pb_json.h"
+#include "pb_step.cuh"
+#include "pb_decode.cuh"
 #include <zlib.h>
 #include <cmath>
 #include <cstdio>
@@ -29,164 +31,6 @@
 #include <mutex>
 
 namespace {
-
-constexpr int PRO_PLAIN = 0, PRO_ADDNORM = 1, PRO_EMBED = 2, PRO_CONV = 3;
-constexpr int EPI_BF16 = 0, EPI_SILU = 1, EPI_ARGMAX = 2;
-constexpr int MAX_CTA = 1024;
-
-// device control block of a state
-struct Ctl {
-  int token;          // input id of the step; the head writes the greedy id here
-  int pos;            // position of the step; the head advances it
-  int step;           // greedy step counter (index into ids)
-  unsigned counter;   // argmax last-CTA counter
-  int* ids;           // optional output: the greedy id of every step
-  const int* prompt;  // optional teacher-forced inputs: step i+1 feeds prompt[i+1]
-  int n_prompt;
-  int _pad;
-  float slot_val[MAX_CTA];
-  int slot_idx[MAX_CTA];
-};
-
-struct StepArgs {
-  // weight stream
-  const uint4* codes;
-  const void* scales;
-  int N;
-  // prologue
-  int pro;
-  int K;               // GEMV input length
-  int H;               // hidden size (prologue vectors)
-  float eps;
-  const bf16_t* xin;   // PLAIN: x [K]; ADDNORM: residual [H]; CONV: in_proj output [3H]
-  const bf16_t* hin;   // ADDNORM: vector to post-normalise and add (null: none)
-  const float* wpost;  // ADDNORM: its norm weight
-  const float* wnorm;  // norm giving x from the residual (null: x = residual)
-  bf16_t* rout;        // residual written by CTA 0 (null: not written)
-  const uint4* emb_codes;   // EMBED: tied table, stream layout
-  const void* emb_scales;
-  int emb_nch;
-  int emb_f32;         // EMBED: scales are fp32 pairs (else fp16 pairs)
-  bf16_t* ring;        // CONV: [W][H], slot = position mod W
-  const float* taps;   // CONV: [H][W]
-  int convw;
-  Ctl* ctl;
-  // epilogue
-  void* y;
-};
-
-// ---------------------------------------------------------------- prologue
-// RMSNorm over v (fp32 values of bf16 numbers, in shared memory) with the
-// reference's order (rmsnorm_body, lfm3_nanode.cu:383-440): thread t owns the
-// E = H/256 consecutive values [E t, E t + E), squares summed pairwise, warp
-// shuffle-down tree, the 8 warp partials ascending; rs = 1/sqrt(mean + eps)
-// correctly rounded; out = bf16(w * bf16(v * rs)).
-// sx (the GEMV input) is stored padded, one spare float per 32, so that lane
-// l reading its 32 consecutive values (index 32 l + j) hits bank (l + j) % 32.
-__device__ __forceinline__ int padx(int i) { return i + (i >> 5); }
-
-template <int E>
-__device__ void block_rmsnorm(const float* v, const float* __restrict__ w, float* out, int H,
-                              float eps, float* red, int opad) {
-  const int t = threadIdx.x;
-  float ss[E];
-#pragma unroll
-  for (int j = 0; j < E; j++) ss[j] = __fmul_rn(v[t * E + j], v[t * E + j]);
-#pragma unroll
-  for (int width = E; width > 1; width >>= 1)
-#pragma unroll
-    for (int i = 0; i < width / 2; i++) ss[i] = __fadd_rn(ss[2 * i], ss[2 * i + 1]);
-  float s = pb_warp_tree(ss[0]);
-  if ((t & 31) == 0) red[t >> 5] = s;
-  __syncthreads();
-  float tot = red[0];
-#pragma unroll
-  for (int i = 1; i < 8; i++) tot = __fadd_rn(tot, red[i]);
-  const float rs = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fmul_rn(tot, __fdiv_rn(1.0f, (float)H)), eps)));
-#pragma unroll
-  for (int j = 0; j < E; j++) {
-    const int i = t * E + j;
-    out[opad ? padx(i) : i] = pb_bf2f(pb_f2bf(__fmul_rn(w[i], pb_bf2f(pb_f2bf(__fmul_rn(v[i], rs))))));
-  }
-  __syncthreads();   // red is reused by the next call; out is complete
-}
-
-__device__ void rmsnorm_dispatch(const float* v, const float* w, float* out, int H, float eps,
-                                 float* red, int opad) {
-  switch (H >> 8) {
-    case 1: block_rmsnorm<1>(v, w, out, H, eps, red, opad); break;
-    case 2: block_rmsnorm<2>(v, w, out, H, eps, red, opad); break;
-    case 4: block_rmsnorm<4>(v, w, out, H, eps, red, opad); break;
-    case 8: block_rmsnorm<8>(v, w, out, H, eps, red, opad); break;
-    case 16: block_rmsnorm<16>(v, w, out, H, eps, red, opad); break;
-    default: break;
-  }
-}
-
-// Computes the GEMV input x (fp32 values of bf16 numbers) into sx, padded
-// (element i at padx(i)); sx must not overlap sa/sb.
-// Scratch sa/sb hold H floats each. Requires blockDim.x == 256.
-__device__ void step_prologue(const StepArgs& a, float* sx, float* sa, float* sb, float* red) {
-  const int t = threadIdx.x, H = a.H;
-  if (a.pro == PRO_PLAIN) {
-    for (int i = t; i < a.K; i += 256) sx[padx(i)] = pb_bf2f(a.xin[i]);
-    __syncthreads();
-    return;
-  }
-  if (a.pro == PRO_CONV) {
-    // lfm3_nanode.cu:3790-3818: bx = bf16(B*x) enters the ring as the newest
-    // slot; y = sum_k taps[i][k] * ring_k (oldest first); out = bf16(C * bf16(y)).
-    const int pos = a.ctl->pos, W = a.convw;
-    for (int i = t; i < H; i += 256) {
-      const float B = pb_bf2f(a.xin[i]), C = pb_bf2f(a.xin[H + i]), X = pb_bf2f(a.xin[2 * H + i]);
-      const bf16_t bx = pb_f2bf(__fmul_rn(B, X));
-      if (blockIdx.x == 0) a.ring[(size_t)(pos % W) * H + i] = bx;
-      float acc = 0.0f;
-      for (int k = 0; k < W; k++) {
-        const int p = pos - (W - 1) + k;
-        const float r = (k == W - 1) ? pb_bf2f(bx) : pb_bf2f(a.ring[(size_t)(((p % W) + W) % W) * H + i]);
-        acc = __fadd_rn(acc, __fmul_rn(a.taps[(size_t)i * W + k], r));
-      }
-      sx[padx(i)] = pb_bf2f(pb_f2bf(__fmul_rn(C, pb_bf2f(pb_f2bf(acc)))));
-    }
-    __syncthreads();
-    return;
-  }
-  // residual into sa
-  if (a.pro == PRO_EMBED) {
-    // k_dequant_row (lfm3_nanode.cu:138-142): bf16(code * scale), row = token
-    const int tok = a.ctl->token;
-    const int nch = a.emb_nch;
-    const int8_t* cb = reinterpret_cast<const int8_t*>(a.emb_codes);
-    for (int i = t; i < H; i += 256) {
-      const int b = i >> 5, j = i & 31, c = b >> 6, bb = b & 63, l = bb & 31, half = bb >> 5;
-      const size_t seg = (size_t)tok * nch + c;
-      const int gi = (half * 2 + (j >> 4)) * 32 + l;
-      const float code = (float)cb[(seg * 128 + gi) * 16 + (j & 15)];
-      const float s = a.emb_f32 ? reinterpret_cast<const float*>(a.emb_scales)[(seg * 32 + l) * 2 + half]
-                                : pb_h2f(reinterpret_cast<const unsigned short*>(a.emb_scales)[(seg * 32 + l) * 2 + half]);
-      sa[i] = pb_bf2f(pb_f2bf(__fmul_rn(code, s)));
-    }
-    __syncthreads();
-  } else {
-    for (int i = t; i < H; i += 256) sa[i] = pb_bf2f(a.xin[i]);
-    if (a.hin) {
-      for (int i = t; i < H; i += 256) sb[i] = pb_bf2f(a.hin[i]);
-      __syncthreads();
-      rmsnorm_dispatch(sb, a.wpost, sb, H, a.eps, red, 0);    // in place: each thread owns its values
-      for (int i = t; i < H; i += 256) sa[i] = pb_bf2f(pb_f2bf(__fadd_rn(sa[i], sb[i])));
-    }
-    __syncthreads();
-  }
-  if (a.rout && blockIdx.x == 0)
-    for (int i = t; i < H; i += 256) a.rout[i] = pb_f2bf(sa[i]);
-  if (a.wnorm) rmsnorm_dispatch(sa, a.wnorm, sx, H, a.eps, red, 1);
-  else {
-    for (int i = t; i < H; i += 256) sx[padx(i)] = sa[i];
-    __syncthreads();
-  }
-}
-
 
 // ------------------------------------------------------------ step GEMV
 // The streaming GEMV of pb_q8.cu (same granule layout, same leaf chains and
@@ -249,9 +93,7 @@ __global__ void __launch_bounds__(256, 2) k_step(StepArgs a) {
   constexpr int U = 2, G = 8 / NCH, RB = G * U;
   extern __shared__ __align__(16) float smem[];
   float* sx = smem;                          // K + K/32 (padded)
-  float* sa = sx + a.K + (a.K >> 5);         // H
-  float* sb = sa + a.H;                      // H
-  __shared__ float red[8];
+  __shared__ float red[16];
   __shared__ float part[2][RB][NCH];
   __shared__ float bestv[8];
   __shared__ int besti[8];
@@ -268,7 +110,7 @@ __global__ void __launch_bounds__(256, 2) k_step(StepArgs a) {
   }
   pb_grid_launch_dependents();
   pb_grid_wait();
-  step_prologue(a, sx, sa, sb, red);
+  step_prologue<0>(a, sx, red);
   float xr[64];
   {
     const float* x0 = sx + (c * 64 + lane) * 33;          // block c*64 + lane, padded
@@ -399,190 +241,25 @@ __global__ void __launch_bounds__(256, 2) k_step(StepArgs a) {
 }
 
 // ------------------------------------------------------------- attention
-struct AttnArgs {
-  const bf16_t* qkvg;      // [NH*HD | NKV*HD | NKV*HD | NH]
-  const float* qnorm;      // [HD]
-  const float* knorm;      // [HD]
-  const float* rope_cos;   // [max_ctx][half]
-  const float* rope_sin;
-  unsigned short* kc;      // fp16 [max_ctx][NKV][HD]
-  unsigned short* vc;
-  bf16_t* out;             // [NH*HD] gated attention output
-  Ctl* ctl;
-  int nh, nkv, half, win, max_ctx;
-  float scaling, eps;
-};
-
-// per-head RMSNorm (k_headnorm, lfm3_nanode.cu:460-479) + NeoX RoPE
-// (k_rope, :483-498) by one warp; result (fp32 of bf16) into o[HD]
-template <int E>
-__device__ void head_norm_rope(const bf16_t* __restrict__ x, const float* __restrict__ w,
-                               const float* cs, const float* sn, int half, float eps, float* o) {
-  const int lane = threadIdx.x & 31;
-  constexpr int HD = 32 * E;
-  float v[E], ss[E];
-#pragma unroll
-  for (int j = 0; j < E; j++) { v[j] = pb_bf2f(x[lane * E + j]); ss[j] = __fmul_rn(v[j], v[j]); }
-#pragma unroll
-  for (int width = E; width > 1; width >>= 1)
-#pragma unroll
-    for (int i = 0; i < width / 2; i++) ss[i] = __fadd_rn(ss[2 * i], ss[2 * i + 1]);
-  float s = pb_warp_tree(__fadd_rn(ss[0], 0.0f));
-  s = __shfl_sync(0xffffffffu, s, 0);
-  const float rs = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fmul_rn(s, __fdiv_rn(1.0f, (float)HD)), eps)));
-#pragma unroll
-  for (int j = 0; j < E; j++) {
-    const int i = lane * E + j;
-    o[i] = pb_bf2f(pb_f2bf(__fmul_rn(w[i], pb_bf2f(pb_f2bf(__fmul_rn(v[j], rs))))));
-  }
-  __syncwarp();
-  float lo_n[E], hi_n[E];
-#pragma unroll
-  for (int j = 0; j < E; j++) {
-    const int i = lane * E + j;   // i < HD/2 covers the pairs when i < half
-    if (i < half) {
-      const float lo = o[i], hi = o[i + HD / 2];
-      lo_n[j] = pb_bf2f(pb_f2bf(__fadd_rn(__fmul_rn(lo, cs[i]), __fmul_rn(-hi, sn[i]))));
-      hi_n[j] = pb_bf2f(pb_f2bf(__fadd_rn(__fmul_rn(hi, cs[i]), __fmul_rn(lo, sn[i]))));
-    }
-  }
-  __syncwarp();
-#pragma unroll
-  for (int j = 0; j < E; j++) {
-    const int i = lane * E + j;
-    if (i < half) { o[i] = lo_n[j]; o[i + HD / 2] = hi_n[j]; }
-  }
-  __syncwarp();
-}
-
-// k_attn_head (lfm3_nanode.cu:503-602) for one q head over the fp16 cache,
-// with the q/k prologue and the sigmoid gate (k_sigmoid_gate, :852-864) fused.
-// The current position's k/v are used from shared memory (the CTA of the
-// group's first q head also appends them to the cache), so no CTA reads a
-// cache row another CTA of this launch writes.
 template <int E>
 __global__ void __launch_bounds__(256) k_attn(AttnArgs a) {
   constexpr int HD = 32 * E;
   extern __shared__ __align__(16) float sl[];     // scores [max_ctx]
   __shared__ float qv[HD], kv[HD], vv[HD];
   __shared__ float red[8];
-  __shared__ float segred[8][HD];
-  const int h = blockIdx.x, t = threadIdx.x, lane = t & 31, wid = t >> 5;
-  const int grp = a.nh / a.nkv, kvh = h / grp;
+  __shared__ float segred[8 * HD];
   pb_grid_launch_dependents();
   pb_grid_wait();
-  const int pos = a.ctl->pos;
-  const int npos = pos + 1;
-  const int lo = (a.win > 0 && npos > a.win) ? npos - a.win : 0;
-  const int np = npos - lo;
-  const float* cs = a.rope_cos + (size_t)pos * a.half;
-  const float* sn = a.rope_sin + (size_t)pos * a.half;
-  const size_t qoff = 0, koff = (size_t)a.nh * HD, voff = koff + (size_t)a.nkv * HD,
-               goff = voff + (size_t)a.nkv * HD;
-  if (wid == 0) head_norm_rope<E>(a.qkvg + qoff + (size_t)h * HD, a.qnorm, cs, sn, a.half, a.eps, qv);
-  if (wid == 1) {
-    head_norm_rope<E>(a.qkvg + koff + (size_t)kvh * HD, a.knorm, cs, sn, a.half, a.eps, kv);
-#pragma unroll
-    for (int j = 0; j < E; j++) {
-      const int i = lane * E + j;
-      const unsigned short k16 = pb_f2h(kv[i]);
-      kv[i] = pb_h2f(k16);
-      if (h % grp == 0) a.kc[((size_t)pos * a.nkv + kvh) * HD + i] = k16;
-    }
-  }
-  if (wid == 2) {
-#pragma unroll
-    for (int j = 0; j < E; j++) {
-      const int i = lane * E + j;
-      const unsigned short v16 = pb_f2h(pb_bf2f(a.qkvg[voff + (size_t)kvh * HD + i]));
-      vv[i] = pb_h2f(v16);
-      if (h % grp == 0) a.vc[((size_t)pos * a.nkv + kvh) * HD + i] = v16;
-    }
-  }
-  __syncthreads();
-  // scores: position p by warp (p - lo) % 8, lane chains over its E dims
-  float ql[E];
-#pragma unroll
-  for (int j = 0; j < E; j++) ql[j] = qv[lane * E + j];
-  for (int p = lo + wid; p < npos; p += 8) {
-    float kl[E];
-    if (p == pos) {
-#pragma unroll
-      for (int j = 0; j < E; j++) kl[j] = kv[lane * E + j];
-    } else {
-      const unsigned short* kr = a.kc + ((size_t)p * a.nkv + kvh) * HD + lane * E;
-#pragma unroll
-      for (int j = 0; j < E; j++) kl[j] = pb_h2f(kr[j]);
-    }
-    float s = 0.0f;
-#pragma unroll
-    for (int j = 0; j < E; j++) s = __fadd_rn(s, __fmul_rn(ql[j], kl[j]));
-    s = pb_warp_tree(s);
-    if (lane == 0) sl[p - lo] = __fmul_rn(s, a.scaling);
-  }
-  __syncthreads();
-  float mx = -1e30f;
-  for (int i = t; i < np; i += 256) mx = fmaxf(mx, sl[i]);
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_down_sync(0xffffffffu, mx, o));
-  if (lane == 0) red[wid] = mx;
-  __syncthreads();
-  float m = red[0];
-#pragma unroll
-  for (int i = 1; i < 8; i++) m = fmaxf(m, red[i]);
-  __syncthreads();
-  float sum = 0.0f;
-  for (int i = t; i < np; i += 256) {
-    const float e = pb_expf(__fadd_rn(sl[i], -m));
-    sl[i] = e;
-    sum = __fadd_rn(sum, e);
-  }
-  sum = pb_warp_tree(sum);
-  if (lane == 0) red[wid] = sum;
-  __syncthreads();
-  // 8-lane shuffle-down tree: ((r0+r4)+(r2+r6))+((r1+r5)+(r3+r7))
-  const float tot = __fadd_rn(__fadd_rn(__fadd_rn(red[0], red[4]), __fadd_rn(red[2], red[6])),
-                              __fadd_rn(__fadd_rn(red[1], red[5]), __fadd_rn(red[3], red[7])));
-  const float inv = __fdiv_rn(1.0f, tot);
-  // P.V: segment = warp, lane owns dims lane*E .. +E
-  float acc[E];
-#pragma unroll
-  for (int j = 0; j < E; j++) acc[j] = 0.0f;
-  for (int p = wid; p < np; p += 8) {
-    const float w = __fmul_rn(sl[p], inv);
-    const int ap = lo + p;
-    float vl[E];
-    if (ap == pos) {
-#pragma unroll
-      for (int j = 0; j < E; j++) vl[j] = vv[lane * E + j];
-    } else {
-      const unsigned short* vr = a.vc + ((size_t)ap * a.nkv + kvh) * HD + lane * E;
-#pragma unroll
-      for (int j = 0; j < E; j++) vl[j] = pb_h2f(vr[j]);
-    }
-#pragma unroll
-    for (int j = 0; j < E; j++) acc[j] = __fadd_rn(acc[j], __fmul_rn(w, vl[j]));
-  }
-#pragma unroll
-  for (int j = 0; j < E; j++) segred[wid][lane * E + j] = acc[j];
-  __syncthreads();
-  if (t < HD) {
-    const float o = __fadd_rn(__fadd_rn(__fadd_rn(segred[0][t], segred[1][t]), __fadd_rn(segred[2][t], segred[3][t])),
-                              __fadd_rn(__fadd_rn(segred[4][t], segred[5][t]), __fadd_rn(segred[6][t], segred[7][t])));
-    const float sg = pb_sigmoid(pb_bf2f(a.qkvg[goff + h]));
-    a.out[(size_t)h * HD + t] = pb_f2bf(__fmul_rn(pb_bf2f(pb_f2bf(o)), sg));
-  }
+  attn_body<E, 0>(a, blockIdx.x, sl, qv, kv, vv, segred, red);
 }
 
 // residual tail for the standalone layer step: x = R + bf16(rms(h, w))
 __global__ void __launch_bounds__(256) k_tail(StepArgs a) {
   extern __shared__ __align__(16) float smem[];
-  __shared__ float red[8];
+  __shared__ float red[16];
   pb_grid_launch_dependents();
   pb_grid_wait();
-  float* sx = smem;
-  float* sa = sx + a.K + (a.K >> 5);
-  step_prologue(a, sx, sa, sa + a.H, red);
+  step_prologue<0>(a, smem, red);
 }
 
 // ----------------------------------------------------------- host model
@@ -643,6 +320,14 @@ struct pb_state {
   Ctl* h_ctl = nullptr;           // pinned host mirror for token/pos uploads
   char* mem = nullptr;
   size_t mem_bytes = 0;
+  // persistent decode kernel: phase table, arrival counter, error word
+  Phase* d_phases = nullptr;
+  int nphase = 0;
+  unsigned* d_bar = nullptr;
+  int* d_err = nullptr;
+  int xregion = 0, ds = 0;
+  size_t dsmem = 0;
+  bool persistent = true;
   cudaGraph_t graph = nullptr;
   cudaGraphExec_t exec = nullptr;
   cudaStream_t graph_stream = nullptr;
@@ -873,6 +558,197 @@ int build_graph(pb_state* s) {
   s->exec = ex;
   s->graph_res = fr;
   s->graph_launches = nk;
+  return PB_OK;
+}
+
+// ---- persistent decode ---------------------------------------------------
+Phase gemv_phase_of(const pb_q8& w, int epi, StepArgs a) {
+  Phase ph = {};
+  ph.kind = PH_GEMV;
+  ph.nch = w.nch;
+  ph.epi = epi;
+  a.codes = reinterpret_cast<const uint4*>(w.codes);
+  a.scales = w.scales;
+  a.N = w.N;
+  a.K = w.K;
+  ph.a = a;
+  return ph;
+}
+
+AttnArgs attn_args(const pb_model* m, pb_state* s, int layer) {
+  const Layer& Ly = m->layers[layer];
+  AttnArgs a;
+  a.qkvg = s->h_first;
+  a.qnorm = Ly.q_norm;
+  a.knorm = Ly.k_norm;
+  a.rope_cos = s->rope_cos;
+  a.rope_sin = s->rope_sin;
+  const size_t per = (size_t)s->max_ctx * m->NKV * m->HD;
+  a.kc = s->kv + (size_t)Ly.attn_idx * 2 * per;
+  a.vc = a.kc + per;
+  a.out = s->h_attn;
+  a.ctl = s->ctl;
+  a.nh = m->NH; a.nkv = m->NKV; a.half = half_rot(m); a.win = m->win; a.max_ctx = s->max_ctx;
+  a.scaling = 1.0f / sqrtf((float)m->HD);
+  a.eps = m->eps;
+  return a;
+}
+
+// The token as a phase list: the same kernels' work, in the same order and
+// with the same buffers, as enqueue_token.
+int build_phases(pb_state* s) {
+  if (s->d_phases) return PB_OK;
+  pb_model* m = s->m;
+  std::vector<Phase> ph;
+  int cur = 0;
+  for (int L = 0; L < m->L; L++) {
+    const Layer& Ly = m->layers[L];
+    StepArgs a = base_args(m, s);
+    a.wnorm = Ly.op_norm;
+    a.y = s->h_first;
+    if (L == 0) {
+      a.pro = PRO_EMBED;
+      a.emb_codes = reinterpret_cast<const uint4*>(m->head.codes);
+      a.emb_scales = m->head.scales;
+      a.emb_nch = m->head.nch;
+      a.emb_f32 = m->head.sdt == PB_DT_F32;
+      a.rout = s->res[cur];
+    } else {
+      a.pro = PRO_ADDNORM;
+      a.xin = s->res[cur];
+      a.hin = s->h_w2;
+      a.wpost = m->layers[L - 1].post_ffn_norm;
+      a.rout = s->res[cur ^ 1];
+      cur ^= 1;
+    }
+    ph.push_back(gemv_phase_of(Ly.first, EPI_BF16, a));
+    StepArgs b = base_args(m, s);
+    b.y = s->h_mix;
+    if (Ly.attn) {
+      Phase at = {};
+      at.kind = PH_ATTN;
+      at.at = attn_args(m, s, L);
+      ph.push_back(at);
+      b.pro = PRO_PLAIN;
+      b.xin = s->h_attn;
+    } else {
+      b.pro = PRO_CONV;
+      b.xin = s->h_first;
+      b.ring = s->ring + (size_t)Ly.conv_idx * m->W * m->H;
+      b.taps = Ly.taps;
+    }
+    ph.push_back(gemv_phase_of(Ly.mix, EPI_BF16, b));
+    StepArgs c = base_args(m, s);
+    c.pro = PRO_ADDNORM;
+    c.xin = s->res[cur];
+    c.hin = s->h_mix;
+    c.wpost = Ly.post_op_norm;
+    c.wnorm = Ly.ffn_norm;
+    c.rout = s->res[cur ^ 1];
+    cur ^= 1;
+    c.y = s->h_u;
+    ph.push_back(gemv_phase_of(Ly.w13, EPI_SILU, c));
+    StepArgs d = base_args(m, s);
+    d.pro = PRO_PLAIN;
+    d.xin = s->h_u;
+    d.y = s->h_w2;
+    ph.push_back(gemv_phase_of(Ly.w2, EPI_BF16, d));
+  }
+  StepArgs h = base_args(m, s);
+  h.pro = PRO_ADDNORM;
+  h.xin = s->res[cur];
+  h.hin = s->h_w2;
+  h.wpost = m->layers[m->L - 1].post_ffn_norm;
+  h.wnorm = m->final_norm;
+  h.rout = s->res[cur ^ 1];
+  s->graph_res = cur ^ 1;
+  h.y = s->logits;
+  ph.push_back(gemv_phase_of(m->head, EPI_ARGMAX, h));
+  Phase am = {};
+  am.kind = PH_ARGMAX;
+  ph.push_back(am);
+  // shared-memory plan: activation region, then as many ring stages as fit
+  int xr = s->max_ctx;
+  for (auto& p : ph)
+    if (p.kind == PH_GEMV) {
+      const int need = p.a.K + p.a.K / 32 + ((p.a.pro == PRO_ADDNORM || p.a.pro == PRO_EMBED) ? 2 * m->H : 0);
+      xr = std::max(xr, need);
+    }
+  int dev = 0;
+  cudaGetDevice(&dev);
+  int optin = 0;
+  cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
+  const size_t stage = m->sdt == PB_DT_F32 ? DGeo<true>::STAGE : DGeo<false>::STAGE;
+  const size_t static_est = 14 * 1024;
+  const size_t xb = (size_t)((xr + 1) & ~1) * 4;
+  long avail = (long)optin - (long)static_est - (long)xb - 2 * 8 * 8;
+  int ds = (int)std::min<long>(6, avail / (long)stage);
+  if (ds < 2) return pb_set_error(PB_ENOTSUP, "persistent decode: shared memory for %d ring stages", ds);
+  s->ds = ds;
+  s->xregion = xr;
+  s->dsmem = (size_t)ds * stage + xb + 2 * (size_t)ds * 8;
+  s->nphase = (int)ph.size();
+  if (cudaMalloc(&s->d_phases, ph.size() * sizeof(Phase)) != cudaSuccess) {
+    cudaGetLastError();
+    s->d_phases = nullptr;
+    return pb_set_error(PB_ENOMEM, "persistent decode: phase table");
+  }
+  PB_TRY_CUDA(cudaMemcpy(s->d_phases, ph.data(), ph.size() * sizeof(Phase), cudaMemcpyHostToDevice));
+  return PB_OK;
+}
+
+template <bool F32S, int E>
+int launch_decode_t(pb_state* s, int ntok, cudaStream_t st) {
+  DecodeArgs d;
+  d.phases = s->d_phases;
+  d.nphase = s->nphase;
+  d.ntok = ntok;
+  d.ctl = s->ctl;
+  d.bar = s->d_bar;
+  d.err = s->d_err;
+  d.xregion = s->xregion;
+  d.nh = s->m->NH;
+  d.ds = s->ds;
+  static bool set = false;
+  if (!set) {
+    PB_TRY_CUDA(cudaFuncSetAttribute(k_decode<F32S, E>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)s->dsmem));
+    set = true;
+  }
+  int per_sm = 0;
+  PB_TRY_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k_decode<F32S, E>, 288, s->dsmem));
+  if (per_sm < 1) return pb_set_error(PB_ENOTSUP, "persistent decode does not fit on an SM");
+  const int grid = pb_num_sms();
+  if (grid > MAX_CTA || grid < s->m->NH) return pb_set_error(PB_ENOTSUP, "persistent decode grid %d", grid);
+  PB_TRY_CUDA(cudaMemsetAsync(s->d_bar, 0, sizeof(unsigned), st));
+  void* args[] = {&d};
+  cudaError_t e = cudaLaunchCooperativeKernel((const void*)k_decode<F32S, E>, dim3(grid), dim3(288), args,
+                                              s->dsmem, st);
+  if (e != cudaSuccess) return pb_set_error(PB_ECUDA, "launch k_decode: %s", cudaGetErrorString(e));
+  pb_count_launch();
+  return PB_OK;
+}
+
+int launch_decode(pb_state* s, int ntok, cudaStream_t st) {
+  int rc = build_phases(s);
+  if (rc) return rc;
+  const bool f = s->m->sdt == PB_DT_F32;
+  switch (s->m->HD) {
+    case 32: return f ? launch_decode_t<true, 1>(s, ntok, st) : launch_decode_t<false, 1>(s, ntok, st);
+    case 64: return f ? launch_decode_t<true, 2>(s, ntok, st) : launch_decode_t<false, 2>(s, ntok, st);
+    case 128: return f ? launch_decode_t<true, 4>(s, ntok, st) : launch_decode_t<false, 4>(s, ntok, st);
+  }
+  return pb_set_error(PB_ENOTSUP, "persistent decode: head_dim %d", s->m->HD);
+}
+
+// the kernel's error word (a bounded wait gave up); clears it
+int check_decode_error(pb_state* s, cudaStream_t st) {
+  int e = 0;
+  PB_TRY_CUDA(cudaMemcpyAsync(&e, s->d_err, sizeof(int), cudaMemcpyDeviceToHost, st));
+  PB_TRY_CUDA(cudaStreamSynchronize(st));
+  if (e) {
+    cudaMemsetAsync(s->d_err, 0, sizeof(int), st);
+    return pb_set_error(PB_ECUDA, "decode kernel: a bounded wait gave up (code %d)", e);
+  }
   return PB_OK;
 }
 
@@ -1194,6 +1070,10 @@ extern "C" int pb_state_create(pb_model* m, int max_ctx, pb_state** out) {
   pb_state* s = new pb_state();
   s->m = m;
   s->max_ctx = max_ctx;
+  {
+    const char* mode = getenv("PB_DECODE_MODE");   // "graph": the per-kernel CUDA-graph path
+    s->persistent = !(mode && strcmp(mode, "graph") == 0);
+  }
   const int H = m->H, n_conv = m->L - m->n_attn, half = half_rot(m);
   const size_t kvb = (size_t)m->n_attn * 2 * max_ctx * m->NKV * m->HD * 2;
   const size_t ringb = (size_t)n_conv * m->W * H * 2;
@@ -1201,7 +1081,7 @@ extern "C" int pb_state_create(pb_model* m, int max_ctx, pb_state** out) {
   const size_t firstn = std::max((size_t)3 * H, (size_t)m->NH * m->HD + 2 * (size_t)m->NKV * m->HD + m->NH);
   size_t sizes[] = {kvb, ringb, ropeb, ropeb, (size_t)H * 2, (size_t)H * 2, (size_t)H * 2, firstn * 2,
                     (size_t)m->NH * m->HD * 2, (size_t)H * 2, (size_t)m->F * 2, (size_t)H * 2,
-                    (size_t)m->V * 4, sizeof(Ctl)};
+                    (size_t)m->V * 4, sizeof(Ctl), 256, 256};
   size_t tot = 0;
   for (size_t x : sizes) tot += align256(x);
   if (cudaMalloc(&s->mem, tot) != cudaSuccess) { cudaGetLastError(); delete s; return pb_set_error(PB_ENOMEM, "pb_state_create: %zu bytes", tot); }
@@ -1210,7 +1090,7 @@ extern "C" int pb_state_create(pb_model* m, int max_ctx, pb_state** out) {
   void** slots[] = {(void**)&s->kv, (void**)&s->ring, (void**)&s->rope_cos, (void**)&s->rope_sin,
                     (void**)&s->res[0], (void**)&s->res[1], (void**)&s->res[2], (void**)&s->h_first,
                     (void**)&s->h_attn, (void**)&s->h_mix, (void**)&s->h_u, (void**)&s->h_w2,
-                    (void**)&s->logits, (void**)&s->ctl};
+                    (void**)&s->logits, (void**)&s->ctl, (void**)&s->d_bar, (void**)&s->d_err};
   for (size_t i = 0; i < sizeof(sizes) / sizeof(sizes[0]); i++) { *slots[i] = p; p += align256(sizes[i]); }
   if (cudaMallocHost(&s->h_ctl, sizeof(Ctl)) != cudaSuccess) {
     cudaGetLastError(); cudaFree(s->mem); delete s;
@@ -1239,6 +1119,7 @@ extern "C" int pb_state_create(pb_model* m, int max_ctx, pb_state** out) {
 
 extern "C" int pb_state_destroy(pb_state* s) {
   if (!s) return PB_OK;
+  if (s->d_phases) cudaFree(s->d_phases);
   if (s->exec) cudaGraphExecDestroy(s->exec);
   if (s->graph) cudaGraphDestroy(s->graph);
   if (s->graph_stream) cudaStreamDestroy(s->graph_stream);
@@ -1257,6 +1138,7 @@ extern "C" int pb_state_reset(pb_state* s, void* stream) {
   if (kvb) PB_TRY_CUDA(cudaMemsetAsync(s->kv, 0, kvb, st));
   if (ringb) PB_TRY_CUDA(cudaMemsetAsync(s->ring, 0, ringb, st));
   PB_TRY_CUDA(cudaMemsetAsync(s->ctl, 0, sizeof(Ctl), st));
+  PB_TRY_CUDA(cudaMemsetAsync(s->d_err, 0, sizeof(int), st));
   return PB_OK;
 }
 
@@ -1304,14 +1186,21 @@ extern "C" int pb_decode_token(pb_model* m, pb_state* s, int token, int pos, int
   if (!m || !s || token < 0 || token >= m->V || pos < 0 || pos >= s->max_ctx)
     return pb_set_error(PB_EINVAL, "pb_decode_token: bad argument");
   cudaStream_t st = (cudaStream_t)stream;
-  int rc = build_graph(s);
-  if (rc) return rc;
-  if ((rc = set_ctl(s, token, pos, nullptr, st))) return rc;
-  PB_TRY_CUDA(cudaGraphLaunch(s->exec, st));
-  pb_count_launch(s->graph_launches);
+  int rc;
+  if (s->persistent) {
+    if ((rc = build_phases(s))) return rc;
+    if ((rc = set_ctl(s, token, pos, nullptr, st))) return rc;
+    if ((rc = launch_decode(s, 1, st))) return rc;
+  } else {
+    if ((rc = build_graph(s))) return rc;
+    if ((rc = set_ctl(s, token, pos, nullptr, st))) return rc;
+    PB_TRY_CUDA(cudaGraphLaunch(s->exec, st));
+    pb_count_launch(s->graph_launches);
+  }
   if (d_logits) PB_TRY_CUDA(cudaMemcpyAsync(d_logits, s->logits, (size_t)m->V * 4, cudaMemcpyDeviceToDevice, st));
   if (h_out_id) {
     PB_TRY_CUDA(cudaMemcpyAsync(&s->h_ctl->token, &s->ctl->token, sizeof(int), cudaMemcpyDeviceToHost, st));
+    if (s->persistent && (rc = check_decode_error(s, st))) return rc;
     PB_TRY_CUDA(cudaStreamSynchronize(st));
     *h_out_id = s->h_ctl->token;
   }
@@ -1323,14 +1212,26 @@ extern "C" int pb_decode_greedy(pb_model* m, pb_state* s, int token, int pos0, i
   if (!m || !s || token < 0 || token >= m->V || pos0 < 0 || n <= 0 || pos0 + n > s->max_ctx)
     return pb_set_error(PB_EINVAL, "pb_decode_greedy: bad argument");
   cudaStream_t st = (cudaStream_t)stream;
-  int rc = build_graph(s);
-  if (rc) return rc;
+  int rc;
+  if (s->persistent) {
+    if ((rc = build_phases(s))) return rc;
+    if ((rc = set_ctl(s, token, pos0, d_ids, st))) return rc;
+    return launch_decode(s, n, st);
+  }
+  if ((rc = build_graph(s))) return rc;
   if ((rc = set_ctl(s, token, pos0, d_ids, st))) return rc;
   for (int i = 0; i < n; i++) {
     PB_TRY_CUDA(cudaGraphLaunch(s->exec, st));
     pb_count_launch(s->graph_launches);
   }
   return PB_OK;
+}
+
+extern "C" int pb_state_status(pb_state* s, void* stream) {
+  if (!s) return pb_set_error(PB_EINVAL, "pb_state_status: null state");
+  cudaStream_t st = (cudaStream_t)stream;
+  PB_TRY_CUDA(cudaStreamSynchronize(st));
+  return check_decode_error(s, st);
 }
 
 // test/inspection helpers (not in the public header): device pointers of a
@@ -1353,12 +1254,13 @@ extern "C" int pb_decode_prompt(pb_model* m, pb_state* s, const int* d_tokens, i
   if (!m || !s || !d_tokens || n <= 0 || pos0 < 0 || pos0 + n > s->max_ctx)
     return pb_set_error(PB_EINVAL, "pb_decode_prompt: bad argument");
   cudaStream_t st = (cudaStream_t)stream;
-  int rc = build_graph(s);
+  int rc = s->persistent ? build_phases(s) : build_graph(s);
   if (rc) return rc;
   int first = 0;
   PB_TRY_CUDA(cudaMemcpy(&first, d_tokens, sizeof(int), cudaMemcpyDeviceToHost));
   if (first < 0 || first >= m->V) return pb_set_error(PB_EINVAL, "pb_decode_prompt: token %d", first);
   if ((rc = set_ctl(s, first, pos0, d_ids, st, d_tokens, n))) return rc;
+  if (s->persistent) return launch_decode(s, n, st);
   for (int i = 0; i < n; i++) {
     PB_TRY_CUDA(cudaGraphLaunch(s->exec, st));
     pb_count_launch(s->graph_launches);
@@ -1368,6 +1270,7 @@ extern "C" int pb_decode_prompt(pb_model* m, pb_state* s, const int* d_tokens, i
 
 extern "C" int pb_decode_kernels_per_token(pb_state* s) {
   if (!s) return pb_set_error(PB_EINVAL, "null state");
+  if (s->persistent) return 1;     // one cooperative launch decodes any number of tokens
   int rc = build_graph(s);
   return rc ? rc : (int)s->graph_launches;
 }

@@ -1,0 +1,486 @@
+// pb_step.cuh -- device code shared by the per-kernel decode step (pb_model.cu)
+// and the persistent decode kernel (pb_decode.cu): argument blocks, the fused
+// prologues (embedding, residual add, RMSNorm, gated short conv) and the
+// attention body. SYNC selects the CTA barrier: 0 = __syncthreads (a 256-thread
+// CTA), 1 = named barrier 1 over the 256 consumer threads of a warp-specialised
+// CTA; with SYNC = 1 the activations written earlier in the same launch by
+// other CTAs are read through L2 (ld.global.cg), never a possibly stale L1.
+#pragma once
+#include "pb_common.cuh"
+
+namespace {
+
+constexpr int PRO_PLAIN = 0, PRO_ADDNORM = 1, PRO_EMBED = 2, PRO_CONV = 3;
+constexpr int EPI_BF16 = 0, EPI_SILU = 1, EPI_ARGMAX = 2;
+constexpr int MAX_CTA = 1024;
+
+// device control block of a state
+struct Ctl {
+  int token;          // input id of the step; the head writes the greedy id here
+  int pos;            // position of the step; the head advances it
+  int step;           // greedy step counter (index into ids)
+  unsigned counter;   // argmax last-CTA counter
+  int* ids;           // optional output: the greedy id of every step
+  const int* prompt;  // optional teacher-forced inputs: step i+1 feeds prompt[i+1]
+  int n_prompt;
+  int _pad;
+  float slot_val[MAX_CTA];
+  int slot_idx[MAX_CTA];
+};
+
+struct StepArgs {
+  // weight stream
+  const uint4* codes;
+  const void* scales;
+  int N;
+  // prologue
+  int pro;
+  int K;               // GEMV input length
+  int H;               // hidden size (prologue vectors)
+  float eps;
+  const bf16_t* xin;   // PLAIN: x [K]; ADDNORM: residual [H]; CONV: in_proj output [3H]
+  const bf16_t* hin;   // ADDNORM: vector to post-normalise and add (null: none)
+  const float* wpost;  // ADDNORM: its norm weight
+  const float* wnorm;  // norm giving x from the residual (null: x = residual)
+  bf16_t* rout;        // residual written by CTA 0 (null: not written)
+  const uint4* emb_codes;   // EMBED: tied table, stream layout
+  const void* emb_scales;
+  int emb_nch;
+  int emb_f32;         // EMBED: scales are fp32 pairs (else fp16 pairs)
+  bf16_t* ring;        // CONV: [W][H], slot = position mod W
+  const float* taps;   // CONV: [H][W]
+  int convw;
+  Ctl* ctl;
+  // epilogue
+  void* y;
+};
+
+struct AttnArgs {
+  const bf16_t* qkvg;      // [NH*HD | NKV*HD | NKV*HD | NH]
+  const float* qnorm;      // [HD]
+  const float* knorm;      // [HD]
+  const float* rope_cos;   // [max_ctx][half]
+  const float* rope_sin;
+  unsigned short* kc;      // fp16 [max_ctx][NKV][HD]
+  unsigned short* vc;
+  bf16_t* out;             // [NH*HD] gated attention output
+  Ctl* ctl;
+  int nh, nkv, half, win, max_ctx;
+  float scaling, eps;
+};
+
+template <int SYNC>
+PB_DEV void csync() {
+  if (SYNC) asm volatile("bar.sync 1, 256;" ::: "memory");
+  else __syncthreads();
+}
+template <int SYNC>
+PB_DEV unsigned short ldu16(const unsigned short* p) { return SYNC ? __ldcg(p) : *p; }
+template <int SYNC>
+PB_DEV int ldi(const int* p) { return SYNC ? __ldcg(p) : *p; }
+
+// ---------------------------------------------------------------- prologue
+// sx (the GEMV input) is stored padded, one spare float per 32, so that lane
+// l reading its 32 consecutive values (index 32 l + j) hits bank (l + j) % 32.
+PB_DEV int padx(int i) { return i + (i >> 5); }
+
+// ---- vector helpers: thread t owns N consecutive elements ---------------
+template <int N, int SYNC>
+PB_DEV void ld_bf(const bf16_t* p, float (&o)[N]) {
+  if (N >= 8) {
+#pragma unroll
+    for (int v = 0; v < N / 8; v++) {
+      const uint4 w = SYNC ? __ldcg(reinterpret_cast<const uint4*>(p) + v) : reinterpret_cast<const uint4*>(p)[v];
+      const unsigned ws[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+      for (int k = 0; k < 4; k++) { o[8 * v + 2 * k] = pb_lo2f(ws[k]); o[8 * v + 2 * k + 1] = pb_hi2f(ws[k]); }
+    }
+  } else if (N == 4) {
+    const uint2 w = SYNC ? __ldcg(reinterpret_cast<const uint2*>(p)) : *reinterpret_cast<const uint2*>(p);
+    o[0] = pb_lo2f(w.x); o[1] = pb_hi2f(w.x); o[2 % N] = pb_lo2f(w.y); o[3 % N] = pb_hi2f(w.y);
+  } else if (N == 2) {
+    const unsigned w = SYNC ? __ldcg(reinterpret_cast<const unsigned*>(p)) : *reinterpret_cast<const unsigned*>(p);
+    o[0] = pb_lo2f(w); o[1 % N] = pb_hi2f(w);
+  } else {
+    o[0] = pb_bf2f(ldu16<SYNC>(p));
+  }
+}
+template <int N>
+PB_DEV void ld_f32(const float* p, float (&o)[N]) {
+  if (N % 4 == 0) {
+#pragma unroll
+    for (int v = 0; v < N / 4; v++) {
+      const float4 w = __ldg(reinterpret_cast<const float4*>(p) + v);
+      o[4 * v] = w.x; o[4 * v + 1] = w.y; o[4 * v + 2] = w.z; o[4 * v + 3] = w.w;
+    }
+  } else {
+#pragma unroll
+    for (int j = 0; j < N; j++) o[j] = __ldg(p + j);
+  }
+}
+template <int N>
+PB_DEV void st_bf(bf16_t* p, const float (&v)[N]) {
+  if (N >= 8) {
+#pragma unroll
+    for (int q = 0; q < N / 8; q++) {
+      uint4 w;
+      w.x = (unsigned)pb_f2bf(v[8 * q]) | ((unsigned)pb_f2bf(v[8 * q + 1]) << 16);
+      w.y = (unsigned)pb_f2bf(v[8 * q + 2]) | ((unsigned)pb_f2bf(v[8 * q + 3]) << 16);
+      w.z = (unsigned)pb_f2bf(v[8 * q + 4]) | ((unsigned)pb_f2bf(v[8 * q + 5]) << 16);
+      w.w = (unsigned)pb_f2bf(v[8 * q + 6]) | ((unsigned)pb_f2bf(v[8 * q + 7]) << 16);
+      reinterpret_cast<uint4*>(p)[q] = w;
+    }
+  } else {
+#pragma unroll
+    for (int j = 0; j < N; j++) p[j] = pb_f2bf(v[j]);
+  }
+}
+
+// RMSNorm over the block's H = 256 E values held E per thread (thread t owns
+// [E t, E t + E)), in the reference's order (rmsnorm_body,
+// lfm3_nanode.cu:383-440): squares summed pairwise, warp shuffle-down tree,
+// the 8 warp partials ascending; rs = 1/sqrt(mean + eps) correctly rounded;
+// out = bf16(w * bf16(v * rs)) (as floats). `red` (8 floats) must not be in
+// use by a neighbouring call: callers alternate two buffers.
+template <int E, int SYNC>
+__device__ void rms_reg(const float (&v)[E], const float* __restrict__ w, float (&out)[E], int H,
+                        float eps, float* red) {
+  const int t = threadIdx.x;
+  float ss[E];
+#pragma unroll
+  for (int j = 0; j < E; j++) ss[j] = __fmul_rn(v[j], v[j]);
+#pragma unroll
+  for (int width = E; width > 1; width >>= 1)
+#pragma unroll
+    for (int i = 0; i < width / 2; i++) ss[i] = __fadd_rn(ss[2 * i], ss[2 * i + 1]);
+  const float s = pb_warp_tree(ss[0]);
+  if ((t & 31) == 0) red[t >> 5] = s;
+  float wv[E];
+  ld_f32<E>(w + (size_t)t * E, wv);
+  csync<SYNC>();
+  float tot = red[0];
+#pragma unroll
+  for (int i = 1; i < 8; i++) tot = __fadd_rn(tot, red[i]);
+  const float rs = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fmul_rn(tot, __fdiv_rn(1.0f, (float)H)), eps)));
+#pragma unroll
+  for (int j = 0; j < E; j++) out[j] = pb_bf2f(pb_f2bf(__fmul_rn(wv[j], pb_bf2f(pb_f2bf(__fmul_rn(v[j], rs))))));
+}
+
+// plain GEMV input: K = 256 EK values, EK consecutive per thread
+template <int EK, int SYNC>
+__device__ void pro_plain(const StepArgs& a, float* sx) {
+  const int t = threadIdx.x;
+  float x[EK];
+  ld_bf<EK, SYNC>(a.xin + (size_t)t * EK, x);
+#pragma unroll
+  for (int j = 0; j < EK; j++) sx[padx(t * EK + j)] = x[j];
+}
+
+// gated short conv (lfm3_nanode.cu:3790-3818): bx = bf16(B*x) enters the ring
+// as the newest slot; y = sum_k taps[i][k] * ring_k (oldest first), one fp32
+// chain; out = bf16(C * bf16(y)). The ring slot of position pos held pos - W,
+// which no CTA reads any more; CTA 0 writes the new value there.
+template <int E, int W, int SYNC>
+__device__ void pro_conv(const StepArgs& a, float* sx) {
+  const int t = threadIdx.x, H = a.H;
+  const int pos = ldi<SYNC>(&a.ctl->pos);
+  float B[E], C[E], X[E], tp[E * W];
+  ld_bf<E, SYNC>(a.xin + (size_t)t * E, B);
+  ld_bf<E, SYNC>(a.xin + H + (size_t)t * E, C);
+  ld_bf<E, SYNC>(a.xin + 2 * H + (size_t)t * E, X);
+  ld_f32<E * W>(a.taps + (size_t)t * E * W, tp);
+  float rg[W - 1][E];
+#pragma unroll
+  for (int k = 0; k < W - 1; k++) {
+    const int p = pos - (W - 1) + k;
+    ld_bf<E, SYNC>(a.ring + (size_t)(((p % W) + W) % W) * H + (size_t)t * E, rg[k]);
+  }
+  float bx[E], y[E];
+#pragma unroll
+  for (int j = 0; j < E; j++) {
+    bx[j] = pb_bf2f(pb_f2bf(__fmul_rn(B[j], X[j])));
+    float acc = 0.0f;
+#pragma unroll
+    for (int k = 0; k < W; k++)
+      acc = __fadd_rn(acc, __fmul_rn(tp[j * W + k], k == W - 1 ? bx[j] : rg[k][j]));
+    y[j] = pb_bf2f(pb_f2bf(__fmul_rn(C[j], pb_bf2f(pb_f2bf(acc)))));
+    sx[padx(t * E + j)] = y[j];
+  }
+  if (blockIdx.x == 0) st_bf<E>(a.ring + (size_t)(pos % W) * H + (size_t)t * E, bx);
+}
+
+// residual (embedding row, or xin [+ post-normalised hin]) -> optional rout
+// -> optional norm -> x
+template <int E, int SYNC>
+__device__ void pro_residual(const StepArgs& a, float* sx, float* red) {
+  const int t = threadIdx.x, H = a.H;
+  float R[E];
+  if (a.pro == PRO_EMBED) {
+    // k_dequant_row (lfm3_nanode.cu:138-142): bf16(code * scale), row = token;
+    // the row is read from the tied table's streaming layout
+    const int tok = ldi<SYNC>(&a.ctl->token);
+    const int8_t* cb = reinterpret_cast<const int8_t*>(a.emb_codes);
+#pragma unroll
+    for (int j = 0; j < E; j++) {
+      const int i = t * E + j;
+      const int b = i >> 5, jj = i & 31, c = b >> 6, bb = b & 63, l = bb & 31, half = bb >> 5;
+      const size_t seg = (size_t)tok * a.emb_nch + c;
+      const int gi = (half * 2 + (jj >> 4)) * 32 + l;
+      const float code = (float)cb[(seg * 128 + gi) * 16 + (jj & 15)];
+      const float s = a.emb_f32 ? reinterpret_cast<const float*>(a.emb_scales)[(seg * 32 + l) * 2 + half]
+                                : pb_h2f(reinterpret_cast<const unsigned short*>(a.emb_scales)[(seg * 32 + l) * 2 + half]);
+      R[j] = pb_bf2f(pb_f2bf(__fmul_rn(code, s)));
+    }
+  } else {
+    ld_bf<E, SYNC>(a.xin + (size_t)t * E, R);
+    if (a.hin) {
+      float Hv[E], hn[E];
+      ld_bf<E, SYNC>(a.hin + (size_t)t * E, Hv);
+      rms_reg<E, SYNC>(Hv, a.wpost, hn, H, a.eps, red);
+#pragma unroll
+      for (int j = 0; j < E; j++) R[j] = pb_bf2f(pb_f2bf(__fadd_rn(R[j], hn[j])));
+    }
+  }
+  if (a.rout && blockIdx.x == 0) st_bf<E>(a.rout + (size_t)t * E, R);
+  float X[E];
+  if (a.wnorm) rms_reg<E, SYNC>(R, a.wnorm, X, H, a.eps, red + 8);
+  else {
+#pragma unroll
+    for (int j = 0; j < E; j++) X[j] = R[j];
+  }
+#pragma unroll
+  for (int j = 0; j < E; j++) sx[padx(t * E + j)] = X[j];
+}
+
+template <int E, int SYNC>
+__device__ void pro_dispatch_conv(const StepArgs& a, float* sx) {
+  switch (a.convw) {
+    case 2: pro_conv<E, 2, SYNC>(a, sx); break;
+    case 3: pro_conv<E, 3, SYNC>(a, sx); break;
+    case 4: pro_conv<E, 4, SYNC>(a, sx); break;
+    case 7: pro_conv<E, 7, SYNC>(a, sx); break;
+    default: break;   // rejected at load time
+  }
+}
+
+// Computes the GEMV input x (fp32 values of bf16 numbers) into sx, padded
+// (element i at padx(i)). Runs on 256 threads; H = 256 E with E in
+// {1, 2, 4, 8, 16}; plain inputs K = 256 EK with EK in {1, 2, 4, 8, 16, 32}.
+// `red` holds 16 floats. Ends with a CTA barrier.
+template <int SYNC>
+__device__ void step_prologue(const StepArgs& a, float* sx, float* red) {
+  if (a.pro == PRO_PLAIN) {
+    switch (a.K >> 8) {
+      case 1: pro_plain<1, SYNC>(a, sx); break;
+      case 2: pro_plain<2, SYNC>(a, sx); break;
+      case 4: pro_plain<4, SYNC>(a, sx); break;
+      case 8: pro_plain<8, SYNC>(a, sx); break;
+      case 16: pro_plain<16, SYNC>(a, sx); break;
+      case 32: pro_plain<32, SYNC>(a, sx); break;
+      default: break;
+    }
+  } else if (a.pro == PRO_CONV) {
+    switch (a.H >> 8) {
+      case 1: pro_dispatch_conv<1, SYNC>(a, sx); break;
+      case 2: pro_dispatch_conv<2, SYNC>(a, sx); break;
+      case 4: pro_dispatch_conv<4, SYNC>(a, sx); break;
+      case 8: pro_dispatch_conv<8, SYNC>(a, sx); break;
+      case 16: pro_dispatch_conv<16, SYNC>(a, sx); break;
+      default: break;
+    }
+  } else {
+    switch (a.H >> 8) {
+      case 1: pro_residual<1, SYNC>(a, sx, red); break;
+      case 2: pro_residual<2, SYNC>(a, sx, red); break;
+      case 4: pro_residual<4, SYNC>(a, sx, red); break;
+      case 8: pro_residual<8, SYNC>(a, sx, red); break;
+      case 16: pro_residual<16, SYNC>(a, sx, red); break;
+      default: break;
+    }
+  }
+  csync<SYNC>();
+}
+
+// ------------------------------------------------------------- attention
+// per-head RMSNorm (k_headnorm, lfm3_nanode.cu:460-479) + NeoX RoPE
+// (k_rope, :483-498) by one warp; result (fp32 of bf16) into o[HD]
+template <int E, int SYNC>
+__device__ void head_norm_rope(const bf16_t* __restrict__ x, const float* __restrict__ w,
+                               const float* cs, const float* sn, int half, float eps, float* o) {
+  const int lane = threadIdx.x & 31;
+  constexpr int HD = 32 * E;
+  float v[E], ss[E];
+#pragma unroll
+  for (int j = 0; j < E; j++) { v[j] = pb_bf2f(ldu16<SYNC>(x + lane * E + j)); ss[j] = __fmul_rn(v[j], v[j]); }
+#pragma unroll
+  for (int width = E; width > 1; width >>= 1)
+#pragma unroll
+    for (int i = 0; i < width / 2; i++) ss[i] = __fadd_rn(ss[2 * i], ss[2 * i + 1]);
+  float s = pb_warp_tree(__fadd_rn(ss[0], 0.0f));
+  s = __shfl_sync(0xffffffffu, s, 0);
+  const float rs = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fmul_rn(s, __fdiv_rn(1.0f, (float)HD)), eps)));
+#pragma unroll
+  for (int j = 0; j < E; j++) {
+    const int i = lane * E + j;
+    o[i] = pb_bf2f(pb_f2bf(__fmul_rn(w[i], pb_bf2f(pb_f2bf(__fmul_rn(v[j], rs))))));
+  }
+  __syncwarp();
+  float lo_n[E], hi_n[E];
+#pragma unroll
+  for (int j = 0; j < E; j++) {
+    const int i = lane * E + j;   // i < HD/2 covers the pairs when i < half
+    if (i < half) {
+      const float lo = o[i], hi = o[i + HD / 2];
+      lo_n[j] = pb_bf2f(pb_f2bf(__fadd_rn(__fmul_rn(lo, cs[i]), __fmul_rn(-hi, sn[i]))));
+      hi_n[j] = pb_bf2f(pb_f2bf(__fadd_rn(__fmul_rn(hi, cs[i]), __fmul_rn(lo, sn[i]))));
+    }
+  }
+  __syncwarp();
+#pragma unroll
+  for (int j = 0; j < E; j++) {
+    const int i = lane * E + j;
+    if (i < half) { o[i] = lo_n[j]; o[i + HD / 2] = hi_n[j]; }
+  }
+  __syncwarp();
+}
+
+// k_attn_head (lfm3_nanode.cu:503-602) for q head h over the fp16 cache, with
+// the q/k prologue and the sigmoid gate (k_sigmoid_gate, :852-864) fused.
+// The current position's k/v are used from shared memory (the CTA of the
+// group's first q head also appends them to the cache), so no CTA reads a
+// cache row another CTA writes in the same step. sl: scores [max_ctx]. Not
+// inlined: the persistent kernel keeps its register budget for the GEMV loop.
+template <int E, int SYNC>
+__device__ __noinline__ void attn_body(const AttnArgs& a, int h, float* sl, float* qv, float* kv, float* vv,
+                          float* segred, float* red) {
+  constexpr int HD = 32 * E;
+  const int t = threadIdx.x, lane = t & 31, wid = t >> 5;
+  const int grp = a.nh / a.nkv, kvh = h / grp;
+  const int pos = ldi<SYNC>(&a.ctl->pos);
+  const int npos = pos + 1;
+  const int lo = (a.win > 0 && npos > a.win) ? npos - a.win : 0;
+  const int np = npos - lo;
+  const float* cs = a.rope_cos + (size_t)pos * a.half;
+  const float* sn = a.rope_sin + (size_t)pos * a.half;
+  const size_t koff = (size_t)a.nh * HD, voff = koff + (size_t)a.nkv * HD, goff = voff + (size_t)a.nkv * HD;
+  if (wid == 0) head_norm_rope<E, SYNC>(a.qkvg + (size_t)h * HD, a.qnorm, cs, sn, a.half, a.eps, qv);
+  if (wid == 1) {
+    head_norm_rope<E, SYNC>(a.qkvg + koff + (size_t)kvh * HD, a.knorm, cs, sn, a.half, a.eps, kv);
+#pragma unroll
+    for (int j = 0; j < E; j++) {
+      const int i = lane * E + j;
+      const unsigned short k16 = pb_f2h(kv[i]);
+      kv[i] = pb_h2f(k16);
+      if (h % grp == 0) a.kc[((size_t)pos * a.nkv + kvh) * HD + i] = k16;
+    }
+  }
+  if (wid == 2) {
+#pragma unroll
+    for (int j = 0; j < E; j++) {
+      const int i = lane * E + j;
+      const unsigned short v16 = pb_f2h(pb_bf2f(ldu16<SYNC>(a.qkvg + voff + (size_t)kvh * HD + i)));
+      vv[i] = pb_h2f(v16);
+      if (h % grp == 0) a.vc[((size_t)pos * a.nkv + kvh) * HD + i] = v16;
+    }
+  }
+  csync<SYNC>();
+  // scores: position p by warp (p - lo) % 8, lane chains over its E dims;
+  // four positions per pass so that their loads and trees overlap
+  float ql[E];
+#pragma unroll
+  for (int j = 0; j < E; j++) ql[j] = qv[lane * E + j];
+  for (int p0 = lo + wid; p0 < npos; p0 += 32) {
+    float kl[4][E];
+#pragma unroll
+    for (int u = 0; u < 4; u++) {
+      const int p = p0 + 8 * u;
+      if (p < pos) {
+        const unsigned short* kr = a.kc + ((size_t)p * a.nkv + kvh) * HD + lane * E;
+#pragma unroll
+        for (int j = 0; j < E; j++) kl[u][j] = pb_h2f(ldu16<SYNC>(kr + j));
+      } else {
+#pragma unroll
+        for (int j = 0; j < E; j++) kl[u][j] = kv[lane * E + j];   // p == pos (or past the end)
+      }
+    }
+    float sv[4];
+#pragma unroll
+    for (int u = 0; u < 4; u++) {
+      float s = 0.0f;
+#pragma unroll
+      for (int j = 0; j < E; j++) s = __fadd_rn(s, __fmul_rn(ql[j], kl[u][j]));
+      sv[u] = s;
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1)
+#pragma unroll
+      for (int u = 0; u < 4; u++) sv[u] = __fadd_rn(sv[u], __shfl_down_sync(0xffffffffu, sv[u], o));
+    if (lane == 0)
+#pragma unroll
+      for (int u = 0; u < 4; u++)
+        if (p0 + 8 * u < npos) sl[p0 + 8 * u - lo] = __fmul_rn(sv[u], a.scaling);
+  }
+  csync<SYNC>();
+  float mx = -1e30f;
+  for (int i = t; i < np; i += 256) mx = fmaxf(mx, sl[i]);
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_down_sync(0xffffffffu, mx, o));
+  if (lane == 0) red[wid] = mx;
+  csync<SYNC>();
+  float m = red[0];
+#pragma unroll
+  for (int i = 1; i < 8; i++) m = fmaxf(m, red[i]);
+  csync<SYNC>();
+  float sum = 0.0f;
+  for (int i = t; i < np; i += 256) {
+    const float e = pb_expf(__fadd_rn(sl[i], -m));
+    sl[i] = e;
+    sum = __fadd_rn(sum, e);
+  }
+  sum = pb_warp_tree(sum);
+  if (lane == 0) red[wid] = sum;
+  csync<SYNC>();
+  // 8-lane shuffle-down tree: ((r0+r4)+(r2+r6))+((r1+r5)+(r3+r7))
+  const float tot = __fadd_rn(__fadd_rn(__fadd_rn(red[0], red[4]), __fadd_rn(red[2], red[6])),
+                              __fadd_rn(__fadd_rn(red[1], red[5]), __fadd_rn(red[3], red[7])));
+  const float inv = __fdiv_rn(1.0f, tot);
+  // P.V: segment = warp, lane owns dims lane*E .. +E; each dim's chain runs
+  // over p = seg, seg+8, ... in order, four positions' loads per pass
+  float acc[E];
+#pragma unroll
+  for (int j = 0; j < E; j++) acc[j] = 0.0f;
+  for (int p0 = wid; p0 < np; p0 += 32) {
+    float vl[4][E], wv[4];
+#pragma unroll
+    for (int u = 0; u < 4; u++) {
+      const int p = p0 + 8 * u, ap = lo + p;
+      wv[u] = p < np ? __fmul_rn(sl[p], inv) : 0.0f;
+      if (ap < pos) {
+        const unsigned short* vr = a.vc + ((size_t)ap * a.nkv + kvh) * HD + lane * E;
+#pragma unroll
+        for (int j = 0; j < E; j++) vl[u][j] = pb_h2f(ldu16<SYNC>(vr + j));
+      } else {
+#pragma unroll
+        for (int j = 0; j < E; j++) vl[u][j] = vv[lane * E + j];
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < 4; u++)
+      if (p0 + 8 * u < np)
+#pragma unroll
+        for (int j = 0; j < E; j++) acc[j] = __fadd_rn(acc[j], __fmul_rn(wv[u], vl[u][j]));
+  }
+#pragma unroll
+  for (int j = 0; j < E; j++) segred[wid * HD + lane * E + j] = acc[j];
+  csync<SYNC>();
+  if (t < HD) {
+    const float* r = segred + t;
+    const float o = __fadd_rn(__fadd_rn(__fadd_rn(r[0], r[HD]), __fadd_rn(r[2 * HD], r[3 * HD])),
+                              __fadd_rn(__fadd_rn(r[4 * HD], r[5 * HD]), __fadd_rn(r[6 * HD], r[7 * HD])));
+    const float sg = pb_sigmoid(pb_bf2f(ldu16<SYNC>(a.qkvg + goff + h)));
+    a.out[(size_t)h * HD + t] = pb_f2bf(__fmul_rn(pb_bf2f(pb_f2bf(o)), sg));
+  }
+  csync<SYNC>();   // sl / segred are reused by the caller
+}
+
+}  // namespace

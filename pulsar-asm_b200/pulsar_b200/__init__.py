@@ -96,6 +96,7 @@ def lib():
     L.pb_time_step_kernel.argtypes = [vp, vp, i, i, C.POINTER(C.c_float), C.POINTER(C.c_double), vp]
     L.pb_test_expf.argtypes = [vp, vp, i, vp]
     L.pb_layer_step_noalloc.argtypes = [vp, vp, i, i, vp, vp]
+    L.pb_state_status.argtypes = [vp, vp]
     _lib = L
     return L
 
@@ -292,6 +293,10 @@ class State:
         """tokens: device int32 [n]; ids (optional device int32 [n])."""
         check(lib().pb_decode_prompt(self.model.h, self.h, _ptr(tokens), tokens.numel(), int(pos0),
                                      _ptr(ids), _stream(stream)))
+
+    def status(self, stream=None):
+        """synchronise and raise if the decode kernel recorded a failure."""
+        check(lib().pb_state_status(self.h, _stream(stream)))
 
     def kernels_per_token(self):
         r = lib().pb_decode_kernels_per_token(self.h)
