@@ -23,7 +23,8 @@
 
 namespace {
 
-constexpr int PH_GEMV = 0, PH_ATTN = 1, PH_ARGMAX = 2;
+constexpr int PH_GEMV = 0, PH_ARGMAX = 2, PH_SCORE = 3, PH_SOFTMAX = 4, PH_PV = 5;
+constexpr int PV_DIMS = 16;                    // head dims per P.V task
 constexpr int DSEGS = 16;                      // 2048-byte segments per stage
 constexpr int STAGE_CODES = DSEGS * 2048;      // 32 KB
 constexpr unsigned PB_WAIT_LIMIT = 1u << 24;   // polls before a wait gives up
@@ -44,7 +45,19 @@ struct DecodeArgs {
   int xregion;         // floats of the activation region in shared memory
   int nh;              // attention heads = CTAs that run an attention phase
   int ds;              // ring stages
+  int pv_per_warp;     // floats of shared memory per warp in a P.V phase
+  unsigned long long* trace;   // optional: per (CTA, phase) globaltimer marks of token 0
 };
+
+PB_DEV unsigned long long gtime() {
+  unsigned long long t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+// trace marks: 0 phase entered, 1 grid barrier passed, 2 prologue done, 3 work done, 4 arrived
+PB_DEV void tmark(const DecodeArgs& d, int tok, int p, int k) {
+  if (d.trace && tok == 0 && threadIdx.x == 0) d.trace[((size_t)blockIdx.x * d.nphase + p) * 8 + k] = gtime();
+}
 
 template <bool F32S>
 struct DGeo {
@@ -157,6 +170,7 @@ __device__ void producer(const DecodeArgs& d, unsigned char* ring, uint64_t* ful
   typedef DGeo<F32S> Gm;
   unsigned it = 0;
   bool ok = true;
+  unsigned long long pwait = 0;
   for (int tok = 0; tok < d.ntok && ok; tok++) {
     for (int p = 0; p < d.nphase && ok; p++) {
       const Phase& ph = d.phases[p];
@@ -168,7 +182,9 @@ __device__ void producer(const DecodeArgs& d, unsigned char* ring, uint64_t* ful
       const char* sc = reinterpret_cast<const char*>(ph.a.scales);
       for (int r = r0; r < r1; r += RB) {
         const unsigned slot = it % d.ds, round = it / d.ds;
+        const unsigned long long tw = d.trace ? gtime() : 0;
         if (!mbar_wait(&empty[slot], (round & 1) ^ 1, abort_flag)) { ok = false; break; }
+        if (d.trace) pwait += gtime() - tw;
         const int nr = min(RB, r1 - r);
         const unsigned bc = (unsigned)nr * nch * 2048, bs = (unsigned)nr * nch * 32 * Gm::SB;
         mbar_expect_tx(&full[slot], bc + bs);
@@ -178,6 +194,7 @@ __device__ void producer(const DecodeArgs& d, unsigned char* ring, uint64_t* ful
       }
     }
   }
+  if (d.trace) d.trace[((size_t)blockIdx.x * d.nphase + 0) * 8 + 6] = pwait;   // producer: ring-full waits
   if (!ok) {
     atomicCAS(d.err, 0, 1);
     *abort_flag = 1;
@@ -200,15 +217,16 @@ constexpr int PSLOTS = 8;   // > ring stages: a partial slot is never reused whi
 // barrier sits in the stage loop. A wait that gives up breaks out of the loop
 // and the phase still ends with the same barriers as on the other warps.
 template <bool F32S, int EPI>
-__device__ void gemv_phase(const DecodeArgs& d, const Phase& ph, unsigned char* ring, float* xreg,
+__device__ __noinline__ void gemv_phase(const DecodeArgs& d, const Phase& ph, unsigned char* ring, float* xreg,
                            uint64_t* full, uint64_t* empty, unsigned& it, float* red,
                            float (*part)[DSEGS][8], int (*cnt)[8], float* bestv, int* besti,
-                           volatile int* abort_flag) {
+                           volatile int* abort_flag, unsigned long long* tmark2) {
   typedef DGeo<F32S> Gm;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (threadIdx.x < PSLOTS * 8) (&cnt[0][0])[threadIdx.x] = 0;
   float* sx = xreg;
   step_prologue<1>(ph.a, sx, red);      // ends with a consumer barrier
+  if (tmark2 && threadIdx.x == 0) *tmark2 = gtime();
   // the few fields the stage loop needs, read once into registers (the loop's
   // global stores would otherwise force the compiler to re-read them)
   void* const yout = ph.a.y;
@@ -232,11 +250,13 @@ __device__ void gemv_phase(const DecodeArgs& d, const Phase& ph, unsigned char* 
     const unsigned slot = it % ds, round = it / ds;
     const unsigned ps = it % PSLOTS;
     it++;
+    const unsigned long long tw = (tmark2 && threadIdx.x == 0) ? gtime() : 0;
     if (!mbar_wait(&full[slot], round & 1, abort_flag)) {
       *abort_flag = 1;
       atomicCAS(d.err, 0, 2);
       break;
     }
+    if (tmark2 && threadIdx.x == 0) tmark2[4] += gtime() - tw;   // slot 6 of the phase: data waits
     const unsigned char* st = ring + (size_t)slot * Gm::STAGE;
     uint4 q[2][4];
     float slo[2], shi[2];
@@ -327,29 +347,294 @@ __device__ void gemv_phase(const DecodeArgs& d, const Phase& ph, unsigned char* 
   }
 }
 
+// ------------------------------------------------------- split attention
+// k_attn_head (lfm3_nanode.cu:503-602) as three grid-wide phases with the
+// reference's exact arithmetic. Each phase issues all of a task's global
+// loads before it consumes any of them (one L2 round trip per task), and the
+// loops stay rolled so that the code of these rarely run phases stays small.
+//  SCORE   task = (head, 32 positions), one warp: lane p forms the score of
+//          position p alone: its 32 per-lane chains (((0 + q0k0) + q1k1) ...)
+//          and then the shuffle-down tree's additions, replayed in registers;
+//          * scaling. The task holding position pos for a group's first head
+//          appends the new fp16 k/v row to the cache.
+//  SOFTMAX task = head, one CTA: the 256 consumer threads are the reference's
+//          256 strided chains i = t, t+256, ...; max over the window;
+//          e = expf(s - m) kept in place; chains summed ascending, eight
+//          shuffle-down trees and the 8-lane tree; inv = 1/sum.
+//  PV      task = (head, segment, 16 dims), one warp: the segment's chain over
+//          p = seg, seg+8, ... of (e_p * inv) * v_p, staged through shared
+//          memory; the 8 segment partials meet in the o_proj prologue.
+// Window spans above 2048 positions take the per-kernel path (host check).
+
+PB_DEV void cp_async16(void* sdst, const void* gsrc) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(sdst)), "l"(gsrc) : "memory");
+}
+PB_DEV void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
+
+// head RMSNorm (k_headnorm, lfm3_nanode.cu:460-479) + NeoX RoPE (k_rope,
+// :483-498) of one warp from values already in registers: lane holds
+// elements lane*E + j; c/s are the rope factors of those elements (i < half)
+template <int E>
+PB_DEV void norm_rope_regs(const float (&v)[E], const float (&w)[E], const float (&c)[E],
+                           const float (&sv)[E], int half, float eps, float* o) {
+  constexpr int HD = 32 * E;
+  const int lane = threadIdx.x & 31;
+  float ss[E];
+#pragma unroll
+  for (int j = 0; j < E; j++) ss[j] = __fmul_rn(v[j], v[j]);
+#pragma unroll
+  for (int width = E; width > 1; width >>= 1)
+#pragma unroll
+    for (int i = 0; i < width / 2; i++) ss[i] = __fadd_rn(ss[2 * i], ss[2 * i + 1]);
+  float s = pb_warp_tree(__fadd_rn(ss[0], 0.0f));
+  s = __shfl_sync(0xffffffffu, s, 0);
+  const float rs = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fmul_rn(s, __fdiv_rn(1.0f, (float)HD)), eps)));
+  float n[E], part[E];
+#pragma unroll
+  for (int j = 0; j < E; j++) n[j] = pb_bf2f(pb_f2bf(__fmul_rn(w[j], pb_bf2f(pb_f2bf(__fmul_rn(v[j], rs))))));
+  // element i + HD/2 sits in lane + 16 at the same j
+#pragma unroll
+  for (int j = 0; j < E; j++) part[j] = __shfl_xor_sync(0xffffffffu, n[j], 16);
+#pragma unroll
+  for (int j = 0; j < E; j++) {
+    const int i = lane * E + j;
+    float r = n[j];
+    if (lane < 16 && i < half) {          // lo = n, hi = part
+      r = pb_bf2f(pb_f2bf(__fadd_rn(__fmul_rn(n[j], c[j]), __fmul_rn(-part[j], sv[j]))));
+    } else if (lane >= 16 && i - HD / 2 < half) {   // hi = n, lo = part; factors of i - HD/2
+      r = pb_bf2f(pb_f2bf(__fadd_rn(__fmul_rn(n[j], c[j]), __fmul_rn(part[j], sv[j]))));
+    }
+    o[i] = r;
+  }
+}
+
+template <int E>
+__device__ __noinline__ void attn_score_phase(const AttnArgs& a, int pos, float* wsm) {
+  constexpr int HD = 32 * E;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int gw = blockIdx.x * 8 + warp, GW = gridDim.x * 8;
+  const int grp = a.nh / a.nkv, nkv = a.nkv, half = a.half;
+  const int npos = pos + 1;
+  const int lo = (a.win > 0 && npos > a.win) ? npos - a.win : 0;
+  const int np = npos - lo, nblk = (np + 31) / 32, ntask = a.nh * nblk;
+  const float scaling = a.scaling, eps = a.eps;
+  float* qs = wsm + warp * 2 * HD;
+  float* ks = qs + HD;
+  const bf16_t* qkvg = a.qkvg;
+  unsigned short* kc = a.kc;
+  unsigned short* vc = a.vc;
+  float* scores = a.scores;
+  const float* qnorm = a.qnorm;
+  const float* knorm = a.knorm;
+  const size_t max_ctx = (size_t)a.max_ctx;
+  // rope factors of this lane's elements: lanes >= 16 use those of i - HD/2
+  const int ri = (lane & 15) * E;
+  const float* cs = a.rope_cos + (size_t)pos * half;
+  const float* sn = a.rope_sin + (size_t)pos * half;
+  const size_t koff = (size_t)a.nh * HD, voff = koff + (size_t)nkv * HD;
+  int cur = -1;
+  for (int task = gw; task < ntask; task += GW) {
+    const int h = task / nblk, pb = task - h * nblk, kvh = h / grp;
+    const int p = lo + pb * 32 + lane;
+    const bool writer = (h % grp == 0) && pos >= lo + pb * 32 && pos < lo + pb * 32 + 32;
+    // all loads first: this lane's cached key row, the new v row (writer),
+    // and when the head changes its q/k rows, norm weights and rope factors
+    uint4 kg[HD / 8];
+    if (p < pos) {
+      const uint4* kr = reinterpret_cast<const uint4*>(kc + ((size_t)p * nkv + kvh) * HD);
+#pragma unroll
+      for (int g = 0; g < HD / 8; g++) kg[g] = __ldcg(kr + g);
+    }
+    unsigned short vraw[E];
+    if (writer) {
+#pragma unroll
+      for (int j = 0; j < E; j++) vraw[j] = __ldcg(qkvg + voff + (size_t)kvh * HD + lane * E + j);
+    }
+    if (h != cur) {
+      float qx[E], kx[E], qw[E], kw[E], c[E], sv[E];
+#pragma unroll
+      for (int j = 0; j < E; j++) {
+        const int i = lane * E + j;
+        qx[j] = pb_bf2f(__ldcg(qkvg + (size_t)h * HD + i));
+        kx[j] = pb_bf2f(__ldcg(qkvg + koff + (size_t)kvh * HD + i));
+        qw[j] = __ldg(qnorm + i);
+        kw[j] = __ldg(knorm + i);
+        c[j] = ri + j < half ? __ldg(cs + ri + j) : 0.0f;
+        sv[j] = ri + j < half ? __ldg(sn + ri + j) : 0.0f;
+      }
+      __syncwarp();                       // previous task's reads of qs/ks are done
+      norm_rope_regs<E>(qx, qw, c, sv, half, eps, qs);
+      norm_rope_regs<E>(kx, kw, c, sv, half, eps, ks);
+#pragma unroll
+      for (int j = 0; j < E; j++) ks[lane * E + j] = pb_h2f(pb_f2h(ks[lane * E + j]));
+      __syncwarp();
+      cur = h;
+    }
+    if (writer) {
+      unsigned short* kd = kc + ((size_t)pos * nkv + kvh) * HD;
+      unsigned short* vd = vc + ((size_t)pos * nkv + kvh) * HD;
+#pragma unroll
+      for (int j = 0; j < E; j++) {
+        kd[lane * E + j] = pb_f2h(ks[lane * E + j]);
+        vd[lane * E + j] = pb_f2h(pb_bf2f(vraw[j]));
+      }
+    }
+    if (p < npos) {
+      float v[32];
+#pragma unroll
+      for (int l = 0; l < 32; l++) {
+        float sl = 0.0f;
+#pragma unroll
+        for (int j = 0; j < E; j++) {
+          const int dd = l * E + j;
+          float kf;
+          if (p < pos) {
+            const unsigned w = reinterpret_cast<const unsigned*>(&kg[dd >> 3])[(dd & 7) >> 1];
+            kf = pb_h2f((unsigned short)((dd & 1) ? (w >> 16) : (w & 0xffffu)));
+          } else {
+            kf = ks[dd];
+          }
+          sl = __fadd_rn(sl, __fmul_rn(qs[dd], kf));
+        }
+        v[l] = sl;
+      }
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1)
+#pragma unroll
+        for (int l = 0; l < o; l++) v[l] = __fadd_rn(v[l], v[l + o]);
+      scores[(size_t)h * max_ctx + (p - lo)] = __fmul_rn(v[0], scaling);
+    }
+  }
+}
+
+__device__ __noinline__ void attn_softmax_phase(const AttnArgs& a, int pos, float* red) {
+  constexpr int PER = 8;     // scores per thread: window spans up to 2048
+  const int t = threadIdx.x, warp = t >> 5, lane = t & 31;
+  const int npos = pos + 1;
+  const int lo = (a.win > 0 && npos > a.win) ? npos - a.win : 0;
+  const int np = npos - lo;
+  for (int h = blockIdx.x; h < a.nh; h += gridDim.x) {
+    float* sc = a.scores + (size_t)h * a.max_ctx;
+    float sv[PER];
+#pragma unroll
+    for (int k = 0; k < PER; k++) sv[k] = (t + 256 * k < np) ? __ldcg(sc + t + 256 * k) : -1e30f;
+    float m = sv[0];
+#pragma unroll
+    for (int k = 1; k < PER; k++) m = fmaxf(m, sv[k]);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+    if (lane == 0) red[warp] = m;
+    csync<1>();
+    m = red[0];
+#pragma unroll
+    for (int w = 1; w < 8; w++) m = fmaxf(m, red[w]);
+    m = fmaxf(-1e30f, m);
+    float sum = 0.0f;            // chain t: i = t, t + 256, ... ascending
+#pragma unroll
+    for (int k = 0; k < PER; k++) {
+      const int i = t + 256 * k;
+      if (i < np) {
+        const float e = pb_expf(__fadd_rn(sv[k], -m));
+        sc[i] = e;
+        sum = __fadd_rn(sum, e);
+      }
+    }
+    sum = pb_warp_tree(sum);
+    if (lane == 0) red[8 + warp] = sum;
+    csync<1>();
+    if (t == 0) {
+      const float* W = red + 8;
+      const float tot = __fadd_rn(__fadd_rn(__fadd_rn(W[0], W[4]), __fadd_rn(W[2], W[6])),
+                                  __fadd_rn(__fadd_rn(W[1], W[5]), __fadd_rn(W[3], W[7])));
+      a.inv[h] = __fdiv_rn(1.0f, tot);
+    }
+    csync<1>();                  // red is reused by the next head
+  }
+}
+
+template <int E>
+__device__ __noinline__ void attn_pv_phase(const AttnArgs& a, int pos, float* wsm, int per_warp) {
+  constexpr int HD = 32 * E, NDQ = HD / PV_DIMS;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int gw = blockIdx.x * 8 + warp, GW = gridDim.x * 8;
+  const int grp = a.nh / a.nkv, nkv = a.nkv;
+  const int npos = pos + 1;
+  const int lo = (a.win > 0 && npos > a.win) ? npos - a.win : 0;
+  const int np = npos - lo, ntask = a.nh * 8 * NDQ;
+  const size_t max_ctx = (size_t)a.max_ctx;
+  const float* scores = a.scores;
+  const float* invp = a.inv;
+  const unsigned short* vc = a.vc;
+  float* segp = a.segp;
+  // per warp: e values [cnt] then v rows [cnt][16 halves] (16-byte aligned)
+  float* we = wsm + (size_t)warp * per_warp;
+  unsigned short* wv = reinterpret_cast<unsigned short*>(we + (per_warp / 9));
+  for (int task = gw; task < ntask; task += GW) {
+    const int h = task / (8 * NDQ), rem = task - h * 8 * NDQ, seg = rem / NDQ, dq = rem - seg * NDQ;
+    const int kvh = h / grp;
+    const int cnt = seg < np ? (np - seg + 7) / 8 : 0;     // <= 256
+    const float* sc = scores + (size_t)h * max_ctx;
+    __syncwarp();                 // previous task's reads of we/wv are done
+    // v rows by asynchronous copies, e values and inv by plain loads: all in flight together
+    for (int it = lane; it < 2 * cnt; it += 32) {
+      const int j = it >> 1, hf = it & 1;
+      cp_async16(wv + it * 8, vc + ((size_t)(lo + seg + 8 * j) * nkv + kvh) * HD + dq * PV_DIMS + hf * 8);
+    }
+    asm volatile("cp.async.commit_group;" ::: "memory");
+    float ev[8];
+#pragma unroll
+    for (int r = 0; r < 8; r++) {
+      const int j = lane + 32 * r;
+      ev[r] = j < cnt ? __ldcg(sc + seg + 8 * j) : 0.0f;
+    }
+    const float inv = __ldcg(invp + h);
+#pragma unroll
+    for (int r = 0; r < 8; r++)
+      if (lane + 32 * r < cnt) we[lane + 32 * r] = ev[r];
+    cp_async_wait_all();
+    __syncwarp();
+    if (lane < PV_DIMS) {
+      float acc = 0.0f;
+      for (int j = 0; j < cnt; j++)
+        acc = __fadd_rn(acc, __fmul_rn(__fmul_rn(we[j], inv), pb_h2f(wv[j * PV_DIMS + lane])));
+      segp[((size_t)h * 8 + seg) * HD + dq * PV_DIMS + lane] = acc;
+    }
+  }
+}
+
 // greedy id from the per-CTA maxima (ties to the lowest index); the next
 // input is the prompt's next token while a prompt is being fed
 __device__ void argmax_phase(const DecodeArgs& d) {
+  // warp 0 of CTA 0: lanes reduce strided slots, then a shuffle tree; ties
+  // resolve to the lowest index (the per-CTA maxima carry their row index)
   Ctl* ctl = d.ctl;
-  float b = __ldcg(&ctl->slot_val[0]);
-  int ix = __ldcg(&ctl->slot_idx[0]);
-  for (int k = 1; k < (int)gridDim.x; k++) {
+  const int lane = threadIdx.x & 31;
+  float b = -INFINITY;
+  int ix = 0x7fffffff;
+  for (int k = lane; k < (int)gridDim.x; k += 32) {
     const float ov = __ldcg(&ctl->slot_val[k]);
     const int oi = __ldcg(&ctl->slot_idx[k]);
     if (ov > b || (ov == b && oi < ix)) { b = ov; ix = oi; }
   }
-  const int step = __ldcg(&ctl->step);
-  const int np = __ldcg(&ctl->n_prompt);
-  ctl->token = (step + 1 < np) ? __ldcg(ctl->prompt + step + 1) : ix;
-  if (ctl->ids) ctl->ids[step] = ix;
-  ctl->step = step + 1;
-  ctl->pos = __ldcg(&ctl->pos) + 1;
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const float ov = __shfl_down_sync(0xffffffffu, b, o);
+    const int oi = __shfl_down_sync(0xffffffffu, ix, o);
+    if (ov > b || (ov == b && oi < ix)) { b = ov; ix = oi; }
+  }
+  if (lane == 0) {
+    const int step = __ldcg(&ctl->step);
+    const int np = __ldcg(&ctl->n_prompt);
+    ctl->token = (step + 1 < np) ? __ldcg(ctl->prompt + step + 1) : ix;
+    if (ctl->ids) ctl->ids[step] = ix;
+    ctl->step = step + 1;
+    ctl->pos = __ldcg(&ctl->pos) + 1;
+  }
 }
 
 template <bool F32S, int E>
 __global__ void __launch_bounds__(288, 1) k_decode(DecodeArgs d) {
   typedef DGeo<F32S> Gm;
-  constexpr int HD = 32 * E;
   extern __shared__ __align__(128) unsigned char dsm[];
   unsigned char* ring = dsm;
   float* xreg = reinterpret_cast<float*>(dsm + (size_t)d.ds * Gm::STAGE);
@@ -360,8 +645,6 @@ __global__ void __launch_bounds__(288, 1) k_decode(DecodeArgs d) {
   __shared__ int cnt[PSLOTS][8];
   __shared__ float bestv[8];
   __shared__ int besti[8];
-  __shared__ float qv[HD], kv[HD], vv[HD];
-  __shared__ float segred[8 * HD];
   __shared__ int abort_flag;
   const int warp = threadIdx.x >> 5;
   if (threadIdx.x == 0) {
@@ -375,34 +658,45 @@ __global__ void __launch_bounds__(288, 1) k_decode(DecodeArgs d) {
     return;
   }
   const unsigned G = gridDim.x;
+  // the position advances by one per token (argmax phase), so it is read once
+  const int pos0 = __ldcg(&d.ctl->pos);
   unsigned it = 0;
   for (int tok = 0; tok < d.ntok; tok++) {
     for (int p = 0; p < d.nphase; p++) {
       const unsigned q = (unsigned)(tok * d.nphase + p);
+      tmark(d, tok, p, 0);
       if (q > 0) {
         if (threadIdx.x == 0 && !abort_flag && !grid_wait(d.bar, G * q)) { abort_flag = 1; atomicCAS(d.err, 0, 3); }
         csync<1>();
       }
       if (abort_flag) return;        // every consumer thread leaves here together
+      tmark(d, tok, p, 1);
       const Phase& ph = d.phases[p];
+      unsigned long long* tm2 = (d.trace && tok == 0) ? d.trace + ((size_t)blockIdx.x * d.nphase + p) * 8 + 2 : nullptr;
       if (ph.kind == PH_GEMV) {
         if (ph.epi == EPI_SILU)
-          gemv_phase<F32S, EPI_SILU>(d, ph, ring, xreg, full, empty, it, red, part, cnt, bestv, besti, &abort_flag);
+          gemv_phase<F32S, EPI_SILU>(d, ph, ring, xreg, full, empty, it, red, part, cnt, bestv, besti, &abort_flag, tm2);
         else if (ph.epi == EPI_ARGMAX)
-          gemv_phase<F32S, EPI_ARGMAX>(d, ph, ring, xreg, full, empty, it, red, part, cnt, bestv, besti, &abort_flag);
+          gemv_phase<F32S, EPI_ARGMAX>(d, ph, ring, xreg, full, empty, it, red, part, cnt, bestv, besti, &abort_flag, tm2);
         else
-          gemv_phase<F32S, EPI_BF16>(d, ph, ring, xreg, full, empty, it, red, part, cnt, bestv, besti, &abort_flag);
-      } else if (ph.kind == PH_ATTN) {
-        if ((int)blockIdx.x < d.nh) attn_body<E, 1>(ph.at, blockIdx.x, xreg, qv, kv, vv, segred, red);
+          gemv_phase<F32S, EPI_BF16>(d, ph, ring, xreg, full, empty, it, red, part, cnt, bestv, besti, &abort_flag, tm2);
+      } else if (ph.kind == PH_SCORE) {
+        attn_score_phase<E>(ph.at, pos0 + tok, xreg);
+      } else if (ph.kind == PH_SOFTMAX) {
+        attn_softmax_phase(ph.at, pos0 + tok, red);
+      } else if (ph.kind == PH_PV) {
+        attn_pv_phase<E>(ph.at, pos0 + tok, xreg, d.pv_per_warp);
       } else {
-        if (blockIdx.x == 0 && threadIdx.x == 0) argmax_phase(d);
+        if (blockIdx.x == 0 && threadIdx.x < 32) argmax_phase(d);
       }
+      tmark(d, tok, p, 3);
       // every consumer thread's writes of this phase are issued: publish them
       csync<1>();
       if (threadIdx.x == 0) {
         __threadfence();
         grid_arrive(d.bar);
       }
+      tmark(d, tok, p, 4);
     }
   }
 }

@@ -328,6 +328,11 @@ struct pb_state {
   int xregion = 0, ds = 0;
   size_t dsmem = 0;
   bool persistent = true;
+  unsigned long long* d_trace = nullptr;   // PB_DECODE_TRACE=1: phase timing marks
+  float* att_scores = nullptr;   // split attention: [NH][max_ctx] scores, then e
+  float* att_inv = nullptr;      // [NH] 1/sum
+  float* att_segp = nullptr;     // [NH][8][HD] P.V segment partials
+  int pv_per_warp = 0;
   cudaGraph_t graph = nullptr;
   cudaGraphExec_t exec = nullptr;
   cudaStream_t graph_stream = nullptr;
@@ -591,6 +596,9 @@ AttnArgs attn_args(const pb_model* m, pb_state* s, int layer) {
   a.nh = m->NH; a.nkv = m->NKV; a.half = half_rot(m); a.win = m->win; a.max_ctx = s->max_ctx;
   a.scaling = 1.0f / sqrtf((float)m->HD);
   a.eps = m->eps;
+  a.scores = s->att_scores;
+  a.inv = s->att_inv;
+  a.segp = s->att_segp;
   return a;
 }
 
@@ -625,12 +633,20 @@ int build_phases(pb_state* s) {
     StepArgs b = base_args(m, s);
     b.y = s->h_mix;
     if (Ly.attn) {
-      Phase at = {};
-      at.kind = PH_ATTN;
-      at.at = attn_args(m, s, L);
-      ph.push_back(at);
-      b.pro = PRO_PLAIN;
-      b.xin = s->h_attn;
+      // split attention: scores, softmax, P.V; the segment partials are
+      // combined (and gated) in the o_proj prologue
+      for (int kind : {PH_SCORE, PH_SOFTMAX, PH_PV}) {
+        Phase at = {};
+        at.kind = kind;
+        at.at = attn_args(m, s, L);
+        ph.push_back(at);
+      }
+      b.pro = PRO_ATTN;
+      b.xin = s->h_first;
+      b.segp = s->att_segp;
+      b.nh = m->NH;
+      b.hd = m->HD;
+      b.goff = m->NH * m->HD + 2 * m->NKV * m->HD;
     } else {
       b.pro = PRO_CONV;
       b.xin = s->h_first;
@@ -668,7 +684,9 @@ int build_phases(pb_state* s) {
   am.kind = PH_ARGMAX;
   ph.push_back(am);
   // shared-memory plan: activation region, then as many ring stages as fit
-  int xr = s->max_ctx;
+  const int cnt_max = (((s->max_ctx + 7) / 8) + 3) & ~3;
+  s->pv_per_warp = 9 * cnt_max;
+  int xr = std::max(s->max_ctx, std::max(8 * 2 * m->HD, 8 * s->pv_per_warp));
   for (auto& p : ph)
     if (p.kind == PH_GEMV) {
       const int need = p.a.K + p.a.K / 32 + ((p.a.pro == PRO_ADDNORM || p.a.pro == PRO_EMBED) ? 2 * m->H : 0);
@@ -688,6 +706,12 @@ int build_phases(pb_state* s) {
   s->xregion = xr;
   s->dsmem = (size_t)ds * stage + xb + 2 * (size_t)ds * 8;
   s->nphase = (int)ph.size();
+  if (getenv("PB_DECODE_TRACE") && !s->d_trace) {
+    if (cudaMalloc(&s->d_trace, (size_t)pb_num_sms() * ph.size() * 8 * 8) != cudaSuccess) {
+      cudaGetLastError();
+      s->d_trace = nullptr;
+    }
+  }
   if (cudaMalloc(&s->d_phases, ph.size() * sizeof(Phase)) != cudaSuccess) {
     cudaGetLastError();
     s->d_phases = nullptr;
@@ -709,6 +733,8 @@ int launch_decode_t(pb_state* s, int ntok, cudaStream_t st) {
   d.xregion = s->xregion;
   d.nh = s->m->NH;
   d.ds = s->ds;
+  d.trace = s->d_trace;
+  d.pv_per_warp = s->pv_per_warp;
   static bool set = false;
   if (!set) {
     PB_TRY_CUDA(cudaFuncSetAttribute(k_decode<F32S, E>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)s->dsmem));
@@ -720,6 +746,7 @@ int launch_decode_t(pb_state* s, int ntok, cudaStream_t st) {
   const int grid = pb_num_sms();
   if (grid > MAX_CTA || grid < s->m->NH) return pb_set_error(PB_ENOTSUP, "persistent decode grid %d", grid);
   PB_TRY_CUDA(cudaMemsetAsync(s->d_bar, 0, sizeof(unsigned), st));
+  if (s->d_trace) PB_TRY_CUDA(cudaMemsetAsync(s->d_trace, 0, (size_t)pb_num_sms() * s->nphase * 8 * 8, st));
   void* args[] = {&d};
   cudaError_t e = cudaLaunchCooperativeKernel((const void*)k_decode<F32S, E>, dim3(grid), dim3(288), args,
                                               s->dsmem, st);
@@ -1073,6 +1100,9 @@ extern "C" int pb_state_create(pb_model* m, int max_ctx, pb_state** out) {
   {
     const char* mode = getenv("PB_DECODE_MODE");   // "graph": the per-kernel CUDA-graph path
     s->persistent = !(mode && strcmp(mode, "graph") == 0);
+    // the persistent softmax holds a head's scores in registers (64 per lane)
+    const int span = (m->win > 0 && m->win < max_ctx) ? m->win : max_ctx;
+    if (span > 2048) s->persistent = false;
   }
   const int H = m->H, n_conv = m->L - m->n_attn, half = half_rot(m);
   const size_t kvb = (size_t)m->n_attn * 2 * max_ctx * m->NKV * m->HD * 2;
@@ -1081,7 +1111,8 @@ extern "C" int pb_state_create(pb_model* m, int max_ctx, pb_state** out) {
   const size_t firstn = std::max((size_t)3 * H, (size_t)m->NH * m->HD + 2 * (size_t)m->NKV * m->HD + m->NH);
   size_t sizes[] = {kvb, ringb, ropeb, ropeb, (size_t)H * 2, (size_t)H * 2, (size_t)H * 2, firstn * 2,
                     (size_t)m->NH * m->HD * 2, (size_t)H * 2, (size_t)m->F * 2, (size_t)H * 2,
-                    (size_t)m->V * 4, sizeof(Ctl), 256, 256};
+                    (size_t)m->V * 4, sizeof(Ctl), 256, 256, (size_t)m->NH * max_ctx * 4, (size_t)m->NH * 4,
+                    (size_t)m->NH * 8 * m->HD * 4};
   size_t tot = 0;
   for (size_t x : sizes) tot += align256(x);
   if (cudaMalloc(&s->mem, tot) != cudaSuccess) { cudaGetLastError(); delete s; return pb_set_error(PB_ENOMEM, "pb_state_create: %zu bytes", tot); }
@@ -1090,7 +1121,8 @@ extern "C" int pb_state_create(pb_model* m, int max_ctx, pb_state** out) {
   void** slots[] = {(void**)&s->kv, (void**)&s->ring, (void**)&s->rope_cos, (void**)&s->rope_sin,
                     (void**)&s->res[0], (void**)&s->res[1], (void**)&s->res[2], (void**)&s->h_first,
                     (void**)&s->h_attn, (void**)&s->h_mix, (void**)&s->h_u, (void**)&s->h_w2,
-                    (void**)&s->logits, (void**)&s->ctl, (void**)&s->d_bar, (void**)&s->d_err};
+                    (void**)&s->logits, (void**)&s->ctl, (void**)&s->d_bar, (void**)&s->d_err,
+                    (void**)&s->att_scores, (void**)&s->att_inv, (void**)&s->att_segp};
   for (size_t i = 0; i < sizeof(sizes) / sizeof(sizes[0]); i++) { *slots[i] = p; p += align256(sizes[i]); }
   if (cudaMallocHost(&s->h_ctl, sizeof(Ctl)) != cudaSuccess) {
     cudaGetLastError(); cudaFree(s->mem); delete s;
@@ -1120,6 +1152,7 @@ extern "C" int pb_state_create(pb_model* m, int max_ctx, pb_state** out) {
 extern "C" int pb_state_destroy(pb_state* s) {
   if (!s) return PB_OK;
   if (s->d_phases) cudaFree(s->d_phases);
+  if (s->d_trace) cudaFree(s->d_trace);
   if (s->exec) cudaGraphExecDestroy(s->exec);
   if (s->graph) cudaGraphDestroy(s->graph);
   if (s->graph_stream) cudaStreamDestroy(s->graph_stream);
@@ -1245,6 +1278,7 @@ extern "C" int pb_state_debug(pb_state* s, int which, void** ptr, size_t* bytes)
     case 2: *ptr = s->res[s->graph_res]; if (bytes) *bytes = (size_t)m->H * 2; return PB_OK;
     case 3: *ptr = s->logits; if (bytes) *bytes = (size_t)m->V * 4; return PB_OK;
     case 4: *ptr = &s->ctl->pos; if (bytes) *bytes = 4; return PB_OK;
+    case 5: *ptr = s->d_trace; if (bytes) *bytes = s->d_trace ? (size_t)pb_num_sms() * s->nphase * 8 * 8 : 0; return PB_OK;
   }
   return PB_EINVAL;
 }

@@ -10,7 +10,7 @@
 
 namespace {
 
-constexpr int PRO_PLAIN = 0, PRO_ADDNORM = 1, PRO_EMBED = 2, PRO_CONV = 3;
+constexpr int PRO_PLAIN = 0, PRO_ADDNORM = 1, PRO_EMBED = 2, PRO_CONV = 3, PRO_ATTN = 4;
 constexpr int EPI_BF16 = 0, EPI_SILU = 1, EPI_ARGMAX = 2;
 constexpr int MAX_CTA = 1024;
 
@@ -50,6 +50,9 @@ struct StepArgs {
   bf16_t* ring;        // CONV: [W][H], slot = position mod W
   const float* taps;   // CONV: [H][W]
   int convw;
+  const float* segp;   // ATTN: per-head P.V segment partials [NH][8][HD]; xin = q|k|v|gate
+  int nh, hd;          // ATTN: heads and head_dim (gate offset = nh*hd + 2*nkv*hd = goff)
+  int goff;
   Ctl* ctl;
   // epilogue
   void* y;
@@ -67,6 +70,11 @@ struct AttnArgs {
   Ctl* ctl;
   int nh, nkv, half, win, max_ctx;
   float scaling, eps;
+  // persistent kernel's split attention: scores/exp [NH][max_ctx], 1/sum [NH],
+  // P.V segment partials [NH][8][HD]
+  float* scores;
+  float* inv;
+  float* segp;
 };
 
 template <int SYNC>
@@ -252,6 +260,30 @@ __device__ void pro_residual(const StepArgs& a, float* sx, float* red) {
   for (int j = 0; j < E; j++) sx[padx(t * E + j)] = X[j];
 }
 
+// attention output from the split attention's segment partials: out_d =
+// bf16(((s0+s1)+(s2+s3))+((s4+s5)+(s6+s7))) (k_attn_head, lfm3_nanode.cu:594-600),
+// then the sigmoid head gate (k_sigmoid_gate, :852-864): bf16(out * 1/(1+e^-g))
+template <int EK, int SYNC>
+__device__ void pro_attn(const StepArgs& a, float* sx) {
+  const int t = threadIdx.x, hd = a.hd;
+#pragma unroll
+  for (int j0 = 0; j0 < EK; j0 += 4) {
+    const int i = t * EK + j0, h = i / hd, d = i - h * hd;
+    float4 sg[8];
+#pragma unroll
+    for (int sgi = 0; sgi < 8; sgi++)
+      sg[sgi] = __ldcg(reinterpret_cast<const float4*>(a.segp + ((size_t)h * 8 + sgi) * hd + d));
+    const float gt = pb_sigmoid(pb_bf2f(ldu16<SYNC>(a.xin + a.goff + h)));
+    const float* f = reinterpret_cast<const float*>(sg);
+#pragma unroll
+    for (int k = 0; k < 4; k++) {
+      const float o = __fadd_rn(__fadd_rn(__fadd_rn(f[0 * 4 + k], f[1 * 4 + k]), __fadd_rn(f[2 * 4 + k], f[3 * 4 + k])),
+                                __fadd_rn(__fadd_rn(f[4 * 4 + k], f[5 * 4 + k]), __fadd_rn(f[6 * 4 + k], f[7 * 4 + k])));
+      sx[padx(i + k)] = pb_bf2f(pb_f2bf(__fmul_rn(pb_bf2f(pb_f2bf(o)), gt)));
+    }
+  }
+}
+
 template <int E, int SYNC>
 __device__ void pro_dispatch_conv(const StepArgs& a, float* sx) {
   switch (a.convw) {
@@ -268,7 +300,7 @@ __device__ void pro_dispatch_conv(const StepArgs& a, float* sx) {
 // {1, 2, 4, 8, 16}; plain inputs K = 256 EK with EK in {1, 2, 4, 8, 16, 32}.
 // `red` holds 16 floats. Ends with a CTA barrier.
 template <int SYNC>
-__device__ void step_prologue(const StepArgs& a, float* sx, float* red) {
+__device__ __noinline__ void step_prologue(const StepArgs& a, float* sx, float* red) {
   if (a.pro == PRO_PLAIN) {
     switch (a.K >> 8) {
       case 1: pro_plain<1, SYNC>(a, sx); break;
@@ -277,6 +309,14 @@ __device__ void step_prologue(const StepArgs& a, float* sx, float* red) {
       case 8: pro_plain<8, SYNC>(a, sx); break;
       case 16: pro_plain<16, SYNC>(a, sx); break;
       case 32: pro_plain<32, SYNC>(a, sx); break;
+      default: break;
+    }
+  } else if (a.pro == PRO_ATTN) {
+    switch (a.K >> 8) {
+      case 4: pro_attn<4, SYNC>(a, sx); break;
+      case 8: pro_attn<8, SYNC>(a, sx); break;
+      case 16: pro_attn<16, SYNC>(a, sx); break;
+      case 32: pro_attn<32, SYNC>(a, sx); break;
       default: break;
     }
   } else if (a.pro == PRO_CONV) {
@@ -309,9 +349,18 @@ __device__ void head_norm_rope(const bf16_t* __restrict__ x, const float* __rest
                                const float* cs, const float* sn, int half, float eps, float* o) {
   const int lane = threadIdx.x & 31;
   constexpr int HD = 32 * E;
-  float v[E], ss[E];
+  // every load first (activations, weights, rope table): one round trip
+  float v[E], ss[E], wv[E], c[E], sv[E];
 #pragma unroll
-  for (int j = 0; j < E; j++) { v[j] = pb_bf2f(ldu16<SYNC>(x + lane * E + j)); ss[j] = __fmul_rn(v[j], v[j]); }
+  for (int j = 0; j < E; j++) {
+    const int i = lane * E + j;
+    v[j] = pb_bf2f(ldu16<SYNC>(x + i));
+    wv[j] = __ldg(w + i);
+    c[j] = i < half ? __ldg(cs + i) : 0.0f;
+    sv[j] = i < half ? __ldg(sn + i) : 0.0f;
+  }
+#pragma unroll
+  for (int j = 0; j < E; j++) ss[j] = __fmul_rn(v[j], v[j]);
 #pragma unroll
   for (int width = E; width > 1; width >>= 1)
 #pragma unroll
@@ -322,7 +371,7 @@ __device__ void head_norm_rope(const bf16_t* __restrict__ x, const float* __rest
 #pragma unroll
   for (int j = 0; j < E; j++) {
     const int i = lane * E + j;
-    o[i] = pb_bf2f(pb_f2bf(__fmul_rn(w[i], pb_bf2f(pb_f2bf(__fmul_rn(v[j], rs))))));
+    o[i] = pb_bf2f(pb_f2bf(__fmul_rn(wv[j], pb_bf2f(pb_f2bf(__fmul_rn(v[j], rs))))));
   }
   __syncwarp();
   float lo_n[E], hi_n[E];
@@ -331,8 +380,8 @@ __device__ void head_norm_rope(const bf16_t* __restrict__ x, const float* __rest
     const int i = lane * E + j;   // i < HD/2 covers the pairs when i < half
     if (i < half) {
       const float lo = o[i], hi = o[i + HD / 2];
-      lo_n[j] = pb_bf2f(pb_f2bf(__fadd_rn(__fmul_rn(lo, cs[i]), __fmul_rn(-hi, sn[i]))));
-      hi_n[j] = pb_bf2f(pb_f2bf(__fadd_rn(__fmul_rn(hi, cs[i]), __fmul_rn(lo, sn[i]))));
+      lo_n[j] = pb_bf2f(pb_f2bf(__fadd_rn(__fmul_rn(lo, c[j]), __fmul_rn(-hi, sv[j]))));
+      hi_n[j] = pb_bf2f(pb_f2bf(__fadd_rn(__fmul_rn(hi, c[j]), __fmul_rn(lo, sv[j]))));
     }
   }
   __syncwarp();
