@@ -27,10 +27,10 @@ constexpr int PH_GEMV = 0, PH_ARGMAX = 2, PH_SCORE = 3, PH_SOFTMAX = 4, PH_PV = 
 constexpr int PV_DIMS = 16;                    // head dims per P.V task
 constexpr int DSEGS = 16;                      // 2048-byte segments per stage
 constexpr int STAGE_CODES = DSEGS * 2048;      // 32 KB
-constexpr unsigned PB_WAIT_LIMIT = 1u << 24;   // polls before a wait gives up
 
 struct Phase {
-  int kind, nch, epi, _pad;
+  int kind, nch, epi;
+  int rowoff;     // GEMV: float offset in the activation region of the row values
   StepArgs a;     // GEMV: weights, prologue, epilogue
   AttnArgs at;    // ATTN
 };
@@ -90,18 +90,17 @@ PB_DEV bool mbar_wait(uint64_t* b, unsigned parity, volatile int* abort_flag) {
   }
   return false;
 }
-PB_DEV void bulk_g2s(void* dst, const void* src, unsigned bytes, uint64_t* bar) {
-  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
-               ::"r"(smem_u32(dst)), "l"(src), "r"(bytes), "r"(smem_u32(bar)) : "memory");
+// the weight stream is read once per token: an evict-first L2 policy keeps it
+// from pushing the small reused state (activations, KV cache, conv rings,
+// norm weights) out of L2
+PB_DEV uint64_t l2_evict_first() {
+  uint64_t pol;
+  asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(pol));
+  return pol;
 }
-PB_DEV bool grid_wait(const unsigned* bar, unsigned target) {
-  for (unsigned i = 0; i < PB_WAIT_LIMIT; i++) {
-    unsigned v;
-    asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(bar) : "memory");
-    if (v >= target) return true;
-    if (i > 16) __nanosleep(20);
-  }
-  return false;
+PB_DEV void bulk_g2s(void* dst, const void* src, unsigned bytes, uint64_t* bar, uint64_t pol) {
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1], %2, [%3], %4;"
+               ::"r"(smem_u32(dst)), "l"(src), "r"(bytes), "r"(smem_u32(bar)), "l"(pol) : "memory");
 }
 PB_DEV void grid_arrive(unsigned* bar) {
   asm volatile("red.release.gpu.global.add.u32 [%0], 1;" ::"l"(bar) : "memory");
@@ -171,6 +170,7 @@ __device__ void producer(const DecodeArgs& d, unsigned char* ring, uint64_t* ful
   unsigned it = 0;
   bool ok = true;
   unsigned long long pwait = 0;
+  const uint64_t pol = l2_evict_first();
   for (int tok = 0; tok < d.ntok && ok; tok++) {
     for (int p = 0; p < d.nphase && ok; p++) {
       const Phase& ph = d.phases[p];
@@ -188,8 +188,8 @@ __device__ void producer(const DecodeArgs& d, unsigned char* ring, uint64_t* ful
         const int nr = min(RB, r1 - r);
         const unsigned bc = (unsigned)nr * nch * 2048, bs = (unsigned)nr * nch * 32 * Gm::SB;
         mbar_expect_tx(&full[slot], bc + bs);
-        bulk_g2s(ring + (size_t)slot * Gm::STAGE, codes + (size_t)r * nch * 2048, bc, &full[slot]);
-        bulk_g2s(ring + (size_t)slot * Gm::STAGE + STAGE_CODES, sc + (size_t)r * nch * 32 * Gm::SB, bs, &full[slot]);
+        bulk_g2s(ring + (size_t)slot * Gm::STAGE, codes + (size_t)r * nch * 2048, bc, &full[slot], pol);
+        bulk_g2s(ring + (size_t)slot * Gm::STAGE + STAGE_CODES, sc + (size_t)r * nch * 32 * Gm::SB, bs, &full[slot], pol);
         it++;
       }
     }
@@ -208,24 +208,23 @@ __device__ void producer(const DecodeArgs& d, unsigned char* ring, uint64_t* ful
   }
 }
 
-constexpr int PSLOTS = 8;   // > ring stages: a partial slot is never reused while read
-
 // One GEMV phase on the consumer warps. Warp (g, c) owns rows 2g, 2g+1 of
-// every stage in chunk c. With several chunks per row the chunk partials meet
-// in shared memory; the warp whose arrival completes a row pair (a shared
-// atomic counter) adds them in chunk order and writes the outputs, so no CTA
-// barrier sits in the stage loop. A wait that gives up breaks out of the loop
-// and the phase still ends with the same barriers as on the other warps.
+// every stage in chunk c. The stage loop only waits, computes each row's
+// chunk value (the lane chains and the shuffle-down tree) and parks it in
+// shared memory (rowv, [local row][chunk]); after one consumer barrier the
+// 256 threads combine the chunks in order and run the epilogue for all of
+// the CTA's rows at once, so no per-row latency sits in the stage loop. A
+// wait that gives up breaks out of the loop and the phase still ends with
+// the same barriers as on the other warps.
 template <bool F32S, int EPI>
 __device__ __noinline__ void gemv_phase(const DecodeArgs& d, const Phase& ph, unsigned char* ring, float* xreg,
                            uint64_t* full, uint64_t* empty, unsigned& it, float* red,
-                           float (*part)[DSEGS][8], int (*cnt)[8], float* bestv, int* besti,
-                           volatile int* abort_flag, unsigned long long* tmark2) {
+                           float* bestv, int* besti,
+                           volatile int* abort_flag, unsigned long long* tmark2, const GridWait* gw, int pos) {
   typedef DGeo<F32S> Gm;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  if (threadIdx.x < PSLOTS * 8) (&cnt[0][0])[threadIdx.x] = 0;
   float* sx = xreg;
-  step_prologue<1>(ph.a, sx, red);      // ends with a consumer barrier
+  step_prologue<1>(ph.a, sx, red, gw, pos);   // grid barrier inside; ends with a consumer barrier
   if (tmark2 && threadIdx.x == 0) *tmark2 = gtime();
   // the few fields the stage loop needs, read once into registers (the loop's
   // global stores would otherwise force the compiler to re-read them)
@@ -233,8 +232,9 @@ __device__ __noinline__ void gemv_phase(const DecodeArgs& d, const Phase& ph, un
   const int Nrows = ph.a.N;
   Ctl* const ctl = ph.a.ctl;
   const int nch = ph.nch, RB = DSEGS / nch;
+  float* const rowv = xreg + ph.rowoff;
   const int c = warp % nch, g = warp / nch;
-  const int ds = d.ds;
+  const unsigned ds = (unsigned)d.ds;
   f2x xr[32];
   {
     const float* x0 = sx + (c * 64 + lane) * 33;
@@ -244,14 +244,10 @@ __device__ __noinline__ void gemv_phase(const DecodeArgs& d, const Phase& ph, un
   }
   int r0, r1;
   row_range(Nrows, RB, r0, r1);
-  float bv = -INFINITY;
-  int bi = 0x7fffffff;
+  unsigned slot = it % ds, par = (it / ds) & 1;
   for (int r = r0; r < r1; r += RB) {
-    const unsigned slot = it % ds, round = it / ds;
-    const unsigned ps = it % PSLOTS;
-    it++;
     const unsigned long long tw = (tmark2 && threadIdx.x == 0) ? gtime() : 0;
-    if (!mbar_wait(&full[slot], round & 1, abort_flag)) {
+    if (!mbar_wait(&full[slot], par, abort_flag)) {
       *abort_flag = 1;
       atomicCAS(d.err, 0, 2);
       break;
@@ -288,43 +284,41 @@ __device__ __noinline__ void gemv_phase(const DecodeArgs& d, const Phase& ph, un
     // the stage's data are consumed (the tree depends on every loaded value):
     // hand the slot back to the producer
     __syncwarp();
-    if (lane == 0) mbar_arrive(&empty[slot]);
-    const int row0 = r + g * 2;
-    if (row0 >= r1 || lane != 0) continue;
-    float o0, o1;
-    if (nch == 1) {
-      o0 = __fadd_rn(0.0f, v[0]);
-      o1 = __fadd_rn(0.0f, v[1]);
-    } else {
-      part[ps][g * 2][c] = v[0];
-      part[ps][g * 2 + 1][c] = v[1];
-      __threadfence_block();
-      const int old = atomicAdd(&cnt[ps][g], 1);
-      if (old != nch - 1) continue;                  // not the last chunk of this row pair
-      __threadfence_block();
-      o0 = 0.0f;
-      o1 = 0.0f;
-      for (int cc = 0; cc < nch; cc++) {
-        o0 = __fadd_rn(o0, part[ps][g * 2][cc]);
-        o1 = __fadd_rn(o1, part[ps][g * 2 + 1][cc]);
-      }
+    if (lane == 0) {
+      mbar_arrive(&empty[slot]);
+      const int lr = r - r0 + g * 2;
+      rowv[lr * nch + c] = v[0];
+      if (r + g * 2 + 1 < r1) rowv[(lr + 1) * nch + c] = v[1];
     }
-    if (EPI == EPI_SILU) {
-      // rows 2i (w1) and 2i+1 (w3): k_silu_mul_bf, lfm3_nanode.cu:821-829
-      if (row0 + 1 < r1) {
-        const float av = pb_bf2f(pb_f2bf(o0)), bw = pb_bf2f(pb_f2bf(o1));
-        reinterpret_cast<bf16_t*>(yout)[row0 >> 1] = pb_f2bf(__fmul_rn(__fmul_rn(av, pb_sigmoid(av)), bw));
+    it++;
+    if (++slot == ds) { slot = 0; par ^= 1; }
+  }
+  csync<1>();
+  // epilogue over the CTA's rows: chunk values added in chunk order from 0
+  const int nr = r1 - r0;
+  float bv = -INFINITY;
+  int bi = 0x7fffffff;
+  if (EPI == EPI_SILU) {
+    // rows 2i (w1) and 2i+1 (w3): k_silu_mul_bf, lfm3_nanode.cu:821-829
+    for (int i = 2 * threadIdx.x; i + 1 < nr; i += 512) {
+      float o0 = 0.0f, o1 = 0.0f;
+      for (int cc = 0; cc < nch; cc++) {
+        o0 = __fadd_rn(o0, rowv[i * nch + cc]);
+        o1 = __fadd_rn(o1, rowv[(i + 1) * nch + cc]);
       }
-    } else if (EPI == EPI_ARGMAX) {
-      reinterpret_cast<float*>(yout)[row0] = o0;
-      if (o0 > bv || (o0 == bv && row0 < bi)) { bv = o0; bi = row0; }
-      if (row0 + 1 < r1) {
-        reinterpret_cast<float*>(yout)[row0 + 1] = o1;
-        if (o1 > bv || (o1 == bv && row0 + 1 < bi)) { bv = o1; bi = row0 + 1; }
+      const float av = pb_bf2f(pb_f2bf(o0)), bw = pb_bf2f(pb_f2bf(o1));
+      reinterpret_cast<bf16_t*>(yout)[(r0 + i) >> 1] = pb_f2bf(__fmul_rn(__fmul_rn(av, pb_sigmoid(av)), bw));
+    }
+  } else {
+    for (int i = threadIdx.x; i < nr; i += 256) {
+      float o = 0.0f;
+      for (int cc = 0; cc < nch; cc++) o = __fadd_rn(o, rowv[i * nch + cc]);
+      if (EPI == EPI_ARGMAX) {
+        reinterpret_cast<float*>(yout)[r0 + i] = o;
+        if (o > bv || (o == bv && r0 + i < bi)) { bv = o; bi = r0 + i; }
+      } else {
+        reinterpret_cast<bf16_t*>(yout)[r0 + i] = pb_f2bf(o);
       }
-    } else {
-      reinterpret_cast<bf16_t*>(yout)[row0] = pb_f2bf(o0);
-      if (row0 + 1 < r1) reinterpret_cast<bf16_t*>(yout)[row0 + 1] = pb_f2bf(o1);
     }
   }
   if (EPI == EPI_ARGMAX) {
@@ -641,8 +635,6 @@ __global__ void __launch_bounds__(288, 1) k_decode(DecodeArgs d) {
   uint64_t* full = reinterpret_cast<uint64_t*>(xreg + ((d.xregion + 1) & ~1));
   uint64_t* empty = full + d.ds;
   __shared__ float red[16];
-  __shared__ float part[PSLOTS][DSEGS][8];
-  __shared__ int cnt[PSLOTS][8];
   __shared__ float bestv[8];
   __shared__ int besti[8];
   __shared__ int abort_flag;
@@ -665,26 +657,35 @@ __global__ void __launch_bounds__(288, 1) k_decode(DecodeArgs d) {
     for (int p = 0; p < d.nphase; p++) {
       const unsigned q = (unsigned)(tok * d.nphase + p);
       tmark(d, tok, p, 0);
-      if (q > 0) {
-        if (threadIdx.x == 0 && !abort_flag && !grid_wait(d.bar, G * q)) { abort_flag = 1; atomicCAS(d.err, 0, 3); }
-        csync<1>();
-      }
-      if (abort_flag) return;        // every consumer thread leaves here together
-      tmark(d, tok, p, 1);
       const Phase& ph = d.phases[p];
+      const int kind = ph.kind;
+      // a GEMV phase takes the grid barrier inside its prologue, once the
+      // loads that do not depend on the previous phase are in flight (the
+      // trace's mark 1 then precedes the barrier)
+      if (kind != PH_GEMV) {
+        if (q > 0) {
+          if (threadIdx.x == 0 && !abort_flag && !grid_wait(d.bar, G * q)) { abort_flag = 1; atomicCAS(d.err, 0, 3); }
+          csync<1>();
+        }
+        if (abort_flag) return;        // every consumer thread leaves here together
+      }
+      tmark(d, tok, p, 1);
       unsigned long long* tm2 = (d.trace && tok == 0) ? d.trace + ((size_t)blockIdx.x * d.nphase + p) * 8 + 2 : nullptr;
-      if (ph.kind == PH_GEMV) {
-        if (ph.epi == EPI_SILU)
-          gemv_phase<F32S, EPI_SILU>(d, ph, ring, xreg, full, empty, it, red, part, cnt, bestv, besti, &abort_flag, tm2);
-        else if (ph.epi == EPI_ARGMAX)
-          gemv_phase<F32S, EPI_ARGMAX>(d, ph, ring, xreg, full, empty, it, red, part, cnt, bestv, besti, &abort_flag, tm2);
+      if (kind == PH_GEMV) {
+        const GridWait gw = {d.bar, G * q, &abort_flag, d.err};
+        const GridWait* gwp = q > 0 ? &gw : nullptr;
+        const int epi = ph.epi, pos = pos0 + tok;
+        if (epi == EPI_SILU)
+          gemv_phase<F32S, EPI_SILU>(d, ph, ring, xreg, full, empty, it, red, bestv, besti, &abort_flag, tm2, gwp, pos);
+        else if (epi == EPI_ARGMAX)
+          gemv_phase<F32S, EPI_ARGMAX>(d, ph, ring, xreg, full, empty, it, red, bestv, besti, &abort_flag, tm2, gwp, pos);
         else
-          gemv_phase<F32S, EPI_BF16>(d, ph, ring, xreg, full, empty, it, red, part, cnt, bestv, besti, &abort_flag, tm2);
-      } else if (ph.kind == PH_SCORE) {
+          gemv_phase<F32S, EPI_BF16>(d, ph, ring, xreg, full, empty, it, red, bestv, besti, &abort_flag, tm2, gwp, pos);
+      } else if (kind == PH_SCORE) {
         attn_score_phase<E>(ph.at, pos0 + tok, xreg);
-      } else if (ph.kind == PH_SOFTMAX) {
+      } else if (kind == PH_SOFTMAX) {
         attn_softmax_phase(ph.at, pos0 + tok, red);
-      } else if (ph.kind == PH_PV) {
+      } else if (kind == PH_PV) {
         attn_pv_phase<E>(ph.at, pos0 + tok, xreg, d.pv_per_warp);
       } else {
         if (blockIdx.x == 0 && threadIdx.x < 32) argmax_phase(d);
@@ -696,6 +697,7 @@ __global__ void __launch_bounds__(288, 1) k_decode(DecodeArgs d) {
         __threadfence();
         grid_arrive(d.bar);
       }
+      if (abort_flag) return;        // read after the barrier: the same value on every consumer thread
       tmark(d, tok, p, 4);
     }
   }

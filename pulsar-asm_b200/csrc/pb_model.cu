@@ -109,8 +109,7 @@ __global__ void __launch_bounds__(256, 2) k_step(StepArgs a) {
                 (size_t)(r1 - r0) * NCH * 32 * SPair<F32S>::BYTES);
   }
   pb_grid_launch_dependents();
-  pb_grid_wait();
-  step_prologue<0>(a, sx, red);
+  step_prologue<0>(a, sx, red, nullptr, -1);   // takes the dependency wait after its constant loads
   float xr[64];
   {
     const float* x0 = sx + (c * 64 + lane) * 33;          // block c*64 + lane, padded
@@ -258,8 +257,7 @@ __global__ void __launch_bounds__(256) k_tail(StepArgs a) {
   extern __shared__ __align__(16) float smem[];
   __shared__ float red[16];
   pb_grid_launch_dependents();
-  pb_grid_wait();
-  step_prologue<0>(a, smem, red);
+  step_prologue<0>(a, smem, red, nullptr, -1);
 }
 
 // ----------------------------------------------------------- host model
@@ -687,10 +685,15 @@ int build_phases(pb_state* s) {
   const int cnt_max = (((s->max_ctx + 7) / 8) + 3) & ~3;
   s->pv_per_warp = 9 * cnt_max;
   int xr = std::max(s->max_ctx, std::max(8 * 2 * m->HD, 8 * s->pv_per_warp));
+  // a GEMV phase holds its padded input, then its row values: at most
+  // ceil(row blocks / CTAs) stages of 16 chunk values per CTA
+  const int G = pb_num_sms();
   for (auto& p : ph)
     if (p.kind == PH_GEMV) {
-      const int need = p.a.K + p.a.K / 32 + ((p.a.pro == PRO_ADDNORM || p.a.pro == PRO_EMBED) ? 2 * m->H : 0);
-      xr = std::max(xr, need);
+      const int RB = DSEGS / p.nch;
+      const int nrb = (p.a.N + RB - 1) / RB;
+      p.rowoff = (p.a.K + p.a.K / 32 + 3) & ~3;
+      xr = std::max(xr, p.rowoff + ((nrb + G - 1) / G) * DSEGS);
     }
   int dev = 0;
   cudaGetDevice(&dev);
@@ -735,11 +738,7 @@ int launch_decode_t(pb_state* s, int ntok, cudaStream_t st) {
   d.ds = s->ds;
   d.trace = s->d_trace;
   d.pv_per_warp = s->pv_per_warp;
-  static bool set = false;
-  if (!set) {
-    PB_TRY_CUDA(cudaFuncSetAttribute(k_decode<F32S, E>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)s->dsmem));
-    set = true;
-  }
+  PB_TRY_CUDA(cudaFuncSetAttribute(k_decode<F32S, E>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)s->dsmem));
   int per_sm = 0;
   PB_TRY_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k_decode<F32S, E>, 288, s->dsmem));
   if (per_sm < 1) return pb_set_error(PB_ENOTSUP, "persistent decode does not fit on an SM");

@@ -87,6 +87,47 @@ PB_DEV unsigned short ldu16(const unsigned short* p) { return SYNC ? __ldcg(p) :
 template <int SYNC>
 PB_DEV int ldi(const int* p) { return SYNC ? __ldcg(p) : *p; }
 
+constexpr unsigned PB_WAIT_LIMIT = 1u << 24;   // polls before a wait gives up
+
+// arrival counter of the persistent kernel's grid barrier: wait until `target`
+// CTAs have arrived (bounded)
+PB_DEV bool grid_wait(const unsigned* bar, unsigned target) {
+  for (unsigned i = 0; i < PB_WAIT_LIMIT; i++) {
+    unsigned v;
+    asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(bar) : "memory");
+    if (v >= target) return true;
+    if (i > 16) __nanosleep(20);
+  }
+  return false;
+}
+
+// The dependency wait a prologue takes once the loads that do not depend on
+// the previous phase (weights of norms, conv taps, ring slots of earlier
+// tokens) are in flight. SYNC = 0: the programmatic-launch wait of the
+// per-kernel path. SYNC = 1: the persistent kernel's grid barrier (null: the
+// launch's first phase, no wait); a wait that gives up raises the abort flag,
+// read by the caller after a consumer barrier.
+struct GridWait {
+  const unsigned* bar;
+  unsigned target;
+  volatile int* abort;
+  int* err;
+};
+template <int SYNC>
+PB_DEV void gw_pass(const GridWait* g) {
+  if (!SYNC) {
+    pb_grid_wait();
+    return;
+  }
+  if (g) {
+    if (threadIdx.x == 0 && !*g->abort && !grid_wait(g->bar, g->target)) {
+      *g->abort = 1;
+      atomicCAS(g->err, 0, 3);
+    }
+    csync<1>();
+  }
+}
+
 // ---------------------------------------------------------------- prologue
 // sx (the GEMV input) is stored padded, one spare float per 32, so that lane
 // l reading its 32 consecutive values (index 32 l + j) hits bank (l + j) % 32.
@@ -148,10 +189,11 @@ PB_DEV void st_bf(bf16_t* p, const float (&v)[N]) {
 // [E t, E t + E)), in the reference's order (rmsnorm_body,
 // lfm3_nanode.cu:383-440): squares summed pairwise, warp shuffle-down tree,
 // the 8 warp partials ascending; rs = 1/sqrt(mean + eps) correctly rounded;
-// out = bf16(w * bf16(v * rs)) (as floats). `red` (8 floats) must not be in
-// use by a neighbouring call: callers alternate two buffers.
+// out = bf16(w * bf16(v * rs)) (as floats), w = this thread's E weights.
+// `red` (8 floats) must not be in use by a neighbouring call: callers
+// alternate two buffers.
 template <int E, int SYNC>
-__device__ void rms_reg(const float (&v)[E], const float* __restrict__ w, float (&out)[E], int H,
+__device__ void rms_reg(const float (&v)[E], const float (&wv)[E], float (&out)[E], int H,
                         float eps, float* red) {
   const int t = threadIdx.x;
   float ss[E];
@@ -163,8 +205,6 @@ __device__ void rms_reg(const float (&v)[E], const float* __restrict__ w, float 
     for (int i = 0; i < width / 2; i++) ss[i] = __fadd_rn(ss[2 * i], ss[2 * i + 1]);
   const float s = pb_warp_tree(ss[0]);
   if ((t & 31) == 0) red[t >> 5] = s;
-  float wv[E];
-  ld_f32<E>(w + (size_t)t * E, wv);
   csync<SYNC>();
   float tot = red[0];
 #pragma unroll
@@ -176,10 +216,12 @@ __device__ void rms_reg(const float (&v)[E], const float* __restrict__ w, float 
 
 // plain GEMV input: K = 256 EK values, EK consecutive per thread
 template <int EK, int SYNC>
-__device__ void pro_plain(const StepArgs& a, float* sx) {
+__device__ void pro_plain(const StepArgs& a, float* sx, const GridWait* gw) {
   const int t = threadIdx.x;
+  const bf16_t* xin = a.xin;
+  gw_pass<SYNC>(gw);
   float x[EK];
-  ld_bf<EK, SYNC>(a.xin + (size_t)t * EK, x);
+  ld_bf<EK, SYNC>(xin + (size_t)t * EK, x);
 #pragma unroll
   for (int j = 0; j < EK; j++) sx[padx(t * EK + j)] = x[j];
 }
@@ -189,20 +231,35 @@ __device__ void pro_plain(const StepArgs& a, float* sx) {
 // chain; out = bf16(C * bf16(y)). The ring slot of position pos held pos - W,
 // which no CTA reads any more; CTA 0 writes the new value there.
 template <int E, int W, int SYNC>
-__device__ void pro_conv(const StepArgs& a, float* sx) {
+__device__ void pro_conv(const StepArgs& a, float* sx, const GridWait* gw, int pos) {
   const int t = threadIdx.x, H = a.H;
-  const int pos = ldi<SYNC>(&a.ctl->pos);
-  float B[E], C[E], X[E], tp[E * W];
-  ld_bf<E, SYNC>(a.xin + (size_t)t * E, B);
-  ld_bf<E, SYNC>(a.xin + H + (size_t)t * E, C);
-  ld_bf<E, SYNC>(a.xin + 2 * H + (size_t)t * E, X);
+  const bf16_t* xin = a.xin;
+  bf16_t* ring = a.ring;
+  float tp[E * W];
   ld_f32<E * W>(a.taps + (size_t)t * E * W, tp);
+  // the W-1 older ring slots hold positions of earlier tokens: in the
+  // persistent kernel (pos given) they are final before this phase's barrier
   float rg[W - 1][E];
+  if (SYNC && pos >= 0) {
 #pragma unroll
-  for (int k = 0; k < W - 1; k++) {
-    const int p = pos - (W - 1) + k;
-    ld_bf<E, SYNC>(a.ring + (size_t)(((p % W) + W) % W) * H + (size_t)t * E, rg[k]);
+    for (int k = 0; k < W - 1; k++) {
+      const int p = pos - (W - 1) + k;
+      ld_bf<E, SYNC>(ring + (size_t)(((p % W) + W) % W) * H + (size_t)t * E, rg[k]);
+    }
   }
+  gw_pass<SYNC>(gw);
+  if (!(SYNC && pos >= 0)) {
+    pos = ldi<SYNC>(&a.ctl->pos);
+#pragma unroll
+    for (int k = 0; k < W - 1; k++) {
+      const int p = pos - (W - 1) + k;
+      ld_bf<E, SYNC>(ring + (size_t)(((p % W) + W) % W) * H + (size_t)t * E, rg[k]);
+    }
+  }
+  float B[E], C[E], X[E];
+  ld_bf<E, SYNC>(xin + (size_t)t * E, B);
+  ld_bf<E, SYNC>(xin + H + (size_t)t * E, C);
+  ld_bf<E, SYNC>(xin + 2 * H + (size_t)t * E, X);
   float bx[E], y[E];
 #pragma unroll
   for (int j = 0; j < E; j++) {
@@ -214,16 +271,27 @@ __device__ void pro_conv(const StepArgs& a, float* sx) {
     y[j] = pb_bf2f(pb_f2bf(__fmul_rn(C[j], pb_bf2f(pb_f2bf(acc)))));
     sx[padx(t * E + j)] = y[j];
   }
-  if (blockIdx.x == 0) st_bf<E>(a.ring + (size_t)(pos % W) * H + (size_t)t * E, bx);
+  if (blockIdx.x == 0) st_bf<E>(ring + (size_t)(pos % W) * H + (size_t)t * E, bx);
 }
 
 // residual (embedding row, or xin [+ post-normalised hin]) -> optional rout
 // -> optional norm -> x
 template <int E, int SYNC>
-__device__ void pro_residual(const StepArgs& a, float* sx, float* red) {
+__device__ void pro_residual(const StepArgs& a, float* sx, float* red, const GridWait* gw) {
   const int t = threadIdx.x, H = a.H;
+  const bf16_t* xin = a.xin;
+  const bf16_t* hin = a.hin;
+  const float* wnorm = a.wnorm;
+  bf16_t* rout = a.rout;
+  const float eps = a.eps;
+  const bool embed = a.pro == PRO_EMBED;
+  // norm weights first: they do not depend on the previous phase
+  float wp[E], wn[E];
+  if (!embed && hin) ld_f32<E>(a.wpost + (size_t)t * E, wp);
+  if (wnorm) ld_f32<E>(wnorm + (size_t)t * E, wn);
+  gw_pass<SYNC>(gw);
   float R[E];
-  if (a.pro == PRO_EMBED) {
+  if (embed) {
     // k_dequant_row (lfm3_nanode.cu:138-142): bf16(code * scale), row = token;
     // the row is read from the tied table's streaming layout
     const int tok = ldi<SYNC>(&a.ctl->token);
@@ -240,18 +308,18 @@ __device__ void pro_residual(const StepArgs& a, float* sx, float* red) {
       R[j] = pb_bf2f(pb_f2bf(__fmul_rn(code, s)));
     }
   } else {
-    ld_bf<E, SYNC>(a.xin + (size_t)t * E, R);
-    if (a.hin) {
+    ld_bf<E, SYNC>(xin + (size_t)t * E, R);
+    if (hin) {
       float Hv[E], hn[E];
-      ld_bf<E, SYNC>(a.hin + (size_t)t * E, Hv);
-      rms_reg<E, SYNC>(Hv, a.wpost, hn, H, a.eps, red);
+      ld_bf<E, SYNC>(hin + (size_t)t * E, Hv);
+      rms_reg<E, SYNC>(Hv, wp, hn, H, eps, red);
 #pragma unroll
       for (int j = 0; j < E; j++) R[j] = pb_bf2f(pb_f2bf(__fadd_rn(R[j], hn[j])));
     }
   }
-  if (a.rout && blockIdx.x == 0) st_bf<E>(a.rout + (size_t)t * E, R);
+  if (rout && blockIdx.x == 0) st_bf<E>(rout + (size_t)t * E, R);
   float X[E];
-  if (a.wnorm) rms_reg<E, SYNC>(R, a.wnorm, X, H, a.eps, red + 8);
+  if (wnorm) rms_reg<E, SYNC>(R, wn, X, H, eps, red + 8);
   else {
 #pragma unroll
     for (int j = 0; j < E; j++) X[j] = R[j];
@@ -264,8 +332,9 @@ __device__ void pro_residual(const StepArgs& a, float* sx, float* red) {
 // bf16(((s0+s1)+(s2+s3))+((s4+s5)+(s6+s7))) (k_attn_head, lfm3_nanode.cu:594-600),
 // then the sigmoid head gate (k_sigmoid_gate, :852-864): bf16(out * 1/(1+e^-g))
 template <int EK, int SYNC>
-__device__ void pro_attn(const StepArgs& a, float* sx) {
+__device__ void pro_attn(const StepArgs& a, float* sx, const GridWait* gw) {
   const int t = threadIdx.x, hd = a.hd;
+  gw_pass<SYNC>(gw);
 #pragma unroll
   for (int j0 = 0; j0 < EK; j0 += 4) {
     const int i = t * EK + j0, h = i / hd, d = i - h * hd;
@@ -285,57 +354,61 @@ __device__ void pro_attn(const StepArgs& a, float* sx) {
 }
 
 template <int E, int SYNC>
-__device__ void pro_dispatch_conv(const StepArgs& a, float* sx) {
+__device__ void pro_dispatch_conv(const StepArgs& a, float* sx, const GridWait* gw, int pos) {
   switch (a.convw) {
-    case 2: pro_conv<E, 2, SYNC>(a, sx); break;
-    case 3: pro_conv<E, 3, SYNC>(a, sx); break;
-    case 4: pro_conv<E, 4, SYNC>(a, sx); break;
-    case 7: pro_conv<E, 7, SYNC>(a, sx); break;
-    default: break;   // rejected at load time
+    case 2: pro_conv<E, 2, SYNC>(a, sx, gw, pos); break;
+    case 3: pro_conv<E, 3, SYNC>(a, sx, gw, pos); break;
+    case 4: pro_conv<E, 4, SYNC>(a, sx, gw, pos); break;
+    case 7: pro_conv<E, 7, SYNC>(a, sx, gw, pos); break;
+    default: gw_pass<SYNC>(gw); break;   // rejected at load time
   }
 }
 
 // Computes the GEMV input x (fp32 values of bf16 numbers) into sx, padded
 // (element i at padx(i)). Runs on 256 threads; H = 256 E with E in
 // {1, 2, 4, 8, 16}; plain inputs K = 256 EK with EK in {1, 2, 4, 8, 16, 32}.
-// `red` holds 16 floats. Ends with a CTA barrier.
+// `red` holds 16 floats. The dependency wait (gw_pass) is taken inside, after
+// the loads that do not need it; pos >= 0 is the step's position when the
+// caller knows it (else it is read from the control block). Ends with a CTA
+// barrier.
 template <int SYNC>
-__device__ __noinline__ void step_prologue(const StepArgs& a, float* sx, float* red) {
-  if (a.pro == PRO_PLAIN) {
+__device__ __noinline__ void step_prologue(const StepArgs& a, float* sx, float* red, const GridWait* gw, int pos) {
+  const int pro = a.pro;
+  if (pro == PRO_PLAIN) {
     switch (a.K >> 8) {
-      case 1: pro_plain<1, SYNC>(a, sx); break;
-      case 2: pro_plain<2, SYNC>(a, sx); break;
-      case 4: pro_plain<4, SYNC>(a, sx); break;
-      case 8: pro_plain<8, SYNC>(a, sx); break;
-      case 16: pro_plain<16, SYNC>(a, sx); break;
-      case 32: pro_plain<32, SYNC>(a, sx); break;
-      default: break;
+      case 1: pro_plain<1, SYNC>(a, sx, gw); break;
+      case 2: pro_plain<2, SYNC>(a, sx, gw); break;
+      case 4: pro_plain<4, SYNC>(a, sx, gw); break;
+      case 8: pro_plain<8, SYNC>(a, sx, gw); break;
+      case 16: pro_plain<16, SYNC>(a, sx, gw); break;
+      case 32: pro_plain<32, SYNC>(a, sx, gw); break;
+      default: gw_pass<SYNC>(gw); break;
     }
-  } else if (a.pro == PRO_ATTN) {
+  } else if (pro == PRO_ATTN) {
     switch (a.K >> 8) {
-      case 4: pro_attn<4, SYNC>(a, sx); break;
-      case 8: pro_attn<8, SYNC>(a, sx); break;
-      case 16: pro_attn<16, SYNC>(a, sx); break;
-      case 32: pro_attn<32, SYNC>(a, sx); break;
-      default: break;
+      case 4: pro_attn<4, SYNC>(a, sx, gw); break;
+      case 8: pro_attn<8, SYNC>(a, sx, gw); break;
+      case 16: pro_attn<16, SYNC>(a, sx, gw); break;
+      case 32: pro_attn<32, SYNC>(a, sx, gw); break;
+      default: gw_pass<SYNC>(gw); break;
     }
-  } else if (a.pro == PRO_CONV) {
+  } else if (pro == PRO_CONV) {
     switch (a.H >> 8) {
-      case 1: pro_dispatch_conv<1, SYNC>(a, sx); break;
-      case 2: pro_dispatch_conv<2, SYNC>(a, sx); break;
-      case 4: pro_dispatch_conv<4, SYNC>(a, sx); break;
-      case 8: pro_dispatch_conv<8, SYNC>(a, sx); break;
-      case 16: pro_dispatch_conv<16, SYNC>(a, sx); break;
-      default: break;
+      case 1: pro_dispatch_conv<1, SYNC>(a, sx, gw, pos); break;
+      case 2: pro_dispatch_conv<2, SYNC>(a, sx, gw, pos); break;
+      case 4: pro_dispatch_conv<4, SYNC>(a, sx, gw, pos); break;
+      case 8: pro_dispatch_conv<8, SYNC>(a, sx, gw, pos); break;
+      case 16: pro_dispatch_conv<16, SYNC>(a, sx, gw, pos); break;
+      default: gw_pass<SYNC>(gw); break;
     }
   } else {
     switch (a.H >> 8) {
-      case 1: pro_residual<1, SYNC>(a, sx, red); break;
-      case 2: pro_residual<2, SYNC>(a, sx, red); break;
-      case 4: pro_residual<4, SYNC>(a, sx, red); break;
-      case 8: pro_residual<8, SYNC>(a, sx, red); break;
-      case 16: pro_residual<16, SYNC>(a, sx, red); break;
-      default: break;
+      case 1: pro_residual<1, SYNC>(a, sx, red, gw); break;
+      case 2: pro_residual<2, SYNC>(a, sx, red, gw); break;
+      case 4: pro_residual<4, SYNC>(a, sx, red, gw); break;
+      case 8: pro_residual<8, SYNC>(a, sx, red, gw); break;
+      case 16: pro_residual<16, SYNC>(a, sx, red, gw); break;
+      default: gw_pass<SYNC>(gw); break;
     }
   }
   csync<SYNC>();
