@@ -54,11 +54,11 @@ def measured_peaks():
 
 
 def ncu_traffic():
-    """dram bytes per launch of the roofline kernel from the committed ncu summary"""
+    """dram bytes per token of the roofline kernel from the committed ncu summary"""
     p = os.path.join(ROOT, "profiles", "roofline_traffic.json")
     if os.path.exists(p):
         try:
-            return json.load(open(p)).get("traffic_bytes_per_launch")
+            return json.load(open(p)).get("traffic_bytes_per_token")
         except Exception:
             return None
     return None
@@ -277,6 +277,9 @@ def main():
         achieved = k_bytes / (k_ms / 1000.0) / 1e9
         rk = {"kernel": "k_step<1,fp16 scales,SiLU epilogue> (w1|w3 GEMV, 16384x2048)",
               "bytes_per_launch": k_bytes, "ms_per_launch": k_ms}
+    # ncu's dram bytes per token (one captured launch), scaled to this launch
+    tpt = ncu_traffic()
+    traffic = tpt * args.steps if (tpt and persistent) else None
     line = {"metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms_max / args.steps, "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "fp32", "data": "synthetic",
@@ -290,7 +293,7 @@ def main():
             "gpu_launches": launches,
             "kernels_per_token": kpt,
             "roofline": dict({"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
-                              "frac": achieved / peak, "traffic": ncu_traffic(),
+                              "frac": achieved / peak, "traffic": traffic,
                               "peak_source": "measured hbm_gbs (MEASURED_PEAKS.json)" if peak_kind == "measured"
                               else "fallback 6.65 TB/s"}, **rk),
             "step_kernel_gbs": k_bytes / (k_ms / 1000.0) / 1e9,
