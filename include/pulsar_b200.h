@@ -133,12 +133,13 @@ int pb_layer_step(pb_model* m, pb_state* s, int layer, int pos, uint16_t* d_x, v
 int pb_decode_token(pb_model* m, pb_state* s, int token, int pos, int* h_out_id,
                     float* d_logits, void* stream);
 /* n greedy steps on the device: step i feeds the previous id (the first feeds
- * `token`), at positions pos0..pos0+n-1, one CUDA graph launch per token,
- * no host round trip; d_ids (int32 [n]) receives the generated ids. */
+ * `token`), at positions pos0..pos0+n-1, no host round trip (one persistent
+ * kernel launch for all n tokens; one CUDA graph launch per token with
+ * PB_DECODE_MODE=graph); d_ids (int32 [n]) receives the generated ids. */
 int pb_decode_greedy(pb_model* m, pb_state* s, int token, int pos0, int n, int* d_ids,
                      void* stream);
 /* teacher-forced prompt: step i feeds d_tokens[i] (device int32 [n]) at
- * position pos0+i, one graph launch per token, no host round trip; d_ids
+ * position pos0+i, launched like pb_decode_greedy, no host round trip; d_ids
  * (optional, int32 [n]) receives the greedy prediction after each token.
  * The prompt feed of the reference's step loop (lfm3_nanode.cu:5828-6030). */
 int pb_decode_prompt(pb_model* m, pb_state* s, const int* d_tokens, int n, int pos0, int* d_ids,
