@@ -1,23 +1,27 @@
 // pb_decode.cuh -- the persistent decode kernel: every phase of a token (each
 // fused GEMV, each attention layer, the greedy argmax), for any number of
-// tokens, in ONE cooperative launch with one CTA per SM.
+// tokens, in ONE cooperative launch with one CTA (8 warps) per SM.
 //
-// Each CTA is warp-specialised:
-//  * warp 8 (the producer) streams the CTA's row slice of every GEMV of every
-//    token, in order, through a ring of DS shared-memory stages with 1-D TMA
-//    bulk copies (cp.async.bulk ... mbarrier::complete_tx). Weights never
-//    depend on activations, so the producer never waits for a phase: while the
-//    consumers sit in a grid barrier, compute a prologue or run attention, HBM
-//    keeps streaming the next GEMV's weights into the ring.
-//  * warps 0-7 (the consumers) run the phases: wait until every CTA finished
-//    the previous phase (a global arrival counter), compute the fused prologue
-//    (the same code as the per-kernel path, pb_step.cuh), then consume stages:
-//    two 2048-code segments per warp per stage, in the reference's reduction
-//    order, with the FMA chains of a lane's two blocks (l and l+32) packed into
-//    one fma.rn.f32x2 (each half is an IEEE fma, so the values are unchanged).
+// Weight stream: the CTA's row slice of every GEMV of every token is a fixed
+// sequence of stages (16 segments of 2048 codes + their scales), known before
+// the launch (host-built schedule: per CTA and GEMV its rows and first stage,
+// and a stage -> GEMV map). Stages flow through a ring of DS shared-memory
+// slots filled by 1-D TMA bulk copies (cp.async.bulk ... complete_tx on the
+// slot's mbarrier). There is no producer warp: the warp that is the last of
+// the eight to finish reading a slot (a shared counter) issues the copy of the
+// stage DS places ahead into it. Weights never depend on activations, so the
+// stream runs ahead across phases: while the warps sit in a grid barrier,
+// compute a prologue or run attention, the next GEMV's first DS stages land.
+//
+// Phases: wait until every CTA finished the previous phase (a global arrival
+// counter), compute the fused prologue (pb_step.cuh), then consume stages:
+// two 2048-code segments per warp per stage, in the reference's reduction
+// order, with the FMA chains of a lane's two blocks (l and l+32) packed into
+// one fma.rn.f32x2 (each half is an IEEE fma, so the values are unchanged).
 // All spin waits are bounded: on a timeout the kernel records an error code,
-// the producer waits (bounded) for its copies in flight, and every thread
-// returns; the host reports the error.
+// every warp leaves at the next phase boundary, and thread 0 waits (bounded)
+// for the copies still in flight before the CTA exits; the host reports the
+// error.
 #pragma once
 #include "pb_step.cuh"
 
@@ -31,9 +35,33 @@ constexpr int STAGE_CODES = DSEGS * 2048;      // 32 KB
 struct Phase {
   int kind, nch, epi;
   int rowoff;     // GEMV: float offset in the activation region of the row values
+  int gidx;       // GEMV: index in the per-CTA GEMV schedule
+  int _pad;
   StepArgs a;     // GEMV: weights, prologue, epilogue
   AttnArgs at;    // ATTN
 };
+
+// one CTA's share of one GEMV: rows [r0, r1), stages base .. base + ceil((r1-r0)/RB) - 1
+struct GemvSched {
+  const char* codes;
+  const char* scales;
+  int r0, r1, base, nch;
+};
+
+// the weight stream's bookkeeping, at the start of dynamic shared memory
+struct IssueCtx {
+  uint64_t pol;           // L2 evict-first policy of the stream
+  unsigned spt;           // stages per token of this CTA
+  unsigned total;         // stages of the launch (spt * tokens)
+  unsigned ds;            // ring slots
+  unsigned ngemv;
+  unsigned cnt[8];        // per slot: warps done reading the current stage
+  unsigned issued[8];     // per slot: last stage issued into it (+1; 0 = none)
+  uint32_t sched_s;       // shared address of GemvSched[ngemv]
+  uint32_t map_s;         // shared address of the stage -> GEMV map (u16 [spt])
+};
+constexpr int ISSUE_BYTES = 128;
+constexpr int MAX_DS = 8;
 
 struct DecodeArgs {
   const Phase* phases;
@@ -47,6 +75,11 @@ struct DecodeArgs {
   int ds;              // ring stages
   int pv_per_warp;     // floats of shared memory per warp in a P.V phase
   unsigned long long* trace;   // optional: per (CTA, phase) globaltimer marks of token 0
+  const GemvSched* sched;      // [CTA][ngemv]
+  const unsigned short* smap;  // [CTA][spt_max]: stage of a token -> GEMV index
+  const int* spt;              // [CTA]: stages per token
+  int ngemv, spt_max;
+  int sched_off, map_off;      // byte offsets of the tables in dynamic shared memory
 };
 
 PB_DEV unsigned long long gtime() {
@@ -155,57 +188,35 @@ PB_DEV float leaf2(const uint4 (&q)[4], float slo, float shi, const f2x (&xr)[32
   return __fmaf_rn(shi, d1, __fmaf_rn(slo, d0, 0.0f));
 }
 
-PB_DEV void row_range(int N, int RB, int& r0, int& r1) {
-  const int nrb = (N + RB - 1) / RB;
-  const int rb0 = (int)(((long long)blockIdx.x * nrb) / gridDim.x);
-  const int rb1 = (int)(((long long)(blockIdx.x + 1) * nrb) / gridDim.x);
-  r0 = rb0 * RB;
-  r1 = min(rb1 * RB, N);
-}
 
+extern __shared__ __align__(128) unsigned char dsm[];
+PB_DEV IssueCtx* issue_ctx() { return reinterpret_cast<IssueCtx*>(dsm); }
+
+// Copy stage S of the launch into its ring slot (S mod DS). Called by thread 0
+// for the first DS stages and afterwards by lane 0 of the warp that releases
+// the slot's previous stage, so every issue follows the slot's last read.
 template <bool F32S>
-__device__ void producer(const DecodeArgs& d, unsigned char* ring, uint64_t* full, uint64_t* empty,
-                         volatile int* abort_flag) {
+PB_DEV void issue_stage(unsigned S, unsigned char* ring, uint64_t* full) {
   typedef DGeo<F32S> Gm;
-  unsigned it = 0;
-  bool ok = true;
-  unsigned long long pwait = 0;
-  const uint64_t pol = l2_evict_first();
-  for (int tok = 0; tok < d.ntok && ok; tok++) {
-    for (int p = 0; p < d.nphase && ok; p++) {
-      const Phase& ph = d.phases[p];
-      if (ph.kind != PH_GEMV) continue;
-      const int nch = ph.nch, RB = DSEGS / nch;
-      int r0, r1;
-      row_range(ph.a.N, RB, r0, r1);
-      const char* codes = reinterpret_cast<const char*>(ph.a.codes);
-      const char* sc = reinterpret_cast<const char*>(ph.a.scales);
-      for (int r = r0; r < r1; r += RB) {
-        const unsigned slot = it % d.ds, round = it / d.ds;
-        const unsigned long long tw = d.trace ? gtime() : 0;
-        if (!mbar_wait(&empty[slot], (round & 1) ^ 1, abort_flag)) { ok = false; break; }
-        if (d.trace) pwait += gtime() - tw;
-        const int nr = min(RB, r1 - r);
-        const unsigned bc = (unsigned)nr * nch * 2048, bs = (unsigned)nr * nch * 32 * Gm::SB;
-        mbar_expect_tx(&full[slot], bc + bs);
-        bulk_g2s(ring + (size_t)slot * Gm::STAGE, codes + (size_t)r * nch * 2048, bc, &full[slot], pol);
-        bulk_g2s(ring + (size_t)slot * Gm::STAGE + STAGE_CODES, sc + (size_t)r * nch * 32 * Gm::SB, bs, &full[slot], pol);
-        it++;
-      }
-    }
-  }
-  if (d.trace) d.trace[((size_t)blockIdx.x * d.nphase + 0) * 8 + 6] = pwait;   // producer: ring-full waits
-  if (!ok) {
-    atomicCAS(d.err, 0, 1);
-    *abort_flag = 1;
-  }
-  // never leave with copies in flight: the latest issued round of every slot
-  // must have landed (bounded wait)
-  for (unsigned s = it > (unsigned)d.ds ? it - d.ds : 0; s < it; s++) {
-    const unsigned slot = s % d.ds, round = s / d.ds;
-    unsigned i = 0;
-    while (!mbar_try(&full[slot], round & 1) && i < PB_WAIT_LIMIT) { i++; if (i > 64) __nanosleep(32); }
-  }
+  IssueCtx* ic = issue_ctx();
+  if (S >= ic->total) return;
+  const unsigned spt = ic->spt, ds = ic->ds;
+  const unsigned k = S % spt, slot = S % ds;
+  unsigned short j;
+  asm volatile("ld.shared.u16 %0, [%1];" : "=h"(j) : "r"(ic->map_s + 2 * k));
+  const GemvSched* gs = reinterpret_cast<const GemvSched*>(dsm + (ic->sched_s - smem_u32(dsm)));
+  const GemvSched g = gs[j];
+  const int RB = DSEGS / g.nch;
+  const int r = g.r0 + ((int)k - g.base) * RB;
+  const int nr = min(RB, g.r1 - r);
+  const unsigned bc = (unsigned)nr * g.nch * 2048, bs = (unsigned)nr * g.nch * 32 * Gm::SB;
+  // the slot's previous contents were read through the generic proxy
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+  mbar_expect_tx(&full[slot], bc + bs);
+  bulk_g2s(ring + (size_t)slot * Gm::STAGE, g.codes + (size_t)r * g.nch * 2048, bc, &full[slot], ic->pol);
+  bulk_g2s(ring + (size_t)slot * Gm::STAGE + STAGE_CODES, g.scales + (size_t)r * g.nch * 32 * Gm::SB, bs,
+           &full[slot], ic->pol);
+  ic->issued[slot] = S + 1;
 }
 
 // One GEMV phase on the consumer warps. Warp (g, c) owns rows 2g, 2g+1 of
@@ -216,20 +227,19 @@ __device__ void producer(const DecodeArgs& d, unsigned char* ring, uint64_t* ful
 // the CTA's rows at once, so no per-row latency sits in the stage loop. A
 // wait that gives up breaks out of the loop and the phase still ends with
 // the same barriers as on the other warps.
-template <bool F32S, int EPI>
-__device__ __noinline__ void gemv_phase(const DecodeArgs& d, const Phase& ph, unsigned char* ring, float* xreg,
-                           uint64_t* full, uint64_t* empty, unsigned& it, float* red,
+template <bool F32S, int EPI, int EH, int W>
+__device__ __forceinline__ unsigned gemv_phase(const DecodeArgs& d, const Phase& ph, unsigned char* ring,
+                           float* xreg, uint64_t* full, unsigned it, float* red,
                            float* bestv, int* besti,
                            volatile int* abort_flag, unsigned long long* tmark2, const GridWait* gw, int pos) {
   typedef DGeo<F32S> Gm;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   float* sx = xreg;
-  step_prologue<1>(ph.a, sx, red, gw, pos);   // grid barrier inside; ends with a consumer barrier
+  step_prologue_fixed<1, EH, W>(ph.a, sx, red, gw, pos);   // grid barrier inside; ends with a consumer barrier
   if (tmark2 && threadIdx.x == 0) *tmark2 = gtime();
   // the few fields the stage loop needs, read once into registers (the loop's
   // global stores would otherwise force the compiler to re-read them)
   void* const yout = ph.a.y;
-  const int Nrows = ph.a.N;
   Ctl* const ctl = ph.a.ctl;
   const int nch = ph.nch, RB = DSEGS / nch;
   float* const rowv = xreg + ph.rowoff;
@@ -243,7 +253,11 @@ __device__ __noinline__ void gemv_phase(const DecodeArgs& d, const Phase& ph, un
     for (int j = 0; j < 32; j++) xr[j] = pk(x0[j], x1[j]);
   }
   int r0, r1;
-  row_range(Nrows, RB, r0, r1);
+  {
+    const GemvSched* gs = reinterpret_cast<const GemvSched*>(dsm + (issue_ctx()->sched_s - smem_u32(dsm)));
+    r0 = gs[ph.gidx].r0;
+    r1 = gs[ph.gidx].r1;
+  }
   unsigned slot = it % ds, par = (it / ds) & 1;
   for (int r = r0; r < r1; r += RB) {
     const unsigned long long tw = (tmark2 && threadIdx.x == 0) ? gtime() : 0;
@@ -282,10 +296,13 @@ __device__ __noinline__ void gemv_phase(const DecodeArgs& d, const Phase& ph, un
 #pragma unroll
     for (int u = 0; u < 2; u++) v[u] = pb_warp_tree(leaf2(q[u], slo[u], shi[u], xr));
     // the stage's data are consumed (the tree depends on every loaded value):
-    // hand the slot back to the producer
+    // the last warp to get here refills the slot with the stage DS ahead
     __syncwarp();
     if (lane == 0) {
-      mbar_arrive(&empty[slot]);
+      if (atomicAdd(&issue_ctx()->cnt[slot], 1u) == 7u) {
+        issue_ctx()->cnt[slot] = 0;
+        issue_stage<F32S>(it + ds, ring, full);
+      }
       const int lr = r - r0 + g * 2;
       rowv[lr * nch + c] = v[0];
       if (r + g * 2 + 1 < r1) rowv[(lr + 1) * nch + c] = v[1];
@@ -339,6 +356,7 @@ __device__ __noinline__ void gemv_phase(const DecodeArgs& d, const Phase& ph, un
       ctl->slot_idx[blockIdx.x] = ix;
     }
   }
+  return it;
 }
 
 // ------------------------------------------------------- split attention
@@ -626,34 +644,49 @@ __device__ void argmax_phase(const DecodeArgs& d) {
   }
 }
 
-template <bool F32S, int E>
-__global__ void __launch_bounds__(288, 1) k_decode(DecodeArgs d) {
+template <bool F32S, int E, int EH, int W>
+__global__ void __launch_bounds__(256, 1) k_decode(DecodeArgs d) {
   typedef DGeo<F32S> Gm;
-  extern __shared__ __align__(128) unsigned char dsm[];
-  unsigned char* ring = dsm;
-  float* xreg = reinterpret_cast<float*>(dsm + (size_t)d.ds * Gm::STAGE);
+  IssueCtx* ic = issue_ctx();
+  unsigned char* ring = dsm + ISSUE_BYTES;
+  float* xreg = reinterpret_cast<float*>(ring + (size_t)d.ds * Gm::STAGE);
   uint64_t* full = reinterpret_cast<uint64_t*>(xreg + ((d.xregion + 1) & ~1));
-  uint64_t* empty = full + d.ds;
   __shared__ float red[16];
   __shared__ float bestv[8];
   __shared__ int besti[8];
   __shared__ int abort_flag;
-  const int warp = threadIdx.x >> 5;
-  if (threadIdx.x == 0) {
-    for (int i = 0; i < d.ds; i++) { mbar_init(&full[i], 1); mbar_init(&empty[i], 8); }
-    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
-    abort_flag = 0;
+  // this CTA's weight-stream schedule into shared memory
+  {
+    const uint4* src = reinterpret_cast<const uint4*>(d.sched + (size_t)blockIdx.x * d.ngemv);
+    uint4* dst = reinterpret_cast<uint4*>(dsm + d.sched_off);
+    for (int i = threadIdx.x; i < d.ngemv * (int)(sizeof(GemvSched) / 16); i += blockDim.x) dst[i] = __ldg(src + i);
+    const int spt = __ldg(d.spt + blockIdx.x);
+    const unsigned short* ms = d.smap + (size_t)blockIdx.x * d.spt_max;
+    unsigned short* md = reinterpret_cast<unsigned short*>(dsm + d.map_off);
+    for (int i = threadIdx.x; i < spt; i += blockDim.x) md[i] = __ldg(ms + i);
+    if (threadIdx.x == 0) {
+      ic->pol = l2_evict_first();
+      ic->spt = (unsigned)spt;
+      ic->total = (unsigned)spt * (unsigned)d.ntok;
+      ic->ds = (unsigned)d.ds;
+      ic->ngemv = (unsigned)d.ngemv;
+      for (int i = 0; i < MAX_DS; i++) { ic->cnt[i] = 0; ic->issued[i] = 0; }
+      ic->sched_s = smem_u32(dsm + d.sched_off);
+      ic->map_s = smem_u32(dsm + d.map_off);
+      for (int i = 0; i < d.ds; i++) mbar_init(&full[i], 1);
+      asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+      abort_flag = 0;
+    }
   }
   __syncthreads();
-  if (warp == 8) {
-    if ((threadIdx.x & 31) == 0) producer<F32S>(d, ring, full, empty, &abort_flag);
-    return;
-  }
+  if (threadIdx.x == 0)
+    for (int i = 0; i < d.ds; i++) issue_stage<F32S>((unsigned)i, ring, full);
   const unsigned G = gridDim.x;
   // the position advances by one per token (argmax phase), so it is read once
   const int pos0 = __ldcg(&d.ctl->pos);
   unsigned it = 0;
-  for (int tok = 0; tok < d.ntok; tok++) {
+  bool stop = false;
+  for (int tok = 0; tok < d.ntok && !stop; tok++) {
     for (int p = 0; p < d.nphase; p++) {
       const unsigned q = (unsigned)(tok * d.nphase + p);
       tmark(d, tok, p, 0);
@@ -667,7 +700,7 @@ __global__ void __launch_bounds__(288, 1) k_decode(DecodeArgs d) {
           if (threadIdx.x == 0 && !abort_flag && !grid_wait(d.bar, G * q)) { abort_flag = 1; atomicCAS(d.err, 0, 3); }
           csync<1>();
         }
-        if (abort_flag) return;        // every consumer thread leaves here together
+        if (abort_flag) { stop = true; break; }   // every thread leaves here together
       }
       tmark(d, tok, p, 1);
       unsigned long long* tm2 = (d.trace && tok == 0) ? d.trace + ((size_t)blockIdx.x * d.nphase + p) * 8 + 2 : nullptr;
@@ -676,11 +709,11 @@ __global__ void __launch_bounds__(288, 1) k_decode(DecodeArgs d) {
         const GridWait* gwp = q > 0 ? &gw : nullptr;
         const int epi = ph.epi, pos = pos0 + tok;
         if (epi == EPI_SILU)
-          gemv_phase<F32S, EPI_SILU>(d, ph, ring, xreg, full, empty, it, red, bestv, besti, &abort_flag, tm2, gwp, pos);
+          it = gemv_phase<F32S, EPI_SILU, EH, W>(d, ph, ring, xreg, full, it, red, bestv, besti, &abort_flag, tm2, gwp, pos);
         else if (epi == EPI_ARGMAX)
-          gemv_phase<F32S, EPI_ARGMAX>(d, ph, ring, xreg, full, empty, it, red, bestv, besti, &abort_flag, tm2, gwp, pos);
+          it = gemv_phase<F32S, EPI_ARGMAX, EH, W>(d, ph, ring, xreg, full, it, red, bestv, besti, &abort_flag, tm2, gwp, pos);
         else
-          gemv_phase<F32S, EPI_BF16>(d, ph, ring, xreg, full, empty, it, red, bestv, besti, &abort_flag, tm2, gwp, pos);
+          it = gemv_phase<F32S, EPI_BF16, EH, W>(d, ph, ring, xreg, full, it, red, bestv, besti, &abort_flag, tm2, gwp, pos);
       } else if (kind == PH_SCORE) {
         attn_score_phase<E>(ph.at, pos0 + tok, xreg);
       } else if (kind == PH_SOFTMAX) {
@@ -691,14 +724,25 @@ __global__ void __launch_bounds__(288, 1) k_decode(DecodeArgs d) {
         if (blockIdx.x == 0 && threadIdx.x < 32) argmax_phase(d);
       }
       tmark(d, tok, p, 3);
-      // every consumer thread's writes of this phase are issued: publish them
+      // every thread's writes of this phase are issued: publish them
       csync<1>();
       if (threadIdx.x == 0) {
         __threadfence();
         grid_arrive(d.bar);
       }
-      if (abort_flag) return;        // read after the barrier: the same value on every consumer thread
+      if (abort_flag) { stop = true; break; }     // read after the barrier: the same value on every thread
       tmark(d, tok, p, 4);
+    }
+  }
+  // never leave with copies in flight: each slot's last issued stage must
+  // have landed (bounded); every issue happened before the barrier above
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < d.ds; i++) {
+      const unsigned s1 = ic->issued[i];
+      if (!s1) continue;
+      const unsigned par = ((s1 - 1) / (unsigned)d.ds) & 1;
+      unsigned n = 0;
+      while (!mbar_try(&full[i], par) && n < PB_WAIT_LIMIT) { n++; if (n > 64) __nanosleep(32); }
     }
   }
 }

@@ -320,6 +320,9 @@ struct pb_state {
   size_t mem_bytes = 0;
   // persistent decode kernel: phase table, arrival counter, error word
   Phase* d_phases = nullptr;
+  char* d_sched = nullptr;         // weight-stream schedule: GemvSched [CTA][ngemv], spt [CTA], map [CTA][spt_max]
+  int ngemv = 0, spt_max = 0;
+  size_t sched_bytes = 0, spt_off = 0, map_off = 0, sched_smem_off = 0;
   int nphase = 0;
   unsigned* d_bar = nullptr;
   int* d_err = nullptr;
@@ -565,6 +568,16 @@ int build_graph(pb_state* s) {
 }
 
 // ---- persistent decode ---------------------------------------------------
+// The persistent kernel is compiled for the shapes listed here (head_dim 64,
+// hidden 2048, conv width 3: the LFM3 2B-class backbone); other models decode
+// on the per-kernel CUDA-graph path, with the same results.
+bool persistent_shape(const pb_model* m) {
+  if (m->HD != 64 || m->H != 2048 || m->W != 3) return false;
+  const int kf = m->F >> 8, ka = (m->NH * m->HD) >> 8;
+  return m->F % 256 == 0 && (kf == 8 || kf == 16 || kf == 32) && (m->NH * m->HD) % 256 == 0 &&
+         (ka == 4 || ka == 8 || ka == 16);
+}
+
 Phase gemv_phase_of(const pb_q8& w, int epi, StepArgs a) {
   Phase ph = {};
   ph.kind = PH_GEMV;
@@ -695,19 +708,75 @@ int build_phases(pb_state* s) {
       p.rowoff = (p.a.K + p.a.K / 32 + 3) & ~3;
       xr = std::max(xr, p.rowoff + ((nrb + G - 1) / G) * DSEGS);
     }
+  // weight-stream schedule: per CTA and GEMV its rows (the same split as the
+  // stage loop) and first stage within the token, and the stage -> GEMV map
+  int ngemv = 0;
+  for (auto& p : ph)
+    if (p.kind == PH_GEMV) p.gidx = ngemv++;
+  std::vector<GemvSched> sched((size_t)G * ngemv);
+  std::vector<int> spt(G, 0);
+  std::vector<std::vector<unsigned short>> smap(G);
+  for (int b = 0; b < G; b++) {
+    int base = 0;
+    for (auto& p : ph) {
+      if (p.kind != PH_GEMV) continue;
+      const int RB = DSEGS / p.nch;
+      const int nrb = (p.a.N + RB - 1) / RB;
+      const int rb0 = (int)(((long long)b * nrb) / G), rb1 = (int)(((long long)(b + 1) * nrb) / G);
+      GemvSched& g = sched[(size_t)b * ngemv + p.gidx];
+      g.codes = reinterpret_cast<const char*>(p.a.codes);
+      g.scales = reinterpret_cast<const char*>(p.a.scales);
+      g.r0 = rb0 * RB;
+      g.r1 = std::min(rb1 * RB, p.a.N);
+      g.base = base;
+      g.nch = p.nch;
+      for (int k = rb0; k < rb1; k++) smap[b].push_back((unsigned short)p.gidx);
+      base += rb1 - rb0;
+    }
+    spt[b] = base;
+  }
+  int spt_max = 1;
+  for (int b = 0; b < G; b++) spt_max = std::max(spt_max, spt[b]);
+  if (ngemv > 65535 || spt_max > 16384)
+    return pb_set_error(PB_ENOTSUP, "persistent decode: %d GEMVs, %d stages per token", ngemv, spt_max);
   int dev = 0;
   cudaGetDevice(&dev);
   int optin = 0;
   cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
   const size_t stage = m->sdt == PB_DT_F32 ? DGeo<true>::STAGE : DGeo<false>::STAGE;
-  const size_t static_est = 14 * 1024;
+  const size_t static_est = 4 * 1024;
   const size_t xb = (size_t)((xr + 1) & ~1) * 4;
-  long avail = (long)optin - (long)static_est - (long)xb - 2 * 8 * 8;
+  const size_t tab = (size_t)ngemv * sizeof(GemvSched) + (((size_t)spt_max * 2 + 15) & ~(size_t)15);
+  long avail = (long)optin - (long)static_est - ISSUE_BYTES - (long)xb - MAX_DS * 8 - 16 - (long)tab;
   int ds = (int)std::min<long>(6, avail / (long)stage);
   if (ds < 2) return pb_set_error(PB_ENOTSUP, "persistent decode: shared memory for %d ring stages", ds);
   s->ds = ds;
   s->xregion = xr;
-  s->dsmem = (size_t)ds * stage + xb + 2 * (size_t)ds * 8;
+  s->ngemv = ngemv;
+  s->spt_max = spt_max;
+  // dynamic shared memory: issue context, ring, activation region, mbarriers, schedule, map
+  const size_t sched_off = (ISSUE_BYTES + (size_t)ds * stage + xb + (size_t)ds * 8 + 15) & ~(size_t)15;
+  s->dsmem = sched_off + tab;
+  {
+    // one device buffer: schedule [G][ngemv], spt [G], map [G][spt_max]
+    const size_t sb = sched.size() * sizeof(GemvSched);
+    s->spt_off = sb;
+    const size_t mo = (sb + (size_t)G * 4 + 15) & ~(size_t)15;
+    s->sched_bytes = mo + (size_t)G * spt_max * 2;
+    std::vector<char> host(s->sched_bytes, 0);
+    memcpy(host.data(), sched.data(), sb);
+    memcpy(host.data() + sb, spt.data(), (size_t)G * 4);
+    for (int b = 0; b < G; b++)
+      if (!smap[b].empty()) memcpy(host.data() + mo + (size_t)b * spt_max * 2, smap[b].data(), smap[b].size() * 2);
+    if (cudaMalloc(&s->d_sched, s->sched_bytes) != cudaSuccess) {
+      cudaGetLastError();
+      s->d_sched = nullptr;
+      return pb_set_error(PB_ENOMEM, "persistent decode: schedule");
+    }
+    PB_TRY_CUDA(cudaMemcpy(s->d_sched, host.data(), s->sched_bytes, cudaMemcpyHostToDevice));
+    s->map_off = mo;
+  }
+  s->sched_smem_off = sched_off;
   s->nphase = (int)ph.size();
   if (getenv("PB_DECODE_TRACE") && !s->d_trace) {
     if (cudaMalloc(&s->d_trace, (size_t)pb_num_sms() * ph.size() * 8 * 8) != cudaSuccess) {
@@ -724,7 +793,7 @@ int build_phases(pb_state* s) {
   return PB_OK;
 }
 
-template <bool F32S, int E>
+template <bool F32S, int E, int EH, int W>
 int launch_decode_t(pb_state* s, int ntok, cudaStream_t st) {
   DecodeArgs d;
   d.phases = s->d_phases;
@@ -738,16 +807,24 @@ int launch_decode_t(pb_state* s, int ntok, cudaStream_t st) {
   d.ds = s->ds;
   d.trace = s->d_trace;
   d.pv_per_warp = s->pv_per_warp;
-  PB_TRY_CUDA(cudaFuncSetAttribute(k_decode<F32S, E>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)s->dsmem));
+  d.sched = reinterpret_cast<const GemvSched*>(s->d_sched);
+  d.spt = reinterpret_cast<const int*>(s->d_sched + s->spt_off);
+  d.smap = reinterpret_cast<const unsigned short*>(s->d_sched + s->map_off);
+  d.ngemv = s->ngemv;
+  d.spt_max = s->spt_max;
+  d.sched_off = (int)s->sched_smem_off;
+  d.map_off = (int)(s->sched_smem_off + (size_t)s->ngemv * sizeof(GemvSched));
+  PB_TRY_CUDA(cudaFuncSetAttribute(k_decode<F32S, E, EH, W>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                   (int)s->dsmem));
   int per_sm = 0;
-  PB_TRY_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k_decode<F32S, E>, 288, s->dsmem));
+  PB_TRY_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k_decode<F32S, E, EH, W>, 256, s->dsmem));
   if (per_sm < 1) return pb_set_error(PB_ENOTSUP, "persistent decode does not fit on an SM");
   const int grid = pb_num_sms();
   if (grid > MAX_CTA || grid < s->m->NH) return pb_set_error(PB_ENOTSUP, "persistent decode grid %d", grid);
   PB_TRY_CUDA(cudaMemsetAsync(s->d_bar, 0, sizeof(unsigned), st));
   if (s->d_trace) PB_TRY_CUDA(cudaMemsetAsync(s->d_trace, 0, (size_t)pb_num_sms() * s->nphase * 8 * 8, st));
   void* args[] = {&d};
-  cudaError_t e = cudaLaunchCooperativeKernel((const void*)k_decode<F32S, E>, dim3(grid), dim3(288), args,
+  cudaError_t e = cudaLaunchCooperativeKernel((const void*)k_decode<F32S, E, EH, W>, dim3(grid), dim3(256), args,
                                               s->dsmem, st);
   if (e != cudaSuccess) return pb_set_error(PB_ECUDA, "launch k_decode: %s", cudaGetErrorString(e));
   pb_count_launch();
@@ -758,12 +835,9 @@ int launch_decode(pb_state* s, int ntok, cudaStream_t st) {
   int rc = build_phases(s);
   if (rc) return rc;
   const bool f = s->m->sdt == PB_DT_F32;
-  switch (s->m->HD) {
-    case 32: return f ? launch_decode_t<true, 1>(s, ntok, st) : launch_decode_t<false, 1>(s, ntok, st);
-    case 64: return f ? launch_decode_t<true, 2>(s, ntok, st) : launch_decode_t<false, 2>(s, ntok, st);
-    case 128: return f ? launch_decode_t<true, 4>(s, ntok, st) : launch_decode_t<false, 4>(s, ntok, st);
-  }
-  return pb_set_error(PB_ENOTSUP, "persistent decode: head_dim %d", s->m->HD);
+  if (persistent_shape(s->m))
+    return f ? launch_decode_t<true, 2, 8, 3>(s, ntok, st) : launch_decode_t<false, 2, 8, 3>(s, ntok, st);
+  return pb_set_error(PB_ENOTSUP, "persistent decode: shape not compiled");
 }
 
 // the kernel's error word (a bounded wait gave up); clears it
@@ -1101,7 +1175,7 @@ extern "C" int pb_state_create(pb_model* m, int max_ctx, pb_state** out) {
     s->persistent = !(mode && strcmp(mode, "graph") == 0);
     // the persistent softmax holds a head's scores in registers (64 per lane)
     const int span = (m->win > 0 && m->win < max_ctx) ? m->win : max_ctx;
-    if (span > 2048) s->persistent = false;
+    if (span > 2048 || !persistent_shape(m)) s->persistent = false;
   }
   const int H = m->H, n_conv = m->L - m->n_attn, half = half_rot(m);
   const size_t kvb = (size_t)m->n_attn * 2 * max_ctx * m->NKV * m->HD * 2;
@@ -1151,6 +1225,7 @@ extern "C" int pb_state_create(pb_model* m, int max_ctx, pb_state** out) {
 extern "C" int pb_state_destroy(pb_state* s) {
   if (!s) return PB_OK;
   if (s->d_phases) cudaFree(s->d_phases);
+  if (s->d_sched) cudaFree(s->d_sched);
   if (s->d_trace) cudaFree(s->d_trace);
   if (s->exec) cudaGraphExecDestroy(s->exec);
   if (s->graph) cudaGraphDestroy(s->graph);

@@ -414,6 +414,35 @@ __device__ __noinline__ void step_prologue(const StepArgs& a, float* sx, float* 
   csync<SYNC>();
 }
 
+// step_prologue for a kernel specialised to one hidden size (H = 256 EH) and
+// conv width W: only those variants are compiled in, and it inlines into its
+// caller (no call, no register save area).
+template <int SYNC, int EH, int W>
+__device__ __forceinline__ void step_prologue_fixed(const StepArgs& a, float* sx, float* red, const GridWait* gw,
+                                                    int pos) {
+  const int pro = a.pro;
+  if (pro == PRO_PLAIN) {
+    switch (a.K >> 8) {
+      case 8: pro_plain<8, SYNC>(a, sx, gw); break;
+      case 16: pro_plain<16, SYNC>(a, sx, gw); break;
+      case 32: pro_plain<32, SYNC>(a, sx, gw); break;
+      default: gw_pass<SYNC>(gw); break;      // other K: the host keeps this kernel off
+    }
+  } else if (pro == PRO_ATTN) {
+    switch (a.K >> 8) {
+      case 4: pro_attn<4, SYNC>(a, sx, gw); break;
+      case 8: pro_attn<8, SYNC>(a, sx, gw); break;
+      case 16: pro_attn<16, SYNC>(a, sx, gw); break;
+      default: gw_pass<SYNC>(gw); break;
+    }
+  } else if (pro == PRO_CONV) {
+    pro_conv<EH, W, SYNC>(a, sx, gw, pos);
+  } else {
+    pro_residual<EH, SYNC>(a, sx, red, gw);
+  }
+  csync<SYNC>();
+}
+
 // ------------------------------------------------------------- attention
 // per-head RMSNorm (k_headnorm, lfm3_nanode.cu:460-479) + NeoX RoPE
 // (k_rope, :483-498) by one warp; result (fp32 of bf16) into o[HD]
