@@ -48,9 +48,16 @@ struct GemvSched {
   int r0, r1, base, nch;
 };
 
+// one stage of a CTA's weight stream: codes and scales as 16-byte offsets
+// into the model's weight arena, and their byte counts
+struct StageDesc {
+  unsigned codes16, scales16, bc, bs;
+};
+
 // the weight stream's bookkeeping, at the start of dynamic shared memory
 struct IssueCtx {
   uint64_t pol;           // L2 evict-first policy of the stream
+  const char* arena;      // the model's weight arena
   unsigned spt;           // stages per token of this CTA
   unsigned total;         // stages of the launch (spt * tokens)
   unsigned ds;            // ring slots
@@ -58,7 +65,7 @@ struct IssueCtx {
   unsigned cnt[8];        // per slot: warps done reading the current stage
   unsigned issued[8];     // per slot: last stage issued into it (+1; 0 = none)
   uint32_t sched_s;       // shared address of GemvSched[ngemv]
-  uint32_t map_s;         // shared address of the stage -> GEMV map (u16 [spt])
+  uint32_t desc_s;        // shared address of StageDesc[spt]
 };
 constexpr int ISSUE_BYTES = 128;
 constexpr int MAX_DS = 8;
@@ -76,10 +83,11 @@ struct DecodeArgs {
   int pv_per_warp;     // floats of shared memory per warp in a P.V phase
   unsigned long long* trace;   // optional: per (CTA, phase) globaltimer marks of token 0
   const GemvSched* sched;      // [CTA][ngemv]
-  const unsigned short* smap;  // [CTA][spt_max]: stage of a token -> GEMV index
+  const StageDesc* sdesc;      // [CTA][spt_max]: the stages of a token
   const int* spt;              // [CTA]: stages per token
+  const char* arena;           // the model's weight arena
   int ngemv, spt_max;
-  int sched_off, map_off;      // byte offsets of the tables in dynamic shared memory
+  int sched_off, desc_off;     // byte offsets of the tables in dynamic shared memory
 };
 
 PB_DEV unsigned long long gtime() {
@@ -192,31 +200,30 @@ PB_DEV float leaf2(const uint4 (&q)[4], float slo, float shi, const f2x (&xr)[32
 extern __shared__ __align__(128) unsigned char dsm[];
 PB_DEV IssueCtx* issue_ctx() { return reinterpret_cast<IssueCtx*>(dsm); }
 
-// Copy stage S of the launch into its ring slot (S mod DS). Called by thread 0
-// for the first DS stages and afterwards by lane 0 of the warp that releases
-// the slot's previous stage, so every issue follows the slot's last read.
+// Copy the stage at position k of a token into ring slot `slot`. Called by
+// thread 0 for the first DS stages and afterwards by lane 0 of the warp that
+// releases the slot's previous stage (stage S + DS follows stage S in the same
+// slot), so every copy follows the slot's last read.
 template <bool F32S>
-PB_DEV void issue_stage(unsigned S, unsigned char* ring, uint64_t* full) {
+PB_DEV void issue_stage(unsigned k, unsigned slot, unsigned S, unsigned char* ring, uint64_t* full) {
   typedef DGeo<F32S> Gm;
   IssueCtx* ic = issue_ctx();
-  if (S >= ic->total) return;
-  const unsigned spt = ic->spt, ds = ic->ds;
-  const unsigned k = S % spt, slot = S % ds;
-  unsigned short j;
-  asm volatile("ld.shared.u16 %0, [%1];" : "=h"(j) : "r"(ic->map_s + 2 * k));
-  const GemvSched* gs = reinterpret_cast<const GemvSched*>(dsm + (ic->sched_s - smem_u32(dsm)));
-  const GemvSched g = gs[j];
-  const int RB = DSEGS / g.nch;
-  const int r = g.r0 + ((int)k - g.base) * RB;
-  const int nr = min(RB, g.r1 - r);
-  const unsigned bc = (unsigned)nr * g.nch * 2048, bs = (unsigned)nr * g.nch * 32 * Gm::SB;
-  // the slot's previous contents were read through the generic proxy
-  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-  mbar_expect_tx(&full[slot], bc + bs);
-  bulk_g2s(ring + (size_t)slot * Gm::STAGE, g.codes + (size_t)r * g.nch * 2048, bc, &full[slot], ic->pol);
-  bulk_g2s(ring + (size_t)slot * Gm::STAGE + STAGE_CODES, g.scales + (size_t)r * g.nch * 32 * Gm::SB, bs,
-           &full[slot], ic->pol);
+  uint4 dsc;
+  asm volatile("ld.shared.v4.u32 {%0, %1, %2, %3}, [%4];"
+               : "=r"(dsc.x), "=r"(dsc.y), "=r"(dsc.z), "=r"(dsc.w) : "r"(ic->desc_s + 16 * k));
+  const char* arena = ic->arena;
+  const uint64_t pol = ic->pol;
+  mbar_expect_tx(&full[slot], dsc.z + dsc.w);
+  bulk_g2s(ring + (size_t)slot * Gm::STAGE, arena + (size_t)dsc.x * 16, dsc.z, &full[slot], pol);
+  bulk_g2s(ring + (size_t)slot * Gm::STAGE + STAGE_CODES, arena + (size_t)dsc.y * 16, dsc.w, &full[slot], pol);
   ic->issued[slot] = S + 1;
+}
+// arrival of a warp that finished reading a slot; true for the last of the 8
+PB_DEV bool slot_release(unsigned slot) {
+  unsigned old;
+  asm volatile("atom.acq_rel.cta.shared::cta.add.u32 %0, [%1], 1;"
+               : "=r"(old) : "r"(smem_u32(&issue_ctx()->cnt[slot])) : "memory");
+  return old == 7u;
 }
 
 // One GEMV phase on the consumer warps. Warp (g, c) owns rows 2g, 2g+1 of
@@ -259,6 +266,10 @@ __device__ __forceinline__ unsigned gemv_phase(const DecodeArgs& d, const Phase&
     r1 = gs[ph.gidx].r1;
   }
   unsigned slot = it % ds, par = (it / ds) & 1;
+  // position within the token of the stage that refills the current slot
+  const unsigned spt = issue_ctx()->spt, total = issue_ctx()->total;
+  unsigned kn = it % spt + ds;
+  while (kn >= spt) kn -= spt;
   for (int r = r0; r < r1; r += RB) {
     const unsigned long long tw = (tmark2 && threadIdx.x == 0) ? gtime() : 0;
     if (!mbar_wait(&full[slot], par, abort_flag)) {
@@ -299,9 +310,9 @@ __device__ __forceinline__ unsigned gemv_phase(const DecodeArgs& d, const Phase&
     // the last warp to get here refills the slot with the stage DS ahead
     __syncwarp();
     if (lane == 0) {
-      if (atomicAdd(&issue_ctx()->cnt[slot], 1u) == 7u) {
+      if (slot_release(slot)) {
         issue_ctx()->cnt[slot] = 0;
-        issue_stage<F32S>(it + ds, ring, full);
+        if (it + ds < total) issue_stage<F32S>(kn, slot, it + ds, ring, full);
       }
       const int lr = r - r0 + g * 2;
       rowv[lr * nch + c] = v[0];
@@ -309,6 +320,7 @@ __device__ __forceinline__ unsigned gemv_phase(const DecodeArgs& d, const Phase&
     }
     it++;
     if (++slot == ds) { slot = 0; par ^= 1; }
+    if (++kn == spt) kn = 0;
   }
   csync<1>();
   // epilogue over the CTA's rows: chunk values added in chunk order from 0
@@ -661,26 +673,27 @@ __global__ void __launch_bounds__(256, 1) k_decode(DecodeArgs d) {
     uint4* dst = reinterpret_cast<uint4*>(dsm + d.sched_off);
     for (int i = threadIdx.x; i < d.ngemv * (int)(sizeof(GemvSched) / 16); i += blockDim.x) dst[i] = __ldg(src + i);
     const int spt = __ldg(d.spt + blockIdx.x);
-    const unsigned short* ms = d.smap + (size_t)blockIdx.x * d.spt_max;
-    unsigned short* md = reinterpret_cast<unsigned short*>(dsm + d.map_off);
+    const uint4* ms = reinterpret_cast<const uint4*>(d.sdesc + (size_t)blockIdx.x * d.spt_max);
+    uint4* md = reinterpret_cast<uint4*>(dsm + d.desc_off);
     for (int i = threadIdx.x; i < spt; i += blockDim.x) md[i] = __ldg(ms + i);
     if (threadIdx.x == 0) {
       ic->pol = l2_evict_first();
+      ic->arena = d.arena;
       ic->spt = (unsigned)spt;
       ic->total = (unsigned)spt * (unsigned)d.ntok;
       ic->ds = (unsigned)d.ds;
       ic->ngemv = (unsigned)d.ngemv;
       for (int i = 0; i < MAX_DS; i++) { ic->cnt[i] = 0; ic->issued[i] = 0; }
       ic->sched_s = smem_u32(dsm + d.sched_off);
-      ic->map_s = smem_u32(dsm + d.map_off);
+      ic->desc_s = smem_u32(dsm + d.desc_off);
       for (int i = 0; i < d.ds; i++) mbar_init(&full[i], 1);
       asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
       abort_flag = 0;
     }
   }
   __syncthreads();
-  if (threadIdx.x == 0)
-    for (int i = 0; i < d.ds; i++) issue_stage<F32S>((unsigned)i, ring, full);
+  if (threadIdx.x == 0 && ic->spt > 0)
+    for (unsigned i = 0; i < (unsigned)d.ds && i < ic->total; i++) issue_stage<F32S>(i % ic->spt, i, i, ring, full);
   const unsigned G = gridDim.x;
   // the position advances by one per token (argmax phase), so it is read once
   const int pos0 = __ldcg(&d.ctl->pos);

@@ -320,7 +320,7 @@ struct pb_state {
   size_t mem_bytes = 0;
   // persistent decode kernel: phase table, arrival counter, error word
   Phase* d_phases = nullptr;
-  char* d_sched = nullptr;         // weight-stream schedule: GemvSched [CTA][ngemv], spt [CTA], map [CTA][spt_max]
+  char* d_sched = nullptr;         // weight-stream schedule: GemvSched [CTA][ngemv], spt [CTA], StageDesc [CTA][spt_max]
   int ngemv = 0, spt_max = 0;
   size_t sched_bytes = 0, spt_off = 0, map_off = 0, sched_smem_off = 0;
   int nphase = 0;
@@ -715,7 +715,8 @@ int build_phases(pb_state* s) {
     if (p.kind == PH_GEMV) p.gidx = ngemv++;
   std::vector<GemvSched> sched((size_t)G * ngemv);
   std::vector<int> spt(G, 0);
-  std::vector<std::vector<unsigned short>> smap(G);
+  std::vector<std::vector<StageDesc>> sdesc(G);
+  const size_t q8s = m->sdt == PB_DT_F32 ? 8 : 4;   // bytes per scale pair
   for (int b = 0; b < G; b++) {
     int base = 0;
     for (auto& p : ph) {
@@ -730,14 +731,22 @@ int build_phases(pb_state* s) {
       g.r1 = std::min(rb1 * RB, p.a.N);
       g.base = base;
       g.nch = p.nch;
-      for (int k = rb0; k < rb1; k++) smap[b].push_back((unsigned short)p.gidx);
+      for (int k = rb0; k < rb1; k++) {
+        const int r = k * RB, nr = std::min(RB, p.a.N - r);
+        StageDesc sd;
+        sd.codes16 = (unsigned)(((size_t)(g.codes - m->arena) + (size_t)r * p.nch * 2048) / 16);
+        sd.scales16 = (unsigned)(((size_t)(g.scales - m->arena) + (size_t)r * p.nch * 32 * q8s) / 16);
+        sd.bc = (unsigned)(nr * p.nch * 2048);
+        sd.bs = (unsigned)(nr * p.nch * 32 * q8s);
+        sdesc[b].push_back(sd);
+      }
       base += rb1 - rb0;
     }
     spt[b] = base;
   }
   int spt_max = 1;
   for (int b = 0; b < G; b++) spt_max = std::max(spt_max, spt[b]);
-  if (ngemv > 65535 || spt_max > 16384)
+  if (m->arena_bytes / 16 > 0xffffffffull || ngemv > 65535 || spt_max > 4096)
     return pb_set_error(PB_ENOTSUP, "persistent decode: %d GEMVs, %d stages per token", ngemv, spt_max);
   int dev = 0;
   cudaGetDevice(&dev);
@@ -746,7 +755,7 @@ int build_phases(pb_state* s) {
   const size_t stage = m->sdt == PB_DT_F32 ? DGeo<true>::STAGE : DGeo<false>::STAGE;
   const size_t static_est = 4 * 1024;
   const size_t xb = (size_t)((xr + 1) & ~1) * 4;
-  const size_t tab = (size_t)ngemv * sizeof(GemvSched) + (((size_t)spt_max * 2 + 15) & ~(size_t)15);
+  const size_t tab = (size_t)ngemv * sizeof(GemvSched) + (size_t)spt_max * sizeof(StageDesc);
   long avail = (long)optin - (long)static_est - ISSUE_BYTES - (long)xb - MAX_DS * 8 - 16 - (long)tab;
   int ds = (int)std::min<long>(6, avail / (long)stage);
   if (ds < 2) return pb_set_error(PB_ENOTSUP, "persistent decode: shared memory for %d ring stages", ds);
@@ -762,12 +771,14 @@ int build_phases(pb_state* s) {
     const size_t sb = sched.size() * sizeof(GemvSched);
     s->spt_off = sb;
     const size_t mo = (sb + (size_t)G * 4 + 15) & ~(size_t)15;
-    s->sched_bytes = mo + (size_t)G * spt_max * 2;
+    s->sched_bytes = mo + (size_t)G * spt_max * sizeof(StageDesc);
     std::vector<char> host(s->sched_bytes, 0);
     memcpy(host.data(), sched.data(), sb);
     memcpy(host.data() + sb, spt.data(), (size_t)G * 4);
     for (int b = 0; b < G; b++)
-      if (!smap[b].empty()) memcpy(host.data() + mo + (size_t)b * spt_max * 2, smap[b].data(), smap[b].size() * 2);
+      if (!sdesc[b].empty())
+        memcpy(host.data() + mo + (size_t)b * spt_max * sizeof(StageDesc), sdesc[b].data(),
+               sdesc[b].size() * sizeof(StageDesc));
     if (cudaMalloc(&s->d_sched, s->sched_bytes) != cudaSuccess) {
       cudaGetLastError();
       s->d_sched = nullptr;
@@ -809,11 +820,12 @@ int launch_decode_t(pb_state* s, int ntok, cudaStream_t st) {
   d.pv_per_warp = s->pv_per_warp;
   d.sched = reinterpret_cast<const GemvSched*>(s->d_sched);
   d.spt = reinterpret_cast<const int*>(s->d_sched + s->spt_off);
-  d.smap = reinterpret_cast<const unsigned short*>(s->d_sched + s->map_off);
+  d.sdesc = reinterpret_cast<const StageDesc*>(s->d_sched + s->map_off);
+  d.arena = s->m->arena;
   d.ngemv = s->ngemv;
   d.spt_max = s->spt_max;
   d.sched_off = (int)s->sched_smem_off;
-  d.map_off = (int)(s->sched_smem_off + (size_t)s->ngemv * sizeof(GemvSched));
+  d.desc_off = (int)(s->sched_smem_off + (size_t)s->ngemv * sizeof(GemvSched));
   PB_TRY_CUDA(cudaFuncSetAttribute(k_decode<F32S, E, EH, W>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                    (int)s->dsmem));
   int per_sm = 0;
