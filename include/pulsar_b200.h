@@ -72,6 +72,22 @@ int pb_q80_quantize(const float* d_x, int K, int8_t* d_qx, uint16_t* d_dx, void*
 int pb_q80_gemv(const pb_q8* w, const int8_t* d_qx, const uint16_t* d_dx, float* d_y,
                 int32_t* d_isum, void* stream);
 
+/* The integer path for T positions on the tensor cores (tcgen05.mma
+ * kind::i8, int32 block dots in TMEM): the chunked prefill (T = 32,
+ * pf_gemv_T's role, lfm3_nanode.cu:4840-4968) and batched decode (T = 64)
+ * forms of pb_q80_gemv. pb_q80tc_pack lays a Q8 tensor (fp16 or fp32 block
+ * scales, K % 256 == 0) out for it; pb_q80_gemm takes T in {16, 32, 48, 64}
+ * positions of quantised activations (qx [T][K] int8, dx [T][K/32] fp16, as
+ * pb_q80_quantize writes them for a [T][K] array), writes y [T][N] fp32 and
+ * optionally the exact block dots isum [T][N][K/32]. Per position the values
+ * equal pb_q80_gemv's bit for bit. pb_q80_gemm_status synchronises `stream`
+ * and reports a bounded wait inside the kernel that gave up.               */
+int pb_q80tc_pack(const int8_t* codes, const void* scales, int scale_dtype, int N, int K,
+                  int src_on_device, void* stream, pb_q8** out);
+int pb_q80_gemm(const pb_q8* w, int T, const int8_t* d_qx, const uint16_t* d_dx, float* d_y,
+                int32_t* d_isum, void* stream);
+int pb_q80_gemm_status(void* stream);
+
 /* ------------------------------------------------------------------ Q1 ---- *
  * Q1_0: 18-byte blocks per 128 weights along K, fp16 scale then 16 bytes of
  * LSB-first sign bits, bit 1 => +1 (pq1_wrap.h:24-35).                        */

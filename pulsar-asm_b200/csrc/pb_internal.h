@@ -30,7 +30,9 @@ void pb_set_capturing(bool on);
   } while (0)
 
 // Q8 tensor layouts
-enum { PB_Q8_ROWMAJOR = 0, PB_Q8_STREAM = 1 };
+// PB_Q8_UMMA: 128-row tiles in the tensor cores' K-major core-matrix order,
+// fp32 scales [tile][block][128] (pb_q80tc_pack; only pb_q80_gemm reads it)
+enum { PB_Q8_ROWMAJOR = 0, PB_Q8_STREAM = 1, PB_Q8_UMMA = 2 };
 
 struct pb_q8 {
   int N = 0, K = 0;

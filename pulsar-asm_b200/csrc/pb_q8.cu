@@ -434,6 +434,7 @@ extern "C" int pb_q8_shape(const pb_q8* w, int* N, int* K) {
 
 extern "C" int pb_q8_gemv(const pb_q8* w, const uint16_t* d_x, void* d_y, int y_dtype, void* stream) {
   if (!w || !d_x || !d_y) return pb_set_error(PB_EINVAL, "pb_q8_gemv: null argument");
+  if (w->layout == PB_Q8_UMMA) return pb_set_error(PB_EINVAL, "pb_q8_gemv: tensor packed for pb_q80_gemm");
   if (y_dtype != PB_DT_BF16 && y_dtype != PB_DT_F32) return pb_set_error(PB_EINVAL, "pb_q8_gemv: y dtype");
   if (((uintptr_t)d_x & 15) != 0) return pb_set_error(PB_EINVAL, "pb_q8_gemv: x must be 16-byte aligned");
   return pb_q8_gemv_launch(w, d_x, d_y, y_dtype, (cudaStream_t)stream);
@@ -442,6 +443,7 @@ extern "C" int pb_q8_gemv(const pb_q8* w, const uint16_t* d_x, void* d_y, int y_
 extern "C" int pb_q8_gemm(const pb_q8* w, int T, const uint16_t* d_x, void* d_y, int y_dtype,
                           void* stream) {
   if (!w || !d_x || !d_y || T <= 0) return pb_set_error(PB_EINVAL, "pb_q8_gemm: bad argument");
+  if (w->layout == PB_Q8_UMMA) return pb_set_error(PB_EINVAL, "pb_q8_gemm: tensor packed for pb_q80_gemm");
   if (y_dtype != PB_DT_BF16 && y_dtype != PB_DT_F32) return pb_set_error(PB_EINVAL, "pb_q8_gemm: y dtype");
   cudaStream_t st = (cudaStream_t)stream;
   if (w->layout == PB_Q8_STREAM) {
@@ -470,6 +472,7 @@ extern "C" int pb_q80_quantize(const float* d_x, int K, int8_t* d_qx, uint16_t* 
 extern "C" int pb_q80_gemv(const pb_q8* w, const int8_t* d_qx, const uint16_t* d_dx, float* d_y,
                            int32_t* d_isum, void* stream) {
   if (!w || !d_qx || !d_dx || !d_y) return pb_set_error(PB_EINVAL, "pb_q80_gemv: null argument");
+  if (w->layout == PB_Q8_UMMA) return pb_set_error(PB_EINVAL, "pb_q80_gemv: tensor packed for pb_q80_gemm");
   if (w->layout != PB_Q8_STREAM) return pb_set_error(PB_ENOTSUP, "pb_q80_gemv: needs K %% 2048 == 0 (K=%d)", w->K);
   if (((uintptr_t)d_qx & 15) != 0) return pb_set_error(PB_EINVAL, "pb_q80_gemv: qx must be 16-byte aligned");
   const size_t smem = (size_t)w->K + (size_t)(w->K / 32) * 4 * 9;

@@ -73,6 +73,9 @@ def lib():
     L.pb_q8_gemm.argtypes = [vp, i, vp, vp, i, vp]
     L.pb_q80_quantize.argtypes = [vp, i, vp, vp, vp]
     L.pb_q80_gemv.argtypes = [vp, vp, vp, vp, vp, vp]
+    L.pb_q80tc_pack.argtypes = [vp, vp, i, i, i, i, vp, pvp]
+    L.pb_q80_gemm.argtypes = [vp, i, vp, vp, vp, vp, vp]
+    L.pb_q80_gemm_status.argtypes = [vp]
     L.pb_q1_pack.argtypes = [vp, i, i, i, vp, pvp]
     L.pb_q1_free.argtypes = [vp]
     L.pb_q8k_quantize.argtypes = [vp, i, vp, vp]
@@ -131,9 +134,11 @@ def _stream(stream=None):
 class Q8Tensor:
     """A packed Q8 weight matrix on the device (int8 codes + per-32 scales)."""
 
-    def __init__(self, codes, scales, stream=None):
+    def __init__(self, codes, scales, stream=None, tensor_cores=False):
         """codes: int8 [N, K]; scales: fp16 (Q8_0) or fp32 (.lfm3q8 dtype 1)
-        [N, K/32]; torch CUDA tensors or numpy arrays (host)."""
+        [N, K/32]; torch CUDA tensors or numpy arrays (host). tensor_cores:
+        pack for the integer GEMM on the tensor cores (gemm_int) instead of the
+        streaming GEMV layout."""
         import torch
         L = lib()
         N, K = codes.shape
@@ -149,7 +154,8 @@ class Q8Tensor:
             scales = np.ascontiguousarray(scales)
             cp, sp = codes.ctypes.data_as(C.c_void_p), scales.ctypes.data_as(C.c_void_p)
         h = C.c_void_p()
-        check(L.pb_q8_pack(cp, sp, sdt, N, K, on_dev, _stream(stream), C.byref(h)))
+        pack = L.pb_q80tc_pack if tensor_cores else L.pb_q8_pack
+        check(pack(cp, sp, sdt, N, K, on_dev, _stream(stream), C.byref(h)))
         self.h, self.N, self.K = h, N, K
 
     def gemv(self, x, y, stream=None):
@@ -167,6 +173,15 @@ class Q8Tensor:
     def gemv_int(self, qx, dx, y, isum=None, stream=None):
         check(lib().pb_q80_gemv(self.h, _ptr(qx), _ptr(dx), _ptr(y), _ptr(isum), _stream(stream)))
 
+    def gemm_int(self, qx, dx, y, isum=None, stream=None):
+        """tensor-core integer GEMM: qx int8 [T, K], dx fp16 bits [T, K/32],
+        y fp32 [T, N], isum (optional) int32 [T, N, K/32]"""
+        check(lib().pb_q80_gemm(self.h, qx.shape[0], _ptr(qx), _ptr(dx), _ptr(y), _ptr(isum), _stream(stream)))
+
+    @staticmethod
+    def gemm_int_status(stream=None):
+        check(lib().pb_q80_gemm_status(_stream(stream)))
+
     def __del__(self):
         try:
             if self.h:
@@ -177,7 +192,8 @@ class Q8Tensor:
 
 
 def q80_quantize(x, qx, dx, stream=None):
-    check(lib().pb_q80_quantize(_ptr(x), x.shape[0], _ptr(qx), _ptr(dx), _stream(stream)))
+    """per 32-block Q8_0 quantisation of x (any shape, last dim % 32 == 0)"""
+    check(lib().pb_q80_quantize(_ptr(x), x.numel(), _ptr(qx), _ptr(dx), _stream(stream)))
 
 
 def q8k_quantize(x, xq, stream=None):

@@ -120,6 +120,61 @@ def test_q80_integer_path_cfg0(cuda, oracle, pb):
     assert np.array_equal(_bits(y.cpu().numpy()), _bits(y_o))
 
 
+@pytest.mark.parametrize("N,K,T", [(300, 2048, 16), (300, 2048, 32), (300, 2048, 64), (2048, 8192, 32),
+                                   (16384, 2048, 32), (640, 2048, 48), (128, 256, 64)])
+def test_q80_gemm_tensor_cores(cuda, oracle, pb, N, K, T):
+    """tcgen05 kind::i8 integer GEMM (prefill chunk / batched decode): every
+    position's block dots exact and its fold bit for bit = the oracle's
+    single-position integer path"""
+    torch = cuda
+    rng = np.random.default_rng(N + K + T)
+    codes = rng.integers(-127, 128, (N, K), dtype=np.int8)
+    codes[0, :32] = -128          # the int8 extreme
+    s16 = (np.abs(rng.standard_normal((N, K // 32))) * 0.01).astype(np.float16)
+    x = rng.standard_normal((T, K)).astype(np.float32)
+    x[1, 32:64] = 0               # an all-zero activation block
+    qx = torch.empty((T, K), dtype=torch.int8, device="cuda")
+    dx = torch.empty((T, K // 32), dtype=torch.int16, device="cuda")
+    pb.q80_quantize(_dev(torch, x), qx, dx)
+    w = pb.Q8Tensor(_dev(torch, codes), _dev(torch, s16), tensor_cores=True)
+    y = torch.full((T, N), float("nan"), dtype=torch.float32, device="cuda")
+    isum = torch.empty((T, N, K // 32), dtype=torch.int32, device="cuda")
+    w.gemm_int(qx, dx, y, isum)
+    pb.Q8Tensor.gemm_int_status()
+    yh, ih = y.cpu().numpy(), isum.cpu().numpy()
+    qxh, dxh = qx.cpu().numpy(), dx.cpu().numpy().view(np.uint16)
+    for t in range(T):
+        qo, do = oracle.q80_quant_act(x[t])
+        assert np.array_equal(qxh[t], qo) and np.array_equal(dxh[t], do)
+        io, yo = oracle.q80_gemv(codes, s16.view(np.uint16), qo, do)
+        assert np.array_equal(ih[t], io), "position %d block dots" % t
+        assert np.array_equal(_bits(yh[t]), _bits(yo)), "position %d outputs" % t
+
+
+def test_q80_gemm_tensor_cores_f32_scales(cuda, oracle, pb):
+    """fp32 block scales (.lfm3q8 dtype 1): the fold in numpy float32, block order"""
+    torch = cuda
+    N, K, T = 256, 512, 32
+    rng = np.random.default_rng(5)
+    codes = rng.integers(-127, 128, (N, K), dtype=np.int8)
+    s32 = (np.abs(rng.standard_normal((N, K // 32))) * 0.01).astype(np.float32)
+    x = rng.standard_normal((T, K)).astype(np.float32)
+    qx = torch.empty((T, K), dtype=torch.int8, device="cuda")
+    dx = torch.empty((T, K // 32), dtype=torch.int16, device="cuda")
+    pb.q80_quantize(_dev(torch, x), qx, dx)
+    w = pb.Q8Tensor(_dev(torch, codes), _dev(torch, s32), tensor_cores=True)
+    y = torch.empty((T, N), dtype=torch.float32, device="cuda")
+    w.gemm_int(qx, dx, y)
+    pb.Q8Tensor.gemm_int_status()
+    q = qx.cpu().numpy().astype(np.int32)
+    d = dx.cpu().numpy().view(np.float16).astype(np.float32)
+    isum = np.einsum("nbj,tbj->tnb", codes.reshape(N, K // 32, 32).astype(np.int32), q.reshape(T, K // 32, 32))
+    acc = np.zeros((T, N), np.float32)
+    for b in range(K // 32):
+        acc = acc + (s32[None, :, b] * d[:, None, b]) * isum[:, :, b].astype(np.float32)
+    assert np.array_equal(_bits(y.cpu().numpy()), _bits(acc))
+
+
 def test_q80_golden_quantizer(cuda, oracle, pb):
     torch = cuda
     g = np.load(os.path.join(GOLDEN, "q80_quant.npz"))
