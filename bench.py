@@ -39,6 +39,7 @@ def parse():
     ap.add_argument("--ctx", type=int, default=1024)
     ap.add_argument("--cpu-seconds", type=float, default=15.0)
     ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--no-kernels", action="store_true", help="skip the per-kernel GB/s suite")
     ap.add_argument("--blob", default=os.environ.get("PB_BENCH_BLOB", "/tmp/pb_cfg1.lfm3q8"))
     ap.add_argument("--layers", type=int, default=0,
                     help="profiling only: a shallower model of the same shapes (0 = the 24-layer cfg1)")
@@ -160,6 +161,106 @@ def cpu_baseline(c, weights, ctx, seconds):
             break
     dt = time.time() - t0
     return n / dt, O.lib().pbo_threads(), n, pos
+
+
+def _time_rotating(torch, stream, fns, reps):
+    """mean ms per call of fns (rotating over distinct weight copies whose
+    total exceeds L2), after a warm-up pass, by CUDA events on `stream`"""
+    for f in fns:
+        f()
+    stream.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(reps):
+        for f in fns:
+            f()
+    e1.record(stream)
+    e1.synchronize()
+    return e0.elapsed_time(e1) / (reps * len(fns))
+
+
+def kernel_suite(torch, pb, peak, stream):
+    """the GEMV/GEMM kernels of the other configs, each over rotating copies
+    larger than L2: cfg0 Q8_0 integer GEMV, cfg3 Q1_0 GEMV (gate|up shape),
+    cfg2/cfg4 integer GEMMs on the tensor cores (one layer's projections at
+    T = 32 and T = 64). Bytes are algorithmic (Q8_0 scales 2 B per block,
+    Q1_0 18 B per 128 weights)."""
+    out = {}
+    g = torch.Generator(device="cuda").manual_seed(SEED)
+    L2 = 126 * 2 ** 20
+
+    def q8_dev(N, K):
+        c = torch.randint(-127, 128, (N, K), dtype=torch.int8, device="cuda", generator=g)
+        s = (torch.randn((N, K // 32), device="cuda", generator=g).abs() * 0.01).half()
+        return c, s
+
+    with torch.cuda.stream(stream):
+        # cfg0: W 8192x2048 Q8_0, x quantised per 32-block, y fp32
+        N, K = 8192, 2048
+        nbytes = N * K + N * (K // 32) * 2 + K + (K // 32) * 2 + N * 4
+        ncp = int(2 * L2 // nbytes) + 1
+        ws = []
+        for _ in range(ncp):
+            c, sc = q8_dev(N, K)
+            ws.append(pb.Q8Tensor(c, sc, stream=stream))
+        x = torch.randn(K, device="cuda", generator=g)
+        qx = torch.empty(K, dtype=torch.int8, device="cuda")
+        dx = torch.empty(K // 32, dtype=torch.int16, device="cuda")
+        pb.q80_quantize(x, qx, dx, stream=stream)
+        y = torch.empty(N, dtype=torch.float32, device="cuda")
+        ms = _time_rotating(torch, stream, [lambda w=w: w.gemv_int(qx, dx, y, stream=stream) for w in ws], 20)
+        gbs = nbytes / (ms / 1e3) / 1e9
+        out["cfg0_q80_gemv"] = {"shape": [N, K], "us": ms * 1e3, "bytes": nbytes, "GB/s": gbs,
+                                "frac": gbs / peak, "copies": ncp}
+        del ws
+        # cfg3: Q1_0 gate|up 24576x4096, Q8_K activation, y fp32
+        N, K = 24576, 4096
+        nbytes = N * K // 8 + N * (K // 128) * 2 + (K // 256) * 292 + N * 4
+        ncp = int(2 * L2 // nbytes) + 1
+        q1s = []
+        for _ in range(ncp):
+            blk = torch.randint(0, 256, (N, (K // 128) * 18), dtype=torch.uint8, device="cuda", generator=g)
+            sc = (torch.randn((N, K // 128), device="cuda", generator=g).abs() * 0.02).half()
+            blk.view(N, K // 128, 18)[:, :, :2].copy_(sc.view(torch.uint8).view(N, K // 128, 2))
+            q1s.append(pb.Q1Tensor(blk, N, K, stream=stream))
+        xq = torch.empty((K // 256) * 292, dtype=torch.uint8, device="cuda")
+        pb.q8k_quantize(torch.randn(K, device="cuda", generator=g), xq, stream=stream)
+        y = torch.empty(N, dtype=torch.float32, device="cuda")
+        ms = _time_rotating(torch, stream, [lambda w=w: w.gemv(xq, y, stream=stream) for w in q1s], 20)
+        gbs = nbytes / (ms / 1e3) / 1e9
+        out["cfg3_q1_gemv"] = {"shape": [N, K], "us": ms * 1e3, "bytes": nbytes, "GB/s": gbs,
+                               "frac": gbs / peak, "copies": ncp}
+        del q1s
+        # cfg2 / cfg4: one conv layer's projections as integer GEMMs on the tensor cores
+        shapes = [(6144, 2048), (2048, 2048), (16384, 2048), (2048, 8192)]
+        lay_bytes = sum(n * k + n * (k // 32) * 2 for n, k in shapes)
+        ncp = int(2 * L2 // lay_bytes) + 1
+        layers = [[pb.Q8Tensor(*q8_dev(n, k), stream=stream, tensor_cores=True) for n, k in shapes]
+                  for _ in range(ncp)]
+        for T, key in ((32, "cfg2_q80_gemm_tc_T32"), (64, "cfg4_q80_gemm_tc_T64")):
+            acts = {}
+            for n, k in shapes:
+                if k not in acts:
+                    xa = torch.randn((T, k), device="cuda", generator=g)
+                    qa = torch.empty((T, k), dtype=torch.int8, device="cuda")
+                    da = torch.empty((T, k // 32), dtype=torch.int16, device="cuda")
+                    pb.q80_quantize(xa, qa, da, stream=stream)
+                    acts[k] = (qa, da)
+            ys = {n: torch.empty((T, n), dtype=torch.float32, device="cuda") for n, _ in shapes}
+
+            def layer(ws=None):
+                for w, (n, k) in zip(ws, shapes):
+                    w.gemm_int(acts[k][0], acts[k][1], ys[n], stream=stream)
+            ms = _time_rotating(torch, stream, [lambda ws=ws: layer(ws) for ws in layers], 10)
+            pb.Q8Tensor.gemm_int_status(stream)
+            nbytes = lay_bytes + sum(T * k + T * (k // 32) * 2 + T * n * 4 for n, k in shapes)
+            ops = sum(2 * n * k * T for n, k in shapes)
+            gbs = nbytes / (ms / 1e3) / 1e9
+            out[key] = {"layer_gemms": shapes, "T": T, "us_per_layer": ms * 1e3, "bytes": nbytes,
+                        "GB/s": gbs, "frac": gbs / peak, "int8_TOPS": ops / (ms / 1e3) / 1e12, "copies": ncp}
+        del layers
+    torch.cuda.synchronize()
+    return out
 
 
 def run_reference(args, rank, world):
@@ -298,6 +399,8 @@ def main():
                               else "fallback 6.65 TB/s"}, **rk),
             "step_kernel_gbs": k_bytes / (k_ms / 1000.0) / 1e9,
             "clocks": clk.summary()}
+    if rank == 0 and world == 1 and not args.no_kernels:
+        line["kernels"] = kernel_suite(torch, pb, peak, stream)
     if rank == 0 and world == 1 and not args.no_cpu:
         tps, cores, n, _ = cpu_baseline(c, weights, args.ctx, args.cpu_seconds)
         line["cpu_baseline"] = {"value": tps, "unit": "tok/s", "cores": cores, "kind": "port",

@@ -76,8 +76,8 @@ int pb_q80_gemv(const pb_q8* w, const int8_t* d_qx, const uint16_t* d_dx, float*
  * kind::i8, int32 block dots in TMEM): the chunked prefill (T = 32,
  * pf_gemv_T's role, lfm3_nanode.cu:4840-4968) and batched decode (T = 64)
  * forms of pb_q80_gemv. pb_q80tc_pack lays a Q8 tensor (fp16 or fp32 block
- * scales, K % 256 == 0) out for it; pb_q80_gemm takes T in {16, 32, 48, 64}
- * positions of quantised activations (qx [T][K] int8, dx [T][K/32] fp16, as
+ * scales, K % 256 == 0) out for it; pb_q80_gemm takes T (a multiple of 16,
+ * at most 256) positions of quantised activations (qx [T][K] int8, dx [T][K/32] fp16, as
  * pb_q80_quantize writes them for a [T][K] array), writes y [T][N] fp32 and
  * optionally the exact block dots isum [T][N][K/32]. Per position the values
  * equal pb_q80_gemv's bit for bit. pb_q80_gemm_status synchronises `stream`

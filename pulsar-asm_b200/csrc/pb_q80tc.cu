@@ -9,15 +9,20 @@
 // accumulator (no accumulation across blocks in the tensor core) and the
 // epilogue warps fold the blocks in order in fp32.
 //
-// CTA = 6 warps, one 128-row tile of W:
+// CTA = 6 warps, one 128-row tile of W and 16 of the T positions (grid
+// tiles x T/16; the CTAs of one tile run side by side and share its weights
+// in L2), two CTAs per SM:
 //   warp 0  lane 0: TMA producer, 1-D bulk copies of each stage (8 blocks of
 //                   weights, activations and their scales) into a ring of NS
 //                   shared-memory stages (full/empty mbarriers);
-//   warp 1  lane 0: MMA issuer, one tcgen05.mma per block into one of NB TMEM
-//                   buffers of T columns, tcgen05.commit to the buffer's
-//                   mbarrier; warp 1 also allocates and frees the TMEM;
-//   warps 2-5:      epilogue, TMEM lane quarter (warp % 4): tcgen05.ld of the
-//                   block's int32 tile, release of the buffer, fp32 fold.
+//   warp 1  lane 0: MMA issuer, one tcgen05.mma (M 128, N 16, K 32) per block
+//                   into one of NB TMEM buffers of 16 columns, tcgen05.commit
+//                   to the buffer's mbarrier; warp 1 also allocates and frees
+//                   the TMEM;
+//   warps 2-5:      epilogue, TMEM lane quarter warp % 4: tcgen05.ld of BK
+//                   blocks' int32 tiles at a time, release of the buffers,
+//                   fp32 fold in block order (int32 -> fp32 by the exact
+//                   2^23 + 2^22 exponent trick: |isum| < 2^22).
 // Operands sit in shared memory in the canonical K-major no-swizzle layout:
 // 8-row x 16-byte core matrices, the two 16-byte halves of a block 128 bytes
 // apart (leading byte offset), 8-row groups 256 bytes apart (stride byte
@@ -35,8 +40,6 @@ namespace {
 
 constexpr int TC_M = 128;            // rows per tile (MMA M)
 constexpr int TC_CB = 8;             // 32-code blocks per stage
-constexpr int TC_NSMAX = 4;
-constexpr int TC_NBMAX = 16;
 constexpr unsigned TC_WAIT = 1u << 24;
 
 struct TcArgs {
@@ -100,91 +103,90 @@ PB_DEV void tc_mma_i8(uint32_t dtmem, uint64_t adesc, uint64_t bdesc, uint32_t i
       ::"r"(dtmem), "l"(adesc), "l"(bdesc), "r"(idesc), "r"(z), "r"(z), "r"(z), "r"(z), "r"(z)
       : "memory");
 }
-// 16 consecutive int32 columns of this thread's TMEM lane
-PB_DEV void tc_ld16(uint32_t taddr, int32_t* v) {
-  asm volatile(
-      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, "
-      "%14, %15}, [%16];"
-      : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7]),
-        "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]), "=r"(v[15])
-      : "r"(taddr));
+// 8 consecutive int32 columns of this thread's TMEM lane
+PB_DEV void tc_ld8(uint32_t taddr, int32_t* v) {
+  asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0, %1, %2, %3, %4, %5, %6, %7}, [%8];"
+               : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7])
+               : "r"(taddr));
 }
 PB_DEV void tc_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 
-template <int T>
-struct TcGeo {
-  static constexpr int NB = (512 / T) < TC_NBMAX ? (512 / T) : TC_NBMAX;   // TMEM buffers
-  static constexpr int SA = TC_M * 32 * TC_CB;       // weights of a stage
-  static constexpr int SB = T * 32 * TC_CB;          // activations
-  static constexpr int SW = TC_CB * TC_M * 4;        // weight scales
-  static constexpr int SX = TC_CB * T * 4;           // activation scales
-  static constexpr int STAGE = SA + SB + SW + SX;
-};
+constexpr int TC_TS = 16;            // positions per CTA (MMA N)
+constexpr int TC_NB = 16;            // TMEM buffers of 16 columns
+constexpr int TC_BK = 4;             // blocks per epilogue step
+constexpr int TC_SA = TC_M * 32 * TC_CB;       // weights of a stage
+constexpr int TC_SB = TC_TS * 32 * TC_CB;      // activations
+constexpr int TC_SW = TC_CB * TC_M * 4;        // weight scales
+constexpr int TC_SX = TC_CB * TC_TS * 4;       // activation scales
+constexpr int TC_STAGE = TC_SA + TC_SB + TC_SW + TC_SX;
+constexpr int TC_NS = 2;
 
-template <int T>
-__global__ void __launch_bounds__(192, 1) k_q80tc(TcArgs p) {
-  typedef TcGeo<T> Gm;
-  static_assert(T % 16 == 0 && T >= 16 && T <= 64, "T");
+PB_DEV float i2f_exact(int32_t v) { return __fsub_rn(__int_as_float(v + 0x4B400000), 12582912.0f); }
+
+__global__ void __launch_bounds__(192, 2) k_q80tc(TcArgs p) {
   extern __shared__ __align__(1024) unsigned char tsm[];
-  __shared__ uint64_t full[TC_NSMAX], empty[TC_NSMAX], tfull[TC_NBMAX], tempty[TC_NBMAX], done;
+  __shared__ uint64_t full[TC_NS], empty[TC_NS], tfull[TC_NB], tempty[TC_NB], done;
   __shared__ uint32_t tbase;
   __shared__ int abort_f;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int nblk = p.K / 32, nst = nblk / TC_CB, ns = p.ns, tile = blockIdx.x;
+  const int nblk = p.K / 32, nst = nblk / TC_CB, tile = blockIdx.x, ts = blockIdx.y;
   if (threadIdx.x == 0) {
-    for (int i = 0; i < ns; i++) { mb_init(&full[i], 1); mb_init(&empty[i], 1 + 4); }
-    for (int i = 0; i < Gm::NB; i++) { mb_init(&tfull[i], 1); mb_init(&tempty[i], 4); }
+    for (int i = 0; i < TC_NS; i++) { mb_init(&full[i], 1); mb_init(&empty[i], 1 + 4); }
+    for (int i = 0; i < TC_NB; i++) { mb_init(&tfull[i], 1); mb_init(&tempty[i], 4); }
     mb_init(&done, 1);
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     abort_f = 0;
   }
   if (warp == 1) {
-    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], 512;" ::"r"(s32(&tbase)));
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], 256;" ::"r"(s32(&tbase)));
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
   }
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = tbase;
+  const int8_t* bsrc = p.b + (size_t)ts * nblk * (TC_TS * 32);
+  const float* xsrc = p.dx + (size_t)ts * nblk * TC_TS;
 
   if (warp == 0) {
     if (lane == 0) {
       int issued = 0;
       for (int s = 0; s < nst; s++) {
-        const int slot = s % ns;
-        if (s >= ns && !mb_wait(&empty[slot], (unsigned)((s / ns) - 1) & 1u, &abort_f)) {
+        const int slot = s % TC_NS;
+        if (s >= TC_NS && !mb_wait(&empty[slot], (unsigned)((s / TC_NS) - 1) & 1u, &abort_f)) {
           abort_f = 1;
           atomicCAS(p.err, 0, 1);
           break;
         }
-        unsigned char* st = tsm + (size_t)slot * Gm::STAGE;
-        mb_expect(&full[slot], Gm::STAGE);
-        bulk(st, p.a + ((size_t)tile * nblk + (size_t)s * TC_CB) * 4096, Gm::SA, &full[slot]);
-        bulk(st + Gm::SA, p.b + (size_t)s * Gm::SB, Gm::SB, &full[slot]);
-        bulk(st + Gm::SA + Gm::SB, p.dw + ((size_t)tile * nblk + (size_t)s * TC_CB) * TC_M, Gm::SW, &full[slot]);
-        bulk(st + Gm::SA + Gm::SB + Gm::SW, p.dx + (size_t)s * TC_CB * T, Gm::SX, &full[slot]);
+        unsigned char* st = tsm + (size_t)slot * TC_STAGE;
+        mb_expect(&full[slot], TC_STAGE);
+        bulk(st, p.a + ((size_t)tile * nblk + (size_t)s * TC_CB) * 4096, TC_SA, &full[slot]);
+        bulk(st + TC_SA, bsrc + (size_t)s * TC_SB, TC_SB, &full[slot]);
+        bulk(st + TC_SA + TC_SB, p.dw + ((size_t)tile * nblk + (size_t)s * TC_CB) * TC_M, TC_SW, &full[slot]);
+        bulk(st + TC_SA + TC_SB + TC_SW, xsrc + (size_t)s * TC_CB * TC_TS, TC_SX, &full[slot]);
         issued = s + 1;
       }
       // no copy may land after the CTA exits: each slot's last issued stage (bounded)
-      for (int s = issued > ns ? issued - ns : 0; s < issued; s++) {
+      for (int s = issued > TC_NS ? issued - TC_NS : 0; s < issued; s++) {
         unsigned n = 0;
-        while (!mb_try(&full[s % ns], (unsigned)(s / ns) & 1u) && n < TC_WAIT) { n++; if (n > 64) __nanosleep(32); }
+        while (!mb_try(&full[s % TC_NS], (unsigned)(s / TC_NS) & 1u) && n < TC_WAIT) { n++; if (n > 64) __nanosleep(32); }
       }
     }
   } else if (warp == 1) {
     if (lane == 0) {
       // kind::i8: D s32 (bits 4-5 = 2), A and B signed (bits 7-9, 10-12 = 1),
-      // both K-major, N = T (bits 17-22 = T/8), M = 128 (bits 24-28 = 128/16)
-      const uint32_t idesc = (2u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(T >> 3) << 17) | ((uint32_t)(TC_M >> 4) << 24);
+      // both K-major, N = 16 (bits 17-22 = 16/8), M = 128 (bits 24-28 = 128/16)
+      const uint32_t idesc = (2u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(TC_TS >> 3) << 17) |
+                             ((uint32_t)(TC_M >> 4) << 24);
       int b = 0;
       for (; b < nblk; b++) {
-        const int s = b / TC_CB, j = b % TC_CB, slot = s % ns, nb = b % Gm::NB;
-        if (j == 0 && !mb_wait(&full[slot], (unsigned)(s / ns) & 1u, &abort_f)) break;
-        if (b >= Gm::NB && !mb_wait(&tempty[nb], (unsigned)((b / Gm::NB) - 1) & 1u, &abort_f)) break;
+        const int s = b / TC_CB, j = b % TC_CB, slot = s % TC_NS, nb = b % TC_NB;
+        if (j == 0 && !mb_wait(&full[slot], (unsigned)(s / TC_NS) & 1u, &abort_f)) break;
+        if (b >= TC_NB && !mb_wait(&tempty[nb], (unsigned)((b / TC_NB) - 1) & 1u, &abort_f)) break;
         tc_fence_after();
-        const uint32_t sa = s32(tsm + (size_t)slot * Gm::STAGE) + j * (TC_M * 32);
-        const uint32_t sb = s32(tsm + (size_t)slot * Gm::STAGE + Gm::SA) + j * (T * 32);
-        tc_mma_i8(tmem + (uint32_t)(nb * T), umma_desc(sa), umma_desc(sb), idesc);
+        const uint32_t sa = s32(tsm + (size_t)slot * TC_STAGE) + j * (TC_M * 32);
+        const uint32_t sb = s32(tsm + (size_t)slot * TC_STAGE + TC_SA) + j * (TC_TS * 32);
+        tc_mma_i8(tmem + (uint32_t)(nb * TC_TS), umma_desc(sa), umma_desc(sb), idesc);
         tc_commit(&tfull[nb]);
         if (j == TC_CB - 1) tc_commit(&empty[slot]);
       }
@@ -199,53 +201,70 @@ __global__ void __launch_bounds__(192, 1) k_q80tc(TcArgs p) {
     const int rloc = q * 32 + lane;
     const int n = tile * TC_M + rloc;
     const uint32_t tq = tmem + ((uint32_t)(q * 32) << 16);
-    float acc[T];
+    float acc[TC_TS];
 #pragma unroll
-    for (int t = 0; t < T; t++) acc[t] = 0.0f;
-    int b = 0;
-    for (; b < nblk; b++) {
-      const int s = b / TC_CB, j = b % TC_CB, slot = s % ns, nb = b % Gm::NB;
-      // the stage's scales: visible once its copies completed
-      if (j == 0 && !mb_wait(&full[slot], (unsigned)(s / ns) & 1u, &abort_f)) break;
-      if (!mb_wait(&tfull[nb], (unsigned)(b / Gm::NB) & 1u, &abort_f)) break;
+    for (int t = 0; t < TC_TS; t++) acc[t] = 0.0f;
+    int b0 = 0;
+    bool ok = true;
+    for (; b0 < nblk && ok; b0 += TC_BK) {
+      // TC_BK blocks per step: one wait for all their TMEM loads
+#pragma unroll
+      for (int k = 0; k < TC_BK; k++) {
+        const int b = b0 + k, s = b / TC_CB, j = b % TC_CB, slot = s % TC_NS;
+        // the stage's scales are visible once its copies completed
+        if (j == 0 && !mb_wait(&full[slot], (unsigned)(s / TC_NS) & 1u, &abort_f)) { ok = false; break; }
+        if (!mb_wait(&tfull[b % TC_NB], (unsigned)(b / TC_NB) & 1u, &abort_f)) { ok = false; break; }
+      }
+      if (!ok) break;
       tc_fence_after();
-      const unsigned char* st = tsm + (size_t)slot * Gm::STAGE;
-      const float dwv = reinterpret_cast<const float*>(st + Gm::SA + Gm::SB)[j * TC_M + rloc];
-      const float* dxs = reinterpret_cast<const float*>(st + Gm::SA + Gm::SB + Gm::SW) + j * T;
-      // 16 columns at a time: load, fold in order, next
+      int32_t v[TC_BK][TC_TS];
 #pragma unroll
-      for (int c = 0; c < T / 16; c++) {
-        int32_t v[16];
-        tc_ld16(tq + (uint32_t)(nb * T + 16 * c), v);
-        tc_wait_ld();
-        if (c == T / 16 - 1) {
-          tc_fence_before();
-          __syncwarp();
-          if (lane == 0) mb_arrive(&tempty[nb]);
+      for (int k = 0; k < TC_BK; k++) {
+        const int nb = (b0 + k) % TC_NB;
+        tc_ld8(tq + (uint32_t)(nb * TC_TS), &v[k][0]);
+        tc_ld8(tq + (uint32_t)(nb * TC_TS + 8), &v[k][8]);
+      }
+      tc_wait_ld();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0)
+        for (int k = 0; k < TC_BK; k++) mb_arrive(&tempty[(b0 + k) % TC_NB]);
+#pragma unroll
+      for (int k = 0; k < TC_BK; k++) {
+        const int b = b0 + k, s = b / TC_CB, j = b % TC_CB, slot = s % TC_NS;
+        const unsigned char* st = tsm + (size_t)slot * TC_STAGE;
+        const float dwv = reinterpret_cast<const float*>(st + TC_SA + TC_SB)[j * TC_M + rloc];
+        const float4* dx4 = reinterpret_cast<const float4*>(st + TC_SA + TC_SB + TC_SW) + j * (TC_TS / 4);
+#pragma unroll
+        for (int t4 = 0; t4 < TC_TS / 4; t4++) {
+          const float4 d = dx4[t4];
+          const float dd[4] = {d.x, d.y, d.z, d.w};
+#pragma unroll
+          for (int u = 0; u < 4; u++) {
+            const int t = 4 * t4 + u;
+            acc[t] = __fadd_rn(acc[t], __fmul_rn(__fmul_rn(dwv, dd[u]), i2f_exact(v[k][t])));
+          }
         }
-#pragma unroll
-        for (int i = 0; i < 16; i++)
-          acc[16 * c + i] = __fadd_rn(acc[16 * c + i], __fmul_rn(__fmul_rn(dwv, dxs[16 * c + i]), __int2float_rn(v[i])));
         if (p.isum && n < p.N) {
 #pragma unroll
-          for (int i = 0; i < 16; i++) p.isum[((size_t)(16 * c + i) * p.N + n) * nblk + b] = v[i];
+          for (int t = 0; t < TC_TS; t++) p.isum[((size_t)(ts * TC_TS + t) * p.N + n) * nblk + b] = v[k][t];
+        }
+        if (j == TC_CB - 1) {
+          __syncwarp();
+          if (lane == 0) mb_arrive(&empty[slot]);
         }
       }
-      if (j == TC_CB - 1) {
-        __syncwarp();
-        if (lane == 0) mb_arrive(&empty[slot]);
-      }
     }
-    if (b < nblk) { abort_f = 1; atomicCAS(p.err, 0, 3); }
+    if (b0 < nblk) { abort_f = 1; atomicCAS(p.err, 0, 3); }
     if (n < p.N) {
 #pragma unroll
-      for (int t = 0; t < T; t++) p.y[(size_t)t * p.N + n] = acc[t];
+      for (int t = 0; t < TC_TS; t++) p.y[(size_t)(ts * TC_TS + t) * p.N + n] = acc[t];
     }
   }
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
-  if (warp == 1) asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, 512;" ::"r"(tmem));
+  if (warp == 1) asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, 256;" ::"r"(tmem));
 }
 
 // row-major codes/scales -> tiles of 128 rows in the K-major core-matrix
@@ -278,30 +297,26 @@ __global__ void k_q80tc_pack(const int8_t* __restrict__ codes, const S* __restri
   }
 }
 
-// activations [T][K] int8 + fp16 scales [T][K/32] -> the kernel's layout
+// activations [T][K] int8 + fp16 scales [T][K/32] -> the kernel's layout:
+// per 16 positions, per block, 2 groups of 8 positions x 2 halves x 16 bytes
 __global__ void k_q80tc_act(const int8_t* __restrict__ qx, const uint16_t* __restrict__ dxh, int T, int K,
                             int8_t* __restrict__ bq, float* __restrict__ dx) {
   const int nblk = K / 32;
   const int total = nblk * T * 2;
   for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < total; i += gridDim.x * blockDim.x) {
     const int kh = i & 1, t = (i >> 1) % T, b = (i >> 1) / T;
+    const int ts = t / TC_TS, tl = t % TC_TS;
+    const size_t blk = (size_t)ts * nblk + b;
     const uint4 v = *reinterpret_cast<const uint4*>(qx + (size_t)t * K + b * 32 + kh * 16);
-    *reinterpret_cast<uint4*>(bq + (size_t)b * T * 32 + (t >> 3) * 256 + kh * 128 + (t & 7) * 16) = v;
-    if (kh == 0) dx[(size_t)b * T + t] = pb_h2f(dxh[(size_t)t * nblk + b]);
+    *reinterpret_cast<uint4*>(bq + blk * (TC_TS * 32) + (tl >> 3) * 256 + kh * 128 + (tl & 7) * 16) = v;
+    if (kh == 0) dx[blk * TC_TS + tl] = pb_h2f(dxh[(size_t)t * nblk + b]);
   }
 }
 
-template <int T>
-int launch_tc(const pb_q8* w, const int8_t* bq, const float* dx, float* y, int32_t* isum, int* err,
+int launch_tc(const pb_q8* w, int T, const int8_t* bq, const float* dx, float* y, int32_t* isum, int* err,
               cudaStream_t st) {
-  typedef TcGeo<T> Gm;
-  int dev = 0, optin = 0;
-  cudaGetDevice(&dev);
-  cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
-  const int ns = std::min(TC_NSMAX, (optin - 2048) / Gm::STAGE);
-  if (ns < 2) return pb_set_error(PB_ENOTSUP, "pb_q80_gemm: shared memory");
-  const size_t smem = (size_t)ns * Gm::STAGE;
-  PB_TRY_CUDA(cudaFuncSetAttribute(k_q80tc<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+  const size_t smem = (size_t)TC_NS * TC_STAGE;
+  PB_TRY_CUDA(cudaFuncSetAttribute(k_q80tc, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
   TcArgs a;
   a.a = w->codes;
   a.dw = reinterpret_cast<const float*>(w->scales);
@@ -311,10 +326,10 @@ int launch_tc(const pb_q8* w, const int8_t* bq, const float* dx, float* y, int32
   a.isum = isum;
   a.N = w->N;
   a.K = w->K;
-  a.ns = ns;
+  a.ns = TC_NS;
   a.err = err;
   const int ntile = (w->N + TC_M - 1) / TC_M;
-  k_q80tc<T><<<ntile, 192, smem, st>>>(a);
+  k_q80tc<<<dim3(ntile, T / TC_TS), 192, smem, st>>>(a);
   PB_LAUNCHED("k_q80tc");
   return PB_OK;
 }
@@ -385,8 +400,8 @@ extern "C" int pb_q80_gemm(const pb_q8* w, int T, const int8_t* d_qx, const uint
                            int32_t* d_isum, void* stream) {
   if (!w || !d_qx || !d_dx || !d_y) return pb_set_error(PB_EINVAL, "pb_q80_gemm: null argument");
   if (w->layout != PB_Q8_UMMA) return pb_set_error(PB_EINVAL, "pb_q80_gemm: tensor not packed by pb_q80tc_pack");
-  if (T != 16 && T != 32 && T != 48 && T != 64)
-    return pb_set_error(PB_ENOTSUP, "pb_q80_gemm: T=%d (16, 32, 48 or 64)", T);
+  if (T <= 0 || T % TC_TS || T > 256)
+    return pb_set_error(PB_ENOTSUP, "pb_q80_gemm: T=%d (a multiple of 16 up to 256)", T);
   if (((uintptr_t)d_qx & 15) != 0) return pb_set_error(PB_EINVAL, "pb_q80_gemm: qx must be 16-byte aligned");
   cudaStream_t st = (cudaStream_t)stream;
   int dev = 0;
@@ -414,13 +429,7 @@ extern "C" int pb_q80_gemm(const pb_q8* w, int T, const int8_t* d_qx, const uint
   const int units = nblk * T * 2;
   k_q80tc_act<<<(units + 255) / 256, 256, 0, st>>>(d_qx, d_dx, T, w->K, bq, dx);
   PB_LAUNCHED("k_q80tc_act");
-  int rc = PB_OK;
-  switch (T) {
-    case 16: rc = launch_tc<16>(w, bq, dx, d_y, d_isum, err, st); break;
-    case 32: rc = launch_tc<32>(w, bq, dx, d_y, d_isum, err, st); break;
-    case 48: rc = launch_tc<48>(w, bq, dx, d_y, d_isum, err, st); break;
-    default: rc = launch_tc<64>(w, bq, dx, d_y, d_isum, err, st); break;
-  }
+  int rc = launch_tc(w, T, bq, dx, d_y, d_isum, err, st);
   return rc;
 }
 

@@ -121,7 +121,7 @@ def test_q80_integer_path_cfg0(cuda, oracle, pb):
 
 
 @pytest.mark.parametrize("N,K,T", [(300, 2048, 16), (300, 2048, 32), (300, 2048, 64), (2048, 8192, 32),
-                                   (16384, 2048, 32), (640, 2048, 48), (128, 256, 64)])
+                                   (16384, 2048, 32), (640, 2048, 48), (128, 256, 64), (200, 512, 128)])
 def test_q80_gemm_tensor_cores(cuda, oracle, pb, N, K, T):
     """tcgen05 kind::i8 integer GEMM (prefill chunk / batched decode): every
     position's block dots exact and its fold bit for bit = the oracle's
