@@ -104,60 +104,98 @@ __global__ void __launch_bounds__(256) k_q8k_quantize(const float* __restrict__ 
 // 528 bytes per group (512 + 16 of padding so that lanes on consecutive
 // groups hit distinct banks).
 #define PB_Q1_GSTRIDE 528
+constexpr int Q1_R = 4;   // rows per warp batch
 __global__ void __launch_bounds__(256)
 k_q1_gemv(const uint4* __restrict__ bits, const uint16_t* __restrict__ wsc,
           const uint8_t* __restrict__ xq, float* __restrict__ y, int32_t* __restrict__ isum,
           int rows, int K) {
   extern __shared__ __align__(16) unsigned char smem[];
-  const int ng = K / 128;
+  const int ng = K / 128, nbk = K / 256, ps = ng + 1;
   unsigned char* act = smem;                                         // ng * 528
   int* asum = reinterpret_cast<int*>(smem + (size_t)ng * PB_Q1_GSTRIDE);   // ng
   float* dbs = reinterpret_cast<float*>(asum + ng);                 // ng (db per group)
-  float* prod = dbs + ng;                                           // 8 warps x ng
-  // stage: thread per (group, word-of-32, k)
+  float* prod = dbs + ng;                                           // 8 warps x Q1_R x (ng + 1)
+  unsigned char* raw = reinterpret_cast<unsigned char*>(prod + (size_t)8 * Q1_R * ps);   // nbk * 292
+  // the Q8_K activation into shared memory once (coalesced words), then
+  // permuted from there
+  for (int i = threadIdx.x; i < nbk * 73; i += blockDim.x)
+    reinterpret_cast<uint32_t*>(raw)[i] = reinterpret_cast<const uint32_t*>(xq)[i];
+  __syncthreads();
+  // thread per (group, word-of-32, k): words (q_k, q_k+8, q_k+16, q_k+24)
   for (int i = threadIdx.x; i < ng * 32; i += blockDim.x) {
     const int g = i >> 5, j = (i >> 3) & 3, k = i & 7;
-    const int8_t* qs = reinterpret_cast<const int8_t*>(xq + (size_t)(g >> 1) * 292 + 4 + (g & 1) * 128 + j * 32);
-    const uint32_t w = (uint32_t)(uint8_t)qs[k] | ((uint32_t)(uint8_t)qs[k + 8] << 8) |
-                       ((uint32_t)(uint8_t)qs[k + 16] << 16) | ((uint32_t)(uint8_t)qs[k + 24] << 24);
+    const unsigned char* qs = raw + (size_t)(g >> 1) * 292 + 4 + (g & 1) * 128 + j * 32;
+    const uint32_t w = (uint32_t)qs[k] | ((uint32_t)qs[k + 8] << 8) | ((uint32_t)qs[k + 16] << 16) |
+                       ((uint32_t)qs[k + 24] << 24);
     reinterpret_cast<uint32_t*>(act + (size_t)g * PB_Q1_GSTRIDE)[j * 8 + k] = w;
   }
-  for (int g = threadIdx.x; g < ng; g += blockDim.x) {
-    const int8_t* qs = reinterpret_cast<const int8_t*>(xq + (size_t)(g >> 1) * 292 + 4 + (g & 1) * 128);
-    int s = 0;
-    for (int i = 0; i < 128; i++) s += qs[i];
-    asum[g] = s;
-    float db;
-    memcpy(&db, xq + (size_t)(g >> 1) * 292, 4);
-    dbs[g] = db;
+  // A_g: the group's activation sum, 8 lanes per group (dp4a over 16 bytes each)
+  // (the loop bound is a multiple of 32: whole warps take part in the shuffles)
+  for (int i = threadIdx.x; i < ((ng * 8 + 31) & ~31); i += blockDim.x) {
+    const int g = i >> 3, part = i & 7;
+    const bool valid = g < ng;
+    const unsigned char* qs = raw + (size_t)(valid ? g >> 1 : 0) * 292 + 4 + (g & 1) * 128 + part * 16;
+    int sum = 0;
+#pragma unroll
+    for (int k = 0; valid && k < 4; k++) {
+      const uint32_t w = (uint32_t)qs[4 * k] | ((uint32_t)qs[4 * k + 1] << 8) | ((uint32_t)qs[4 * k + 2] << 16) |
+                         ((uint32_t)qs[4 * k + 3] << 24);
+      sum = __dp4a((int)w, 0x01010101, sum);
+    }
+    sum += __shfl_xor_sync(0xffffffffu, sum, 1);
+    sum += __shfl_xor_sync(0xffffffffu, sum, 2);
+    sum += __shfl_xor_sync(0xffffffffu, sum, 4);
+    if (valid && part == 0) {
+      asum[g] = sum;
+      float db;
+      memcpy(&db, raw + (size_t)(g >> 1) * 292, 4);
+      dbs[g] = db;
+    }
   }
   __syncthreads();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  float* pw = prod + warp * ng;
-  for (int row = blockIdx.x * 8 + warp; row < rows; row += gridDim.x * 8) {
+  float* pw = prod + (size_t)warp * Q1_R * ps;
+  for (int row0 = (blockIdx.x * 8 + warp) * Q1_R; row0 < rows; row0 += gridDim.x * 8 * Q1_R) {
     for (int g = lane; g < ng; g += 32) {
-      const uint4 wv = pb_ldg_stream(bits + (size_t)row * ng + g);
-      const unsigned short hs = wsc[(size_t)row * ng + g];
+      uint4 wv[Q1_R];
+      unsigned short hs[Q1_R];
+#pragma unroll
+      for (int r = 0; r < Q1_R; r++) {
+        const int row = min(row0 + r, rows - 1);
+        wv[r] = pb_ldg_stream(bits + (size_t)row * ng + g);
+        hs[r] = wsc[(size_t)row * ng + g];
+      }
       const uint4* av = reinterpret_cast<const uint4*>(act + (size_t)g * PB_Q1_GSTRIDE);
-      const unsigned ws[4] = {wv.x, wv.y, wv.z, wv.w};
-      int P = 0;
+      int P[Q1_R];
+#pragma unroll
+      for (int r = 0; r < Q1_R; r++) P[r] = 0;
 #pragma unroll
       for (int j = 0; j < 4; j++) {
         const uint4 a0 = av[2 * j], a1 = av[2 * j + 1];
         const unsigned aw[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
 #pragma unroll
-        for (int k = 0; k < 8; k++) P = __dp4a((int)((ws[j] >> k) & 0x01010101u), (int)aw[k], P);
+        for (int r = 0; r < Q1_R; r++) {
+          const unsigned ws = j == 0 ? wv[r].x : j == 1 ? wv[r].y : j == 2 ? wv[r].z : wv[r].w;
+#pragma unroll
+          for (int k = 0; k < 8; k++) P[r] = __dp4a((int)((ws >> k) & 0x01010101u), (int)aw[k], P[r]);
+        }
       }
-      const int s = 2 * P - asum[g];
-      if (isum) isum[(size_t)row * ng + g] = s;
-      const float wsf = hs == 0x8000u ? 0.0f : pb_h2f(hs);
-      pw[g] = __fmul_rn(__fmul_rn(wsf, dbs[g]), __int2float_rn(s));
+      const int ag = asum[g];
+      const float dbg = dbs[g];
+#pragma unroll
+      for (int r = 0; r < Q1_R; r++) {
+        const int s = 2 * P[r] - ag;
+        if (isum && row0 + r < rows) isum[(size_t)(row0 + r) * ng + g] = s;
+        const float wsf = hs[r] == 0x8000u ? 0.0f : pb_h2f(hs[r]);
+        pw[r * ps + g] = __fmul_rn(__fmul_rn(wsf, dbg), __int2float_rn(s));
+      }
     }
     __syncwarp();
-    if (lane == 0) {
+    if (lane < Q1_R && row0 + lane < rows) {
+      const float* pr = pw + lane * ps;
       float acc = 0.0f;
-      for (int g = 0; g < ng; g++) acc = __fadd_rn(acc, pw[g]);
-      y[row] = acc;
+      for (int g = 0; g < ng; g++) acc = __fadd_rn(acc, pr[g]);
+      y[row0 + lane] = acc;
     }
     __syncwarp();
   }
@@ -165,7 +203,8 @@ k_q1_gemv(const uint4* __restrict__ bits, const uint16_t* __restrict__ wsc,
 
 static size_t q1_smem(int K) {
   const int ng = K / 128;
-  return (size_t)ng * PB_Q1_GSTRIDE + (size_t)ng * 4 * 2 + (size_t)8 * ng * 4;
+  return (size_t)ng * PB_Q1_GSTRIDE + (size_t)ng * 4 * 2 + (size_t)8 * Q1_R * (ng + 1) * 4 +
+         (size_t)(K / 256) * 292;
 }
 
 static int q1_gemv_launch(const pb_q1* w, const uint8_t* d_xq, float* d_y, int32_t* d_isum,
@@ -177,8 +216,8 @@ static int q1_gemv_launch(const pb_q1* w, const uint8_t* d_xq, float* d_y, int32
     cudaFuncSetAttribute(k_q1_gemv, cudaFuncAttributeMaxDynamicSharedMemorySize, 220 * 1024);
     attr = true;
   }
-  int grid = 2 * pb_num_sms();
-  if (grid * 8 > w->rows) grid = (w->rows + 7) / 8;
+  int grid = 4 * pb_num_sms();
+  if (grid * 8 * Q1_R > w->rows) grid = (w->rows + 8 * Q1_R - 1) / (8 * Q1_R);
   k_q1_gemv<<<grid, 256, smem, st>>>(reinterpret_cast<const uint4*>(w->bits), w->scales, d_xq,
                                     d_y, d_isum, w->rows, w->K);
   PB_LAUNCHED("k_q1_gemv");

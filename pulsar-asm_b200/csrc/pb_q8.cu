@@ -241,56 +241,66 @@ __global__ void k_q80_quantize(const float* __restrict__ x, int K, int8_t* __res
   if (lane == 0) dx[b] = pb_f2h(d);
 }
 
-// Streaming layout; one warp per row (all chunks). Lane l owns blocks l and
-// l+32 of each chunk: exact int32 block dots by dp4a, products
-// (dw*dx)*(float)isum into a per-warp row buffer, then lane 0 folds the row in
-// block order (no contraction), the reference's serial accumulation.
+// Streaming layout. A warp takes Q80_R consecutive rows at a time: lane l
+// owns blocks l and l+32 of each 2048-code chunk of every row, forms their
+// exact int32 dots by dp4a and the products (dw*dx)*(float)isum into a
+// shared row buffer (all rows' loads in flight together); then lane r folds
+// row r in block order (no contraction), the reference's serial accumulation.
+constexpr int Q80_R = 4;
 template <bool F32S>
 __global__ void __launch_bounds__(256)
 k_q80_stream(const uint4* __restrict__ codes, const void* __restrict__ scales,
              const int8_t* __restrict__ qx, const unsigned short* __restrict__ dx,
              float* __restrict__ y, int32_t* __restrict__ isum, int N, int K) {
   extern __shared__ __align__(16) unsigned char smem[];
-  const int nch = K / 2048, nb = K / 32;
+  const int nch = K / 2048, nb = K / 32, ps = nb + 1;
   int8_t* sq = reinterpret_cast<int8_t*>(smem);                       // K bytes
   float* sdx = reinterpret_cast<float*>(smem + K);                    // nb floats
-  float* prod = sdx + nb;                                             // 8 warps x nb
+  float* prod = sdx + nb;                                             // 8 warps x Q80_R x (nb + 1)
   for (int i = threadIdx.x; i < K / 16; i += blockDim.x)
     reinterpret_cast<uint4*>(sq)[i] = reinterpret_cast<const uint4*>(qx)[i];
   for (int i = threadIdx.x; i < nb; i += blockDim.x) sdx[i] = pb_h2f(dx[i]);
   __syncthreads();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  float* pw = prod + warp * nb;
-  for (int row = blockIdx.x * 8 + warp; row < N; row += gridDim.x * 8) {
+  float* pw = prod + (size_t)warp * Q80_R * ps;
+  for (int row0 = (blockIdx.x * 8 + warp) * Q80_R; row0 < N; row0 += gridDim.x * 8 * Q80_R) {
     for (int c = 0; c < nch; c++) {
-      const size_t seg = (size_t)row * nch + c;
-      const uint4* base = codes + seg * 128 + lane;
-      uint4 q[4];
+      uint4 q[Q80_R][4];
+      float slo[Q80_R], shi[Q80_R];
 #pragma unroll
-      for (int h = 0; h < 4; h++) q[h] = pb_ldg_stream(base + 32 * h);
-      float slo, shi;
-      ScalePair<F32S>::load(scales, seg * 32 + lane, slo, shi);
+      for (int r = 0; r < Q80_R; r++) {
+        const int row = min(row0 + r, N - 1);
+        const size_t seg = (size_t)row * nch + c;
+        const uint4* base = codes + seg * 128 + lane;
+#pragma unroll
+        for (int h = 0; h < 4; h++) q[r][h] = pb_ldg_stream(base + 32 * h);
+        ScalePair<F32S>::load(scales, seg * 32 + lane, slo[r], shi[r]);
+      }
 #pragma unroll
       for (int half = 0; half < 2; half++) {
         const int blk = c * 64 + lane + 32 * half;
         const uint4* xq = reinterpret_cast<const uint4*>(sq + blk * 32);
         const uint4 x0 = xq[0], x1 = xq[1];
-        const uint4 w0 = q[2 * half], w1 = q[2 * half + 1];
-        int s = 0;
-        s = __dp4a((int)w0.x, (int)x0.x, s); s = __dp4a((int)w0.y, (int)x0.y, s);
-        s = __dp4a((int)w0.z, (int)x0.z, s); s = __dp4a((int)w0.w, (int)x0.w, s);
-        s = __dp4a((int)w1.x, (int)x1.x, s); s = __dp4a((int)w1.y, (int)x1.y, s);
-        s = __dp4a((int)w1.z, (int)x1.z, s); s = __dp4a((int)w1.w, (int)x1.w, s);
-        if (isum) isum[(size_t)row * nb + blk] = s;
-        const float dw = half ? shi : slo;
-        pw[blk] = __fmul_rn(__fmul_rn(dw, sdx[blk]), __int2float_rn(s));
+        const float sx = sdx[blk];
+#pragma unroll
+        for (int r = 0; r < Q80_R; r++) {
+          const uint4 w0 = q[r][2 * half], w1 = q[r][2 * half + 1];
+          int s = 0;
+          s = __dp4a((int)w0.x, (int)x0.x, s); s = __dp4a((int)w0.y, (int)x0.y, s);
+          s = __dp4a((int)w0.z, (int)x0.z, s); s = __dp4a((int)w0.w, (int)x0.w, s);
+          s = __dp4a((int)w1.x, (int)x1.x, s); s = __dp4a((int)w1.y, (int)x1.y, s);
+          s = __dp4a((int)w1.z, (int)x1.z, s); s = __dp4a((int)w1.w, (int)x1.w, s);
+          if (isum && row0 + r < N) isum[(size_t)(row0 + r) * nb + blk] = s;
+          pw[r * ps + blk] = __fmul_rn(__fmul_rn(half ? shi[r] : slo[r], sx), __int2float_rn(s));
+        }
       }
     }
     __syncwarp();
-    if (lane == 0) {
+    if (lane < Q80_R && row0 + lane < N) {
+      const float* pr = pw + lane * ps;
       float acc = 0.0f;
-      for (int b = 0; b < nb; b++) acc = __fadd_rn(acc, pw[b]);
-      y[row] = acc;
+      for (int b = 0; b < nb; b++) acc = __fadd_rn(acc, pr[b]);
+      y[row0 + lane] = acc;
     }
     __syncwarp();
   }
@@ -475,10 +485,10 @@ extern "C" int pb_q80_gemv(const pb_q8* w, const int8_t* d_qx, const uint16_t* d
   if (w->layout == PB_Q8_UMMA) return pb_set_error(PB_EINVAL, "pb_q80_gemv: tensor packed for pb_q80_gemm");
   if (w->layout != PB_Q8_STREAM) return pb_set_error(PB_ENOTSUP, "pb_q80_gemv: needs K %% 2048 == 0 (K=%d)", w->K);
   if (((uintptr_t)d_qx & 15) != 0) return pb_set_error(PB_EINVAL, "pb_q80_gemv: qx must be 16-byte aligned");
-  const size_t smem = (size_t)w->K + (size_t)(w->K / 32) * 4 * 9;
+  const size_t smem = (size_t)w->K + (size_t)(w->K / 32) * 4 + (size_t)8 * Q80_R * (w->K / 32 + 1) * 4;
   if (smem > 200 * 1024) return pb_set_error(PB_ENOTSUP, "pb_q80_gemv: K=%d too large", w->K);
-  int grid = 2 * pb_num_sms();
-  if (grid * 8 > w->N) grid = (w->N + 7) / 8;
+  int grid = 3 * pb_num_sms();
+  if (grid * 8 * Q80_R > w->N) grid = (w->N + 8 * Q80_R - 1) / (8 * Q80_R);
   cudaStream_t st = (cudaStream_t)stream;
   const uint4* q = reinterpret_cast<const uint4*>(w->codes);
   if (w->sdt == PB_DT_F32) {
