@@ -303,17 +303,26 @@ __device__ __forceinline__ unsigned gemv_phase(const DecodeArgs& d, const Phase&
         slo[u] = shi[u] = 0.0f;
       }
     }
+    // release the slot as soon as its data sit in registers (the empty asm
+    // makes every load complete first), so the refill of the stage DS ahead
+    // overlaps this stage's arithmetic; the last warp to release issues it
+    asm volatile("" ::"r"(q[0][0].x), "r"(q[0][0].y), "r"(q[0][0].z), "r"(q[0][0].w), "r"(q[0][1].x),
+                 "r"(q[0][1].y), "r"(q[0][1].z), "r"(q[0][1].w), "r"(q[0][2].x), "r"(q[0][2].y),
+                 "r"(q[0][2].z), "r"(q[0][2].w), "r"(q[0][3].x), "r"(q[0][3].y), "r"(q[0][3].z),
+                 "r"(q[0][3].w), "f"(slo[0]), "f"(shi[0]));
+    asm volatile("" ::"r"(q[1][0].x), "r"(q[1][0].y), "r"(q[1][0].z), "r"(q[1][0].w), "r"(q[1][1].x),
+                 "r"(q[1][1].y), "r"(q[1][1].z), "r"(q[1][1].w), "r"(q[1][2].x), "r"(q[1][2].y),
+                 "r"(q[1][2].z), "r"(q[1][2].w), "r"(q[1][3].x), "r"(q[1][3].y), "r"(q[1][3].z),
+                 "r"(q[1][3].w), "f"(slo[1]), "f"(shi[1]));
+    __syncwarp();
+    if (lane == 0 && slot_release(slot)) {
+      issue_ctx()->cnt[slot] = 0;
+      if (it + ds < total) issue_stage<F32S>(kn, slot, it + ds, ring, full);
+    }
     float v[2];
 #pragma unroll
     for (int u = 0; u < 2; u++) v[u] = pb_warp_tree(leaf2(q[u], slo[u], shi[u], xr));
-    // the stage's data are consumed (the tree depends on every loaded value):
-    // the last warp to get here refills the slot with the stage DS ahead
-    __syncwarp();
     if (lane == 0) {
-      if (slot_release(slot)) {
-        issue_ctx()->cnt[slot] = 0;
-        if (it + ds < total) issue_stage<F32S>(kn, slot, it + ds, ring, full);
-      }
       const int lr = r - r0 + g * 2;
       rowv[lr * nch + c] = v[0];
       if (r + g * 2 + 1 < r1) rowv[(lr + 1) * nch + c] = v[1];
