@@ -269,6 +269,8 @@ def run_reference(args, rank, world):
     host cores, rank 0 only."""
     if rank != 0:
         return
+    # torchrun sets OMP_NUM_THREADS=1 for N > 1; the reference arm uses every host core
+    os.environ["OMP_NUM_THREADS"] = str(len(os.sched_getaffinity(0)))
     sys.path.insert(0, os.path.join(ROOT, "oracle"))
     import oracle as O
     O.build() if not os.path.exists(O.LIB_PATH) else None
