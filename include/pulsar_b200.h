@@ -172,6 +172,19 @@ int pb_decode_prompt(pb_model* m, pb_state* s, const int* d_tokens, int n, int p
  * stream. Results are identical to pb_layer_step's. */
 int pb_layer_step_noalloc(pb_model* m, pb_state* s, int layer, int pos, uint16_t* d_x,
                           void* stream);
+/* chunked prefill on the integer path (the tensor-core GEMMs of pb_q80_gemm
+ * for every projection): T prompt tokens (device int32, T a multiple of 16,
+ * at most 256) at positions pos0 .. pos0+T-1 through every layer, updating
+ * the KV caches and conv rings as T decode steps would. Each position's
+ * values are those of the decode step with every projection (and the head)
+ * on the Q8_0 integer path: activations quantised per 32-block, exact int32
+ * block dots, in-order fp32 fold, bf16 outputs. d_ids (optional, int32 [T])
+ * receives each position's greedy id, d_logits (optional, fp32 [T][vocab])
+ * the logits. The first call builds tensor-core copies of the weights.
+ * Replaces layer_chunk_T / prefill_e2e (lfm3_nanode.cu:4997-5162,
+ * :5248-5313) in its integer form. */
+int pb_prefill_chunk(pb_model* m, pb_state* s, const int* d_tokens, int T, int pos0, int* d_ids,
+                     float* d_logits, void* stream);
 /* synchronise `stream` and report a decode failure recorded on the device
  * (a bounded wait inside the decode kernel that gave up): PB_OK or PB_ECUDA */
 int pb_state_status(pb_state* s, void* stream);

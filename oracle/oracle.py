@@ -67,6 +67,7 @@ def lib():
         L.pbo_model_free.argtypes = [vp]
         L.pbo_model_set_q8.argtypes = [vp, i, i, vp, vp, i, i]
         L.pbo_model_set_f32.argtypes = [vp, i, i, vp]
+        L.pbo_model_set_int.argtypes = [vp, i]
         L.pbo_state_new.restype = vp; L.pbo_state_new.argtypes = [vp]
         L.pbo_state_free.argtypes = [vp]
         L.pbo_decode.restype = i; L.pbo_decode.argtypes = [vp, vp, i, i, vp, vp]
@@ -177,7 +178,9 @@ class Model:
     SLOTS_F = {"op_norm": 0, "post_op_norm": 1, "ffn_norm": 2, "post_ffn_norm": 3,
                "q_norm": 4, "k_norm": 5, "taps": 6}
 
-    def __init__(self, cfg, weights):
+    def __init__(self, cfg, weights, int_path=False):
+        """int_path: every projection on the Q8_0 integer path (the chunked
+        prefill's tensor-core form) instead of the reference's float path."""
         L = lib()
         self.cfg = cfg
         self._keep = []
@@ -207,6 +210,7 @@ class Model:
         fn = np.ascontiguousarray(weights["final_norm"], np.float32)
         self._keep.append(fn)
         L.pbo_model_set_f32(self.m, -1, 0, _p(fn))
+        L.pbo_model_set_int(self.m, 1 if int_path else 0)
         self.s = L.pbo_state_new(self.m)
 
     def reset(self):
@@ -223,6 +227,13 @@ class Model:
         c = self.cfg
         ptr = lib().pbo_state_kv(self.s, layer, which)
         return np.ctypeslib.as_array(C.cast(ptr, C.POINTER(C.c_uint16)), shape=(n * c["n_kv"] * c["head_dim"],)).copy()
+
+    def ring(self, layer):
+        """the conv layer's ring [W][H] (bf16 bits), oldest position first"""
+        c = self.cfg
+        ptr = lib().pbo_state_ring(self.s, layer)
+        return np.ctypeslib.as_array(C.cast(ptr, C.POINTER(C.c_uint16)),
+                                     shape=(c["conv_w"] * c["hidden"],)).copy().reshape(c["conv_w"], c["hidden"])
 
     def __del__(self):
         try:

@@ -411,6 +411,7 @@ int pbo_argmax(const float* v, int n) {
 typedef struct { const int8_t* c; const float* s; int N, K; } q8t;
 struct pbo_model {
   pbo_cfg cfg;
+  int int_mode;          /* 1: every projection on the Q8_0 integer path */
   int* is_attn;
   q8t (*q)[PBO_NQ8];
   const float* (*f)[PBO_NF32];
@@ -477,12 +478,41 @@ const uint16_t* pbo_state_kv(const pbo_state* s, int layer, int which) {
 }
 const uint16_t* pbo_state_ring(const pbo_state* s, int layer) { return s->ring[layer]; }
 
+/* the integer path of one projection: x (bf16 values) quantised per 32-block
+ * (fwd35_ref.c:332-343), exact int32 block dots, then the fold
+ * acc = acc + (dw * dx) * (float)isum in block order (pq1_host.c:112-116
+ * pattern); fp32 out */
+static void gemv_int(const q8t* t, const uint16_t* x, float* yf) {
+  const int K = t->K, nb = K / 32;
+  float* xf = (float*)malloc(sizeof(float) * K);
+  int8_t* qx = (int8_t*)malloc(K);
+  uint16_t* dx = (uint16_t*)malloc(2 * (size_t)nb);
+  float* dxf = (float*)malloc(sizeof(float) * nb);
+  for (int i = 0; i < K; i++) xf[i] = pbo_bf2f(x[i]);
+  pbo_q80_quant_act(xf, K, qx, dx);
+  for (int b = 0; b < nb; b++) dxf[b] = pbo_h2f(dx[b]);
+#pragma omp parallel for schedule(static)
+  for (int n = 0; n < t->N; n++) {
+    float acc = 0.0f;
+    for (int b = 0; b < nb; b++) {
+      const int8_t* cw = t->c + (size_t)n * K + (size_t)b * 32;
+      int32_t sum = 0;
+      for (int j = 0; j < 32; j++) sum += (int32_t)cw[j] * (int32_t)qx[32 * b + j];
+      acc = acc + (t->s[(size_t)n * nb + b] * dxf[b]) * (float)sum;
+    }
+    yf[n] = acc;
+  }
+  free(xf); free(qx); free(dx); free(dxf);
+}
+static int g_int_mode = 0;   /* set for the duration of one pbo_decode call */
 static void gemv_bf(const q8t* t, const uint16_t* x, uint16_t* y) {
   float* yf = (float*)malloc(sizeof(float) * t->N);
-  pbo_q8f_gemv(t->c, t->s, t->N, t->K, x, yf);
+  if (g_int_mode) gemv_int(t, x, yf);
+  else pbo_q8f_gemv(t->c, t->s, t->N, t->K, x, yf);
   for (int i = 0; i < t->N; i++) y[i] = pbo_f2bf(yf[i]);
   free(yf);
 }
+void pbo_model_set_int(pbo_model* m, int on) { m->int_mode = on; }
 
 /* layer_body, lfm3_nanode.cu:3739-3856 (sandwich norms, conv or attention
  * mixer, SwiGLU FFN), with the conv width and head geometry taken from cfg. */
@@ -492,6 +522,7 @@ int pbo_decode(const pbo_model* m, pbo_state* s, int token, int pos, float* logi
   const int H = c->hidden, F = c->inter, NH = c->n_heads, NKV = c->n_kv, HD = c->head_dim;
   const int W = c->conv_w;
   uint16_t* x = s->x;
+  g_int_mode = m->int_mode;
   uint16_t *h1 = malloc(2 * (size_t)H), *h2 = malloc(2 * (size_t)(F > 3 * H ? F : 3 * H));
   uint16_t *h3 = malloc(2 * (size_t)F), *bx = malloc(2 * (size_t)3 * H);
   uint16_t *qb = malloc(2 * (size_t)NH * HD), *kb = malloc(2 * (size_t)NKV * HD);
@@ -555,7 +586,12 @@ int pbo_decode(const pbo_model* m, pbo_state* s, int token, int pos, float* logi
   /* embedding_norm, then the tied head in fp32 (gemv_f + k_combine_f) */
   pbo_rmsnorm(x, m->final_norm, h1, H, c->norm_eps);
   float* lg = logits ? logits : (float*)malloc(sizeof(float) * c->vocab);
-  pbo_q8f_gemv(m->emb.c, m->emb.s, c->vocab, H, h1, lg);
+  if (m->int_mode) {
+    const q8t head = {m->emb.c, m->emb.s, c->vocab, H};
+    gemv_int(&head, h1, lg);
+  } else {
+    pbo_q8f_gemv(m->emb.c, m->emb.s, c->vocab, H, h1, lg);
+  }
   const int id = pbo_argmax(lg, c->vocab);
   if (x_out) memcpy(x_out, x, 2 * (size_t)H);
   if (!logits) free(lg);

@@ -88,6 +88,10 @@ void pbo_model_free(pbo_model* m);
 void pbo_model_set_q8(pbo_model* m, int layer, int slot, const int8_t* codes,
                       const float* scales, int N, int K);
 void pbo_model_set_f32(pbo_model* m, int layer, int slot, const float* p);
+/* 1: every projection (and the head) on the Q8_0 integer path: activations
+ * quantised per 32-block, exact block dots, in-order fp32 fold (the chunked
+ * prefill's tensor-core form); 0: the reference's float path (default) */
+void pbo_model_set_int(pbo_model* m, int on);
 /* layer -1: the tied embedding / head (Q8) and the final norm (fp32). */
 pbo_state* pbo_state_new(const pbo_model* m);
 void pbo_state_free(pbo_state* s);

@@ -70,3 +70,8 @@ int pb_q8_pack_into(pb_q8* w, const int8_t* d_codes, const void* d_scales, cudaS
 int pb_q8_gemv_launch(const pb_q8* w, const uint16_t* d_x, void* d_y, int y_dtype,
                       cudaStream_t st);
 int pb_num_sms();
+
+// tensor-core (kind::i8) copies of streaming-layout tensors, for the
+// chunked prefill: bytes of the copy, and the conversion into caller storage
+size_t pb_q80tc_bytes(int N, int K);
+int pb_q80tc_from_stream(const pb_q8* src, char* storage, pb_q8* out, cudaStream_t st);

@@ -21,6 +21,7 @@
 #include "pb_json.h"
 #include "pb_step.cuh"
 #include "pb_decode.cuh"
+#include "pb_prefill.cuh"
 #include <zlib.h>
 #include <cmath>
 #include <cstdio>
@@ -249,7 +250,7 @@ __global__ void __launch_bounds__(256) k_attn(AttnArgs a) {
   __shared__ float segred[8 * HD];
   pb_grid_launch_dependents();
   pb_grid_wait();
-  attn_body<E, 0>(a, blockIdx.x, sl, qv, kv, vv, segred, red);
+  attn_body<E, 0>(a, blockIdx.x, a.ctl->pos, sl, qv, kv, vv, segred, red);
 }
 
 // residual tail for the standalone layer step: x = R + bf16(rms(h, w))
@@ -298,6 +299,9 @@ struct pb_model {
   std::vector<float> invf;
   uint64_t weight_bytes = 0;
   bool decode_ok = true;     // every decode tensor in the streaming layout
+  // tensor-core copies of every projection for the chunked prefill (built on first use)
+  char* tc_arena = nullptr;
+  std::vector<pb_q8> tc;     // per layer: first, mix, w13, w2; then the head
 };
 
 struct pb_state {
@@ -339,6 +343,17 @@ struct pb_state {
   cudaStream_t graph_stream = nullptr;
   int graph_res = 0;              // residual buffer holding the final residual
   uint64_t graph_launches = 0;    // kernels per graph replay
+  // chunked prefill buffers (allocated on first use, for up to pf_cap positions)
+  char* pf_mem = nullptr;
+  int pf_cap = 0;
+  bf16_t* pf_R = nullptr;         // [T][H] residual
+  int8_t* pf_qx = nullptr;        // [T][Kmax] quantised projection input
+  uint16_t* pf_dx = nullptr;      // [T][Kmax/32]
+  float* pf_y = nullptr;          // [T][Nmax] projection output
+  bf16_t* pf_qkvg = nullptr;      // [T][q|k|v|gate]
+  bf16_t* pf_att = nullptr;       // [T][NH*HD] gated attention output
+  float* pf_logits = nullptr;     // [T][V]
+  int* pf_tok = nullptr;          // [T]
 };
 
 namespace {
@@ -1152,6 +1167,7 @@ extern "C" int pb_open(const char* path, int device, pb_model** out) {
 extern "C" int pb_close(pb_model* m) {
   if (!m) return PB_OK;
   cudaFree(m->arena);
+  cudaFree(m->tc_arena);
   delete m;
   return PB_OK;
 }
@@ -1244,6 +1260,7 @@ extern "C" int pb_state_destroy(pb_state* s) {
   if (s->graph_stream) cudaStreamDestroy(s->graph_stream);
   cudaFreeHost(s->h_ctl);
   cudaFree(s->mem);
+  cudaFree(s->pf_mem);
   delete s;
   return PB_OK;
 }
@@ -1603,3 +1620,161 @@ extern "C" int pb_layer_step_noalloc(pb_model* m, pb_state* s, int layer, int po
   PB_LAUNCHED("k_tail");
   return PB_OK;
 }
+
+// ------------------------------------------------------------ chunked prefill
+namespace {
+
+int prefill_prepare(pb_model* m, pb_state* s, int T, cudaStream_t st) {
+  if (!m->tc_arena) {
+    std::vector<const pb_q8*> src;
+    for (auto& Ly : m->layers) { src.push_back(&Ly.first); src.push_back(&Ly.mix); src.push_back(&Ly.w13); src.push_back(&Ly.w2); }
+    src.push_back(&m->head);
+    size_t tot = 0;
+    for (auto* w : src) tot += align256(pb_q80tc_bytes(w->N, w->K));
+    if (cudaMalloc(&m->tc_arena, tot) != cudaSuccess) {
+      cudaGetLastError();
+      m->tc_arena = nullptr;
+      return pb_set_error(PB_ENOMEM, "prefill: tensor-core weight copies (%zu bytes)", tot);
+    }
+    m->tc.assign(src.size(), pb_q8());
+    size_t off = 0;
+    for (size_t i = 0; i < src.size(); i++) {
+      int rc = pb_q80tc_from_stream(src[i], m->tc_arena + off, &m->tc[i], st);
+      if (rc) return rc;
+      off += align256(pb_q80tc_bytes(src[i]->N, src[i]->K));
+    }
+  }
+  if (s->pf_cap < T) {
+    cudaFree(s->pf_mem);
+    s->pf_mem = nullptr;
+    s->pf_cap = 0;
+    const int H = m->H, F = m->F;
+    const int nq = m->NH * m->HD + 2 * m->NKV * m->HD + m->NH;
+    const int kmax = std::max(H, std::max(F, m->NH * m->HD));
+    int nmax = std::max(std::max(3 * H, nq), std::max(2 * F, H));
+    const size_t sizes[] = {(size_t)T * H * 2, (size_t)T * kmax, (size_t)T * (kmax / 32) * 2, (size_t)T * nmax * 4,
+                            (size_t)T * nq * 2, (size_t)T * m->NH * m->HD * 2, (size_t)T * m->V * 4, (size_t)T * 4};
+    size_t tot = 0;
+    for (size_t x : sizes) tot += align256(x);
+    if (cudaMalloc(&s->pf_mem, tot) != cudaSuccess) {
+      cudaGetLastError();
+      s->pf_mem = nullptr;
+      return pb_set_error(PB_ENOMEM, "prefill: buffers");
+    }
+    void** slots[] = {(void**)&s->pf_R, (void**)&s->pf_qx, (void**)&s->pf_dx, (void**)&s->pf_y, (void**)&s->pf_qkvg,
+                      (void**)&s->pf_att, (void**)&s->pf_logits, (void**)&s->pf_tok};
+    char* p = s->pf_mem;
+    for (size_t i = 0; i < sizeof(sizes) / sizeof(sizes[0]); i++) { *slots[i] = p; p += align256(sizes[i]); }
+    s->pf_cap = T;
+  }
+  return PB_OK;
+}
+
+int pf_norm(const pb_model* m, pb_state* s, int T, const int* tokens, const float* hin, const float* wpost,
+            const float* wnorm, cudaStream_t st) {
+  PfNormArgs a = {};
+  a.tokens = tokens;
+  a.emb_codes = reinterpret_cast<const uint4*>(m->head.codes);
+  a.emb_scales = m->head.scales;
+  a.emb_nch = m->head.nch;
+  a.emb_f32 = m->head.sdt == PB_DT_F32;
+  a.rin = s->pf_R;
+  a.hin = hin;
+  a.wpost = wpost;
+  a.wnorm = wnorm;
+  a.rout = s->pf_R;
+  a.qx = s->pf_qx;
+  a.dx = s->pf_dx;
+  a.H = m->H;
+  a.eps = m->eps;
+  k_pf_norm_quant<8><<<T, 256, 0, st>>>(a);
+  PB_LAUNCHED("k_pf_norm_quant");
+  return PB_OK;
+}
+
+}  // namespace
+
+// The chunked prefill on the integer path (see pb_prefill.cuh): T prompt
+// tokens (device int32, T a multiple of 16, at most 256) at positions
+// pos0 .. pos0+T-1 through every layer, the KV caches and conv rings updated
+// as T decode steps would update them. d_ids (optional, int32 [T]) receives
+// each position's greedy id, d_logits (optional, fp32 [T][vocab]) the logits.
+// Compiled for the LFM3 2B shape (hidden 2048, head_dim 64, conv width 3).
+extern "C" int pb_prefill_chunk(pb_model* m, pb_state* s, const int* d_tokens, int T, int pos0, int* d_ids,
+                                float* d_logits, void* stream) {
+  if (!m || !s || !d_tokens || T <= 0) return pb_set_error(PB_EINVAL, "pb_prefill_chunk: bad argument");
+  if (T % 16 || T > 256) return pb_set_error(PB_ENOTSUP, "pb_prefill_chunk: T=%d (a multiple of 16, at most 256)", T);
+  if (pos0 < 0 || pos0 + T > s->max_ctx) return pb_set_error(PB_EINVAL, "pb_prefill_chunk: positions beyond max_ctx");
+  if (m->H != 2048 || m->HD != 64 || m->W != 3 || m->F % 256 || m->F / 256 > 32 || (m->NH * m->HD) != 2048)
+    return pb_set_error(PB_ENOTSUP, "pb_prefill_chunk: shape not compiled");
+  if (!m->decode_ok) return pb_set_error(PB_ENOTSUP, "pb_prefill_chunk: needs every K a multiple of 2048");
+  PB_TRY_CUDA(cudaSetDevice(m->device));
+  cudaStream_t st = (cudaStream_t)stream;
+  int rc = prefill_prepare(m, s, T, st);
+  if (rc) return rc;
+  const int H = m->H, F = m->F;
+  const int nq = m->NH * m->HD + 2 * m->NKV * m->HD + m->NH;
+  const size_t per = (size_t)s->max_ctx * m->NKV * m->HD;
+  for (int L = 0; L < m->L; L++) {
+    const Layer& Ly = m->layers[L];
+    const pb_q8* tc = &m->tc[(size_t)L * 4];
+    if (L == 0) rc = pf_norm(m, s, T, d_tokens, nullptr, nullptr, Ly.op_norm, st);
+    else rc = pf_norm(m, s, T, nullptr, s->pf_y, m->layers[L - 1].post_ffn_norm, Ly.op_norm, st);
+    if (rc) return rc;
+    if ((rc = pb_q80_gemm(&tc[0], T, s->pf_qx, s->pf_dx, s->pf_y, nullptr, st))) return rc;
+    if (Ly.attn) {
+      PfQkvArgs q = {};
+      q.y = s->pf_y;
+      q.qkvg = s->pf_qkvg;
+      q.knorm = Ly.k_norm;
+      q.rope_cos = s->rope_cos;
+      q.rope_sin = s->rope_sin;
+      q.kc = s->kv + (size_t)Ly.attn_idx * 2 * per;
+      q.vc = q.kc + per;
+      q.nq = nq; q.nh = m->NH; q.nkv = m->NKV; q.half = half_rot(m); q.pos0 = pos0; q.eps = m->eps;
+      k_pf_qkv<2><<<T, 256, 0, st>>>(q);
+      PB_LAUNCHED("k_pf_qkv");
+      AttnArgs a = attn_args(m, s, L);
+      a.qkvg = s->pf_qkvg;
+      a.out = s->pf_att;
+      PB_TRY_CUDA(cudaFuncSetAttribute(k_pf_attn<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, 160 * 1024));
+      k_pf_attn<2><<<dim3(m->NH, T), 256, (size_t)s->max_ctx * sizeof(float), st>>>(a, pos0, nq, m->NH * m->HD);
+      PB_LAUNCHED("k_pf_attn");
+      k_pf_quant<8><<<T, 256, 0, st>>>(s->pf_att, m->NH * m->HD, s->pf_qx, s->pf_dx);
+      PB_LAUNCHED("k_pf_quant");
+    } else {
+      PfConvArgs c = {};
+      c.y = s->pf_y;
+      c.ring = s->ring + (size_t)Ly.conv_idx * m->W * H;
+      c.taps = Ly.taps;
+      c.qx = s->pf_qx;
+      c.dx = s->pf_dx;
+      c.H = H;
+      c.pos0 = pos0;
+      k_pf_conv_quant<8, 3><<<T, 256, 0, st>>>(c);
+      PB_LAUNCHED("k_pf_conv_quant");
+      k_pf_ring<<<dim3((H + 255) / 256, m->W), 256, 0, st>>>(s->pf_y, s->ring + (size_t)Ly.conv_idx * m->W * H,
+                                                             H, m->W, T, pos0);
+      PB_LAUNCHED("k_pf_ring");
+    }
+    if ((rc = pb_q80_gemm(&tc[1], T, s->pf_qx, s->pf_dx, s->pf_y, nullptr, st))) return rc;
+    if ((rc = pf_norm(m, s, T, nullptr, s->pf_y, Ly.post_op_norm, Ly.ffn_norm, st))) return rc;
+    if ((rc = pb_q80_gemm(&tc[2], T, s->pf_qx, s->pf_dx, s->pf_y, nullptr, st))) return rc;
+    switch (F / 256) {
+      case 8: k_pf_silu_quant<8><<<T, 256, 0, st>>>(s->pf_y, F, s->pf_qx, s->pf_dx); break;
+      case 16: k_pf_silu_quant<16><<<T, 256, 0, st>>>(s->pf_y, F, s->pf_qx, s->pf_dx); break;
+      default: k_pf_silu_quant<32><<<T, 256, 0, st>>>(s->pf_y, F, s->pf_qx, s->pf_dx); break;
+    }
+    PB_LAUNCHED("k_pf_silu_quant");
+    if ((rc = pb_q80_gemm(&tc[3], T, s->pf_qx, s->pf_dx, s->pf_y, nullptr, st))) return rc;
+  }
+  if ((rc = pf_norm(m, s, T, nullptr, s->pf_y, m->layers[m->L - 1].post_ffn_norm, m->final_norm, st))) return rc;
+  float* lg = d_logits ? d_logits : s->pf_logits;
+  if ((rc = pb_q80_gemm(&m->tc.back(), T, s->pf_qx, s->pf_dx, lg, nullptr, st))) return rc;
+  if (d_ids) {
+    k_pf_argmax<<<T, 256, 0, st>>>(lg, m->V, d_ids);
+    PB_LAUNCHED("k_pf_argmax");
+  }
+  return PB_OK;
+}
+

@@ -297,6 +297,36 @@ __global__ void k_q80tc_pack(const int8_t* __restrict__ codes, const S* __restri
   }
 }
 
+// the same tiles from a tensor in the streaming layout (pb_q8.cu): granule
+// h*32 + l of segment (row, chunk) holds codes [16(h&1), +16) of block
+// l + 32(h>>1) of the chunk; scales are pairs (s_l, s_{l+32}) per segment
+template <typename S>
+__global__ void k_q80tc_from_stream(const uint4* __restrict__ codes, const S* __restrict__ scales, int N, int K,
+                                    int ntile, int8_t* __restrict__ a, float* __restrict__ dw) {
+  const int nblk = K / 32, nch = K / 2048;
+  const size_t total = (size_t)ntile * TC_M * nblk * 2;
+  for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (size_t)gridDim.x * blockDim.x) {
+    const int kh = (int)(i & 1);
+    const size_t rb = i >> 1;
+    const int row = (int)(rb % TC_M);
+    const size_t tb = rb / TC_M;
+    const int b = (int)(tb % nblk);
+    const int tile = (int)(tb / nblk);
+    const int n = tile * TC_M + row;
+    const int c = b / 64, bl = b % 64, l = bl % 32, hb = bl / 32;
+    uint4 v = make_uint4(0, 0, 0, 0);
+    float sc = 0.0f;
+    if (n < N) {
+      const size_t seg = (size_t)n * nch + c;
+      v = codes[seg * 128 + (hb * 2 + kh) * 32 + l];
+      if (sizeof(S) == 2) sc = pb_h2f((unsigned short)scales[(seg * 32 + l) * 2 + hb]);
+      else sc = (float)scales[(seg * 32 + l) * 2 + hb];
+    }
+    *reinterpret_cast<uint4*>(a + tb * 4096 + (row >> 3) * 256 + kh * 128 + (row & 7) * 16) = v;
+    if (kh == 0) dw[tb * TC_M + row] = sc;
+  }
+}
+
 // activations [T][K] int8 + fp16 scales [T][K/32] -> the kernel's layout:
 // per 16 positions, per block, 2 groups of 8 positions x 2 halves x 16 bytes
 __global__ void k_q80tc_act(const int8_t* __restrict__ qx, const uint16_t* __restrict__ dxh, int T, int K,
@@ -393,6 +423,33 @@ extern "C" int pb_q80tc_pack(const int8_t* codes, const void* scales, int scale_
   cudaFree(tc); cudaFree(ts);
   if (rc != PB_OK) { cudaFree(w->codes); cudaFree(w->scales); delete w; return rc; }
   *out = w;
+  return PB_OK;
+}
+
+// a tensor-core copy of a tensor held in the streaming layout (the model's
+// weights), into caller-provided storage of pb_q80tc_bytes() bytes
+size_t pb_q80tc_bytes(int N, int K) {
+  const size_t ntile = (size_t)(N + TC_M - 1) / TC_M;
+  return ntile * TC_M * K + ntile * TC_M * (K / 32) * 4;
+}
+int pb_q80tc_from_stream(const pb_q8* src, char* storage, pb_q8* out, cudaStream_t st) {
+  if (src->layout != PB_Q8_STREAM || src->K % (32 * TC_CB))
+    return pb_set_error(PB_ENOTSUP, "tensor-core copy: needs the streaming layout");
+  const int N = src->N, K = src->K, ntile = (N + TC_M - 1) / TC_M;
+  out->N = N; out->K = K; out->sdt = src->sdt; out->layout = PB_Q8_UMMA; out->nch = 1; out->owner = false;
+  out->codes = reinterpret_cast<int8_t*>(storage);
+  out->scales = storage + (size_t)ntile * TC_M * K;
+  const size_t units = (size_t)ntile * TC_M * (K / 32) * 2;
+  const int grid = (int)std::min<size_t>((units + 255) / 256, (size_t)pb_num_sms() * 16);
+  if (src->sdt == PB_DT_F32)
+    k_q80tc_from_stream<float><<<grid, 256, 0, st>>>(reinterpret_cast<const uint4*>(src->codes),
+                                                     (const float*)src->scales, N, K, ntile, out->codes,
+                                                     (float*)out->scales);
+  else
+    k_q80tc_from_stream<unsigned short><<<grid, 256, 0, st>>>(reinterpret_cast<const uint4*>(src->codes),
+                                                              (const unsigned short*)src->scales, N, K, ntile,
+                                                              out->codes, (float*)out->scales);
+  PB_LAUNCHED("k_q80tc_from_stream");
   return PB_OK;
 }
 

@@ -502,12 +502,11 @@ __device__ void head_norm_rope(const bf16_t* __restrict__ x, const float* __rest
 // cache row another CTA writes in the same step. sl: scores [max_ctx]. Not
 // inlined: the persistent kernel keeps its register budget for the GEMV loop.
 template <int E, int SYNC>
-__device__ __noinline__ void attn_body(const AttnArgs& a, int h, float* sl, float* qv, float* kv, float* vv,
+__device__ __noinline__ void attn_body(const AttnArgs& a, int h, int pos, float* sl, float* qv, float* kv, float* vv,
                           float* segred, float* red) {
   constexpr int HD = 32 * E;
   const int t = threadIdx.x, lane = t & 31, wid = t >> 5;
   const int grp = a.nh / a.nkv, kvh = h / grp;
-  const int pos = ldi<SYNC>(&a.ctl->pos);
   const int npos = pos + 1;
   const int lo = (a.win > 0 && npos > a.win) ? npos - a.win : 0;
   const int np = npos - lo;

@@ -100,6 +100,7 @@ def lib():
     L.pb_test_expf.argtypes = [vp, vp, i, vp]
     L.pb_layer_step_noalloc.argtypes = [vp, vp, i, i, vp, vp]
     L.pb_state_status.argtypes = [vp, vp]
+    L.pb_prefill_chunk.argtypes = [vp, vp, vp, i, i, vp, vp, vp]
     _lib = L
     return L
 
@@ -309,6 +310,11 @@ class State:
         """tokens: device int32 [n]; ids (optional device int32 [n])."""
         check(lib().pb_decode_prompt(self.model.h, self.h, _ptr(tokens), tokens.numel(), int(pos0),
                                      _ptr(ids), _stream(stream)))
+
+    def prefill_chunk(self, tokens, pos0, ids=None, logits=None, stream=None):
+        """integer-path chunked prefill of device int32 tokens [T] at pos0.."""
+        check(lib().pb_prefill_chunk(self.model.h, self.h, _ptr(tokens), tokens.shape[0], int(pos0), _ptr(ids),
+                                     _ptr(logits), _stream(stream)))
 
     def status(self, stream=None):
         """synchronise and raise if the decode kernel recorded a failure."""
