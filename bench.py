@@ -263,6 +263,31 @@ def kernel_suite(torch, pb, peak, stream):
     return out
 
 
+def prefill_bench(torch, model, prompt, stream, T=32):
+    """cfg2: the 1024-token prompt in chunks of T positions through the whole
+    backbone on the integer path (tensor-core GEMMs), timed by CUDA events
+    after one untimed pass (which also builds the tensor-core weight copies)"""
+    n = (prompt.numel() // T) * T
+    st = model.new_state(n + 8)
+    ids = torch.empty(T, dtype=torch.int32, device="cuda")
+    with torch.cuda.stream(stream):
+        for c in range(0, n, T):
+            st.prefill_chunk(prompt[c:c + T], c, ids, stream=stream)
+        stream.synchronize()
+        st.reset(stream=stream)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for c in range(0, n, T):
+            st.prefill_chunk(prompt[c:c + T], c, ids, stream=stream)
+        e1.record(stream)
+        e1.synchronize()
+    st.status(stream)
+    ms = e0.elapsed_time(e1)
+    st.destroy()
+    return {"tokens": n, "chunk": T, "ms": ms, "tok/s": n / (ms / 1e3), "ms_per_chunk": ms / (n // T),
+            "path": "integer (Q8_0 activations, tcgen05 kind::i8 GEMMs)"}
+
+
 def run_reference(args, rank, world):
     """--impl reference: the reference's CPU implementation of this path (the
     oracle port: the reference's decode engine has no CPU form) on this box's
@@ -403,6 +428,7 @@ def main():
             "clocks": clk.summary()}
     if rank == 0 and world == 1 and not args.no_kernels:
         line["kernels"] = kernel_suite(torch, pb, peak, stream)
+        line["kernels"]["cfg2_prefill"] = prefill_bench(torch, model, prompt, stream)
     if rank == 0 and world == 1 and not args.no_cpu:
         tps, cores, n, _ = cpu_baseline(c, weights, args.ctx, args.cpu_seconds)
         line["cpu_baseline"] = {"value": tps, "unit": "tok/s", "cores": cores, "kind": "port",
