@@ -185,6 +185,17 @@ int pb_layer_step_noalloc(pb_model* m, pb_state* s, int layer, int pos, uint16_t
  * :5248-5313) in its integer form. */
 int pb_prefill_chunk(pb_model* m, pb_state* s, const int* d_tokens, int T, int pos0, int* d_ids,
                      float* d_logits, void* stream);
+/* one decode step of B independent sequences (B a multiple of 16, at most
+ * 256; batched decode, the multi-stream form of the reference's step loop):
+ * sequence b is states[b] (a host array of states of model m) at position
+ * d_pos[b] fed d_tokens[b] (device int32 [B]). Every projection and the head
+ * is one integer-path GEMM over the B sequences on the tensor cores; each
+ * sequence's values are those of its own decode step on the integer path.
+ * d_ids (device int32 [B]) receives the greedy ids, d_logits (optional,
+ * fp32 [B][vocab]) the logits; each state's caches and rings advance by one
+ * position. The step's scratch is states[0]'s prefill workspace. */
+int pb_decode_batch(pb_model* m, pb_state* const* states, int B, const int* d_tokens, const int* d_pos,
+                    int* d_ids, float* d_logits, void* stream);
 /* synchronise `stream` and report a decode failure recorded on the device
  * (a bounded wait inside the decode kernel that gave up): PB_OK or PB_ECUDA */
 int pb_state_status(pb_state* s, void* stream);

@@ -1778,3 +1778,129 @@ extern "C" int pb_prefill_chunk(pb_model* m, pb_state* s, const int* d_tokens, i
   return PB_OK;
 }
 
+
+// ------------------------------------------------------------ batched decode
+namespace {
+struct BatchTable {
+  std::mutex mu;
+  std::vector<pb_state*> key;
+  SeqPtrs* d = nullptr;
+  size_t cap = 0;
+};
+BatchTable g_bt;
+}  // namespace
+
+// One decode step of B independent sequences (B a multiple of 16, at most
+// 256), each at its own position, every projection (and the head) one
+// integer-path GEMM on the tensor cores over the B sequences: the per
+// sequence values equal the decode step's with the integer path (the
+// oracle's integer mode). states: B states of model m (host array); d_tokens,
+// d_pos: device int32 [B]; d_ids (device int32 [B]) receives the greedy ids,
+// d_logits (optional, fp32 [B][vocab]) the logits. The states' caches and
+// rings advance by one position each. Compiled for the LFM3 2B shape.
+extern "C" int pb_decode_batch(pb_model* m, pb_state* const* states, int B, const int* d_tokens, const int* d_pos,
+                               int* d_ids, float* d_logits, void* stream) {
+  if (!m || !states || !d_tokens || !d_pos || !d_ids || B <= 0) return pb_set_error(PB_EINVAL, "pb_decode_batch: bad argument");
+  if (B % 16 || B > 256) return pb_set_error(PB_ENOTSUP, "pb_decode_batch: B=%d (a multiple of 16, at most 256)", B);
+  if (m->H != 2048 || m->HD != 64 || m->W != 3 || m->F % 256 || m->F / 256 > 32 || (m->NH * m->HD) != 2048)
+    return pb_set_error(PB_ENOTSUP, "pb_decode_batch: shape not compiled");
+  if (!m->decode_ok) return pb_set_error(PB_ENOTSUP, "pb_decode_batch: needs every K a multiple of 2048");
+  int max_ctx = 0;
+  for (int b = 0; b < B; b++) {
+    if (!states[b] || states[b]->m != m) return pb_set_error(PB_EINVAL, "pb_decode_batch: state %d is not of this model", b);
+    max_ctx = std::max(max_ctx, states[b]->max_ctx);
+  }
+  PB_TRY_CUDA(cudaSetDevice(m->device));
+  cudaStream_t st = (cudaStream_t)stream;
+  pb_state* ws = states[0];        // its prefill buffers are the step's workspace
+  int rc = prefill_prepare(m, ws, B, st);
+  if (rc) return rc;
+  const SeqPtrs* seq = nullptr;
+  {
+    std::lock_guard<std::mutex> lk(g_bt.mu);
+    std::vector<pb_state*> key(states, states + B);
+    if (key != g_bt.key) {
+      std::vector<SeqPtrs> h(B);
+      for (int b = 0; b < B; b++) {
+        const pb_state* s = states[b];
+        h[b].kv = s->kv; h[b].ring = s->ring; h[b].rope_cos = s->rope_cos; h[b].rope_sin = s->rope_sin;
+        h[b].max_ctx = s->max_ctx; h[b]._pad = 0;
+      }
+      if (g_bt.cap < (size_t)B) {
+        PB_TRY_CUDA(cudaDeviceSynchronize());   // the table may still be read by a step in flight
+        cudaFree(g_bt.d);
+        g_bt.d = nullptr;
+        g_bt.cap = 0;
+        if (cudaMalloc(&g_bt.d, 256 * sizeof(SeqPtrs)) != cudaSuccess) {
+          cudaGetLastError();
+          return pb_set_error(PB_ENOMEM, "pb_decode_batch: sequence table");
+        }
+        g_bt.cap = 256;
+      } else {
+        PB_TRY_CUDA(cudaStreamSynchronize(st));
+      }
+      PB_TRY_CUDA(cudaMemcpy(g_bt.d, h.data(), B * sizeof(SeqPtrs), cudaMemcpyHostToDevice));
+      g_bt.key = key;
+    }
+    seq = g_bt.d;
+  }
+  const int H = m->H, F = m->F;
+  const int nq = m->NH * m->HD + 2 * m->NKV * m->HD + m->NH;
+  for (int L = 0; L < m->L; L++) {
+    const Layer& Ly = m->layers[L];
+    const pb_q8* tc = &m->tc[(size_t)L * 4];
+    if (L == 0) rc = pf_norm(m, ws, B, d_tokens, nullptr, nullptr, Ly.op_norm, st);
+    else rc = pf_norm(m, ws, B, nullptr, ws->pf_y, m->layers[L - 1].post_ffn_norm, Ly.op_norm, st);
+    if (rc) return rc;
+    if ((rc = pb_q80_gemm(&tc[0], B, ws->pf_qx, ws->pf_dx, ws->pf_y, nullptr, st))) return rc;
+    if (Ly.attn) {
+      BdArgs a = {};
+      a.seq = seq;
+      a.pos = d_pos;
+      a.y = ws->pf_y;
+      a.qkvg = ws->pf_qkvg;
+      a.qnorm = Ly.q_norm;
+      a.knorm = Ly.k_norm;
+      a.att = ws->pf_att;
+      a.attn_idx = Ly.attn_idx;
+      a.nq = nq; a.nh = m->NH; a.nkv = m->NKV; a.half = half_rot(m); a.win = m->win;
+      a.eps = m->eps;
+      a.scaling = 1.0f / sqrtf((float)m->HD);
+      k_bd_qkv<2><<<B, 256, 0, st>>>(a);
+      PB_LAUNCHED("k_bd_qkv");
+      PB_TRY_CUDA(cudaFuncSetAttribute(k_bd_attn<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, 160 * 1024));
+      k_bd_attn<2><<<dim3(m->NH, B), 256, (size_t)max_ctx * sizeof(float), st>>>(a);
+      PB_LAUNCHED("k_bd_attn");
+      k_pf_quant<8><<<B, 256, 0, st>>>(ws->pf_att, m->NH * m->HD, ws->pf_qx, ws->pf_dx);
+      PB_LAUNCHED("k_pf_quant");
+    } else {
+      BdConvArgs c = {};
+      c.seq = seq;
+      c.pos = d_pos;
+      c.y = ws->pf_y;
+      c.taps = Ly.taps;
+      c.conv_idx = Ly.conv_idx;
+      c.H = H;
+      c.qx = ws->pf_qx;
+      c.dx = ws->pf_dx;
+      k_bd_conv_quant<8, 3><<<B, 256, 0, st>>>(c);
+      PB_LAUNCHED("k_bd_conv_quant");
+    }
+    if ((rc = pb_q80_gemm(&tc[1], B, ws->pf_qx, ws->pf_dx, ws->pf_y, nullptr, st))) return rc;
+    if ((rc = pf_norm(m, ws, B, nullptr, ws->pf_y, Ly.post_op_norm, Ly.ffn_norm, st))) return rc;
+    if ((rc = pb_q80_gemm(&tc[2], B, ws->pf_qx, ws->pf_dx, ws->pf_y, nullptr, st))) return rc;
+    switch (F / 256) {
+      case 8: k_pf_silu_quant<8><<<B, 256, 0, st>>>(ws->pf_y, F, ws->pf_qx, ws->pf_dx); break;
+      case 16: k_pf_silu_quant<16><<<B, 256, 0, st>>>(ws->pf_y, F, ws->pf_qx, ws->pf_dx); break;
+      default: k_pf_silu_quant<32><<<B, 256, 0, st>>>(ws->pf_y, F, ws->pf_qx, ws->pf_dx); break;
+    }
+    PB_LAUNCHED("k_pf_silu_quant");
+    if ((rc = pb_q80_gemm(&tc[3], B, ws->pf_qx, ws->pf_dx, ws->pf_y, nullptr, st))) return rc;
+  }
+  if ((rc = pf_norm(m, ws, B, nullptr, ws->pf_y, m->layers[m->L - 1].post_ffn_norm, m->final_norm, st))) return rc;
+  float* lg = d_logits ? d_logits : ws->pf_logits;
+  if ((rc = pb_q80_gemm(&m->tc.back(), B, ws->pf_qx, ws->pf_dx, lg, nullptr, st))) return rc;
+  k_pf_argmax<<<B, 256, 0, st>>>(lg, m->V, d_ids);
+  PB_LAUNCHED("k_pf_argmax");
+  return PB_OK;
+}

@@ -251,3 +251,126 @@ __global__ void __launch_bounds__(256) k_pf_argmax(const float* __restrict__ lg,
 }
 
 }  // namespace
+
+// ----------------------------------------------------------- batched decode
+// B independent sequences, one position each: the projections are the same
+// tensor-core GEMMs (T = B), every per-position step reads and writes its
+// own sequence's state.
+namespace {
+
+struct SeqPtrs {
+  unsigned short* kv;       // [n_attn][2][max_ctx][NKV][HD]
+  bf16_t* ring;             // [n_conv][W][H]
+  const float* rope_cos;    // [max_ctx][half]
+  const float* rope_sin;
+  int max_ctx;
+  int _pad;
+};
+
+struct BdArgs {
+  const SeqPtrs* seq;       // [B]
+  const int* pos;           // [B]
+  const float* y;           // [B][nq] projection outputs
+  bf16_t* qkvg;             // [B][nq]
+  const float* qnorm;
+  const float* knorm;
+  bf16_t* att;              // [B][NH*HD]
+  int attn_idx, nq, nh, nkv, half, win;
+  float eps, scaling;
+};
+
+// per sequence: the bf16 projection row and its new K/V rows
+template <int E>
+__global__ void __launch_bounds__(256) k_bd_qkv(BdArgs p) {
+  constexpr int HD = 32 * E;
+  __shared__ float ks[8][HD];
+  const int b = blockIdx.x, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  for (int i = threadIdx.x; i < p.nq; i += blockDim.x)
+    p.qkvg[(size_t)b * p.nq + i] = pb_f2bf(p.y[(size_t)b * p.nq + i]);
+  __syncthreads();
+  const SeqPtrs sq = p.seq[b];
+  const int pos = p.pos[b];
+  const size_t per = (size_t)sq.max_ctx * p.nkv * HD;
+  unsigned short* kc = sq.kv + (size_t)p.attn_idx * 2 * per;
+  unsigned short* vc = kc + per;
+  const size_t koff = (size_t)p.nh * HD, voff = koff + (size_t)p.nkv * HD;
+  const bf16_t* row = p.qkvg + (size_t)b * p.nq;
+  for (int kvh = warp; kvh < p.nkv; kvh += 8) {
+    head_norm_rope<E, 0>(row + koff + (size_t)kvh * HD, p.knorm, sq.rope_cos + (size_t)pos * p.half,
+                         sq.rope_sin + (size_t)pos * p.half, p.half, p.eps, ks[warp]);
+#pragma unroll
+    for (int j = 0; j < E; j++) {
+      const int i = lane * E + j;
+      kc[((size_t)pos * p.nkv + kvh) * HD + i] = pb_f2h(ks[warp][i]);
+      vc[((size_t)pos * p.nkv + kvh) * HD + i] = pb_f2h(pb_bf2f(row[voff + (size_t)kvh * HD + i]));
+    }
+    __syncwarp();
+  }
+}
+
+// CTA (head, sequence): the decode's per-head attention over that sequence's cache
+template <int E>
+__global__ void __launch_bounds__(256) k_bd_attn(BdArgs p) {
+  constexpr int HD = 32 * E;
+  extern __shared__ __align__(16) float sl[];     // scores [max_ctx of the longest sequence]
+  __shared__ float qv[HD], kv[HD], vv[HD];
+  __shared__ float red[8];
+  __shared__ float segred[8 * HD];
+  const int b = blockIdx.y;
+  const SeqPtrs sq = p.seq[b];
+  AttnArgs a = {};
+  a.qkvg = p.qkvg + (size_t)b * p.nq;
+  a.qnorm = p.qnorm;
+  a.knorm = p.knorm;
+  a.rope_cos = sq.rope_cos;
+  a.rope_sin = sq.rope_sin;
+  const size_t per = (size_t)sq.max_ctx * p.nkv * HD;
+  a.kc = sq.kv + (size_t)p.attn_idx * 2 * per;
+  a.vc = a.kc + per;
+  a.out = p.att + (size_t)b * p.nh * HD;
+  a.nh = p.nh; a.nkv = p.nkv; a.half = p.half; a.win = p.win; a.max_ctx = sq.max_ctx;
+  a.scaling = p.scaling;
+  a.eps = p.eps;
+  attn_body<E, 0>(a, blockIdx.x, p.pos[b], sl, qv, kv, vv, segred, red);
+}
+
+struct BdConvArgs {
+  const SeqPtrs* seq;
+  const int* pos;
+  const float* y;       // [B][3H]
+  const float* taps;
+  int conv_idx, H;
+  int8_t* qx;
+  uint16_t* dx;
+};
+
+// per sequence: the gated short conv with its own ring (the step's pro_conv),
+// the new ring slot, and the quantised output
+template <int E, int W>
+__global__ void __launch_bounds__(256) k_bd_conv_quant(BdConvArgs p) {
+  const int b = blockIdx.x, th = threadIdx.x, H = p.H;
+  const int pos = p.pos[b];
+  bf16_t* ring = p.seq[b].ring + (size_t)p.conv_idx * W * H;
+  const float* yr = p.y + (size_t)b * 3 * H;
+  float out[E], bxv[E];
+#pragma unroll
+  for (int j = 0; j < E; j++) {
+    const int i = th * E + j;
+    const float bx = pb_bf2f(pb_f2bf(__fmul_rn(pb_bf2f(pb_f2bf(yr[i])), pb_bf2f(pb_f2bf(yr[2 * H + i])))));
+    bxv[j] = bx;
+    float acc = 0.0f;
+#pragma unroll
+    for (int k = 0; k < W; k++) {
+      const int pp = pos - (W - 1) + k;
+      const float v = k == W - 1 ? bx : pb_bf2f(ring[(size_t)(((pp % W) + W) % W) * H + i]);
+      acc = __fadd_rn(acc, __fmul_rn(p.taps[(size_t)i * W + k], v));
+    }
+    out[j] = pb_bf2f(pb_f2bf(__fmul_rn(pb_bf2f(pb_f2bf(yr[H + i])), pb_bf2f(pb_f2bf(acc)))));
+  }
+  // the slot of this position held position pos - W, read by no one any more
+#pragma unroll
+  for (int j = 0; j < E; j++) ring[(size_t)(pos % W) * H + th * E + j] = pb_f2bf(bxv[j]);
+  pf_quant_store<E>(out, p.qx + (size_t)b * H, p.dx + (size_t)b * (H / 32), th);
+}
+
+}  // namespace

@@ -101,6 +101,7 @@ def lib():
     L.pb_layer_step_noalloc.argtypes = [vp, vp, i, i, vp, vp]
     L.pb_state_status.argtypes = [vp, vp]
     L.pb_prefill_chunk.argtypes = [vp, vp, vp, i, i, vp, vp, vp]
+    L.pb_decode_batch.argtypes = [vp, C.POINTER(vp), i, vp, vp, vp, vp, vp]
     _lib = L
     return L
 
@@ -257,6 +258,13 @@ class Model:
         if r < 0:
             raise PBError(r, last_error())
         return r
+
+    def decode_batch(self, states, tokens, pos, ids, logits=None, stream=None):
+        """one integer-path decode step of len(states) sequences: device int32
+        tokens [B] and positions [B]; ids (device int32 [B]) receives the greedy ids"""
+        arr = (C.c_void_p * len(states))(*[st.h.value if isinstance(st.h, C.c_void_p) else st.h for st in states])
+        check(lib().pb_decode_batch(self.h, arr, len(states), _ptr(tokens), _ptr(pos), _ptr(ids), _ptr(logits),
+                                    _stream(stream)))
 
     def new_state(self, max_ctx):
         return State(self, max_ctx)
