@@ -14,6 +14,7 @@ flush is needed between steps.
 """
 import argparse
 import json
+import numpy as np
 import os
 import statistics
 import subprocess
@@ -288,6 +289,47 @@ def prefill_bench(torch, model, prompt, stream, T=32):
             "path": "integer (Q8_0 activations, tcgen05 kind::i8 GEMMs)"}
 
 
+def batch_bench(torch, model, c, stream, B=64, steps=10):
+    """cfg4: B independent sequences with ragged contexts drawn uniformly from
+    [16, 2048] (seeded, rounded up to multiples of 16 for the chunked prefill
+    that fills them), then `steps` batched decode steps (one integer-path
+    tensor-core GEMM per projection over the batch), timed by CUDA events"""
+    rng = np.random.default_rng(SEED + 4)
+    ctx = ((rng.integers(16, 2049, B) + 15) // 16) * 16
+    g = torch.Generator().manual_seed(SEED + 5)
+    states = []
+    with torch.cuda.stream(stream):
+        for b in range(B):
+            st = model.new_state(int(ctx[b]) + steps + 16)
+            toks = torch.randint(0, c["vocab"], (int(ctx[b]),), generator=g, dtype=torch.int32).cuda()
+            for p0 in range(0, int(ctx[b]), 64):
+                n = min(64, int(ctx[b]) - p0)
+                st.prefill_chunk(toks[p0:p0 + n], p0, stream=stream)
+            states.append(st)
+        stream.synchronize()
+        tokens = torch.randint(0, c["vocab"], (B,), generator=g, dtype=torch.int32).cuda()
+        pos = torch.from_numpy(ctx.astype(np.int32)).cuda()
+        ids = torch.empty(B, dtype=torch.int32, device="cuda")
+        model.decode_batch(states, tokens, pos, ids, stream=stream)      # warm-up step
+        pos += 1
+        tokens = ids.clone()
+        stream.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(steps):
+            model.decode_batch(states, tokens, pos, ids, stream=stream)
+            pos += 1
+            tokens.copy_(ids)
+        e1.record(stream)
+        e1.synchronize()
+    for st in states:
+        st.status(stream)
+        st.destroy()
+    ms = e0.elapsed_time(e1)
+    return {"sequences": B, "steps": steps, "mean_ctx": float(ctx.mean()), "ms_per_step": ms / steps,
+            "tok/s": B * steps / (ms / 1e3), "path": "integer (Q8_0 activations, tcgen05 kind::i8 GEMMs, N = 64)"}
+
+
 def run_reference(args, rank, world):
     """--impl reference: the reference's CPU implementation of this path (the
     oracle port: the reference's decode engine has no CPU form) on this box's
@@ -429,6 +471,7 @@ def main():
     if rank == 0 and world == 1 and not args.no_kernels:
         line["kernels"] = kernel_suite(torch, pb, peak, stream)
         line["kernels"]["cfg2_prefill"] = prefill_bench(torch, model, prompt, stream)
+        line["kernels"]["cfg4_batched_decode"] = batch_bench(torch, model, c, stream)
     if rank == 0 and world == 1 and not args.no_cpu:
         tps, cores, n, _ = cpu_baseline(c, weights, args.ctx, args.cpu_seconds)
         line["cpu_baseline"] = {"value": tps, "unit": "tok/s", "cores": cores, "kind": "port",
