@@ -70,11 +70,12 @@ PB_DEV bool mb_try(uint64_t* b, unsigned par) {
   return ok != 0;
 }
 // bounded wait; false when it gave up or another role aborted
+// (try_wait itself suspends the thread until the phase completes or a short
+// hardware time limit passes, so the loop needs no sleep)
 PB_DEV bool mb_wait(uint64_t* b, unsigned par, volatile int* abort_f) {
   for (unsigned i = 0; i < TC_WAIT; i++) {
     if (mb_try(b, par)) return true;
     if ((i & 255) == 255 && *abort_f) return false;
-    if (i > 64) __nanosleep(32);
   }
   return false;
 }
