@@ -330,6 +330,80 @@ def batch_bench(torch, model, c, stream, B=64, steps=10):
             "tok/s": B * steps / (ms / 1e3), "path": "integer (Q8_0 activations, tcgen05 kind::i8 GEMMs, N = 64)"}
 
 
+def bonsai_bench(torch, pb, peak, stream, steps=20, warmup=3):
+    """cfg3: the Bonsai-8B-shaped Q1_0 decoder (36 layers, hidden 4096, 32/8
+    heads x 128, FFN 12288, vocab 151936, tied head) over an f16 K/V cache
+    filled to just below 2048 positions; `warmup` + `steps` greedy tokens end
+    at position 2047 (each step's CUDA graph: 364 kernels). Weights are
+    seeded on the device (uniform sign bits, fp16 scales |N(0,1)|*0.02), the
+    cache with N(0,1) f16 rows. Also timed end to end through the public
+    call with a host token in and the host id out per step."""
+    from pulsar_b200 import synth
+    c = dict(synth.BONSAI_CFG3)
+    max_ctx = 2048
+    g = torch.Generator(device="cuda").manual_seed(SEED + 3)
+    H, F, NH, NKV = c["hidden"], c["inter"], c["n_heads"], c["n_kv"]
+    m = pb.Bonsai(c)
+
+    def q1(rows, K):
+        b = torch.randint(0, 256, (rows, K // 128, 18), dtype=torch.uint8, device="cuda", generator=g)
+        sc = (torch.randn((rows, K // 128), device="cuda", generator=g).abs() * 0.02).half()
+        b[:, :, :2].copy_(sc.view(torch.uint8).view(rows, K // 128, 2))
+        return b
+
+    def norm(n):
+        return (1.0 + 0.05 * torch.randn(n, generator=torch.Generator().manual_seed(n))).numpy()
+    st = pb._stream(stream)
+    shapes = {0: (NH * 128, H), 1: (NKV * 128, H), 2: (NKV * 128, H), 3: (H, NH * 128),
+              4: (F, H), 5: (F, H), 6: (H, F)}
+    for L in range(c["n_layers"]):
+        for slot, (r, k) in shapes.items():
+            m.set_q1(L, slot, q1(r, k), st)
+        for slot, n in ((0, H), (1, H), (2, 128), (3, 128)):
+            m.set_norm(L, slot, norm(n), st)
+    m.set_q1(-1, 16, q1(c["vocab"], H), st)
+    m.set_norm(-1, 16, norm(H), st)
+    s = m.new_state(max_ctx)
+    pos0 = max_ctx - (warmup + steps)
+    for L in range(c["n_layers"]):
+        for which in (0, 1):
+            kv = s.kv(L, which)
+            kv.copy_(torch.randn(kv.shape, device="cuda", generator=g).half().view(torch.int16))
+            kv[:, pos0:].zero_()
+    ids = torch.empty(warmup + steps, dtype=torch.int32, device="cuda")
+    with torch.cuda.stream(stream):
+        s.decode_greedy(7, pos0, warmup, ids[:warmup], stream=stream)
+        nxt = int(ids[warmup - 1].item())
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        s.decode_greedy(nxt, pos0 + warmup, steps, ids[warmup:], stream=stream)
+        e1.record(stream)
+        e1.synchronize()
+        ms = e0.elapsed_time(e1)
+        # end to end: the same positions again through the per-token public call
+        tok = nxt
+        e2, e3 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e2.record(stream)
+        for i in range(steps):
+            tok = s.decode(tok, pos0 + warmup + i, stream=stream)
+        e3.record(stream)
+        e3.synchronize()
+        ms_e2e = e2.elapsed_time(e3)
+    fb = s.fallbacks()
+    ctx_mean = pos0 + warmup + (steps + 1) / 2.0
+    nbytes = synth.bonsai_bytes_per_token(c, ctx_mean)
+    step_s = ms / 1e3 / steps
+    s.destroy()
+    m.close()
+    return {"model": "Bonsai-8B shape, Q1_0, 36 layers, vocab 151936", "steps": steps, "warmup": warmup,
+            "positions": [pos0 + warmup, pos0 + warmup + steps - 1], "mean_ctx": ctx_mean,
+            "ms_per_token": ms / steps, "tok/s": steps / (ms / 1e3),
+            "e2e_tok/s": steps / (ms_e2e / 1e3), "bytes_per_token": nbytes,
+            "GB/s": nbytes / step_s / 1e9, "frac": nbytes / step_s / 1e9 / peak,
+            "kernels_per_token": 36 * 10 + 4, "rms_serial_fallbacks": fb,
+            "path": "CUDA graph of PDL launches: Q1_0 x Q8_K GEMVs, f16 flash-attention decode in fork order"}
+
+
 def run_reference(args, rank, world):
     """--impl reference: the reference's CPU implementation of this path (the
     oracle port: the reference's decode engine has no CPU form) on this box's
@@ -472,6 +546,7 @@ def main():
         line["kernels"] = kernel_suite(torch, pb, peak, stream)
         line["kernels"]["cfg2_prefill"] = prefill_bench(torch, model, prompt, stream)
         line["kernels"]["cfg4_batched_decode"] = batch_bench(torch, model, c, stream)
+        line["kernels"]["cfg3_decode"] = bonsai_bench(torch, pb, peak, stream)
     if rank == 0 and world == 1 and not args.no_cpu:
         tps, cores, n, _ = cpu_baseline(c, weights, args.ctx, args.cpu_seconds)
         line["cpu_baseline"] = {"value": tps, "unit": "tok/s", "cores": cores, "kind": "port",

@@ -208,6 +208,59 @@ int pb_decode_kernels_per_token(pb_state* s);
 int pb_time_step_kernel(pb_model* m, pb_state* s, int which, int iters, float* ms, double* bytes,
                         void* stream);
 
+/* ------------------------------------------------------- Bonsai decoder ---- *
+ * The Q1_0 token step of pulsar_arm/bonsai2/fwd8.c (Qwen3-style dense GQA
+ * layers, head_dim 128, f16 K/V cache): per layer rms -> q|k|v -> head norms +
+ * YaRN rope -> f16 flash-attention decode in the fork's order (pq1_host.c:
+ * 404-434) -> o -> rms -> gate|up -> silu(g)*u -> down; output norm, head,
+ * greedy argmax. Replaces the device side of pq1_token_fused
+ * (pq1_fwd8_shim.h:44-51, pq1_fwd8_glue.c:1530) with device-pointer calls.
+ * Shapes: hidden and inter multiples of 256 (hidden <= 8192), n_heads/n_kv
+ * even and <= 8.                                                              */
+typedef struct pb_bonsai pb_bonsai;
+typedef struct pb_bonsai_state pb_bonsai_state;
+typedef struct {
+  int hidden, inter, n_layers, n_heads, n_kv, vocab;
+  float rope_factor;   /* YaRN factor (fwd8.c:51: 4) */
+  int rope_orig_ctx;   /* YaRN original context (fwd8.c:56: 16384 for the 8B) */
+  float rope_base;     /* fwd8.c:57: 1e6 for the 8B */
+  float attn_scale;    /* fwd8.c:566: 0.0883883476 */
+} pb_bonsai_cfg;
+/* tensor slots: the 7 per-layer tensors in pq1_token_fused's wt order, then
+ * the layer -1 tensors (token_embd; output.weight, absent = tied) */
+enum { PB_BS_Q = 0, PB_BS_K, PB_BS_V, PB_BS_O, PB_BS_GATE, PB_BS_UP, PB_BS_DOWN,
+       PB_BS_EMBED = 16, PB_BS_HEAD = 17 };
+/* norm slots in pq1_token_fused's nw order, then output_norm (layer -1) */
+enum { PB_BS_ATTN_NORM = 0, PB_BS_FFN_NORM, PB_BS_Q_NORM, PB_BS_K_NORM, PB_BS_OUT_NORM = 16 };
+int pb_bonsai_create(const pb_bonsai_cfg* cfg, int device, pb_bonsai** out);
+int pb_bonsai_destroy(pb_bonsai* m);
+/* Q1_0 18-byte blocks [rows][K/128] (GGUF layout, pq1_wrap.h:24-26) of one
+ * tensor; q|k|v and gate|up are merged into one matrix each on the device */
+int pb_bonsai_set_q1(pb_bonsai* m, int layer, int slot, const uint8_t* blocks, int src_on_device,
+                     void* stream);
+/* fp32 norm weights: hidden values (attn, ffn, output) or 128 (q, k) */
+int pb_bonsai_set_norm(pb_bonsai* m, int layer, int slot, const float* w, int src_on_device,
+                       void* stream);
+/* per sequence: K/V cache [layer][K|V][n_kv][max_ctx][128] f16 and the rope
+ * table of every position (max_ctx a multiple of 32, <= 8192) */
+int pb_bonsai_state_create(pb_bonsai* m, int max_ctx, pb_bonsai_state** out);
+int pb_bonsai_state_destroy(pb_bonsai_state* s);
+/* device address of one layer's K (which 0) or V (which 1) cache [n_kv][max_ctx][128] */
+int pb_bonsai_state_kv(pb_bonsai_state* s, int layer, int which, void** d_ptr);
+/* copy the residual stream after the last step (fp32 [hidden]) */
+int pb_bonsai_state_residual(pb_bonsai_state* s, float* d_x, void* stream);
+/* RMS norms that fell back to the serial double chain since creation */
+int pb_bonsai_state_fallbacks(pb_bonsai_state* s, int* out);
+/* one token at position pos: the embedding row of `token`, or d_x (fp32
+ * [hidden], the caller's row, as pq1_token_fused receives it) when non-null.
+ * d_logits (fp32 [vocab]) and out_id (host, synchronises) are optional. */
+int pb_bonsai_decode(pb_bonsai* m, pb_bonsai_state* s, int token, int pos, const float* d_x,
+                     float* d_logits, int* out_id, void* stream);
+/* n greedy tokens from (token, pos), each step's id fed back on the device;
+ * d_ids (int [n]) receives them; synchronises */
+int pb_bonsai_decode_greedy(pb_bonsai* m, pb_bonsai_state* s, int token, int pos, int n, int* d_ids,
+                            void* stream);
+
 #ifdef __cplusplus
 }
 #endif

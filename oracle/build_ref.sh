@@ -15,6 +15,8 @@
 #   q8_gemv_cpu.c (whole file)  gemv_q8 / quant_row (main renamed away)
 #   lfm3_nanode.cu:4598-4603    cpu_f2bf / cpu_bf2f
 #   lfm3_nanode.cu:4658-4684    cpuchk_run's scalar leaf-order transcription
+#   fwd8.c:312-317, 320-369     rms, YaRN rope table and rotation (8B constants)
+#   pq1_host.c:373-434, 226     pq1_fa16_head (f16 flash-attention decode), silu tail
 #
 # Needs the reference checkout (default /root/reference, override with
 # PB_REFERENCE_ROOT). Without it this script does nothing and exits 0.
@@ -104,6 +106,39 @@ EOF
   printf '  return c.bad;\n}\n'
 } | "$CXX" -O2 -fPIC -ffp-contract=off -w -x c++ -c -o "$out/pins_cpuchk.o" -
 
-"$CXX" -shared -fopenmp -o "$out/libpb_refpins.so" "$out/pins_bonsai.o" "$out/pins_q8cpu.o" "$out/pins_cpuchk.o" -lm
+# --- D: fwd8.c's rms and YaRN rope, built with gcc's default contraction as
+#        the reference's own build is (8B constants, fwd8.c:51-57) -------------
+{
+  printf '#include <stdint.h>\n#include <math.h>\n#define YARN_FACTOR 4.0f\n#define YARN_ORIG 16384\n#define FREQ_BASE 1000000.0f\n'
+  sed -n '312,317p' "$B2/fwd8.c"
+  sed -n '320,369p' "$B2/fwd8.c"
+  cat <<'EOF'
+void pbref_bs_rms(const float* x, const float* w, int n, float* y) { rms(x, w, n, y); }
+void pbref_bs_rope_table(int pos, float* c, float* s) {
+  rope_table(pos);
+  for (int j = 0; j < 64; j++) { c[j] = RC_C[j]; s[j] = RC_S[j]; }
+}
+void pbref_bs_rope(float* x, int heads, int pos) { rope_yarn_apply(x, heads, pos); }
+EOF
+} | "$CC" -O2 -fPIC -ffp-contract=fast -mfma -w -x c -c -o "$out/pins_fwd8.o" -
+
+# --- E: pq1_host.c's f16 flash-attention decode and scalar silu tail, built
+#        -ffp-contract=off as the reference builds that file; expf goes through
+#        a hook (default libm) that the tests may point at the oracle's -----------
+{
+  printf '#include <stdint.h>\n#include <string.h>\n#include <math.h>\n#include <stddef.h>\n'
+  printf 'float (*pbref_expf_hook)(float) = 0;\n'
+  printf 'static float pbref_expf(float x) { return pbref_expf_hook ? pbref_expf_hook(x) : expf(x); }\n'
+  printf '#define expf pbref_expf\n#define __fp16 _Float16\n'
+  sed -n '373,434p' "$B2/pq1_host.c"
+  printf 'void pbref_silu_mul(float* lu, const float* lg, int n) {\n  int i = 0;\n'
+  sed -n '226p' "$B2/pq1_host.c"
+  printf '}\n'
+  printf 'void pbref_fa16_head(const float* q, const uint16_t* K, const uint16_t* V, int T, float scale, float* out) {\n'
+  printf '  pq1_fa16_head(q, K, V, T, scale, out);\n}\n'
+} | "$CC" $CFL -x c -c -o "$out/pins_fa16.o" -
+
+"$CXX" -shared -fopenmp -o "$out/libpb_refpins.so" "$out/pins_bonsai.o" "$out/pins_q8cpu.o" "$out/pins_cpuchk.o" \
+    "$out/pins_fwd8.o" "$out/pins_fa16.o" -lm
 rm -f "$out"/pins_*.o
 echo "build_ref: built $out/libpb_refpins.so"

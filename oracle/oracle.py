@@ -35,6 +35,13 @@ class _Cfg(C.Structure):
                [(n, C.c_float) for n in ("rope_theta", "rope_partial", "norm_eps")]
 
 
+class _BsCfg(C.Structure):
+    _fields_ = [(n, C.c_int) for n in ("hidden", "inter", "n_layers", "n_heads", "n_kv", "vocab",
+                                       "max_ctx")] + \
+               [("rope_factor", C.c_float), ("rope_orig_ctx", C.c_int), ("rope_base", C.c_float),
+                ("attn_scale", C.c_float)]
+
+
 def lib():
     global _lib
     if _lib is None:
@@ -74,6 +81,19 @@ def lib():
         L.pbo_state_kv.restype = vp; L.pbo_state_kv.argtypes = [vp, i, i]
         L.pbo_state_ring.restype = vp; L.pbo_state_ring.argtypes = [vp, i]
         L.pbo_threads.restype = i
+        L.pbo_bs_rms.argtypes = [vp, vp, i, vp]
+        L.pbo_bs_rope_table.argtypes = [i, f, i, f, vp, vp]
+        L.pbo_bs_rope.argtypes = [vp, i, vp, vp]
+        L.pbo_bs_fa16_head.argtypes = [vp, vp, vp, i, f, vp]
+        L.pbo_bs_silu_mul.argtypes = [vp, vp, i]
+        L.pbo_bs_model_new.restype = vp; L.pbo_bs_model_new.argtypes = [C.POINTER(_BsCfg)]
+        L.pbo_bs_model_free.argtypes = [vp]
+        L.pbo_bs_model_set_q1.argtypes = [vp, i, i, vp, i, i]
+        L.pbo_bs_model_set_f32.argtypes = [vp, i, i, vp]
+        L.pbo_bs_state_new.restype = vp; L.pbo_bs_state_new.argtypes = [vp]
+        L.pbo_bs_state_free.argtypes = [vp]
+        L.pbo_bs_state_kv.restype = vp; L.pbo_bs_state_kv.argtypes = [vp, i, i]
+        L.pbo_bs_decode.restype = i; L.pbo_bs_decode.argtypes = [vp, vp, i, i, vp, vp, vp]
         _lib = L
     return _lib
 
@@ -97,6 +117,11 @@ def ref():
         R.pbref_quant_row.argtypes = [vp, i, vp, vp]
         R.pbref_cpuchk.restype = C.c_long
         R.pbref_cpuchk.argtypes = [vp, vp, vp, vp, i, i, i, i]
+        R.pbref_bs_rms.argtypes = [vp, vp, i, vp]
+        R.pbref_bs_rope_table.argtypes = [i, vp, vp]
+        R.pbref_bs_rope.argtypes = [vp, i, i]
+        R.pbref_fa16_head.argtypes = [vp, vp, vp, i, C.c_float, vp]
+        R.pbref_silu_mul.argtypes = [vp, vp, i]
         _ref = R
     return _ref
 
@@ -250,3 +275,103 @@ def h2f_vec(h):
     if h.dtype == np.uint16:
         h = h.view(np.float16)
     return h.astype(np.float32)
+
+
+# ------------------------------------------------------------------ Bonsai ----
+def bs_rms(x, w):
+    x = np.ascontiguousarray(x, np.float32)
+    y = np.zeros_like(x)
+    lib().pbo_bs_rms(_p(x), _p(np.ascontiguousarray(w, np.float32)), x.shape[0], _p(y))
+    return y
+
+
+def bs_rope_table(pos, factor=4.0, orig_ctx=16384, base=1e6):
+    c = np.zeros(64, np.float32); s = np.zeros(64, np.float32)
+    lib().pbo_bs_rope_table(int(pos), factor, int(orig_ctx), base, _p(c), _p(s))
+    return c, s
+
+
+def bs_rope(x, c, s):
+    x = np.array(x, np.float32)
+    lib().pbo_bs_rope(_p(x), x.shape[0] // 128, _p(np.ascontiguousarray(c)), _p(np.ascontiguousarray(s)))
+    return x
+
+
+def bs_fa16_head(q, K16, V16, scale=0.0883883476):
+    """q fp32 [128]; K16, V16 f16 bits [T][128]"""
+    out = np.zeros(128, np.float32)
+    T = K16.shape[0]
+    lib().pbo_bs_fa16_head(_p(np.ascontiguousarray(q, np.float32)), _p(np.ascontiguousarray(K16, np.uint16)),
+                           _p(np.ascontiguousarray(V16, np.uint16)), T, scale, _p(out))
+    return out
+
+
+def bs_silu_mul(lg, lu):
+    u = np.array(lu, np.float32)
+    lib().pbo_bs_silu_mul(_p(u), _p(np.ascontiguousarray(lg, np.float32)), u.shape[0])
+    return u
+
+
+class BsModel:
+    """Oracle Bonsai decode (fwd8.c) over weights shaped like
+    pulsar_b200.synth.make_bonsai_weights."""
+
+    SLOTS = {"q": 0, "k": 1, "v": 2, "o": 3, "gate": 4, "up": 5, "down": 6}
+    NORMS = {"attn_norm": 0, "ffn_norm": 1, "q_norm": 2, "k_norm": 3}
+
+    def __init__(self, cfg, weights, max_ctx):
+        L = lib()
+        self.cfg = dict(cfg)
+        self.max_ctx = max_ctx
+        self._keep = []
+        c = _BsCfg(cfg["hidden"], cfg["inter"], cfg["n_layers"], cfg["n_heads"], cfg["n_kv"], cfg["vocab"],
+                   max_ctx, cfg["rope_factor"], cfg["rope_orig_ctx"], cfg["rope_base"], cfg["attn_scale"])
+        self.m = L.pbo_bs_model_new(C.byref(c))
+        for li, lw in enumerate(weights["layers"]):
+            for name, slot in self.SLOTS.items():
+                b = np.ascontiguousarray(lw[name], np.uint8)
+                L.pbo_bs_model_set_q1(self.m, li, slot, _p(b), b.shape[0], b.shape[1] * 128)
+            for name, slot in self.NORMS.items():
+                a = np.ascontiguousarray(lw[name], np.float32)
+                self._keep.append(a)
+                L.pbo_bs_model_set_f32(self.m, li, slot, _p(a))
+        e = np.ascontiguousarray(weights["embed"], np.uint8)
+        L.pbo_bs_model_set_q1(self.m, -1, 0, _p(e), e.shape[0], e.shape[1] * 128)
+        if weights.get("head") is not None:
+            hd = np.ascontiguousarray(weights["head"], np.uint8)
+            L.pbo_bs_model_set_q1(self.m, -1, 1, _p(hd), hd.shape[0], hd.shape[1] * 128)
+        on = np.ascontiguousarray(weights["out_norm"], np.float32)
+        self._keep.append(on)
+        L.pbo_bs_model_set_f32(self.m, -1, 0, _p(on))
+        self.s = L.pbo_bs_state_new(self.m)
+
+    def decode(self, token, pos, x_in=None, want_logits=False):
+        """-> (greedy id, logits or None, final residual fp32 [hidden])"""
+        lg = np.zeros(self.cfg["vocab"], np.float32) if want_logits else None
+        x = np.zeros(self.cfg["hidden"], np.float32)
+        xi = None if x_in is None else np.ascontiguousarray(x_in, np.float32)
+        tid = lib().pbo_bs_decode(self.m, self.s, int(token), int(pos), _p(xi) if xi is not None else None,
+                                  _p(lg) if lg is not None else None, _p(x))
+        return tid, lg, x
+
+    def kv(self, layer, which):
+        """the layer's K (0) or V (1) cache, f16 bits [n_kv][max_ctx][128]"""
+        c = self.cfg
+        ptr = lib().pbo_bs_state_kv(self.s, layer, which)
+        n = c["n_kv"] * self.max_ctx * 128
+        return np.ctypeslib.as_array(C.cast(ptr, C.POINTER(C.c_uint16)), shape=(n,)).copy().reshape(
+            c["n_kv"], self.max_ctx, 128)
+
+    def set_kv(self, layer, which, a):
+        """overwrite the layer's K (0) or V (1) cache with f16 bits [n_kv][max_ctx][128]"""
+        c = self.cfg
+        a = np.ascontiguousarray(a, np.uint16)
+        assert a.size == c["n_kv"] * self.max_ctx * 128
+        C.memmove(lib().pbo_bs_state_kv(self.s, layer, which), a.ctypes.data, a.nbytes)
+
+    def __del__(self):
+        try:
+            lib().pbo_bs_state_free(self.s)
+            lib().pbo_bs_model_free(self.m)
+        except Exception:
+            pass

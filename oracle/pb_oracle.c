@@ -599,3 +599,235 @@ int pbo_decode(const pbo_model* m, pbo_state* s, int token, int pos, float* logi
   free(cs); free(sn);
   return id;
 }
+
+/* ================================================================ Bonsai ====
+ * The Q1_0 decode step of pulsar_arm/bonsai2/fwd8.c (Qwen3-style dense GQA
+ * layer, head_dim 128). Departure: expf -> pbo_expf (above), as on the device. */
+
+/* fwd8.c:312-317: s = serial double sum of x*x (the products are exact in
+ * double, so a contracted fma gives the same value); sc = 1/sqrtf(float(s/n) +
+ * 1e-6); y = (x*sc)*w. In place when y == x. */
+void pbo_bs_rms(const float* x, const float* w, int n, float* y) {
+  double s = 0;
+  for (int i = 0; i < n; i++) s = s + (double)x[i] * (double)x[i];
+  const float sc = 1.0f / sqrtf((float)(s / n) + 1e-6f);
+  for (int i = 0; i < n; i++) y[i] = (x[i] * sc) * w[i];
+}
+
+/* fwd8.c:322-358: the YaRN correction range and the 64 (cos, sin) pairs of one
+ * position, the contraction of gcc's default build written out: msc =
+ * fma(0.1, ln factor, 1), th = fma(ti, 1 - ramp, te*ramp). */
+static float bs_corr_dim(int n_ctx, float rot, float base) {
+  return 128 * logf(n_ctx / (rot * 2 * (float)M_PI)) / (2 * logf(base));
+}
+void pbo_bs_rope_table(int pos, float factor, int orig_ctx, float base, float* c, float* s) {
+  const float st = floorf(bs_corr_dim(orig_ctx, 32.0f, base));
+  const float en = ceilf(bs_corr_dim(orig_ctx, 1.0f, base));
+  const float c0 = st > 0 ? st : 0, c1 = en < 127 ? en : 127;
+  const float fs = 1.0f / factor, msc = fmaf(0.1f, logf(factor), 1.0f);
+  const float tscale = powf(base, -2.0f / 128.0f);
+  float theta = (float)pos;
+  for (int j = 0; j < 64; j++, theta *= tscale) {
+    const float y = (j - c0) / fmaxf(0.001f, c1 - c0);
+    const float ramp = 1.0f - fminf(1.0f, fmaxf(0.0f, y));
+    const float ti = fs * theta, te = theta;
+    const float th = fmaf(ti, 1 - ramp, te * ramp);
+    c[j] = cosf(th) * msc;
+    s[j] = sinf(th) * msc;
+  }
+}
+/* fwd8.c:359-369 on NEOX pairs (j, j+64), contracted as gcc emits it
+ * (fmul; fnmsub; fmul; fmadd): x[j] = fma(a, c, -(b*s)), x[j+64] = fma(a, s, b*c) */
+void pbo_bs_rope(float* x, int heads, const float* c, const float* s) {
+  for (int h = 0; h < heads; h++) {
+    float* xh = x + (size_t)h * 128;
+    for (int j = 0; j < 64; j++) {
+      const float a = xh[j], b = xh[j + 64];
+      xh[j] = fmaf(a, c[j], -(b * s[j]));
+      xh[j + 64] = fmaf(a, s[j], b * c[j]);
+    }
+  }
+}
+
+/* pq1_host.c:404-434: one query head over positions 0..T-1 of its kv head with
+ * f16 K/V rows [T][128], the fork's flash-attention decode order: Q rounded to
+ * f16; q.k as 16 fma chains (chain c = elements 16j+c) reduced
+ * ((a_l + a_8+l) + (a_4+l + a_12+l)), ((r0 + r1) + (r2 + r3)); s *= scale;
+ * online softmax with the accumulator rounded to f16 after every update. */
+void pbo_bs_fa16_head(const float* q, const uint16_t* K, const uint16_t* V, int T, float scale,
+                      float* out) {
+  float qh[128], vkq[128];
+  for (int i = 0; i < 128; i++) { qh[i] = pbo_h2f(pbo_f2h(q[i])); vkq[i] = 0.0f; }
+  float S = 0.0f, M = -INFINITY;
+  for (int t = 0; t < T; t++) {
+    const uint16_t *k = K + (size_t)t * 128, *v = V + (size_t)t * 128;
+    float a[16];
+    for (int c = 0; c < 16; c++) a[c] = 0.0f;
+    for (int j = 0; j < 8; j++)
+      for (int c = 0; c < 16; c++) a[c] = fmaf(pbo_h2f(k[16 * j + c]), qh[16 * j + c], a[c]);
+    float r[4];
+    for (int l = 0; l < 4; l++) r[l] = (a[l] + a[8 + l]) + (a[4 + l] + a[12 + l]);
+    float sc = ((r[0] + r[1]) + (r[2] + r[3])) * scale;
+    float ms = 1.0f, vs = 1.0f;
+    const float Mold = M;
+    if (sc > M) {
+      M = sc;
+      ms = pbo_expf(Mold - M);
+      for (int d = 0; d < 128; d++) vkq[d] = pbo_h2f(pbo_f2h(vkq[d] * ms));
+    } else {
+      vs = pbo_expf(sc - M);
+    }
+    for (int d = 0; d < 128; d++) vkq[d] = pbo_h2f(pbo_f2h(fmaf(pbo_h2f(v[d]), vs, vkq[d])));
+    S = fmaf(S, ms, vs);
+  }
+  const float si = S == 0.0f ? 0.0f : 1.0f / S;
+  for (int d = 0; d < 128; d++) out[d] = vkq[d] * si;
+}
+
+/* pq1_host.c:196-227: lu = (g * (1 / (1 + e^-g))) * lu */
+void pbo_bs_silu_mul(float* lu, const float* lg, int n) {
+  for (int i = 0; i < n; i++) lu[i] = (lg[i] * (1.0f / (1.0f + pbo_expf(-lg[i])))) * lu[i];
+}
+
+/* ---- the whole step --------------------------------------------------------- */
+typedef struct { uint32_t* bits; uint16_t* scales; int rows, K; } q1t;
+struct pbo_bs_model {
+  pbo_bs_cfg cfg;
+  q1t (*q)[PBO_BS_NQ1];
+  const float* (*f)[PBO_BS_NF32];
+  q1t emb, head;
+  const float* out_norm;
+};
+struct pbo_bs_state {
+  int n_layers;
+  uint16_t **kc, **vc;   /* [layer] -> [n_kv][max_ctx][128] f16 */
+  float* x;
+};
+pbo_bs_model* pbo_bs_model_new(const pbo_bs_cfg* cfg) {
+  pbo_bs_model* m = (pbo_bs_model*)calloc(1, sizeof *m);
+  m->cfg = *cfg;
+  m->q = calloc((size_t)cfg->n_layers, sizeof *m->q);
+  m->f = calloc((size_t)cfg->n_layers, sizeof *m->f);
+  return m;
+}
+static void q1t_free(q1t* t) { free(t->bits); free(t->scales); t->bits = NULL; t->scales = NULL; }
+void pbo_bs_model_free(pbo_bs_model* m) {
+  if (!m) return;
+  for (int L = 0; L < m->cfg.n_layers; L++)
+    for (int j = 0; j < PBO_BS_NQ1; j++) q1t_free(&m->q[L][j]);
+  q1t_free(&m->emb); q1t_free(&m->head);
+  free(m->q); free(m->f); free(m);
+}
+/* layer -1: slot 0 = token_embd, slot 1 = output.weight (absent: tied) */
+void pbo_bs_model_set_q1(pbo_bs_model* m, int layer, int slot, const uint8_t* blocks, int rows, int K) {
+  q1t t = {malloc((size_t)rows * (K / 32) * 4), malloc((size_t)rows * (K / 128) * 2), rows, K};
+  pbo_q1_repack(blocks, rows, K, t.bits, t.scales);
+  q1t* d = layer < 0 ? (slot == 0 ? &m->emb : &m->head) : &m->q[layer][slot];
+  q1t_free(d);
+  *d = t;
+}
+/* layer -1: the output norm */
+void pbo_bs_model_set_f32(pbo_bs_model* m, int layer, int slot, const float* p) {
+  if (layer < 0) m->out_norm = p; else m->f[layer][slot] = p;
+}
+pbo_bs_state* pbo_bs_state_new(const pbo_bs_model* m) {
+  const pbo_bs_cfg* c = &m->cfg;
+  pbo_bs_state* s = (pbo_bs_state*)calloc(1, sizeof *s);
+  s->n_layers = c->n_layers;
+  s->kc = calloc((size_t)c->n_layers, sizeof(uint16_t*));
+  s->vc = calloc((size_t)c->n_layers, sizeof(uint16_t*));
+  for (int L = 0; L < c->n_layers; L++) {
+    s->kc[L] = calloc((size_t)c->n_kv * c->max_ctx * 128, 2);
+    s->vc[L] = calloc((size_t)c->n_kv * c->max_ctx * 128, 2);
+  }
+  s->x = calloc((size_t)c->hidden, 4);
+  return s;
+}
+void pbo_bs_state_free(pbo_bs_state* s) {
+  if (!s) return;
+  for (int L = 0; L < s->n_layers; L++) { free(s->kc[L]); free(s->vc[L]); }
+  free(s->kc); free(s->vc); free(s->x); free(s);
+}
+const uint16_t* pbo_bs_state_kv(const pbo_bs_state* s, int layer, int which) {
+  return which ? s->vc[layer] : s->kc[layer];
+}
+/* gemvP (fwd8.c:288-293): Q8_K of x, then the Q1 GEMV */
+static void bs_gemv(const q1t* t, const float* x, uint8_t* xq, float* y) {
+  pbo_q8k_quant(x, t->K, xq);
+  pbo_q1_gemv(t->rows, t->K, t->bits, t->scales, xq, NULL, y);
+}
+/* embed (fwd8.c:438-452, Q1_0 branch): x = bit ? sc : -sc, sc the widened
+ * fp16 scale with -0 read as +0 (fwd8.c:265-272) */
+static void bs_embed(const q1t* e, int id, float* x) {
+  const int ng = e->K / 128;
+  for (int g = 0; g < ng; g++) {
+    const uint16_t h = e->scales[(size_t)id * ng + g];
+    const float sc = h == 0x8000u ? 0.0f : pbo_h2f(h);
+    for (int j = 0; j < 128; j++) {
+      const uint32_t w = e->bits[(size_t)id * (e->K / 32) + g * 4 + (j >> 5)];
+      x[g * 128 + j] = ((w >> (j & 31)) & 1u) ? sc : -sc;
+    }
+  }
+}
+/* fwd8.c:812-883 with attn_cpu (:529-647, the PQ1 f16 branch): one token at
+ * position pos. x_in (fp32 [hidden]) replaces the embedding when non-NULL
+ * (pq1_token_fused's contract); logits (fp32 [vocab]) and x_out (the final
+ * residual) are optional. Returns the greedy id (fwd8.c:465-469: first max). */
+int pbo_bs_decode(const pbo_bs_model* m, pbo_bs_state* s, int token, int pos, const float* x_in,
+                  float* logits, float* x_out) {
+  const pbo_bs_cfg* c = &m->cfg;
+  const int H = c->hidden, F = c->inter, NH = c->n_heads, NKV = c->n_kv;
+  const int QD = NH * 128, KD = NKV * 128, G = NH / NKV;
+  const int KMAX = (F > QD ? F : QD) > H ? (F > QD ? F : QD) : H;
+  float* x = s->x;
+  float *xn = malloc(4 * (size_t)H), *qf = malloc(4 * (size_t)QD), *kf = malloc(4 * (size_t)KD);
+  float *vf = malloc(4 * (size_t)KD), *at = malloc(4 * (size_t)QD), *ao = malloc(4 * (size_t)H);
+  float *lg = malloc(4 * (size_t)F), *lu = malloc(4 * (size_t)F);
+  uint8_t* xq = malloc((size_t)(KMAX / 256) * 292);
+  float rc[64], rs[64];
+  pbo_bs_rope_table(pos, c->rope_factor, c->rope_orig_ctx, c->rope_base, rc, rs);
+  if (x_in) memcpy(x, x_in, 4 * (size_t)H);
+  else bs_embed(&m->emb, token, x);
+  for (int L = 0; L < c->n_layers; L++) {
+    const q1t* T = m->q[L];
+    const float* const* fw = m->f[L];
+    pbo_bs_rms(x, fw[PBO_BS_ATTN_NORM], H, xn);
+    pbo_q8k_quant(xn, H, xq);
+    pbo_q1_gemv(QD, H, T[PBO_BS_Q].bits, T[PBO_BS_Q].scales, xq, NULL, qf);
+    pbo_q1_gemv(KD, H, T[PBO_BS_K].bits, T[PBO_BS_K].scales, xq, NULL, kf);
+    pbo_q1_gemv(KD, H, T[PBO_BS_V].bits, T[PBO_BS_V].scales, xq, NULL, vf);
+    for (int h = 0; h < NH; h++) pbo_bs_rms(qf + h * 128, fw[PBO_BS_Q_NORM], 128, qf + h * 128);
+    for (int h = 0; h < NKV; h++) pbo_bs_rms(kf + h * 128, fw[PBO_BS_K_NORM], 128, kf + h * 128);
+    pbo_bs_rope(qf, NH, rc, rs);
+    pbo_bs_rope(kf, NKV, rc, rs);
+    for (int kh = 0; kh < NKV; kh++)
+      for (int d = 0; d < 128; d++) {
+        const size_t o = ((size_t)kh * c->max_ctx + pos) * 128 + d;
+        s->kc[L][o] = pbo_f2h(kf[kh * 128 + d]);
+        s->vc[L][o] = pbo_f2h(vf[kh * 128 + d]);
+      }
+    for (int h = 0; h < NH; h++) {
+      const size_t base = (size_t)(h / G) * c->max_ctx * 128;
+      pbo_bs_fa16_head(qf + h * 128, s->kc[L] + base, s->vc[L] + base, pos + 1, c->attn_scale,
+                       at + h * 128);
+    }
+    bs_gemv(&T[PBO_BS_O], at, xq, ao);
+    for (int i = 0; i < H; i++) x[i] = x[i] + ao[i];
+    pbo_bs_rms(x, fw[PBO_BS_FFN_NORM], H, xn);
+    pbo_q8k_quant(xn, H, xq);
+    pbo_q1_gemv(F, H, T[PBO_BS_GATE].bits, T[PBO_BS_GATE].scales, xq, NULL, lg);
+    pbo_q1_gemv(F, H, T[PBO_BS_UP].bits, T[PBO_BS_UP].scales, xq, NULL, lu);
+    pbo_bs_silu_mul(lu, lg, F);
+    bs_gemv(&T[PBO_BS_DOWN], lu, xq, ao);
+    for (int i = 0; i < H; i++) x[i] = x[i] + ao[i];
+  }
+  pbo_bs_rms(x, m->out_norm, H, xn);
+  const q1t* hd = m->head.bits ? &m->head : &m->emb;
+  float* out = logits ? logits : (float*)malloc(sizeof(float) * c->vocab);
+  bs_gemv(hd, xn, xq, out);
+  const int id = pbo_argmax(out, c->vocab);
+  if (x_out) memcpy(x_out, x, 4 * (size_t)H);
+  if (!logits) free(out);
+  free(xn); free(qf); free(kf); free(vf); free(at); free(ao); free(lg); free(lu); free(xq);
+  return id;
+}

@@ -103,6 +103,37 @@ int pbo_decode(const pbo_model* m, pbo_state* s, int token, int pos, float* logi
 const uint16_t* pbo_state_kv(const pbo_state* s, int layer, int which);
 const uint16_t* pbo_state_ring(const pbo_state* s, int layer);
 
+/* ---- Bonsai-8B-shaped Q1_0 decode step (fwd8.c), head_dim 128 ------------- */
+void pbo_bs_rms(const float* x, const float* w, int n, float* y);          /* fwd8.c:312-317 */
+void pbo_bs_rope_table(int pos, float factor, int orig_ctx, float base, float* c, float* s);
+void pbo_bs_rope(float* x, int heads, const float* c, const float* s);    /* fwd8.c:359-369 */
+void pbo_bs_fa16_head(const float* q, const uint16_t* K, const uint16_t* V, int T, float scale,
+                      float* out);                                         /* pq1_host.c:404-434 */
+void pbo_bs_silu_mul(float* lu, const float* lg, int n);                   /* pq1_host.c:196-227 */
+
+typedef struct {
+  int hidden, inter, n_layers, n_heads, n_kv, vocab, max_ctx;
+  float rope_factor;   /* YaRN factor (fwd8.c:51: 4) */
+  int rope_orig_ctx;   /* YaRN original context (fwd8.c:56: 16384 for the 8B) */
+  float rope_base;     /* fwd8.c:57: 1e6 for the 8B */
+  float attn_scale;    /* fwd8.c:566: 0.0883883476 = 1/sqrt(128) */
+} pbo_bs_cfg;
+enum { PBO_BS_Q = 0, PBO_BS_K, PBO_BS_V, PBO_BS_O, PBO_BS_GATE, PBO_BS_UP, PBO_BS_DOWN, PBO_BS_NQ1 };
+enum { PBO_BS_ATTN_NORM = 0, PBO_BS_FFN_NORM, PBO_BS_Q_NORM, PBO_BS_K_NORM, PBO_BS_NF32 };
+typedef struct pbo_bs_model pbo_bs_model;
+typedef struct pbo_bs_state pbo_bs_state;
+pbo_bs_model* pbo_bs_model_new(const pbo_bs_cfg* cfg);
+void pbo_bs_model_free(pbo_bs_model* m);
+/* Q1_0 18-byte blocks [rows][K/128]; layer -1: slot 0 token_embd, slot 1 output.weight */
+void pbo_bs_model_set_q1(pbo_bs_model* m, int layer, int slot, const uint8_t* blocks, int rows, int K);
+/* fp32 norm weights (kept by pointer); layer -1: output_norm */
+void pbo_bs_model_set_f32(pbo_bs_model* m, int layer, int slot, const float* p);
+pbo_bs_state* pbo_bs_state_new(const pbo_bs_model* m);
+void pbo_bs_state_free(pbo_bs_state* s);
+const uint16_t* pbo_bs_state_kv(const pbo_bs_state* s, int layer, int which);
+int pbo_bs_decode(const pbo_bs_model* m, pbo_bs_state* s, int token, int pos, const float* x_in,
+                  float* logits, float* x_out);
+
 int pbo_threads(void);
 
 #ifdef __cplusplus

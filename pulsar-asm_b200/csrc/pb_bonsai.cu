@@ -1,0 +1,911 @@
+// pb_bonsai.cu -- the Bonsai Q1_0 decoder's token step (pulsar_arm/bonsai2/
+// fwd8.c:812-883 with attn_cpu :529-647 on the f16 cache) on sm_100a, as one
+// CUDA graph per state of programmatic-dependent launches:
+//
+//   embed | per layer: [residual add +] RMS norm + Q8_K -> q|k|v Q1 GEMV ->
+//   head norms + YaRN rope + f16 K/V append -> q.k scores -> online-softmax
+//   P.V + Q8_K -> o GEMV -> residual add + RMS norm + Q8_K -> gate|up GEMV ->
+//   silu(g)*u + Q8_K -> down GEMV | residual add + output norm + Q8_K -> head
+//   GEMV -> greedy argmax
+//
+// Arithmetic, each step as the reference states it (the CPU oracle performs
+// the same operations):
+//  * rms (fwd8.c:312-317): s = serial double sum of x*x, sc = 1/sqrtf(float(
+//    s/n) + 1e-6), y = (x*sc)*w. The serial double sum is not recomputed
+//    serially: a parallel double sum P differs from it by at most 2(n-1)u*P
+//    (u = 2^-53, every term >= 0), so when P(1 -+ n 2^-51)/n round to the same
+//    float, that float is float(serial/n). Otherwise one thread runs the serial
+//    chain (counted in the control block).
+//  * rope (fwd8.c:359-369, contracted as gcc builds it, pq1_swar_sm53.cu:2147):
+//    x[j] = fma(a, c, -(b*s)), x[j+64] = fma(a, s, b*c), with the (cos, sin)
+//    table of every position built on the host (fwd8.c:339-358).
+//  * attention (pq1_host.c:404-434): q rounded to f16; q.k as 16 fma chains
+//    reduced ((a_l+a_8+l)+(a_4+l+a_12+l)), ((r0+r1)+(r2+r3)), times scale; the
+//    online softmax keeps the running max M, ms = e^(Mold-M) at a new maximum
+//    (rescaling the f16 accumulator), vs = e^(s-M) otherwise; the accumulator
+//    is rounded to f16 after every update, S = fma(S, ms, vs), out = acc/S.
+//    The running maxima come from a parallel prefix max (exact); the per-
+//    dimension accumulator chain runs in position order.
+//  * silu(g)*u (pq1_host.c:196-227): (g * (1/(1+e^-g))) * u.
+//  * Q8_K and the Q1 GEMV: pb_q8k.cuh and pb_q1.cu.
+// expf is pb_expf (pb_common.cuh) on both sides.
+#include "pb_common.cuh"
+#include "pb_internal.h"
+#include "pb_q8k.cuh"
+#include <cmath>
+#include <cstring>
+#include <vector>
+
+namespace {
+
+constexpr int BS_HD = 128;          // head_dim (fwd8.c hard-codes 128)
+constexpr int BS_AM_CTAS = 296;     // argmax partial slots
+constexpr int BS_PV_TT = 64;        // positions per V tile in the P.V chain
+
+struct BsCtl {
+  int token;          // input id (the argmax writes the greedy id here)
+  int pos;            // position (the argmax advances it)
+  int step;           // greedy step counter (index into ids)
+  int use_x;          // 1: the step's input row is xin (pq1_token_fused), not the embedding
+  unsigned counter;   // argmax last-CTA counter
+  int top;            // greedy id of the last step
+  float topv;         // its logit
+  int fallbacks;      // RMS norms that took the serial double chain
+  int* ids;           // optional: greedy id of every step
+  float slot_val[BS_AM_CTAS];
+  int slot_idx[BS_AM_CTAS];
+};
+
+// ------------------------------------------------------------- RMS norm
+// float(s/n) of the serial double sum of squares, from a parallel sum P
+// (every term >= 0; see the file header). ok = 0: not certified.
+PB_DEV float bs_mean_sq(double P, int n, bool& ok) {
+  const double e = (double)n * 0x1p-51, dn = (double)n;
+  const float lo = __double2float_rn(__ddiv_rn(__dsub_rn(P, __dmul_rn(P, e)), dn));
+  const float hi = __double2float_rn(__ddiv_rn(__dadd_rn(P, __dmul_rn(P, e)), dn));
+  ok = lo == hi;
+  return lo;
+}
+PB_DEV float bs_mean_sq_serial(const float* v, int n) {
+  double s = 0.0;
+  for (int i = 0; i < n; i++) { const double d = (double)v[i]; s = __fma_rn(d, d, s); }
+  return __double2float_rn(__ddiv_rn(s, (double)n));
+}
+PB_DEV double warp_sum_d(double v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = __dadd_rn(v, __shfl_xor_sync(0xffffffffu, v, o));
+  return v;
+}
+
+struct BsNormArgs {
+  const float* xin;   // residual stream in
+  const float* r;     // added to it first (null: none)
+  float* xout;        // updated residual stream (written when r != null)
+  const float* w;     // norm weight [H]
+  uint8_t* xq;        // Q8_K of the normalised vector [H/256][292]
+  int H;
+  BsCtl* ctl;
+};
+// grid H/256 CTAs of 256 threads; every CTA sums all H squares (from L2) and
+// writes its own 256-value slice and Q8_K block
+__global__ void __launch_bounds__(256) k_bs_norm(BsNormArgs a) {
+  extern __shared__ __align__(16) float sv[];   // [H]
+  __shared__ double wsum[8];
+  __shared__ float s_sc;
+  __shared__ Q8kScratch q8s;
+  pb_grid_launch_dependents();
+  pb_grid_wait();
+  const int t = threadIdx.x, H = a.H;
+  double ps = 0.0;
+  for (int i = t; i < H; i += 256) {
+    float v = a.xin[i];
+    if (a.r) v = __fadd_rn(v, a.r[i]);
+    sv[i] = v;
+    const double d = (double)v;
+    ps = __fma_rn(d, d, ps);
+  }
+  ps = warp_sum_d(ps);
+  if ((t & 31) == 0) wsum[t >> 5] = ps;
+  __syncthreads();
+  if (t == 0) {
+    double P = 0.0;
+    for (int w = 0; w < 8; w++) P = __dadd_rn(P, wsum[w]);
+    bool ok;
+    float mean = bs_mean_sq(P, H, ok);
+    if (!ok) {
+      mean = bs_mean_sq_serial(sv, H);
+      if (blockIdx.x == 0) atomicAdd(&a.ctl->fallbacks, 1);
+    }
+    s_sc = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(mean, 1e-6f)));
+  }
+  __syncthreads();
+  const int i = blockIdx.x * 256 + t;
+  const float v = sv[i];
+  if (a.r) a.xout[i] = v;
+  const float y = __fmul_rn(__fmul_rn(v, s_sc), a.w[i]);
+  pb_q8k_block256(y, a.xq + (size_t)blockIdx.x * 292, q8s);
+}
+
+// ---------------------------------------------------------------- embed
+struct BsEmbedArgs {
+  const uint32_t* bits;     // token_embd [vocab][H/32]
+  const uint16_t* scales;   // [vocab][H/128]
+  const float* xin;         // ctl->use_x: the caller's row
+  float* x;
+  int H;
+  const BsCtl* ctl;
+};
+// fwd8.c:438-452 (Q1_0 branch): x = bit ? sc : -sc, sc the fp16 scale widened
+// with -0 read as +0 (fwd8.c:265-272)
+__global__ void __launch_bounds__(256) k_bs_embed(BsEmbedArgs a) {
+  pb_grid_launch_dependents();
+  pb_grid_wait();
+  const int i = blockIdx.x * 256 + threadIdx.x;
+  if (i >= a.H) return;
+  if (a.ctl->use_x) { a.x[i] = a.xin[i]; return; }
+  const size_t tok = (size_t)a.ctl->token;
+  const unsigned short h = a.scales[tok * (a.H / 128) + i / 128];
+  const float sc = h == 0x8000u ? 0.0f : pb_h2f(h);
+  const uint32_t w = a.bits[tok * (a.H / 32) + i / 32];
+  a.x[i] = ((w >> (i & 31)) & 1u) ? sc : -sc;
+}
+
+// ------------------------------------------------ head norms, rope, K/V
+struct BsPreArgs {
+  const float* qkv;     // [NH + 2 NKV][128] GEMV output
+  const float* qn;      // q_norm [128]
+  const float* kn;      // k_norm [128]
+  const float* rope;    // [max_ctx][cos 64 | sin 64]
+  uint16_t* qh;         // [NH][128] f16 post-rope q
+  uint16_t* kc;         // layer's K cache [NKV][max_ctx][128]
+  uint16_t* vc;         // layer's V cache
+  int NH, NKV, max_ctx;
+  BsCtl* ctl;
+};
+// one warp per head: q heads, k heads (rms, rope), then v heads (copied)
+__global__ void __launch_bounds__(32) k_bs_attn_pre(BsPreArgs a) {
+  __shared__ float sx[BS_HD];
+  pb_grid_launch_dependents();
+  pb_grid_wait();
+  const int hh = blockIdx.x, l = threadIdx.x, pos = a.ctl->pos;
+  const float* src = a.qkv + (size_t)hh * BS_HD;
+  float x[4];
+#pragma unroll
+  for (int k = 0; k < 4; k++) x[k] = src[l + 32 * k];
+  if (hh >= a.NH + a.NKV) {
+    uint16_t* dst = a.vc + ((size_t)(hh - a.NH - a.NKV) * a.max_ctx + pos) * BS_HD;
+#pragma unroll
+    for (int k = 0; k < 4; k++) dst[l + 32 * k] = pb_f2h(x[k]);
+    return;
+  }
+  double ps = 0.0;
+#pragma unroll
+  for (int k = 0; k < 4; k++) { const double d = (double)x[k]; ps = __fma_rn(d, d, ps); sx[l + 32 * k] = x[k]; }
+  ps = warp_sum_d(ps);
+  bool ok;
+  float mean = bs_mean_sq(ps, BS_HD, ok);
+  if (!ok) {   // warp-uniform
+    __syncwarp();
+    if (l == 0) {
+      mean = bs_mean_sq_serial(sx, BS_HD);
+      atomicAdd(&a.ctl->fallbacks, 1);
+    }
+    mean = __shfl_sync(0xffffffffu, mean, 0);
+  }
+  const float sc = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(mean, 1e-6f)));
+  const float* w = hh < a.NH ? a.qn : a.kn;
+  float y[4];
+#pragma unroll
+  for (int k = 0; k < 4; k++) y[k] = __fmul_rn(__fmul_rn(x[k], sc), w[l + 32 * k]);
+  const float* rc = a.rope + (size_t)pos * BS_HD;
+  float o[4];
+#pragma unroll
+  for (int k = 0; k < 2; k++) {   // pairs (j, j+64), j = l + 32k
+    const float c = rc[l + 32 * k], s = rc[64 + l + 32 * k], av = y[k], bv = y[k + 2];
+    o[k] = __fmaf_rn(av, c, -__fmul_rn(bv, s));
+    o[k + 2] = __fmaf_rn(av, s, __fmul_rn(bv, c));
+  }
+  uint16_t* dst = hh < a.NH ? a.qh + (size_t)hh * BS_HD
+                            : a.kc + ((size_t)(hh - a.NH) * a.max_ctx + pos) * BS_HD;
+#pragma unroll
+  for (int k = 0; k < 4; k++) dst[l + 32 * k] = pb_f2h(o[k]);
+}
+
+// ----------------------------------------------------------- q.k scores
+struct BsQkArgs {
+  const uint16_t* qh;   // [NH][128] f16
+  const uint16_t* kc;   // layer's K cache [NKV][max_ctx][128]
+  float* sc;            // [NH][max_ctx] scaled scores
+  int NH, NKV, max_ctx;
+  float scale;
+  const BsCtl* ctl;
+};
+constexpr int BS_KROW = 272;   // K row stride in shared memory (bank-conflict-free 16-byte reads)
+// grid (max_ctx/32, NKV); warp g = query head kvh*G + g, lane = position
+__global__ void __launch_bounds__(256) k_bs_fa_qk(BsQkArgs a) {
+  __shared__ __align__(16) unsigned char ks[32 * BS_KROW];
+  __shared__ __align__(16) uint16_t qs[8][BS_HD];
+  pb_grid_launch_dependents();
+  pb_grid_wait();
+  const int T = a.ctl->pos + 1, t0 = blockIdx.x * 32;
+  if (t0 >= T) return;
+  const int kvh = blockIdx.y, G = a.NH / a.NKV;
+  for (int i = threadIdx.x; i < 32 * 16; i += blockDim.x) {
+    const int r = i >> 4, c = i & 15;
+    if (t0 + r < T)
+      *reinterpret_cast<uint4*>(ks + r * BS_KROW + c * 16) =
+          *reinterpret_cast<const uint4*>(a.kc + ((size_t)kvh * a.max_ctx + t0 + r) * BS_HD + c * 8);
+  }
+  for (int i = threadIdx.x; i < G * 16; i += blockDim.x) {
+    const int g = i >> 4, c = i & 15;
+    *reinterpret_cast<uint4*>(&qs[g][c * 8]) =
+        *reinterpret_cast<const uint4*>(a.qh + (size_t)(kvh * G + g) * BS_HD + c * 8);
+  }
+  __syncthreads();
+  const int g = threadIdx.x >> 5, r = threadIdx.x & 31, t = t0 + r;
+  if (t >= T) return;
+  float acc[16];
+#pragma unroll
+  for (int c = 0; c < 16; c++) acc[c] = 0.0f;
+  const unsigned char* kr = ks + r * BS_KROW;
+#pragma unroll
+  for (int j = 0; j < 8; j++) {
+    const uint4 k0 = *reinterpret_cast<const uint4*>(kr + 32 * j);
+    const uint4 k1 = *reinterpret_cast<const uint4*>(kr + 32 * j + 16);
+    const uint4 q0 = *reinterpret_cast<const uint4*>(&qs[g][16 * j]);
+    const uint4 q1 = *reinterpret_cast<const uint4*>(&qs[g][16 * j + 8]);
+    const unsigned kw[8] = {k0.x, k0.y, k0.z, k0.w, k1.x, k1.y, k1.z, k1.w};
+    const unsigned qw[8] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w};
+#pragma unroll
+    for (int c = 0; c < 16; c++) {
+      const unsigned short kh = (unsigned short)(c & 1 ? kw[c >> 1] >> 16 : kw[c >> 1] & 0xffffu);
+      const unsigned short qv = (unsigned short)(c & 1 ? qw[c >> 1] >> 16 : qw[c >> 1] & 0xffffu);
+      acc[c] = __fmaf_rn(pb_h2f(kh), pb_h2f(qv), acc[c]);
+    }
+  }
+  float rr[4];
+#pragma unroll
+  for (int l = 0; l < 4; l++) rr[l] = __fadd_rn(__fadd_rn(acc[l], acc[8 + l]), __fadd_rn(acc[4 + l], acc[12 + l]));
+  const float s = __fmul_rn(__fadd_rn(__fadd_rn(rr[0], rr[1]), __fadd_rn(rr[2], rr[3])), a.scale);
+  a.sc[(size_t)(kvh * G + g) * a.max_ctx + t] = s;
+}
+
+// ------------------------------------------------- online softmax and P.V
+struct BsPvArgs {
+  const float* sc;    // [NH][max_ctx]
+  const uint16_t* vc; // layer's V cache [NKV][max_ctx][128]
+  float* atto;        // [NH][128]
+  uint8_t* xq;        // Q8_K of atto (one 256-block per CTA)
+  int NH, NKV, max_ctx;
+  const BsCtl* ctl;
+};
+PB_DEV float bs_r16(float x) { return __half2float(__float2half_rn(x)); }
+// the serial algorithm's "s > M" keeps the earliest of equal maxima and never
+// takes a NaN: the prefix max maps NaN to -inf and combines (earlier, later)
+PB_DEV float bs_max_comb(float m, float s) { return s > m ? s : m; }
+PB_DEV void bs_cp16(void* dst, const void* src) {
+  const unsigned d = (unsigned)__cvta_generic_to_shared(dst);
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(d), "l"(src) : "memory");
+}
+PB_DEV void bs_cp_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+PB_DEV void bs_cp_wait0() { asm volatile("cp.async.wait_group 0;" ::: "memory"); }
+// grid NH/2 CTAs of 256 threads: thread (hh, d) owns dimension d of head
+// 2*blockIdx.x + hh (both heads read the same kv head, G even)
+__global__ void __launch_bounds__(256) k_bs_fa_pv(BsPvArgs a) {
+  extern __shared__ __align__(16) unsigned char smem[];
+  float* sms = reinterpret_cast<float*>(smem);                 // [2][max_ctx] ms
+  float* svs = sms + 2 * a.max_ctx;                            // [2][max_ctx] vs
+  uint16_t* vt = reinterpret_cast<uint16_t*>(svs + 2 * a.max_ctx);   // [2][TT][128]
+  __shared__ float wmax[8];
+  __shared__ float s_S[2];
+  __shared__ Q8kScratch q8s;
+  pb_grid_launch_dependents();
+  pb_grid_wait();
+  const int T = a.ctl->pos + 1, tid = threadIdx.x, hh = tid >> 7, d = tid & 127;
+  const int h = 2 * blockIdx.x + hh, kvh = h / (a.NH / a.NKV);
+  const uint16_t* V = a.vc + (size_t)kvh * a.max_ctx * BS_HD;
+  const int ntile = (T + BS_PV_TT - 1) / BS_PV_TT;
+  auto issue = [&](int tile) {
+    uint16_t* dst = vt + (size_t)(tile & 1) * BS_PV_TT * BS_HD;
+    const int r0 = tile * BS_PV_TT;
+    for (int i = tid; i < BS_PV_TT * 16; i += 256) {
+      const int r = i >> 4, c = i & 15;
+      if (r0 + r < T) bs_cp16(dst + r * BS_HD + c * 8, V + (size_t)(r0 + r) * BS_HD + c * 8);
+    }
+    bs_cp_commit();
+  };
+  issue(0);
+  // ---- running maxima: thread j of the head owns positions [j*C, j*C + C)
+  const float* S = a.sc + (size_t)h * a.max_ctx;
+  const int C = (T + 127) / 128, p0 = d * C, p1 = min(T, p0 + C);
+  float m = -INFINITY;
+  for (int p = p0; p < p1; p++) { const float s = S[p]; m = bs_max_comb(m, s != s ? -INFINITY : s); }
+  // exclusive scan over the head's 128 threads (4 warps)
+  const int lane = tid & 31, w = tid >> 5;
+  float inc = m;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const float u = __shfl_up_sync(0xffffffffu, inc, o);
+    if (lane >= o) inc = bs_max_comb(u, inc);
+  }
+  if (lane == 31) wmax[w] = inc;
+  __syncthreads();
+  float ex = __shfl_up_sync(0xffffffffu, inc, 1);
+  if (lane == 0) ex = -INFINITY;
+  float before = -INFINITY;
+  for (int ww = hh * 4; ww < w; ww++) before = bs_max_comb(before, wmax[ww]);
+  float M = bs_max_comb(before, ex);
+  float* ms_h = sms + (size_t)hh * a.max_ctx;
+  float* vs_h = svs + (size_t)hh * a.max_ctx;
+  for (int p = p0; p < p1; p++) {
+    const float s = S[p];
+    if (s > M) { ms_h[p] = pb_expf(__fsub_rn(M, s)); vs_h[p] = 1.0f; M = s; }
+    else { ms_h[p] = 1.0f; vs_h[p] = pb_expf(__fsub_rn(s, M)); }
+  }
+  __syncthreads();
+  // ---- the accumulator chain, positions in order
+  float acc = 0.0f, Ssum = 0.0f;
+  for (int tile = 0; tile < ntile; tile++) {
+    bs_cp_wait0();
+    __syncthreads();
+    if (tile + 1 < ntile) issue(tile + 1);
+    const uint16_t* vb = vt + (size_t)(tile & 1) * BS_PV_TT * BS_HD + d;
+    const int r0 = tile * BS_PV_TT, n = min(BS_PV_TT, T - r0);
+    if (n == BS_PV_TT) {
+#pragma unroll 16
+      for (int r = 0; r < BS_PV_TT; r++) {
+        const float ms = ms_h[r0 + r], vs = vs_h[r0 + r], v = pb_h2f(vb[r * BS_HD]);
+        if (ms != 1.0f) acc = bs_r16(__fmul_rn(acc, ms));
+        acc = bs_r16(__fmaf_rn(v, vs, acc));
+        Ssum = __fmaf_rn(Ssum, ms, vs);
+      }
+    } else {
+      for (int r = 0; r < n; r++) {
+        const float ms = ms_h[r0 + r], vs = vs_h[r0 + r], v = pb_h2f(vb[r * BS_HD]);
+        if (ms != 1.0f) acc = bs_r16(__fmul_rn(acc, ms));
+        acc = bs_r16(__fmaf_rn(v, vs, acc));
+        Ssum = __fmaf_rn(Ssum, ms, vs);
+      }
+    }
+  }
+  if (d == 0) s_S[hh] = Ssum;
+  __syncthreads();
+  const float St = s_S[hh];
+  const float si = St == 0.0f ? 0.0f : __fdiv_rn(1.0f, St);
+  const float out = __fmul_rn(acc, si);
+  a.atto[(size_t)h * BS_HD + d] = out;
+  pb_q8k_block256(out, a.xq + (size_t)blockIdx.x * 292, q8s);
+}
+
+// -------------------------------------------------------- silu(g)*u + Q8_K
+struct BsSiluArgs {
+  const float* gu;   // [2F]: gate rows then up rows
+  uint8_t* xq;       // [F/256][292]
+  int F;
+};
+__global__ void __launch_bounds__(256) k_bs_silu_q8k(BsSiluArgs a) {
+  __shared__ Q8kScratch q8s;
+  pb_grid_launch_dependents();
+  pb_grid_wait();
+  const int i = blockIdx.x * 256 + threadIdx.x;
+  const float g = a.gu[i], u = a.gu[a.F + i];
+  const float v = __fmul_rn(__fmul_rn(g, __fdiv_rn(1.0f, __fadd_rn(1.0f, pb_expf(-g)))), u);
+  pb_q8k_block256(v, a.xq + (size_t)blockIdx.x * 292, q8s);
+}
+
+// ------------------------------------------------------------- argmax
+struct BsArgmaxArgs {
+  const float* lg;
+  int V;
+  BsCtl* ctl;
+};
+// fwd8.c:465-469: the first index of the maximum. Per-CTA best -> slot; the
+// last CTA reduces the slots, publishes the id and advances the step.
+__global__ void __launch_bounds__(256) k_bs_argmax(BsArgmaxArgs a) {
+  __shared__ float bv[8];
+  __shared__ int bi[8];
+  __shared__ int am_last;
+  pb_grid_launch_dependents();
+  pb_grid_wait();
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  float b = -INFINITY;
+  int ix = 0x7fffffff;
+  for (int i = blockIdx.x * 256 + threadIdx.x; i < a.V; i += gridDim.x * 256) {
+    const float v = a.lg[i];
+    if (v > b || (v == b && i < ix)) { b = v; ix = i; }
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const float ov = __shfl_down_sync(0xffffffffu, b, o);
+    const int oi = __shfl_down_sync(0xffffffffu, ix, o);
+    if (ov > b || (ov == b && oi < ix)) { b = ov; ix = oi; }
+  }
+  if (lane == 0) { bv[warp] = b; bi[warp] = ix; }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    for (int w = 1; w < 8; w++)
+      if (bv[w] > bv[0] || (bv[w] == bv[0] && bi[w] < bi[0])) { bv[0] = bv[w]; bi[0] = bi[w]; }
+    a.ctl->slot_val[blockIdx.x] = bv[0];
+    a.ctl->slot_idx[blockIdx.x] = bi[0];
+    __threadfence();
+    am_last = atomicAdd(&a.ctl->counter, 1u) == gridDim.x - 1;
+  }
+  __syncthreads();
+  if (am_last && threadIdx.x == 0) {
+    __threadfence();
+    volatile float* sv = a.ctl->slot_val;
+    volatile int* si = a.ctl->slot_idx;
+    float best = sv[0];
+    int id = si[0];
+    for (int k = 1; k < (int)gridDim.x; k++) {
+      const float ov = sv[k]; const int oi = si[k];
+      if (ov > best || (ov == best && oi < id)) { best = ov; id = oi; }
+    }
+    // no finite maximum (all NaN): index 0, as the serial scan leaves it
+    // (and a NaN first logit, which the serial scan never leaves)
+    if (id == 0x7fffffff || a.lg[0] != a.lg[0]) { id = 0; best = a.lg[0]; }
+    a.ctl->top = id;
+    a.ctl->topv = best;
+    if (a.ctl->ids) a.ctl->ids[a.ctl->step] = id;
+    a.ctl->step += 1;
+    a.ctl->token = id;
+    a.ctl->pos += 1;
+    a.ctl->counter = 0;
+  }
+}
+
+template <typename Args>
+int bs_launch(void (*k)(Args), dim3 grid, int block, size_t smem, cudaStream_t st, const Args& args,
+              const char* name) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = dim3(block);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  cudaError_t e = cudaLaunchKernelEx(&cfg, k, args);
+  if (e != cudaSuccess) return pb_set_error(PB_ECUDA, "launch %s: %s", name, cudaGetErrorString(e));
+  pb_count_launch();
+  return PB_OK;
+}
+
+size_t a256(size_t x) { return (x + 255) & ~(size_t)255; }
+
+}  // namespace
+
+// ===================================================================== host
+struct pb_bonsai {
+  pb_bonsai_cfg c{};
+  int device = 0;
+  int QD = 0, KD = 0;
+  // per layer: merged q|k|v, o, merged gate|up, down (views into one arena)
+  std::vector<pb_q1> qkv, o, gu, down;
+  pb_q1 emb, head;
+  char* arena = nullptr;
+  float* norms = nullptr;   // [layer][attn H | ffn H | q 128 | k 128], then output_norm [H]
+  std::vector<unsigned> have;   // per layer bit mask of tensors and norms set
+  unsigned have_top = 0;        // embed 1, head 2, output norm 4
+  size_t weight_bytes = 0;
+};
+
+struct pb_bonsai_state {
+  pb_bonsai* m = nullptr;
+  int max_ctx = 0;
+  char* mem = nullptr;
+  uint16_t* kv = nullptr;   // [layer][2][NKV][max_ctx][128]
+  float* rope = nullptr;    // [max_ctx][128]
+  float* x[2] = {nullptr, nullptr};
+  float* xin = nullptr;
+  float* qkv = nullptr;
+  uint16_t* qh = nullptr;
+  float* scores = nullptr;
+  float* atto = nullptr;
+  float* ao = nullptr;
+  float* gu = nullptr;
+  float* fo = nullptr;
+  uint8_t* xq = nullptr;
+  float* logits = nullptr;
+  BsCtl* ctl = nullptr;
+  BsCtl* h_ctl = nullptr;   // pinned mirror for uploads
+  cudaGraphExec_t graph = nullptr;
+  uint64_t graph_launches = 0;   // kernels per graph launch
+  int final_x = 0;          // which x buffer holds the residual after a step
+};
+
+namespace {
+
+size_t pv_smem(int max_ctx) { return (size_t)16 * max_ctx + (size_t)2 * BS_PV_TT * BS_HD * 2; }
+
+// fwd8.c:322-358 (yarn_corr_dim, yarn_init, rope_table) for every position,
+// written as gcc's default (contracting) build computes it: msc = fma(0.1,
+// ln factor, 1), th = fma(ti, 1 - ramp, te*ramp)
+float bs_corr_dim(int n_ctx, float rot, float base) {
+  return 128 * logf(n_ctx / (rot * 2 * (float)M_PI)) / (2 * logf(base));
+}
+void bs_rope_table(const pb_bonsai_cfg& c, int pos, float* cs) {
+  const float st = floorf(bs_corr_dim(c.rope_orig_ctx, 32.0f, c.rope_base));
+  const float en = ceilf(bs_corr_dim(c.rope_orig_ctx, 1.0f, c.rope_base));
+  const float c0 = st > 0 ? st : 0, c1 = en < 127 ? en : 127;
+  const float fs = 1.0f / c.rope_factor, msc = fmaf(0.1f, logf(c.rope_factor), 1.0f);
+  const float tscale = powf(c.rope_base, -2.0f / 128.0f);
+  float theta = (float)pos;
+  for (int j = 0; j < 64; j++, theta *= tscale) {
+    const float y = (j - c0) / fmaxf(0.001f, c1 - c0);
+    const float ramp = 1.0f - fminf(1.0f, fmaxf(0.0f, y));
+    const float ti = fs * theta, te = theta;
+    const float th = fmaf(ti, 1 - ramp, te * ramp);
+    cs[j] = cosf(th) * msc;
+    cs[64 + j] = sinf(th) * msc;
+  }
+}
+
+int bs_check_ready(const pb_bonsai* m) {
+  for (int L = 0; L < m->c.n_layers; L++)
+    if (m->have[L] != 0x7ffu) return pb_set_error(PB_EINVAL, "bonsai: layer %d incomplete (mask 0x%x)", L, m->have[L]);
+  if ((m->have_top & 5u) != 5u) return pb_set_error(PB_EINVAL, "bonsai: token_embd or output_norm missing");
+  return PB_OK;
+}
+
+// the whole token as launches on st (captured into the state's graph)
+int bs_record(pb_bonsai* m, pb_bonsai_state* s, cudaStream_t st) {
+  const pb_bonsai_cfg& c = m->c;
+  const int H = c.hidden, F = c.inter, NH = c.n_heads, NKV = c.n_kv;
+  int rc;
+  int cur = 0;
+  const pb_q1& hd = (m->have_top & 2u) ? m->head : m->emb;
+  {
+    BsEmbedArgs a{m->emb.bits, m->emb.scales, s->xin, s->x[cur], H, s->ctl};
+    if ((rc = bs_launch(k_bs_embed, dim3((H + 255) / 256), 256, 0, st, a, "k_bs_embed"))) return rc;
+  }
+  const size_t nsm = (size_t)H * 4;
+  for (int L = 0; L < c.n_layers; L++) {
+    const float* nw = m->norms + (size_t)L * (2 * H + 2 * BS_HD);
+    uint16_t* kc = s->kv + (size_t)L * 2 * NKV * s->max_ctx * BS_HD;
+    uint16_t* vc = kc + (size_t)NKV * s->max_ctx * BS_HD;
+    {   // [x += down output] ; rms(attn_norm) ; Q8_K
+      BsNormArgs a{s->x[cur], L ? s->fo : nullptr, s->x[cur ^ 1], nw, s->xq, H, s->ctl};
+      if (L) cur ^= 1;
+      if ((rc = bs_launch(k_bs_norm, dim3(H / 256), 256, nsm, st, a, "k_bs_norm"))) return rc;
+    }
+    if ((rc = pb_q1_gemv_launch(&m->qkv[L], s->xq, s->qkv, nullptr, st, true))) return rc;
+    {
+      BsPreArgs a{s->qkv, nw + 2 * H, nw + 2 * H + BS_HD, s->rope, s->qh, kc, vc, NH, NKV, s->max_ctx, s->ctl};
+      if ((rc = bs_launch(k_bs_attn_pre, dim3(NH + 2 * NKV), 32, 0, st, a, "k_bs_attn_pre"))) return rc;
+    }
+    {
+      BsQkArgs a{s->qh, kc, s->scores, NH, NKV, s->max_ctx, c.attn_scale, s->ctl};
+      if ((rc = bs_launch(k_bs_fa_qk, dim3(s->max_ctx / 32, NKV), 32 * (NH / NKV), 0, st, a, "k_bs_fa_qk"))) return rc;
+    }
+    {
+      BsPvArgs a{s->scores, vc, s->atto, s->xq, NH, NKV, s->max_ctx, s->ctl};
+      if ((rc = bs_launch(k_bs_fa_pv, dim3(NH / 2), 256, pv_smem(s->max_ctx), st, a, "k_bs_fa_pv"))) return rc;
+    }
+    if ((rc = pb_q1_gemv_launch(&m->o[L], s->xq, s->ao, nullptr, st, true))) return rc;
+    {   // x += attention output ; rms(ffn_norm) ; Q8_K
+      BsNormArgs a{s->x[cur], s->ao, s->x[cur ^ 1], nw + H, s->xq, H, s->ctl};
+      cur ^= 1;
+      if ((rc = bs_launch(k_bs_norm, dim3(H / 256), 256, nsm, st, a, "k_bs_norm"))) return rc;
+    }
+    if ((rc = pb_q1_gemv_launch(&m->gu[L], s->xq, s->gu, nullptr, st, true))) return rc;
+    {
+      BsSiluArgs a{s->gu, s->xq, F};
+      if ((rc = bs_launch(k_bs_silu_q8k, dim3(F / 256), 256, 0, st, a, "k_bs_silu_q8k"))) return rc;
+    }
+    if ((rc = pb_q1_gemv_launch(&m->down[L], s->xq, s->fo, nullptr, st, true))) return rc;
+  }
+  {   // x += last down output ; rms(output_norm) ; Q8_K
+    BsNormArgs a{s->x[cur], s->fo, s->x[cur ^ 1], m->norms + (size_t)c.n_layers * (2 * H + 2 * BS_HD), s->xq, H, s->ctl};
+    cur ^= 1;
+    if ((rc = bs_launch(k_bs_norm, dim3(H / 256), 256, nsm, st, a, "k_bs_norm"))) return rc;
+  }
+  if ((rc = pb_q1_gemv_launch(&hd, s->xq, s->logits, nullptr, st, true))) return rc;
+  {
+    BsArgmaxArgs a{s->logits, c.vocab, s->ctl};
+    if ((rc = bs_launch(k_bs_argmax, dim3(BS_AM_CTAS), 256, 0, st, a, "k_bs_argmax"))) return rc;
+  }
+  s->final_x = cur;
+  return PB_OK;
+}
+
+int bs_graph(pb_bonsai* m, pb_bonsai_state* s, cudaStream_t st) {
+  if (s->graph) return PB_OK;
+  if (bs_check_ready(m)) return PB_EINVAL;
+  cudaStream_t cap;
+  PB_TRY_CUDA(cudaStreamCreateWithFlags(&cap, cudaStreamNonBlocking));
+  PB_TRY_CUDA(cudaFuncSetAttribute(k_bs_fa_pv, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)pv_smem(s->max_ctx)));
+  PB_TRY_CUDA(cudaFuncSetAttribute(k_bs_norm, cudaFuncAttributeMaxDynamicSharedMemorySize, m->c.hidden * 4));
+  pb_set_capturing(true);
+  cudaGraph_t g = nullptr;
+  const int L = m->c.n_layers;
+  s->graph_launches = (uint64_t)L * 10 + 4;
+  int rc = PB_OK;
+  if (cudaStreamBeginCapture(cap, cudaStreamCaptureModeThreadLocal) != cudaSuccess) {
+    rc = pb_set_error(PB_ECUDA, "bonsai: begin capture");
+  } else {
+    rc = bs_record(m, s, cap);
+    cudaError_t e = cudaStreamEndCapture(cap, &g);
+    if (rc == PB_OK && e != cudaSuccess) rc = pb_set_error(PB_ECUDA, "bonsai: end capture: %s", cudaGetErrorString(e));
+  }
+  pb_set_capturing(false);
+  if (rc == PB_OK && cudaGraphInstantiate(&s->graph, g, 0) != cudaSuccess)
+    rc = pb_set_error(PB_ECUDA, "bonsai: instantiate: %s", cudaGetErrorString(cudaGetLastError()));
+  if (g) cudaGraphDestroy(g);
+  cudaStreamDestroy(cap);
+  (void)st;
+  return rc;
+}
+
+// upload token/pos (and the input-row flag) then run the graph
+int bs_step(pb_bonsai* m, pb_bonsai_state* s, int token, int pos, int use_x, cudaStream_t st) {
+  if (pos < 0 || pos >= s->max_ctx) return pb_set_error(PB_EINVAL, "bonsai: pos %d outside [0, %d)", pos, s->max_ctx);
+  if (!use_x && (token < 0 || token >= m->c.vocab)) return pb_set_error(PB_EINVAL, "bonsai: token %d", token);
+  int rc;
+  if ((rc = bs_graph(m, s, st))) return rc;
+  // from pageable memory: staged at call time, so back-to-back calls cannot
+  // overwrite a pending upload
+  const int hdr[4] = {token, pos, 0, use_x};
+  PB_TRY_CUDA(cudaMemcpyAsync(s->ctl, hdr, sizeof hdr, cudaMemcpyHostToDevice, st));
+  PB_TRY_CUDA(cudaGraphLaunch(s->graph, st));
+  pb_count_launch(s->graph_launches);
+  return PB_OK;
+}
+
+}  // namespace
+
+// =================================================================== C ABI
+extern "C" int pb_bonsai_create(const pb_bonsai_cfg* cfg, int device, pb_bonsai** out) {
+  if (!cfg || !out) return pb_set_error(PB_EINVAL, "pb_bonsai_create: null argument");
+  *out = nullptr;
+  const pb_bonsai_cfg& c = *cfg;
+  if (c.hidden <= 0 || c.hidden % 256 || c.hidden > 8192 || c.inter <= 0 || c.inter % 256 ||
+      c.n_layers <= 0 || c.n_heads <= 0 || c.n_kv <= 0 || c.n_heads % c.n_kv || c.n_heads % 2 ||
+      (c.n_heads / c.n_kv) % 2 || c.n_heads / c.n_kv > 8 || c.vocab <= 0)
+    return pb_set_error(PB_EINVAL, "pb_bonsai_create: unsupported shape (hidden %% 256, <= 8192; "
+                                   "inter %% 256; n_heads/n_kv even and <= 8)");
+  PB_TRY_CUDA(cudaSetDevice(device));
+  pb_bonsai* m = new pb_bonsai();
+  m->c = c;
+  m->device = device;
+  m->QD = c.n_heads * BS_HD;
+  m->KD = c.n_kv * BS_HD;
+  const int H = c.hidden, F = c.inter, L = c.n_layers;
+  auto bytes = [](int rows, int K) { return a256((size_t)rows * (K / 32) * 4) + a256((size_t)rows * (K / 128) * 2); };
+  const size_t layer_b = bytes(m->QD + 2 * m->KD, H) + bytes(H, m->QD) + bytes(2 * F, H) + bytes(H, F);
+  const size_t norm_b = a256(((size_t)L * (2 * H + 2 * BS_HD) + H) * 4);
+  const size_t tot = layer_b * L + 2 * bytes(c.vocab, H) + norm_b;
+  if (cudaMalloc(&m->arena, tot) != cudaSuccess) {
+    cudaGetLastError();
+    delete m;
+    return pb_set_error(PB_ENOMEM, "pb_bonsai_create: %zu bytes", tot);
+  }
+  char* p = m->arena;
+  auto carve = [&](pb_q1& t, int rows, int K) {
+    t.rows = rows; t.K = K; t.owner = false;
+    t.bits = reinterpret_cast<uint32_t*>(p); p += a256((size_t)rows * (K / 32) * 4);
+    t.scales = reinterpret_cast<uint16_t*>(p); p += a256((size_t)rows * (K / 128) * 2);
+  };
+  m->qkv.resize(L); m->o.resize(L); m->gu.resize(L); m->down.resize(L);
+  for (int l = 0; l < L; l++) {
+    carve(m->qkv[l], m->QD + 2 * m->KD, H);
+    carve(m->o[l], H, m->QD);
+    carve(m->gu[l], 2 * F, H);
+    carve(m->down[l], H, F);
+  }
+  carve(m->emb, c.vocab, H);
+  carve(m->head, c.vocab, H);
+  m->norms = reinterpret_cast<float*>(p);
+  m->have.assign(L, 0u);
+  m->weight_bytes = tot;
+  *out = m;
+  return PB_OK;
+}
+
+extern "C" int pb_bonsai_destroy(pb_bonsai* m) {
+  if (!m) return PB_OK;
+  cudaSetDevice(m->device);
+  cudaFree(m->arena);
+  delete m;
+  return PB_OK;
+}
+
+extern "C" int pb_bonsai_set_q1(pb_bonsai* m, int layer, int slot, const uint8_t* blocks, int src_on_device,
+                                void* stream) {
+  if (!m || !blocks) return pb_set_error(PB_EINVAL, "pb_bonsai_set_q1: null argument");
+  const pb_bonsai_cfg& c = m->c;
+  pb_q1* t = nullptr;
+  int rows = 0, row0 = 0;
+  unsigned bit = 0;
+  if (layer < 0) {
+    if (slot == PB_BS_EMBED) { t = &m->emb; rows = c.vocab; bit = 1; }
+    else if (slot == PB_BS_HEAD) { t = &m->head; rows = c.vocab; bit = 2; }
+  } else if (layer < c.n_layers) {
+    switch (slot) {
+      case PB_BS_Q: t = &m->qkv[layer]; rows = m->QD; row0 = 0; break;
+      case PB_BS_K: t = &m->qkv[layer]; rows = m->KD; row0 = m->QD; break;
+      case PB_BS_V: t = &m->qkv[layer]; rows = m->KD; row0 = m->QD + m->KD; break;
+      case PB_BS_O: t = &m->o[layer]; rows = c.hidden; break;
+      case PB_BS_GATE: t = &m->gu[layer]; rows = c.inter; row0 = 0; break;
+      case PB_BS_UP: t = &m->gu[layer]; rows = c.inter; row0 = c.inter; break;
+      case PB_BS_DOWN: t = &m->down[layer]; rows = c.hidden; break;
+      default: break;
+    }
+    bit = 1u << slot;
+  }
+  if (!t) return pb_set_error(PB_EINVAL, "pb_bonsai_set_q1: bad layer %d / slot %d", layer, slot);
+  PB_TRY_CUDA(cudaSetDevice(m->device));
+  cudaStream_t st = (cudaStream_t)stream;
+  const size_t nbytes = (size_t)rows * (t->K / 128) * 18;
+  const uint8_t* src = blocks;
+  uint8_t* tmp = nullptr;
+  if (!src_on_device) {
+    PB_TRY_CUDA(cudaMalloc(&tmp, nbytes));
+    if (cudaMemcpyAsync(tmp, blocks, nbytes, cudaMemcpyHostToDevice, st) != cudaSuccess) {
+      cudaFree(tmp);
+      return pb_set_error(PB_ECUDA, "pb_bonsai_set_q1: upload");
+    }
+    src = tmp;
+  }
+  int rc = pb_q1_pack_into(t, src, rows, row0, st);
+  if (rc == PB_OK && cudaStreamSynchronize(st) != cudaSuccess)
+    rc = pb_set_error(PB_ECUDA, "pb_bonsai_set_q1: %s", cudaGetErrorString(cudaGetLastError()));
+  cudaFree(tmp);
+  if (rc == PB_OK) {
+    if (layer < 0) m->have_top |= bit; else m->have[layer] |= bit;
+  }
+  return rc;
+}
+
+extern "C" int pb_bonsai_set_norm(pb_bonsai* m, int layer, int slot, const float* w, int src_on_device,
+                                  void* stream) {
+  if (!m || !w) return pb_set_error(PB_EINVAL, "pb_bonsai_set_norm: null argument");
+  const pb_bonsai_cfg& c = m->c;
+  const int H = c.hidden;
+  size_t off = 0, n = 0;
+  if (layer < 0 && slot == PB_BS_OUT_NORM) { off = (size_t)c.n_layers * (2 * H + 2 * BS_HD); n = H; }
+  else if (layer >= 0 && layer < c.n_layers && slot >= PB_BS_ATTN_NORM && slot <= PB_BS_K_NORM) {
+    const size_t base = (size_t)layer * (2 * H + 2 * BS_HD);
+    const size_t offs[4] = {0, (size_t)H, 2 * (size_t)H, 2 * (size_t)H + BS_HD};
+    off = base + offs[slot];
+    n = slot < PB_BS_Q_NORM ? H : BS_HD;
+  } else {
+    return pb_set_error(PB_EINVAL, "pb_bonsai_set_norm: bad layer %d / slot %d", layer, slot);
+  }
+  PB_TRY_CUDA(cudaSetDevice(m->device));
+  cudaStream_t st = (cudaStream_t)stream;
+  PB_TRY_CUDA(cudaMemcpyAsync(m->norms + off, w, n * 4, src_on_device ? cudaMemcpyDeviceToDevice : cudaMemcpyHostToDevice, st));
+  PB_TRY_CUDA(cudaStreamSynchronize(st));
+  if (layer < 0) m->have_top |= 4u; else m->have[layer] |= 1u << (7 + slot);
+  return PB_OK;
+}
+
+extern "C" int pb_bonsai_state_create(pb_bonsai* m, int max_ctx, pb_bonsai_state** out) {
+  if (!m || !out || max_ctx <= 0 || max_ctx % 32) return pb_set_error(PB_EINVAL, "pb_bonsai_state_create: bad argument (max_ctx a positive multiple of 32)");
+  *out = nullptr;
+  if (pv_smem(max_ctx) > 200 * 1024) return pb_set_error(PB_ENOTSUP, "pb_bonsai_state_create: max_ctx %d too large (<= 8192)", max_ctx);
+  PB_TRY_CUDA(cudaSetDevice(m->device));
+  const pb_bonsai_cfg& c = m->c;
+  const int H = c.hidden, F = c.inter, NH = c.n_heads, NKV = c.n_kv;
+  pb_bonsai_state* s = new pb_bonsai_state();
+  s->m = m;
+  s->max_ctx = max_ctx;
+  const size_t kvb = (size_t)c.n_layers * 2 * NKV * max_ctx * BS_HD * 2;
+  const int kmax = std::max(std::max(H, F), m->QD);
+  const size_t sizes[] = {kvb, (size_t)max_ctx * BS_HD * 4, (size_t)H * 4, (size_t)H * 4, (size_t)H * 4,
+                          (size_t)(m->QD + 2 * m->KD) * 4, (size_t)NH * BS_HD * 2, (size_t)NH * max_ctx * 4,
+                          (size_t)m->QD * 4, (size_t)H * 4, (size_t)2 * F * 4, (size_t)H * 4,
+                          (size_t)(kmax / 256) * 292, (size_t)c.vocab * 4, sizeof(BsCtl)};
+  size_t tot = 0;
+  for (size_t x : sizes) tot += a256(x);
+  if (cudaMalloc(&s->mem, tot) != cudaSuccess) {
+    cudaGetLastError();
+    delete s;
+    return pb_set_error(PB_ENOMEM, "pb_bonsai_state_create: %zu bytes", tot);
+  }
+  char* p = s->mem;
+  size_t k = 0;
+  auto take = [&]() { char* r = p; p += a256(sizes[k++]); return r; };
+  s->kv = reinterpret_cast<uint16_t*>(take());
+  s->rope = reinterpret_cast<float*>(take());
+  s->x[0] = reinterpret_cast<float*>(take());
+  s->x[1] = reinterpret_cast<float*>(take());
+  s->xin = reinterpret_cast<float*>(take());
+  s->qkv = reinterpret_cast<float*>(take());
+  s->qh = reinterpret_cast<uint16_t*>(take());
+  s->scores = reinterpret_cast<float*>(take());
+  s->atto = reinterpret_cast<float*>(take());
+  s->ao = reinterpret_cast<float*>(take());
+  s->gu = reinterpret_cast<float*>(take());
+  s->fo = reinterpret_cast<float*>(take());
+  s->xq = reinterpret_cast<uint8_t*>(take());
+  s->logits = reinterpret_cast<float*>(take());
+  s->ctl = reinterpret_cast<BsCtl*>(take());
+  int rc = PB_OK;
+  if (cudaMemset(s->mem, 0, tot) != cudaSuccess) rc = pb_set_error(PB_ECUDA, "pb_bonsai_state_create: memset");
+  if (rc == PB_OK && cudaMallocHost(&s->h_ctl, sizeof(BsCtl)) != cudaSuccess) rc = pb_set_error(PB_ENOMEM, "pb_bonsai_state_create: pinned");
+  if (rc == PB_OK) {
+    memset(s->h_ctl, 0, sizeof(BsCtl));
+    std::vector<float> tab((size_t)max_ctx * BS_HD);
+    for (int pos = 0; pos < max_ctx; pos++) bs_rope_table(c, pos, tab.data() + (size_t)pos * BS_HD);
+    if (cudaMemcpy(s->rope, tab.data(), tab.size() * 4, cudaMemcpyHostToDevice) != cudaSuccess)
+      rc = pb_set_error(PB_ECUDA, "pb_bonsai_state_create: rope table");
+  }
+  if (rc != PB_OK) {
+    cudaFree(s->mem); if (s->h_ctl) cudaFreeHost(s->h_ctl);
+    delete s;
+    return rc;
+  }
+  *out = s;
+  return PB_OK;
+}
+
+extern "C" int pb_bonsai_state_destroy(pb_bonsai_state* s) {
+  if (!s) return PB_OK;
+  cudaSetDevice(s->m->device);
+  if (s->graph) cudaGraphExecDestroy(s->graph);
+  cudaFree(s->mem);
+  cudaFreeHost(s->h_ctl);
+  delete s;
+  return PB_OK;
+}
+
+extern "C" int pb_bonsai_state_kv(pb_bonsai_state* s, int layer, int which, void** d_ptr) {
+  if (!s || !d_ptr || layer < 0 || layer >= s->m->c.n_layers || which < 0 || which > 1)
+    return pb_set_error(PB_EINVAL, "pb_bonsai_state_kv: bad argument");
+  *d_ptr = s->kv + ((size_t)layer * 2 + which) * s->m->c.n_kv * s->max_ctx * BS_HD;
+  return PB_OK;
+}
+
+extern "C" int pb_bonsai_state_residual(pb_bonsai_state* s, float* d_x, void* stream) {
+  if (!s || !d_x) return pb_set_error(PB_EINVAL, "pb_bonsai_state_residual: null argument");
+  PB_TRY_CUDA(cudaMemcpyAsync(d_x, s->x[s->final_x], (size_t)s->m->c.hidden * 4, cudaMemcpyDeviceToDevice,
+                              (cudaStream_t)stream));
+  return PB_OK;
+}
+
+extern "C" int pb_bonsai_decode(pb_bonsai* m, pb_bonsai_state* s, int token, int pos, const float* d_x,
+                                float* d_logits, int* out_id, void* stream) {
+  if (!m || !s || s->m != m) return pb_set_error(PB_EINVAL, "pb_bonsai_decode: bad argument");
+  PB_TRY_CUDA(cudaSetDevice(m->device));
+  cudaStream_t st = (cudaStream_t)stream;
+  if (d_x) PB_TRY_CUDA(cudaMemcpyAsync(s->xin, d_x, (size_t)m->c.hidden * 4, cudaMemcpyDeviceToDevice, st));
+  int rc = bs_step(m, s, token, pos, d_x != nullptr, st);
+  if (rc) return rc;
+  if (d_logits) PB_TRY_CUDA(cudaMemcpyAsync(d_logits, s->logits, (size_t)m->c.vocab * 4, cudaMemcpyDeviceToDevice, st));
+  if (out_id) {
+    PB_TRY_CUDA(cudaMemcpyAsync(&s->h_ctl->top, &s->ctl->top, sizeof(int), cudaMemcpyDeviceToHost, st));
+    PB_TRY_CUDA(cudaStreamSynchronize(st));
+    *out_id = s->h_ctl->top;
+  }
+  return PB_OK;
+}
+
+extern "C" int pb_bonsai_decode_greedy(pb_bonsai* m, pb_bonsai_state* s, int token, int pos, int n, int* d_ids,
+                                       void* stream) {
+  if (!m || !s || s->m != m || n <= 0) return pb_set_error(PB_EINVAL, "pb_bonsai_decode_greedy: bad argument");
+  if (pos + n > s->max_ctx) return pb_set_error(PB_EINVAL, "pb_bonsai_decode_greedy: pos %d + %d exceeds max_ctx", pos, n);
+  PB_TRY_CUDA(cudaSetDevice(m->device));
+  cudaStream_t st = (cudaStream_t)stream;
+  int rc;
+  if ((rc = bs_graph(m, s, st))) return rc;
+  const int hdr[4] = {token, pos, 0, 0};
+  PB_TRY_CUDA(cudaMemcpyAsync(s->ctl, hdr, sizeof hdr, cudaMemcpyHostToDevice, st));
+  PB_TRY_CUDA(cudaMemcpyAsync(&s->ctl->ids, &d_ids, sizeof(int*), cudaMemcpyHostToDevice, st));
+  for (int i = 0; i < n; i++) {
+    PB_TRY_CUDA(cudaGraphLaunch(s->graph, st));
+    pb_count_launch(s->graph_launches);
+  }
+  int* null_ids = nullptr;
+  PB_TRY_CUDA(cudaMemcpyAsync(&s->ctl->ids, &null_ids, sizeof(int*), cudaMemcpyHostToDevice, st));
+  PB_TRY_CUDA(cudaStreamSynchronize(st));
+  return PB_OK;
+}
+
+extern "C" int pb_bonsai_state_fallbacks(pb_bonsai_state* s, int* out) {
+  if (!s || !out) return pb_set_error(PB_EINVAL, "pb_bonsai_state_fallbacks: null argument");
+  PB_TRY_CUDA(cudaMemcpy(out, &s->ctl->fallbacks, sizeof(int), cudaMemcpyDeviceToHost));
+  return PB_OK;
+}

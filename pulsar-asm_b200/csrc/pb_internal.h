@@ -75,3 +75,9 @@ int pb_num_sms();
 // chunked prefill: bytes of the copy, and the conversion into caller storage
 size_t pb_q80tc_bytes(int N, int K);
 int pb_q80tc_from_stream(const pb_q8* src, char* storage, pb_q8* out, cudaStream_t st);
+
+// Q1_0 GEMV launch (pdl: programmatic dependent launch) and packing of device
+// Q1_0 blocks into rows [row0, row0 + rows) of an allocated tensor
+int pb_q1_gemv_launch(const pb_q1* w, const uint8_t* d_xq, float* d_y, int32_t* d_isum,
+                      cudaStream_t st, bool pdl);
+int pb_q1_pack_into(pb_q1* w, const uint8_t* d_blocks, int rows, int row0, cudaStream_t st);

@@ -15,6 +15,7 @@
 // (q_k, q_{k+8}, q_{k+16}, q_{k+24}), k = 0..7.
 #include "pb_common.cuh"
 #include "pb_internal.h"
+#include "pb_q8k.cuh"
 #include <cstdio>
 #include <cstring>
 #include <map>
@@ -39,62 +40,12 @@ __global__ void k_q1_pack(const uint8_t* __restrict__ src, uint32_t* __restrict_
 }
 
 // ------------------------------------------------------- Q8_K quantiser
-// fwd8.c:67-139 as stated in scalar form by pq1_parity.c:131-147: amax and the
-// value at the FIRST index reaching it, iscale = -127/mx, q = min(127,
-// nearest_int(fma(x, iscale, 1.5*2^23))), d = 1/iscale, int16 bsums per 16.
-// One CTA (256 threads) per 256-value block.
+// One CTA (256 threads) per 256-value block (pb_q8k.cuh).
 __global__ void __launch_bounds__(256) k_q8k_quantize(const float* __restrict__ x,
                                                       uint8_t* __restrict__ xq) {
-  const int b = blockIdx.x, t = threadIdx.x, lane = t & 31, wid = t >> 5;
-  const float v = x[(size_t)b * 256 + t];
-  float a = fabsf(v);
-  int idx = t;
-  // (max |x|, first index) reduction
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) {
-    const float oa = __shfl_down_sync(0xffffffffu, a, o);
-    const int oi = __shfl_down_sync(0xffffffffu, idx, o);
-    if (oa > a || (oa == a && oi < idx)) { a = oa; idx = oi; }
-  }
-  __shared__ float sa[8];
-  __shared__ int si[8];
-  __shared__ float smx;
-  __shared__ int sidx;
-  if (lane == 0) { sa[wid] = a; si[wid] = idx; }
-  __syncthreads();
-  if (t == 0) {
-    float ba = sa[0]; int bi = si[0];
-    for (int w = 1; w < 8; w++) if (sa[w] > ba) { ba = sa[w]; bi = si[w]; }
-    smx = ba; sidx = bi;
-  }
-  __syncthreads();
-  uint8_t* qb = xq + (size_t)b * 292;
-  const float amax = smx;
-  if (amax == 0.0f) {   // whole block zero: d, qs and bsums all zero bytes
-    for (int i = t; i < 292; i += 256) qb[i] = 0;
-    return;
-  }
-  const float mx = x[(size_t)b * 256 + sidx];
-  const float iscale = __fdiv_rn(-127.0f, mx);
-  const float f = __fmaf_rn(v, iscale, 12582912.0f);
-  int q = (int)(__float_as_uint(f) & 0x007fffffu) - 0x00400000;
-  q = q < 127 ? q : 127;
-  qb[4 + t] = (uint8_t)(int8_t)q;
-  // bsums: 16 consecutive values = half a warp
-  int s = q;
-#pragma unroll
-  for (int o = 8; o > 0; o >>= 1) s += __shfl_down_sync(0xffffffffu, s, o, 16);
-  if ((lane & 15) == 0) {
-    const int16_t s16 = (int16_t)s;
-    const int g = t >> 4;
-    qb[260 + 2 * g] = (uint8_t)(s16 & 0xff);
-    qb[261 + 2 * g] = (uint8_t)((uint16_t)s16 >> 8);
-  }
-  if (t == 0) {
-    const float d = __fdiv_rn(1.0f, iscale);
-    const unsigned u = __float_as_uint(d);
-    qb[0] = u & 0xff; qb[1] = (u >> 8) & 0xff; qb[2] = (u >> 16) & 0xff; qb[3] = u >> 24;
-  }
+  __shared__ Q8kScratch sc;
+  const int b = blockIdx.x;
+  pb_q8k_block256(x[(size_t)b * 256 + threadIdx.x], xq + (size_t)b * 292, sc);
 }
 
 // ------------------------------------------------------------ Q1 GEMV
@@ -116,6 +67,22 @@ k_q1_gemv(const uint4* __restrict__ bits, const uint16_t* __restrict__ wsc,
   float* dbs = reinterpret_cast<float*>(asum + ng);                 // ng (db per group)
   float* prod = dbs + ng;                                           // 8 warps x Q1_R x (ng + 1)
   unsigned char* raw = reinterpret_cast<unsigned char*>(prod + (size_t)8 * Q1_R * ps);   // nbk * 292
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int row_first = (blockIdx.x * 8 + warp) * Q1_R;
+  // the first weight words do not depend on the previous kernel: request them
+  // before waiting on it (programmatic dependent launch; no-op otherwise)
+  uint4 wv0[Q1_R];
+  unsigned short hs0[Q1_R];
+  if (row_first < rows && lane < ng) {
+#pragma unroll
+    for (int r = 0; r < Q1_R; r++) {
+      const int row = min(row_first + r, rows - 1);
+      wv0[r] = pb_ldg_stream(bits + (size_t)row * ng + lane);
+      hs0[r] = wsc[(size_t)row * ng + lane];
+    }
+  }
+  pb_grid_launch_dependents();
+  pb_grid_wait();
   // the Q8_K activation into shared memory once (coalesced words), then
   // permuted from there
   for (int i = threadIdx.x; i < nbk * 73; i += blockDim.x)
@@ -153,17 +120,21 @@ k_q1_gemv(const uint4* __restrict__ bits, const uint16_t* __restrict__ wsc,
     }
   }
   __syncthreads();
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   float* pw = prod + (size_t)warp * Q1_R * ps;
-  for (int row0 = (blockIdx.x * 8 + warp) * Q1_R; row0 < rows; row0 += gridDim.x * 8 * Q1_R) {
+  for (int row0 = row_first; row0 < rows; row0 += gridDim.x * 8 * Q1_R) {
     for (int g = lane; g < ng; g += 32) {
       uint4 wv[Q1_R];
       unsigned short hs[Q1_R];
+      if (row0 == row_first && g == lane) {
 #pragma unroll
-      for (int r = 0; r < Q1_R; r++) {
-        const int row = min(row0 + r, rows - 1);
-        wv[r] = pb_ldg_stream(bits + (size_t)row * ng + g);
-        hs[r] = wsc[(size_t)row * ng + g];
+        for (int r = 0; r < Q1_R; r++) { wv[r] = wv0[r]; hs[r] = hs0[r]; }
+      } else {
+#pragma unroll
+        for (int r = 0; r < Q1_R; r++) {
+          const int row = min(row0 + r, rows - 1);
+          wv[r] = pb_ldg_stream(bits + (size_t)row * ng + g);
+          hs[r] = wsc[(size_t)row * ng + g];
+        }
       }
       const uint4* av = reinterpret_cast<const uint4*>(act + (size_t)g * PB_Q1_GSTRIDE);
       int P[Q1_R];
@@ -207,21 +178,38 @@ static size_t q1_smem(int K) {
          (size_t)(K / 256) * 292;
 }
 
-static int q1_gemv_launch(const pb_q1* w, const uint8_t* d_xq, float* d_y, int32_t* d_isum,
-                          cudaStream_t st) {
+int pb_q1_gemv_launch(const pb_q1* w, const uint8_t* d_xq, float* d_y, int32_t* d_isum,
+                      cudaStream_t st, bool pdl) {
   const size_t smem = q1_smem(w->K);
   if (smem > 220 * 1024) return pb_set_error(PB_ENOTSUP, "pb_q1_gemv: K=%d too large", w->K);
-  static bool attr = false;
-  if (!attr) {
+  static bool smem_set[64] = {};   // the attribute is per device
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= 64 || !smem_set[dev]) {
     cudaFuncSetAttribute(k_q1_gemv, cudaFuncAttributeMaxDynamicSharedMemorySize, 220 * 1024);
-    attr = true;
+    if (dev >= 0 && dev < 64) smem_set[dev] = true;
   }
   int grid = 4 * pb_num_sms();
   if (grid * 8 * Q1_R > w->rows) grid = (w->rows + 8 * Q1_R - 1) / (8 * Q1_R);
-  k_q1_gemv<<<grid, 256, smem, st>>>(reinterpret_cast<const uint4*>(w->bits), w->scales, d_xq,
-                                    d_y, d_isum, w->rows, w->K);
-  PB_LAUNCHED("k_q1_gemv");
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(256);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl ? 1 : 0;
+  cudaError_t e = cudaLaunchKernelEx(&cfg, k_q1_gemv, reinterpret_cast<const uint4*>(w->bits),
+                                     (const uint16_t*)w->scales, d_xq, d_y, d_isum, w->rows, w->K);
+  if (e != cudaSuccess) return pb_set_error(PB_ECUDA, "launch k_q1_gemv: %s", cudaGetErrorString(e));
+  pb_count_launch();
   return PB_OK;
+}
+static int q1_gemv_launch(const pb_q1* w, const uint8_t* d_xq, float* d_y, int32_t* d_isum,
+                          cudaStream_t st) {
+  return pb_q1_gemv_launch(w, d_xq, d_y, d_isum, st, false);
 }
 
 // ---------------------------------------------------------------- C ABI
@@ -259,6 +247,17 @@ extern "C" int pb_q1_pack(const uint8_t* blocks, int rows, int K, int src_on_dev
   cudaFree(tmp);
   if (rc != PB_OK) { cudaFree(w->bits); cudaFree(w->scales); delete w; return rc; }
   *out = w;
+  return PB_OK;
+}
+
+// device Q1_0 blocks of `rows` rows into w's storage from row row0 on (the
+// merged tensors of the Bonsai decoder are filled this way)
+int pb_q1_pack_into(pb_q1* w, const uint8_t* d_blocks, int rows, int row0, cudaStream_t st) {
+  if (row0 < 0 || row0 + rows > w->rows) return pb_set_error(PB_EINVAL, "pb_q1_pack_into: rows out of range");
+  const size_t nblk = (size_t)rows * (w->K / 128);
+  k_q1_pack<<<(unsigned)((nblk + 255) / 256), 256, 0, st>>>(d_blocks, w->bits + (size_t)row0 * (w->K / 32),
+                                                           w->scales + (size_t)row0 * (w->K / 128), rows, w->K);
+  PB_LAUNCHED("k_q1_pack");
   return PB_OK;
 }
 

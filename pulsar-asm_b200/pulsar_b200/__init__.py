@@ -102,8 +102,26 @@ def lib():
     L.pb_state_status.argtypes = [vp, vp]
     L.pb_prefill_chunk.argtypes = [vp, vp, vp, i, i, vp, vp, vp]
     L.pb_decode_batch.argtypes = [vp, C.POINTER(vp), i, vp, vp, vp, vp, vp]
+    L.pb_bonsai_create.argtypes = [C.POINTER(BonsaiCfg), i, pvp]
+    L.pb_bonsai_destroy.argtypes = [vp]
+    L.pb_bonsai_set_q1.argtypes = [vp, i, i, vp, i, vp]
+    L.pb_bonsai_set_norm.argtypes = [vp, i, i, vp, i, vp]
+    L.pb_bonsai_state_create.argtypes = [vp, i, pvp]
+    L.pb_bonsai_state_destroy.argtypes = [vp]
+    L.pb_bonsai_state_kv.argtypes = [vp, i, i, pvp]
+    L.pb_bonsai_state_residual.argtypes = [vp, vp, vp]
+    L.pb_bonsai_state_fallbacks.argtypes = [vp, C.POINTER(i)]
+    L.pb_bonsai_decode.argtypes = [vp, vp, i, i, vp, vp, C.POINTER(i), vp]
+    L.pb_bonsai_decode_greedy.argtypes = [vp, vp, i, i, i, vp, vp]
     _lib = L
     return L
+
+
+class BonsaiCfg(C.Structure):
+    """pb_bonsai_cfg (include/pulsar_b200.h)"""
+    _fields_ = [(n, C.c_int) for n in ("hidden", "inter", "n_layers", "n_heads", "n_kv", "vocab")] + \
+               [("rope_factor", C.c_float), ("rope_orig_ctx", C.c_int), ("rope_base", C.c_float),
+                ("attn_scale", C.c_float)]
 
 
 def last_error():
@@ -378,3 +396,112 @@ def _view_device(ptr, nbytes):
     a.__cuda_array_interface__ = {"shape": (nbytes,), "typestr": "|u1", "data": (ptr, False),
                                   "version": 3, "strides": None}
     return torch.as_tensor(a, device="cuda")
+
+
+class Bonsai:
+    """The Bonsai Q1_0 decoder (fwd8.c token step) on one GPU. `cfg` holds
+    hidden, inter, n_layers, n_heads, n_kv, vocab, rope_factor, rope_orig_ctx,
+    rope_base, attn_scale; `weights` is shaped like
+    pulsar_b200.synth.make_bonsai_weights (Q1_0 18-byte blocks per tensor)."""
+
+    SLOTS = {"q": 0, "k": 1, "v": 2, "o": 3, "gate": 4, "up": 5, "down": 6}
+    NORMS = {"attn_norm": 0, "ffn_norm": 1, "q_norm": 2, "k_norm": 3}
+
+    def __init__(self, cfg, weights=None, device=0, stream=None):
+        import numpy as np
+        c = BonsaiCfg(cfg["hidden"], cfg["inter"], cfg["n_layers"], cfg["n_heads"], cfg["n_kv"],
+                      cfg["vocab"], cfg["rope_factor"], cfg["rope_orig_ctx"], cfg["rope_base"],
+                      cfg["attn_scale"])
+        h = C.c_void_p()
+        check(lib().pb_bonsai_create(C.byref(c), device, C.byref(h)))
+        self.h, self.cfg = h, dict(cfg)
+        if weights is not None:
+            st = _stream(stream)
+            for li, lw in enumerate(weights["layers"]):
+                for name, slot in self.SLOTS.items():
+                    self.set_q1(li, slot, lw[name], st)
+                for name, slot in self.NORMS.items():
+                    self.set_norm(li, slot, lw[name], st)
+            self.set_q1(-1, 16, weights["embed"], st)
+            if weights.get("head") is not None:
+                self.set_q1(-1, 17, weights["head"], st)
+            self.set_norm(-1, 16, weights["out_norm"], st)
+
+    def set_q1(self, layer, slot, blocks, st=None):
+        """blocks: Q1_0 bytes [rows][K/128][18], numpy (host) or a CUDA tensor"""
+        import numpy as np
+        st = st if st is not None else _stream()
+        if hasattr(blocks, "is_cuda") and blocks.is_cuda:
+            check(lib().pb_bonsai_set_q1(self.h, layer, slot, C.c_void_p(blocks.data_ptr()), 1, st))
+            return
+        b = np.ascontiguousarray(blocks, dtype=np.uint8)
+        check(lib().pb_bonsai_set_q1(self.h, layer, slot, b.ctypes.data_as(C.c_void_p), 0, st))
+
+    def set_norm(self, layer, slot, w, st=None):
+        import numpy as np
+        a = np.ascontiguousarray(w, dtype=np.float32)
+        check(lib().pb_bonsai_set_norm(self.h, layer, slot, a.ctypes.data_as(C.c_void_p), 0,
+                                       st if st is not None else _stream()))
+
+    def new_state(self, max_ctx):
+        return BonsaiState(self, max_ctx)
+
+    def close(self):
+        if self.h:
+            lib().pb_bonsai_destroy(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+class BonsaiState:
+    """One sequence: f16 K/V cache and rope table (pb_bonsai_state)."""
+
+    def __init__(self, model, max_ctx):
+        h = C.c_void_p()
+        check(lib().pb_bonsai_state_create(model.h, max_ctx, C.byref(h)))
+        self.h, self.model, self.max_ctx = h, model, max_ctx
+
+    def decode(self, token, pos, x=None, logits=None, want_id=True, stream=None):
+        """one token; returns the greedy id (synchronises) when want_id."""
+        out = C.c_int(-1)
+        check(lib().pb_bonsai_decode(self.model.h, self.h, int(token), int(pos), _ptr(x), _ptr(logits),
+                                     C.byref(out) if want_id else None, _stream(stream)))
+        return out.value if want_id else None
+
+    def decode_greedy(self, token, pos, n, ids, stream=None):
+        check(lib().pb_bonsai_decode_greedy(self.model.h, self.h, int(token), int(pos), int(n), _ptr(ids),
+                                            _stream(stream)))
+
+    def kv(self, layer, which):
+        """torch int16 view [n_kv][max_ctx][128] of a layer's K (0) or V (1) cache"""
+        import torch
+        p = C.c_void_p()
+        check(lib().pb_bonsai_state_kv(self.h, layer, which, C.byref(p)))
+        c = self.model.cfg
+        n = c["n_kv"] * self.max_ctx * 128 * 2
+        return _view_device(p.value, n).view(torch.int16).view(c["n_kv"], self.max_ctx, 128)
+
+    def residual(self, out, stream=None):
+        check(lib().pb_bonsai_state_residual(self.h, _ptr(out), _stream(stream)))
+
+    def fallbacks(self):
+        v = C.c_int(0)
+        check(lib().pb_bonsai_state_fallbacks(self.h, C.byref(v)))
+        return v.value
+
+    def destroy(self):
+        if self.h:
+            lib().pb_bonsai_state_destroy(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.destroy()
+        except Exception:
+            pass
+

@@ -128,3 +128,53 @@ def kv_bytes_per_token(c, ctx):
     """fp16 K and V read by the attention layers at context ctx."""
     n_attn = len(c["attn_layers"])
     return n_attn * 2 * ctx * c["n_kv"] * c["head_dim"] * 2
+
+
+# ------------------------------------------------------------------ Bonsai ----
+# Bonsai-8B shape (fwd8.c:35-57): YaRN factor 4 over an original 16384-token
+# context, base 1e6, attention scale 1/sqrt(128) as fwd8.c:566 writes it
+BONSAI_CFG3 = dict(hidden=4096, inter=12288, n_layers=36, n_heads=32, n_kv=8, vocab=151936,
+                   rope_factor=4.0, rope_orig_ctx=16384, rope_base=1e6, attn_scale=0.0883883476)
+# small model for parity tests: same kernels, quick oracle
+BONSAI_TINY = dict(hidden=1024, inter=2048, n_layers=2, n_heads=8, n_kv=2, vocab=2048,
+                   rope_factor=4.0, rope_orig_ctx=16384, rope_base=1e6, attn_scale=0.0883883476)
+
+
+def q1_blocks(rng, rows, K, scale=0.02):
+    """Q1_0 18-byte blocks [rows][K/128]: fp16 scale |N(0,1)|*scale, then 16
+    bytes of uniform sign bits"""
+    nb = K // 128
+    b = rng.integers(0, 256, size=(rows, nb, 18), dtype=np.uint8)
+    sc = (np.abs(rng.standard_normal((rows, nb), dtype=np.float32)) * np.float32(scale)).astype(np.float16)
+    b[:, :, 0:2] = sc.view(np.uint8).reshape(rows, nb, 2)
+    return b
+
+
+def make_bonsai_weights(c, seed=4321, tied=True):
+    rng = np.random.default_rng(seed)
+    H, F, NH, NKV = c["hidden"], c["inter"], c["n_heads"], c["n_kv"]
+
+    def norm(n):
+        return (1.0 + 0.05 * rng.standard_normal(n)).astype(np.float32)
+    layers = []
+    for _ in range(c["n_layers"]):
+        layers.append(dict(q=q1_blocks(rng, NH * 128, H), k=q1_blocks(rng, NKV * 128, H),
+                           v=q1_blocks(rng, NKV * 128, H), o=q1_blocks(rng, H, NH * 128),
+                           gate=q1_blocks(rng, F, H), up=q1_blocks(rng, F, H), down=q1_blocks(rng, H, F),
+                           attn_norm=norm(H), ffn_norm=norm(H), q_norm=norm(128), k_norm=norm(128)))
+    emb = q1_blocks(rng, c["vocab"], H)
+    return dict(layers=layers, embed=emb, head=None if tied else q1_blocks(rng, c["vocab"], H),
+                out_norm=norm(H))
+
+
+def bonsai_bytes_per_token(c, ctx):
+    """algorithmic bytes of one decode token at context ctx: every Q1_0 tensor
+    (18 B per 128 weights), the norm vectors, the head once, and the f16 K and
+    V rows the attention reads"""
+    H, F, NH, NKV, L = c["hidden"], c["inter"], c["n_heads"], c["n_kv"], c["n_layers"]
+
+    def q(rows, K):
+        return rows * (K // 128) * 18
+    layer = q((NH + 2 * NKV) * 128, H) + q(H, NH * 128) + 2 * q(F, H) + q(H, F) + (2 * H + 256) * 4
+    kv = 2 * NKV * ctx * 128 * 2
+    return L * (layer + kv) + q(c["vocab"], H) + H * 4

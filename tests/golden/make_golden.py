@@ -16,6 +16,10 @@ Fixtures (numpy .npz, inputs and the reference's outputs):
                     with zero bitwise differences (single-chunk shapes, T = 1 and 4)
   q8_gemv_cpu.npz   the x86/C CPU GEMV gemv_q8 (.auto/lfm3/q8_gemv_cpu.c:29-60)
                     output, a different summation order: a tolerance fixture
+  bonsai.npz        the Bonsai step pieces: fwd8.c's rms (:312-317), YaRN rope
+                    table and rotation (:320-369, gcc's default contraction),
+                    pq1_host.c's f16 flash-attention decode (:373-434) and silu
+                    tail (:226), the last two with expf set to the oracle's
 """
 import os
 import sys
@@ -100,7 +104,55 @@ def main():
     yr = np.zeros(N, np.float32)
     R.pbref_gemv_q8(p(codes), p(s32), p(xf), p(yr), N, Kc)
     np.savez_compressed(os.path.join(HERE, "q8_gemv_cpu.npz"), codes=codes, s=s32, x=xb, y=yr)
+
+    # ---- Bonsai step pieces (fwd8.c rms and YaRN rope; pq1_host.c f16
+    #      attention and silu tail, their expf pointed at the oracle's)
+    np.savez_compressed(os.path.join(HERE, "bonsai.npz"), **bonsai_fixtures(R))
     print("golden fixtures written to", HERE)
+
+
+def set_expf_hook(R, on):
+    import ctypes as C
+    h = C.c_void_p.in_dll(R, "pbref_expf_hook")
+    h.value = C.cast(O.lib().pbo_expf, C.c_void_p).value if on else None
+
+
+def bonsai_fixtures(R):
+    p = O._p
+    rng = np.random.default_rng(8)
+    f = {}
+    for n in (4096, 128):
+        x = (rng.standard_normal(n) * 2).astype(np.float32)
+        w = (1 + 0.05 * rng.standard_normal(n)).astype(np.float32)
+        y = np.zeros(n, np.float32)
+        R.pbref_bs_rms(p(x), p(w), n, p(y))
+        f["rms%d_x" % n], f["rms%d_w" % n], f["rms%d_y" % n] = x, w, y
+    pos = np.array([0, 1, 7, 100, 1023, 2047, 8191, 16383], np.int32)
+    cs = np.zeros((len(pos), 128), np.float32)
+    for i, ps in enumerate(pos):
+        R.pbref_bs_rope_table(int(ps), p(cs[i]), p(cs[i, 64:]))
+    f["rope_pos"], f["rope_cs"] = pos, cs
+    xr = rng.standard_normal(4 * 128).astype(np.float32)
+    yr = xr.copy()
+    R.pbref_bs_rope(p(yr), 4, 37)
+    f["rope_x"], f["rope_y"] = xr, yr
+    set_expf_hook(R, True)
+    for T in (1, 2, 31, 33, 97, 512):
+        q = rng.standard_normal(128).astype(np.float32) * 3
+        K = rng.standard_normal((T, 128)).astype(np.float16).view(np.uint16)
+        V = rng.standard_normal((T, 128)).astype(np.float16).view(np.uint16)
+        if T > 8:
+            K[T // 2] = K[3]       # an exact tie of two scores
+        out = np.zeros(128, np.float32)
+        R.pbref_fa16_head(p(q), p(K), p(V), T, np.float32(0.0883883476), p(out))
+        f["fa%d_q" % T], f["fa%d_k" % T], f["fa%d_v" % T], f["fa%d_out" % T] = q, K, V, out
+    g = (rng.standard_normal(4096) * 4).astype(np.float32)
+    u = rng.standard_normal(4096).astype(np.float32)
+    o = u.copy()
+    R.pbref_silu_mul(p(o), p(g), 4096)
+    f["silu_g"], f["silu_u"], f["silu_out"] = g, u, o
+    set_expf_hook(R, False)
+    return f
 
 
 if __name__ == "__main__":

@@ -133,3 +133,76 @@ def test_pins_random_shapes(oracle):
         R.pbref_q1_gemv(rows, K, p(wb), p(sc), p(xq), p(yr))
         _, y = oracle.q1_gemv(wb, sc, xq, K)
         assert np.array_equal(y.view(np.uint32), yr.view(np.uint32))
+
+
+# ------------------------------------------------------------------ Bonsai ----
+def test_golden_bonsai_rms_rope(oracle):
+    """fwd8.c's rms (:312-317) and YaRN rope (:320-369) as the reference computes them"""
+    g = _load("bonsai.npz")
+    for n in (4096, 128):
+        y = oracle.bs_rms(g["rms%d_x" % n], g["rms%d_w" % n])
+        assert np.array_equal(y.view(np.uint32), g["rms%d_y" % n].view(np.uint32))
+    for i, pos in enumerate(g["rope_pos"]):
+        c, s = oracle.bs_rope_table(int(pos))
+        assert np.array_equal(np.concatenate([c, s]).view(np.uint32), g["rope_cs"][i].view(np.uint32)), pos
+    c, s = oracle.bs_rope_table(37)
+    y = oracle.bs_rope(g["rope_x"], c, s)
+    assert np.array_equal(y.view(np.uint32), g["rope_y"].view(np.uint32))
+
+
+def test_golden_bonsai_fa16_silu(oracle):
+    """pq1_host.c's f16 flash-attention decode (:373-434) and silu tail (:226),
+    bit for bit (both sides on the oracle's expf)"""
+    g = _load("bonsai.npz")
+    for T in (1, 2, 31, 33, 97, 512):
+        out = oracle.bs_fa16_head(g["fa%d_q" % T], g["fa%d_k" % T], g["fa%d_v" % T])
+        assert np.array_equal(out.view(np.uint32), g["fa%d_out" % T].view(np.uint32)), T
+    o = oracle.bs_silu_mul(g["silu_g"], g["silu_u"])
+    assert np.array_equal(o.view(np.uint32), g["silu_out"].view(np.uint32))
+
+
+@pytest.mark.skipif(not os.path.exists(os.path.join(os.path.dirname(GOLDEN), "..", "oracle", "_ref",
+                                                    "libpb_refpins.so")), reason="reference pins not built")
+def test_pins_bonsai_libm_expf(oracle):
+    """the reference's own attention and silu on the host libm's expf against
+    the oracle (pbo_expf): the departure stays at the f16 rounding level"""
+    import ctypes as C
+    R = oracle.ref()
+    p = oracle._p
+    rng = np.random.default_rng(5)
+    C.c_void_p.in_dll(R, "pbref_expf_hook").value = None
+    worst = 0.0
+    for T in (17, 300, 2048):
+        q = rng.standard_normal(128).astype(np.float32) * 3
+        K = rng.standard_normal((T, 128)).astype(np.float16).view(np.uint16)
+        V = rng.standard_normal((T, 128)).astype(np.float16).view(np.uint16)
+        ref = np.zeros(128, np.float32)
+        R.pbref_fa16_head(p(q), p(K), p(V), T, np.float32(0.0883883476), p(ref))
+        out = oracle.bs_fa16_head(q, K, V)
+        worst = max(worst, float(np.max(np.abs(out - ref)) / max(1e-3, np.abs(ref).max())))
+    assert worst < 2e-3, worst
+    g = (rng.standard_normal(4096) * 4).astype(np.float32)
+    u = rng.standard_normal(4096).astype(np.float32)
+    ref = u.copy()
+    R.pbref_silu_mul(p(ref), p(g), 4096)
+    out = oracle.bs_silu_mul(g, u)
+    rel = np.abs(out - ref) / np.maximum(np.abs(ref), 1e-30)
+    assert rel.max() < 1e-6, rel.max()
+
+
+def test_bonsai_oracle_decode_runs(oracle):
+    """the whole Bonsai step on a tiny model: deterministic, finite, and the
+    step's K/V rows are the post-rope f16 values it stored"""
+    import sys
+    sys.path.insert(0, os.path.join(os.path.dirname(GOLDEN), "..", "..", "pulsar-asm_b200"))
+    from pulsar_b200 import synth
+    c = synth.BONSAI_TINY
+    w = synth.make_bonsai_weights(c, seed=3)
+    a, b = oracle.BsModel(c, w, 32), oracle.BsModel(c, w, 32)
+    for pos, tok in enumerate([5, 99, 1000, 7]):
+        ia, la, xa = a.decode(tok, pos, want_logits=True)
+        ib, lb, xb = b.decode(tok, pos, want_logits=True)
+        assert ia == ib and np.array_equal(la, lb) and np.all(np.isfinite(la))
+        assert ia == int(np.argmax(la))
+    k = a.kv(0, 0)
+    assert np.any(k[:, 3] != 0) and not np.any(k[:, 4:] != 0)
