@@ -339,37 +339,9 @@ def bonsai_bench(torch, pb, peak, stream, steps=20, warmup=3):
     cache with N(0,1) f16 rows. Also timed end to end through the public
     call with a host token in and the host id out per step."""
     from pulsar_b200 import synth
-    c = dict(synth.BONSAI_CFG3)
     max_ctx = 2048
-    g = torch.Generator(device="cuda").manual_seed(SEED + 3)
-    H, F, NH, NKV = c["hidden"], c["inter"], c["n_heads"], c["n_kv"]
-    m = pb.Bonsai(c)
-
-    def q1(rows, K):
-        b = torch.randint(0, 256, (rows, K // 128, 18), dtype=torch.uint8, device="cuda", generator=g)
-        sc = (torch.randn((rows, K // 128), device="cuda", generator=g).abs() * 0.02).half()
-        b[:, :, :2].copy_(sc.view(torch.uint8).view(rows, K // 128, 2))
-        return b
-
-    def norm(n):
-        return (1.0 + 0.05 * torch.randn(n, generator=torch.Generator().manual_seed(n))).numpy()
-    st = pb._stream(stream)
-    shapes = {0: (NH * 128, H), 1: (NKV * 128, H), 2: (NKV * 128, H), 3: (H, NH * 128),
-              4: (F, H), 5: (F, H), 6: (H, F)}
-    for L in range(c["n_layers"]):
-        for slot, (r, k) in shapes.items():
-            m.set_q1(L, slot, q1(r, k), st)
-        for slot, n in ((0, H), (1, H), (2, 128), (3, 128)):
-            m.set_norm(L, slot, norm(n), st)
-    m.set_q1(-1, 16, q1(c["vocab"], H), st)
-    m.set_norm(-1, 16, norm(H), st)
-    s = m.new_state(max_ctx)
     pos0 = max_ctx - (warmup + steps)
-    for L in range(c["n_layers"]):
-        for which in (0, 1):
-            kv = s.kv(L, which)
-            kv.copy_(torch.randn(kv.shape, device="cuda", generator=g).half().view(torch.int16))
-            kv[:, pos0:].zero_()
+    c, m, s = bonsai_setup(torch, pb, stream, max_ctx, pos0)
     ids = torch.empty(warmup + steps, dtype=torch.int32, device="cuda")
     with torch.cuda.stream(stream):
         s.decode_greedy(7, pos0, warmup, ids[:warmup], stream=stream)
@@ -402,6 +374,45 @@ def bonsai_bench(torch, pb, peak, stream, steps=20, warmup=3):
             "GB/s": nbytes / step_s / 1e9, "frac": nbytes / step_s / 1e9 / peak,
             "kernels_per_token": 36 * 10 + 4, "rms_serial_fallbacks": fb,
             "path": "CUDA graph of PDL launches: Q1_0 x Q8_K GEMVs, f16 flash-attention decode in fork order"}
+
+
+def bonsai_setup(torch, pb, stream, max_ctx, pos0, n_layers=None):
+    """the cfg3 model with seeded device weights and a state whose K/V cache
+    holds N(0,1) f16 rows at positions < pos0"""
+    from pulsar_b200 import synth
+    c = dict(synth.BONSAI_CFG3)
+    if n_layers:
+        c["n_layers"] = n_layers
+    g = torch.Generator(device="cuda").manual_seed(SEED + 3)
+    H, F, NH, NKV = c["hidden"], c["inter"], c["n_heads"], c["n_kv"]
+    m = pb.Bonsai(c)
+
+    def q1(rows, K):
+        b = torch.randint(0, 256, (rows, K // 128, 18), dtype=torch.uint8, device="cuda", generator=g)
+        sc = (torch.randn((rows, K // 128), device="cuda", generator=g).abs() * 0.02).half()
+        b[:, :, :2].copy_(sc.view(torch.uint8).view(rows, K // 128, 2))
+        return b
+
+    def norm(n):
+        return (1.0 + 0.05 * torch.randn(n, generator=torch.Generator().manual_seed(n))).numpy()
+    st = pb._stream(stream)
+    shapes = {0: (NH * 128, H), 1: (NKV * 128, H), 2: (NKV * 128, H), 3: (H, NH * 128),
+              4: (F, H), 5: (F, H), 6: (H, F)}
+    for L in range(c["n_layers"]):
+        for slot, (r, k) in shapes.items():
+            m.set_q1(L, slot, q1(r, k), st)
+        for slot, n in ((0, H), (1, H), (2, 128), (3, 128)):
+            m.set_norm(L, slot, norm(n), st)
+    m.set_q1(-1, 16, q1(c["vocab"], H), st)
+    m.set_norm(-1, 16, norm(H), st)
+    s = m.new_state(max_ctx)
+    for L in range(c["n_layers"]):
+        for which in (0, 1):
+            kv = s.kv(L, which)
+            kv.copy_(torch.randn(kv.shape, device="cuda", generator=g).half().view(torch.int16))
+            kv[:, pos0:].zero_()
+    torch.cuda.synchronize()
+    return c, m, s
 
 
 def run_reference(args, rank, world):

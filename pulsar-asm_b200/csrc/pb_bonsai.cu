@@ -8,6 +8,10 @@
 //   silu(g)*u + Q8_K -> down GEMV | residual add + output norm + Q8_K -> head
 //   GEMV -> greedy argmax
 //
+// Each kernel waits for its predecessor before it lets the next one launch,
+// so at most two kernels of the chain are resident at a time (the next one
+// parked in its wait, or prefetching weights that do not depend on this one).
+//
 // Arithmetic, each step as the reference states it (the CPU oracle performs
 // the same operations):
 //  * rms (fwd8.c:312-317): s = serial double sum of x*x, sc = 1/sqrtf(float(
@@ -41,6 +45,7 @@ namespace {
 constexpr int BS_HD = 128;          // head_dim (fwd8.c hard-codes 128)
 constexpr int BS_AM_CTAS = 296;     // argmax partial slots
 constexpr int BS_PV_TT = 64;        // positions per V tile in the P.V chain
+constexpr int BS_PV_NST = 4;        // V tiles in flight
 
 struct BsCtl {
   int token;          // input id (the argmax writes the greedy id here)
@@ -59,17 +64,22 @@ struct BsCtl {
 // ------------------------------------------------------------- RMS norm
 // float(s/n) of the serial double sum of squares, from a parallel sum P
 // (every term >= 0; see the file header). ok = 0: not certified.
+// s / n in double: a multiply by the exact reciprocal when n is a power of two
+// (the same value, sums of squares are far above the subnormal range)
+PB_DEV double bs_div_n(double s, int n) {
+  return (n & (n - 1)) == 0 ? __dmul_rn(s, 1.0 / (double)n) : __ddiv_rn(s, (double)n);
+}
 PB_DEV float bs_mean_sq(double P, int n, bool& ok) {
-  const double e = (double)n * 0x1p-51, dn = (double)n;
-  const float lo = __double2float_rn(__ddiv_rn(__dsub_rn(P, __dmul_rn(P, e)), dn));
-  const float hi = __double2float_rn(__ddiv_rn(__dadd_rn(P, __dmul_rn(P, e)), dn));
+  const double e = (double)n * 0x1p-51;
+  const float lo = __double2float_rn(bs_div_n(__dsub_rn(P, __dmul_rn(P, e)), n));
+  const float hi = __double2float_rn(bs_div_n(__dadd_rn(P, __dmul_rn(P, e)), n));
   ok = lo == hi;
   return lo;
 }
 PB_DEV float bs_mean_sq_serial(const float* v, int n) {
   double s = 0.0;
   for (int i = 0; i < n; i++) { const double d = (double)v[i]; s = __fma_rn(d, d, s); }
-  return __double2float_rn(__ddiv_rn(s, (double)n));
+  return __double2float_rn(bs_div_n(s, n));
 }
 PB_DEV double warp_sum_d(double v) {
 #pragma unroll
@@ -93,8 +103,8 @@ __global__ void __launch_bounds__(256) k_bs_norm(BsNormArgs a) {
   __shared__ double wsum[8];
   __shared__ float s_sc;
   __shared__ Q8kScratch q8s;
-  pb_grid_launch_dependents();
   pb_grid_wait();
+  pb_grid_launch_dependents();
   const int t = threadIdx.x, H = a.H;
   double ps = 0.0;
   for (int i = t; i < H; i += 256) {
@@ -138,8 +148,8 @@ struct BsEmbedArgs {
 // fwd8.c:438-452 (Q1_0 branch): x = bit ? sc : -sc, sc the fp16 scale widened
 // with -0 read as +0 (fwd8.c:265-272)
 __global__ void __launch_bounds__(256) k_bs_embed(BsEmbedArgs a) {
-  pb_grid_launch_dependents();
   pb_grid_wait();
+  pb_grid_launch_dependents();
   const int i = blockIdx.x * 256 + threadIdx.x;
   if (i >= a.H) return;
   if (a.ctl->use_x) { a.x[i] = a.xin[i]; return; }
@@ -165,8 +175,8 @@ struct BsPreArgs {
 // one warp per head: q heads, k heads (rms, rope), then v heads (copied)
 __global__ void __launch_bounds__(32) k_bs_attn_pre(BsPreArgs a) {
   __shared__ float sx[BS_HD];
-  pb_grid_launch_dependents();
   pb_grid_wait();
+  pb_grid_launch_dependents();
   const int hh = blockIdx.x, l = threadIdx.x, pos = a.ctl->pos;
   const float* src = a.qkv + (size_t)hh * BS_HD;
   float x[4];
@@ -225,8 +235,8 @@ constexpr int BS_KROW = 272;   // K row stride in shared memory (bank-conflict-f
 __global__ void __launch_bounds__(256) k_bs_fa_qk(BsQkArgs a) {
   __shared__ __align__(16) unsigned char ks[32 * BS_KROW];
   __shared__ __align__(16) uint16_t qs[8][BS_HD];
-  pb_grid_launch_dependents();
   pb_grid_wait();
+  pb_grid_launch_dependents();
   const int T = a.ctl->pos + 1, t0 = blockIdx.x * 32;
   if (t0 >= T) return;
   const int kvh = blockIdx.y, G = a.NH / a.NKV;
@@ -288,39 +298,65 @@ PB_DEV void bs_cp16(void* dst, const void* src) {
   asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(d), "l"(src) : "memory");
 }
 PB_DEV void bs_cp_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
-PB_DEV void bs_cp_wait0() { asm volatile("cp.async.wait_group 0;" ::: "memory"); }
-// grid NH/2 CTAs of 256 threads: thread (hh, d) owns dimension d of head
-// 2*blockIdx.x + hh (both heads read the same kv head, G even)
-__global__ void __launch_bounds__(256) k_bs_fa_pv(BsPvArgs a) {
+template <int N>
+PB_DEV void bs_cp_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
+// grid NH/2 CTAs of 128 threads: thread (hh, j) owns dimensions 2j and 2j+1
+// of head 2*blockIdx.x + hh (both heads read the same kv head, G even), two
+// independent accumulator chains per thread.
+//
+// Softmax weights: thread j of a head owns positions [j*C, j*C + C) of the
+// running-max scan (the scratch copy of the scores is skewed by one word per
+// 32 so that these strided walks hit distinct banks). Per position the scan
+// leaves the exponent argument (Mold - s at a new maximum, s - M otherwise)
+// and a flag; a second, coalesced pass takes the exponentials into the
+// chain's array w (bit 31 = new maximum: w is ms, vs = 1; else w is vs,
+// ms = 1) and marks each 16-position group that holds a new maximum.
+PB_DEV int bs_skew(int p) { return p + (p >> 5); }
+// skewed length, a multiple of 4 floats so that the ring after it starts on a
+// 16-byte boundary (cp.async destinations)
+__host__ __device__ inline int bs_skew_len(int mc) { return (mc + mc / 32 + 3) & ~3; }
+__global__ void __launch_bounds__(128) k_bs_fa_pv(BsPvArgs a) {
   extern __shared__ __align__(16) unsigned char smem[];
-  float* sms = reinterpret_cast<float*>(smem);                 // [2][max_ctx] ms
-  float* svs = sms + 2 * a.max_ctx;                            // [2][max_ctx] vs
-  uint16_t* vt = reinterpret_cast<uint16_t*>(svs + 2 * a.max_ctx);   // [2][TT][128]
-  __shared__ float wmax[8];
+  const int mc = a.max_ctx, mcs = bs_skew_len(mc);
+  uint32_t* sw = reinterpret_cast<uint32_t*>(smem);                  // [2][mc] encoded weights
+  float* sk = reinterpret_cast<float*>(sw + 2 * mc);                 // [2][mcs] skewed scratch
+  uint16_t* vt = reinterpret_cast<uint16_t*>(sk + 2 * mcs);          // [NST][TT][128] f16 ring
+  unsigned char* nmg = reinterpret_cast<unsigned char*>(vt + (size_t)BS_PV_NST * BS_PV_TT * BS_HD);   // [2][mc/16]
+  __shared__ float wmax[4];
   __shared__ float s_S[2];
   __shared__ Q8kScratch q8s;
-  pb_grid_launch_dependents();
   pb_grid_wait();
-  const int T = a.ctl->pos + 1, tid = threadIdx.x, hh = tid >> 7, d = tid & 127;
+  pb_grid_launch_dependents();
+  const int T = a.ctl->pos + 1, tid = threadIdx.x, hh = tid >> 6, j = tid & 63;
   const int h = 2 * blockIdx.x + hh, kvh = h / (a.NH / a.NKV);
-  const uint16_t* V = a.vc + (size_t)kvh * a.max_ctx * BS_HD;
+  const uint16_t* V = a.vc + (size_t)kvh * mc * BS_HD;
   const int ntile = (T + BS_PV_TT - 1) / BS_PV_TT;
+  // V tiles of BS_PV_TT rows through a ring of BS_PV_NST buffers, issued
+  // BS_PV_NST - 1 tiles ahead of the chain
   auto issue = [&](int tile) {
-    uint16_t* dst = vt + (size_t)(tile & 1) * BS_PV_TT * BS_HD;
-    const int r0 = tile * BS_PV_TT;
-    for (int i = tid; i < BS_PV_TT * 16; i += 256) {
-      const int r = i >> 4, c = i & 15;
-      if (r0 + r < T) bs_cp16(dst + r * BS_HD + c * 8, V + (size_t)(r0 + r) * BS_HD + c * 8);
+    if (tile < ntile) {
+      uint16_t* dst = vt + (size_t)(tile % BS_PV_NST) * BS_PV_TT * BS_HD;
+      const int r0 = tile * BS_PV_TT;
+      for (int i = tid; i < BS_PV_TT * 16; i += 128) {
+        const int r = i >> 4, c = i & 15;
+        if (r0 + r < T) bs_cp16(dst + r * BS_HD + c * 8, V + (size_t)(r0 + r) * BS_HD + c * 8);
+      }
     }
-    bs_cp_commit();
+    bs_cp_commit();   // an empty group past the end keeps the wait counts uniform
   };
-  issue(0);
-  // ---- running maxima: thread j of the head owns positions [j*C, j*C + C)
-  const float* S = a.sc + (size_t)h * a.max_ctx;
-  const int C = (T + 127) / 128, p0 = d * C, p1 = min(T, p0 + C);
+#pragma unroll
+  for (int k = 0; k < BS_PV_NST - 1; k++) issue(k);
+  uint32_t* sw_h = sw + (size_t)hh * mc;
+  float* sk_h = sk + (size_t)hh * mcs;
+  unsigned char* nm_h = nmg + (size_t)hh * (mc / 16);
+  const float* S = a.sc + (size_t)h * mc;
+#pragma unroll 4
+  for (int p = j; p < T; p += 64) sk_h[bs_skew(p)] = S[p];
+  __syncthreads();
+  const int C = (T + 63) / 64, p0 = j * C, p1 = min(T, p0 + C);
   float m = -INFINITY;
-  for (int p = p0; p < p1; p++) { const float s = S[p]; m = bs_max_comb(m, s != s ? -INFINITY : s); }
-  // exclusive scan over the head's 128 threads (4 warps)
+  for (int p = p0; p < p1; p++) { const float sv = sk_h[bs_skew(p)]; m = bs_max_comb(m, sv != sv ? -INFINITY : sv); }
+  // exclusive scan over the head's 64 threads (2 warps)
   const int lane = tid & 31, w = tid >> 5;
   float inc = m;
 #pragma unroll
@@ -332,49 +368,108 @@ __global__ void __launch_bounds__(256) k_bs_fa_pv(BsPvArgs a) {
   __syncthreads();
   float ex = __shfl_up_sync(0xffffffffu, inc, 1);
   if (lane == 0) ex = -INFINITY;
-  float before = -INFINITY;
-  for (int ww = hh * 4; ww < w; ww++) before = bs_max_comb(before, wmax[ww]);
-  float M = bs_max_comb(before, ex);
-  float* ms_h = sms + (size_t)hh * a.max_ctx;
-  float* vs_h = svs + (size_t)hh * a.max_ctx;
-  for (int p = p0; p < p1; p++) {
-    const float s = S[p];
-    if (s > M) { ms_h[p] = pb_expf(__fsub_rn(M, s)); vs_h[p] = 1.0f; M = s; }
-    else { ms_h[p] = 1.0f; vs_h[p] = pb_expf(__fsub_rn(s, M)); }
+  float M = (w & 1) ? bs_max_comb(wmax[w - 1], ex) : ex;
+  for (int p = p0; p < p1; p++) {   // in place: the score becomes the exponent argument
+    const int q = bs_skew(p);
+    const float sv = sk_h[q];
+    float arg;
+    uint32_t flag = 0;
+    if (sv > M) { arg = __fsub_rn(M, sv); M = sv; flag = 1; }
+    else arg = __fsub_rn(sv, M);
+    sk_h[q] = __uint_as_float((__float_as_uint(arg) & 0x7fffffffu) | (flag << 31));   // the argument's sign is known
   }
   __syncthreads();
-  // ---- the accumulator chain, positions in order
-  float acc = 0.0f, Ssum = 0.0f;
+  // exponentials, coalesced; group flags by ballot (32 positions per warp pass)
+  for (int pb = (j & ~31); pb < ((T + 31) & ~31); pb += 64) {
+    const int p = pb + lane;
+    uint32_t enc = 0;
+    bool nmax = false;
+    if (p < T) {
+      const uint32_t ab = __float_as_uint(sk_h[bs_skew(p)]);
+      nmax = (ab >> 31) != 0;
+      // the argument is <= 0 (or NaN): restore its sign, then e^arg
+      const float arg = __uint_as_float((ab & 0x7fffffffu) | (ab & 0x7fffffffu ? 0x80000000u : 0u));
+      const float e = pb_expf(arg);
+      enc = (__float_as_uint(e) & 0x7fffffffu) | (nmax ? 0x80000000u : 0u);
+      sw_h[p] = enc;
+    }
+    const unsigned bal = __ballot_sync(0xffffffffu, nmax);
+    if (lane == 0 && pb < T) nm_h[pb >> 4] = (bal & 0xffffu) != 0;
+    if (lane == 16 && pb + 16 < T) nm_h[(pb >> 4) + 1] = (bal >> 16) != 0;
+  }
+  // ---- the accumulator chains, positions in order. A 16-position group with
+  // no new maximum takes the branch-free form acc = r16(fma(v, vs, acc)),
+  // S = S + vs (= fma(S, 1, vs)); its loads are issued one group ahead.
+  float accA = 0.0f, accB = 0.0f, Ssum = 0.0f;
+  const bool sw0 = (j >> 5) == 0;   // the head's first warp also runs the S chain
   for (int tile = 0; tile < ntile; tile++) {
-    bs_cp_wait0();
-    __syncthreads();
-    if (tile + 1 < ntile) issue(tile + 1);
-    const uint16_t* vb = vt + (size_t)(tile & 1) * BS_PV_TT * BS_HD + d;
+    bs_cp_wait<BS_PV_NST - 2>();
+    __syncthreads();   // tile landed; every thread has left the previous one
+    issue(tile + BS_PV_NST - 1);
+    const uint32_t* vb = reinterpret_cast<const uint32_t*>(vt + (size_t)(tile % BS_PV_NST) * BS_PV_TT * BS_HD) + j;
     const int r0 = tile * BS_PV_TT, n = min(BS_PV_TT, T - r0);
-    if (n == BS_PV_TT) {
-#pragma unroll 16
-      for (int r = 0; r < BS_PV_TT; r++) {
-        const float ms = ms_h[r0 + r], vs = vs_h[r0 + r], v = pb_h2f(vb[r * BS_HD]);
-        if (ms != 1.0f) acc = bs_r16(__fmul_rn(acc, ms));
-        acc = bs_r16(__fmaf_rn(v, vs, acc));
-        Ssum = __fmaf_rn(Ssum, ms, vs);
+    uint4 wn[4];
+    uint32_t vn[16];
+#pragma unroll
+    for (int k = 0; k < 4; k++) wn[k] = reinterpret_cast<const uint4*>(sw_h + r0)[k];
+#pragma unroll
+    for (int k = 0; k < 16; k++) vn[k] = vb[k * 64];
+#pragma unroll
+    for (int gi = 0; gi < BS_PV_TT / 16; gi++) {
+      const int g0 = gi * 16;
+      float wc[16];
+      uint32_t vc[16];
+#pragma unroll
+      for (int k = 0; k < 4; k++) {
+        wc[4 * k] = __uint_as_float(wn[k].x); wc[4 * k + 1] = __uint_as_float(wn[k].y);
+        wc[4 * k + 2] = __uint_as_float(wn[k].z); wc[4 * k + 3] = __uint_as_float(wn[k].w);
       }
-    } else {
-      for (int r = 0; r < n; r++) {
-        const float ms = ms_h[r0 + r], vs = vs_h[r0 + r], v = pb_h2f(vb[r * BS_HD]);
-        if (ms != 1.0f) acc = bs_r16(__fmul_rn(acc, ms));
-        acc = bs_r16(__fmaf_rn(v, vs, acc));
-        Ssum = __fmaf_rn(Ssum, ms, vs);
+#pragma unroll
+      for (int k = 0; k < 16; k++) vc[k] = vn[k];
+      if (gi + 1 < BS_PV_TT / 16) {
+#pragma unroll
+        for (int k = 0; k < 4; k++) wn[k] = reinterpret_cast<const uint4*>(sw_h + r0 + g0 + 16)[k];
+#pragma unroll
+        for (int k = 0; k < 16; k++) vn[k] = vb[(g0 + 16 + k) * 64];
+      }
+      if (g0 >= n) break;
+      if (g0 + 16 <= n && !nm_h[(r0 + g0) >> 4]) {
+        if (sw0) {
+#pragma unroll
+          for (int k = 0; k < 16; k++) {
+            accA = bs_r16(__fmaf_rn(pb_h2f((unsigned short)(vc[k] & 0xffffu)), wc[k], accA));
+            accB = bs_r16(__fmaf_rn(pb_h2f((unsigned short)(vc[k] >> 16)), wc[k], accB));
+            Ssum = __fadd_rn(Ssum, wc[k]);
+          }
+        } else {
+#pragma unroll
+          for (int k = 0; k < 16; k++) {
+            accA = bs_r16(__fmaf_rn(pb_h2f((unsigned short)(vc[k] & 0xffffu)), wc[k], accA));
+            accB = bs_r16(__fmaf_rn(pb_h2f((unsigned short)(vc[k] >> 16)), wc[k], accB));
+          }
+        }
+      } else {
+        const int ge = min(16, n - g0);
+        for (int k = 0; k < ge; k++) {
+          const uint32_t e = sw_h[r0 + g0 + k];
+          const bool nmax = (e >> 31) != 0;
+          const float wk = __uint_as_float(e & 0x7fffffffu), ms = nmax ? wk : 1.0f, vs = nmax ? 1.0f : wk;
+          const uint32_t v = vb[(g0 + k) * 64];
+          if (ms != 1.0f) { accA = bs_r16(__fmul_rn(accA, ms)); accB = bs_r16(__fmul_rn(accB, ms)); }
+          accA = bs_r16(__fmaf_rn(pb_h2f((unsigned short)(v & 0xffffu)), vs, accA));
+          accB = bs_r16(__fmaf_rn(pb_h2f((unsigned short)(v >> 16)), vs, accB));
+          Ssum = __fmaf_rn(Ssum, ms, vs);
+        }
       }
     }
   }
-  if (d == 0) s_S[hh] = Ssum;
+  if (j == 0) s_S[hh] = Ssum;
   __syncthreads();
   const float St = s_S[hh];
   const float si = St == 0.0f ? 0.0f : __fdiv_rn(1.0f, St);
-  const float out = __fmul_rn(acc, si);
-  a.atto[(size_t)h * BS_HD + d] = out;
-  pb_q8k_block256(out, a.xq + (size_t)blockIdx.x * 292, q8s);
+  const float o0 = __fmul_rn(accA, si), o1 = __fmul_rn(accB, si);
+  *reinterpret_cast<float2*>(a.atto + (size_t)h * BS_HD + 2 * j) = make_float2(o0, o1);
+  pb_q8k_block256x2(o0, o1, a.xq + (size_t)blockIdx.x * 292, q8s);
 }
 
 // -------------------------------------------------------- silu(g)*u + Q8_K
@@ -385,8 +480,8 @@ struct BsSiluArgs {
 };
 __global__ void __launch_bounds__(256) k_bs_silu_q8k(BsSiluArgs a) {
   __shared__ Q8kScratch q8s;
-  pb_grid_launch_dependents();
   pb_grid_wait();
+  pb_grid_launch_dependents();
   const int i = blockIdx.x * 256 + threadIdx.x;
   const float g = a.gu[i], u = a.gu[a.F + i];
   const float v = __fmul_rn(__fmul_rn(g, __fdiv_rn(1.0f, __fadd_rn(1.0f, pb_expf(-g)))), u);
@@ -405,8 +500,8 @@ __global__ void __launch_bounds__(256) k_bs_argmax(BsArgmaxArgs a) {
   __shared__ float bv[8];
   __shared__ int bi[8];
   __shared__ int am_last;
-  pb_grid_launch_dependents();
   pb_grid_wait();
+  pb_grid_launch_dependents();
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   float b = -INFINITY;
   int ix = 0x7fffffff;
@@ -431,16 +526,30 @@ __global__ void __launch_bounds__(256) k_bs_argmax(BsArgmaxArgs a) {
     am_last = atomicAdd(&a.ctl->counter, 1u) == gridDim.x - 1;
   }
   __syncthreads();
-  if (am_last && threadIdx.x == 0) {
-    __threadfence();
-    volatile float* sv = a.ctl->slot_val;
-    volatile int* si = a.ctl->slot_idx;
-    float best = sv[0];
-    int id = si[0];
-    for (int k = 1; k < (int)gridDim.x; k++) {
-      const float ov = sv[k]; const int oi = si[k];
-      if (ov > best || (ov == best && oi < id)) { best = ov; id = oi; }
-    }
+  if (!am_last) return;
+  // the last CTA reduces the slots (read through L2) the same way
+  __threadfence();
+  b = -INFINITY;
+  ix = 0x7fffffff;
+  for (int k = threadIdx.x; k < (int)gridDim.x; k += 256) {
+    const float ov = __ldcg(&a.ctl->slot_val[k]);
+    const int oi = __ldcg(&a.ctl->slot_idx[k]);
+    if (ov > b || (ov == b && oi < ix)) { b = ov; ix = oi; }
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const float ov = __shfl_down_sync(0xffffffffu, b, o);
+    const int oi = __shfl_down_sync(0xffffffffu, ix, o);
+    if (ov > b || (ov == b && oi < ix)) { b = ov; ix = oi; }
+  }
+  __syncthreads();
+  if (lane == 0) { bv[warp] = b; bi[warp] = ix; }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    float best = bv[0];
+    int id = bi[0];
+    for (int w = 1; w < 8; w++)
+      if (bv[w] > best || (bv[w] == best && bi[w] < id)) { best = bv[w]; id = bi[w]; }
     // no finite maximum (all NaN): index 0, as the serial scan leaves it
     // (and a NaN first logit, which the serial scan never leaves)
     if (id == 0x7fffffff || a.lg[0] != a.lg[0]) { id = 0; best = a.lg[0]; }
@@ -518,7 +627,10 @@ struct pb_bonsai_state {
 
 namespace {
 
-size_t pv_smem(int max_ctx) { return (size_t)16 * max_ctx + (size_t)2 * BS_PV_TT * BS_HD * 2; }
+size_t pv_smem(int max_ctx) {
+  return (size_t)8 * max_ctx + (size_t)8 * bs_skew_len(max_ctx) + (size_t)BS_PV_NST * BS_PV_TT * BS_HD * 2 +
+         (size_t)2 * (max_ctx / 16);
+}
 
 // fwd8.c:322-358 (yarn_corr_dim, yarn_init, rope_table) for every position,
 // written as gcc's default (contracting) build computes it: msc = fma(0.1,
@@ -582,7 +694,7 @@ int bs_record(pb_bonsai* m, pb_bonsai_state* s, cudaStream_t st) {
     }
     {
       BsPvArgs a{s->scores, vc, s->atto, s->xq, NH, NKV, s->max_ctx, s->ctl};
-      if ((rc = bs_launch(k_bs_fa_pv, dim3(NH / 2), 256, pv_smem(s->max_ctx), st, a, "k_bs_fa_pv"))) return rc;
+      if ((rc = bs_launch(k_bs_fa_pv, dim3(NH / 2), 128, pv_smem(s->max_ctx), st, a, "k_bs_fa_pv"))) return rc;
     }
     if ((rc = pb_q1_gemv_launch(&m->o[L], s->xq, s->ao, nullptr, st, true))) return rc;
     {   // x += attention output ; rms(ffn_norm) ; Q8_K

@@ -49,14 +49,33 @@ __global__ void __launch_bounds__(256) k_q8k_quantize(const float* __restrict__ 
 }
 
 // ------------------------------------------------------------ Q1 GEMV
-// One warp per row, lane l owns groups l, l+32, ...; products
-// (ws*db)*(float)isum go to a per-warp row buffer and lane 0 folds them in
-// group order. Activations staged once per CTA, permuted as described above,
-// 528 bytes per group (512 + 16 of padding so that lanes on consecutive
-// groups hit distinct banks).
+// One warp per batch of Q1_R rows, lane l owns groups l, l+32, ... (GPL per
+// lane); products (ws*db)*(float)isum go to a per-warp row buffer and lane r
+// folds row r in group order. Every weight word of a batch is requested
+// before any is used, and the next batch's words while this one computes.
+// Activations staged once per CTA, permuted as described above, 528 bytes per
+// group (512 + 16 of padding so that lanes on consecutive groups hit distinct
+// banks).
 #define PB_Q1_GSTRIDE 528
 constexpr int Q1_R = 4;   // rows per warp batch
-__global__ void __launch_bounds__(256)
+template <int GPL>
+PB_DEV void q1_load(uint4 (&wv)[GPL][Q1_R], unsigned short (&hs)[GPL][Q1_R], const uint4* __restrict__ bits,
+                    const uint16_t* __restrict__ wsc, int row0, int rows, int ng, int lane) {
+#pragma unroll
+  for (int j = 0; j < GPL; j++) {
+    const int g = lane + 32 * j;
+    if (g < ng) {
+#pragma unroll
+      for (int r = 0; r < Q1_R; r++) {
+        const int row = min(row0 + r, rows - 1);
+        wv[j][r] = pb_ldg_stream(bits + (size_t)row * ng + g);
+        hs[j][r] = wsc[(size_t)row * ng + g];
+      }
+    }
+  }
+}
+template <int GPL>
+__global__ void __launch_bounds__(256, GPL <= 2 ? 2 : 1)
 k_q1_gemv(const uint4* __restrict__ bits, const uint16_t* __restrict__ wsc,
           const uint8_t* __restrict__ xq, float* __restrict__ y, int32_t* __restrict__ isum,
           int rows, int K) {
@@ -69,20 +88,14 @@ k_q1_gemv(const uint4* __restrict__ bits, const uint16_t* __restrict__ wsc,
   unsigned char* raw = reinterpret_cast<unsigned char*>(prod + (size_t)8 * Q1_R * ps);   // nbk * 292
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int row_first = (blockIdx.x * 8 + warp) * Q1_R;
+  const int stride = gridDim.x * 8 * Q1_R;
+  uint4 wv[GPL][Q1_R];
+  unsigned short hs[GPL][Q1_R];
   // the first weight words do not depend on the previous kernel: request them
   // before waiting on it (programmatic dependent launch; no-op otherwise)
-  uint4 wv0[Q1_R];
-  unsigned short hs0[Q1_R];
-  if (row_first < rows && lane < ng) {
-#pragma unroll
-    for (int r = 0; r < Q1_R; r++) {
-      const int row = min(row_first + r, rows - 1);
-      wv0[r] = pb_ldg_stream(bits + (size_t)row * ng + lane);
-      hs0[r] = wsc[(size_t)row * ng + lane];
-    }
-  }
-  pb_grid_launch_dependents();
+  if (row_first < rows) q1_load<GPL>(wv, hs, bits, wsc, row_first, rows, ng, lane);
   pb_grid_wait();
+  pb_grid_launch_dependents();
   // the Q8_K activation into shared memory once (coalesced words), then
   // permuted from there
   for (int i = threadIdx.x; i < nbk * 73; i += blockDim.x)
@@ -121,32 +134,29 @@ k_q1_gemv(const uint4* __restrict__ bits, const uint16_t* __restrict__ wsc,
   }
   __syncthreads();
   float* pw = prod + (size_t)warp * Q1_R * ps;
-  for (int row0 = row_first; row0 < rows; row0 += gridDim.x * 8 * Q1_R) {
-    for (int g = lane; g < ng; g += 32) {
-      uint4 wv[Q1_R];
-      unsigned short hs[Q1_R];
-      if (row0 == row_first && g == lane) {
+  for (int row0 = row_first; row0 < rows; row0 += stride) {
+    uint4 cw[GPL][Q1_R];
+    unsigned short ch[GPL][Q1_R];
 #pragma unroll
-        for (int r = 0; r < Q1_R; r++) { wv[r] = wv0[r]; hs[r] = hs0[r]; }
-      } else {
+    for (int j = 0; j < GPL; j++)
 #pragma unroll
-        for (int r = 0; r < Q1_R; r++) {
-          const int row = min(row0 + r, rows - 1);
-          wv[r] = pb_ldg_stream(bits + (size_t)row * ng + g);
-          hs[r] = wsc[(size_t)row * ng + g];
-        }
-      }
+      for (int r = 0; r < Q1_R; r++) { cw[j][r] = wv[j][r]; ch[j][r] = hs[j][r]; }
+    if (row0 + stride < rows) q1_load<GPL>(wv, hs, bits, wsc, row0 + stride, rows, ng, lane);
+#pragma unroll
+    for (int j = 0; j < GPL; j++) {
+      const int g = lane + 32 * j;
+      if (g >= ng) break;
       const uint4* av = reinterpret_cast<const uint4*>(act + (size_t)g * PB_Q1_GSTRIDE);
       int P[Q1_R];
 #pragma unroll
       for (int r = 0; r < Q1_R; r++) P[r] = 0;
 #pragma unroll
-      for (int j = 0; j < 4; j++) {
-        const uint4 a0 = av[2 * j], a1 = av[2 * j + 1];
+      for (int jj = 0; jj < 4; jj++) {
+        const uint4 a0 = av[2 * jj], a1 = av[2 * jj + 1];
         const unsigned aw[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
 #pragma unroll
         for (int r = 0; r < Q1_R; r++) {
-          const unsigned ws = j == 0 ? wv[r].x : j == 1 ? wv[r].y : j == 2 ? wv[r].z : wv[r].w;
+          const unsigned ws = jj == 0 ? cw[j][r].x : jj == 1 ? cw[j][r].y : jj == 2 ? cw[j][r].z : cw[j][r].w;
 #pragma unroll
           for (int k = 0; k < 8; k++) P[r] = __dp4a((int)((ws >> k) & 0x01010101u), (int)aw[k], P[r]);
         }
@@ -155,10 +165,10 @@ k_q1_gemv(const uint4* __restrict__ bits, const uint16_t* __restrict__ wsc,
       const float dbg = dbs[g];
 #pragma unroll
       for (int r = 0; r < Q1_R; r++) {
-        const int s = 2 * P[r] - ag;
-        if (isum && row0 + r < rows) isum[(size_t)(row0 + r) * ng + g] = s;
-        const float wsf = hs[r] == 0x8000u ? 0.0f : pb_h2f(hs[r]);
-        pw[r * ps + g] = __fmul_rn(__fmul_rn(wsf, dbg), __int2float_rn(s));
+        const int sm = 2 * P[r] - ag;
+        if (isum && row0 + r < rows) isum[(size_t)(row0 + r) * ng + g] = sm;
+        const float wsf = ch[j][r] == 0x8000u ? 0.0f : pb_h2f(ch[j][r]);
+        pw[r * ps + g] = __fmul_rn(__fmul_rn(wsf, dbg), __int2float_rn(sm));
       }
     }
     __syncwarp();
@@ -182,14 +192,26 @@ int pb_q1_gemv_launch(const pb_q1* w, const uint8_t* d_xq, float* d_y, int32_t* 
                       cudaStream_t st, bool pdl) {
   const size_t smem = q1_smem(w->K);
   if (smem > 220 * 1024) return pb_set_error(PB_ENOTSUP, "pb_q1_gemv: K=%d too large", w->K);
-  static bool smem_set[64] = {};   // the attribute is per device
+  const int gpl = (w->K / 128 + 31) / 32;
+  if (gpl > 4) return pb_set_error(PB_ENOTSUP, "pb_q1_gemv: K=%d above 16384", w->K);
+  void (*kern)(const uint4*, const uint16_t*, const uint8_t*, float*, int32_t*, int, int) =
+      gpl == 1 ? k_q1_gemv<1> : gpl == 2 ? k_q1_gemv<2> : gpl == 3 ? k_q1_gemv<3> : k_q1_gemv<4>;
+  static bool smem_set[64][4] = {};   // the attribute is per device and instance
   int dev = 0;
   cudaGetDevice(&dev);
-  if (dev < 0 || dev >= 64 || !smem_set[dev]) {
-    cudaFuncSetAttribute(k_q1_gemv, cudaFuncAttributeMaxDynamicSharedMemorySize, 220 * 1024);
-    if (dev >= 0 && dev < 64) smem_set[dev] = true;
+  if (dev < 0 || dev >= 64 || !smem_set[dev][gpl - 1]) {
+    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 220 * 1024);
+    if (dev >= 0 && dev < 64) smem_set[dev][gpl - 1] = true;
   }
-  int grid = 4 * pb_num_sms();
+  // one resident wave: every CTA walks its row batches with the next batch's
+  // words in flight
+  static int occ[64][4] = {};
+  if (dev >= 0 && dev < 64 && !occ[dev][gpl - 1]) {
+    int n = 0;
+    cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, kern, 256, smem);
+    occ[dev][gpl - 1] = n > 0 ? n : 1;
+  }
+  int grid = (dev >= 0 && dev < 64 ? occ[dev][gpl - 1] : 1) * pb_num_sms();
   if (grid * 8 * Q1_R > w->rows) grid = (w->rows + 8 * Q1_R - 1) / (8 * Q1_R);
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(grid);
@@ -201,7 +223,7 @@ int pb_q1_gemv_launch(const pb_q1* w, const uint8_t* d_xq, float* d_y, int32_t* 
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = pdl ? 1 : 0;
-  cudaError_t e = cudaLaunchKernelEx(&cfg, k_q1_gemv, reinterpret_cast<const uint4*>(w->bits),
+  cudaError_t e = cudaLaunchKernelEx(&cfg, kern, reinterpret_cast<const uint4*>(w->bits),
                                      (const uint16_t*)w->scales, d_xq, d_y, d_isum, w->rows, w->K);
   if (e != cudaSuccess) return pb_set_error(PB_ECUDA, "launch k_q1_gemv: %s", cudaGetErrorString(e));
   pb_count_launch();
