@@ -215,8 +215,8 @@ int pb_time_step_kernel(pb_model* m, pb_state* s, int which, int iters, float* m
  * 404-434) -> o -> rms -> gate|up -> silu(g)*u -> down; output norm, head,
  * greedy argmax. Replaces the device side of pq1_token_fused
  * (pq1_fwd8_shim.h:44-51, pq1_fwd8_glue.c:1530) with device-pointer calls.
- * Shapes: hidden and inter multiples of 256 (hidden <= 8192), n_heads/n_kv
- * even and <= 8.                                                              */
+ * Shapes: hidden and inter multiples of 256 (hidden <= 8192), n_heads even
+ * and <= 128, n_heads/n_kv <= 8.                                              */
 typedef struct pb_bonsai pb_bonsai;
 typedef struct pb_bonsai_state pb_bonsai_state;
 typedef struct {
@@ -251,6 +251,9 @@ int pb_bonsai_state_kv(pb_bonsai_state* s, int layer, int which, void** d_ptr);
 int pb_bonsai_state_residual(pb_bonsai_state* s, float* d_x, void* stream);
 /* RMS norms that fell back to the serial double chain since creation */
 int pb_bonsai_state_fallbacks(pb_bonsai_state* s, int* out);
+/* synchronise `stream` and report a failure recorded on the device (a bounded
+ * wait that gave up): PB_OK or PB_ECUDA */
+int pb_bonsai_state_status(pb_bonsai_state* s, void* stream);
 /* one token at position pos: the embedding row of `token`, or d_x (fp32
  * [hidden], the caller's row, as pq1_token_fused receives it) when non-null.
  * d_logits (fp32 [vocab]) and out_id (host, synchronises) are optional. */

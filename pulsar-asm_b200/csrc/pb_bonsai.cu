@@ -1,6 +1,6 @@
 // pb_bonsai.cu -- the Bonsai Q1_0 decoder's token step (pulsar_arm/bonsai2/
 // fwd8.c:812-883 with attn_cpu :529-647 on the f16 cache) on sm_100a, as one
-// CUDA graph per state of programmatic-dependent launches:
+// CUDA graph per state of programmatic-dependent launches, 10 per layer:
 //
 //   embed | per layer: [residual add +] RMS norm + Q8_K -> q|k|v Q1 GEMV ->
 //   head norms + YaRN rope + f16 K/V append -> q.k scores -> online-softmax
@@ -14,12 +14,9 @@
 //
 // Arithmetic, each step as the reference states it (the CPU oracle performs
 // the same operations):
-//  * rms (fwd8.c:312-317): s = serial double sum of x*x, sc = 1/sqrtf(float(
-//    s/n) + 1e-6), y = (x*sc)*w. The serial double sum is not recomputed
-//    serially: a parallel double sum P differs from it by at most 2(n-1)u*P
-//    (u = 2^-53, every term >= 0), so when P(1 -+ n 2^-51)/n round to the same
-//    float, that float is float(serial/n). Otherwise one thread runs the serial
-//    chain (counted in the control block).
+//  * rms and silu: pb_bsnum.cuh (a certified parallel form of the serial
+//    double sum, with the serial chain as the fallback, counted in the
+//    control block).
 //  * rope (fwd8.c:359-369, contracted as gcc builds it, pq1_swar_sm53.cu:2147):
 //    x[j] = fma(a, c, -(b*s)), x[j+64] = fma(a, s, b*c), with the (cos, sin)
 //    table of every position built on the host (fwd8.c:339-358).
@@ -36,6 +33,7 @@
 #include "pb_common.cuh"
 #include "pb_internal.h"
 #include "pb_q8k.cuh"
+#include "pb_bsnum.cuh"
 #include <cmath>
 #include <cstring>
 #include <vector>
@@ -57,36 +55,14 @@ struct BsCtl {
   float topv;         // its logit
   int fallbacks;      // RMS norms that took the serial double chain
   int* ids;           // optional: greedy id of every step
+  unsigned pv_pair[64];   // attention: heads of each pair that have finished (reset by the second)
+  int err;            // a bounded wait in a kernel gave up
   float slot_val[BS_AM_CTAS];
   int slot_idx[BS_AM_CTAS];
 };
 
 // ------------------------------------------------------------- RMS norm
-// float(s/n) of the serial double sum of squares, from a parallel sum P
-// (every term >= 0; see the file header). ok = 0: not certified.
-// s / n in double: a multiply by the exact reciprocal when n is a power of two
-// (the same value, sums of squares are far above the subnormal range)
-PB_DEV double bs_div_n(double s, int n) {
-  return (n & (n - 1)) == 0 ? __dmul_rn(s, 1.0 / (double)n) : __ddiv_rn(s, (double)n);
-}
-PB_DEV float bs_mean_sq(double P, int n, bool& ok) {
-  const double e = (double)n * 0x1p-51;
-  const float lo = __double2float_rn(bs_div_n(__dsub_rn(P, __dmul_rn(P, e)), n));
-  const float hi = __double2float_rn(bs_div_n(__dadd_rn(P, __dmul_rn(P, e)), n));
-  ok = lo == hi;
-  return lo;
-}
-PB_DEV float bs_mean_sq_serial(const float* v, int n) {
-  double s = 0.0;
-  for (int i = 0; i < n; i++) { const double d = (double)v[i]; s = __fma_rn(d, d, s); }
-  return __double2float_rn(bs_div_n(s, n));
-}
-PB_DEV double warp_sum_d(double v) {
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) v = __dadd_rn(v, __shfl_xor_sync(0xffffffffu, v, o));
-  return v;
-}
-
+// the step's RMS norms (pb_bsnum.cuh) with the residual add and Q8_K
 struct BsNormArgs {
   const float* xin;   // residual stream in
   const float* r;     // added to it first (null: none)
@@ -126,7 +102,7 @@ __global__ void __launch_bounds__(256) k_bs_norm(BsNormArgs a) {
       mean = bs_mean_sq_serial(sv, H);
       if (blockIdx.x == 0) atomicAdd(&a.ctl->fallbacks, 1);
     }
-    s_sc = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(mean, 1e-6f)));
+    s_sc = bs_rms_scale(mean);
   }
   __syncthreads();
   const int i = blockIdx.x * 256 + t;
@@ -202,7 +178,7 @@ __global__ void __launch_bounds__(32) k_bs_attn_pre(BsPreArgs a) {
     }
     mean = __shfl_sync(0xffffffffu, mean, 0);
   }
-  const float sc = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(mean, 1e-6f)));
+  const float sc = bs_rms_scale(mean);
   const float* w = hh < a.NH ? a.qn : a.kn;
   float y[4];
 #pragma unroll
@@ -285,191 +261,224 @@ struct BsPvArgs {
   const float* sc;    // [NH][max_ctx]
   const uint16_t* vc; // layer's V cache [NKV][max_ctx][128]
   float* atto;        // [NH][128]
-  uint8_t* xq;        // Q8_K of atto (one 256-block per CTA)
+  uint8_t* xq;        // Q8_K of atto (one 256-block per head pair)
   int NH, NKV, max_ctx;
-  const BsCtl* ctl;
+  BsCtl* ctl;
 };
 PB_DEV float bs_r16(float x) { return __half2float(__float2half_rn(x)); }
 // the serial algorithm's "s > M" keeps the earliest of equal maxima and never
 // takes a NaN: the prefix max maps NaN to -inf and combines (earlier, later)
 PB_DEV float bs_max_comb(float m, float s) { return s > m ? s : m; }
-PB_DEV void bs_cp16(void* dst, const void* src) {
-  const unsigned d = (unsigned)__cvta_generic_to_shared(dst);
-  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(d), "l"(src) : "memory");
-}
-PB_DEV void bs_cp_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
-template <int N>
-PB_DEV void bs_cp_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
-// grid NH/2 CTAs of 128 threads: thread (hh, j) owns dimensions 2j and 2j+1
-// of head 2*blockIdx.x + hh (both heads read the same kv head, G even), two
-// independent accumulator chains per thread.
+// grid NH CTAs of 64 threads, one head each; thread j owns dimensions 2j and
+// 2j+1: two independent accumulator chains.
 //
-// Softmax weights: thread j of a head owns positions [j*C, j*C + C) of the
-// running-max scan (the scratch copy of the scores is skewed by one word per
-// 32 so that these strided walks hit distinct banks). Per position the scan
-// leaves the exponent argument (Mold - s at a new maximum, s - M otherwise)
-// and a flag; a second, coalesced pass takes the exponentials into the
-// chain's array w (bit 31 = new maximum: w is ms, vs = 1; else w is vs,
-// ms = 1) and marks each 16-position group that holds a new maximum.
+// Softmax weights: thread j owns positions [j*C, j*C +
+// C) of the running-max scan (the scratch copy of the scores is skewed by one
+// word per 32 so that these strided walks hit distinct banks). Per position
+// the scan leaves the exponent argument (Mold - s at a new maximum, s - M
+// otherwise) and a flag; a coalesced pass takes the exponentials into the
+// chain's array w (bit 31 = new maximum: w is ms and vs = 1; else w is vs and
+// ms = 1) and marks every 16-position group that holds a new maximum.
+//
+// The chains read V as f16 pairs straight from a ring of BS_PV_NST tiles,
+// each tile (contiguous rows of the kv head) one bulk copy completing on its
+// slot's mbarrier (bounded waits: a copy that never lands sets the control
+// block's error and ends the CTA). A 16-position group with no new maximum
+// takes the branch-free form acc = r16(fma(v, vs, acc)), S = S + vs (= fma(S,
+// 1, vs)); other groups take the general step.
 PB_DEV int bs_skew(int p) { return p + (p >> 5); }
-// skewed length, a multiple of 4 floats so that the ring after it starts on a
+// skewed length, a multiple of 4 floats so that what follows it starts on a
 // 16-byte boundary (cp.async destinations)
 __host__ __device__ inline int bs_skew_len(int mc) { return (mc + mc / 32 + 3) & ~3; }
-__global__ void __launch_bounds__(128) k_bs_fa_pv(BsPvArgs a) {
+// group flags per head, padded to whole words (the chain reads a tile's four at once)
+__host__ __device__ inline int bs_nm_len(int mc) { return (mc / 16 + 3) & ~3; }
+// one 16-position group of the general step (a group that holds a new maximum)
+PB_DEV void bs_chain_group_general(const uint32_t* __restrict__ vb, const uint32_t* __restrict__ w, int n,
+                                   float& accA, float& accB, float& Ssum) {
+  for (int k = 0; k < n; k++) {
+    const uint32_t e = w[k];
+    const bool nmax = (e >> 31) != 0;
+    const float wk = __uint_as_float(e & 0x7fffffffu), ms = nmax ? wk : 1.0f, vs = nmax ? 1.0f : wk;
+    const uint32_t v = vb[k * 64];
+    if (ms != 1.0f) { accA = bs_r16(__fmul_rn(accA, ms)); accB = bs_r16(__fmul_rn(accB, ms)); }
+    accA = bs_r16(__fmaf_rn(pb_h2f((unsigned short)(v & 0xffffu)), vs, accA));
+    accB = bs_r16(__fmaf_rn(pb_h2f((unsigned short)(v >> 16)), vs, accB));
+    Ssum = __fmaf_rn(Ssum, ms, vs);
+  }
+}
+// one 16-position group of the branch-free step (all weights are vs)
+PB_DEV void bs_chain_group_fast(const uint32_t* __restrict__ vb, const uint32_t* __restrict__ w, float& accA,
+                                float& accB, float& Ssum) {
+  uint4 wn[4];
+  uint32_t vn[16];
+#pragma unroll
+  for (int k = 0; k < 4; k++) wn[k] = reinterpret_cast<const uint4*>(w)[k];
+#pragma unroll
+  for (int k = 0; k < 16; k++) vn[k] = vb[k * 64];
+  const uint32_t wk[16] = {wn[0].x, wn[0].y, wn[0].z, wn[0].w, wn[1].x, wn[1].y, wn[1].z, wn[1].w,
+                           wn[2].x, wn[2].y, wn[2].z, wn[2].w, wn[3].x, wn[3].y, wn[3].z, wn[3].w};
+#pragma unroll
+  for (int k = 0; k < 16; k++) {
+    const float wf = __uint_as_float(wk[k]);
+    accA = bs_r16(__fmaf_rn(pb_h2f((unsigned short)(vn[k] & 0xffffu)), wf, accA));
+    accB = bs_r16(__fmaf_rn(pb_h2f((unsigned short)(vn[k] >> 16)), wf, accB));
+    Ssum = __fadd_rn(Ssum, wf);
+  }
+}
+PB_DEV uint32_t bs_smem_u32(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
+PB_DEV bool bs_mbar_try(uint64_t* b, unsigned parity) {
+  uint32_t ok;
+  asm volatile("{ .reg .pred p; mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2; selp.u32 %0, 1, 0, p; }"
+               : "=r"(ok) : "r"(bs_smem_u32(b)), "r"(parity) : "memory");
+  return ok != 0;
+}
+PB_DEV bool bs_mbar_wait(uint64_t* b, unsigned parity) {   // bounded
+  for (unsigned i = 0; i < (1u << 24); i++)
+    if (bs_mbar_try(b, parity)) return true;
+  return false;
+}
+__global__ void __launch_bounds__(64) k_bs_fa_pv(BsPvArgs a) {
   extern __shared__ __align__(16) unsigned char smem[];
   const int mc = a.max_ctx, mcs = bs_skew_len(mc);
-  uint32_t* sw = reinterpret_cast<uint32_t*>(smem);                  // [2][mc] encoded weights
-  float* sk = reinterpret_cast<float*>(sw + 2 * mc);                 // [2][mcs] skewed scratch
-  uint16_t* vt = reinterpret_cast<uint16_t*>(sk + 2 * mcs);          // [NST][TT][128] f16 ring
-  unsigned char* nmg = reinterpret_cast<unsigned char*>(vt + (size_t)BS_PV_NST * BS_PV_TT * BS_HD);   // [2][mc/16]
-  __shared__ float wmax[4];
-  __shared__ float s_S[2];
-  __shared__ Q8kScratch q8s;
+  uint32_t* sw = reinterpret_cast<uint32_t*>(smem);                  // [mc] encoded weights
+  float* sk = reinterpret_cast<float*>(sw + mc);                     // [mcs] skewed scratch
+  uint16_t* vt = reinterpret_cast<uint16_t*>(sk + mcs);              // [NST][TT][128] f16 ring
+  unsigned char* nm = reinterpret_cast<unsigned char*>(vt + (size_t)BS_PV_NST * BS_PV_TT * BS_HD);   // [nm_len]
+  __shared__ __align__(8) uint64_t full[BS_PV_NST];
+  __shared__ float wmax[2];
+  __shared__ float s_S;
+  __shared__ int s_last;
   pb_grid_wait();
   pb_grid_launch_dependents();
-  const int T = a.ctl->pos + 1, tid = threadIdx.x, hh = tid >> 6, j = tid & 63;
-  const int h = 2 * blockIdx.x + hh, kvh = h / (a.NH / a.NKV);
+  const int T = a.ctl->pos + 1, tid = threadIdx.x, lane = tid & 31, w = tid >> 5, j = tid;
+  const int h = blockIdx.x, kvh = h / (a.NH / a.NKV);
   const uint16_t* V = a.vc + (size_t)kvh * mc * BS_HD;
   const int ntile = (T + BS_PV_TT - 1) / BS_PV_TT;
-  // V tiles of BS_PV_TT rows through a ring of BS_PV_NST buffers, issued
-  // BS_PV_NST - 1 tiles ahead of the chain
-  auto issue = [&](int tile) {
+  // V tiles (contiguous rows of the kv head) by one bulk copy each into a ring
+  // of BS_PV_NST slots, completion on the slot's mbarrier
+  if (tid == 0) {
+    for (int k = 0; k < BS_PV_NST; k++)
+      asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(bs_smem_u32(&full[k])) : "memory");
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  __syncthreads();
+  auto issue = [&](int tile) {   // thread 0
     if (tile < ntile) {
-      uint16_t* dst = vt + (size_t)(tile % BS_PV_NST) * BS_PV_TT * BS_HD;
-      const int r0 = tile * BS_PV_TT;
-      for (int i = tid; i < BS_PV_TT * 16; i += 128) {
-        const int r = i >> 4, c = i & 15;
-        if (r0 + r < T) bs_cp16(dst + r * BS_HD + c * 8, V + (size_t)(r0 + r) * BS_HD + c * 8);
+      uint64_t* bar = &full[tile % BS_PV_NST];
+      const unsigned bytes = (unsigned)min(BS_PV_TT, T - tile * BS_PV_TT) * BS_HD * 2;
+      asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bs_smem_u32(bar)), "r"(bytes) : "memory");
+      asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
+                   ::"r"(bs_smem_u32(vt + (size_t)(tile % BS_PV_NST) * BS_PV_TT * BS_HD)),
+                   "l"(V + (size_t)tile * BS_PV_TT * BS_HD), "r"(bytes), "r"(bs_smem_u32(bar)) : "memory");
+    }
+  };
+  if (tid == 0)
+    for (int k = 0; k < BS_PV_NST; k++) issue(k);
+  {
+    // ---- the head's scores (16 loads in flight per thread)
+    const float* S = a.sc + (size_t)h * mc;
+    for (int p0 = j; p0 < T; p0 += 16 * 64) {
+      float sv[16];
+#pragma unroll
+      for (int k = 0; k < 16; k++) { const int p = p0 + 64 * k; sv[k] = p < T ? S[p] : 0.0f; }
+#pragma unroll
+      for (int k = 0; k < 16; k++) { const int p = p0 + 64 * k; if (p < T) sk[bs_skew(p)] = sv[k]; }
+    }
+    __syncthreads();
+    // ---- running maxima
+    const int C = (T + 63) / 64, p0 = j * C, p1 = min(T, p0 + C);
+    float m = -INFINITY;
+    for (int p = p0; p < p1; p++) { const float x = sk[bs_skew(p)]; m = bs_max_comb(m, x != x ? -INFINITY : x); }
+    float inc = m;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const float u = __shfl_up_sync(0xffffffffu, inc, o);
+      if (lane >= o) inc = bs_max_comb(u, inc);
+    }
+    if (lane == 31) wmax[w] = inc;
+    __syncthreads();
+    float ex = __shfl_up_sync(0xffffffffu, inc, 1);
+    if (lane == 0) ex = -INFINITY;
+    float M = w ? bs_max_comb(wmax[0], ex) : ex;
+    for (int p = p0; p < p1; p++) {   // in place: the score becomes |exponent argument| | flag
+      const int q = bs_skew(p);
+      const float x = sk[q];
+      float arg;
+      uint32_t flag = 0;
+      if (x > M) { arg = __fsub_rn(M, x); M = x; flag = 1; }
+      else arg = __fsub_rn(x, M);
+      sk[q] = __uint_as_float((__float_as_uint(arg) & 0x7fffffffu) | (flag << 31));
+    }
+    __syncthreads();
+    // ---- exponentials, coalesced, four 32-position blocks per warp pass;
+    // group flags by ballot. Every argument is <= 0 or NaN: its sign is restored.
+    for (int pb0 = w * 32; pb0 < ((T + 31) & ~31); pb0 += 4 * 64) {
+      uint32_t ab[4];
+#pragma unroll
+      for (int u = 0; u < 4; u++) {
+        const int p = pb0 + u * 64 + lane;
+        ab[u] = p < T ? __float_as_uint(sk[bs_skew(p)]) : 0u;
+      }
+#pragma unroll
+      for (int u = 0; u < 4; u++) {
+        const int pb = pb0 + u * 64, p = pb + lane;
+        const bool nmax = p < T && (ab[u] >> 31) != 0;
+        if (p < T) {
+          const uint32_t mag = ab[u] & 0x7fffffffu;
+          const float e = pb_expf(__uint_as_float(mag | (mag ? 0x80000000u : 0u)));
+          sw[p] = (__float_as_uint(e) & 0x7fffffffu) | (nmax ? 0x80000000u : 0u);
+        }
+        const unsigned bal = __ballot_sync(0xffffffffu, nmax);
+        if (lane == 0 && pb < T) nm[pb >> 4] = (bal & 0xffffu) != 0;
+        if (lane == 16 && pb + 16 < T) nm[(pb >> 4) + 1] = (bal >> 16) != 0;
       }
     }
-    bs_cp_commit();   // an empty group past the end keeps the wait counts uniform
-  };
-#pragma unroll
-  for (int k = 0; k < BS_PV_NST - 1; k++) issue(k);
-  uint32_t* sw_h = sw + (size_t)hh * mc;
-  float* sk_h = sk + (size_t)hh * mcs;
-  unsigned char* nm_h = nmg + (size_t)hh * (mc / 16);
-  const float* S = a.sc + (size_t)h * mc;
-#pragma unroll 4
-  for (int p = j; p < T; p += 64) sk_h[bs_skew(p)] = S[p];
-  __syncthreads();
-  const int C = (T + 63) / 64, p0 = j * C, p1 = min(T, p0 + C);
-  float m = -INFINITY;
-  for (int p = p0; p < p1; p++) { const float sv = sk_h[bs_skew(p)]; m = bs_max_comb(m, sv != sv ? -INFINITY : sv); }
-  // exclusive scan over the head's 64 threads (2 warps)
-  const int lane = tid & 31, w = tid >> 5;
-  float inc = m;
-#pragma unroll
-  for (int o = 1; o < 32; o <<= 1) {
-    const float u = __shfl_up_sync(0xffffffffu, inc, o);
-    if (lane >= o) inc = bs_max_comb(u, inc);
+    __syncthreads();
   }
-  if (lane == 31) wmax[w] = inc;
-  __syncthreads();
-  float ex = __shfl_up_sync(0xffffffffu, inc, 1);
-  if (lane == 0) ex = -INFINITY;
-  float M = (w & 1) ? bs_max_comb(wmax[w - 1], ex) : ex;
-  for (int p = p0; p < p1; p++) {   // in place: the score becomes the exponent argument
-    const int q = bs_skew(p);
-    const float sv = sk_h[q];
-    float arg;
-    uint32_t flag = 0;
-    if (sv > M) { arg = __fsub_rn(M, sv); M = sv; flag = 1; }
-    else arg = __fsub_rn(sv, M);
-    sk_h[q] = __uint_as_float((__float_as_uint(arg) & 0x7fffffffu) | (flag << 31));   // the argument's sign is known
-  }
-  __syncthreads();
-  // exponentials, coalesced; group flags by ballot (32 positions per warp pass)
-  for (int pb = (j & ~31); pb < ((T + 31) & ~31); pb += 64) {
-    const int p = pb + lane;
-    uint32_t enc = 0;
-    bool nmax = false;
-    if (p < T) {
-      const uint32_t ab = __float_as_uint(sk_h[bs_skew(p)]);
-      nmax = (ab >> 31) != 0;
-      // the argument is <= 0 (or NaN): restore its sign, then e^arg
-      const float arg = __uint_as_float((ab & 0x7fffffffu) | (ab & 0x7fffffffu ? 0x80000000u : 0u));
-      const float e = pb_expf(arg);
-      enc = (__float_as_uint(e) & 0x7fffffffu) | (nmax ? 0x80000000u : 0u);
-      sw_h[p] = enc;
-    }
-    const unsigned bal = __ballot_sync(0xffffffffu, nmax);
-    if (lane == 0 && pb < T) nm_h[pb >> 4] = (bal & 0xffffu) != 0;
-    if (lane == 16 && pb + 16 < T) nm_h[(pb >> 4) + 1] = (bal >> 16) != 0;
-  }
-  // ---- the accumulator chains, positions in order. A 16-position group with
-  // no new maximum takes the branch-free form acc = r16(fma(v, vs, acc)),
-  // S = S + vs (= fma(S, 1, vs)); its loads are issued one group ahead.
+  // ---- the chains, positions in order; a group with no new maximum takes
+  // the branch-free step
   float accA = 0.0f, accB = 0.0f, Ssum = 0.0f;
-  const bool sw0 = (j >> 5) == 0;   // the head's first warp also runs the S chain
+  int failed = -1;   // the tile whose copy never landed (the CTA gives up)
   for (int tile = 0; tile < ntile; tile++) {
-    bs_cp_wait<BS_PV_NST - 2>();
-    __syncthreads();   // tile landed; every thread has left the previous one
-    issue(tile + BS_PV_NST - 1);
+    const bool ok = bs_mbar_wait(&full[tile % BS_PV_NST], (unsigned)(tile / BS_PV_NST) & 1u);
+    if (__syncthreads_or(!ok)) { failed = tile; break; }   // the same decision in every thread
     const uint32_t* vb = reinterpret_cast<const uint32_t*>(vt + (size_t)(tile % BS_PV_NST) * BS_PV_TT * BS_HD) + j;
     const int r0 = tile * BS_PV_TT, n = min(BS_PV_TT, T - r0);
-    uint4 wn[4];
-    uint32_t vn[16];
-#pragma unroll
-    for (int k = 0; k < 4; k++) wn[k] = reinterpret_cast<const uint4*>(sw_h + r0)[k];
-#pragma unroll
-    for (int k = 0; k < 16; k++) vn[k] = vb[k * 64];
-#pragma unroll
-    for (int gi = 0; gi < BS_PV_TT / 16; gi++) {
-      const int g0 = gi * 16;
-      float wc[16];
-      uint32_t vc[16];
-#pragma unroll
-      for (int k = 0; k < 4; k++) {
-        wc[4 * k] = __uint_as_float(wn[k].x); wc[4 * k + 1] = __uint_as_float(wn[k].y);
-        wc[4 * k + 2] = __uint_as_float(wn[k].z); wc[4 * k + 3] = __uint_as_float(wn[k].w);
-      }
-#pragma unroll
-      for (int k = 0; k < 16; k++) vc[k] = vn[k];
-      if (gi + 1 < BS_PV_TT / 16) {
-#pragma unroll
-        for (int k = 0; k < 4; k++) wn[k] = reinterpret_cast<const uint4*>(sw_h + r0 + g0 + 16)[k];
-#pragma unroll
-        for (int k = 0; k < 16; k++) vn[k] = vb[(g0 + 16 + k) * 64];
-      }
-      if (g0 >= n) break;
-      if (g0 + 16 <= n && !nm_h[(r0 + g0) >> 4]) {
-        if (sw0) {
-#pragma unroll
-          for (int k = 0; k < 16; k++) {
-            accA = bs_r16(__fmaf_rn(pb_h2f((unsigned short)(vc[k] & 0xffffu)), wc[k], accA));
-            accB = bs_r16(__fmaf_rn(pb_h2f((unsigned short)(vc[k] >> 16)), wc[k], accB));
-            Ssum = __fadd_rn(Ssum, wc[k]);
-          }
-        } else {
-#pragma unroll
-          for (int k = 0; k < 16; k++) {
-            accA = bs_r16(__fmaf_rn(pb_h2f((unsigned short)(vc[k] & 0xffffu)), wc[k], accA));
-            accB = bs_r16(__fmaf_rn(pb_h2f((unsigned short)(vc[k] >> 16)), wc[k], accB));
-          }
-        }
-      } else {
-        const int ge = min(16, n - g0);
-        for (int k = 0; k < ge; k++) {
-          const uint32_t e = sw_h[r0 + g0 + k];
-          const bool nmax = (e >> 31) != 0;
-          const float wk = __uint_as_float(e & 0x7fffffffu), ms = nmax ? wk : 1.0f, vs = nmax ? 1.0f : wk;
-          const uint32_t v = vb[(g0 + k) * 64];
-          if (ms != 1.0f) { accA = bs_r16(__fmul_rn(accA, ms)); accB = bs_r16(__fmul_rn(accB, ms)); }
-          accA = bs_r16(__fmaf_rn(pb_h2f((unsigned short)(v & 0xffffu)), vs, accA));
-          accB = bs_r16(__fmaf_rn(pb_h2f((unsigned short)(v >> 16)), vs, accB));
-          Ssum = __fmaf_rn(Ssum, ms, vs);
-        }
-      }
+#pragma unroll 1
+    for (int g0 = 0; g0 < n; g0 += 16) {
+      if (g0 + 16 <= n && !nm[(r0 + g0) >> 4]) bs_chain_group_fast(vb + g0 * 64, sw + r0 + g0, accA, accB, Ssum);
+      else bs_chain_group_general(vb + g0 * 64, sw + r0 + g0, min(16, n - g0), accA, accB, Ssum);
     }
+    __syncthreads();   // every thread has left the slot: refill it
+    if (tid == 0) issue(tile + BS_PV_NST);
   }
-  if (j == 0) s_S[hh] = Ssum;
+  if (failed >= 0) {   // wait (bounded) for the copies still in flight, then report
+    if (tid == 0) {
+      for (int t = failed; t < min(ntile, failed + BS_PV_NST); t++)
+        bs_mbar_wait(&full[t % BS_PV_NST], (unsigned)(t / BS_PV_NST) & 1u);
+      atomicExch(&a.ctl->err, 1);
+    }
+    return;
+  }
+  if (j == 0) s_S = Ssum;
   __syncthreads();
-  const float St = s_S[hh];
-  const float si = St == 0.0f ? 0.0f : __fdiv_rn(1.0f, St);
-  const float o0 = __fmul_rn(accA, si), o1 = __fmul_rn(accB, si);
-  *reinterpret_cast<float2*>(a.atto + (size_t)h * BS_HD + 2 * j) = make_float2(o0, o1);
-  pb_q8k_block256x2(o0, o1, a.xq + (size_t)blockIdx.x * 292, q8s);
+  const float si = s_S == 0.0f ? 0.0f : __fdiv_rn(1.0f, s_S);
+  *reinterpret_cast<float2*>(a.atto + (size_t)h * BS_HD + 2 * j) = make_float2(__fmul_rn(accA, si), __fmul_rn(accB, si));
+  // the second head of each pair to finish quantises the pair's 256 outputs
+  // (one Q8_K block); the first one's stores are visible through the fence
+  __threadfence();
+  __syncthreads();
+  if (tid == 0) s_last = atomicAdd(&a.ctl->pv_pair[h >> 1], 1u) == 1u;
+  __syncthreads();
+  if (!s_last) return;
+  __threadfence();
+  float* y = reinterpret_cast<float*>(vt);   // [256] staging
+  const float* src = a.atto + (size_t)(h & ~1) * BS_HD;
+#pragma unroll
+  for (int k = 0; k < 4; k++) y[tid + 64 * k] = __ldcg(src + tid + 64 * k);
+  __syncthreads();
+  if (w == 0) pb_q8k_block256_warp(y, a.xq + (size_t)(h >> 1) * 292);
+  if (tid == 0) a.ctl->pv_pair[h >> 1] = 0u;
 }
 
 // -------------------------------------------------------- silu(g)*u + Q8_K
@@ -484,7 +493,7 @@ __global__ void __launch_bounds__(256) k_bs_silu_q8k(BsSiluArgs a) {
   pb_grid_launch_dependents();
   const int i = blockIdx.x * 256 + threadIdx.x;
   const float g = a.gu[i], u = a.gu[a.F + i];
-  const float v = __fmul_rn(__fmul_rn(g, __fdiv_rn(1.0f, __fadd_rn(1.0f, pb_expf(-g)))), u);
+  const float v = bs_silu_mul(g, u);
   pb_q8k_block256(v, a.xq + (size_t)blockIdx.x * 292, q8s);
 }
 
@@ -628,8 +637,8 @@ struct pb_bonsai_state {
 namespace {
 
 size_t pv_smem(int max_ctx) {
-  return (size_t)8 * max_ctx + (size_t)8 * bs_skew_len(max_ctx) + (size_t)BS_PV_NST * BS_PV_TT * BS_HD * 2 +
-         (size_t)2 * (max_ctx / 16);
+  return (size_t)4 * max_ctx + (size_t)4 * bs_skew_len(max_ctx) + (size_t)BS_PV_NST * BS_PV_TT * BS_HD * 2 +
+         (size_t)bs_nm_len(max_ctx);
 }
 
 // fwd8.c:322-358 (yarn_corr_dim, yarn_init, rope_table) for every position,
@@ -694,7 +703,7 @@ int bs_record(pb_bonsai* m, pb_bonsai_state* s, cudaStream_t st) {
     }
     {
       BsPvArgs a{s->scores, vc, s->atto, s->xq, NH, NKV, s->max_ctx, s->ctl};
-      if ((rc = bs_launch(k_bs_fa_pv, dim3(NH / 2), 128, pv_smem(s->max_ctx), st, a, "k_bs_fa_pv"))) return rc;
+      if ((rc = bs_launch(k_bs_fa_pv, dim3(NH), 64, pv_smem(s->max_ctx), st, a, "k_bs_fa_pv"))) return rc;
     }
     if ((rc = pb_q1_gemv_launch(&m->o[L], s->xq, s->ao, nullptr, st, true))) return rc;
     {   // x += attention output ; rms(ffn_norm) ; Q8_K
@@ -775,9 +784,9 @@ extern "C" int pb_bonsai_create(const pb_bonsai_cfg* cfg, int device, pb_bonsai*
   const pb_bonsai_cfg& c = *cfg;
   if (c.hidden <= 0 || c.hidden % 256 || c.hidden > 8192 || c.inter <= 0 || c.inter % 256 ||
       c.n_layers <= 0 || c.n_heads <= 0 || c.n_kv <= 0 || c.n_heads % c.n_kv || c.n_heads % 2 ||
-      (c.n_heads / c.n_kv) % 2 || c.n_heads / c.n_kv > 8 || c.vocab <= 0)
+      c.n_heads > 128 || c.n_heads / c.n_kv > 8 || c.vocab <= 0)
     return pb_set_error(PB_EINVAL, "pb_bonsai_create: unsupported shape (hidden %% 256, <= 8192; "
-                                   "inter %% 256; n_heads/n_kv even and <= 8)");
+                                   "inter %% 256; n_heads even and <= 128; n_heads/n_kv <= 8)");
   PB_TRY_CUDA(cudaSetDevice(device));
   pb_bonsai* m = new pb_bonsai();
   m->c = c;
@@ -897,7 +906,7 @@ extern "C" int pb_bonsai_set_norm(pb_bonsai* m, int layer, int slot, const float
 extern "C" int pb_bonsai_state_create(pb_bonsai* m, int max_ctx, pb_bonsai_state** out) {
   if (!m || !out || max_ctx <= 0 || max_ctx % 32) return pb_set_error(PB_EINVAL, "pb_bonsai_state_create: bad argument (max_ctx a positive multiple of 32)");
   *out = nullptr;
-  if (pv_smem(max_ctx) > 200 * 1024) return pb_set_error(PB_ENOTSUP, "pb_bonsai_state_create: max_ctx %d too large (<= 8192)", max_ctx);
+  if (pv_smem(max_ctx) > 200 * 1024) return pb_set_error(PB_ENOTSUP, "pb_bonsai_state_create: max_ctx %d too large for the attention kernel (<= 8192)", max_ctx);
   PB_TRY_CUDA(cudaSetDevice(m->device));
   const pb_bonsai_cfg& c = m->c;
   const int H = c.hidden, F = c.inter, NH = c.n_heads, NKV = c.n_kv;
@@ -1013,6 +1022,15 @@ extern "C" int pb_bonsai_decode_greedy(pb_bonsai* m, pb_bonsai_state* s, int tok
   int* null_ids = nullptr;
   PB_TRY_CUDA(cudaMemcpyAsync(&s->ctl->ids, &null_ids, sizeof(int*), cudaMemcpyHostToDevice, st));
   PB_TRY_CUDA(cudaStreamSynchronize(st));
+  return PB_OK;
+}
+
+extern "C" int pb_bonsai_state_status(pb_bonsai_state* s, void* stream) {
+  if (!s) return pb_set_error(PB_EINVAL, "pb_bonsai_state_status: null argument");
+  PB_TRY_CUDA(cudaStreamSynchronize((cudaStream_t)stream));
+  int err = 0;
+  PB_TRY_CUDA(cudaMemcpy(&err, &s->ctl->err, sizeof(int), cudaMemcpyDeviceToHost));
+  if (err) return pb_set_error(PB_ECUDA, "bonsai decode: a bounded wait in the attention kernel gave up");
   return PB_OK;
 }
 

@@ -1,0 +1,42 @@
+// pb_bsnum.cuh -- the Bonsai step's RMS norm and SwiGLU arithmetic (fwd8.c,
+// pq1_host.c), shared by the decoder's kernels and the Q1 GEMV's fused
+// prologues.
+//
+// rms (fwd8.c:312-317): s = serial double sum of x*x, sc = 1/sqrtf(float(s/n)
+// + 1e-6), y = (x*sc)*w. The serial double sum is not recomputed serially: a
+// parallel double sum P of the same (exact) products differs from it by at
+// most 2(n-1)u*P (u = 2^-53, every term >= 0), so when P(1 -+ n 2^-51)/n
+// round to the same float, that float is float(serial/n); otherwise the
+// caller runs the serial chain.
+// silu (pq1_host.c:196-227): (g * (1/(1+e^-g))) * u, e^x = pb_expf.
+#pragma once
+#include "pb_common.cuh"
+
+// s / n in double: a multiply by the exact reciprocal when n is a power of two
+// (the same value, sums of squares are far above the subnormal range)
+PB_DEV double bs_div_n(double s, int n) {
+  return (n & (n - 1)) == 0 ? __dmul_rn(s, 1.0 / (double)n) : __ddiv_rn(s, (double)n);
+}
+// float(s/n) of the serial double sum of squares from a parallel sum P;
+// ok = false: not certified
+PB_DEV float bs_mean_sq(double P, int n, bool& ok) {
+  const double e = (double)n * 0x1p-51;
+  const float lo = __double2float_rn(bs_div_n(__dsub_rn(P, __dmul_rn(P, e)), n));
+  const float hi = __double2float_rn(bs_div_n(__dadd_rn(P, __dmul_rn(P, e)), n));
+  ok = lo == hi;
+  return lo;
+}
+PB_DEV float bs_mean_sq_serial(const float* v, int n) {
+  double s = 0.0;
+  for (int i = 0; i < n; i++) { const double d = (double)v[i]; s = __fma_rn(d, d, s); }
+  return __double2float_rn(bs_div_n(s, n));
+}
+PB_DEV double warp_sum_d(double v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = __dadd_rn(v, __shfl_xor_sync(0xffffffffu, v, o));
+  return v;
+}
+PB_DEV float bs_rms_scale(float mean) { return __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(mean, 1e-6f))); }
+PB_DEV float bs_silu_mul(float g, float u) {
+  return __fmul_rn(__fmul_rn(g, __fdiv_rn(1.0f, __fadd_rn(1.0f, pb_expf(-g)))), u);
+}

@@ -68,61 +68,52 @@ PB_DEV void pb_q8k_block256(float v, uint8_t* __restrict__ qb, Q8kScratch& sc) {
   __syncthreads();
 }
 
-// the same block quantiser over a 128-thread CTA holding two values each:
-// thread t holds values 2t (v0) and 2t+1 (v1)
-PB_DEV void pb_q8k_block256x2(float v0, float v1, uint8_t* __restrict__ qb, Q8kScratch& sc) {
-  const int t = threadIdx.x, lane = t & 31, wid = t >> 5;
-  const float a0 = v0 != v0 ? -1.0f : fabsf(v0), a1 = v1 != v1 ? -1.0f : fabsf(v1);
-  float a = a0;
-  int idx = 2 * t;
-  if (a1 > a) { a = a1; idx = 2 * t + 1; }
+// the same block quantiser run by one warp over 256 values y (thread l reads
+// y[l + 32k], k < 8); no CTA barrier
+PB_DEV void pb_q8k_block256_warp(const float* __restrict__ y, uint8_t* __restrict__ qb) {
+  const int l = threadIdx.x & 31;
+  float v[8];
+#pragma unroll
+  for (int k = 0; k < 8; k++) v[k] = y[l + 32 * k];
+  float a = -1.0f;
+  int idx = 0;
+#pragma unroll
+  for (int k = 0; k < 8; k++) {   // ascending index within the lane: strict > keeps the first
+    const float ak = v[k] != v[k] ? -1.0f : fabsf(v[k]);
+    if (ak > a) { a = ak; idx = l + 32 * k; }
+  }
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) {
-    const float oa = __shfl_down_sync(0xffffffffu, a, o);
-    const int oi = __shfl_down_sync(0xffffffffu, idx, o);
+    const float oa = __shfl_xor_sync(0xffffffffu, a, o);
+    const int oi = __shfl_xor_sync(0xffffffffu, idx, o);
     if (oa > a || (oa == a && oi < idx)) { a = oa; idx = oi; }
   }
-  if (lane == 0) { sc.a[wid] = a; sc.i[wid] = idx; }
-  __syncthreads();
-  if (t == 0) {
-    float ba = sc.a[0]; int bi = sc.i[0];
-    for (int w = 1; w < 4; w++) if (sc.a[w] > ba) { ba = sc.a[w]; bi = sc.i[w]; }
-    sc.zero = !(ba > 0.0f);
-    sc.i[0] = bi;
-  }
-  __syncthreads();
-  if (2 * t == sc.i[0]) sc.mx = v0;
-  if (2 * t + 1 == sc.i[0]) sc.mx = v1;
-  __syncthreads();
-  if (sc.zero) {
-    for (int i = t; i < 292; i += 128) qb[i] = 0;
-    __syncthreads();
+  if (!(a > 0.0f)) {
+    for (int i = l; i < 292; i += 32) qb[i] = 0;
     return;
   }
-  const float iscale = __fdiv_rn(-127.0f, sc.mx);
-  int q[2];
-  const float vv[2] = {v0, v1};
+  const float mx = y[idx];
+  const float iscale = __fdiv_rn(-127.0f, mx);
 #pragma unroll
-  for (int k = 0; k < 2; k++) {
-    unsigned f = __float_as_uint(__fmaf_rn(vv[k], iscale, 12582912.0f));
+  for (int k = 0; k < 8; k++) {
+    unsigned f = __float_as_uint(__fmaf_rn(v[k], iscale, 12582912.0f));
     if ((f & 0x7fffffffu) > 0x7f800000u) f = 0x7fc00000u;
-    const int qq = (int)(f & 0x007fffffu) - 0x00400000;
-    q[k] = qq < 127 ? qq : 127;
-  }
-  qb[4 + 2 * t] = (uint8_t)(int8_t)q[0];
-  qb[5 + 2 * t] = (uint8_t)(int8_t)q[1];
-  int s = q[0] + q[1];   // 16 values = 8 consecutive threads
+    int q = (int)(f & 0x007fffffu) - 0x00400000;
+    q = q < 127 ? q : 127;
+    qb[4 + l + 32 * k] = (uint8_t)(int8_t)q;
+    // value l + 32k lies in 16-group 2k + (l >= 16): sum over each half-warp
+    int s = q;
 #pragma unroll
-  for (int o = 4; o > 0; o >>= 1) s += __shfl_down_sync(0xffffffffu, s, o, 8);
-  if ((lane & 7) == 0) {
-    const uint16_t s16 = (uint16_t)(int16_t)s;
-    const int g = t >> 3;
-    qb[260 + 2 * g] = (uint8_t)(s16 & 0xff);
-    qb[261 + 2 * g] = (uint8_t)(s16 >> 8);
+    for (int o = 8; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+    if ((l & 15) == 0) {
+      const uint16_t s16 = (uint16_t)(int16_t)s;
+      const int g = 2 * k + (l >> 4);
+      qb[260 + 2 * g] = (uint8_t)(s16 & 0xff);
+      qb[261 + 2 * g] = (uint8_t)(s16 >> 8);
+    }
   }
-  if (t == 0) {
+  if (l == 0) {
     const unsigned u = __float_as_uint(__fdiv_rn(1.0f, iscale));
     qb[0] = u & 0xff; qb[1] = (u >> 8) & 0xff; qb[2] = (u >> 16) & 0xff; qb[3] = u >> 24;
   }
-  __syncthreads();
 }

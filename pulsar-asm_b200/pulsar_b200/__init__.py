@@ -111,6 +111,7 @@ def lib():
     L.pb_bonsai_state_kv.argtypes = [vp, i, i, pvp]
     L.pb_bonsai_state_residual.argtypes = [vp, vp, vp]
     L.pb_bonsai_state_fallbacks.argtypes = [vp, C.POINTER(i)]
+    L.pb_bonsai_state_status.argtypes = [vp, vp]
     L.pb_bonsai_decode.argtypes = [vp, vp, i, i, vp, vp, C.POINTER(i), vp]
     L.pb_bonsai_decode_greedy.argtypes = [vp, vp, i, i, i, vp, vp]
     _lib = L
@@ -488,6 +489,9 @@ class BonsaiState:
 
     def residual(self, out, stream=None):
         check(lib().pb_bonsai_state_residual(self.h, _ptr(out), _stream(stream)))
+
+    def status(self, stream=None):
+        check(lib().pb_bonsai_state_status(self.h, _stream(stream)))
 
     def fallbacks(self):
         v = C.c_int(0)

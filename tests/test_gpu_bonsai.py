@@ -39,6 +39,7 @@ def test_bonsai_tiny_steps(oracle, pb, cuda):
         assert np.array_equal(_bits(lg.cpu().numpy()), _bits(lw)), "logits differ at position %d" % pos
         assert np.array_equal(_bits(xr.cpu().numpy()), _bits(xw)), "residual differs at position %d" % pos
         assert got == want
+    s.status()
     n = len(toks)
     for L in range(c["n_layers"]):
         for which in (0, 1):
@@ -72,6 +73,7 @@ def test_bonsai_8b_layers_ctx2048(oracle, pb, cuda):
         torch.cuda.synchronize()
         assert np.array_equal(_bits(lg.cpu().numpy()), _bits(lw)), "logits differ at position %d" % p
         assert got == want
+    s.status()
     for L in range(c["n_layers"]):
         for which in (0, 1):
             dev = s.kv(L, which).cpu().numpy().view(np.uint16)
