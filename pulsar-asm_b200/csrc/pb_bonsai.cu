@@ -269,18 +269,16 @@ PB_DEV float bs_r16(float x) { return __half2float(__float2half_rn(x)); }
 // the serial algorithm's "s > M" keeps the earliest of equal maxima and never
 // takes a NaN: the prefix max maps NaN to -inf and combines (earlier, later)
 PB_DEV float bs_max_comb(float m, float s) { return s > m ? s : m; }
-// grid NH CTAs of 64 threads, one head each; thread j owns dimensions 2j and
-// 2j+1: two independent accumulator chains.
-//
-// Softmax weights: thread j owns positions [j*C, j*C +
-// C) of the running-max scan (the scratch copy of the scores is skewed by one
+// grid NH CTAs of 256 threads, one head each. Softmax weights (all 256
+// threads): thread i owns positions [i*C, i*C + C) of the running-max scan (the scratch copy of the scores is skewed by one
 // word per 32 so that these strided walks hit distinct banks). Per position
 // the scan leaves the exponent argument (Mold - s at a new maximum, s - M
 // otherwise) and a flag; a coalesced pass takes the exponentials into the
 // chain's array w (bit 31 = new maximum: w is ms and vs = 1; else w is vs and
 // ms = 1) and marks every 16-position group that holds a new maximum.
 //
-// The chains read V as f16 pairs straight from a ring of BS_PV_NST tiles,
+// The chains (two warps; thread j owns dimensions 2j and 2j+1: two
+// independent accumulator chains) read V as f16 pairs from a ring of BS_PV_NST tiles,
 // each tile (contiguous rows of the kv head) one bulk copy completing on its
 // slot's mbarrier (bounded waits: a copy that never lands sets the control
 // block's error and ends the CTA). A 16-position group with no new maximum
@@ -292,37 +290,54 @@ PB_DEV int bs_skew(int p) { return p + (p >> 5); }
 __host__ __device__ inline int bs_skew_len(int mc) { return (mc + mc / 32 + 3) & ~3; }
 // group flags per head, padded to whole words (the chain reads a tile's four at once)
 __host__ __device__ inline int bs_nm_len(int mc) { return (mc / 16 + 3) & ~3; }
-// one 16-position group of the general step (a group that holds a new maximum)
-PB_DEV void bs_chain_group_general(const uint32_t* __restrict__ vb, const uint32_t* __restrict__ w, int n,
-                                   float& accA, float& accB, float& Ssum) {
-  for (int k = 0; k < n; k++) {
-    const uint32_t e = w[k];
-    const bool nmax = (e >> 31) != 0;
-    const float wk = __uint_as_float(e & 0x7fffffffu), ms = nmax ? wk : 1.0f, vs = nmax ? 1.0f : wk;
-    const uint32_t v = vb[k * 64];
-    if (ms != 1.0f) { accA = bs_r16(__fmul_rn(accA, ms)); accB = bs_r16(__fmul_rn(accB, ms)); }
-    accA = bs_r16(__fmaf_rn(pb_h2f((unsigned short)(v & 0xffffu)), vs, accA));
-    accB = bs_r16(__fmaf_rn(pb_h2f((unsigned short)(v >> 16)), vs, accB));
-    Ssum = __fmaf_rn(Ssum, ms, vs);
-  }
-}
-// one 16-position group of the branch-free step (all weights are vs)
-PB_DEV void bs_chain_group_fast(const uint32_t* __restrict__ vb, const uint32_t* __restrict__ w, float& accA,
-                                float& accB, float& Ssum) {
+// one tile of the chain for dims (2j, 2j+1): vb[r * 64] is row r's pair, w
+// the tile's encoded weights, nmt its 4 group flags, n <= 64 valid rows. Each
+// group's operands are loaded one group ahead; a full group with no new
+// maximum takes the branch-free step, any other group the general one.
+PB_DEV void bs_chain_tile(const uint32_t* __restrict__ vb, const uint32_t* __restrict__ w,
+                          const unsigned char* __restrict__ nmt, int n, float& accA, float& accB, float& Ssum) {
   uint4 wn[4];
   uint32_t vn[16];
 #pragma unroll
   for (int k = 0; k < 4; k++) wn[k] = reinterpret_cast<const uint4*>(w)[k];
 #pragma unroll
   for (int k = 0; k < 16; k++) vn[k] = vb[k * 64];
-  const uint32_t wk[16] = {wn[0].x, wn[0].y, wn[0].z, wn[0].w, wn[1].x, wn[1].y, wn[1].z, wn[1].w,
-                           wn[2].x, wn[2].y, wn[2].z, wn[2].w, wn[3].x, wn[3].y, wn[3].z, wn[3].w};
 #pragma unroll
-  for (int k = 0; k < 16; k++) {
-    const float wf = __uint_as_float(wk[k]);
-    accA = bs_r16(__fmaf_rn(pb_h2f((unsigned short)(vn[k] & 0xffffu)), wf, accA));
-    accB = bs_r16(__fmaf_rn(pb_h2f((unsigned short)(vn[k] >> 16)), wf, accB));
-    Ssum = __fadd_rn(Ssum, wf);
+  for (int gi = 0; gi < BS_PV_TT / 16; gi++) {
+    const int g0 = gi * 16;
+    if (g0 >= n) break;
+    const uint32_t wc[16] = {wn[0].x, wn[0].y, wn[0].z, wn[0].w, wn[1].x, wn[1].y, wn[1].z, wn[1].w,
+                             wn[2].x, wn[2].y, wn[2].z, wn[2].w, wn[3].x, wn[3].y, wn[3].z, wn[3].w};
+    uint32_t vc[16];
+#pragma unroll
+    for (int k = 0; k < 16; k++) vc[k] = vn[k];
+    if (gi + 1 < BS_PV_TT / 16) {   // rows past n are stale shared memory, never used
+#pragma unroll
+      for (int k = 0; k < 4; k++) wn[k] = reinterpret_cast<const uint4*>(w + g0 + 16)[k];
+#pragma unroll
+      for (int k = 0; k < 16; k++) vn[k] = vb[(g0 + 16 + k) * 64];
+    }
+    if (g0 + 16 <= n && !nmt[gi]) {
+#pragma unroll
+      for (int k = 0; k < 16; k++) {
+        const float wf = __uint_as_float(wc[k]);
+        accA = bs_r16(__fmaf_rn(pb_h2f((unsigned short)(vc[k] & 0xffffu)), wf, accA));
+        accB = bs_r16(__fmaf_rn(pb_h2f((unsigned short)(vc[k] >> 16)), wf, accB));
+        Ssum = __fadd_rn(Ssum, wf);
+      }
+    } else {
+#pragma unroll
+      for (int k = 0; k < 16; k++) {
+        if (g0 + k < n) {
+          const bool nmax = (wc[k] >> 31) != 0;
+          const float wk = __uint_as_float(wc[k] & 0x7fffffffu), ms = nmax ? wk : 1.0f, vs = nmax ? 1.0f : wk;
+          if (ms != 1.0f) { accA = bs_r16(__fmul_rn(accA, ms)); accB = bs_r16(__fmul_rn(accB, ms)); }
+          accA = bs_r16(__fmaf_rn(pb_h2f((unsigned short)(vc[k] & 0xffffu)), vs, accA));
+          accB = bs_r16(__fmaf_rn(pb_h2f((unsigned short)(vc[k] >> 16)), vs, accB));
+          Ssum = __fmaf_rn(Ssum, ms, vs);
+        }
+      }
+    }
   }
 }
 PB_DEV uint32_t bs_smem_u32(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
@@ -337,7 +352,7 @@ PB_DEV bool bs_mbar_wait(uint64_t* b, unsigned parity) {   // bounded
     if (bs_mbar_try(b, parity)) return true;
   return false;
 }
-__global__ void __launch_bounds__(64) k_bs_fa_pv(BsPvArgs a) {
+__global__ void __launch_bounds__(256) k_bs_fa_pv(BsPvArgs a) {
   extern __shared__ __align__(16) unsigned char smem[];
   const int mc = a.max_ctx, mcs = bs_skew_len(mc);
   uint32_t* sw = reinterpret_cast<uint32_t*>(smem);                  // [mc] encoded weights
@@ -345,12 +360,12 @@ __global__ void __launch_bounds__(64) k_bs_fa_pv(BsPvArgs a) {
   uint16_t* vt = reinterpret_cast<uint16_t*>(sk + mcs);              // [NST][TT][128] f16 ring
   unsigned char* nm = reinterpret_cast<unsigned char*>(vt + (size_t)BS_PV_NST * BS_PV_TT * BS_HD);   // [nm_len]
   __shared__ __align__(8) uint64_t full[BS_PV_NST];
-  __shared__ float wmax[2];
+  __shared__ float wmax[8];
   __shared__ float s_S;
-  __shared__ int s_last;
+  __shared__ int s_last, s_fail;
   pb_grid_wait();
   pb_grid_launch_dependents();
-  const int T = a.ctl->pos + 1, tid = threadIdx.x, lane = tid & 31, w = tid >> 5, j = tid;
+  const int T = a.ctl->pos + 1, tid = threadIdx.x, lane = tid & 31, w = tid >> 5;
   const int h = blockIdx.x, kvh = h / (a.NH / a.NKV);
   const uint16_t* V = a.vc + (size_t)kvh * mc * BS_HD;
   const int ntile = (T + BS_PV_TT - 1) / BS_PV_TT;
@@ -360,6 +375,7 @@ __global__ void __launch_bounds__(64) k_bs_fa_pv(BsPvArgs a) {
     for (int k = 0; k < BS_PV_NST; k++)
       asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(bs_smem_u32(&full[k])) : "memory");
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    s_fail = 0;
   }
   __syncthreads();
   auto issue = [&](int tile) {   // thread 0
@@ -375,18 +391,18 @@ __global__ void __launch_bounds__(64) k_bs_fa_pv(BsPvArgs a) {
   if (tid == 0)
     for (int k = 0; k < BS_PV_NST; k++) issue(k);
   {
-    // ---- the head's scores (16 loads in flight per thread)
+    // ---- softmax weights, all 256 threads: the head's scores
     const float* S = a.sc + (size_t)h * mc;
-    for (int p0 = j; p0 < T; p0 += 16 * 64) {
-      float sv[16];
+    for (int p0 = tid; p0 < T; p0 += 8 * 256) {
+      float sv[8];
 #pragma unroll
-      for (int k = 0; k < 16; k++) { const int p = p0 + 64 * k; sv[k] = p < T ? S[p] : 0.0f; }
+      for (int k = 0; k < 8; k++) { const int p = p0 + 256 * k; sv[k] = p < T ? S[p] : 0.0f; }
 #pragma unroll
-      for (int k = 0; k < 16; k++) { const int p = p0 + 64 * k; if (p < T) sk[bs_skew(p)] = sv[k]; }
+      for (int k = 0; k < 8; k++) { const int p = p0 + 256 * k; if (p < T) sk[bs_skew(p)] = sv[k]; }
     }
     __syncthreads();
-    // ---- running maxima
-    const int C = (T + 63) / 64, p0 = j * C, p1 = min(T, p0 + C);
+    // ---- running maxima: thread i owns positions [i*C, i*C + C)
+    const int C = (T + 255) / 256, p0 = tid * C, p1 = min(T, p0 + C);
     float m = -INFINITY;
     for (int p = p0; p < p1; p++) { const float x = sk[bs_skew(p)]; m = bs_max_comb(m, x != x ? -INFINITY : x); }
     float inc = m;
@@ -399,7 +415,9 @@ __global__ void __launch_bounds__(64) k_bs_fa_pv(BsPvArgs a) {
     __syncthreads();
     float ex = __shfl_up_sync(0xffffffffu, inc, 1);
     if (lane == 0) ex = -INFINITY;
-    float M = w ? bs_max_comb(wmax[0], ex) : ex;
+    float M = -INFINITY;
+    for (int ww = 0; ww < w; ww++) M = bs_max_comb(M, wmax[ww]);
+    M = bs_max_comb(M, ex);
     for (int p = p0; p < p1; p++) {   // in place: the score becomes |exponent argument| | flag
       const int q = bs_skew(p);
       const float x = sk[q];
@@ -410,46 +428,38 @@ __global__ void __launch_bounds__(64) k_bs_fa_pv(BsPvArgs a) {
       sk[q] = __uint_as_float((__float_as_uint(arg) & 0x7fffffffu) | (flag << 31));
     }
     __syncthreads();
-    // ---- exponentials, coalesced, four 32-position blocks per warp pass;
-    // group flags by ballot. Every argument is <= 0 or NaN: its sign is restored.
-    for (int pb0 = w * 32; pb0 < ((T + 31) & ~31); pb0 += 4 * 64) {
-      uint32_t ab[4];
-#pragma unroll
-      for (int u = 0; u < 4; u++) {
-        const int p = pb0 + u * 64 + lane;
-        ab[u] = p < T ? __float_as_uint(sk[bs_skew(p)]) : 0u;
+    // ---- exponentials, coalesced; group flags by ballot. Every argument
+    // is <= 0 or NaN: its sign is restored.
+    for (int pb = w * 32; pb < ((T + 31) & ~31); pb += 8 * 32) {
+      const int p = pb + lane;
+      bool nmax = false;
+      if (p < T) {
+        const uint32_t ab = __float_as_uint(sk[bs_skew(p)]);
+        nmax = (ab >> 31) != 0;
+        const uint32_t mag = ab & 0x7fffffffu;
+        const float e = pb_expf(__uint_as_float(mag | (mag ? 0x80000000u : 0u)));
+        sw[p] = (__float_as_uint(e) & 0x7fffffffu) | (nmax ? 0x80000000u : 0u);
       }
-#pragma unroll
-      for (int u = 0; u < 4; u++) {
-        const int pb = pb0 + u * 64, p = pb + lane;
-        const bool nmax = p < T && (ab[u] >> 31) != 0;
-        if (p < T) {
-          const uint32_t mag = ab[u] & 0x7fffffffu;
-          const float e = pb_expf(__uint_as_float(mag | (mag ? 0x80000000u : 0u)));
-          sw[p] = (__float_as_uint(e) & 0x7fffffffu) | (nmax ? 0x80000000u : 0u);
-        }
-        const unsigned bal = __ballot_sync(0xffffffffu, nmax);
-        if (lane == 0 && pb < T) nm[pb >> 4] = (bal & 0xffffu) != 0;
-        if (lane == 16 && pb + 16 < T) nm[(pb >> 4) + 1] = (bal >> 16) != 0;
-      }
+      const unsigned bal = __ballot_sync(0xffffffffu, nmax);
+      if (lane == 0 && pb < T) nm[pb >> 4] = (bal & 0xffffu) != 0;
+      if (lane == 16 && pb + 16 < T) nm[(pb >> 4) + 1] = (bal >> 16) != 0;
     }
     __syncthreads();
   }
-  // ---- the chains, positions in order; a group with no new maximum takes
-  // the branch-free step
+  if (w >= 2) return;   // the chains are two warps; the others are done
+  // ---- the chains (thread j < 64 owns dims 2j, 2j+1), positions in order;
+  // named barrier 1 over the 64 chain threads
+  const int j = tid;
   float accA = 0.0f, accB = 0.0f, Ssum = 0.0f;
   int failed = -1;   // the tile whose copy never landed (the CTA gives up)
   for (int tile = 0; tile < ntile; tile++) {
-    const bool ok = bs_mbar_wait(&full[tile % BS_PV_NST], (unsigned)(tile / BS_PV_NST) & 1u);
-    if (__syncthreads_or(!ok)) { failed = tile; break; }   // the same decision in every thread
-    const uint32_t* vb = reinterpret_cast<const uint32_t*>(vt + (size_t)(tile % BS_PV_NST) * BS_PV_TT * BS_HD) + j;
-    const int r0 = tile * BS_PV_TT, n = min(BS_PV_TT, T - r0);
-#pragma unroll 1
-    for (int g0 = 0; g0 < n; g0 += 16) {
-      if (g0 + 16 <= n && !nm[(r0 + g0) >> 4]) bs_chain_group_fast(vb + g0 * 64, sw + r0 + g0, accA, accB, Ssum);
-      else bs_chain_group_general(vb + g0 * 64, sw + r0 + g0, min(16, n - g0), accA, accB, Ssum);
-    }
-    __syncthreads();   // every thread has left the slot: refill it
+    if (!bs_mbar_wait(&full[tile % BS_PV_NST], (unsigned)(tile / BS_PV_NST) & 1u)) s_fail = 1;
+    asm volatile("bar.sync 1, 64;" ::: "memory");
+    if (s_fail) { failed = tile; break; }   // read after the barrier: the same decision in every thread
+    const int r0 = tile * BS_PV_TT;
+    bs_chain_tile(reinterpret_cast<const uint32_t*>(vt + (size_t)(tile % BS_PV_NST) * BS_PV_TT * BS_HD) + j,
+                  sw + r0, nm + (r0 >> 4), min(BS_PV_TT, T - r0), accA, accB, Ssum);
+    asm volatile("bar.sync 1, 64;" ::: "memory");   // every chain thread has left the slot: refill it
     if (tid == 0) issue(tile + BS_PV_NST);
   }
   if (failed >= 0) {   // wait (bounded) for the copies still in flight, then report
@@ -461,22 +471,22 @@ __global__ void __launch_bounds__(64) k_bs_fa_pv(BsPvArgs a) {
     return;
   }
   if (j == 0) s_S = Ssum;
-  __syncthreads();
+  asm volatile("bar.sync 1, 64;" ::: "memory");
   const float si = s_S == 0.0f ? 0.0f : __fdiv_rn(1.0f, s_S);
   *reinterpret_cast<float2*>(a.atto + (size_t)h * BS_HD + 2 * j) = make_float2(__fmul_rn(accA, si), __fmul_rn(accB, si));
   // the second head of each pair to finish quantises the pair's 256 outputs
   // (one Q8_K block); the first one's stores are visible through the fence
   __threadfence();
-  __syncthreads();
+  asm volatile("bar.sync 1, 64;" ::: "memory");
   if (tid == 0) s_last = atomicAdd(&a.ctl->pv_pair[h >> 1], 1u) == 1u;
-  __syncthreads();
+  asm volatile("bar.sync 1, 64;" ::: "memory");
   if (!s_last) return;
   __threadfence();
   float* y = reinterpret_cast<float*>(vt);   // [256] staging
   const float* src = a.atto + (size_t)(h & ~1) * BS_HD;
 #pragma unroll
   for (int k = 0; k < 4; k++) y[tid + 64 * k] = __ldcg(src + tid + 64 * k);
-  __syncthreads();
+  asm volatile("bar.sync 1, 64;" ::: "memory");
   if (w == 0) pb_q8k_block256_warp(y, a.xq + (size_t)(h >> 1) * 292);
   if (tid == 0) a.ctl->pv_pair[h >> 1] = 0u;
 }
@@ -703,7 +713,7 @@ int bs_record(pb_bonsai* m, pb_bonsai_state* s, cudaStream_t st) {
     }
     {
       BsPvArgs a{s->scores, vc, s->atto, s->xq, NH, NKV, s->max_ctx, s->ctl};
-      if ((rc = bs_launch(k_bs_fa_pv, dim3(NH), 64, pv_smem(s->max_ctx), st, a, "k_bs_fa_pv"))) return rc;
+      if ((rc = bs_launch(k_bs_fa_pv, dim3(NH), 256, pv_smem(s->max_ctx), st, a, "k_bs_fa_pv"))) return rc;
     }
     if ((rc = pb_q1_gemv_launch(&m->o[L], s->xq, s->ao, nullptr, st, true))) return rc;
     {   // x += attention output ; rms(ffn_norm) ; Q8_K
