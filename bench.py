@@ -41,6 +41,7 @@ def parse():
     ap.add_argument("--cpu-seconds", type=float, default=15.0)
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--no-kernels", action="store_true", help="skip the per-kernel GB/s suite")
+    ap.add_argument("--no-tp", action="store_true", help="skip the row-sharded decode at N > 1")
     ap.add_argument("--blob", default=os.environ.get("PB_BENCH_BLOB", "/tmp/pb_cfg1.lfm3q8"))
     ap.add_argument("--layers", type=int, default=0,
                     help="profiling only: a shallower model of the same shapes (0 = the 24-layer cfg1)")
@@ -415,6 +416,38 @@ def bonsai_setup(torch, pb, stream, max_ctx, pos0, n_layers=None):
     return c, m, s
 
 
+def tp_bench(torch, pb, model, prompt, stream, rank, world, steps=32, warmup=3):
+    """one sequence decoded with every GEMV's rows split over the ranks and
+    each output all-gathered over NVLink (pb_state_shard); the same prompt as
+    the replica measurement, then `steps` greedy tokens timed by CUDA events,
+    max over ranks"""
+    from pulsar_b200 import dist
+    ctx = int(prompt.numel())
+    st = model.new_state(ctx + warmup + steps + 8)
+    uid = dist.share_from_rank0(pb.nccl_unique_id)
+    st.shard(rank, world, uid)
+    ids = torch.empty(warmup + steps, dtype=torch.int32, device="cuda")
+    with torch.cuda.stream(stream):
+        st.decode_prompt(prompt, 0, stream=stream)
+        st.decode_greedy(int(prompt[-1].item()), ctx, warmup, ids[:warmup], stream=stream)
+        stream.synchronize()
+        nxt = int(ids[warmup - 1].item())
+        dist.barrier()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        st.decode_greedy(nxt, ctx + warmup, steps, ids[warmup:], stream=stream)
+        e1.record(stream)
+        e1.synchronize()
+    st.status(stream)
+    ms = dist.max_over_ranks(e0.elapsed_time(e1), device="cuda")
+    kpt = st.kernels_per_token()
+    st.destroy()
+    return {"ranks": world, "steps": steps, "ms_per_token": ms / steps, "tok/s": steps / (ms / 1e3),
+            "kernels_per_token": kpt,
+            "path": "row-sharded GEMVs (rank r computes rows [r N/world, (r+1) N/world)), in-place NCCL "
+                    "all-gather of every output, CUDA graph per token; one sequence over all GPUs"}
+
+
 def run_reference(args, rank, world):
     """--impl reference: the reference's CPU implementation of this path (the
     oracle port: the reference's decode engine has no CPU form) on this box's
@@ -553,6 +586,8 @@ def main():
                               else "fallback 6.65 TB/s"}, **rk),
             "step_kernel_gbs": k_bytes / (k_ms / 1000.0) / 1e9,
             "clocks": clk.summary()}
+    if world > 1 and not args.no_tp:
+        line["tp_decode"] = tp_bench(torch, pb, model, prompt, stream, rank, world)
     if rank == 0 and world == 1 and not args.no_kernels:
         line["kernels"] = kernel_suite(torch, pb, peak, stream)
         line["kernels"]["cfg2_prefill"] = prefill_bench(torch, model, prompt, stream)

@@ -199,6 +199,19 @@ int pb_decode_batch(pb_model* m, pb_state* const* states, int B, const int* d_to
 /* synchronise `stream` and report a decode failure recorded on the device
  * (a bounded wait inside the decode kernel that gave up): PB_OK or PB_ECUDA */
 int pb_state_status(pb_state* s, void* stream);
+/* Row sharding of one sequence's decode over `world` GPUs (one process per
+ * GPU, every rank holding the same model and calling the same decode entry
+ * points in the same order): each GEMV computes the rank's rows [rank*N/world,
+ * (rank+1)*N/world) and an in-place NCCL all-gather over NVLink completes the
+ * output vector before the next kernel; the head's logits are gathered and a
+ * global greedy argmax publishes the id. Results equal the unsharded decode
+ * bit for bit (every row is computed whole on one rank). `id` is the
+ * ncclUniqueId from pb_nccl_unique_id on rank 0, shared by the caller;
+ * pb_state_shard is collective. NCCL is resolved at run time (libnccl.so.2).
+ * The survey's row-sharded layout with per-layer all-gather (no reference
+ * counterpart: the reference engine runs on one device). */
+int pb_nccl_unique_id(void* out, size_t bytes);
+int pb_state_shard(pb_state* s, int rank, int world, const void* id);
 /* kernel launches per decode token: 1 on the persistent path (one launch
  * decodes any number of tokens), the CUDA graph's node count otherwise */
 int pb_decode_kernels_per_token(pb_state* s);

@@ -30,6 +30,8 @@
 #include <vector>
 #include <algorithm>
 #include <mutex>
+#include <dlfcn.h>
+#include <nccl.h>   // types only: the library resolves NCCL at run time
 
 namespace {
 
@@ -198,7 +200,7 @@ __global__ void __launch_bounds__(256, 2) k_step(StepArgs a) {
       }
     }
   }
-  if (EPI == EPI_ARGMAX) {
+  if (EPI == EPI_ARGMAX && !a.no_publish) {
     // greedy argmax, ties to the lowest index: per-thread best -> warp -> CTA
     // slot; the last CTA to finish reduces the slots and publishes the id.
 #pragma unroll
@@ -354,6 +356,10 @@ struct pb_state {
   bf16_t* pf_att = nullptr;       // [T][NH*HD] gated attention output
   float* pf_logits = nullptr;     // [T][V]
   int* pf_tok = nullptr;          // [T]
+  // row sharding over tp_world ranks (pb_state_shard): every GEMV computes its
+  // rank's rows, an in-place NCCL all-gather completes the output vector
+  int tp_rank = 0, tp_world = 1;
+  ncclComm_t comm = nullptr;
 };
 
 namespace {
@@ -458,6 +464,96 @@ int launch_attn(const pb_model* m, pb_state* s, int layer, cudaStream_t st, bool
   return PB_OK;
 }
 
+// ---- row sharding --------------------------------------------------------
+// NCCL is resolved at run time from the libnccl.so.2 already in the process
+// (the one torch.distributed loaded) or, failing that, the system one; the
+// library itself links only libcudart and libz.
+struct NcclApi {
+  ncclResult_t (*get_unique_id)(ncclUniqueId*) = nullptr;
+  ncclResult_t (*comm_init_rank)(ncclComm_t*, int, ncclUniqueId, int) = nullptr;
+  ncclResult_t (*all_gather)(const void*, void*, size_t, ncclDataType_t, ncclComm_t, cudaStream_t) = nullptr;
+  ncclResult_t (*comm_destroy)(ncclComm_t) = nullptr;
+  const char* (*error_string)(ncclResult_t) = nullptr;
+  bool ok = false;
+};
+NcclApi& nccl() {
+  static NcclApi api;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* h = dlopen("libnccl.so.2", RTLD_NOW | RTLD_NOLOAD);
+    if (!h) h = dlopen("libnccl.so.2", RTLD_NOW | RTLD_GLOBAL);
+    if (!h) return;
+    api.get_unique_id = reinterpret_cast<decltype(api.get_unique_id)>(dlsym(h, "ncclGetUniqueId"));
+    api.comm_init_rank = reinterpret_cast<decltype(api.comm_init_rank)>(dlsym(h, "ncclCommInitRank"));
+    api.all_gather = reinterpret_cast<decltype(api.all_gather)>(dlsym(h, "ncclAllGather"));
+    api.comm_destroy = reinterpret_cast<decltype(api.comm_destroy)>(dlsym(h, "ncclCommDestroy"));
+    api.error_string = reinterpret_cast<decltype(api.error_string)>(dlsym(h, "ncclGetErrorString"));
+    api.ok = api.get_unique_id && api.comm_init_rank && api.all_gather && api.comm_destroy && api.error_string;
+  });
+  return api;
+}
+
+// the greedy id of the full (gathered) logits, ties to the lowest index; the
+// control block advances as the unsharded head's epilogue advances it
+__global__ void __launch_bounds__(1024) k_tp_argmax(const float* __restrict__ lg, int V, Ctl* ctl) {
+  __shared__ float bv[32];
+  __shared__ int bi[32];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  float b = -INFINITY;
+  int ix = 0x7fffffff;
+  for (int i = threadIdx.x; i < V; i += blockDim.x) {
+    const float v = lg[i];
+    if (v > b || (v == b && i < ix)) { b = v; ix = i; }
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const float ov = __shfl_down_sync(0xffffffffu, b, o);
+    const int oi = __shfl_down_sync(0xffffffffu, ix, o);
+    if (ov > b || (ov == b && oi < ix)) { b = ov; ix = oi; }
+  }
+  if (lane == 0) { bv[warp] = b; bi[warp] = ix; }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    for (int w = 1; w < 32; w++)
+      if (bv[w] > bv[0] || (bv[w] == bv[0] && bi[w] < bi[0])) { bv[0] = bv[w]; bi[0] = bi[w]; }
+    const int id = bi[0];
+    const int step = ctl->step;
+    ctl->token = (step + 1 < ctl->n_prompt) ? ctl->prompt[step + 1] : id;
+    if (ctl->ids) ctl->ids[step] = id;
+    ctl->step = step + 1;
+    ctl->pos += 1;
+  }
+}
+
+// one GEMV of the step: the whole tensor, or this rank's rows followed by the
+// in-place all-gather of the output (bf16 rows, bf16 SiLU pairs, fp32 logits)
+int launch_gemv(pb_state* s, const pb_q8& w, int epi, StepArgs a, cudaStream_t st, bool pdl, uint64_t& nk) {
+  if (s->tp_world <= 1) {
+    const int rc = launch_step(w, epi, a, st, pdl);
+    if (!rc) nk++;
+    return rc;
+  }
+  const int world = s->tp_world, r = s->tp_rank, rows = w.N / world, r0 = r * rows;
+  pb_q8 part = w;
+  part.N = rows;
+  part.owner = false;
+  part.codes = w.codes + (size_t)r0 * w.nch * 2048;
+  part.scales = static_cast<char*>(w.scales) + (size_t)r0 * w.nch * 32 * (w.sdt == PB_DT_F32 ? 8 : 4);
+  size_t elem = 2, per_rank = rows, first = r0;
+  if (epi == EPI_SILU) { per_rank = rows / 2; first = r0 / 2; }
+  else if (epi == EPI_ARGMAX) { elem = 4; a.no_publish = 1; }
+  char* full = static_cast<char*>(a.y);
+  a.y = full + first * elem;
+  int rc = launch_step(part, epi, a, st, pdl);
+  if (rc) return rc;
+  nk++;
+  const ncclResult_t nr = nccl().all_gather(full + (size_t)r * per_rank * elem, full, per_rank * elem, ncclUint8,
+                                            s->comm, st);
+  if (nr != ncclSuccess) return pb_set_error(PB_ECUDA, "ncclAllGather: %s", nccl().error_string(nr));
+  nk++;
+  return PB_OK;
+}
+
 StepArgs base_args(const pb_model* m, pb_state* s) {
   StepArgs a = {};
   a.H = m->H;
@@ -495,8 +591,7 @@ int enqueue_layer(const pb_model* m, pb_state* s, int L, int& cur, int first_mod
       cur ^= 1;
     }
   }
-  if ((rc = launch_step(Ly.first, EPI_BF16, a, st, pdl))) return rc;
-  nk++;
+  if ((rc = launch_gemv(s, Ly.first, EPI_BF16, a, st, pdl, nk))) return rc;
   if (Ly.attn) {
     if ((rc = launch_attn(m, s, L, st, pdl))) return rc;
     nk++;
@@ -504,8 +599,7 @@ int enqueue_layer(const pb_model* m, pb_state* s, int L, int& cur, int first_mod
     b.pro = PRO_PLAIN;
     b.xin = s->h_attn;
     b.y = s->h_mix;
-    if ((rc = launch_step(Ly.mix, EPI_BF16, b, st, pdl))) return rc;
-    nk++;
+    if ((rc = launch_gemv(s, Ly.mix, EPI_BF16, b, st, pdl, nk))) return rc;
   } else {
     StepArgs b = base_args(m, s);
     b.pro = PRO_CONV;
@@ -513,8 +607,7 @@ int enqueue_layer(const pb_model* m, pb_state* s, int L, int& cur, int first_mod
     b.ring = s->ring + (size_t)Ly.conv_idx * m->W * m->H;
     b.taps = Ly.taps;
     b.y = s->h_mix;
-    if ((rc = launch_step(Ly.mix, EPI_BF16, b, st, pdl))) return rc;
-    nk++;
+    if ((rc = launch_gemv(s, Ly.mix, EPI_BF16, b, st, pdl, nk))) return rc;
   }
   // post_operator_norm + residual + ffn_norm -> w1|w3 (+ SiLU*mul)
   StepArgs c = base_args(m, s);
@@ -526,14 +619,12 @@ int enqueue_layer(const pb_model* m, pb_state* s, int L, int& cur, int first_mod
   c.rout = s->res[cur ^ 1];
   cur ^= 1;
   c.y = s->h_u;
-  if ((rc = launch_step(Ly.w13, EPI_SILU, c, st, pdl))) return rc;
-  nk++;
+  if ((rc = launch_gemv(s, Ly.w13, EPI_SILU, c, st, pdl, nk))) return rc;
   StepArgs d = base_args(m, s);
   d.pro = PRO_PLAIN;
   d.xin = s->h_u;
   d.y = s->h_w2;
-  if ((rc = launch_step(Ly.w2, EPI_BF16, d, st, pdl))) return rc;
-  nk++;
+  if ((rc = launch_gemv(s, Ly.w2, EPI_BF16, d, st, pdl, nk))) return rc;
   return PB_OK;
 }
 
@@ -552,8 +643,12 @@ int enqueue_token(const pb_model* m, pb_state* s, cudaStream_t st, bool pdl, int
   h.rout = s->res[cur ^ 1];
   final_res = cur ^ 1;
   h.y = s->logits;
-  if ((rc = launch_step(m->head, EPI_ARGMAX, h, st, pdl))) return rc;
-  nk++;
+  if ((rc = launch_gemv(s, m->head, EPI_ARGMAX, h, st, pdl, nk))) return rc;
+  if (s->tp_world > 1) {
+    k_tp_argmax<<<1, 1024, 0, st>>>(s->logits, m->V, s->ctl);
+    PB_LAUNCHED("k_tp_argmax");
+    nk++;
+  }
   return PB_OK;
 }
 
@@ -1252,6 +1347,7 @@ extern "C" int pb_state_create(pb_model* m, int max_ctx, pb_state** out) {
 
 extern "C" int pb_state_destroy(pb_state* s) {
   if (!s) return PB_OK;
+  if (s->comm) nccl().comm_destroy(s->comm);
   if (s->d_phases) cudaFree(s->d_phases);
   if (s->d_sched) cudaFree(s->d_sched);
   if (s->d_trace) cudaFree(s->d_trace);
@@ -1360,6 +1456,48 @@ extern "C" int pb_decode_greedy(pb_model* m, pb_state* s, int token, int pos0, i
     PB_TRY_CUDA(cudaGraphLaunch(s->exec, st));
     pb_count_launch(s->graph_launches);
   }
+  return PB_OK;
+}
+
+extern "C" int pb_nccl_unique_id(void* out, size_t bytes) {
+  if (!out || bytes < sizeof(ncclUniqueId))
+    return pb_set_error(PB_EINVAL, "pb_nccl_unique_id: buffer under %zu bytes", sizeof(ncclUniqueId));
+  NcclApi& api = nccl();
+  if (!api.ok) return pb_set_error(PB_ENOTSUP, "pb_nccl_unique_id: libnccl.so.2 not found");
+  ncclUniqueId id;
+  const ncclResult_t r = api.get_unique_id(&id);
+  if (r != ncclSuccess) return pb_set_error(PB_ECUDA, "ncclGetUniqueId: %s", api.error_string(r));
+  memcpy(out, &id, sizeof id);
+  return PB_OK;
+}
+
+extern "C" int pb_state_shard(pb_state* s, int rank, int world, const void* id) {
+  if (!s || !id || world < 1 || rank < 0 || rank >= world) return pb_set_error(PB_EINVAL, "pb_state_shard: bad argument");
+  if (s->comm) return pb_set_error(PB_EINVAL, "pb_state_shard: state already sharded");
+  const pb_model* m = s->m;
+  if (!m->decode_ok) return pb_set_error(PB_ENOTSUP, "pb_state_shard: decode needs the streaming layout");
+  auto fits = [&](const pb_q8& w, int mult) { return w.N % (world * mult) == 0; };
+  for (int L = 0; L < m->L; L++) {
+    const Layer& Ly = m->layers[L];
+    if (!fits(Ly.first, 1) || !fits(Ly.mix, 1) || !fits(Ly.w13, 2) || !fits(Ly.w2, 1))
+      return pb_set_error(PB_ENOTSUP, "pb_state_shard: layer %d rows do not split over %d ranks", L, world);
+  }
+  if (!fits(m->head, 1)) return pb_set_error(PB_ENOTSUP, "pb_state_shard: head rows do not split over %d ranks", world);
+  if (world == 1) return PB_OK;
+  NcclApi& api = nccl();
+  if (!api.ok) return pb_set_error(PB_ENOTSUP, "pb_state_shard: libnccl.so.2 not found");
+  PB_TRY_CUDA(cudaSetDevice(m->device));
+  ncclUniqueId uid;
+  memcpy(&uid, id, sizeof uid);
+  ncclComm_t comm = nullptr;
+  const ncclResult_t r = api.comm_init_rank(&comm, world, uid, rank);   // collective over the ranks
+  if (r != ncclSuccess) return pb_set_error(PB_ECUDA, "ncclCommInitRank: %s", api.error_string(r));
+  s->comm = comm;
+  s->tp_rank = rank;
+  s->tp_world = world;
+  s->persistent = false;   // the per-kernel graph carries the all-gathers
+  if (s->exec) { cudaGraphExecDestroy(s->exec); s->exec = nullptr; }
+  if (s->graph) { cudaGraphDestroy(s->graph); s->graph = nullptr; }
   return PB_OK;
 }
 

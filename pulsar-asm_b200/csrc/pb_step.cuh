@@ -56,6 +56,7 @@ struct StepArgs {
   Ctl* ctl;
   // epilogue
   void* y;
+  int no_publish;      // ARGMAX: write the logits only (the row-sharded head; a separate argmax publishes)
 };
 
 struct AttnArgs {

@@ -102,6 +102,8 @@ def lib():
     L.pb_state_status.argtypes = [vp, vp]
     L.pb_prefill_chunk.argtypes = [vp, vp, vp, i, i, vp, vp, vp]
     L.pb_decode_batch.argtypes = [vp, C.POINTER(vp), i, vp, vp, vp, vp, vp]
+    L.pb_nccl_unique_id.argtypes = [vp, sz]
+    L.pb_state_shard.argtypes = [vp, i, i, vp]
     L.pb_bonsai_create.argtypes = [C.POINTER(BonsaiCfg), i, pvp]
     L.pb_bonsai_destroy.argtypes = [vp]
     L.pb_bonsai_set_q1.argtypes = [vp, i, i, vp, i, vp]
@@ -123,6 +125,13 @@ class BonsaiCfg(C.Structure):
     _fields_ = [(n, C.c_int) for n in ("hidden", "inter", "n_layers", "n_heads", "n_kv", "vocab")] + \
                [("rope_factor", C.c_float), ("rope_orig_ctx", C.c_int), ("rope_base", C.c_float),
                 ("attn_scale", C.c_float)]
+
+
+def nccl_unique_id():
+    """a fresh NCCL unique id (128 bytes) for State.shard"""
+    b = C.create_string_buffer(128)
+    check(lib().pb_nccl_unique_id(b, 128))
+    return b.raw
 
 
 def last_error():
@@ -346,6 +355,12 @@ class State:
     def status(self, stream=None):
         """synchronise and raise if the decode kernel recorded a failure."""
         check(lib().pb_state_status(self.h, _stream(stream)))
+
+    def shard(self, rank, world, uid):
+        """row-shard this state's decode over `world` ranks (collective);
+        uid: the 128-byte id from nccl_unique_id() on rank 0"""
+        b = C.create_string_buffer(bytes(uid), len(uid))
+        check(lib().pb_state_shard(self.h, int(rank), int(world), b))
 
     def kernels_per_token(self):
         r = lib().pb_decode_kernels_per_token(self.h)

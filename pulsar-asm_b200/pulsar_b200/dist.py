@@ -1,9 +1,11 @@
-"""Multi-GPU plumbing for the benchmark: one process per GPU, torch.distributed
-for rendezvous and the max-over-ranks timing reduction only.
+"""Multi-GPU plumbing: one process per GPU, torch.distributed for rendezvous,
+the max-over-ranks timing reduction, and the hand-over of the NCCL id that
+row-sharded decode states share.
 
-The decode path shards by sequence (independent replicas of the model, each
-rank decoding its own sequences), so there is no data-path collective; ranks
-meet only in barriers and in the final MAX reduction of their device timings.
+The default decode shards by sequence (independent replicas of the model,
+each rank decoding its own sequences): no data-path collective. A row-sharded
+state (State.shard) splits every GEMV's rows over the ranks and all-gathers
+each output through the library's own NCCL communicator.
 """
 import os
 
@@ -64,3 +66,15 @@ def finish():
     import torch.distributed as dist
     if dist.is_initialized():
         dist.destroy_process_group()
+
+
+def share_from_rank0(make):
+    """the value make() returns on rank 0, on every rank (picklable)"""
+    import torch.distributed as dist
+    rank, world, _ = env_rank()
+    if world <= 1 or not dist.is_initialized():
+        return make()
+    box = [make() if rank == 0 else None]
+    dist.broadcast_object_list(box, src=0)
+    return box[0]
+

@@ -66,3 +66,43 @@ def test_failed_rank_is_an_error_not_a_hang():
     status = {o[0]: o[1] for o in out}
     assert status[1] == "err"
     assert status[0] == "err"      # the survivor's collective times out or aborts
+
+
+def _uid_worker(rank, world, port, q):
+    import sys
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    sys.path.insert(0, os.path.join(root, "pulsar-asm_b200"))
+    os.environ.update(RANK=str(rank), WORLD_SIZE=str(world), LOCAL_RANK=str(rank),
+                      MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    from pulsar_b200 import dist
+    try:
+        dist.init(backend="gloo", timeout_s=20)
+        calls = []
+
+        def make():
+            calls.append(rank)
+            return bytes([7, rank, 9]) * 42 + b"xy"
+        v = dist.share_from_rank0(make)
+        q.put((rank, v, calls))
+    except Exception as e:  # noqa: BLE001
+        q.put((rank, repr(e), None))
+    finally:
+        try:
+            dist.finish()
+        except Exception:
+            pass
+
+
+def test_share_from_rank0_gloo():
+    """the row-sharded state's NCCL id: made once on rank 0, the same bytes on every rank"""
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    ps = [ctx.Process(target=_uid_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in ps:
+        p.start()
+    out = sorted(q.get(timeout=120) for _ in range(2))
+    for p in ps:
+        p.join(timeout=60)
+    want = bytes([7, 0, 9]) * 42 + b"xy"
+    assert out[0] == (0, want, [0]) and out[1] == (1, want, [])
