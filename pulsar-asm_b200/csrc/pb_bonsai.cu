@@ -77,27 +77,33 @@ struct BsNormArgs {
 __global__ void __launch_bounds__(256) k_bs_norm(BsNormArgs a) {
   extern __shared__ __align__(16) float sv[];   // [H]
   __shared__ double wsum[8];
+  __shared__ int wmin[8];
   __shared__ float s_sc;
   __shared__ Q8kScratch q8s;
   pb_grid_wait();
   pb_grid_launch_dependents();
   const int t = threadIdx.x, H = a.H;
   double ps = 0.0;
+  int me = 0x7fffffff;
   for (int i = t; i < H; i += 256) {
     float v = a.xin[i];
     if (a.r) v = __fadd_rn(v, a.r[i]);
     sv[i] = v;
     const double d = (double)v;
     ps = __fma_rn(d, d, ps);
+    me = min(me, bs_sq_lowbit(v));
   }
   ps = warp_sum_d(ps);
-  if ((t & 31) == 0) wsum[t >> 5] = ps;
+  me = __reduce_min_sync(0xffffffffu, me);
+  if ((t & 31) == 0) { wsum[t >> 5] = ps; wmin[t >> 5] = me; }
   __syncthreads();
   if (t == 0) {
     double P = 0.0;
-    for (int w = 0; w < 8; w++) P = __dadd_rn(P, wsum[w]);
+    int m = 0x7fffffff;
+    for (int w = 0; w < 8; w++) { P = __dadd_rn(P, wsum[w]); m = min(m, wmin[w]); }
     bool ok;
     float mean = bs_mean_sq(P, H, ok);
+    if (!ok && bs_sum_exact(P, m)) { ok = true; mean = __double2float_rn(bs_div_n(P, H)); }
     if (!ok) {
       mean = bs_mean_sq_serial(sv, H);
       if (blockIdx.x == 0) atomicAdd(&a.ctl->fallbacks, 1);
@@ -165,11 +171,19 @@ __global__ void __launch_bounds__(32) k_bs_attn_pre(BsPreArgs a) {
     return;
   }
   double ps = 0.0;
+  int me = 0x7fffffff;
 #pragma unroll
-  for (int k = 0; k < 4; k++) { const double d = (double)x[k]; ps = __fma_rn(d, d, ps); sx[l + 32 * k] = x[k]; }
+  for (int k = 0; k < 4; k++) {
+    const double d = (double)x[k];
+    ps = __fma_rn(d, d, ps);
+    sx[l + 32 * k] = x[k];
+    me = min(me, bs_sq_lowbit(x[k]));
+  }
   ps = warp_sum_d(ps);
+  me = __reduce_min_sync(0xffffffffu, me);
   bool ok;
   float mean = bs_mean_sq(ps, BS_HD, ok);
+  if (!ok && bs_sum_exact(ps, me)) { ok = true; mean = __double2float_rn(bs_div_n(ps, BS_HD)); }
   if (!ok) {   // warp-uniform
     __syncwarp();
     if (l == 0) {

@@ -26,6 +26,24 @@ PB_DEV float bs_mean_sq(double P, int n, bool& ok) {
   ok = lo == hi;
   return lo;
 }
+// The other certified case: every square x^2 = k^2 2^(2e) (k odd) is a
+// multiple of 2^m, m = min 2e, and P < 2^(m+53). Every partial sum of these
+// non-negative terms, in any order, is then a multiple of 2^m below 2^(m+53),
+// hence exact: the serial sum equals P (inputs from fp16 data often sum this
+// way and land exactly on a float rounding midpoint, which the interval test
+// cannot separate). P >= 2^(m+53) exactly when the exact sum is, rounding
+// being monotone and 2^(m+53) a double.
+PB_DEV int bs_sq_lowbit(float x) {   // 2e for x != 0, INT_MAX for 0
+  const unsigned u = __float_as_uint(x) & 0x7fffffffu;
+  if (u == 0) return 0x7fffffff;
+  const unsigned E = u >> 23, M = u & 0x7fffffu;
+  const int e = E ? (int)E - 150 + (__ffs((int)(M | 0x800000u)) - 1) : -149 + (__ffs((int)M) - 1);
+  return 2 * e;
+}
+PB_DEV bool bs_sum_exact(double P, int m) {
+  if (m == 0x7fffffff) return true;   // every term zero
+  return P < __longlong_as_double((long long)(m + 53 + 1023) << 52);   // 2^(m+53), m in [-298, 208]
+}
 PB_DEV float bs_mean_sq_serial(const float* v, int n) {
   double s = 0.0;
   for (int i = 0; i < n; i++) { const double d = (double)v[i]; s = __fma_rn(d, d, s); }

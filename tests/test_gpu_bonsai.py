@@ -95,10 +95,13 @@ def test_bonsai_greedy_and_caller_row(oracle, pb, cuda):
         want.append(tok)
     assert ids.cpu().tolist() == want
     # the caller supplies the input row (pq1_token_fused): here a row whose
-    # mean square sits exactly on a float rounding midpoint, so the device's
-    # parallel sum cannot certify it and takes the serial chain
+    # serial double sum of squares stops exactly on a float rounding midpoint
+    # (2^40 + 2^16; the 2^-60 terms vanish below its ulp) while the exact sum
+    # lies just above it, so neither certificate holds and the device runs the
+    # serial chain
     s2, om2 = m.new_state(max_ctx), oracle.BsModel(c, synth.make_bonsai_weights(c, seed=33), max_ctx)
-    x = np.full(c["hidden"], 1.0 + 2.0 ** -12, np.float32)
+    x = np.full(c["hidden"], 2.0 ** -30, np.float32)
+    x[0], x[1] = 2.0 ** 20, 2.0 ** 8
     lg = torch.empty(c["vocab"], dtype=torch.float32, device="cuda")
     before = s2.fallbacks()
     got = s2.decode(0, 0, x=torch.from_numpy(x).cuda(), logits=lg)
