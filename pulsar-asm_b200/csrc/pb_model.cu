@@ -1347,12 +1347,19 @@ extern "C" int pb_state_create(pb_model* m, int max_ctx, pb_state** out) {
 
 extern "C" int pb_state_destroy(pb_state* s) {
   if (!s) return PB_OK;
-  if (s->comm) nccl().comm_destroy(s->comm);
+  // the graph holds the communicator's captured collectives: release it first,
+  // or the communicator's destruction waits for it forever
+  if (s->exec) cudaGraphExecDestroy(s->exec);
+  if (s->graph) cudaGraphDestroy(s->graph);
+  s->exec = nullptr;
+  s->graph = nullptr;
+  if (s->comm) {
+    cudaDeviceSynchronize();
+    nccl().comm_destroy(s->comm);
+  }
   if (s->d_phases) cudaFree(s->d_phases);
   if (s->d_sched) cudaFree(s->d_sched);
   if (s->d_trace) cudaFree(s->d_trace);
-  if (s->exec) cudaGraphExecDestroy(s->exec);
-  if (s->graph) cudaGraphDestroy(s->graph);
   if (s->graph_stream) cudaStreamDestroy(s->graph_stream);
   cudaFreeHost(s->h_ctl);
   cudaFree(s->mem);

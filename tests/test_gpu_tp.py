@@ -19,10 +19,32 @@ def _free_port():
     return p
 
 
-def test_row_sharded_decode_two_gpus(cuda, tmp_path):
+def _expected(oracle, path):
+    """the oracle's logits and ids for the workers' token sequence (same seeds
+    as tp_worker.py), computed here once with every host thread"""
+    import numpy as np
+    from pulsar_b200 import synth
+    c = dict(synth.LFM3_TINY)
+    w = synth.make_weights(c, seed=91)
+    om = oracle.Model(synth.oracle_cfg(c, 64), w)
+    toks = np.random.default_rng(5).integers(0, c["vocab"], 24)
+    lgs, ids = [], []
+    for pos, tok in enumerate(toks):
+        i, lg, _ = om.decode(int(tok), pos, want_logits=True)
+        lgs.append(lg)
+        ids.append(i)
+    greedy, t = [], int(toks[-1])
+    for i in range(8):
+        t, _, _ = om.decode(t, len(toks) + i)
+        greedy.append(t)
+    np.savez(path, toks=toks, logits=np.stack(lgs), ids=np.array(ids), greedy=np.array(greedy))
+
+
+def test_row_sharded_decode_two_gpus(cuda, oracle, tmp_path):
     torch = cuda
     if torch.cuda.device_count() < 2:
         pytest.skip("row-sharded decode needs two GPUs")
+    _expected(oracle, str(tmp_path / "expected.npz"))
     here = os.path.dirname(os.path.abspath(__file__))
     env = dict(os.environ, PB_TP_DIR=str(tmp_path), NCCL_NVLS_ENABLE="0")
     cmd = ["timeout", "-k", "30", "240", sys.executable, "-m", "torch.distributed.run", "--nnodes=1",
