@@ -161,6 +161,15 @@ def _stream(stream=None):
     return C.c_void_p(s.cuda_stream)
 
 
+def _produced(t):
+    """A CUDA tensor handed to an upload is read on the upload's stream, which
+    need not be the stream that wrote it: wait until the tensor's producer (the
+    current stream of its device) has finished. Uploads are one-time setup."""
+    import torch
+    if isinstance(t, torch.Tensor) and t.is_cuda:
+        torch.cuda.current_stream(t.device).synchronize()
+
+
 class Q8Tensor:
     """A packed Q8 weight matrix on the device (int8 codes + per-32 scales)."""
 
@@ -175,6 +184,8 @@ class Q8Tensor:
         if isinstance(codes, torch.Tensor):
             sdt = PB_DT_F32 if scales.dtype == torch.float32 else PB_DT_F16
             on_dev = 1 if codes.is_cuda else 0
+            _produced(codes)
+            _produced(scales)
             cp, sp = C.c_void_p(codes.data_ptr()), C.c_void_p(scales.data_ptr())
         else:
             import numpy as np
@@ -237,6 +248,7 @@ class Q1Tensor:
         import torch
         if isinstance(blocks, torch.Tensor):
             on_dev = 1 if blocks.is_cuda else 0
+            _produced(blocks)
             bp = C.c_void_p(blocks.data_ptr())
         else:
             import numpy as np
@@ -448,6 +460,7 @@ class Bonsai:
         import numpy as np
         st = st if st is not None else _stream()
         if hasattr(blocks, "is_cuda") and blocks.is_cuda:
+            _produced(blocks)
             check(lib().pb_bonsai_set_q1(self.h, layer, slot, C.c_void_p(blocks.data_ptr()), 1, st))
             return
         b = np.ascontiguousarray(blocks, dtype=np.uint8)
