@@ -43,6 +43,8 @@ def parse():
     ap.add_argument("--no-kernels", action="store_true", help="skip the per-kernel GB/s suite")
     ap.add_argument("--no-tp", action="store_true", help="skip the row-sharded decode at N > 1")
     ap.add_argument("--blob", default=os.environ.get("PB_BENCH_BLOB", "/tmp/pb_cfg1.lfm3q8"))
+    ap.add_argument("--phase-trace", action="store_true",
+                    help="print the persistent decode kernel's per-phase time breakdown (one GPU) and exit")
     ap.add_argument("--layers", type=int, default=0,
                     help="profiling only: a shallower model of the same shapes (0 = the 24-layer cfg1)")
     return ap.parse_args()
@@ -416,6 +418,55 @@ def bonsai_setup(torch, pb, stream, max_ctx, pos0, n_layers=None):
     return c, m, s
 
 
+def phase_trace(torch, model, prompt, stream, ctx):
+    """Per-phase breakdown of one decode token (token 0 of a 4-token launch of
+    the persistent kernel, after two warm launches) from the kernel's own
+    globaltimer marks (PB_DECODE_TRACE): per CTA and phase the entry, grid
+    barrier, prologue end, work end and arrival times, plus warp 0's data
+    waits, slot releases (with refill issues) and chain arithmetic inside the
+    GEMV stage loops. Times are means over the CTAs, in microseconds."""
+    import numpy as np
+    os.environ["PB_DECODE_TRACE"] = "1"
+    st = model.new_state(ctx + 64)
+    ids = torch.empty(4, dtype=torch.int32, device="cuda")
+    with torch.cuda.stream(stream):
+        st.decode_prompt(prompt, 0, stream=stream)
+        for _ in range(3):
+            st.decode_greedy(int(prompt[-1].item()), ctx, 4, ids, stream=stream)
+        stream.synchronize()
+    tr = st.debug_tensor(5, torch.int64).cpu().numpy().astype(np.int64)
+    st.destroy()
+    del os.environ["PB_DECODE_TRACE"]
+    G = torch.cuda.get_device_properties(0).multi_processor_count
+    nph = tr.size // (G * 8)
+    tr = tr.reshape(G, nph, 8).astype(np.float64) / 1e3
+    gemv = (tr[:, :, 2] != 0).any(axis=0)
+    mean = lambda a: a.mean(axis=0)
+    bar = mean(tr[:, :, 1] - tr[:, :, 0])
+    pro = mean(tr[:, :, 2] - tr[:, :, 1])
+    work_g = mean(tr[:, :, 3] - tr[:, :, 2])
+    work_a = mean(tr[:, :, 3] - tr[:, :, 1])
+    arr = mean(tr[:, :, 4] - tr[:, :, 3])
+    other = ~gemv
+    other[-1] = False          # the last phase is the greedy argmax
+    out = {"phases": int(nph), "gemv_phases": int(gemv.sum()), "attention_phases": int(other.sum()),
+           "token_us": float(tr[:, -1, 4].max() - tr[:, 0, 0].min()),
+           "gemv_prologue_with_grid_barrier_us": float(pro[gemv].sum()),
+           "gemv_work_us": float(work_g[gemv].sum()),
+           "attention_barrier_us": float(bar[other].sum()), "attention_work_us": float(work_a[other].sum()),
+           "arrive_us": float(arr.sum()),
+           "warp0_data_wait_us": float(mean(tr[:, :, 6])[gemv].sum()),
+           "warp0_release_issue_us": float(mean(tr[:, :, 5])[gemv].sum()),
+           "warp0_chains_trees_us": float(mean(tr[:, :, 7])[gemv].sum()),
+           "first_phases": [{"phase": p, "kind": "gemv" if gemv[p] else "attention",
+                             "prologue_us": round(float(pro[p] if gemv[p] else bar[p]), 2),
+                             "work_us": round(float(work_g[p] if gemv[p] else work_a[p]), 2),
+                             "arrive_us": round(float(arr[p]), 2),
+                             "span_us": round(float(tr[:, p, 4].max() - tr[:, p, 0].min()), 2)}
+                            for p in range(min(nph, 12))]}
+    return out
+
+
 def tp_bench(torch, pb, model, prompt, stream, rank, world, steps=32, warmup=3):
     """one sequence decoded with every GEMV's rows split over the ranks and
     each output all-gathered over NVLink (pb_state_shard); the same prompt as
@@ -501,6 +552,13 @@ def main():
     stream = torch.cuda.Stream()
     rng = torch.Generator().manual_seed(SEED + rank)
     prompt = torch.randint(0, c["vocab"], (args.ctx,), generator=rng, dtype=torch.int32).cuda()
+    if args.phase_trace:
+        if rank == 0:
+            print(json.dumps({"phase_trace": phase_trace(torch, model, prompt, stream, args.ctx),
+                              "config": {"workload": "cfg1", "ctx": args.ctx}}))
+        st.destroy()
+        dist.finish()
+        return
     with torch.cuda.stream(stream):
         # prefill the KV cache and conv rings: `ctx` teacher-forced tokens
         st.decode_prompt(prompt, 0, stream=stream)
