@@ -291,8 +291,9 @@ PB_DEV float bs_max_comb(float m, float s) { return s > m ? s : m; }
 // chain's array w (bit 31 = new maximum: w is ms and vs = 1; else w is vs and
 // ms = 1) and marks every 16-position group that holds a new maximum.
 //
-// The chains (two warps; thread j owns dimensions 2j and 2j+1: two
-// independent accumulator chains) read V as f16 pairs from a ring of BS_PV_NST tiles,
+// The chains (four warps, one per SM sub-partition, so that the chain's f16
+// rounding conversions spread over all four; thread j owns dimension j) read
+// V rows from a ring of BS_PV_NST tiles,
 // each tile (contiguous rows of the kv head) one bulk copy completing on its
 // slot's mbarrier (bounded waits: a copy that never lands sets the control
 // block's error and ends the CTA). A 16-position group with no new maximum
@@ -304,39 +305,38 @@ PB_DEV int bs_skew(int p) { return p + (p >> 5); }
 __host__ __device__ inline int bs_skew_len(int mc) { return (mc + mc / 32 + 3) & ~3; }
 // group flags per head, padded to whole words (the chain reads a tile's four at once)
 __host__ __device__ inline int bs_nm_len(int mc) { return (mc / 16 + 3) & ~3; }
-// one tile of the chain for dims (2j, 2j+1): vb[r * 64] is row r's pair, w
-// the tile's encoded weights, nmt its 4 group flags, n <= 64 valid rows. Each
+// one tile of the chain for dim j: vb[r * 128] is row r's value, w the
+// tile's encoded weights, nmt its 4 group flags, n <= 64 valid rows. Each
 // group's operands are loaded one group ahead; a full group with no new
 // maximum takes the branch-free step, any other group the general one.
-PB_DEV void bs_chain_tile(const uint32_t* __restrict__ vb, const uint32_t* __restrict__ w,
-                          const unsigned char* __restrict__ nmt, int n, float& accA, float& accB, float& Ssum) {
+PB_DEV void bs_chain_tile(const uint16_t* __restrict__ vb, const uint32_t* __restrict__ w,
+                          const unsigned char* __restrict__ nmt, int n, float& acc, float& Ssum) {
   uint4 wn[4];
-  uint32_t vn[16];
+  uint16_t vn[16];
 #pragma unroll
   for (int k = 0; k < 4; k++) wn[k] = reinterpret_cast<const uint4*>(w)[k];
 #pragma unroll
-  for (int k = 0; k < 16; k++) vn[k] = vb[k * 64];
+  for (int k = 0; k < 16; k++) vn[k] = vb[k * BS_HD];
 #pragma unroll
   for (int gi = 0; gi < BS_PV_TT / 16; gi++) {
     const int g0 = gi * 16;
     if (g0 >= n) break;
     const uint32_t wc[16] = {wn[0].x, wn[0].y, wn[0].z, wn[0].w, wn[1].x, wn[1].y, wn[1].z, wn[1].w,
                              wn[2].x, wn[2].y, wn[2].z, wn[2].w, wn[3].x, wn[3].y, wn[3].z, wn[3].w};
-    uint32_t vc[16];
+    uint16_t vc[16];
 #pragma unroll
     for (int k = 0; k < 16; k++) vc[k] = vn[k];
     if (gi + 1 < BS_PV_TT / 16) {   // rows past n are stale shared memory, never used
 #pragma unroll
       for (int k = 0; k < 4; k++) wn[k] = reinterpret_cast<const uint4*>(w + g0 + 16)[k];
 #pragma unroll
-      for (int k = 0; k < 16; k++) vn[k] = vb[(g0 + 16 + k) * 64];
+      for (int k = 0; k < 16; k++) vn[k] = vb[(g0 + 16 + k) * BS_HD];
     }
     if (g0 + 16 <= n && !nmt[gi]) {
 #pragma unroll
       for (int k = 0; k < 16; k++) {
         const float wf = __uint_as_float(wc[k]);
-        accA = bs_r16(__fmaf_rn(pb_h2f((unsigned short)(vc[k] & 0xffffu)), wf, accA));
-        accB = bs_r16(__fmaf_rn(pb_h2f((unsigned short)(vc[k] >> 16)), wf, accB));
+        acc = bs_r16(__fmaf_rn(pb_h2f(vc[k]), wf, acc));
         Ssum = __fadd_rn(Ssum, wf);
       }
     } else {
@@ -345,9 +345,8 @@ PB_DEV void bs_chain_tile(const uint32_t* __restrict__ vb, const uint32_t* __res
         if (g0 + k < n) {
           const bool nmax = (wc[k] >> 31) != 0;
           const float wk = __uint_as_float(wc[k] & 0x7fffffffu), ms = nmax ? wk : 1.0f, vs = nmax ? 1.0f : wk;
-          if (ms != 1.0f) { accA = bs_r16(__fmul_rn(accA, ms)); accB = bs_r16(__fmul_rn(accB, ms)); }
-          accA = bs_r16(__fmaf_rn(pb_h2f((unsigned short)(vc[k] & 0xffffu)), vs, accA));
-          accB = bs_r16(__fmaf_rn(pb_h2f((unsigned short)(vc[k] >> 16)), vs, accB));
+          if (ms != 1.0f) acc = bs_r16(__fmul_rn(acc, ms));
+          acc = bs_r16(__fmaf_rn(pb_h2f(vc[k]), vs, acc));
           Ssum = __fmaf_rn(Ssum, ms, vs);
         }
       }
@@ -460,20 +459,20 @@ __global__ void __launch_bounds__(256) k_bs_fa_pv(BsPvArgs a) {
     }
     __syncthreads();
   }
-  if (w >= 2) return;   // the chains are two warps; the others are done
-  // ---- the chains (thread j < 64 owns dims 2j, 2j+1), positions in order;
-  // named barrier 1 over the 64 chain threads
+  if (w >= 4) return;   // the chains are four warps; the others are done
+  // ---- the chains (thread j < 128 owns dim j), positions in order; named
+  // barrier 1 over the 128 chain threads
   const int j = tid;
-  float accA = 0.0f, accB = 0.0f, Ssum = 0.0f;
+  float acc = 0.0f, Ssum = 0.0f;
   int failed = -1;   // the tile whose copy never landed (the CTA gives up)
   for (int tile = 0; tile < ntile; tile++) {
     if (!bs_mbar_wait(&full[tile % BS_PV_NST], (unsigned)(tile / BS_PV_NST) & 1u)) s_fail = 1;
-    asm volatile("bar.sync 1, 64;" ::: "memory");
+    asm volatile("bar.sync 1, 128;" ::: "memory");
     if (s_fail) { failed = tile; break; }   // read after the barrier: the same decision in every thread
     const int r0 = tile * BS_PV_TT;
-    bs_chain_tile(reinterpret_cast<const uint32_t*>(vt + (size_t)(tile % BS_PV_NST) * BS_PV_TT * BS_HD) + j,
-                  sw + r0, nm + (r0 >> 4), min(BS_PV_TT, T - r0), accA, accB, Ssum);
-    asm volatile("bar.sync 1, 64;" ::: "memory");   // every chain thread has left the slot: refill it
+    bs_chain_tile(vt + (size_t)(tile % BS_PV_NST) * BS_PV_TT * BS_HD + j,
+                  sw + r0, nm + (r0 >> 4), min(BS_PV_TT, T - r0), acc, Ssum);
+    asm volatile("bar.sync 1, 128;" ::: "memory");   // every chain thread has left the slot: refill it
     if (tid == 0) issue(tile + BS_PV_NST);
   }
   if (failed >= 0) {   // wait (bounded) for the copies still in flight, then report
@@ -485,22 +484,22 @@ __global__ void __launch_bounds__(256) k_bs_fa_pv(BsPvArgs a) {
     return;
   }
   if (j == 0) s_S = Ssum;
-  asm volatile("bar.sync 1, 64;" ::: "memory");
+  asm volatile("bar.sync 1, 128;" ::: "memory");
   const float si = s_S == 0.0f ? 0.0f : __fdiv_rn(1.0f, s_S);
-  *reinterpret_cast<float2*>(a.atto + (size_t)h * BS_HD + 2 * j) = make_float2(__fmul_rn(accA, si), __fmul_rn(accB, si));
+  a.atto[(size_t)h * BS_HD + j] = __fmul_rn(acc, si);
   // the second head of each pair to finish quantises the pair's 256 outputs
   // (one Q8_K block); the first one's stores are visible through the fence
   __threadfence();
-  asm volatile("bar.sync 1, 64;" ::: "memory");
+  asm volatile("bar.sync 1, 128;" ::: "memory");
   if (tid == 0) s_last = atomicAdd(&a.ctl->pv_pair[h >> 1], 1u) == 1u;
-  asm volatile("bar.sync 1, 64;" ::: "memory");
+  asm volatile("bar.sync 1, 128;" ::: "memory");
   if (!s_last) return;
   __threadfence();
   float* y = reinterpret_cast<float*>(vt);   // [256] staging
   const float* src = a.atto + (size_t)(h & ~1) * BS_HD;
 #pragma unroll
-  for (int k = 0; k < 4; k++) y[tid + 64 * k] = __ldcg(src + tid + 64 * k);
-  asm volatile("bar.sync 1, 64;" ::: "memory");
+  for (int k = 0; k < 2; k++) y[tid + 128 * k] = __ldcg(src + tid + 128 * k);
+  asm volatile("bar.sync 1, 128;" ::: "memory");
   if (w == 0) pb_q8k_block256_warp(y, a.xq + (size_t)(h >> 1) * 292);
   if (tid == 0) a.ctl->pv_pair[h >> 1] = 0u;
 }
