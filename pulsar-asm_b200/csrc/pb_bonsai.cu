@@ -85,6 +85,7 @@ __global__ void __launch_bounds__(256) k_bs_norm(BsNormArgs a) {
   const int t = threadIdx.x, H = a.H;
   double ps = 0.0;
   int me = 0x7fffffff;
+#pragma unroll 8
   for (int i = t; i < H; i += 256) {
     float v = a.xin[i];
     if (a.r) v = __fadd_rn(v, a.r[i]);

@@ -33,12 +33,14 @@ PB_DEV float bs_mean_sq(double P, int n, bool& ok) {
 // way and land exactly on a float rounding midpoint, which the interval test
 // cannot separate). P >= 2^(m+53) exactly when the exact sum is, rounding
 // being monotone and 2^(m+53) a double.
-PB_DEV int bs_sq_lowbit(float x) {   // 2e for x != 0, INT_MAX for 0
+// 2e for x != 0, INT_MAX for 0; branch-free (selects only), so that a load
+// loop calling it keeps all its loads in flight
+PB_DEV int bs_sq_lowbit(float x) {
   const unsigned u = __float_as_uint(x) & 0x7fffffffu;
-  if (u == 0) return 0x7fffffff;
   const unsigned E = u >> 23, M = u & 0x7fffffu;
-  const int e = E ? (int)E - 150 + (__ffs((int)(M | 0x800000u)) - 1) : -149 + (__ffs((int)M) - 1);
-  return 2 * e;
+  const unsigned mm = E ? (M | 0x800000u) : M;
+  const int e = (E ? (int)E - 150 : -149) + (__ffs((int)mm) - 1);
+  return u == 0 ? 0x7fffffff : 2 * e;
 }
 PB_DEV bool bs_sum_exact(double P, int m) {
   if (m == 0x7fffffff) return true;   // every term zero
