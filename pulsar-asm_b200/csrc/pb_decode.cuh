@@ -96,8 +96,10 @@ PB_DEV unsigned long long gtime() {
   return t;
 }
 // trace marks: 0 phase entered, 1 grid barrier passed, 2 prologue done, 3 work done, 4 arrived;
-// GEMV phases add warp 0's stage-loop totals: 5 slot releases (with the refill
-// issues), 6 waits for stage data, 7 chain and tree arithmetic
+// GEMV phases add warp 0's stage-loop totals: 6 waits for stage data and, in a
+// build with PB_TRACE_STAGE_LOOP defined (the two extra timers per stage cost
+// about 4 % of decode throughput even with tracing off), 5 slot releases with
+// their refill issues and 7 chain and tree arithmetic
 PB_DEV void tmark(const DecodeArgs& d, int tok, int p, int k) {
   if (d.trace && tok == 0 && threadIdx.x == 0) d.trace[((size_t)blockIdx.x * d.nphase + p) * 8 + k] = gtime();
 }
@@ -317,20 +319,26 @@ __device__ __forceinline__ unsigned gemv_phase(const DecodeArgs& d, const Phase&
                  "r"(q[1][2].z), "r"(q[1][2].w), "r"(q[1][3].x), "r"(q[1][3].y), "r"(q[1][3].z),
                  "r"(q[1][3].w), "f"(slo[1]), "f"(shi[1]));
     __syncwarp();
+#ifdef PB_TRACE_STAGE_LOOP
     const unsigned long long tr0 = (tmark2 && threadIdx.x == 0) ? gtime() : 0;
+#endif
     if (lane == 0 && slot_release(slot)) {
       issue_ctx()->cnt[slot] = 0;
       if (it + ds < total) issue_stage<F32S>(kn, slot, it + ds, ring, full);
     }
+#ifdef PB_TRACE_STAGE_LOOP
     const unsigned long long tr1 = (tmark2 && threadIdx.x == 0) ? gtime() : 0;
+#endif
     float v[2];
 #pragma unroll
     for (int u = 0; u < 2; u++) v[u] = pb_warp_tree(leaf2(q[u], slo[u], shi[u], xr));
+#ifdef PB_TRACE_STAGE_LOOP
     if (tmark2 && threadIdx.x == 0) {
       asm volatile("" ::"f"(v[0]), "f"(v[1]));
       tmark2[3] += tr1 - tr0;            // slot 5: release (+ refill issue) of warp 0
       tmark2[5] += gtime() - tr1;        // slot 7: chains and trees of warp 0
     }
+#endif
     if (lane == 0) {
       const int lr = r - r0 + g * 2;
       rowv[lr * nch + c] = v[0];
