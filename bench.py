@@ -455,9 +455,9 @@ def phase_trace(torch, model, prompt, stream, ctx):
            "gemv_work_us": float(work_g[gemv].sum()),
            "attention_barrier_us": float(bar[other].sum()), "attention_work_us": float(work_a[other].sum()),
            "arrive_us": float(arr.sum()),
-           "warp0_data_wait_us": float(mean(tr[:, :, 6])[gemv].sum()),
-           # slots 5 and 7 are written only by a library built with
+           # slots 5 to 7 are written only by a library built with
            # EXTRA=-DPB_TRACE_STAGE_LOOP (null otherwise)
+           "warp0_data_wait_us": float(mean(tr[:, :, 6])[gemv].sum()) if tr[:, :, 6].any() else None,
            "warp0_release_issue_us": float(mean(tr[:, :, 5])[gemv].sum()) if tr[:, :, 5].any() else None,
            "warp0_chains_trees_us": float(mean(tr[:, :, 7])[gemv].sum()) if tr[:, :, 7].any() else None,
            "first_phases": [{"phase": p, "kind": "gemv" if gemv[p] else "attention",

@@ -96,10 +96,10 @@ PB_DEV unsigned long long gtime() {
   return t;
 }
 // trace marks: 0 phase entered, 1 grid barrier passed, 2 prologue done, 3 work done, 4 arrived;
-// GEMV phases add warp 0's stage-loop totals: 6 waits for stage data and, in a
-// build with PB_TRACE_STAGE_LOOP defined (the two extra timers per stage cost
-// about 4 % of decode throughput even with tracing off), 5 slot releases with
-// their refill issues and 7 chain and tree arithmetic
+// in a build with PB_TRACE_STAGE_LOOP defined, GEMV phases add warp 0's
+// stage-loop totals: 5 slot releases with their refill issues, 6 waits for
+// stage data, 7 chain and tree arithmetic (these timers cost about 4.5 % of
+// decode throughput even with tracing off, so default builds leave them out)
 PB_DEV void tmark(const DecodeArgs& d, int tok, int p, int k) {
   if (d.trace && tok == 0 && threadIdx.x == 0) d.trace[((size_t)blockIdx.x * d.nphase + p) * 8 + k] = gtime();
 }
@@ -275,13 +275,17 @@ __device__ __forceinline__ unsigned gemv_phase(const DecodeArgs& d, const Phase&
   unsigned kn = it % spt + ds;
   while (kn >= spt) kn -= spt;
   for (int r = r0; r < r1; r += RB) {
+#ifdef PB_TRACE_STAGE_LOOP
     const unsigned long long tw = (tmark2 && threadIdx.x == 0) ? gtime() : 0;
+#endif
     if (!mbar_wait(&full[slot], par, abort_flag)) {
       *abort_flag = 1;
       atomicCAS(d.err, 0, 2);
       break;
     }
+#ifdef PB_TRACE_STAGE_LOOP
     if (tmark2 && threadIdx.x == 0) tmark2[4] += gtime() - tw;   // slot 6 of the phase: data waits
+#endif
     const unsigned char* st = ring + (size_t)slot * Gm::STAGE;
     uint4 q[2][4];
     float slo[2], shi[2];
