@@ -91,13 +91,14 @@ PB_DEV int ldi(const int* p) { return SYNC ? __ldcg(p) : *p; }
 constexpr unsigned PB_WAIT_LIMIT = 1u << 24;   // polls before a wait gives up
 
 // arrival counter of the persistent kernel's grid barrier: wait until `target`
-// CTAs have arrived (bounded)
+// CTAs have arrived (bounded: PB_WAIT_LIMIT polls, a few seconds). One thread
+// per CTA polls with acquire loads and no sleep between them; a sleep, or
+// relaxed polls with a fence after the last, measured slower.
 PB_DEV bool grid_wait(const unsigned* bar, unsigned target) {
   for (unsigned i = 0; i < PB_WAIT_LIMIT; i++) {
     unsigned v;
     asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(bar) : "memory");
     if (v >= target) return true;
-    if (i > 16) __nanosleep(20);
   }
   return false;
 }
