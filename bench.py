@@ -70,24 +70,33 @@ def ncu_traffic():
 
 
 class Clocks:
-    """nvidia-smi sampling during the timed region (SM clock and throttle reasons)."""
+    """nvidia-smi sampling during the timed region (SM clock and throttle
+    reasons). The sampler is started and seen to print before the region
+    begins; every sample carries nvidia-smi's own timestamp, and only samples
+    taken between the region's start and end count. The period (25 ms) leaves
+    several samples in the bench's shortest timed region."""
 
-    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+    Q = ("timestamp,index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
          "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
          "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
 
-    def __init__(self, index):
-        self.index, self.p, self.lines = index, None, []
+    def __init__(self, index, period_ms=25):
+        self.index, self.period, self.p, self.lines = index, period_ms, None, []
+        self.t0 = self.t1 = None
 
     def __enter__(self):
         try:
             self.p = subprocess.Popen(["nvidia-smi", "-i", str(self.index), "--query-gpu=" + self.Q,
-                                       "--format=csv,noheader,nounits", "-lms", "200"],
+                                       "--format=csv,noheader,nounits", "-lms", str(self.period)],
                                       stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
             self.t = threading.Thread(target=self._read, daemon=True)
             self.t.start()
+            t = time.time()
+            while not self.lines and time.time() - t < 10:
+                time.sleep(0.005)
         except Exception:
             self.p = None
+        self.t0 = time.time()
         return self
 
     def _read(self):
@@ -95,26 +104,40 @@ class Clocks:
             self.lines.append(line.strip())
 
     def __exit__(self, *a):
+        self.t1 = time.time()
         if self.p:
+            time.sleep(2 * self.period / 1000.0)   # samples of the region's last instants
             self.p.terminate()
             try:
                 self.p.wait(timeout=5)
             except Exception:
                 self.p.kill()
+            self.t.join(timeout=2)
+
+    @staticmethod
+    def _when(stamp):
+        import datetime
+        try:
+            return datetime.datetime.strptime(stamp, "%Y/%m/%d %H:%M:%S.%f").timestamp()
+        except ValueError:
+            return None
 
     def summary(self):
         sm, mx, reasons = [], None, set()
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for ln in self.lines:
+        for ln in list(self.lines):
             f = [x.strip() for x in ln.split(",")]
-            if len(f) < 9:
+            if len(f) < 10:
+                continue
+            w = self._when(f[0])
+            if w is None or self.t0 is None or not (self.t0 <= w <= self.t1):
                 continue
             try:
-                sm.append(float(f[1]))
-                mx = float(f[2])
+                sm.append(float(f[2]))
+                mx = float(f[3])
             except ValueError:
                 continue
-            for n, v in zip(names, f[5:9]):
+            for n, v in zip(names, f[6:10]):
                 if v.lower() == "active":
                     reasons.add(n)
         return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx,
