@@ -321,7 +321,8 @@ struct pb_state {
   bf16_t* h_w2 = nullptr;
   float* logits = nullptr;
   Ctl* ctl = nullptr;
-  Ctl* h_ctl = nullptr;           // pinned host mirror for token/pos uploads
+  Ctl* h_ctl = nullptr;           // pinned host mirror for token/pos uploads, then one
+                                  // pinned int for the decode kernel's error word
   char* mem = nullptr;
   size_t mem_bytes = 0;
   // persistent decode kernel: phase table, arrival counter, error word
@@ -334,6 +335,7 @@ struct pb_state {
   int* d_err = nullptr;
   int xregion = 0, ds = 0;
   size_t dsmem = 0;
+  bool decode_checked = false;     // the kernel's shared-memory attribute set and its fit checked for dsmem
   bool persistent = true;
   unsigned long long* d_trace = nullptr;   // PB_DECODE_TRACE=1: phase timing marks
   float* att_scores = nullptr;   // split attention: [NH][max_ctx] scores, then e
@@ -876,6 +878,7 @@ int build_phases(pb_state* s) {
   // dynamic shared memory: issue context, ring, activation region, mbarriers, schedule, map
   const size_t sched_off = (ISSUE_BYTES + (size_t)ds * stage + xb + (size_t)ds * 8 + 15) & ~(size_t)15;
   s->dsmem = sched_off + tab;
+  s->decode_checked = false;
   {
     // one device buffer: schedule [G][ngemv], spt [G], map [G][spt_max]
     const size_t sb = sched.size() * sizeof(GemvSched);
@@ -936,11 +939,26 @@ int launch_decode_t(pb_state* s, int ntok, cudaStream_t st) {
   d.spt_max = s->spt_max;
   d.sched_off = (int)s->sched_smem_off;
   d.desc_off = (int)(s->sched_smem_off + (size_t)s->ngemv * sizeof(GemvSched));
-  PB_TRY_CUDA(cudaFuncSetAttribute(k_decode<F32S, E, EH, W>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                   (int)s->dsmem));
-  int per_sm = 0;
-  PB_TRY_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k_decode<F32S, E, EH, W>, 256, s->dsmem));
-  if (per_sm < 1) return pb_set_error(PB_ENOTSUP, "persistent decode does not fit on an SM");
+  if (!s->decode_checked) {   // once per state and schedule, not per launch
+    // the attribute belongs to the kernel on a device, shared by every state
+    // there: only ever raise it, to the largest shared memory any state needs
+    static std::mutex mu;
+    static size_t attr_max[64] = {};
+    int dev = 0;
+    PB_TRY_CUDA(cudaGetDevice(&dev));
+    {
+      std::lock_guard<std::mutex> lk(mu);
+      if (dev < 0 || dev >= 64 || s->dsmem > attr_max[dev]) {
+        PB_TRY_CUDA(cudaFuncSetAttribute(k_decode<F32S, E, EH, W>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         (int)s->dsmem));
+        if (dev >= 0 && dev < 64) attr_max[dev] = s->dsmem;
+      }
+    }
+    int per_sm = 0;
+    PB_TRY_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k_decode<F32S, E, EH, W>, 256, s->dsmem));
+    if (per_sm < 1) return pb_set_error(PB_ENOTSUP, "persistent decode does not fit on an SM");
+    s->decode_checked = true;
+  }
   const int grid = pb_num_sms();
   if (grid > MAX_CTA || grid < s->m->NH) return pb_set_error(PB_ENOTSUP, "persistent decode grid %d", grid);
   PB_TRY_CUDA(cudaMemsetAsync(s->d_bar, 0, sizeof(unsigned), st));
@@ -964,9 +982,10 @@ int launch_decode(pb_state* s, int ntok, cudaStream_t st) {
 
 // the kernel's error word (a bounded wait gave up); clears it
 int check_decode_error(pb_state* s, cudaStream_t st) {
-  int e = 0;
-  PB_TRY_CUDA(cudaMemcpyAsync(&e, s->d_err, sizeof(int), cudaMemcpyDeviceToHost, st));
+  int* he = reinterpret_cast<int*>(s->h_ctl + 1);   // pinned: the copy stays asynchronous
+  PB_TRY_CUDA(cudaMemcpyAsync(he, s->d_err, sizeof(int), cudaMemcpyDeviceToHost, st));
   PB_TRY_CUDA(cudaStreamSynchronize(st));
+  const int e = *he;
   if (e) {
     cudaMemsetAsync(s->d_err, 0, sizeof(int), st);
     return pb_set_error(PB_ECUDA, "decode kernel: a bounded wait gave up (code %d)", e);
@@ -1320,7 +1339,7 @@ extern "C" int pb_state_create(pb_model* m, int max_ctx, pb_state** out) {
                     (void**)&s->logits, (void**)&s->ctl, (void**)&s->d_bar, (void**)&s->d_err,
                     (void**)&s->att_scores, (void**)&s->att_inv, (void**)&s->att_segp};
   for (size_t i = 0; i < sizeof(sizes) / sizeof(sizes[0]); i++) { *slots[i] = p; p += align256(sizes[i]); }
-  if (cudaMallocHost(&s->h_ctl, sizeof(Ctl)) != cudaSuccess) {
+  if (cudaMallocHost(&s->h_ctl, sizeof(Ctl) + 16) != cudaSuccess) {
     cudaGetLastError(); cudaFree(s->mem); delete s;
     return pb_set_error(PB_ENOMEM, "pb_state_create: pinned control block");
   }
@@ -1439,8 +1458,11 @@ extern "C" int pb_decode_token(pb_model* m, pb_state* s, int token, int pos, int
   if (d_logits) PB_TRY_CUDA(cudaMemcpyAsync(d_logits, s->logits, (size_t)m->V * 4, cudaMemcpyDeviceToDevice, st));
   if (h_out_id) {
     PB_TRY_CUDA(cudaMemcpyAsync(&s->h_ctl->token, &s->ctl->token, sizeof(int), cudaMemcpyDeviceToHost, st));
-    if (s->persistent && (rc = check_decode_error(s, st))) return rc;
-    PB_TRY_CUDA(cudaStreamSynchronize(st));
+    if (s->persistent) {
+      if ((rc = check_decode_error(s, st))) return rc;   // synchronises the stream
+    } else {
+      PB_TRY_CUDA(cudaStreamSynchronize(st));
+    }
     *h_out_id = s->h_ctl->token;
   }
   return PB_OK;
