@@ -80,6 +80,9 @@ __global__ void __launch_bounds__(256) k_bs_norm(BsNormArgs a) {
   __shared__ int wmin[8];
   __shared__ float s_sc;
   __shared__ Q8kScratch q8s;
+  // the norm weight does not depend on the previous kernel: load it before
+  // the dependency wait
+  const float wv = a.w[blockIdx.x * 256 + threadIdx.x];
   pb_grid_wait();
   pb_grid_launch_dependents();
   const int t = threadIdx.x, H = a.H;
@@ -115,7 +118,7 @@ __global__ void __launch_bounds__(256) k_bs_norm(BsNormArgs a) {
   const int i = blockIdx.x * 256 + t;
   const float v = sv[i];
   if (a.r) a.xout[i] = v;
-  const float y = __fmul_rn(__fmul_rn(v, s_sc), a.w[i]);
+  const float y = __fmul_rn(__fmul_rn(v, s_sc), wv);
   pb_q8k_block256(y, a.xq + (size_t)blockIdx.x * 292, q8s);
 }
 
@@ -158,6 +161,14 @@ struct BsPreArgs {
 // one warp per head: q heads, k heads (rms, rope), then v heads (copied)
 __global__ void __launch_bounds__(32) k_bs_attn_pre(BsPreArgs a) {
   __shared__ float sx[BS_HD];
+  // the head-norm weights do not depend on the previous kernel: load them
+  // before the dependency wait (v heads load and ignore k_norm)
+  float wq[4];
+  {
+    const float* w = (int)blockIdx.x < a.NH ? a.qn : a.kn;
+#pragma unroll
+    for (int k = 0; k < 4; k++) wq[k] = w[threadIdx.x + 32 * k];
+  }
   pb_grid_wait();
   pb_grid_launch_dependents();
   const int hh = blockIdx.x, l = threadIdx.x, pos = a.ctl->pos;
@@ -194,10 +205,9 @@ __global__ void __launch_bounds__(32) k_bs_attn_pre(BsPreArgs a) {
     mean = __shfl_sync(0xffffffffu, mean, 0);
   }
   const float sc = bs_rms_scale(mean);
-  const float* w = hh < a.NH ? a.qn : a.kn;
   float y[4];
 #pragma unroll
-  for (int k = 0; k < 4; k++) y[k] = __fmul_rn(__fmul_rn(x[k], sc), w[l + 32 * k]);
+  for (int k = 0; k < 4; k++) y[k] = __fmul_rn(__fmul_rn(x[k], sc), wq[k]);
   const float* rc = a.rope + (size_t)pos * BS_HD;
   float o[4];
 #pragma unroll
