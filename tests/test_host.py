@@ -44,3 +44,31 @@ def test_shard_range_partitions():
             assert parts[0][0] == 0 and parts[-1][1] == n
             assert all(parts[i][1] == parts[i + 1][0] for i in range(world - 1))
             assert max(b - a for a, b in parts) - min(b - a for a, b in parts) <= 1
+
+
+def test_bench_clock_samples_only_inside_the_timed_region():
+    """The bench's nvidia-smi sampler keeps only the samples whose own
+    timestamps fall inside the timed region, and reads clock and throttle
+    fields by position after the timestamp."""
+    import datetime
+    import os
+    import sys
+    import time
+    sys.path.insert(0, os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
+    import bench
+    c = bench.Clocks(0)
+    now = time.time()
+    c.t0, c.t1 = now - 1.0, now + 1.0
+
+    def stamp(t):
+        return datetime.datetime.fromtimestamp(t).strftime("%Y/%m/%d %H:%M:%S.%f")[:-3]
+    quiet = "Not Active, Not Active, Not Active, Not Active"
+    c.lines = [stamp(now - 5) + ", 0, 900, 1965, 100.0, 0x1, Active, Not Active, Not Active, Not Active",
+               stamp(now - 0.5) + ", 0, 1965, 1965, 300.0, 0x0, " + quiet,
+               stamp(now) + ", 0, 1900, 1965, 320.0, 0x4, Not Active, Not Active, Not Active, Active",
+               stamp(now + 5) + ", 0, 800, 1965, 100.0, 0x0, " + quiet,
+               "garbage line"]
+    s = c.summary()
+    assert s["samples"] == 2
+    assert s["sm_mhz"] == (1965.0 + 1900.0) / 2 and s["sm_max_mhz"] == 1965.0
+    assert s["reasons"] == ["sw_power_cap"]
