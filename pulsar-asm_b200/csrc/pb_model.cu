@@ -1658,6 +1658,24 @@ extern "C" int pb_test_expf(const float* d_x, float* d_y, int n, void* stream) {
   return PB_OK;
 }
 
+namespace {
+// the persistent kernel's grid wait on a counter that nothing advances: it
+// must give up after `limit` polls and report it, as the kernel does with
+// its error word (status 1 = gave up, 2 = passed)
+__global__ void k_test_grid_wait(const unsigned* bar, unsigned target, unsigned limit, int* status) {
+  if (threadIdx.x == 0) *status = grid_wait(bar, target, limit) ? 2 : 1;
+}
+}  // namespace
+// test hook (not part of the public ABI): one bounded grid wait; d_bar and
+// d_status are device ints, limit the number of polls
+extern "C" int pb_test_grid_wait(const unsigned* d_bar, unsigned target, unsigned limit, int* d_status,
+                                 void* stream) {
+  if (!d_bar || !d_status) return pb_set_error(PB_EINVAL, "pb_test_grid_wait: null argument");
+  k_test_grid_wait<<<1, 32, 0, (cudaStream_t)stream>>>(d_bar, target, limit, d_status);
+  PB_LAUNCHED("k_test_grid_wait");
+  return PB_OK;
+}
+
 // ============================================ layer step without allocation
 // Some callers cannot call cudaMalloc at all: a host runtime that owns every
 // allocation through its own pool or arena, code running where allocation is

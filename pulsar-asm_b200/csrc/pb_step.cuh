@@ -94,8 +94,8 @@ constexpr unsigned PB_WAIT_LIMIT = 1u << 24;   // polls before a wait gives up
 // CTAs have arrived (bounded: PB_WAIT_LIMIT polls, a few seconds). One thread
 // per CTA polls with acquire loads and no sleep between them; a sleep, or
 // relaxed polls with a fence after the last, measured slower.
-PB_DEV bool grid_wait(const unsigned* bar, unsigned target) {
-  for (unsigned i = 0; i < PB_WAIT_LIMIT; i++) {
+PB_DEV bool grid_wait(const unsigned* bar, unsigned target, unsigned limit = PB_WAIT_LIMIT) {
+  for (unsigned i = 0; i < limit; i++) {
     unsigned v;
     asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(bar) : "memory");
     if (v >= target) return true;

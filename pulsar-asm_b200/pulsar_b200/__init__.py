@@ -98,6 +98,7 @@ def lib():
     L.pb_decode_kernels_per_token.argtypes = [vp]
     L.pb_time_step_kernel.argtypes = [vp, vp, i, i, C.POINTER(C.c_float), C.POINTER(C.c_double), vp]
     L.pb_test_expf.argtypes = [vp, vp, i, vp]
+    L.pb_test_grid_wait.argtypes = [vp, C.c_uint, C.c_uint, vp, vp]
     L.pb_layer_step_noalloc.argtypes = [vp, vp, i, i, vp, vp]
     L.pb_state_status.argtypes = [vp, vp]
     L.pb_prefill_chunk.argtypes = [vp, vp, vp, i, i, vp, vp, vp]
@@ -274,6 +275,16 @@ class Q1Tensor:
 def device_expf(x, y, stream=None):
     """test hook: the kernels' e^x on a device fp32 tensor."""
     check(lib().pb_test_expf(_ptr(x), _ptr(y), x.numel(), _stream(stream)))
+
+
+def device_grid_wait(counter, target, limit, stream=None):
+    """test hook: one bounded grid wait of the persistent decode kernel on a
+    device int32 counter; 1 = gave up after `limit` polls, 2 = passed."""
+    import torch
+    status = torch.zeros(1, dtype=torch.int32, device=counter.device)
+    check(lib().pb_test_grid_wait(_ptr(counter), target, limit, _ptr(status), _stream(stream)))
+    torch.cuda.synchronize()
+    return int(status.item())
 
 
 def compat_gemv(rows, cols, w, xq, y):

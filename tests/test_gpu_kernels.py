@@ -249,6 +249,20 @@ def test_q1_compat_host_abi(cuda, oracle, pb):
     assert np.array_equal(_bits(y), _bits(g["y"]))
 
 
+def test_grid_wait_gives_up_and_reports(cuda, pb):
+    """The decode kernel's grid wait is bounded: on a counter that nothing
+    advances it gives up after its poll limit and reports it (the kernel then
+    records an error code and leaves); the context stays usable. A counter
+    that has reached the target passes at once."""
+    torch = cuda
+    counter = torch.zeros(1, dtype=torch.int32, device="cuda")
+    assert pb.device_grid_wait(counter, 1, 1 << 12) == 1
+    counter.fill_(5)
+    assert pb.device_grid_wait(counter, 5, 1 << 12) == 2
+    x = torch.ones(4, device="cuda")
+    assert float((x * 2).sum().item()) == 8.0
+
+
 def test_device_expf_matches_oracle_and_cuda(cuda, oracle, pb):
     torch = cuda
     xs = np.concatenate([np.linspace(-104, 89, 400001), np.linspace(-2, 2, 10001)]).astype(np.float32)
