@@ -260,6 +260,22 @@ class Model:
         return np.ctypeslib.as_array(C.cast(ptr, C.POINTER(C.c_uint16)),
                                      shape=(c["conv_w"] * c["hidden"],)).copy().reshape(c["conv_w"], c["hidden"])
 
+    def set_kv(self, layer, which, a):
+        """overwrite the attention layer's K (0) or V (1) cache with f16 bits
+        [max_ctx][n_kv][head_dim]"""
+        c = self.cfg
+        a = np.ascontiguousarray(a, np.uint16)
+        assert a.size == c["max_ctx"] * c["n_kv"] * c["head_dim"]
+        C.memmove(lib().pbo_state_kv(self.s, layer, which), a.ctypes.data, a.nbytes)
+
+    def set_ring(self, layer, a):
+        """overwrite the conv layer's ring with bf16 bits [W][H]: row k holds
+        position pos - W + k before the step at pos"""
+        c = self.cfg
+        a = np.ascontiguousarray(a, np.uint16)
+        assert a.size == c["conv_w"] * c["hidden"]
+        C.memmove(lib().pbo_state_ring(self.s, layer), a.ctypes.data, a.nbytes)
+
     def __del__(self):
         try:
             lib().pbo_state_free(self.s)
