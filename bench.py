@@ -69,12 +69,26 @@ def ncu_traffic():
     return None
 
 
+CLOCK_ROLL_S = 0.15   # identical untimed launches before and after the timed one
+
+
+def clock_roll(state, tok, pos, n, ids, stream, seconds):
+    """back-to-back launches of the timed workload (n greedy tokens from pos)
+    on a second state for `seconds`: the clock record around the timed launch"""
+    t_end = time.time() + seconds
+    while time.time() < t_end:
+        state.decode_greedy(tok, pos, n, ids, stream=stream)
+        stream.synchronize()
+
+
 class Clocks:
-    """nvidia-smi sampling during the timed region (SM clock and throttle
-    reasons). The sampler is started and seen to print before the region
+    """nvidia-smi sampling around the timed region (SM clock and throttle
+    reasons). The sampler is started and seen to print before the window
     begins; every sample carries nvidia-smi's own timestamp, and only samples
-    taken between the region's start and end count. The period (25 ms) leaves
-    several samples in the bench's shortest timed region."""
+    taken between the window's start and end count. The window is the timed
+    launch plus identical untimed launches before and after it (clock_roll),
+    because a K-token launch lasts less than one 25 ms sampler period; the
+    summary also says how many samples fell inside the timed launch itself."""
 
     Q = ("timestamp,index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
          "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
@@ -83,6 +97,13 @@ class Clocks:
     def __init__(self, index, period_ms=25):
         self.index, self.period, self.p, self.lines = index, period_ms, None, []
         self.t0 = self.t1 = None
+        self.r0 = self.r1 = None
+
+    def region_start(self):
+        self.r0 = time.time()
+
+    def region_end(self):
+        self.r1 = time.time()
 
     def __enter__(self):
         try:
@@ -125,6 +146,7 @@ class Clocks:
     def summary(self):
         sm, mx, reasons = [], None, set()
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        in_region = 0
         for ln in list(self.lines):
             f = [x.strip() for x in ln.split(",")]
             if len(f) < 10:
@@ -132,6 +154,8 @@ class Clocks:
             w = self._when(f[0])
             if w is None or self.t0 is None or not (self.t0 <= w <= self.t1):
                 continue
+            if self.r0 is not None and self.r1 is not None and self.r0 <= w <= self.r1:
+                in_region += 1
             try:
                 sm.append(float(f[2]))
                 mx = float(f[3])
@@ -140,8 +164,13 @@ class Clocks:
             for n, v in zip(names, f[6:10]):
                 if v.lower() == "active":
                     reasons.add(n)
-        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx,
-                "reasons": sorted(reasons), "samples": len(sm)}
+        out = {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx,
+               "reasons": sorted(reasons), "samples": len(sm)}
+        if self.t0 is not None and self.t1 is not None:
+            out["window_ms"] = round((self.t1 - self.t0) * 1e3, 1)
+        if self.r0 is not None and self.r1 is not None:
+            out["samples_in_timed_launch"] = in_region
+        return out
 
 
 def bench_cfg(layers):
@@ -444,10 +473,12 @@ def bonsai_setup(torch, pb, stream, max_ctx, pos0, n_layers=None):
 def phase_trace(torch, model, prompt, stream, ctx):
     """Per-phase breakdown of one decode token (token 0 of a 4-token launch of
     the persistent kernel, after two warm launches) from the kernel's own
-    globaltimer marks (PB_DECODE_TRACE): per CTA and phase the entry, grid
-    barrier, prologue end, work end and arrival times, plus warp 0's data
-    waits, slot releases (with refill issues) and chain arithmetic inside the
-    GEMV stage loops. Times are means over the CTAs, in microseconds."""
+    globaltimer marks (PB_DECODE_TRACE): per CTA and phase the entry, the end
+    of the prologue (the previous phase's tagged output arrived and the GEMV
+    input built), the end of the work and the phase's closing CTA barrier, plus
+    warp 0's data waits, slot releases (with refill issues) and chain
+    arithmetic inside the GEMV stage loops. Times are means over the CTAs (over
+    the head CTAs for attention phases), in microseconds."""
     import numpy as np
     os.environ["PB_DECODE_TRACE"] = "1"
     st = model.new_state(ctx + 64)
@@ -463,30 +494,29 @@ def phase_trace(torch, model, prompt, stream, ctx):
     G = torch.cuda.get_device_properties(0).multi_processor_count
     nph = tr.size // (G * 8)
     tr = tr.reshape(G, nph, 8).astype(np.float64) / 1e3
-    gemv = (tr[:, :, 2] != 0).any(axis=0)
+    gemv = (tr[:, :, 1] != 0).any(axis=0)
+    nh = int(model.info["n_heads"])
     mean = lambda a: a.mean(axis=0)
-    bar = mean(tr[:, :, 1] - tr[:, :, 0])
-    pro = mean(tr[:, :, 2] - tr[:, :, 1])
-    work_g = mean(tr[:, :, 3] - tr[:, :, 2])
-    work_a = mean(tr[:, :, 3] - tr[:, :, 1])
-    arr = mean(tr[:, :, 4] - tr[:, :, 3])
-    other = ~gemv
-    other[-1] = False          # the last phase is the greedy argmax
-    out = {"phases": int(nph), "gemv_phases": int(gemv.sum()), "attention_phases": int(other.sum()),
+    pro = mean(tr[:, :, 1] - tr[:, :, 0])
+    work_g = mean(tr[:, :, 3] - tr[:, :, 1])
+    work_a = (tr[:nh, :, 3] - tr[:nh, :, 0]).mean(axis=0)
+    close = mean(tr[:, :, 4] - tr[:, :, 3])
+    attn = ~gemv
+    out = {"phases": int(nph), "gemv_phases": int(gemv.sum()), "attention_phases": int(attn.sum()),
            "token_us": float(tr[:, -1, 4].max() - tr[:, 0, 0].min()),
-           "gemv_prologue_with_grid_barrier_us": float(pro[gemv].sum()),
+           "gemv_prologue_with_input_wait_us": float(pro[gemv].sum()),
            "gemv_work_us": float(work_g[gemv].sum()),
-           "attention_barrier_us": float(bar[other].sum()), "attention_work_us": float(work_a[other].sum()),
-           "arrive_us": float(arr.sum()),
+           "attention_work_us_head_ctas": float(work_a[attn].sum()),
+           "phase_close_us": float(close.sum()),
            # slots 5 to 7 are written only by a library built with
            # EXTRA=-DPB_TRACE_STAGE_LOOP (null otherwise)
            "warp0_data_wait_us": float(mean(tr[:, :, 6])[gemv].sum()) if tr[:, :, 6].any() else None,
            "warp0_release_issue_us": float(mean(tr[:, :, 5])[gemv].sum()) if tr[:, :, 5].any() else None,
            "warp0_chains_trees_us": float(mean(tr[:, :, 7])[gemv].sum()) if tr[:, :, 7].any() else None,
            "first_phases": [{"phase": p, "kind": "gemv" if gemv[p] else "attention",
-                             "prologue_us": round(float(pro[p] if gemv[p] else bar[p]), 2),
+                             "prologue_us": round(float(pro[p]), 2) if gemv[p] else None,
                              "work_us": round(float(work_g[p] if gemv[p] else work_a[p]), 2),
-                             "arrive_us": round(float(arr[p]), 2),
+                             "close_us": round(float(close[p]), 2),
                              "span_us": round(float(tr[:, p, 4].max() - tr[:, p, 0].min()), 2)}
                             for p in range(min(nph, 12))]}
     return out
@@ -595,16 +625,28 @@ def main():
         stream.synchronize()
         pos += args.warmup
         nxt = int(ids[args.warmup - 1].item()) if args.warmup else first
+        # a second state at the same positions runs identical launches around
+        # the timed one, so that the clock record spans many sampler periods
+        # (a K-token launch is shorter than one)
+        aux = model.new_state(max_ctx)
+        aux.decode_prompt(prompt, 0, stream=stream)
+        aux_ids = torch.empty(args.steps, dtype=torch.int32, device="cuda")
+        stream.synchronize()
         dist.barrier()
         torch.cuda.synchronize()
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        launches0 = pb.launch_count()
         with Clocks(local) as clk:
+            clock_roll(aux, nxt, pos, args.steps, aux_ids, stream, CLOCK_ROLL_S)
+            clk.region_start()
+            launches0 = pb.launch_count()
             e0.record(stream)
             st.decode_greedy(nxt, pos, args.steps, ids[args.warmup:], stream=stream)
             e1.record(stream)
             e1.synchronize()
-        launches = pb.launch_count() - launches0
+            launches = pb.launch_count() - launches0
+            clk.region_end()
+            clock_roll(aux, nxt, pos, args.steps, aux_ids, stream, CLOCK_ROLL_S)
+        aux.destroy()
         dist.barrier()
         torch.cuda.synchronize()
         ms = e0.elapsed_time(e1)
@@ -641,7 +683,7 @@ def main():
         # the decode kernel: one cooperative launch for the K timed tokens; its
         # algorithmic bytes are every token's weights plus the KV it reads
         achieved = (wb + kvb) / step_s / 1e9
-        rk = {"kernel": "k_decode (persistent, warp-specialised: TMA bulk weight stream + fused phases)",
+        rk = {"kernel": "k_decode (persistent: TMA bulk weight ring, tagged phase hand-off, fused prologues)",
               "bytes_per_launch": (wb + kvb) * args.steps, "ms_per_launch": ms,
               "bytes_per_token": wb + kvb}
     else:

@@ -167,9 +167,13 @@ int pb_decode_prompt(pb_model* m, pb_state* s, const int* d_tokens, int n, int p
  * layer's intermediate activations live in one static device array of at most
  * 512 KB per GPU (held by every GPU that loads the library until exit); models
  * needing more scratch get PB_EINVAL. The first call on a device looks up that
- * array's device address (make it before any stream capture). All calls share
- * the array, so calls that overlap on the GPU race: serialise them on one
- * stream. Results are identical to pb_layer_step's. */
+ * array's device address, and the first use of the library's kernels may load
+ * its module, which commits the array: make that first call (or any earlier
+ * call into the library) in the caller's start-up phase, before any stream
+ * capture. The looked-up address lasts for the life of the device's primary
+ * context. All calls share the array, so calls that overlap on the GPU race:
+ * serialise them on one stream. Row-sharded states (pb_state_shard) get
+ * PB_ENOTSUP. Results are identical to pb_layer_step's. */
 int pb_layer_step_noalloc(pb_model* m, pb_state* s, int layer, int pos, uint16_t* d_x,
                           void* stream);
 /* chunked prefill on the integer path (the tensor-core GEMMs of pb_q80_gemm

@@ -326,7 +326,17 @@ struct pb_state {
   char* mem = nullptr;
   size_t mem_bytes = 0;
   // persistent decode kernel: phase table, arrival counter, error word
-  Phase* d_phases = nullptr;
+  DPhase* d_phases = nullptr;
+  // tagged activations of the persistent kernel (bf16 value | 16-bit phase tag)
+  uint32_t* t_first = nullptr;    // q|k|v|gate or in_proj output
+  uint32_t* t_attn = nullptr;     // gated attention output
+  uint32_t* t_mix = nullptr;      // o_proj / out_proj output
+  uint32_t* t_u = nullptr;        // SwiGLU output
+  uint32_t* t_w2 = nullptr;       // w2 output
+  unsigned long long* t_scores = nullptr;   // [NH][max_ctx] attention scores (phase << 32 | fp32 bits)
+  size_t tag_bytes = 0;           // the six buffers, contiguous from t_first
+  unsigned qbase = 0;             // sequence number of the next launch's first phase
+  size_t res_smem_off = 0;
   char* d_sched = nullptr;         // weight-stream schedule: GemvSched [CTA][ngemv], spt [CTA], StageDesc [CTA][spt_max]
   int ngemv = 0, spt_max = 0;
   size_t sched_bytes = 0, spt_off = 0, map_off = 0, sched_smem_off = 0;
@@ -685,22 +695,11 @@ int build_graph(pb_state* s) {
 // on the per-kernel CUDA-graph path, with the same results.
 bool persistent_shape(const pb_model* m) {
   if (m->HD != 64 || m->H != 2048 || m->W != 3) return false;
+  // PRO_PLAIN inputs (w2: K = F; o_proj: K = NH*HD) take 256*{8,16,32} values;
+  // the P.V phase runs on 4 NH CTAs
   const int kf = m->F >> 8, ka = (m->NH * m->HD) >> 8;
   return m->F % 256 == 0 && (kf == 8 || kf == 16 || kf == 32) && (m->NH * m->HD) % 256 == 0 &&
-         (ka == 4 || ka == 8 || ka == 16);
-}
-
-Phase gemv_phase_of(const pb_q8& w, int epi, StepArgs a) {
-  Phase ph = {};
-  ph.kind = PH_GEMV;
-  ph.nch = w.nch;
-  ph.epi = epi;
-  a.codes = reinterpret_cast<const uint4*>(w.codes);
-  a.scales = w.scales;
-  a.N = w.N;
-  a.K = w.K;
-  ph.a = a;
-  return ph;
+         (ka == 8 || ka == 16 || ka == 32) && 4 * m->NH <= pb_num_sms();
 }
 
 AttnArgs attn_args(const pb_model* m, pb_state* s, int layer) {
@@ -725,103 +724,95 @@ AttnArgs attn_args(const pb_model* m, pb_state* s, int layer) {
   return a;
 }
 
-// The token as a phase list: the same kernels' work, in the same order and
-// with the same buffers, as enqueue_token.
+DPhase dgemv(const pb_model* m, const pb_q8& w, int pro, int epi, const uint32_t* tin, uint32_t* tout) {
+  DPhase ph = {};
+  ph.kind = PH_GEMV;
+  ph.pro = pro;
+  ph.epi = epi;
+  ph.N = w.N;
+  ph.K = w.K;
+  ph.nch = w.nch;
+  ph.H = m->H;
+  ph.eps = m->eps;
+  ph.tin = tin;
+  ph.tout = tout;
+  return ph;
+}
+
+// The token as a phase list (the same arithmetic, in the same order, as
+// enqueue_token): per layer the first GEMV (embedding or residual add +
+// post-norm + operator_norm), attention (one phase) or nothing, the mixer
+// GEMV (conv prologue or the attention output), w1|w3 (residual add +
+// post-norm + ffn_norm; SwiGLU epilogue), w2; then the head (residual add +
+// post-norm + embedding_norm; logits and per-CTA argmax). Every phase reads
+// the previous phase's tagged output.
 int build_phases(pb_state* s) {
   if (s->d_phases) return PB_OK;
   pb_model* m = s->m;
-  std::vector<Phase> ph;
-  int cur = 0;
+  std::vector<DPhase> ph;
   for (int L = 0; L < m->L; L++) {
     const Layer& Ly = m->layers[L];
-    StepArgs a = base_args(m, s);
+    DPhase a = dgemv(m, Ly.first, L == 0 ? PRO_EMBED : PRO_ADDNORM, EPI_BF16, s->t_w2, s->t_first);
     a.wnorm = Ly.op_norm;
-    a.y = s->h_first;
     if (L == 0) {
-      a.pro = PRO_EMBED;
+      a.tin = nullptr;
       a.emb_codes = reinterpret_cast<const uint4*>(m->head.codes);
       a.emb_scales = m->head.scales;
       a.emb_nch = m->head.nch;
       a.emb_f32 = m->head.sdt == PB_DT_F32;
-      a.rout = s->res[cur];
     } else {
-      a.pro = PRO_ADDNORM;
-      a.xin = s->res[cur];
-      a.hin = s->h_w2;
       a.wpost = m->layers[L - 1].post_ffn_norm;
-      a.rout = s->res[cur ^ 1];
-      cur ^= 1;
     }
-    ph.push_back(gemv_phase_of(Ly.first, EPI_BF16, a));
-    StepArgs b = base_args(m, s);
-    b.y = s->h_mix;
+    ph.push_back(a);
     if (Ly.attn) {
-      // split attention: scores, softmax, P.V; the segment partials are
-      // combined (and gated) in the o_proj prologue
-      for (int kind : {PH_SCORE, PH_SOFTMAX, PH_PV}) {
-        Phase at = {};
-        at.kind = kind;
-        at.at = attn_args(m, s, L);
-        ph.push_back(at);
-      }
-      b.pro = PRO_ATTN;
-      b.xin = s->h_first;
-      b.segp = s->att_segp;
-      b.nh = m->NH;
-      b.hd = m->HD;
-      b.goff = m->NH * m->HD + 2 * m->NKV * m->HD;
+      DPhase sc = {};
+      sc.kind = PH_SCORE;
+      sc.tin = s->t_first;
+      sc.tsc = s->t_scores;
+      sc.at = attn_args(m, s, L);
+      ph.push_back(sc);
+      DPhase pv = sc;
+      pv.kind = PH_PV;
+      pv.tout = s->t_attn;
+      ph.push_back(pv);
+      ph.push_back(dgemv(m, Ly.mix, PRO_PLAIN, EPI_BF16, s->t_attn, s->t_mix));
     } else {
-      b.pro = PRO_CONV;
-      b.xin = s->h_first;
+      DPhase b = dgemv(m, Ly.mix, PRO_CONV, EPI_BF16, s->t_first, s->t_mix);
       b.ring = s->ring + (size_t)Ly.conv_idx * m->W * m->H;
       b.taps = Ly.taps;
+      ph.push_back(b);
     }
-    ph.push_back(gemv_phase_of(Ly.mix, EPI_BF16, b));
-    StepArgs c = base_args(m, s);
-    c.pro = PRO_ADDNORM;
-    c.xin = s->res[cur];
-    c.hin = s->h_mix;
+    DPhase c = dgemv(m, Ly.w13, PRO_ADDNORM, EPI_SILU, s->t_mix, s->t_u);
     c.wpost = Ly.post_op_norm;
     c.wnorm = Ly.ffn_norm;
-    c.rout = s->res[cur ^ 1];
-    cur ^= 1;
-    c.y = s->h_u;
-    ph.push_back(gemv_phase_of(Ly.w13, EPI_SILU, c));
-    StepArgs d = base_args(m, s);
-    d.pro = PRO_PLAIN;
-    d.xin = s->h_u;
-    d.y = s->h_w2;
-    ph.push_back(gemv_phase_of(Ly.w2, EPI_BF16, d));
+    ph.push_back(c);
+    ph.push_back(dgemv(m, Ly.w2, PRO_PLAIN, EPI_BF16, s->t_u, s->t_w2));
   }
-  StepArgs h = base_args(m, s);
-  h.pro = PRO_ADDNORM;
-  h.xin = s->res[cur];
-  h.hin = s->h_w2;
+  DPhase h = dgemv(m, m->head, PRO_ADDNORM, EPI_ARGMAX, s->t_w2, nullptr);
   h.wpost = m->layers[m->L - 1].post_ffn_norm;
   h.wnorm = m->final_norm;
-  h.rout = s->res[cur ^ 1];
-  s->graph_res = cur ^ 1;
-  h.y = s->logits;
-  ph.push_back(gemv_phase_of(m->head, EPI_ARGMAX, h));
-  Phase am = {};
-  am.kind = PH_ARGMAX;
-  ph.push_back(am);
-  // shared-memory plan: activation region, then as many ring stages as fit
-  const int cnt_max = (((s->max_ctx + 7) / 8) + 3) & ~3;
-  s->pv_per_warp = 9 * cnt_max;
-  int xr = std::max(s->max_ctx, std::max(8 * 2 * m->HD, 8 * s->pv_per_warp));
-  // a GEMV phase holds its padded input, then its row values: at most
-  // ceil(row blocks / CTAs) stages of 16 chunk values per CTA
+  h.rout = s->res[0];
+  h.fout = s->logits;
+  h.at.ctl = s->ctl;
+  s->graph_res = 0;
+  ph.push_back(h);
+  // shared-memory plan: the activation region holds a GEMV phase's padded
+  // input, then its row values (at most ceil(row blocks / CTAs) stages of 16
+  // chunk values per CTA); the score phase's q and k per warp; the P.V
+  // phase's V chunk (32 KB), scores, partials, current v row and gate
+  const int span = (m->win > 0 && m->win < s->max_ctx) ? m->win : s->max_ctx;
+  const int dq = m->HD / 4;
+  int xr = std::max(DWARPS * 2 * m->HD, 32768 / 4 + ((span + 3) & ~3) + 9 * dq + 4);
   const int G = pb_num_sms();
   for (auto& p : ph)
     if (p.kind == PH_GEMV) {
       const int RB = DSEGS / p.nch;
-      const int nrb = (p.a.N + RB - 1) / RB;
-      p.rowoff = (p.a.K + p.a.K / 32 + 3) & ~3;
+      const int nrb = (p.N + RB - 1) / RB;
+      p.rowoff = (p.K + p.K / 32 + 3) & ~3;
       xr = std::max(xr, p.rowoff + ((nrb + G - 1) / G) * DSEGS);
     }
-  // weight-stream schedule: per CTA and GEMV its rows (the same split as the
-  // stage loop) and first stage within the token, and the stage -> GEMV map
+  // weight-stream schedule: per CTA and GEMV its rows and first stage within
+  // the token, and one descriptor per stage
   int ngemv = 0;
   for (auto& p : ph)
     if (p.kind == PH_GEMV) p.gidx = ngemv++;
@@ -829,22 +820,29 @@ int build_phases(pb_state* s) {
   std::vector<int> spt(G, 0);
   std::vector<std::vector<StageDesc>> sdesc(G);
   const size_t q8s = m->sdt == PB_DT_F32 ? 8 : 4;   // bytes per scale pair
+  std::vector<const pb_q8*> wts;   // the GEMV phases' tensors, in phase order
+  for (int L = 0; L < m->L; L++) {
+    const Layer& Ly = m->layers[L];
+    wts.push_back(&Ly.first); wts.push_back(&Ly.mix); wts.push_back(&Ly.w13); wts.push_back(&Ly.w2);
+  }
+  wts.push_back(&m->head);
   for (int b = 0; b < G; b++) {
-    int base = 0;
+    int base = 0, k = 0;
     for (auto& p : ph) {
       if (p.kind != PH_GEMV) continue;
+      const pb_q8& w = *wts[k++];
       const int RB = DSEGS / p.nch;
-      const int nrb = (p.a.N + RB - 1) / RB;
+      const int nrb = (p.N + RB - 1) / RB;
       const int rb0 = (int)(((long long)b * nrb) / G), rb1 = (int)(((long long)(b + 1) * nrb) / G);
       GemvSched& g = sched[(size_t)b * ngemv + p.gidx];
-      g.codes = reinterpret_cast<const char*>(p.a.codes);
-      g.scales = reinterpret_cast<const char*>(p.a.scales);
+      g.codes = reinterpret_cast<const char*>(w.codes);
+      g.scales = reinterpret_cast<const char*>(w.scales);
       g.r0 = rb0 * RB;
-      g.r1 = std::min(rb1 * RB, p.a.N);
+      g.r1 = std::min(rb1 * RB, p.N);
       g.base = base;
       g.nch = p.nch;
-      for (int k = rb0; k < rb1; k++) {
-        const int r = k * RB, nr = std::min(RB, p.a.N - r);
+      for (int kb = rb0; kb < rb1; kb++) {
+        const int r = kb * RB, nr = std::min(RB, p.N - r);
         StageDesc sd;
         sd.codes16 = (unsigned)(((size_t)(g.codes - m->arena) + (size_t)r * p.nch * 2048) / 16);
         sd.scales16 = (unsigned)(((size_t)(g.scales - m->arena) + (size_t)r * p.nch * 32 * q8s) / 16);
@@ -865,18 +863,22 @@ int build_phases(pb_state* s) {
   int optin = 0;
   cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
   const size_t stage = m->sdt == PB_DT_F32 ? DGeo<true>::STAGE : DGeo<false>::STAGE;
-  const size_t static_est = 4 * 1024;
+  const size_t static_est = 1024;
   const size_t xb = (size_t)((xr + 1) & ~1) * 4;
+  const size_t resb = ((size_t)m->H * 2 + 15) & ~(size_t)15;
   const size_t tab = (size_t)ngemv * sizeof(GemvSched) + (size_t)spt_max * sizeof(StageDesc);
-  long avail = (long)optin - (long)static_est - ISSUE_BYTES - (long)xb - MAX_DS * 8 - 16 - (long)tab;
+  long avail = (long)optin - (long)static_est - ISSUE_BYTES - (long)xb - MAX_DS * 8 - 16 - (long)resb - (long)tab;
   int ds = (int)std::min<long>(6, avail / (long)stage);
   if (ds < 2) return pb_set_error(PB_ENOTSUP, "persistent decode: shared memory for %d ring stages", ds);
   s->ds = ds;
   s->xregion = xr;
   s->ngemv = ngemv;
   s->spt_max = spt_max;
-  // dynamic shared memory: issue context, ring, activation region, mbarriers, schedule, map
-  const size_t sched_off = (ISSUE_BYTES + (size_t)ds * stage + xb + (size_t)ds * 8 + 15) & ~(size_t)15;
+  // dynamic shared memory: issue context, ring, activation region, mbarriers,
+  // residual copy, schedule, stage descriptors
+  const size_t res_off = (ISSUE_BYTES + (size_t)ds * stage + xb + (size_t)ds * 8 + 15) & ~(size_t)15;
+  const size_t sched_off = res_off + resb;
+  s->res_smem_off = res_off;
   s->dsmem = sched_off + tab;
   s->decode_checked = false;
   {
@@ -908,12 +910,12 @@ int build_phases(pb_state* s) {
       s->d_trace = nullptr;
     }
   }
-  if (cudaMalloc(&s->d_phases, ph.size() * sizeof(Phase)) != cudaSuccess) {
+  if (cudaMalloc(&s->d_phases, ph.size() * sizeof(DPhase)) != cudaSuccess) {
     cudaGetLastError();
     s->d_phases = nullptr;
     return pb_set_error(PB_ENOMEM, "persistent decode: phase table");
   }
-  PB_TRY_CUDA(cudaMemcpy(s->d_phases, ph.data(), ph.size() * sizeof(Phase), cudaMemcpyHostToDevice));
+  PB_TRY_CUDA(cudaMemcpy(s->d_phases, ph.data(), ph.size() * sizeof(DPhase), cudaMemcpyHostToDevice));
   return PB_OK;
 }
 
@@ -923,6 +925,7 @@ int launch_decode_t(pb_state* s, int ntok, cudaStream_t st) {
   d.phases = s->d_phases;
   d.nphase = s->nphase;
   d.ntok = ntok;
+  d.qbase = s->qbase;
   d.ctl = s->ctl;
   d.bar = s->d_bar;
   d.err = s->d_err;
@@ -930,7 +933,6 @@ int launch_decode_t(pb_state* s, int ntok, cudaStream_t st) {
   d.nh = s->m->NH;
   d.ds = s->ds;
   d.trace = s->d_trace;
-  d.pv_per_warp = s->pv_per_warp;
   d.sched = reinterpret_cast<const GemvSched*>(s->d_sched);
   d.spt = reinterpret_cast<const int*>(s->d_sched + s->spt_off);
   d.sdesc = reinterpret_cast<const StageDesc*>(s->d_sched + s->map_off);
@@ -939,6 +941,7 @@ int launch_decode_t(pb_state* s, int ntok, cudaStream_t st) {
   d.spt_max = s->spt_max;
   d.sched_off = (int)s->sched_smem_off;
   d.desc_off = (int)(s->sched_smem_off + (size_t)s->ngemv * sizeof(GemvSched));
+  d.res_off = (int)s->res_smem_off;
   if (!s->decode_checked) {   // once per state and schedule, not per launch
     // the attribute belongs to the kernel on a device, shared by every state
     // there: only ever raise it, to the largest shared memory any state needs
@@ -955,7 +958,7 @@ int launch_decode_t(pb_state* s, int ntok, cudaStream_t st) {
       }
     }
     int per_sm = 0;
-    PB_TRY_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k_decode<F32S, E, EH, W>, 256, s->dsmem));
+    PB_TRY_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k_decode<F32S, E, EH, W>, DTHREADS, s->dsmem));
     if (per_sm < 1) return pb_set_error(PB_ENOTSUP, "persistent decode does not fit on an SM");
     s->decode_checked = true;
   }
@@ -964,8 +967,11 @@ int launch_decode_t(pb_state* s, int ntok, cudaStream_t st) {
   PB_TRY_CUDA(cudaMemsetAsync(s->d_bar, 0, sizeof(unsigned), st));
   if (s->d_trace) PB_TRY_CUDA(cudaMemsetAsync(s->d_trace, 0, (size_t)pb_num_sms() * s->nphase * 8 * 8, st));
   void* args[] = {&d};
-  cudaError_t e = cudaLaunchCooperativeKernel((const void*)k_decode<F32S, E, EH, W>, dim3(grid), dim3(256), args,
+  cudaError_t e = cudaLaunchCooperativeKernel((const void*)k_decode<F32S, E, EH, W>, dim3(grid), dim3(DTHREADS), args,
                                               s->dsmem, st);
+  // the tags of the next launch continue after this one's, whether or not it
+  // ran to the end (a launch that gave up leaves words of its own tag range)
+  s->qbase += (unsigned)ntok * (unsigned)s->nphase;
   if (e != cudaSuccess) return pb_set_error(PB_ECUDA, "launch k_decode: %s", cudaGetErrorString(e));
   pb_count_launch();
   return PB_OK;
@@ -1327,7 +1333,9 @@ extern "C" int pb_state_create(pb_model* m, int max_ctx, pb_state** out) {
   size_t sizes[] = {kvb, ringb, ropeb, ropeb, (size_t)H * 2, (size_t)H * 2, (size_t)H * 2, firstn * 2,
                     (size_t)m->NH * m->HD * 2, (size_t)H * 2, (size_t)m->F * 2, (size_t)H * 2,
                     (size_t)m->V * 4, sizeof(Ctl), 256, 256, (size_t)m->NH * max_ctx * 4, (size_t)m->NH * 4,
-                    (size_t)m->NH * 8 * m->HD * 4};
+                    (size_t)m->NH * 8 * m->HD * 4,
+                    firstn * 4, (size_t)m->NH * m->HD * 4, (size_t)H * 4, (size_t)m->F * 4, (size_t)H * 4,
+                    (size_t)m->NH * max_ctx * 8};
   size_t tot = 0;
   for (size_t x : sizes) tot += align256(x);
   if (cudaMalloc(&s->mem, tot) != cudaSuccess) { cudaGetLastError(); delete s; return pb_set_error(PB_ENOMEM, "pb_state_create: %zu bytes", tot); }
@@ -1337,8 +1345,11 @@ extern "C" int pb_state_create(pb_model* m, int max_ctx, pb_state** out) {
                     (void**)&s->res[0], (void**)&s->res[1], (void**)&s->res[2], (void**)&s->h_first,
                     (void**)&s->h_attn, (void**)&s->h_mix, (void**)&s->h_u, (void**)&s->h_w2,
                     (void**)&s->logits, (void**)&s->ctl, (void**)&s->d_bar, (void**)&s->d_err,
-                    (void**)&s->att_scores, (void**)&s->att_inv, (void**)&s->att_segp};
+                    (void**)&s->att_scores, (void**)&s->att_inv, (void**)&s->att_segp,
+                    (void**)&s->t_first, (void**)&s->t_attn, (void**)&s->t_mix, (void**)&s->t_u, (void**)&s->t_w2,
+                    (void**)&s->t_scores};
   for (size_t i = 0; i < sizeof(sizes) / sizeof(sizes[0]); i++) { *slots[i] = p; p += align256(sizes[i]); }
+  s->tag_bytes = (size_t)((char*)s->t_scores - (char*)s->t_first) + align256((size_t)m->NH * max_ctx * 8);
   if (cudaMallocHost(&s->h_ctl, sizeof(Ctl) + 16) != cudaSuccess) {
     cudaGetLastError(); cudaFree(s->mem); delete s;
     return pb_set_error(PB_ENOMEM, "pb_state_create: pinned control block");
@@ -1397,6 +1408,10 @@ extern "C" int pb_state_reset(pb_state* s, void* stream) {
   if (ringb) PB_TRY_CUDA(cudaMemsetAsync(s->ring, 0, ringb, st));
   PB_TRY_CUDA(cudaMemsetAsync(s->ctl, 0, sizeof(Ctl), st));
   PB_TRY_CUDA(cudaMemsetAsync(s->d_err, 0, sizeof(int), st));
+  // tagged activations: tag 0xffff, which no phase of the next 65535 carries
+  // (scores: 0xffffffff)
+  PB_TRY_CUDA(cudaMemsetAsync(s->t_first, 0xff, s->tag_bytes, st));
+  s->qbase = 0;
   return PB_OK;
 }
 
@@ -1721,6 +1736,10 @@ extern "C" int pb_layer_step_noalloc(pb_model* m, pb_state* s, int layer, int po
                                      void* stream) {
   if (!m || !s || !d_x || layer < 0 || layer >= m->L || pos < 0 || pos >= s->max_ctx)
     return pb_set_error(PB_EINVAL, "pb_layer_step_noalloc: bad argument");
+  // a row-sharded state's layer step needs the all-gathers of the state's
+  // graph path; this step has none, so it serves unsharded states only
+  if (s->tp_world > 1)
+    return pb_set_error(PB_ENOTSUP, "pb_layer_step_noalloc: the state is row-sharded over %d ranks", s->tp_world);
   const size_t need = noalloc_bytes(m);
   if (need > PB_NOALLOC_SCRATCH_BYTES)
     return pb_set_error(PB_EINVAL, "pb_layer_step_noalloc: this model needs %zu bytes of scratch, "
@@ -1731,7 +1750,9 @@ extern "C" int pb_layer_step_noalloc(pb_model* m, pb_state* s, int layer, int po
   void* base = nullptr;
   {
     // set-up, once per device with that device current: the array's device
-    // address (its name in host code is only a stand-in, not an address)
+    // address (its name in host code is only a stand-in, not an address). The
+    // cached address is valid for the life of the device's primary context;
+    // after a cudaDeviceReset the process must not call this entry point again.
     std::lock_guard<std::mutex> lk(g_noalloc_mu);
     if (!g_noalloc_ptr[dev]) {
       void* p = nullptr;

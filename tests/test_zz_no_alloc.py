@@ -34,6 +34,13 @@ def test_noalloc_layer_step_matches_layer_step(tmp_path, pb, cuda):
             s_new.layer_step_noalloc(layer, pos, x_new)
             torch.cuda.synchronize()
             assert torch.equal(x_ref, x_new), "layer %d pos %d" % (layer, pos)
+    # the promise itself: once warm, more calls take no device memory
+    free0 = torch.cuda.mem_get_info()[0]
+    for pos in (2, 3):
+        for layer in (0, 1):
+            s_new.layer_step_noalloc(layer, pos, x_new)
+    torch.cuda.synchronize()
+    assert torch.cuda.mem_get_info()[0] == free0
     kv_ref = s_ref.debug_tensor(0, torch.int16)
     kv_new = s_new.debug_tensor(0, torch.int16)
     ring_ref = s_ref.debug_tensor(1, torch.int16)
