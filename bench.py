@@ -502,9 +502,19 @@ def phase_trace(torch, model, prompt, stream, ctx):
     work_a = (tr[:nh, :, 3] - tr[:nh, :, 0]).mean(axis=0)
     close = mean(tr[:, :, 4] - tr[:, :, 3])
     attn = ~gemv
+    # GEMV inputs: when thread 0's poll saw the previous phase's tagged output
+    # (mark 2), against when the last producer CTA ended its work (mark 3)
+    polled = (tr[:, :, 2] != 0).all(axis=0)
+    prev_last = np.concatenate([[np.nan], tr[:, :-1, 3].max(axis=0)])
+    prev_first = np.concatenate([[np.nan], tr[:, :-1, 3].min(axis=0)])
+    detect = mean(tr[:, :, 2]) - prev_last
     out = {"phases": int(nph), "gemv_phases": int(gemv.sum()), "attention_phases": int(attn.sum()),
            "token_us": float(tr[:, -1, 4].max() - tr[:, 0, 0].min()),
            "gemv_prologue_with_input_wait_us": float(pro[gemv].sum()),
+           "gemv_input_wait_us": float(mean(tr[:, :, 2] - tr[:, :, 0])[polled].sum()),
+           "gemv_input_after_last_producer_us": float(detect[polled].sum()),
+           "producer_end_spread_us": float((prev_last - prev_first)[polled].sum()),
+           "gemv_norm_and_x_us": float(mean(tr[:, :, 1] - tr[:, :, 2])[polled].sum()),
            "gemv_work_us": float(work_g[gemv].sum()),
            "attention_work_us_head_ctas": float(work_a[attn].sum()),
            "phase_close_us": float(close.sum()),

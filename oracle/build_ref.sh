@@ -142,3 +142,121 @@ EOF
     "$out/pins_fwd8.o" "$out/pins_fa16.o" -lm
 rm -f "$out"/pins_*.o
 echo "build_ref: built $out/libpb_refpins.so"
+
+# --- F: the reference's own LFM3 layer kernels (CUDA, sm_100a) --------------
+#   lfm3_nanode.cu:74-83, 93     the compile-time shapes (H 2048, NH 16, NKV 4, HD 128, MAXTOK)
+#   lfm3_nanode.cu:114-121       bf16 storage and its round-to-nearest-even pair
+#   lfm3_nanode.cu:382-445       rmsnorm_body / k_rmsnorm
+#   lfm3_nanode.cu:460-498       k_headnorm, k_rope
+#   lfm3_nanode.cu:503-602       k_attn_head
+#   lfm3_nanode.cu:811-829       k_mul_bf, k_add_bf, k_silu_mul_bf
+#   lfm3_nanode.cu:852-859       k_sigmoid_gate
+#   lfm3_nanode.cu:892-911       k_shift_in, k_conv7
+#   lfm3_nanode.cu:942-964       k_argmax
+# followed by host wrappers written here (host buffers in and out) and probes
+# that return CUDA's own expf / rsqrtf / cosf / sinf for given arguments. The
+# library runs on the GPU box only (tests/golden/make_golden_lfm3.py).
+NVCC="${NVCC:-/usr/local/cuda/bin/nvcc}"
+if [ -x "$NVCC" ]; then
+  A="$REF/pulsar_arm/asm/lfm3_nanode.cu"
+  {
+    printf '#include <cstdint>\n#include <cstdio>\n#include <cmath>\n#include <cuda_runtime.h>\n#include <cuda_fp16.h>\n'
+    sed -n '74,83p' "$A"
+    sed -n '93p' "$A"
+    sed -n '114,121p' "$A"
+    sed -n '382,445p' "$A"
+    sed -n '460,498p' "$A"
+    sed -n '503,602p' "$A"
+    sed -n '811,829p' "$A"
+    sed -n '852,859p' "$A"
+    sed -n '892,911p' "$A"
+    sed -n '942,964p' "$A"
+    cat <<'WRAP'
+/* ---- host wrappers and probes (this repository's code) ---- */
+namespace {
+template <class T> T* up(const T* h, size_t n) { T* d = nullptr; cudaMalloc(&d, n * sizeof(T)); if (h) cudaMemcpy(d, h, n * sizeof(T), cudaMemcpyHostToDevice); return d; }
+template <class T> int down(T* h, const T* d, size_t n) { cudaMemcpy(h, d, n * sizeof(T), cudaMemcpyDeviceToHost); return cudaDeviceSynchronize() == cudaSuccess && cudaGetLastError() == cudaSuccess ? 0 : -1; }
+__global__ void p_expf(const float* x, float* y, int n) { int i = blockIdx.x * blockDim.x + threadIdx.x; if (i < n) y[i] = expf(x[i]); }
+__global__ void p_rsqrtf(const float* x, float* y, int n) { int i = blockIdx.x * blockDim.x + threadIdx.x; if (i < n) y[i] = rsqrtf(x[i]); }
+__global__ void p_cossin(const float* x, float* c, float* s, int n) { int i = blockIdx.x * blockDim.x + threadIdx.x; if (i < n) { c[i] = cosf(x[i]); s[i] = sinf(x[i]); } }
+}
+extern "C" {
+int pbref_shapes(int* o) { o[0] = H; o[1] = NH; o[2] = NKV; o[3] = HD; o[4] = MAXTOK; return 0; }
+int pbref_gpu_rmsnorm(const uint16_t* x, const float* w, uint16_t* y, float eps) {
+  bf16* dx = up((const bf16*)x, H); float* dw = up(w, H); bf16* dy = up((const bf16*)nullptr, H);
+  k_rmsnorm<<<1, 256>>>(dx, dw, dy, eps, H);
+  int rc = down((bf16*)y, dy, H); cudaFree(dx); cudaFree(dw); cudaFree(dy); return rc;
+}
+int pbref_gpu_headnorm(uint16_t* x, const float* w, int nheads, float eps) {
+  bf16* dx = up((const bf16*)x, (size_t)nheads * HD); float* dw = up(w, HD);
+  k_headnorm<<<nheads, 32>>>(dx, dw, eps, HD);
+  int rc = down((bf16*)x, dx, (size_t)nheads * HD); cudaFree(dx); cudaFree(dw); return rc;
+}
+int pbref_gpu_rope(uint16_t* x, const float* invf, int nheads, int pos, int rot) {
+  bf16* dx = up((const bf16*)x, (size_t)nheads * HD); float* di = up(invf, HD / 2);
+  k_rope<<<nheads, 64>>>(dx, di, pos, HD, rot);
+  int rc = down((bf16*)x, dx, (size_t)nheads * HD); cudaFree(dx); cudaFree(di); return rc;
+}
+/* q [NH][HD]; kc, vc [npos][NKV][HD]; out [NH][HD] */
+int pbref_gpu_attn(const uint16_t* q, const uint16_t* kc, const uint16_t* vc, uint16_t* out, int npos, int win,
+                   float scaling) {
+  bf16* dq = up((const bf16*)q, (size_t)NH * HD);
+  bf16* dk = up((const bf16*)kc, (size_t)npos * NKV * HD);
+  bf16* dv = up((const bf16*)vc, (size_t)npos * NKV * HD);
+  bf16* dout = up((const bf16*)nullptr, (size_t)NH * HD);
+  k_attn_head<<<NH, 256>>>(dq, dk, dv, dout, npos, win, scaling, HD, NKV);
+  int rc = down((bf16*)out, dout, (size_t)NH * HD); cudaFree(dq); cudaFree(dk); cudaFree(dv); cudaFree(dout); return rc;
+}
+int pbref_gpu_silu_mul(const uint16_t* a, const uint16_t* b, uint16_t* y, int n) {
+  bf16* da = up((const bf16*)a, n); bf16* db = up((const bf16*)b, n); bf16* dy = up((const bf16*)nullptr, n);
+  k_silu_mul_bf<<<(n + 255) / 256, 256>>>(da, db, dy, n);
+  int rc = down((bf16*)y, dy, n); cudaFree(da); cudaFree(db); cudaFree(dy); return rc;
+}
+int pbref_gpu_mul_bf(const uint16_t* a, const uint16_t* b, uint16_t* y, int n) {
+  bf16* da = up((const bf16*)a, n); bf16* db = up((const bf16*)b, n); bf16* dy = up((const bf16*)nullptr, n);
+  k_mul_bf<<<(n + 255) / 256, 256>>>(da, db, dy, n);
+  int rc = down((bf16*)y, dy, n); cudaFree(da); cudaFree(db); cudaFree(dy); return rc;
+}
+/* g [nh]; attn [nh][HD] gated in place */
+int pbref_gpu_sigmoid_gate(const uint16_t* g, uint16_t* attn, int nh) {
+  bf16* dg = up((const bf16*)g, nh); bf16* da = up((const bf16*)attn, (size_t)nh * HD);
+  k_sigmoid_gate<<<1, nh>>>(dg, da, HD);
+  int rc = down((bf16*)attn, da, (size_t)nh * HD); cudaFree(dg); cudaFree(da); return rc;
+}
+/* ring [7][H] (newest last) shifted in place with xin [H]; y [H] = the conv */
+int pbref_gpu_conv(uint16_t* ring, const uint16_t* xin, const float* taps, uint16_t* y) {
+  bf16* dr = up((const bf16*)ring, (size_t)7 * H); bf16* dx = up((const bf16*)xin, H);
+  float* dt = up(taps, (size_t)H * 7); bf16* dy = up((const bf16*)nullptr, H);
+  k_shift_in<<<H / 256, 256>>>(dr, dx, H);
+  k_conv7<<<H / 256, 256>>>(dr, dt, dy, H);
+  int rc = down((bf16*)y, dy, H); if (!rc) rc = down((bf16*)ring, dr, (size_t)7 * H);
+  cudaFree(dr); cudaFree(dx); cudaFree(dt); cudaFree(dy); return rc;
+}
+int pbref_gpu_argmax(const float* lg, int n, int* out) {
+  float* dl = up(lg, n); int* di = up((const int*)nullptr, 1);
+  k_argmax<<<1, 256>>>(dl, di, n);
+  int rc = down(out, di, 1); cudaFree(dl); cudaFree(di); return rc;
+}
+int pbref_gpu_expf(const float* x, float* y, int n) {
+  float* dx = up(x, n); float* dy = up((const float*)nullptr, n);
+  p_expf<<<(n + 255) / 256, 256>>>(dx, dy, n);
+  int rc = down(y, dy, n); cudaFree(dx); cudaFree(dy); return rc;
+}
+int pbref_gpu_rsqrtf(const float* x, float* y, int n) {
+  float* dx = up(x, n); float* dy = up((const float*)nullptr, n);
+  p_rsqrtf<<<(n + 255) / 256, 256>>>(dx, dy, n);
+  int rc = down(y, dy, n); cudaFree(dx); cudaFree(dy); return rc;
+}
+int pbref_gpu_cossin(const float* x, float* c, float* s, int n) {
+  float* dx = up(x, n); float* dc = up((const float*)nullptr, n); float* ds = up((const float*)nullptr, n);
+  p_cossin<<<(n + 255) / 256, 256>>>(dx, dc, ds, n);
+  int rc = down(c, dc, n); if (!rc) rc = down(s, ds, n); cudaFree(dx); cudaFree(dc); cudaFree(ds); return rc;
+}
+}
+WRAP
+  } > "$out/refgpu.cu"
+  "$NVCC" -gencode arch=compute_100a,code=sm_100a -O3 -std=c++17 -Xcompiler -fPIC -shared -w \
+      -o "$out/libpb_refgpu.so" "$out/refgpu.cu"
+  rm -f "$out/refgpu.cu"
+  echo "build_ref: built $out/libpb_refgpu.so"
+fi

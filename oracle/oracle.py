@@ -70,6 +70,9 @@ def lib():
         L.pbo_rope.argtypes = [vp, i, i, i, vp, vp]
         L.pbo_attn_head.argtypes = [vp, vp, vp, i, i, i, i, i, f, C.c_uint16, i, vp]
         L.pbo_argmax.restype = i; L.pbo_argmax.argtypes = [vp, i]
+        L.pbo_conv_step.argtypes = [vp, vp, vp, i, i, vp]
+        L.pbo_silu_mul_bf.argtypes = [vp, vp, vp, i]
+        L.pbo_sigmoid_gate.argtypes = [vp, vp, i, i]
         L.pbo_model_new.restype = vp; L.pbo_model_new.argtypes = [C.POINTER(_Cfg), vp]
         L.pbo_model_free.argtypes = [vp]
         L.pbo_model_set_q8.argtypes = [vp, i, i, vp, vp, i, i]

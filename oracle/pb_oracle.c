@@ -399,6 +399,34 @@ void pbo_attn_head(const uint16_t* q, const uint16_t* kc, const uint16_t* vc, in
   free(sl);
 }
 
+/* k_shift_in + k_conv7 (lfm3_nanode.cu:892-911) for any width W: the ring
+ * [W][H] (oldest first) shifts by one and takes xin as its newest row; y_i =
+ * bf16 of the fp32 chain ((0 + t_i0 r_0i) + t_i1 r_1i) + ... over the taps. */
+void pbo_conv_step(uint16_t* ring, const uint16_t* xin, const float* taps, int W, int H, uint16_t* y) {
+  for (int k = 0; k + 1 < W; k++) memcpy(ring + (size_t)k * H, ring + (size_t)(k + 1) * H, 2 * (size_t)H);
+  memcpy(ring + (size_t)(W - 1) * H, xin, 2 * (size_t)H);
+  for (int i = 0; i < H; i++) {
+    float acc = 0.0f;
+    for (int k = 0; k < W; k++) acc = acc + taps[(size_t)i * W + k] * pbo_bf2f(ring[(size_t)k * H + i]);
+    y[i] = pbo_f2bf(acc);
+  }
+}
+/* k_silu_mul_bf (lfm3_nanode.cu:821-829): y = bf16((a * 1/(1+e^-a)) * b) */
+void pbo_silu_mul_bf(const uint16_t* a, const uint16_t* b, uint16_t* y, int n) {
+  for (int i = 0; i < n; i++) {
+    const float av = pbo_bf2f(a[i]);
+    const float sg = 1.0f / (1.0f + pbo_expf(-av));
+    y[i] = pbo_f2bf((av * sg) * pbo_bf2f(b[i]));
+  }
+}
+/* k_sigmoid_gate (lfm3_nanode.cu:852-859): attn[h][:] = bf16(attn * 1/(1+e^-g_h)) */
+void pbo_sigmoid_gate(const uint16_t* g, uint16_t* attn, int nh, int hd) {
+  for (int h = 0; h < nh; h++) {
+    const float sg = 1.0f / (1.0f + pbo_expf(-pbo_bf2f(g[h])));
+    for (int j = 0; j < hd; j++) attn[(size_t)h * hd + j] = pbo_f2bf(pbo_bf2f(attn[(size_t)h * hd + j]) * sg);
+  }
+}
+
 /* greedy argmax; ties go to the lowest index (the reference's k_argmax,
  * lfm3_nanode.cu:942-964, resolves ties by its reduction tree instead). */
 int pbo_argmax(const float* v, int n) {
@@ -556,17 +584,11 @@ int pbo_decode(const pbo_model* m, pbo_state* s, int token, int pos, float* logi
       gemv_bf(&T[PBO_O], at, h2);
     } else {
       gemv_bf(&T[PBO_IN], h1, bx);
-      uint16_t* ring = s->ring[L];
-      for (int k = 0; k + 1 < W; k++) memcpy(ring + (size_t)k * H, ring + (size_t)(k + 1) * H, 2 * (size_t)H);
       for (int i = 0; i < H; i++)                       /* B * x, k_mul_bf (:811-815) */
-        ring[(size_t)(W - 1) * H + i] = pbo_f2bf(pbo_bf2f(bx[i]) * pbo_bf2f(bx[2 * H + i]));
-      const float* taps = fw[PBO_TAPS];
-      for (int i = 0; i < H; i++) {                     /* k_conv7 (:901-911), C * y */
-        float acc = 0.0f;
-        for (int k = 0; k < W; k++) acc = acc + taps[(size_t)i * W + k] * pbo_bf2f(ring[(size_t)k * H + i]);
-        const uint16_t cy = pbo_f2bf(acc);
-        h3[i] = pbo_f2bf(pbo_bf2f(bx[H + i]) * pbo_bf2f(cy));
-      }
+        h3[i] = pbo_f2bf(pbo_bf2f(bx[i]) * pbo_bf2f(bx[2 * H + i]));
+      pbo_conv_step(s->ring[L], h3, fw[PBO_TAPS], W, H, h3);   /* h3 <- conv output */
+      for (int i = 0; i < H; i++)                       /* C * y */
+        h3[i] = pbo_f2bf(pbo_bf2f(bx[H + i]) * pbo_bf2f(h3[i]));
       gemv_bf(&T[PBO_OUT], h3, h2);
     }
     pbo_rmsnorm(h2, fw[PBO_POSTOPN], h3, H, c->norm_eps);

@@ -64,6 +64,9 @@ void pbo_attn_head(const uint16_t* q, const uint16_t* kc, const uint16_t* vc, in
                    int nkv, int hd, int npos, int win, float scaling, uint16_t gate,
                    int use_gate, uint16_t* out);
 int pbo_argmax(const float* v, int n);
+void pbo_conv_step(uint16_t* ring, const uint16_t* xin, const float* taps, int W, int H, uint16_t* y);
+void pbo_silu_mul_bf(const uint16_t* a, const uint16_t* b, uint16_t* y, int n);
+void pbo_sigmoid_gate(const uint16_t* g, uint16_t* attn, int nh, int hd);
 
 /* ---- whole LFM3-style decode step ----------------------------------------- */
 typedef struct {

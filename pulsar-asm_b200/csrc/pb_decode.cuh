@@ -138,7 +138,7 @@ PB_DEV unsigned long long gtime() {
   return t;
 }
 // trace marks: 0 phase entered, 1 prologue done (input arrived and x built),
-// 3 work done, 4 phase left; in a build with PB_TRACE_STAGE_LOOP defined, GEMV
+// 2 thread 0's input poll ended (GEMV), 3 work done, 4 phase left; in a build with PB_TRACE_STAGE_LOOP defined, GEMV
 // phases add warp 0's stage-loop totals: 5 slot releases with their refill
 // issues, 6 waits for stage data, 7 chain and tree arithmetic
 PB_DEV void tmark(const DecodeArgs& d, int tok, int p, int k) {
@@ -192,12 +192,21 @@ PB_DEV void dsync() { asm volatile("bar.sync 0;" ::: "memory"); }   // all 16 wa
 
 // ---------------------------------------------------------- tagged words
 PB_DEV void st_tag(uint32_t* p, uint32_t v) {
+#ifdef PBX_WEAK_ST
+  asm volatile("st.global.cg.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+#else
   asm volatile("st.relaxed.gpu.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+#endif
 }
 PB_DEV uint4 ld_tag4(const uint32_t* p) {
   uint4 r;
+#ifdef PBX_CG_LD
+  asm volatile("ld.global.cg.v4.u32 {%0, %1, %2, %3}, [%4];"
+               : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w) : "l"(p) : "memory");
+#else
   asm volatile("ld.relaxed.gpu.global.v4.u32 {%0, %1, %2, %3}, [%4];"
                : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w) : "l"(p) : "memory");
+#endif
   return r;
 }
 PB_DEV uint2 ld_tag2(const uint32_t* p) {
@@ -245,6 +254,9 @@ PB_DEV bool poll_words(const uint32_t* p, uint32_t tw, uint32_t (&w)[N], const P
     if (bad < 0x10000u) return true;
     if (i >= PB_POLL_LIMIT) return false;
     if ((i & 255) == 255 && (*pc.abort || ld_relaxed_int(pc.err))) return false;
+#ifdef PBX_POLL_SLEEP
+    __nanosleep(PBX_POLL_SLEEP);
+#endif
 #ifdef PBX_POLL_SLEEP
     __nanosleep(PBX_POLL_SLEEP);
 #endif
@@ -344,9 +356,14 @@ PB_DEV bool slot_release(unsigned slot) {
 // residual (embedding row, or the CTA's residual copy + the post-normalised
 // input vector) -> the CTA's residual copy (and the global one when rout) ->
 // norm -> x.
+// trace mark 2 of a GEMV phase: thread 0's input poll ended
+PB_DEV void mark_input(unsigned long long* tm2) {
+  if (tm2 && threadIdx.x == 0) tm2[0] = gtime();
+}
+
 template <int E>
 PB_DEV void dpro_residual(const DPhase& ph, float* sx, bf16_t* res_s, float* red, uint32_t tw, int tok_id,
-                          const PollCtx& pc) {
+                          const PollCtx& pc, unsigned long long* tm2) {
   const int t = threadIdx.x;
   const int H = ph.H;
   const float eps = ph.eps;
@@ -372,6 +389,7 @@ PB_DEV void dpro_residual(const DPhase& ph, float* sx, bf16_t* res_s, float* red
   } else {
     uint32_t w[E];
     if (!poll_words<E>(ph.tin + (size_t)t * E, tw, w, pc)) poll_fail(pc, 4);
+    mark_input(tm2);
     float Hv[E], hn[E];
 #pragma unroll
     for (int j = 0; j < E; j++) Hv[j] = pb_lo2f(w[j]);
@@ -395,7 +413,8 @@ PB_DEV void dpro_residual(const DPhase& ph, float* sx, bf16_t* res_s, float* red
 // pos held pos - W, which no CTA reads any more, and CTA 0 writes the new value
 // there. E = H/256 channels per thread.
 template <int E, int W>
-PB_DEV void dpro_conv(const DPhase& ph, float* sx, uint32_t tw, int pos, const PollCtx& pc) {
+PB_DEV void dpro_conv(const DPhase& ph, float* sx, uint32_t tw, int pos, const PollCtx& pc,
+                      unsigned long long* tm2) {
   const int t = threadIdx.x, H = ph.H;
   bf16_t* ring = ph.ring;
   float tp[E * W];
@@ -411,6 +430,7 @@ PB_DEV void dpro_conv(const DPhase& ph, float* sx, uint32_t tw, int pos, const P
   ok = ok && poll_words<E>(ph.tin + H + (size_t)t * E, tw, wC, pc);
   ok = ok && poll_words<E>(ph.tin + 2 * H + (size_t)t * E, tw, wX, pc);
   if (!ok) poll_fail(pc, 4);
+  mark_input(tm2);
   float bx[E];
 #pragma unroll
   for (int j = 0; j < E; j++) {
@@ -425,10 +445,11 @@ PB_DEV void dpro_conv(const DPhase& ph, float* sx, uint32_t tw, int pos, const P
 
 // plain input: K = 256 EK tagged values, EK per thread.
 template <int EK>
-PB_DEV void dpro_plain(const DPhase& ph, float* sx, uint32_t tw, const PollCtx& pc) {
+PB_DEV void dpro_plain(const DPhase& ph, float* sx, uint32_t tw, const PollCtx& pc, unsigned long long* tm2) {
   const int t = threadIdx.x;
   uint32_t w[EK];
   if (!poll_words<EK>(ph.tin + (size_t)t * EK, tw, w, pc)) poll_fail(pc, 4);
+  mark_input(tm2);
 #pragma unroll
   for (int j = 0; j < EK; j++) sx[padx(t * EK + j)] = pb_lo2f(w[j]);
 }
@@ -453,14 +474,14 @@ __device__ __forceinline__ unsigned gemv_phase(const DecodeArgs& d, const DPhase
     const PollCtx pc = {abort_flag, d.err};
     const int pro = ph.pro;
     if (pro == PRO_EMBED || pro == PRO_ADDNORM) {
-      dpro_residual<EH>(ph, sx, res_s, red, tw_in, tok_id, pc);
+      dpro_residual<EH>(ph, sx, res_s, red, tw_in, tok_id, pc, tm2);
     } else if (pro == PRO_CONV) {
-      dpro_conv<EH, W>(ph, sx, tw_in, pos, pc);
+      dpro_conv<EH, W>(ph, sx, tw_in, pos, pc, tm2);
     } else {
       switch (ph.K >> 8) {
-        case 8: dpro_plain<8>(ph, sx, tw_in, pc); break;
-        case 16: dpro_plain<16>(ph, sx, tw_in, pc); break;
-        case 32: dpro_plain<32>(ph, sx, tw_in, pc); break;
+        case 8: dpro_plain<8>(ph, sx, tw_in, pc, tm2); break;
+        case 16: dpro_plain<16>(ph, sx, tw_in, pc, tm2); break;
+        case 32: dpro_plain<32>(ph, sx, tw_in, pc, tm2); break;
         default: break;   // other K: the host keeps this kernel off
       }
     }
