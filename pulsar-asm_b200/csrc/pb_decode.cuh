@@ -188,25 +188,16 @@ PB_DEV void bulk_g2s(void* dst, const void* src, unsigned bytes, uint64_t* bar, 
 PB_DEV void grid_arrive(unsigned* bar) {
   asm volatile("red.release.gpu.global.add.u32 [%0], 1;" ::"l"(bar) : "memory");
 }
-PB_DEV void dsync() { asm volatile("bar.sync 0;" ::: "memory"); }   // all 16 warps
+PB_DEV void dsync() { asm volatile("bar.sync 0;" ::: "memory"); }   // all warps of the CTA
 
 // ---------------------------------------------------------- tagged words
 PB_DEV void st_tag(uint32_t* p, uint32_t v) {
-#ifdef PBX_WEAK_ST
-  asm volatile("st.global.cg.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
-#else
   asm volatile("st.relaxed.gpu.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
-#endif
 }
 PB_DEV uint4 ld_tag4(const uint32_t* p) {
   uint4 r;
-#ifdef PBX_CG_LD
-  asm volatile("ld.global.cg.v4.u32 {%0, %1, %2, %3}, [%4];"
-               : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w) : "l"(p) : "memory");
-#else
   asm volatile("ld.relaxed.gpu.global.v4.u32 {%0, %1, %2, %3}, [%4];"
                : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w) : "l"(p) : "memory");
-#endif
   return r;
 }
 PB_DEV uint2 ld_tag2(const uint32_t* p) {
@@ -254,12 +245,6 @@ PB_DEV bool poll_words(const uint32_t* p, uint32_t tw, uint32_t (&w)[N], const P
     if (bad < 0x10000u) return true;
     if (i >= PB_POLL_LIMIT) return false;
     if ((i & 255) == 255 && (*pc.abort || ld_relaxed_int(pc.err))) return false;
-#ifdef PBX_POLL_SLEEP
-    __nanosleep(PBX_POLL_SLEEP);
-#endif
-#ifdef PBX_POLL_SLEEP
-    __nanosleep(PBX_POLL_SLEEP);
-#endif
   }
 }
 PB_DEV void poll_fail(const PollCtx& pc, int code) {
