@@ -69,6 +69,8 @@ def ncu_traffic():
     return None
 
 
+CPU_SAMPLE = ("%d decode steps of the full cfg1 model at positions %d.. over seeded fp16 KV rows and conv "
+              "rings (the oracle's restatement of layer_body + head + argmax, C, OpenMP over rows)")
 CLOCK_ROLL_S = 0.15   # identical untimed launches before and after the timed one
 
 
@@ -196,27 +198,98 @@ def make_blob(path, c):
 
 def cpu_baseline(c, weights, ctx, seconds):
     """the oracle's decode step (C, OpenMP over rows) on the host cores, over a
-    bounded sample: tokens decoded after a short prefix, until `seconds` pass."""
+    bounded sample at the timed workload's own positions: the KV caches hold
+    ctx seeded fp16 rows and the conv rings a seeded history (so each step
+    reads the same context the GPU's timed steps read), then whole decode
+    steps at positions ctx, ctx+1, ... are timed until `seconds` pass."""
     sys.path.insert(0, os.path.join(ROOT, "oracle"))
     import numpy as np
     import oracle as O
     from pulsar_b200 import synth
     if weights is None:
         weights = synth.make_weights(c, seed=SEED)
-    om = O.Model(synth.oracle_cfg(c, ctx + 64), weights)
+    max_ctx = ctx + 64
+    om = O.Model(synth.oracle_cfg(c, max_ctx), weights)
     rng = np.random.default_rng(SEED)
+    for L in range(c["n_layers"]):
+        if L in c["attn_layers"]:
+            for which in (0, 1):
+                a = (rng.standard_normal((max_ctx, c["n_kv"], c["head_dim"])) * 0.5).astype(np.float16)
+                a[ctx:] = 0
+                om.set_kv(L, which, a.view(np.uint16))
+        else:
+            om.set_ring(L, O.f2bf(rng.standard_normal((c["conv_w"], c["hidden"])).astype(np.float32)))
     tok = int(rng.integers(0, c["vocab"]))
-    # a short prefix; the sample then times whole decode steps
     t0 = time.time()
-    n, pos = 0, 0
+    n, pos = 0, ctx
     while True:
         tok, _, _ = om.decode(tok, pos)
         pos += 1
         n += 1
-        if time.time() - t0 > seconds and n >= 2:
+        if (time.time() - t0 > seconds and n >= 2) or pos >= max_ctx:
             break
     dt = time.time() - t0
     return n / dt, O.lib().pbo_threads(), n, pos
+
+
+def config_dict(ctx, world):
+    """the workload's config, the same in both arms"""
+    return {"workload": WORKLOAD, "ctx": ctx, "seqs_per_gpu": 1,
+            "weights": "Q8_0 int8 codes + fp16 scales per 32, activations bf16",
+            "l2": "inputs larger than L2 (1.8 GB of weights per token)",
+            "parallelism": "sequence split, one replica per GPU (dp%d)" % world}
+
+
+def cpu_model():
+    try:
+        for ln in subprocess.run(["lscpu"], capture_output=True, text=True, timeout=10).stdout.splitlines():
+            if ln.startswith("Model name:"):
+                return ln.split(":", 1)[1].strip()
+    except Exception:
+        pass
+    return None
+
+
+def cpu_reference_gemv(seconds=2.0):
+    """the reference's own x86/C CPU Q8 GEMV (.auto/lfm3/q8_gemv_cpu.c, built
+    unmodified by oracle/build_ref.sh at -O3 and -O3 -march=x86-64-v3) at the
+    cfg0 shape (8192 x 2048, fp32 x, fp32 scales): GB/s of codes + scales + x +
+    y, with every host core and with one; null where it was not built"""
+    import ctypes as C
+    import numpy as np
+    out = {}
+    ncores = len(os.sched_getaffinity(0))
+    N, K = 8192, 2048
+    rng = np.random.default_rng(SEED)
+    q = rng.integers(-127, 128, (N, K), dtype=np.int8)
+    sc = (np.abs(rng.standard_normal((N, K // 32))) * 0.01).astype(np.float16).astype(np.float32)
+    x = rng.standard_normal(K).astype(np.float32)
+    y = np.zeros(N, np.float32)
+    nbytes = N * K + N * (K // 32) * 4 + K * 4 + N * 4
+    for arm in ("O3", "v3"):
+        path = os.path.join(ROOT, "oracle", "_ref", "libpb_q8cpu_%s.so" % arm)
+        if not os.path.exists(path):
+            continue
+        L = C.CDLL(path)
+        vp = C.c_void_p
+        L.pbref_gemv_q8.argtypes = [vp, vp, vp, vp, C.c_int, C.c_int]
+        L.pbref_set_threads.argtypes = [C.c_int]
+        res = {}
+        for th in (ncores, 1):
+            L.pbref_set_threads(th)
+            args = [q.ctypes.data_as(vp), sc.ctypes.data_as(vp), x.ctypes.data_as(vp), y.ctypes.data_as(vp), N, K]
+            for _ in range(3):
+                L.pbref_gemv_q8(*args)
+            best = float("inf")
+            t_end = time.time() + seconds
+            while time.time() < t_end:
+                t0 = time.perf_counter()
+                L.pbref_gemv_q8(*args)
+                best = min(best, time.perf_counter() - t0)
+            res["threads_%d" % th] = {"ms": best * 1e3, "gbs": nbytes / best / 1e9}
+        out["-O3" if arm == "O3" else "-O3 -march=x86-64-v3"] = res
+    return {"kernel": ".auto/lfm3/q8_gemv_cpu.c gemv_q8 (the reference's x86/C path), cfg0 8192x2048",
+            "cpu": cpu_model(), "cores": ncores, "arms": out} if out else None
 
 
 def _time_rotating(torch, stream, fns, reps):
@@ -583,10 +656,10 @@ def run_reference(args, rank, world):
     line = {"impl": "reference", "metric": METRIC, "value": tps, "unit": "tok/s", "n_gpus": args.gpus,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1000.0 / tps,
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "fp32",
-            "data": "synthetic", "config": {"workload": WORKLOAD, "ctx": args.ctx},
-            "cpu_baseline": {"value": tps, "unit": "tok/s", "cores": cores, "kind": "port",
-                             "sample": "%d decode steps of the full cfg1 model from position 0 "
-                                       "(oracle restatement of layer_body, OpenMP over rows)" % n},
+            "data": "synthetic", "config": config_dict(args.ctx, world),
+            "cpu_baseline": {"value": tps, "unit": "tok/s", "cores": cores, "kind": "port", "cpu": cpu_model(),
+                             "sample": CPU_SAMPLE % (n, args.ctx)},
+            "cpu_reference": cpu_reference_gemv(),
             "e2e": {"value": tps, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
 
@@ -706,11 +779,8 @@ def main():
     line = {"metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms_max / args.steps, "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "fp32", "data": "synthetic",
-            "config": {"workload": WORKLOAD, "ctx": args.ctx, "seqs_per_gpu": 1,
-                       "weights": "Q8_0 int8 codes + fp16 scales per 32, activations bf16",
-                       "l2": "inputs larger than L2 (1.8 GB of weights per token)",
-                       "parallelism": "sequence split, one replica per GPU (dp%d)" % world,
-                       "decode_path": "persistent" if persistent else "graph"},
+            "config": config_dict(args.ctx, world),
+            "decode_path": "persistent" if persistent else "graph",
             "e2e": {"value": e2e_steps * world / (ms_e2e / 1000.0), "unit": "tok/s",
                     "h2d_bytes_per_step": 40, "d2h_bytes_per_step": 4},
             "gpu_launches": launches,
@@ -730,9 +800,9 @@ def main():
         line["kernels"]["cfg3_decode"] = bonsai_bench(torch, pb, peak, stream)
     if rank == 0 and world == 1 and not args.no_cpu:
         tps, cores, n, _ = cpu_baseline(c, weights, args.ctx, args.cpu_seconds)
-        line["cpu_baseline"] = {"value": tps, "unit": "tok/s", "cores": cores, "kind": "port",
-                                "sample": "%d decode steps of the full cfg1 model from position 0 on "
-                                          "the oracle (C restatement, OpenMP over rows)" % n}
+        line["cpu_baseline"] = {"value": tps, "unit": "tok/s", "cores": cores, "kind": "port", "cpu": cpu_model(),
+                                "sample": CPU_SAMPLE % (n, args.ctx)}
+        line["cpu_reference"] = cpu_reference_gemv()
     if rank == 0:
         print(json.dumps(line), flush=True)
     st.destroy()

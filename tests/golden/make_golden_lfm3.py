@@ -46,7 +46,7 @@ def bf16_f16_exact(rng, shape, scale=1.0):
     return v
 
 
-def main(out):
+def main(path):
     L = C.CDLL(LIB)
     vp, i, f = C.c_void_p, C.c_int, C.c_float
     for name, args in [("pbref_shapes", [vp]), ("pbref_gpu_rmsnorm", [vp, vp, vp, f]),
@@ -173,8 +173,8 @@ def main(out):
     for j, (lg, o) in enumerate(am):
         g["argmax%d_lg" % j] = lg
         g["argmax%d_id" % j] = np.array(o, np.int32)
-    np.savez_compressed(out, **g)
-    print("wrote", out, "(%d arrays)" % len(g))
+    np.savez_compressed(path, **g)
+    print("wrote", path, "(%d arrays)" % len(g))
 
 
 if __name__ == "__main__":

@@ -46,10 +46,10 @@ def _ulp_f32(a, b):
 
 
 def _within_one_bf16_ulp(a, b):
+    """every pair of bf16 codes equal in value (+0 / -0 included) or adjacent"""
     ia = np.asarray(a, np.uint16).astype(np.int32)
     ib = np.asarray(b, np.uint16).astype(np.int32)
-    # same sign: adjacent codes; zero crossing: +0 / -0 and the smallest values
-    return np.all(np.abs(ia - ib) <= 1) or np.all((np.abs(ia - ib) <= 1) | (np.abs(R.bf2f(a) - R.bf2f(b)) == 0))
+    return bool(np.all((np.abs(ia - ib) <= 1) | (R.bf2f(a) == R.bf2f(b))))
 
 
 def test_replay_rmsnorm(g):
@@ -125,7 +125,7 @@ def test_oracle_attention(oracle, g):
     for npos, win, q, kc, vc, out, e in _attn_cases(g):
         k16 = R.bf2f(kc).astype(np.float16).view(np.uint16)
         v16 = R.bf2f(vc).astype(np.float16).view(np.uint16)
-        assert np.array_equal(k16.astype(np.float16).astype(np.float32), R.bf2f(kc))
+        assert np.array_equal(k16.view(np.float16).astype(np.float32), R.bf2f(kc))
         for h in range(nh):
             sc = R.attn_scores(q[h], kc, h // (nh // nkv), npos, win, scaling)
             args = R.attn_exp_args(sc)
