@@ -32,7 +32,8 @@ class _Cfg(C.Structure):
     _fields_ = [(n, C.c_int) for n in ("hidden", "inter", "n_layers", "n_heads", "n_kv",
                                        "head_dim", "vocab", "conv_w", "max_ctx",
                                        "sliding_window")] + \
-               [(n, C.c_float) for n in ("rope_theta", "rope_partial", "norm_eps")]
+               [(n, C.c_float) for n in ("rope_theta", "rope_partial", "norm_eps")] + \
+               [("slide_window", C.c_int), ("slide_theta", C.c_float), ("slide_partial", C.c_float)]
 
 
 class _BsCfg(C.Structure):
@@ -215,8 +216,10 @@ class Model:
         c = _Cfg(cfg["hidden"], cfg["inter"], cfg["n_layers"], cfg["n_heads"], cfg["n_kv"],
                  cfg["head_dim"], cfg["vocab"], cfg["conv_w"], cfg["max_ctx"],
                  cfg.get("sliding_window", 0), cfg["rope_theta"], cfg["rope_partial"],
-                 cfg["norm_eps"])
-        isa = np.array([1 if t != "conv" else 0 for t in cfg["layer_types"]], np.int32)
+                 cfg["norm_eps"], cfg.get("slide_window", 256), cfg.get("slide_theta", 1e4),
+                 cfg.get("slide_partial", 1.0))
+        kinds = {"conv": 0, "sliding_attention": 2}
+        isa = np.array([kinds.get(t, 1) for t in cfg["layer_types"]], np.int32)
         self._keep.append(isa)
         self.m = L.pbo_model_new(C.byref(c), _p(isa))
         for li, lw in enumerate(weights["layers"]):

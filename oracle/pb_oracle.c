@@ -445,7 +445,8 @@ struct pbo_model {
   const float* (*f)[PBO_NF32];
   q8t emb;
   const float* final_norm;
-  float* invf;
+  float* invf;           /* full-attention layers */
+  float* invf_slide;     /* sliding-attention layers */
 };
 struct pbo_state {
   int n_layers;
@@ -453,20 +454,22 @@ struct pbo_state {
   uint16_t* x;
 };
 
-pbo_model* pbo_model_new(const pbo_cfg* cfg, const int* layer_is_attn) {
+pbo_model* pbo_model_new(const pbo_cfg* cfg, const int* layer_kind) {
   pbo_model* m = (pbo_model*)calloc(1, sizeof *m);
   m->cfg = *cfg;
-  m->is_attn = (int*)malloc(sizeof(int) * cfg->n_layers);
-  memcpy(m->is_attn, layer_is_attn, sizeof(int) * cfg->n_layers);
+  m->is_attn = (int*)malloc(sizeof(int) * cfg->n_layers);      /* 0 conv, 1 full, 2 sliding */
+  memcpy(m->is_attn, layer_kind, sizeof(int) * cfg->n_layers);
   m->q = calloc((size_t)cfg->n_layers, sizeof *m->q);
   m->f = calloc((size_t)cfg->n_layers, sizeof *m->f);
   m->invf = (float*)malloc(sizeof(float) * cfg->head_dim / 2);
   pbo_rope_invf(m->invf, cfg->rope_theta, cfg->head_dim, cfg->rope_partial);
+  m->invf_slide = (float*)malloc(sizeof(float) * cfg->head_dim / 2);
+  pbo_rope_invf(m->invf_slide, cfg->slide_theta, cfg->head_dim, cfg->slide_partial);
   return m;
 }
 void pbo_model_free(pbo_model* m) {
   if (!m) return;
-  free(m->is_attn); free(m->q); free(m->f); free(m->invf); free(m);
+  free(m->is_attn); free(m->q); free(m->f); free(m->invf); free(m->invf_slide); free(m);
 }
 void pbo_model_set_q8(pbo_model* m, int layer, int slot, const int8_t* codes,
                       const float* scales, int N, int K) {
@@ -556,7 +559,11 @@ int pbo_decode(const pbo_model* m, pbo_state* s, int token, int pos, float* logi
   uint16_t *qb = malloc(2 * (size_t)NH * HD), *kb = malloc(2 * (size_t)NKV * HD);
   uint16_t *vb = malloc(2 * (size_t)NKV * HD), *gb = malloc(2 * (size_t)NH);
   uint16_t *at = malloc(2 * (size_t)NH * HD), *ab = malloc(2 * (size_t)F);
-  const int half = (int)((double)c->rope_partial * HD) / 2;
+  /* per layer type (lfm3_nanode.cu:3753-3785): full attention rotates
+   * (partial * HD)/2 pairs with its own base over every key; sliding attention
+   * its own rotation and base over the last slide_window keys */
+  const int half_full = (int)((double)c->rope_partial * HD) / 2;
+  const int half_slide = (int)((double)c->slide_partial * HD) / 2;
   float* cs = malloc(sizeof(float) * (HD / 2 + 1)); float* sn = malloc(sizeof(float) * (HD / 2 + 1));
   /* embedding row: bf16(code * scale), k_dequant_row (:138-142) */
   for (int i = 0; i < H; i++)
@@ -570,7 +577,9 @@ int pbo_decode(const pbo_model* m, pbo_state* s, int token, int pos, float* logi
       gemv_bf(&T[PBO_V], h1, vb); gemv_bf(&T[PBO_GATE], h1, gb);
       pbo_headnorm(qb, fw[PBO_QN], NH, HD, c->norm_eps);
       pbo_headnorm(kb, fw[PBO_KN], NKV, HD, c->norm_eps);
-      pbo_rope_cs(m->invf, pos, half, cs, sn);
+      const int slide = m->is_attn[L] == 2;
+      const int half = slide ? half_slide : half_full;
+      pbo_rope_cs(slide ? m->invf_slide : m->invf, pos, half, cs, sn);
       pbo_rope(qb, NH, HD, half, cs, sn);
       pbo_rope(kb, NKV, HD, half, cs, sn);
       for (int i = 0; i < NKV * HD; i++) {
@@ -580,7 +589,7 @@ int pbo_decode(const pbo_model* m, pbo_state* s, int token, int pos, float* logi
       const float scaling = 1.0f / sqrtf((float)HD);
       for (int h = 0; h < NH; h++)
         pbo_attn_head(qb + (size_t)h * HD, s->kc[L], s->vc[L], h / (NH / NKV), NKV, HD, pos + 1,
-                      c->sliding_window, scaling, gb[h], 1, at + (size_t)h * HD);
+                      slide ? c->slide_window : c->sliding_window, scaling, gb[h], 1, at + (size_t)h * HD);
       gemv_bf(&T[PBO_O], at, h2);
     } else {
       gemv_bf(&T[PBO_IN], h1, bx);

@@ -71,8 +71,11 @@ void pbo_sigmoid_gate(const uint16_t* g, uint16_t* attn, int nh, int hd);
 /* ---- whole LFM3-style decode step ----------------------------------------- */
 typedef struct {
   int hidden, inter, n_layers, n_heads, n_kv, head_dim, vocab, conv_w, max_ctx;
-  int sliding_window;          /* 0 = full attention */
+  int sliding_window;          /* full-attention layers' window; 0 = every key */
   float rope_theta, rope_partial, norm_eps;
+  /* sliding-attention layers (layer kind 2): their window and RoPE */
+  int slide_window;
+  float slide_theta, slide_partial;
 } pbo_cfg;
 
 enum {  /* tensor slots per layer */
@@ -86,7 +89,8 @@ enum {  /* fp32 slots per layer */
 typedef struct pbo_model pbo_model;
 typedef struct pbo_state pbo_state;
 
-pbo_model* pbo_model_new(const pbo_cfg* cfg, const int* layer_is_attn);
+/* layer_kind per layer: 0 gated short conv, 1 full attention, 2 sliding attention */
+pbo_model* pbo_model_new(const pbo_cfg* cfg, const int* layer_kind);
 void pbo_model_free(pbo_model* m);
 void pbo_model_set_q8(pbo_model* m, int layer, int slot, const int8_t* codes,
                       const float* scales, int N, int K);

@@ -266,6 +266,7 @@ __global__ void __launch_bounds__(256) k_tail(StepArgs a) {
 // ----------------------------------------------------------- host model
 struct Layer {
   bool attn = false;
+  bool slide = false;    // sliding-window attention layer
   pb_q8 first;           // q|k|v|gate or in_proj
   pb_q8 mix;             // o_proj or out_proj
   pb_q8 w13;             // w1 row i at 2i, w3 row i at 2i+1
@@ -291,6 +292,11 @@ struct pb_model {
   int device = 0;
   int H = 0, F = 0, L = 0, NH = 0, NKV = 0, HD = 0, V = 0, W = 3, n_attn = 0, win = 0;
   float theta = 1e6f, partial = 1.0f, eps = 1e-5f;
+  // sliding-attention layers (lfm3_nanode.cu:3753-3785, :5402-5420): their
+  // own RoPE base and rotated share, over the last win_s keys
+  float theta_s = 1e4f, partial_s = 1.0f;
+  int win_s = 256;
+  bool any_slide = false;
   int sdt = PB_DT_F16;
   std::vector<Layer> layers;
   pb_q8 head;
@@ -298,7 +304,8 @@ struct pb_model {
   char* arena = nullptr;
   size_t arena_bytes = 0;
   std::vector<Tensor> table;
-  std::vector<float> invf;
+  std::vector<float> invf;        // full-attention layers
+  std::vector<float> invf_s;      // sliding-attention layers
   uint64_t weight_bytes = 0;
   bool decode_ok = true;     // every decode tensor in the streaming layout
   // tensor-core copies of every projection for the chunked prefill (built on first use)
@@ -311,8 +318,10 @@ struct pb_state {
   int max_ctx = 0;
   unsigned short* kv = nullptr;   // [n_attn][2][max_ctx][NKV][HD]
   bf16_t* ring = nullptr;         // [n_conv][W][H]
-  float* rope_cos = nullptr;      // [max_ctx][half]
+  float* rope_cos = nullptr;      // [max_ctx][half] of the full-attention layers
   float* rope_sin = nullptr;
+  float* rope_cos_s = nullptr;    // [max_ctx][half_s] of the sliding-attention layers
+  float* rope_sin_s = nullptr;
   bf16_t* res[3] = {nullptr, nullptr, nullptr};
   bf16_t* h_first = nullptr;      // q|k|v|gate or in_proj output
   bf16_t* h_attn = nullptr;
@@ -379,6 +388,22 @@ namespace {
 size_t align256(size_t x) { return (x + 255) & ~(size_t)255; }
 
 int half_rot(const pb_model* m) { return (int)((double)m->partial * m->HD) / 2; }
+int half_rot_s(const pb_model* m) { return (int)((double)m->partial_s * m->HD) / 2; }
+// per attention layer: rotated pairs, key window, RoPE tables
+int layer_half(const pb_model* m, int L) { return m->layers[L].slide ? half_rot_s(m) : half_rot(m); }
+int layer_win(const pb_model* m, int L) { return m->layers[L].slide ? m->win_s : m->win; }
+const float* layer_cos(const pb_state* s, int L) { return s->m->layers[L].slide ? s->rope_cos_s : s->rope_cos; }
+const float* layer_sin(const pb_state* s, int L) { return s->m->layers[L].slide ? s->rope_sin_s : s->rope_sin; }
+// the longest attention span any layer of the model reads at max_ctx
+int max_span(const pb_model* m, int max_ctx) {
+  int span = 0;
+  for (int L = 0; L < m->L; L++)
+    if (m->layers[L].attn) {
+      const int w = layer_win(m, L);
+      span = std::max(span, (w > 0 && w < max_ctx) ? w : max_ctx);
+    }
+  return span > 0 ? span : 1;
+}
 
 // ---- launches ---------------------------------------------------------------
 size_t step_smem(int K, int H) { return (size_t)(K + K / 32 + 2 * H) * sizeof(float); }
@@ -441,14 +466,15 @@ int launch_attn(const pb_model* m, pb_state* s, int layer, cudaStream_t st, bool
   a.qkvg = s->h_first;
   a.qnorm = Ly.q_norm;
   a.knorm = Ly.k_norm;
-  a.rope_cos = s->rope_cos;
-  a.rope_sin = s->rope_sin;
+  a.rope_cos = layer_cos(s, layer);
+  a.rope_sin = layer_sin(s, layer);
   const size_t per = (size_t)s->max_ctx * m->NKV * m->HD;
   a.kc = s->kv + (size_t)Ly.attn_idx * 2 * per;
   a.vc = a.kc + per;
   a.out = s->h_attn;
   a.ctl = s->ctl;
-  a.nh = m->NH; a.nkv = m->NKV; a.half = half_rot(m); a.win = m->win; a.max_ctx = s->max_ctx;
+  a.nh = m->NH; a.nkv = m->NKV; a.half = layer_half(m, layer); a.win = layer_win(m, layer);
+  a.max_ctx = s->max_ctx;
   a.scaling = 1.0f / sqrtf((float)m->HD);
   a.eps = m->eps;
   cudaLaunchConfig_t cfg = {};
@@ -708,14 +734,15 @@ AttnArgs attn_args(const pb_model* m, pb_state* s, int layer) {
   a.qkvg = s->h_first;
   a.qnorm = Ly.q_norm;
   a.knorm = Ly.k_norm;
-  a.rope_cos = s->rope_cos;
-  a.rope_sin = s->rope_sin;
+  a.rope_cos = layer_cos(s, layer);
+  a.rope_sin = layer_sin(s, layer);
   const size_t per = (size_t)s->max_ctx * m->NKV * m->HD;
   a.kc = s->kv + (size_t)Ly.attn_idx * 2 * per;
   a.vc = a.kc + per;
   a.out = s->h_attn;
   a.ctl = s->ctl;
-  a.nh = m->NH; a.nkv = m->NKV; a.half = half_rot(m); a.win = m->win; a.max_ctx = s->max_ctx;
+  a.nh = m->NH; a.nkv = m->NKV; a.half = layer_half(m, layer); a.win = layer_win(m, layer);
+  a.max_ctx = s->max_ctx;
   a.scaling = 1.0f / sqrtf((float)m->HD);
   a.eps = m->eps;
   a.scores = s->att_scores;
@@ -800,7 +827,7 @@ int build_phases(pb_state* s) {
   // input, then its row values (at most ceil(row blocks / CTAs) stages of 16
   // chunk values per CTA); the score phase's q and k per warp; the P.V
   // phase's V chunk (32 KB), scores, partials, current v row and gate
-  const int span = (m->win > 0 && m->win < s->max_ctx) ? m->win : s->max_ctx;
+  const int span = max_span(m, s->max_ctx);
   const int dq = m->HD / 4;
   int xr = std::max(DWARPS * 2 * m->HD, 32768 / 4 + ((span + 3) & ~3) + 9 * dq + 4);
   const int G = pb_num_sms();
@@ -1064,6 +1091,23 @@ extern "C" int pb_open(const char* path, int device, pb_model** out) {
   m->theta = (float)cnum("rope_theta", 1e6);
   m->partial = (float)cnum("partial_rotary_factor", 1.0);
   m->eps = (float)cnum("norm_eps", 1e-5);
+  // sliding-attention layers: window and RoPE of their own (top-level keys,
+  // or the per-type rope_parameters object of the HF config)
+  m->win_s = (int)cint("sliding_window", 256);
+  m->theta_s = (float)cnum("sliding_rope_theta", 1e4);
+  m->partial_s = (float)cnum("sliding_partial_rotary_factor", 1.0);
+  if (const pbjson::Value* rp = cfg->get("rope_parameters")) {
+    if (rp->kind == pbjson::Value::OBJ) {
+      if (const pbjson::Value* fa = rp->get("full_attention")) {
+        if (const pbjson::Value* v = fa->get("rope_theta")) m->theta = (float)v->as_num(m->theta);
+        if (const pbjson::Value* v = fa->get("partial_rotary_factor")) m->partial = (float)v->as_num(m->partial);
+      }
+      if (const pbjson::Value* sa = rp->get("sliding_attention")) {
+        if (const pbjson::Value* v = sa->get("rope_theta")) m->theta_s = (float)v->as_num(m->theta_s);
+        if (const pbjson::Value* v = sa->get("partial_rotary_factor")) m->partial_s = (float)v->as_num(m->partial_s);
+      }
+    }
+  }
   const pbjson::Value* lt = cfg->get("layer_types");
   auto bad = [&](int code, const char* msg) { fclose(f); delete m; return pb_set_error(code, "pb_open: %s", msg); };
   if (m->H <= 0 || m->F <= 0 || m->L <= 0 || m->NH <= 0 || m->NKV <= 0 || m->HD <= 0 || m->V <= 0 || m->W <= 0)
@@ -1120,6 +1164,8 @@ extern "C" int pb_open(const char* path, int device, pb_model** out) {
     const pbjson::Value& v = lt->arr[L];
     if (v.kind != pbjson::Value::STR) return bad(PB_EFORMAT, "layer_types entries must be strings");
     m->layers[L].attn = v.str != "conv";
+    m->layers[L].slide = v.str == "sliding_attention";
+    m->any_slide = m->any_slide || m->layers[L].slide;
     if (m->layers[L].attn) m->layers[L].attn_idx = n_attn++;
     else m->layers[L].conv_idx = n_conv++;
   }
@@ -1274,12 +1320,15 @@ extern "C" int pb_open(const char* path, int device, pb_model** out) {
   if (st) cudaStreamDestroy(st);
   fclose(f);
   if (rc != PB_OK) { cudaFree(m->arena); delete m; return rc; }
-  m->invf.resize(m->HD / 2);
-  {
-    const int angles = (int)((double)m->partial * m->HD) / 2;
+  // build_invf (lfm3_nanode.cu:3719-3723) for each attention layer type
+  auto invf = [&](std::vector<float>& out, float base, float partial) {
+    out.resize(m->HD / 2);
+    const int angles = (int)((double)partial * m->HD) / 2;
     for (int i = 0; i < m->HD / 2; i++)
-      m->invf[i] = (i < angles) ? 1.0f / powf(m->theta, (float)(2 * i) / (float)m->HD) : 0.0f;
-  }
+      out[i] = (i < angles) ? 1.0f / powf(base, (float)(2 * i) / (float)m->HD) : 0.0f;
+  };
+  invf(m->invf, m->theta, m->partial);
+  invf(m->invf_s, m->theta_s, m->partial_s);
   *out = m;
   return PB_OK;
 }
@@ -1322,20 +1371,20 @@ extern "C" int pb_state_create(pb_model* m, int max_ctx, pb_state** out) {
     const char* mode = getenv("PB_DECODE_MODE");   // "graph": the per-kernel CUDA-graph path
     s->persistent = !(mode && strcmp(mode, "graph") == 0);
     // the persistent softmax holds a head's scores in registers (64 per lane)
-    const int span = (m->win > 0 && m->win < max_ctx) ? m->win : max_ctx;
-    if (span > 2048 || !persistent_shape(m)) s->persistent = false;
+    if (max_span(m, max_ctx) > 2048 || !persistent_shape(m)) s->persistent = false;
   }
-  const int H = m->H, n_conv = m->L - m->n_attn, half = half_rot(m);
+  const int H = m->H, n_conv = m->L - m->n_attn, half = half_rot(m), half_s = half_rot_s(m);
   const size_t kvb = (size_t)m->n_attn * 2 * max_ctx * m->NKV * m->HD * 2;
   const size_t ringb = (size_t)n_conv * m->W * H * 2;
   const size_t ropeb = (size_t)max_ctx * (half > 0 ? half : 1) * 4;
+  const size_t ropeb_s = m->any_slide ? (size_t)max_ctx * (half_s > 0 ? half_s : 1) * 4 : 0;
   const size_t firstn = std::max((size_t)3 * H, (size_t)m->NH * m->HD + 2 * (size_t)m->NKV * m->HD + m->NH);
   size_t sizes[] = {kvb, ringb, ropeb, ropeb, (size_t)H * 2, (size_t)H * 2, (size_t)H * 2, firstn * 2,
                     (size_t)m->NH * m->HD * 2, (size_t)H * 2, (size_t)m->F * 2, (size_t)H * 2,
                     (size_t)m->V * 4, sizeof(Ctl), 256, 256, (size_t)m->NH * max_ctx * 4, (size_t)m->NH * 4,
                     (size_t)m->NH * 8 * m->HD * 4,
                     firstn * 4, (size_t)m->NH * m->HD * 4, (size_t)H * 4, (size_t)m->F * 4, (size_t)H * 4,
-                    (size_t)m->NH * max_ctx * 8};
+                    (size_t)m->NH * max_ctx * 8, ropeb_s, ropeb_s};
   size_t tot = 0;
   for (size_t x : sizes) tot += align256(x);
   if (cudaMalloc(&s->mem, tot) != cudaSuccess) { cudaGetLastError(); delete s; return pb_set_error(PB_ENOMEM, "pb_state_create: %zu bytes", tot); }
@@ -1347,24 +1396,31 @@ extern "C" int pb_state_create(pb_model* m, int max_ctx, pb_state** out) {
                     (void**)&s->logits, (void**)&s->ctl, (void**)&s->d_bar, (void**)&s->d_err,
                     (void**)&s->att_scores, (void**)&s->att_inv, (void**)&s->att_segp,
                     (void**)&s->t_first, (void**)&s->t_attn, (void**)&s->t_mix, (void**)&s->t_u, (void**)&s->t_w2,
-                    (void**)&s->t_scores};
+                    (void**)&s->t_scores, (void**)&s->rope_cos_s, (void**)&s->rope_sin_s};
   for (size_t i = 0; i < sizeof(sizes) / sizeof(sizes[0]); i++) { *slots[i] = p; p += align256(sizes[i]); }
   s->tag_bytes = (size_t)((char*)s->t_scores - (char*)s->t_first) + align256((size_t)m->NH * max_ctx * 8);
   if (cudaMallocHost(&s->h_ctl, sizeof(Ctl) + 16) != cudaSuccess) {
     cudaGetLastError(); cudaFree(s->mem); delete s;
     return pb_set_error(PB_ENOMEM, "pb_state_create: pinned control block");
   }
-  // RoPE table on the host: angle (float)pos * invf[i] in fp32 (lfm3_nanode.cu:492),
-  // cos/sin evaluated in double and rounded once to float
-  std::vector<float> hc((size_t)max_ctx * (half > 0 ? half : 1)), hs(hc.size());
-  for (int pos = 0; pos < max_ctx; pos++)
-    for (int i = 0; i < half; i++) {
-      const float ang = (float)pos * m->invf[i];
-      hc[(size_t)pos * half + i] = (float)cos((double)ang);
-      hs[(size_t)pos * half + i] = (float)sin((double)ang);
-    }
-  if (cudaMemcpy(s->rope_cos, hc.data(), hc.size() * 4, cudaMemcpyHostToDevice) != cudaSuccess ||
-      cudaMemcpy(s->rope_sin, hs.data(), hs.size() * 4, cudaMemcpyHostToDevice) != cudaSuccess) {
+  // RoPE tables on the host, one per attention layer type: angle (float)pos *
+  // invf[i] in fp32 (lfm3_nanode.cu:492), cos/sin evaluated in double and
+  // rounded once to float
+  auto table = [&](const std::vector<float>& invf, int hf, float* dc, float* dsn) -> bool {
+    std::vector<float> hc((size_t)max_ctx * (hf > 0 ? hf : 1)), hs(hc.size());
+    for (int pos = 0; pos < max_ctx; pos++)
+      for (int i = 0; i < hf; i++) {
+        const float ang = (float)pos * invf[i];
+        hc[(size_t)pos * hf + i] = (float)cos((double)ang);
+        hs[(size_t)pos * hf + i] = (float)sin((double)ang);
+      }
+    return cudaMemcpy(dc, hc.data(), hc.size() * 4, cudaMemcpyHostToDevice) == cudaSuccess &&
+           cudaMemcpy(dsn, hs.data(), hs.size() * 4, cudaMemcpyHostToDevice) == cudaSuccess;
+  };
+  bool rope_ok = table(m->invf, half, s->rope_cos, s->rope_sin);
+  if (m->any_slide) rope_ok = rope_ok && table(m->invf_s, half_s, s->rope_cos_s, s->rope_sin_s);
+  else { s->rope_cos_s = s->rope_cos; s->rope_sin_s = s->rope_sin; }
+  if (!rope_ok) {
     cudaFreeHost(s->h_ctl); cudaFree(s->mem); delete s;
     return pb_set_error(PB_ECUDA, "pb_state_create: rope upload");
   }
@@ -1786,11 +1842,11 @@ extern "C" int pb_layer_step_noalloc(pb_model* m, pb_state* s, int layer, int po
   if (Ly.attn) {
     AttnArgs t;
     t.qkvg = b.h_first; t.qnorm = Ly.q_norm; t.knorm = Ly.k_norm;
-    t.rope_cos = s->rope_cos; t.rope_sin = s->rope_sin;
+    t.rope_cos = layer_cos(s, layer); t.rope_sin = layer_sin(s, layer);
     const size_t per = (size_t)s->max_ctx * m->NKV * m->HD;
     t.kc = s->kv + (size_t)Ly.attn_idx * 2 * per; t.vc = t.kc + per;
     t.out = b.h_attn; t.ctl = b.ctl;
-    t.nh = m->NH; t.nkv = m->NKV; t.half = half_rot(m); t.win = m->win; t.max_ctx = s->max_ctx;
+    t.nh = m->NH; t.nkv = m->NKV; t.half = layer_half(m, layer); t.win = layer_win(m, layer); t.max_ctx = s->max_ctx;
     t.scaling = 1.0f / sqrtf((float)m->HD); t.eps = m->eps;
     const size_t sm = (size_t)s->max_ctx * sizeof(float);
     switch (m->HD) {
@@ -1933,11 +1989,11 @@ extern "C" int pb_prefill_chunk(pb_model* m, pb_state* s, const int* d_tokens, i
       q.y = s->pf_y;
       q.qkvg = s->pf_qkvg;
       q.knorm = Ly.k_norm;
-      q.rope_cos = s->rope_cos;
-      q.rope_sin = s->rope_sin;
+      q.rope_cos = layer_cos(s, L);
+      q.rope_sin = layer_sin(s, L);
       q.kc = s->kv + (size_t)Ly.attn_idx * 2 * per;
       q.vc = q.kc + per;
-      q.nq = nq; q.nh = m->NH; q.nkv = m->NKV; q.half = half_rot(m); q.pos0 = pos0; q.eps = m->eps;
+      q.nq = nq; q.nh = m->NH; q.nkv = m->NKV; q.half = layer_half(m, L); q.pos0 = pos0; q.eps = m->eps;
       k_pf_qkv<2><<<T, 256, 0, st>>>(q);
       PB_LAUNCHED("k_pf_qkv");
       AttnArgs a = attn_args(m, s, L);
@@ -2030,6 +2086,7 @@ extern "C" int pb_decode_batch(pb_model* m, pb_state* const* states, int B, cons
       for (int b = 0; b < B; b++) {
         const pb_state* s = states[b];
         h[b].kv = s->kv; h[b].ring = s->ring; h[b].rope_cos = s->rope_cos; h[b].rope_sin = s->rope_sin;
+        h[b].rope_cos_s = s->rope_cos_s; h[b].rope_sin_s = s->rope_sin_s;
         h[b].max_ctx = s->max_ctx; h[b]._pad = 0;
       }
       if (g_bt.cap < (size_t)B) {
@@ -2069,7 +2126,8 @@ extern "C" int pb_decode_batch(pb_model* m, pb_state* const* states, int B, cons
       a.knorm = Ly.k_norm;
       a.att = ws->pf_att;
       a.attn_idx = Ly.attn_idx;
-      a.nq = nq; a.nh = m->NH; a.nkv = m->NKV; a.half = half_rot(m); a.win = m->win;
+      a.nq = nq; a.nh = m->NH; a.nkv = m->NKV; a.half = layer_half(m, L); a.win = layer_win(m, L);
+      a.slide = Ly.slide ? 1 : 0;
       a.eps = m->eps;
       a.scaling = 1.0f / sqrtf((float)m->HD);
       k_bd_qkv<2><<<B, 256, 0, st>>>(a);

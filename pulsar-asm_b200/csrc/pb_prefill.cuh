@@ -261,8 +261,10 @@ namespace {
 struct SeqPtrs {
   unsigned short* kv;       // [n_attn][2][max_ctx][NKV][HD]
   bf16_t* ring;             // [n_conv][W][H]
-  const float* rope_cos;    // [max_ctx][half]
+  const float* rope_cos;    // [max_ctx][half]: full-attention layers
   const float* rope_sin;
+  const float* rope_cos_s;  // [max_ctx][half]: sliding-attention layers
+  const float* rope_sin_s;
   int max_ctx;
   int _pad;
 };
@@ -277,6 +279,7 @@ struct BdArgs {
   bf16_t* att;              // [B][NH*HD]
   int attn_idx, nq, nh, nkv, half, win;
   float eps, scaling;
+  int slide;                // the layer's RoPE table: 1 sliding, 0 full
 };
 
 // per sequence: the bf16 projection row and its new K/V rows
@@ -296,8 +299,8 @@ __global__ void __launch_bounds__(256) k_bd_qkv(BdArgs p) {
   const size_t koff = (size_t)p.nh * HD, voff = koff + (size_t)p.nkv * HD;
   const bf16_t* row = p.qkvg + (size_t)b * p.nq;
   for (int kvh = warp; kvh < p.nkv; kvh += 8) {
-    head_norm_rope<E, 0>(row + koff + (size_t)kvh * HD, p.knorm, sq.rope_cos + (size_t)pos * p.half,
-                         sq.rope_sin + (size_t)pos * p.half, p.half, p.eps, ks[warp]);
+    head_norm_rope<E, 0>(row + koff + (size_t)kvh * HD, p.knorm, (p.slide ? sq.rope_cos_s : sq.rope_cos) + (size_t)pos * p.half,
+                         (p.slide ? sq.rope_sin_s : sq.rope_sin) + (size_t)pos * p.half, p.half, p.eps, ks[warp]);
 #pragma unroll
     for (int j = 0; j < E; j++) {
       const int i = lane * E + j;
@@ -322,8 +325,8 @@ __global__ void __launch_bounds__(256) k_bd_attn(BdArgs p) {
   a.qkvg = p.qkvg + (size_t)b * p.nq;
   a.qnorm = p.qnorm;
   a.knorm = p.knorm;
-  a.rope_cos = sq.rope_cos;
-  a.rope_sin = sq.rope_sin;
+  a.rope_cos = p.slide ? sq.rope_cos_s : sq.rope_cos;
+  a.rope_sin = p.slide ? sq.rope_sin_s : sq.rope_sin;
   const size_t per = (size_t)sq.max_ctx * p.nkv * HD;
   a.kc = sq.kv + (size_t)p.attn_idx * 2 * per;
   a.vc = a.kc + per;

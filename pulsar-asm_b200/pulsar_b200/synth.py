@@ -19,17 +19,24 @@ LFM3_TINY = dict(hidden=2048, inter=2048, n_layers=4, n_heads=32, n_kv=8, head_d
 
 
 def layer_types(c):
-    return ["full_attention" if i in c["attn_layers"] else "conv" for i in range(c["n_layers"])]
+    """conv, full_attention, or sliding_attention (layers listed in slide_layers)"""
+    slide = set(c.get("slide_layers", ()))
+    return [("sliding_attention" if i in slide else "full_attention") if i in c["attn_layers"] else "conv"
+            for i in range(c["n_layers"])]
 
 
 def hf_cfg(c):
     """the blob header's cfg object (HF-style keys the loader reads)."""
-    return dict(hidden_size=c["hidden"], intermediate_size=c["inter"],
-                num_hidden_layers=c["n_layers"], num_attention_heads=c["n_heads"],
-                num_key_value_heads=c["n_kv"], head_dim=c["head_dim"], vocab_size=c["vocab"],
-                conv_L_cache=c["conv_w"], rope_theta=c["rope_theta"],
-                partial_rotary_factor=c["rope_partial"], norm_eps=c["norm_eps"],
-                layer_types=layer_types(c))
+    d = dict(hidden_size=c["hidden"], intermediate_size=c["inter"],
+             num_hidden_layers=c["n_layers"], num_attention_heads=c["n_heads"],
+             num_key_value_heads=c["n_kv"], head_dim=c["head_dim"], vocab_size=c["vocab"],
+             conv_L_cache=c["conv_w"], rope_theta=c["rope_theta"],
+             partial_rotary_factor=c["rope_partial"], norm_eps=c["norm_eps"],
+             layer_types=layer_types(c))
+    if c.get("slide_layers"):
+        d.update(sliding_window=c.get("slide_window", 256), sliding_rope_theta=c.get("slide_theta", 1e4),
+                 sliding_partial_rotary_factor=c.get("slide_partial", 1.0))
+    return d
 
 
 def oracle_cfg(c, max_ctx):

@@ -138,3 +138,31 @@ def test_corrupt_blob_rejected_on_device_open(tmp_path, pb, cuda):
     with pytest.raises(pb.PBError) as e:
         pb.Model(path)
     assert e.value.code == -5
+
+
+def test_full_and_sliding_attention_layers(tmp_path, oracle, pb, cuda):
+    """per-layer attention types as the reference builds them
+    (lfm3_nanode.cu:3753-3785): a full-attention layer rotating half of the
+    head dims with base 1e6 over every key, and a sliding-attention layer
+    rotating all of them with base 1e4 over the last 8 keys; 40 positions, so
+    the window slides, through the persistent kernel; bit-exact"""
+    torch = cuda
+    from pulsar_b200 import synth
+    c = dict(synth.LFM3_TINY, n_layers=4, attn_layers=(1, 3), slide_layers=(3,), rope_partial=0.5,
+             slide_window=8, slide_theta=1e4, slide_partial=1.0, vocab=1024)
+    w = synth.make_weights(c, seed=404)
+    path = str(tmp_path / "slide.lfm3q8")
+    synth.write_model(path, c, w)
+    m = pb.Model(path)
+    max_ctx = 48
+    s = m.new_state(max_ctx)
+    om = oracle.Model(synth.oracle_cfg(c, max_ctx), w)
+    logits = torch.empty(c["vocab"], dtype=torch.float32, device="cuda")
+    tok = 17
+    for pos in range(40):
+        got = s.decode_token(tok, pos, logits=logits)
+        want, lg, _ = om.decode(tok, pos, want_logits=True)
+        torch.cuda.synchronize()
+        assert np.array_equal(_bits32(logits.cpu().numpy()), _bits32(lg)), "logits differ at pos %d" % pos
+        assert got == want
+        tok = got
