@@ -260,3 +260,22 @@ WRAP
   rm -f "$out/refgpu.cu"
   echo "build_ref: built $out/libpb_refgpu.so"
 fi
+
+# --- G: the reference's x86/C CPU Q8 GEMV, unmodified, for timing: its own
+#        flags (.auto/lfm3/q8_gemv_cpu.c:16, -fopenmp -ffp-contract=off) at -O3,
+#        once for the baseline x86-64 ISA and once for x86-64-v3 (AVX2); the
+#        second arm stands in for -march=native because this build runs off the
+#        GPU box, whose host CPU may differ. Timed by bench.py (cpu_reference).
+Q8C="$REF/.auto/lfm3/q8_gemv_cpu.c"
+for arm in O3 v3; do
+  extra=""; [ "$arm" = v3 ] && extra="-march=x86-64-v3"
+  {
+    printf '#define main pbref_q8_gemv_cpu_main\n#include "%s"\n#undef main\n' "$Q8C"
+    cat <<'WRAP'
+void pbref_gemv_q8(const signed char* q, const float* s, const float* x, float* y, int N, int K) { gemv_q8(q, s, x, y, N, K); }
+void pbref_quant_row(const float* w, int K, signed char* q, float* s) { quant_row(w, K, q, s); }
+void pbref_set_threads(int n) { omp_set_num_threads(n); }
+WRAP
+  } | "$CC" -O3 -fPIC -fopenmp -ffp-contract=off -w $extra -shared -x c -o "$out/libpb_q8cpu_$arm.so" - -lm
+  echo "build_ref: built $out/libpb_q8cpu_$arm.so"
+done
