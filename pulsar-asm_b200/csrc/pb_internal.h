@@ -30,7 +30,7 @@ void pb_set_capturing(bool on);
   } while (0)
 
 // Q8 tensor layouts
-// PB_Q8_UMMA: 128-row tiles in the tensor cores' K-major core-matrix order,
+// PB_Q8_UMMA: 128-row tiles in the tensor cores' K-major 128-byte-swizzle order,
 // fp32 scales [tile][block][128] (pb_q80tc_pack; only pb_q80_gemm reads it)
 enum { PB_Q8_ROWMAJOR = 0, PB_Q8_STREAM = 1, PB_Q8_UMMA = 2 };
 

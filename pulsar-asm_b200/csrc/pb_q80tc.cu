@@ -9,24 +9,18 @@
 // accumulator (no accumulation across blocks in the tensor core) and the
 // epilogue warps fold the blocks in order in fp32.
 //
-// CTA = 6 warps, one 128-row tile of W and 16 of the T positions (grid
-// tiles x T/16; the CTAs of one tile run side by side and share its weights
-// in L2), two CTAs per SM:
-//   warp 0  lane 0: TMA producer, 1-D bulk copies of each stage (8 blocks of
-//                   weights, activations and their scales) into a ring of NS
-//                   shared-memory stages (full/empty mbarriers);
-//   warp 1  lane 0: MMA issuer, one tcgen05.mma (M 128, N 16, K 32) per block
-//                   into one of NB TMEM buffers of 16 columns, tcgen05.commit
-//                   to the buffer's mbarrier; warp 1 also allocates and frees
-//                   the TMEM;
-//   warps 2-5:      epilogue, TMEM lane quarter warp % 4: tcgen05.ld of BK
-//                   blocks' int32 tiles at a time, release of the buffers,
-//                   fp32 fold in block order (int32 -> fp32 by the exact
-//                   2^23 + 2^22 exponent trick: |isum| < 2^22).
-// Operands sit in shared memory in the canonical K-major no-swizzle layout:
-// 8-row x 16-byte core matrices, the two 16-byte halves of a block 128 bytes
-// apart (leading byte offset), 8-row groups 256 bytes apart (stride byte
-// offset). The weights are stored that way in HBM at pack time and the
+// CTA = 10 warps, one 128-row tile of W and TS (16, 32 or 64) of the T
+// positions: a TMA producer warp, an MMA warp and eight epilogue warps (two
+// per TMEM lane quarter, each folding half of the positions); see k_q80tc.
+// The weight scales keep the tensor's own dtype (fp16 for Q8_0, fp32 for the
+// .lfm3q8 dtype-1 format).
+// Operands sit in shared memory in the K-major 128-byte-swizzle layout: a
+// stage's 8 blocks (256 bytes of K per row) are two 128-byte-wide column
+// slabs of 128-byte rows, 8-row groups 1024 bytes apart, the 16-byte chunk c
+// of row r stored at chunk c ^ (r & 7); the MMA of block j starts at slab
+// j / 4, byte (j % 4) * 32. (The no-swizzle core-matrix layout feeds the
+// tensor cores about 16 bytes a cycle: an M128 N32 K32 MMA then takes some 500
+// cycles.) The weights are stored that way in HBM at pack time and the
 // activations are re-laid once per call, so every stage is four contiguous
 // bulk copies. All waits are bounded; a wait that gives up records an error,
 // every role leaves its loop, the issuer waits (bounded) for its MMAs and the
@@ -41,11 +35,12 @@ namespace {
 constexpr int TC_M = 128;            // rows per tile (MMA M)
 constexpr int TC_CB = 8;             // 32-code blocks per stage
 constexpr unsigned TC_WAIT = 1u << 24;
+constexpr unsigned long long TC_WAIT_NS = 1000000000ull;   // a wait gives up after about a second
 
 struct TcArgs {
-  const int8_t* a;     // weights [tile][block][16 groups][2 halves][8 rows][16 bytes]
-  const float* dw;     // weight scales [tile][block][128]
-  const int8_t* b;     // activations [block][T/8 groups][2 halves][8 rows][16 bytes]
+  const int8_t* a;     // weights [tile][stage][128 rows x 256 bytes, 128-byte swizzle]
+  const void* dw;      // weight scales [tile][block][128] (fp16 or fp32, the tensor's dtype)
+  const int8_t* b;     // activations [T/TS][stage][TS rows x 256 bytes, 128-byte swizzle]
   const float* dx;     // activation scales [block][T]
   float* y;            // [T][N]
   int32_t* isum;       // optional [T][N][K/32]
@@ -72,22 +67,47 @@ PB_DEV bool mb_try(uint64_t* b, unsigned par) {
 // bounded wait; false when it gave up or another role aborted
 // (try_wait itself suspends the thread until the phase completes or a short
 // hardware time limit passes, so the loop needs no sleep)
+PB_DEV unsigned long long tc_now() {
+  unsigned long long t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
 PB_DEV bool mb_wait(uint64_t* b, unsigned par, volatile int* abort_f) {
+  if (mb_try(b, par)) return true;
+  const unsigned long long t0 = tc_now();
   for (unsigned i = 0; i < TC_WAIT; i++) {
     if (mb_try(b, par)) return true;
-    if ((i & 255) == 255 && *abort_f) return false;
+    if ((i & 63) == 63 && (*abort_f || tc_now() - t0 > TC_WAIT_NS)) return false;
   }
   return false;
+}
+// wait for a phase whatever the other roles did (in-flight copies and MMAs
+// before exit), bounded by time
+PB_DEV void mb_drain(uint64_t* b, unsigned par) {
+  const unsigned long long t0 = tc_now();
+  for (unsigned i = 0; !mb_try(b, par); i++)
+    if ((i & 63) == 63 && tc_now() - t0 > TC_WAIT_NS) return;
+}
+// the same, by a whole warp, with one answer for every lane
+PB_DEV bool mb_wait_warp(uint64_t* b, unsigned par, volatile int* abort_f) {
+  return __all_sync(0xffffffffu, mb_wait(b, par, abort_f));
 }
 PB_DEV void bulk(void* dst, const void* src, unsigned bytes, uint64_t* bar) {
   asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
                ::"r"(s32(dst)), "l"(src), "r"(bytes), "r"(s32(bar)) : "memory");
 }
-// K-major, no swizzle: LBO 128 B between the block's two 16-byte halves,
-// SBO 256 B between 8-row groups, descriptor version 1 (sm_100)
+// K-major, 128-byte swizzle (layout type 2, bits 61-63): LBO 16 B (unused by
+// swizzled K-major layouts), SBO 1024 B between 8-row groups, descriptor
+// version 1 (sm_100, bits 46-47), base offset 0 (slabs are 1024-byte aligned)
 PB_DEV uint64_t umma_desc(uint32_t saddr) {
-  return (uint64_t)((saddr >> 4) & 0x3FFFu) | ((uint64_t)(128 >> 4) << 16) | ((uint64_t)(256 >> 4) << 32) |
-         (1ull << 46);
+  return (uint64_t)((saddr >> 4) & 0x3FFFu) | (1ull << 16) | ((uint64_t)(1024 >> 4) << 32) | (1ull << 46) |
+         (2ull << 61);
+}
+// byte offset of (row r, K byte c of the stage, c < 256) in a stage region of
+// R rows (R a multiple of 8) in the 128-byte-swizzle layout
+PB_DEV size_t tc_sw(int r, int c, int R) {
+  return (size_t)(c >> 7) * (R * 128) + (size_t)(r >> 3) * 1024 + (r & 7) * 128 + ((((c >> 4) & 7) ^ (r & 7)) << 4) +
+         (c & 15);
 }
 PB_DEV void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
 PB_DEV void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
@@ -112,167 +132,290 @@ PB_DEV void tc_ld8(uint32_t taddr, int32_t* v) {
 }
 PB_DEV void tc_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 
-constexpr int TC_TS = 16;            // positions per CTA (MMA N)
-constexpr int TC_NB = 16;            // TMEM buffers of 16 columns
-constexpr int TC_BK = 4;             // blocks per epilogue step
-constexpr int TC_SA = TC_M * 32 * TC_CB;       // weights of a stage
-constexpr int TC_SB = TC_TS * 32 * TC_CB;      // activations
-constexpr int TC_SW = TC_CB * TC_M * 4;        // weight scales
-constexpr int TC_SX = TC_CB * TC_TS * 4;       // activation scales
-constexpr int TC_STAGE = TC_SA + TC_SB + TC_SW + TC_SX;
-constexpr int TC_NS = 2;
+// 8 consecutive / 16 / 32 int32 columns of this thread's TMEM lane
+PB_DEV void tc_ld16(uint32_t taddr, int32_t* v) {
+  asm volatile("tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, "
+               "%14, %15}, [%16];"
+               : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7]),
+                 "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]), "=r"(v[15])
+               : "r"(taddr));
+}
+template <int NC>
+PB_DEV void tc_ld_cols(uint32_t taddr, int32_t* v) {
+#pragma unroll
+  for (int c = 0; c < NC; c += 16) {
+    if (NC - c >= 16) tc_ld16(taddr + (uint32_t)c, v + c);
+    else tc_ld8(taddr + (uint32_t)c, v + c);
+  }
+}
 
-PB_DEV float i2f_exact(int32_t v) { return __fsub_rn(__int_as_float(v + 0x4B400000), 12582912.0f); }
+constexpr int TC_NS = 4;             // shared-memory stages
+constexpr int TC_EW = 16;            // epilogue warps: four per TMEM lane quarter
 
-__global__ void __launch_bounds__(192, 2) k_q80tc(TcArgs p) {
-  extern __shared__ __align__(1024) unsigned char tsm[];
-  __shared__ uint64_t full[TC_NS], empty[TC_NS], tfull[TC_NB], tempty[TC_NB], done;
+// shared-memory geometry of one stage for TS positions per CTA and weight
+// scales of SB bytes
+template <int TS, int SB>
+struct TcGeo {
+  static constexpr int SA = TC_M * 32 * TC_CB;       // weights
+  static constexpr int SBX = TS * 32 * TC_CB;        // activations
+  static constexpr int SW = TC_CB * TC_M * SB;       // weight scales
+  static constexpr int SX = TC_CB * TS * 4;          // activation scales (fp32)
+  static constexpr int BYTES = SA + SBX + SW + SX;                // copied per stage
+  static constexpr int STAGE = (BYTES + 1023) / 1024 * 1024;     // stride: slabs stay 1024-aligned
+  static constexpr int NB = (512 / TS) < 16 ? (512 / TS) : 16;   // TMEM buffers of TS columns
+  // blocks per TMEM group (one handshake per group): the epilogue holds two
+  // groups' columns, 2 GB TS/4 registers, within its budget of 96
+  static constexpr int GB = 64 / TS;
+  static constexpr int NG = NB / GB;                 // buffer groups
+  static constexpr int SMEM = TC_NS * STAGE + 1024;  // + room to align the base
+};
+
+// packed fp32 pairs; every operation rounds on its own (explicit .rn: no
+// contraction into an fma)
+typedef unsigned long long tc_f2;
+PB_DEV tc_f2 tc_pk(float a, float b) {
+  tc_f2 r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(a), "f"(b));
+  return r;
+}
+PB_DEV void tc_upk(tc_f2 v, float& a, float& b) { asm("mov.b64 {%0, %1}, %2;" : "=f"(a), "=f"(b) : "l"(v)); }
+PB_DEV tc_f2 tc_mul2(tc_f2 a, tc_f2 b) {
+  tc_f2 d;
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+PB_DEV tc_f2 tc_add2(tc_f2 a, tc_f2 b) {
+  tc_f2 d;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+// two int32 block dots -> fp32, exactly (|isum| < 2^22): the integer is added
+// to the mantissa of 1.5 * 2^23 and the bias subtracted
+PB_DEV tc_f2 tc_i2f2(int32_t a, int32_t b) {
+  tc_f2 r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "r"(a + 0x4B400000), "r"(b + 0x4B400000));
+  return tc_add2(r, tc_pk(-12582912.0f, -12582912.0f));
+}
+
+// CTA = 18 warps, one 128-row tile of W and TS of the T positions (grid
+// tiles x T/TS; for T <= 64 every weight byte is read once):
+//   warp 0:     TMA producer (lane 0 issues), 1-D bulk copies of each stage
+//               (8 blocks of weights, activations and their scales) into a
+//               ring of TC_NS shared-memory stages (full/empty mbarriers);
+//   warp 1:     MMA issuer (lane 0 issues), one tcgen05.mma (M 128, N TS,
+//               K 32) per block into one of NB TMEM buffers of TS columns, one
+//               tcgen05.commit per group of GB blocks; warp 1 allocates and
+//               frees the TMEM (all 512 columns: one CTA per SM);
+//   warps 2-17: epilogue; warp w reads TMEM lane quarter w % 4 and a
+//               quarter of the positions, (w - 2) / 4: per group one wait,
+//               tcgen05.ld of its columns of the group's blocks (issued a
+//               group ahead of the fold), release of the group's buffers,
+//               fp32 fold in block order (products two positions per packed
+//               multiply, the accumulation scalar).
+// The issuing loops run one stage per iteration with every block of the
+// stage unrolled: a single issuing thread runs its instructions back to back,
+// so each index or descriptor computed at run time costs tens of cycles per
+// MMA (a loop computing them per block issued one M128 N32 MMA per 470
+// cycles; precomputed descriptors plus constants reach about 50).
+template <int TS, typename ST>
+__global__ void __launch_bounds__(32 * (2 + TC_EW), 1) k_q80tc(TcArgs p) {
+  typedef TcGeo<TS, (int)sizeof(ST)> Gm;
+  constexpr int NB = Gm::NB, NG = Gm::NG, HT = TS / 4, GB = Gm::GB, GPS = TC_CB / GB;
+  static_assert((NB & (NB - 1)) == 0 && NB % TC_CB == 0, "TMEM buffers: whole stages, a power of two");
+  static_assert(TC_CB % GB == 0 && HT % 2 == 0, "group shape");
+  extern __shared__ __align__(1024) unsigned char tsm_raw[];
+  __shared__ uint64_t full[TC_NS], empty[TC_NS], tfull[NG], tempty[NG], done;
   __shared__ uint32_t tbase;
   __shared__ int abort_f;
+  unsigned char* tsm = tsm_raw + ((1024u - (s32(tsm_raw) & 1023u)) & 1023u);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int nblk = p.K / 32, nst = nblk / TC_CB, tile = blockIdx.x, ts = blockIdx.y;
+  const int nblk = p.K / 32, nst = nblk / TC_CB, ngrp = nblk / GB, tile = blockIdx.x, ts = blockIdx.y;
   if (threadIdx.x == 0) {
-    for (int i = 0; i < TC_NS; i++) { mb_init(&full[i], 1); mb_init(&empty[i], 1 + 4); }
-    for (int i = 0; i < TC_NB; i++) { mb_init(&tfull[i], 1); mb_init(&tempty[i], 4); }
+    for (int i = 0; i < TC_NS; i++) { mb_init(&full[i], 1); mb_init(&empty[i], 1 + TC_EW); }
+    for (int i = 0; i < NG; i++) { mb_init(&tfull[i], 1); mb_init(&tempty[i], TC_EW); }   // every epilogue warp reads every group
     mb_init(&done, 1);
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     abort_f = 0;
   }
   if (warp == 1) {
-    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], 256;" ::"r"(s32(&tbase)));
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], 512;" ::"r"(s32(&tbase)));
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
   }
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = tbase;
-  const int8_t* bsrc = p.b + (size_t)ts * nblk * (TC_TS * 32);
-  const float* xsrc = p.dx + (size_t)ts * nblk * TC_TS;
 
   if (warp == 0) {
-    if (lane == 0) {
-      int issued = 0;
-      for (int s = 0; s < nst; s++) {
-        const int slot = s % TC_NS;
-        if (s >= TC_NS && !mb_wait(&empty[slot], (unsigned)((s / TC_NS) - 1) & 1u, &abort_f)) {
-          abort_f = 1;
-          atomicCAS(p.err, 0, 1);
-          break;
-        }
-        unsigned char* st = tsm + (size_t)slot * TC_STAGE;
-        mb_expect(&full[slot], TC_STAGE);
-        bulk(st, p.a + ((size_t)tile * nblk + (size_t)s * TC_CB) * 4096, TC_SA, &full[slot]);
-        bulk(st + TC_SA, bsrc + (size_t)s * TC_SB, TC_SB, &full[slot]);
-        bulk(st + TC_SA + TC_SB, p.dw + ((size_t)tile * nblk + (size_t)s * TC_CB) * TC_M, TC_SW, &full[slot]);
-        bulk(st + TC_SA + TC_SB + TC_SW, xsrc + (size_t)s * TC_CB * TC_TS, TC_SX, &full[slot]);
-        issued = s + 1;
+    // the whole warp runs the loop; lane 0 issues the copies
+    const int8_t* pa = p.a + (size_t)tile * nblk * 4096;
+    const int8_t* pbx = p.b + (size_t)ts * nblk * (TS * 32);
+    const unsigned char* pw = reinterpret_cast<const unsigned char*>(p.dw) + (size_t)tile * nblk * TC_M * sizeof(ST);
+    const float* px = p.dx + (size_t)ts * nblk * TS;
+    int slot = 0, issued = 0;
+    unsigned epar = 1;   // parity of the empty phase a refill of this slot waits for (flips per ring pass)
+    for (int s = 0; s < nst; s++) {
+      if (s >= TC_NS && !mb_wait_warp(&empty[slot], epar, &abort_f)) {
+        if (lane == 0) { abort_f = 1; atomicCAS(p.err, 0, 1); }
+        break;
       }
-      // no copy may land after the CTA exits: each slot's last issued stage (bounded)
-      for (int s = issued > TC_NS ? issued - TC_NS : 0; s < issued; s++) {
-        unsigned n = 0;
-        while (!mb_try(&full[s % TC_NS], (unsigned)(s / TC_NS) & 1u) && n < TC_WAIT) { n++; if (n > 64) __nanosleep(32); }
+      if (lane == 0) {
+        unsigned char* st = tsm + (size_t)slot * Gm::STAGE;
+        mb_expect(&full[slot], Gm::BYTES);
+        bulk(st, pa, Gm::SA, &full[slot]);
+        bulk(st + Gm::SA, pbx, Gm::SBX, &full[slot]);
+        bulk(st + Gm::SA + Gm::SBX, pw, Gm::SW, &full[slot]);
+        bulk(st + Gm::SA + Gm::SBX + Gm::SW, px, Gm::SX, &full[slot]);
       }
+      __syncwarp();
+      pa += Gm::SA;
+      pbx += Gm::SBX;
+      pw += Gm::SW;
+      px += Gm::SX / 4;
+      issued = s + 1;
+      if (++slot == TC_NS) { slot = 0; epar ^= 1; }
     }
+    // no copy may land after the CTA exits: each slot's last issued stage (bounded)
+    for (int s = issued > TC_NS ? issued - TC_NS : 0; s < issued; s++) mb_drain(&full[s % TC_NS], (unsigned)(s / TC_NS) & 1u);
   } else if (warp == 1) {
-    if (lane == 0) {
-      // kind::i8: D s32 (bits 4-5 = 2), A and B signed (bits 7-9, 10-12 = 1),
-      // both K-major, N = 16 (bits 17-22 = 16/8), M = 128 (bits 24-28 = 128/16)
-      const uint32_t idesc = (2u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(TC_TS >> 3) << 17) |
-                             ((uint32_t)(TC_M >> 4) << 24);
-      int b = 0;
-      for (; b < nblk; b++) {
-        const int s = b / TC_CB, j = b % TC_CB, slot = s % TC_NS, nb = b % TC_NB;
-        if (j == 0 && !mb_wait(&full[slot], (unsigned)(s / TC_NS) & 1u, &abort_f)) break;
-        if (b >= TC_NB && !mb_wait(&tempty[nb], (unsigned)((b / TC_NB) - 1) & 1u, &abort_f)) break;
+    // kind::i8: D s32 (bits 4-5 = 2), A and B signed (bits 7-9, 10-12 = 1),
+    // both K-major, N = TS (bits 17-22 = TS/8), M = 128 (bits 24-28 = 128/16)
+    constexpr uint32_t idesc = (2u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(TS >> 3) << 17) |
+                               ((uint32_t)(TC_M >> 4) << 24);
+    // descriptors of slot 0, block 0; others add constant offsets (in 16-byte
+    // units) to the start-address field, which never carries
+    const uint64_t da0 = umma_desc(s32(tsm)), db0 = umma_desc(s32(tsm + Gm::SA));
+    int slot = 0, gs = 0, nb0 = 0;
+    unsigned fpar = 0;   // parity of full[slot]
+    unsigned tpass = 0;  // passes over the TMEM group slots completed
+    bool ok = true;
+    for (int s = 0; s < nst && ok; s++) {
+      if (!mb_wait_warp(&full[slot], fpar, &abort_f)) { ok = false; break; }
+      tc_fence_after();
+      const uint64_t so = (uint64_t)((slot * Gm::STAGE) >> 4);
+      const uint64_t da = da0 + so, db = db0 + so;
+#pragma unroll
+      for (int q = 0; q < GPS; q++) {
+        if (tpass > 0 && !mb_wait_warp(&tempty[gs], (tpass - 1) & 1u, &abort_f)) { ok = false; break; }
         tc_fence_after();
-        const uint32_t sa = s32(tsm + (size_t)slot * TC_STAGE) + j * (TC_M * 32);
-        const uint32_t sb = s32(tsm + (size_t)slot * TC_STAGE + TC_SA) + j * (TC_TS * 32);
-        tc_mma_i8(tmem + (uint32_t)(nb * TC_TS), umma_desc(sa), umma_desc(sb), idesc);
-        tc_commit(&tfull[nb]);
-        if (j == TC_CB - 1) tc_commit(&empty[slot]);
+        if (lane == 0) {
+#pragma unroll
+          for (int k = 0; k < GB; k++) {
+            const int j = q * GB + k;
+            tc_mma_i8(tmem + (uint32_t)((nb0 + j) * TS),
+                      da + (uint64_t)(((j >> 2) * (TC_M * 128) + (j & 3) * 32) >> 4),
+                      db + (uint64_t)(((j >> 2) * (TS * 128) + (j & 3) * 32) >> 4), idesc);
+          }
+          tc_commit(&tfull[gs]);
+          if (q == GPS - 1) tc_commit(&empty[slot]);
+        }
+        __syncwarp();
+        if (++gs == NG) { gs = 0; tpass++; }
       }
-      if (b < nblk) { abort_f = 1; atomicCAS(p.err, 0, 2); }
-      // every MMA issued so far has completed before the TMEM is freed (bounded)
-      tc_commit(&done);
-      unsigned n = 0;
-      while (!mb_try(&done, 0) && n < TC_WAIT) { n++; if (n > 64) __nanosleep(32); }
+      nb0 = (nb0 + TC_CB) & (NB - 1);
+      if (++slot == TC_NS) { slot = 0; fpar ^= 1; }
     }
+    if (!ok && lane == 0) { abort_f = 1; atomicCAS(p.err, 0, 2); }
+    // every MMA issued so far has completed before the TMEM is freed (bounded)
+    if (lane == 0) tc_commit(&done);
+    __syncwarp();
+    mb_drain(&done, 0);
   } else {
     const int q = warp & 3;                     // TMEM lane quarter of this warp
+    const int part = (warp - 2) >> 2;           // which quarter of the positions
     const int rloc = q * 32 + lane;
     const int n = tile * TC_M + rloc;
-    const uint32_t tq = tmem + ((uint32_t)(q * 32) << 16);
-    float acc[TC_TS];
+    const uint32_t tq = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(part * HT);
+    float acc[HT];
 #pragma unroll
-    for (int t = 0; t < TC_TS; t++) acc[t] = 0.0f;
-    int b0 = 0;
+    for (int t = 0; t < HT; t++) acc[t] = 0.0f;
+    int32_t va[GB][HT], vb[GB][HT];
     bool ok = true;
-    for (; b0 < nblk && ok; b0 += TC_BK) {
-      // TC_BK blocks per step: one wait for all their TMEM loads
-#pragma unroll
-      for (int k = 0; k < TC_BK; k++) {
-        const int b = b0 + k, s = b / TC_CB, j = b % TC_CB, slot = s % TC_NS;
-        // the stage's scales are visible once its copies completed
-        if (j == 0 && !mb_wait(&full[slot], (unsigned)(s / TC_NS) & 1u, &abort_f)) { ok = false; break; }
-        if (!mb_wait(&tfull[b % TC_NB], (unsigned)(b / TC_NB) & 1u, &abort_f)) { ok = false; break; }
-      }
-      if (!ok) break;
+    // wait until group g is in TMEM (its stage's scales are then in shared
+    // memory too: the MMAs read the same stage), then issue its loads into v
+    auto fetch = [&](int g, int32_t (&v)[GB][HT]) -> bool {
+      if (!mb_wait(&tfull[g % NG], (unsigned)(g / NG) & 1u, &abort_f)) return false;
       tc_fence_after();
-      int32_t v[TC_BK][TC_TS];
 #pragma unroll
-      for (int k = 0; k < TC_BK; k++) {
-        const int nb = (b0 + k) % TC_NB;
-        tc_ld8(tq + (uint32_t)(nb * TC_TS), &v[k][0]);
-        tc_ld8(tq + (uint32_t)(nb * TC_TS + 8), &v[k][8]);
-      }
+      for (int k = 0; k < GB; k++) tc_ld_cols<HT>(tq + (uint32_t)(((g * GB + k) % NB) * TS), v[k]);
+      return true;
+    };
+    // the loads of group g have landed: hand its buffers back to the MMA warp
+    auto landed = [&](int g) {
       tc_wait_ld();
       tc_fence_before();
       __syncwarp();
-      if (lane == 0)
-        for (int k = 0; k < TC_BK; k++) mb_arrive(&tempty[(b0 + k) % TC_NB]);
+      if (lane == 0) mb_arrive(&tempty[g % NG]);
+    };
+    auto fold = [&](int g, const int32_t (&v)[GB][HT]) {
+      const int s = (g * GB) / TC_CB, slot = s % TC_NS, j0 = (g * GB) % TC_CB;
+      const unsigned char* st = tsm + (size_t)slot * Gm::STAGE;
 #pragma unroll
-      for (int k = 0; k < TC_BK; k++) {
-        const int b = b0 + k, s = b / TC_CB, j = b % TC_CB, slot = s % TC_NS;
-        const unsigned char* st = tsm + (size_t)slot * TC_STAGE;
-        const float dwv = reinterpret_cast<const float*>(st + TC_SA + TC_SB)[j * TC_M + rloc];
-        const float4* dx4 = reinterpret_cast<const float4*>(st + TC_SA + TC_SB + TC_SW) + j * (TC_TS / 4);
+      for (int k = 0; k < GB; k++) {
+        const int j = j0 + k, b = g * GB + k;
+        const ST sraw = reinterpret_cast<const ST*>(st + Gm::SA + Gm::SBX)[j * TC_M + rloc];
+        float dwv;
+        if (sizeof(ST) == 2) dwv = pb_h2f((unsigned short)sraw);
+        else dwv = (float)sraw;
+        const tc_f2 dw2 = tc_pk(dwv, dwv);
+        const float4* dx4 = reinterpret_cast<const float4*>(st + Gm::SA + Gm::SBX + Gm::SW) + j * (TS / 4) + part * (HT / 4);
 #pragma unroll
-        for (int t4 = 0; t4 < TC_TS / 4; t4++) {
+        for (int t4 = 0; t4 < HT / 4; t4++) {
           const float4 d = dx4[t4];
-          const float dd[4] = {d.x, d.y, d.z, d.w};
-#pragma unroll
-          for (int u = 0; u < 4; u++) {
-            const int t = 4 * t4 + u;
-            acc[t] = __fadd_rn(acc[t], __fmul_rn(__fmul_rn(dwv, dd[u]), i2f_exact(v[k][t])));
-          }
+          // acc += (dw * dx) * (float)isum, per position, in block order; the
+          // products as packed pairs, the accumulation scalar (a packed add
+          // after a packed multiply is not kept apart: its results differ)
+          float p0, p1, p2, p3;
+          tc_upk(tc_mul2(tc_mul2(dw2, tc_pk(d.x, d.y)), tc_i2f2(v[k][4 * t4], v[k][4 * t4 + 1])), p0, p1);
+          tc_upk(tc_mul2(tc_mul2(dw2, tc_pk(d.z, d.w)), tc_i2f2(v[k][4 * t4 + 2], v[k][4 * t4 + 3])), p2, p3);
+          acc[4 * t4] = __fadd_rn(acc[4 * t4], p0);
+          acc[4 * t4 + 1] = __fadd_rn(acc[4 * t4 + 1], p1);
+          acc[4 * t4 + 2] = __fadd_rn(acc[4 * t4 + 2], p2);
+          acc[4 * t4 + 3] = __fadd_rn(acc[4 * t4 + 3], p3);
         }
         if (p.isum && n < p.N) {
 #pragma unroll
-          for (int t = 0; t < TC_TS; t++) p.isum[((size_t)(ts * TC_TS + t) * p.N + n) * nblk + b] = v[k][t];
+          for (int t = 0; t < HT; t++) p.isum[((size_t)(ts * TS + part * HT + t) * p.N + n) * nblk + b] = v[k][t];
         }
         if (j == TC_CB - 1) {
           __syncwarp();
           if (lane == 0) mb_arrive(&empty[slot]);
         }
       }
+    };
+    int b = 0;
+    if (ngrp > 0) ok = fetch(0, va);
+    for (int g = 0; ok && g < ngrp; g += 2) {
+      landed(g);
+      const bool h1 = g + 1 < ngrp;
+      if (h1 && !(ok = fetch(g + 1, vb))) { fold(g, va); b = (g + 1) * GB; break; }
+      fold(g, va);
+      b = (g + 1) * GB;
+      if (!h1) break;
+      landed(g + 1);
+      const bool h2 = g + 2 < ngrp;
+      if (h2 && !(ok = fetch(g + 2, va))) { fold(g + 1, vb); b = (g + 2) * GB; break; }
+      fold(g + 1, vb);
+      b = (g + 2) * GB;
     }
-    if (b0 < nblk) { abort_f = 1; atomicCAS(p.err, 0, 3); }
+    if (b < nblk) { abort_f = 1; atomicCAS(p.err, 0, 3); }
     if (n < p.N) {
 #pragma unroll
-      for (int t = 0; t < TC_TS; t++) p.y[(size_t)(ts * TC_TS + t) * p.N + n] = acc[t];
+      for (int t = 0; t < HT; t++) p.y[(size_t)(ts * TS + part * HT + t) * p.N + n] = acc[t];
     }
   }
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
-  if (warp == 1) asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, 256;" ::"r"(tmem));
+  if (warp == 1) asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, 512;" ::"r"(tmem));
 }
 
-// row-major codes/scales -> tiles of 128 rows in the K-major core-matrix
-// order (rows >= N are zero); one thread per 16-byte (row, block, half)
+// row-major codes/scales -> tiles of 128 rows, per stage of 8 blocks in the
+// 128-byte-swizzle order (rows >= N are zero); one thread per 16-byte
+// (row, block, half)
 template <typename S>
 __global__ void k_q80tc_pack(const int8_t* __restrict__ codes, const S* __restrict__ scales, int N, int K,
-                             int ntile, int8_t* __restrict__ a, float* __restrict__ dw) {
+                             int ntile, int8_t* __restrict__ a, S* __restrict__ dw) {
   const int nblk = K / 32;
   const size_t total = (size_t)ntile * TC_M * nblk * 2;
   for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (size_t)gridDim.x * blockDim.x) {
@@ -285,16 +428,9 @@ __global__ void k_q80tc_pack(const int8_t* __restrict__ codes, const S* __restri
     const int n = tile * TC_M + row;
     uint4 v = make_uint4(0, 0, 0, 0);
     if (n < N) v = *reinterpret_cast<const uint4*>(codes + (size_t)n * K + b * 32 + kh * 16);
-    int8_t* dst = a + tb * 4096 + (row >> 3) * 256 + kh * 128 + (row & 7) * 16;
+    int8_t* dst = a + ((size_t)tile * nblk + (b & ~(TC_CB - 1))) * 4096 + tc_sw(row, (b % TC_CB) * 32 + kh * 16, TC_M);
     *reinterpret_cast<uint4*>(dst) = v;
-    if (kh == 0) {
-      float s = 0.0f;
-      if (n < N) {
-        if (sizeof(S) == 2) s = pb_h2f((unsigned short)scales[(size_t)n * nblk + b]);
-        else s = (float)scales[(size_t)n * nblk + b];
-      }
-      dw[tb * TC_M + row] = s;
-    }
+    if (kh == 0) dw[tb * TC_M + row] = n < N ? scales[(size_t)n * nblk + b] : (S)0;
   }
 }
 
@@ -303,7 +439,7 @@ __global__ void k_q80tc_pack(const int8_t* __restrict__ codes, const S* __restri
 // l + 32(h>>1) of the chunk; scales are pairs (s_l, s_{l+32}) per segment
 template <typename S>
 __global__ void k_q80tc_from_stream(const uint4* __restrict__ codes, const S* __restrict__ scales, int N, int K,
-                                    int ntile, int8_t* __restrict__ a, float* __restrict__ dw) {
+                                    int ntile, int8_t* __restrict__ a, S* __restrict__ dw) {
   const int nblk = K / 32, nch = K / 2048;
   const size_t total = (size_t)ntile * TC_M * nblk * 2;
   for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (size_t)gridDim.x * blockDim.x) {
@@ -316,41 +452,53 @@ __global__ void k_q80tc_from_stream(const uint4* __restrict__ codes, const S* __
     const int n = tile * TC_M + row;
     const int c = b / 64, bl = b % 64, l = bl % 32, hb = bl / 32;
     uint4 v = make_uint4(0, 0, 0, 0);
-    float sc = 0.0f;
+    S sc = (S)0;
     if (n < N) {
       const size_t seg = (size_t)n * nch + c;
       v = codes[seg * 128 + (hb * 2 + kh) * 32 + l];
-      if (sizeof(S) == 2) sc = pb_h2f((unsigned short)scales[(seg * 32 + l) * 2 + hb]);
-      else sc = (float)scales[(seg * 32 + l) * 2 + hb];
+      sc = scales[(seg * 32 + l) * 2 + hb];
     }
-    *reinterpret_cast<uint4*>(a + tb * 4096 + (row >> 3) * 256 + kh * 128 + (row & 7) * 16) = v;
+    *reinterpret_cast<uint4*>(a + ((size_t)tile * nblk + (b & ~(TC_CB - 1))) * 4096 +
+                              tc_sw(row, (b % TC_CB) * 32 + kh * 16, TC_M)) = v;
     if (kh == 0) dw[tb * TC_M + row] = sc;
   }
 }
 
+// positions per CTA for T positions (T a multiple of 16)
+int tc_ts(int T) { return T % 64 == 0 ? 64 : (T % 32 == 0 ? 32 : 16); }
+
 // activations [T][K] int8 + fp16 scales [T][K/32] -> the kernel's layout:
-// per 16 positions, per block, 2 groups of 8 positions x 2 halves x 16 bytes
-__global__ void k_q80tc_act(const int8_t* __restrict__ qx, const uint16_t* __restrict__ dxh, int T, int K,
+// per TS positions, per stage of 8 blocks, TS rows in the 128-byte-swizzle
+// order; scales fp32 [TS group][block][TS]
+__global__ void k_q80tc_act(const int8_t* __restrict__ qx, const uint16_t* __restrict__ dxh, int T, int K, int TS,
                             int8_t* __restrict__ bq, float* __restrict__ dx) {
   const int nblk = K / 32;
   const int total = nblk * T * 2;
   for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < total; i += gridDim.x * blockDim.x) {
     const int kh = i & 1, t = (i >> 1) % T, b = (i >> 1) / T;
-    const int ts = t / TC_TS, tl = t % TC_TS;
+    const int ts = t / TS, tl = t % TS;
     const size_t blk = (size_t)ts * nblk + b;
     const uint4 v = *reinterpret_cast<const uint4*>(qx + (size_t)t * K + b * 32 + kh * 16);
-    *reinterpret_cast<uint4*>(bq + blk * (TC_TS * 32) + (tl >> 3) * 256 + kh * 128 + (tl & 7) * 16) = v;
-    if (kh == 0) dx[blk * TC_TS + tl] = pb_h2f(dxh[(size_t)t * nblk + b]);
+    *reinterpret_cast<uint4*>(bq + ((size_t)ts * nblk + (b & ~(TC_CB - 1))) * (TS * 32) +
+                              tc_sw(tl, (b % TC_CB) * 32 + kh * 16, TS)) = v;
+    if (kh == 0) dx[blk * TS + tl] = pb_h2f(dxh[(size_t)t * nblk + b]);
   }
 }
 
-int launch_tc(const pb_q8* w, int T, const int8_t* bq, const float* dx, float* y, int32_t* isum, int* err,
-              cudaStream_t st) {
-  const size_t smem = (size_t)TC_NS * TC_STAGE;
-  PB_TRY_CUDA(cudaFuncSetAttribute(k_q80tc, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+template <int TS, typename ST>
+int launch_tc_t(const pb_q8* w, int T, const int8_t* bq, const float* dx, float* y, int32_t* isum, int* err,
+                cudaStream_t st) {
+  typedef TcGeo<TS, (int)sizeof(ST)> Gm;
+  static bool attr[64] = {};
+  int dev = 0;
+  PB_TRY_CUDA(cudaGetDevice(&dev));
+  if (dev >= 0 && dev < 64 && !attr[dev]) {
+    PB_TRY_CUDA(cudaFuncSetAttribute(k_q80tc<TS, ST>, cudaFuncAttributeMaxDynamicSharedMemorySize, Gm::SMEM));
+    attr[dev] = true;
+  }
   TcArgs a;
   a.a = w->codes;
-  a.dw = reinterpret_cast<const float*>(w->scales);
+  a.dw = w->scales;
   a.b = bq;
   a.dx = dx;
   a.y = y;
@@ -360,9 +508,22 @@ int launch_tc(const pb_q8* w, int T, const int8_t* bq, const float* dx, float* y
   a.ns = TC_NS;
   a.err = err;
   const int ntile = (w->N + TC_M - 1) / TC_M;
-  k_q80tc<<<dim3(ntile, T / TC_TS), 192, smem, st>>>(a);
+  k_q80tc<TS, ST><<<dim3(ntile, T / TS), 32 * (2 + TC_EW), Gm::SMEM, st>>>(a);
   PB_LAUNCHED("k_q80tc");
   return PB_OK;
+}
+
+int launch_tc(const pb_q8* w, int T, const int8_t* bq, const float* dx, float* y, int32_t* isum, int* err,
+              cudaStream_t st) {
+  const bool f32 = w->sdt == PB_DT_F32;
+  switch (tc_ts(T)) {
+    case 64: return f32 ? launch_tc_t<64, float>(w, T, bq, dx, y, isum, err, st)
+                        : launch_tc_t<64, unsigned short>(w, T, bq, dx, y, isum, err, st);
+    case 32: return f32 ? launch_tc_t<32, float>(w, T, bq, dx, y, isum, err, st)
+                        : launch_tc_t<32, unsigned short>(w, T, bq, dx, y, isum, err, st);
+    default: return f32 ? launch_tc_t<16, float>(w, T, bq, dx, y, isum, err, st)
+                        : launch_tc_t<16, unsigned short>(w, T, bq, dx, y, isum, err, st);
+  }
 }
 
 // per-device scratch of the activation re-layout and the error word, grown on demand
@@ -384,7 +545,7 @@ extern "C" int pb_q80tc_pack(const int8_t* codes, const void* scales, int scale_
     return pb_set_error(PB_EINVAL, "pb_q80tc_pack: scale dtype %d", scale_dtype);
   cudaStream_t st = (cudaStream_t)stream;
   const int ntile = (N + TC_M - 1) / TC_M, nblk = K / 32;
-  const size_t ab = (size_t)ntile * TC_M * K, wb = (size_t)ntile * TC_M * nblk * 4;
+  const size_t ab = (size_t)ntile * TC_M * K, wb = (size_t)ntile * TC_M * nblk * (scale_dtype == PB_DT_F32 ? 4 : 2);
   const size_t cb = (size_t)N * K, sb = pb_q8_scale_bytes(N, K, scale_dtype);
   pb_q8* w = new pb_q8();
   w->N = N; w->K = K; w->sdt = scale_dtype; w->layout = PB_Q8_UMMA; w->nch = 1;
@@ -412,7 +573,7 @@ extern "C" int pb_q80tc_pack(const int8_t* codes, const void* scales, int scale_
     const int grid = (int)std::min<size_t>((units + 255) / 256, (size_t)pb_num_sms() * 16);
     if (scale_dtype == PB_DT_F16)
       k_q80tc_pack<unsigned short><<<grid, 256, 0, st>>>(dc, (const unsigned short*)ds, N, K, ntile, w->codes,
-                                                         (float*)w->scales);
+                                                         (unsigned short*)w->scales);
     else
       k_q80tc_pack<float><<<grid, 256, 0, st>>>(dc, (const float*)ds, N, K, ntile, w->codes, (float*)w->scales);
     cudaError_t e = cudaGetLastError();
@@ -431,7 +592,7 @@ extern "C" int pb_q80tc_pack(const int8_t* codes, const void* scales, int scale_
 // weights), into caller-provided storage of pb_q80tc_bytes() bytes
 size_t pb_q80tc_bytes(int N, int K) {
   const size_t ntile = (size_t)(N + TC_M - 1) / TC_M;
-  return ntile * TC_M * K + ntile * TC_M * (K / 32) * 4;
+  return ntile * TC_M * K + ntile * TC_M * (K / 32) * 4;   // room for fp32 scales
 }
 int pb_q80tc_from_stream(const pb_q8* src, char* storage, pb_q8* out, cudaStream_t st) {
   if (src->layout != PB_Q8_STREAM || src->K % (32 * TC_CB))
@@ -449,7 +610,7 @@ int pb_q80tc_from_stream(const pb_q8* src, char* storage, pb_q8* out, cudaStream
   else
     k_q80tc_from_stream<unsigned short><<<grid, 256, 0, st>>>(reinterpret_cast<const uint4*>(src->codes),
                                                               (const unsigned short*)src->scales, N, K, ntile,
-                                                              out->codes, (float*)out->scales);
+                                                              out->codes, (unsigned short*)out->scales);
   PB_LAUNCHED("k_q80tc_from_stream");
   return PB_OK;
 }
@@ -458,7 +619,7 @@ extern "C" int pb_q80_gemm(const pb_q8* w, int T, const int8_t* d_qx, const uint
                            int32_t* d_isum, void* stream) {
   if (!w || !d_qx || !d_dx || !d_y) return pb_set_error(PB_EINVAL, "pb_q80_gemm: null argument");
   if (w->layout != PB_Q8_UMMA) return pb_set_error(PB_EINVAL, "pb_q80_gemm: tensor not packed by pb_q80tc_pack");
-  if (T <= 0 || T % TC_TS || T > 256)
+  if (T <= 0 || T % 16 || T > 256)
     return pb_set_error(PB_ENOTSUP, "pb_q80_gemm: T=%d (a multiple of 16 up to 256)", T);
   if (((uintptr_t)d_qx & 15) != 0) return pb_set_error(PB_EINVAL, "pb_q80_gemm: qx must be 16-byte aligned");
   cudaStream_t st = (cudaStream_t)stream;
@@ -485,7 +646,7 @@ extern "C" int pb_q80_gemm(const pb_q8* w, int T, const int8_t* d_qx, const uint
   int8_t* bq = reinterpret_cast<int8_t*>(g_tc.p[dev] + 256);
   float* dx = reinterpret_cast<float*>(g_tc.p[dev] + 256 + bqb);
   const int units = nblk * T * 2;
-  k_q80tc_act<<<(units + 255) / 256, 256, 0, st>>>(d_qx, d_dx, T, w->K, bq, dx);
+  k_q80tc_act<<<(units + 255) / 256, 256, 0, st>>>(d_qx, d_dx, T, w->K, tc_ts(T), bq, dx);
   PB_LAUNCHED("k_q80tc_act");
   int rc = launch_tc(w, T, bq, dx, d_y, d_isum, err, st);
   return rc;
