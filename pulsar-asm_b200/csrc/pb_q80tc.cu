@@ -39,7 +39,7 @@ constexpr unsigned long long TC_WAIT_NS = 1000000000ull;   // a wait gives up af
 
 struct TcArgs {
   const int8_t* a;     // weights [tile][stage][128 rows x 256 bytes, 128-byte swizzle]
-  const void* dw;      // weight scales [tile][block][128] (fp16 or fp32, the tensor's dtype)
+  const void* dw;      // weight scales [tile][stage][128 rows][8 blocks] (fp16 or fp32, the tensor's dtype)
   const int8_t* b;     // activations [T/TS][stage][TS rows x 256 bytes, 128-byte swizzle]
   const float* dx;     // activation scales [block][T]
   float* y;            // [T][N]
@@ -150,7 +150,13 @@ PB_DEV void tc_ld_cols(uint32_t taddr, int32_t* v) {
 }
 
 constexpr int TC_NS = 4;             // shared-memory stages
-constexpr int TC_EW = 16;            // epilogue warps: four per TMEM lane quarter
+#ifndef PB_TC_EW
+#define PB_TC_EW 8
+#endif
+constexpr int TC_EW = PB_TC_EW;      // epilogue warps: TC_EW / 4 per TMEM lane quarter
+constexpr int TC_EP = TC_EW / 4;     // position parts per lane quarter
+// registers of an epilogue thread for two groups of TMEM columns
+constexpr int TC_VREGS = TC_EW >= 16 ? 32 : 128;
 
 // shared-memory geometry of one stage for TS positions per CTA and weight
 // scales of SB bytes
@@ -158,14 +164,16 @@ template <int TS, int SB>
 struct TcGeo {
   static constexpr int SA = TC_M * 32 * TC_CB;       // weights
   static constexpr int SBX = TS * 32 * TC_CB;        // activations
-  static constexpr int SW = TC_CB * TC_M * SB;       // weight scales
+  static constexpr int SW = TC_CB * TC_M * SB;       // weight scales [row][8 blocks]
   static constexpr int SX = TC_CB * TS * 4;          // activation scales (fp32)
   static constexpr int BYTES = SA + SBX + SW + SX;                // copied per stage
   static constexpr int STAGE = (BYTES + 1023) / 1024 * 1024;     // stride: slabs stay 1024-aligned
   static constexpr int NB = (512 / TS) < 16 ? (512 / TS) : 16;   // TMEM buffers of TS columns
-  // blocks per TMEM group (one handshake per group): the epilogue holds two
-  // groups' columns, 2 GB TS/4 registers, within its budget of 96
-  static constexpr int GB = 64 / TS;
+  static constexpr int HT = TS / TC_EP;                           // positions per epilogue thread
+  // blocks per TMEM group (one handshake per group): an epilogue thread
+  // holds two groups' columns, 2 GB HT registers
+  static constexpr int GBR = (HT >= 32 ? TC_VREGS / 2 : TC_VREGS) / (2 * HT);
+  static constexpr int GB = GBR >= TC_CB ? TC_CB : (GBR >= 4 ? 4 : (GBR >= 2 ? 2 : 1));
   static constexpr int NG = NB / GB;                 // buffer groups
   static constexpr int SMEM = TC_NS * STAGE + 1024;  // + room to align the base
 };
@@ -197,7 +205,42 @@ PB_DEV tc_f2 tc_i2f2(int32_t a, int32_t b) {
   return tc_add2(r, tc_pk(-12582912.0f, -12582912.0f));
 }
 
-// CTA = 18 warps, one 128-row tile of W and TS of the T positions (grid
+// the weight scales of GB consecutive blocks of one row (GB * sizeof(ST)
+// bytes, aligned to that size) in one vector load, as fp32
+template <int GB, typename ST>
+PB_DEV void tc_scales(const ST* p, float (&o)[GB]) {
+  if constexpr (sizeof(ST) == 4) {
+    if constexpr (GB >= 4) {
+#pragma unroll
+      for (int i = 0; i < GB; i += 4) {
+        const float4 v = reinterpret_cast<const float4*>(p)[i / 4];
+        o[i] = v.x; o[i + 1] = v.y; o[i + 2] = v.z; o[i + 3] = v.w;
+      }
+    } else if constexpr (GB == 2) {
+      const float2 v = *reinterpret_cast<const float2*>(p);
+      o[0] = v.x; o[1] = v.y;
+    } else {
+      o[0] = p[0];
+    }
+  } else {
+    unsigned w[(GB + 1) / 2];
+    if constexpr (GB == 8) {
+      const uint4 v = *reinterpret_cast<const uint4*>(p);
+      w[0] = v.x; w[1] = v.y; w[2] = v.z; w[3] = v.w;
+    } else if constexpr (GB == 4) {
+      const uint2 v = *reinterpret_cast<const uint2*>(p);
+      w[0] = v.x; w[1] = v.y;
+    } else if constexpr (GB == 2) {
+      w[0] = *reinterpret_cast<const unsigned*>(p);
+    } else {
+      w[0] = p[0];
+    }
+#pragma unroll
+    for (int i = 0; i < GB; i++) o[i] = pb_h2f((unsigned short)(w[i / 2] >> (16 * (i & 1))));
+  }
+}
+
+// CTA = 2 + TC_EW warps, one 128-row tile of W and TS of the T positions (grid
 // tiles x T/TS; for T <= 64 every weight byte is read once):
 //   warp 0:     TMA producer (lane 0 issues), 1-D bulk copies of each stage
 //               (8 blocks of weights, activations and their scales) into a
@@ -206,8 +249,8 @@ PB_DEV tc_f2 tc_i2f2(int32_t a, int32_t b) {
 //               K 32) per block into one of NB TMEM buffers of TS columns, one
 //               tcgen05.commit per group of GB blocks; warp 1 allocates and
 //               frees the TMEM (all 512 columns: one CTA per SM);
-//   warps 2-17: epilogue; warp w reads TMEM lane quarter w % 4 and a
-//               quarter of the positions, (w - 2) / 4: per group one wait,
+//   warps 2-:   epilogue; warp w reads TMEM lane quarter w % 4 and part
+//               (w - 2) / 4 of the positions: per group one wait,
 //               tcgen05.ld of its columns of the group's blocks (issued a
 //               group ahead of the fold), release of the group's buffers,
 //               fp32 fold in block order (products two positions per packed
@@ -217,10 +260,10 @@ PB_DEV tc_f2 tc_i2f2(int32_t a, int32_t b) {
 // so each index or descriptor computed at run time costs tens of cycles per
 // MMA (a loop computing them per block issued one M128 N32 MMA per 470
 // cycles; precomputed descriptors plus constants reach about 50).
-template <int TS, typename ST>
+template <int TS, typename ST, bool ISUM>
 __global__ void __launch_bounds__(32 * (2 + TC_EW), 1) k_q80tc(TcArgs p) {
   typedef TcGeo<TS, (int)sizeof(ST)> Gm;
-  constexpr int NB = Gm::NB, NG = Gm::NG, HT = TS / 4, GB = Gm::GB, GPS = TC_CB / GB;
+  constexpr int NB = Gm::NB, NG = Gm::NG, HT = Gm::HT, GB = Gm::GB, GPS = TC_CB / GB;
   static_assert((NB & (NB - 1)) == 0 && NB % TC_CB == 0, "TMEM buffers: whole stages, a power of two");
   static_assert(TC_CB % GB == 0 && HT % 2 == 0, "group shape");
   extern __shared__ __align__(1024) unsigned char tsm_raw[];
@@ -322,7 +365,7 @@ __global__ void __launch_bounds__(32 * (2 + TC_EW), 1) k_q80tc(TcArgs p) {
     mb_drain(&done, 0);
   } else {
     const int q = warp & 3;                     // TMEM lane quarter of this warp
-    const int part = (warp - 2) >> 2;           // which quarter of the positions
+    const int part = (warp - 2) >> 2;           // which part of the positions
     const int rloc = q * 32 + lane;
     const int n = tile * TC_M + rloc;
     const uint32_t tq = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(part * HT);
@@ -350,14 +393,12 @@ __global__ void __launch_bounds__(32 * (2 + TC_EW), 1) k_q80tc(TcArgs p) {
     auto fold = [&](int g, const int32_t (&v)[GB][HT]) {
       const int s = (g * GB) / TC_CB, slot = s % TC_NS, j0 = (g * GB) % TC_CB;
       const unsigned char* st = tsm + (size_t)slot * Gm::STAGE;
+      float dws[GB];
+      tc_scales<GB, ST>(reinterpret_cast<const ST*>(st + Gm::SA + Gm::SBX) + rloc * TC_CB + j0, dws);
 #pragma unroll
       for (int k = 0; k < GB; k++) {
         const int j = j0 + k, b = g * GB + k;
-        const ST sraw = reinterpret_cast<const ST*>(st + Gm::SA + Gm::SBX)[j * TC_M + rloc];
-        float dwv;
-        if (sizeof(ST) == 2) dwv = pb_h2f((unsigned short)sraw);
-        else dwv = (float)sraw;
-        const tc_f2 dw2 = tc_pk(dwv, dwv);
+        const tc_f2 dw2 = tc_pk(dws[k], dws[k]);
         const float4* dx4 = reinterpret_cast<const float4*>(st + Gm::SA + Gm::SBX + Gm::SW) + j * (TS / 4) + part * (HT / 4);
 #pragma unroll
         for (int t4 = 0; t4 < HT / 4; t4++) {
@@ -373,7 +414,7 @@ __global__ void __launch_bounds__(32 * (2 + TC_EW), 1) k_q80tc(TcArgs p) {
           acc[4 * t4 + 2] = __fadd_rn(acc[4 * t4 + 2], p2);
           acc[4 * t4 + 3] = __fadd_rn(acc[4 * t4 + 3], p3);
         }
-        if (p.isum && n < p.N) {
+        if (ISUM && n < p.N) {
 #pragma unroll
           for (int t = 0; t < HT; t++) p.isum[((size_t)(ts * TS + part * HT + t) * p.N + n) * nblk + b] = v[k][t];
         }
@@ -430,7 +471,7 @@ __global__ void k_q80tc_pack(const int8_t* __restrict__ codes, const S* __restri
     if (n < N) v = *reinterpret_cast<const uint4*>(codes + (size_t)n * K + b * 32 + kh * 16);
     int8_t* dst = a + ((size_t)tile * nblk + (b & ~(TC_CB - 1))) * 4096 + tc_sw(row, (b % TC_CB) * 32 + kh * 16, TC_M);
     *reinterpret_cast<uint4*>(dst) = v;
-    if (kh == 0) dw[tb * TC_M + row] = n < N ? scales[(size_t)n * nblk + b] : (S)0;
+    if (kh == 0) dw[((tb >> 3) * TC_M + row) * TC_CB + (b % TC_CB)] = n < N ? scales[(size_t)n * nblk + b] : (S)0;
   }
 }
 
@@ -460,7 +501,7 @@ __global__ void k_q80tc_from_stream(const uint4* __restrict__ codes, const S* __
     }
     *reinterpret_cast<uint4*>(a + ((size_t)tile * nblk + (b & ~(TC_CB - 1))) * 4096 +
                               tc_sw(row, (b % TC_CB) * 32 + kh * 16, TC_M)) = v;
-    if (kh == 0) dw[tb * TC_M + row] = sc;
+    if (kh == 0) dw[((tb >> 3) * TC_M + row) * TC_CB + (b % TC_CB)] = sc;
   }
 }
 
@@ -485,15 +526,15 @@ __global__ void k_q80tc_act(const int8_t* __restrict__ qx, const uint16_t* __res
   }
 }
 
-template <int TS, typename ST>
-int launch_tc_t(const pb_q8* w, int T, const int8_t* bq, const float* dx, float* y, int32_t* isum, int* err,
+template <int TS, typename ST, bool ISUM>
+int launch_tc_t2(const pb_q8* w, int T, const int8_t* bq, const float* dx, float* y, int32_t* isum, int* err,
                 cudaStream_t st) {
   typedef TcGeo<TS, (int)sizeof(ST)> Gm;
   static bool attr[64] = {};
   int dev = 0;
   PB_TRY_CUDA(cudaGetDevice(&dev));
   if (dev >= 0 && dev < 64 && !attr[dev]) {
-    PB_TRY_CUDA(cudaFuncSetAttribute(k_q80tc<TS, ST>, cudaFuncAttributeMaxDynamicSharedMemorySize, Gm::SMEM));
+    PB_TRY_CUDA(cudaFuncSetAttribute(k_q80tc<TS, ST, ISUM>, cudaFuncAttributeMaxDynamicSharedMemorySize, Gm::SMEM));
     attr[dev] = true;
   }
   TcArgs a;
@@ -508,9 +549,16 @@ int launch_tc_t(const pb_q8* w, int T, const int8_t* bq, const float* dx, float*
   a.ns = TC_NS;
   a.err = err;
   const int ntile = (w->N + TC_M - 1) / TC_M;
-  k_q80tc<TS, ST><<<dim3(ntile, T / TS), 32 * (2 + TC_EW), Gm::SMEM, st>>>(a);
+  k_q80tc<TS, ST, ISUM><<<dim3(ntile, T / TS), 32 * (2 + TC_EW), Gm::SMEM, st>>>(a);
   PB_LAUNCHED("k_q80tc");
   return PB_OK;
+}
+// the block dots are written out only when asked for (tests)
+template <int TS, typename ST>
+int launch_tc_t(const pb_q8* w, int T, const int8_t* bq, const float* dx, float* y, int32_t* isum, int* err,
+                cudaStream_t st) {
+  return isum ? launch_tc_t2<TS, ST, true>(w, T, bq, dx, y, isum, err, st)
+              : launch_tc_t2<TS, ST, false>(w, T, bq, dx, y, isum, err, st);
 }
 
 int launch_tc(const pb_q8* w, int T, const int8_t* bq, const float* dx, float* y, int32_t* isum, int* err,
