@@ -155,7 +155,7 @@ constexpr int TC_NS = 4;             // shared-memory stages
 #endif
 constexpr int TC_EW = PB_TC_EW;      // epilogue warps: TC_EW / 4 per TMEM lane quarter
 constexpr int TC_EP = TC_EW / 4;     // position parts per lane quarter
-// registers of an epilogue thread for two groups of TMEM columns
+// registers of an epilogue thread for one group of TMEM columns
 constexpr int TC_VREGS = TC_EW >= 16 ? 32 : 128;
 
 // shared-memory geometry of one stage for TS positions per CTA and weight
@@ -171,8 +171,8 @@ struct TcGeo {
   static constexpr int NB = (512 / TS) < 16 ? (512 / TS) : 16;   // TMEM buffers of TS columns
   static constexpr int HT = TS / TC_EP;                           // positions per epilogue thread
   // blocks per TMEM group (one handshake per group): an epilogue thread
-  // holds two groups' columns, 2 GB HT registers
-  static constexpr int GBR = (HT >= 32 ? TC_VREGS / 2 : TC_VREGS) / (2 * HT);
+  // holds one group's columns, GB HT registers
+  static constexpr int GBR = TC_VREGS / HT;
   static constexpr int GB = GBR >= TC_CB ? TC_CB : (GBR >= 4 ? 4 : (GBR >= 2 ? 2 : 1));
   static constexpr int NG = NB / GB;                 // buffer groups
   static constexpr int SMEM = TC_NS * STAGE + 1024;  // + room to align the base
@@ -251,8 +251,8 @@ PB_DEV void tc_scales(const ST* p, float (&o)[GB]) {
 //               frees the TMEM (all 512 columns: one CTA per SM);
 //   warps 2-:   epilogue; warp w reads TMEM lane quarter w % 4 and part
 //               (w - 2) / 4 of the positions: per group one wait,
-//               tcgen05.ld of its columns of the group's blocks (issued a
-//               group ahead of the fold), release of the group's buffers,
+//               tcgen05.ld of its columns of the group's blocks, release of
+//               the group's buffers,
 //               fp32 fold in block order (products two positions per packed
 //               multiply, the accumulation scalar).
 // The issuing loops run one stage per iteration with every block of the
@@ -372,10 +372,10 @@ __global__ void __launch_bounds__(32 * (2 + TC_EW), 1) k_q80tc(TcArgs p) {
     float acc[HT];
 #pragma unroll
     for (int t = 0; t < HT; t++) acc[t] = 0.0f;
-    int32_t va[GB][HT], vb[GB][HT];
+    int32_t va[GB][HT];
     bool ok = true;
     // wait until group g is in TMEM (its stage's scales are then in shared
-    // memory too: the MMAs read the same stage), then issue its loads into v
+    // memory too: the MMAs read the same stage), then load it into v
     auto fetch = [&](int g, int32_t (&v)[GB][HT]) -> bool {
       if (!mb_wait(&tfull[g % NG], (unsigned)(g / NG) & 1u, &abort_f)) return false;
       tc_fence_after();
@@ -424,20 +424,14 @@ __global__ void __launch_bounds__(32 * (2 + TC_EW), 1) k_q80tc(TcArgs p) {
         }
       }
     };
+    // one register set: the fold keeps the registers for its own parallelism
+    // (a second set, loaded a group ahead, left too few and was slower)
     int b = 0;
-    if (ngrp > 0) ok = fetch(0, va);
-    for (int g = 0; ok && g < ngrp; g += 2) {
+    for (int g = 0; g < ngrp; g++) {
+      if (!(ok = fetch(g, va))) break;
       landed(g);
-      const bool h1 = g + 1 < ngrp;
-      if (h1 && !(ok = fetch(g + 1, vb))) { fold(g, va); b = (g + 1) * GB; break; }
       fold(g, va);
       b = (g + 1) * GB;
-      if (!h1) break;
-      landed(g + 1);
-      const bool h2 = g + 2 < ngrp;
-      if (h2 && !(ok = fetch(g + 2, va))) { fold(g + 1, vb); b = (g + 2) * GB; break; }
-      fold(g + 1, vb);
-      b = (g + 2) * GB;
     }
     if (b < nblk) { abort_f = 1; atomicCAS(p.err, 0, 3); }
     if (n < p.N) {
