@@ -62,7 +62,10 @@ constexpr unsigned PB_POLL_LIMIT = 1u << 22;   // tagged-word polls before a wai
 struct DPhase {
   int kind;            // PH_GEMV or PH_ATTN
   int pro, epi;        // GEMV prologue (PRO_*) and epilogue (EPI_*)
-  int N, K, nch;       // GEMV rows, input length, 2048-code chunks per row
+  int N, K, nch;       // GEMV rows, input length, 2048-code segments per row
+  int one;             // one-chunk rows (K not a multiple of 2048): lane chains
+                       // run on over the segments; the row values region then
+                       // holds (dot_lo, dot_hi, s_lo, s_hi) per segment and lane
   int gidx;            // index in the per-CTA GEMV schedule
   int rowoff;          // float offset of the row values in the activation region
   int H;
@@ -301,6 +304,13 @@ PB_DEV float leaf2(const uint4 (&q)[4], float slo, float shi, const f2x (&xr)[32
   upk(d, d0, d1);
   return __fmaf_rn(shi, d1, __fmaf_rn(slo, d0, 0.0f));
 }
+// the two block dots of lane l (blocks l and l+32 of the segment)
+PB_DEV void dots2(const uint4 (&q)[4], const f2x (&xr)[32], float& d0, float& d1) {
+  f2x d = pk(0.0f, 0.0f);
+  d = dot16x2(q[0], q[2], xr, d);
+  d = dot16x2(q[1], q[3], xr + 16, d);
+  upk(d, d0, d1);
+}
 
 extern __shared__ __align__(128) unsigned char dsm[];
 PB_DEV IssueCtx* issue_ctx() { return reinterpret_cast<IssueCtx*>(dsm); }
@@ -428,12 +438,19 @@ PB_DEV void dpro_conv(const DPhase& ph, float* sx, uint32_t tw, int pos, const P
   if (blockIdx.x == 0) st_bf<E>(ring + (size_t)(pos % W) * H + (size_t)t * E, bx);
 }
 
-// plain input: K = 256 EK tagged values, EK per thread.
+// plain input: 256 EK values staged, EK per thread: the K tagged values,
+// then zeros (a one-chunk tensor's padding; K is a multiple of 32, so a
+// thread's EK values are all inside or all past it)
 template <int EK>
 PB_DEV void dpro_plain(const DPhase& ph, float* sx, uint32_t tw, const PollCtx& pc, unsigned long long* tm2) {
   const int t = threadIdx.x;
   uint32_t w[EK];
-  if (!poll_words<EK>(ph.tin + (size_t)t * EK, tw, w, pc)) poll_fail(pc, 4);
+  if (t * EK < ph.K) {
+    if (!poll_words<EK>(ph.tin + (size_t)t * EK, tw, w, pc)) poll_fail(pc, 4);
+  } else {
+#pragma unroll
+    for (int j = 0; j < EK; j++) w[j] = 0u;   // bf16 +0
+  }
   mark_input(tm2);
 #pragma unroll
   for (int j = 0; j < EK; j++) sx[padx(t * EK + j)] = pb_lo2f(w[j]);
@@ -463,7 +480,7 @@ __device__ __forceinline__ unsigned gemv_phase(const DecodeArgs& d, const DPhase
     } else if (pro == PRO_CONV) {
       dpro_conv<EH, W>(ph, sx, tw_in, pos, pc, tm2);
     } else {
-      switch (ph.K >> 8) {
+      switch (pb_kpad(ph.K) >> 8) {
         case 8: dpro_plain<8>(ph, sx, tw_in, pc, tm2); break;
         case 16: dpro_plain<16>(ph, sx, tw_in, pc, tm2); break;
         case 32: dpro_plain<32>(ph, sx, tw_in, pc, tm2); break;
@@ -555,6 +572,21 @@ __device__ __forceinline__ unsigned gemv_phase(const DecodeArgs& d, const DPhase
 #ifdef PB_TRACE_STAGE_LOOP
     const unsigned long long tr1 = (tm2 && threadIdx.x == 0) ? gtime() : 0;
 #endif
+    if (ph.one) {
+      // park this lane's two block dots and scales per (row, segment)
+      float4* rq = reinterpret_cast<float4*>(rowv);
+#pragma unroll
+      for (int u = 0; u < 2; u++) {
+        float d0, d1;
+        dots2(q[u], xr, d0, d1);
+        const int lr = r - r0 + g * 2 + u;
+        if (r + g * 2 + u < r1) rq[(lr * nch + c) * 32 + lane] = make_float4(d0, d1, slo[u], shi[u]);
+      }
+      it++;
+      if (++slot == ds) { slot = 0; par ^= 1; }
+      if (++kn == spt) kn = 0;
+      continue;
+    }
     float v[2];
 #pragma unroll
     for (int u = 0; u < 2; u++) v[u] = pb_warp_tree(leaf2(q[u], slo[u], shi[u], xr));
@@ -577,7 +609,21 @@ __device__ __forceinline__ unsigned gemv_phase(const DecodeArgs& d, const DPhase
   dsync();
   // epilogue over the CTA's rows: chunk values added in chunk order from 0
   const int nr = r1 - r0;
-  if (ph.epi == EPI_SILU) {
+  if (ph.one) {
+    // one-chunk rows (bf16 output only): a warp per row chains every lane's
+    // blocks l, l+32, l+64, ... in order, then the tree; the chunk sum is 0 + v
+    const float4* rq = reinterpret_cast<const float4*>(rowv);
+    for (int i = warp; i < nr; i += DWARPS) {
+      float acc = 0.0f;
+      for (int cc = 0; cc < nch; cc++) {
+        const float4 pv = rq[(i * nch + cc) * 32 + lane];
+        acc = __fmaf_rn(pv.z, pv.x, acc);
+        acc = __fmaf_rn(pv.w, pv.y, acc);
+      }
+      const float v = pb_warp_tree(acc);
+      if (lane == 0) st_tag(ph.tout + r0 + i, tagged(tw_out, __fadd_rn(0.0f, v)));
+    }
+  } else if (ph.epi == EPI_SILU) {
     // rows 2i (w1) and 2i+1 (w3): k_silu_mul_bf, lfm3_nanode.cu:821-829
     uint32_t* out = ph.tout;
     for (int i = 2 * threadIdx.x; i + 1 < nr; i += 2 * DTHREADS) {

@@ -39,6 +39,10 @@ struct pb_q8 {
   int sdt = PB_DT_F16;       // scale dtype: PB_DT_F16 or PB_DT_F32
   int layout = PB_Q8_ROWMAJOR;
   int nch = 1;               // 2048-code chunks per row (stream layout)
+  int one = 0;               // stream layout of a K that is not a multiple of
+                             // 2048: one chunk per row (the lane chains run on
+                             // over the row's segments, one tree), codes and
+                             // scales zero past K up to nch * 2048
   int8_t* codes = nullptr;   // device
   void* scales = nullptr;    // device
   bool owner = true;         // false: views into a model arena
@@ -51,11 +55,26 @@ struct pb_q1 {
   bool owner = true;
 };
 
-// streaming layout: 2048-code chunks, needs K % 2048 == 0 and chunks | 8
-inline bool pb_q8_stream_ok(int K) {
-  if (K % 2048) return false;
-  const int n = K / 2048;
-  return n == 1 || n == 2 || n == 4 || n == 8;
+// streaming layout: 2048-code segments, chunks | 8. A K that is a multiple of
+// 2048 reduces per 2048-code chunk; any other K (a multiple of 32) reduces as
+// ONE chunk (pick(), lfm3_nanode.cu:1763-1768: KCHUNK = K unless 2048 divides
+// K) and is padded with zero blocks to whole segments. 0: row-major layout.
+inline int pb_q8_stream_chunks(int K, int* one) {
+  if (K <= 0 || K % 32) return 0;
+  const int n = (K + 2047) / 2048;
+  if (!(n == 1 || n == 2 || n == 4 || n == 8)) return 0;
+  if (one) *one = K % 2048 != 0;
+  return n;
+}
+inline bool pb_q8_stream_ok(int K) { return pb_q8_stream_chunks(K, nullptr) > 0; }
+// device bytes of a tensor's codes / scales in its layout
+inline size_t pb_q8_code_bytes(int N, int K) {
+  const int n = pb_q8_stream_chunks(K, nullptr);
+  return n ? (size_t)N * n * 2048 : (size_t)N * K;
+}
+inline size_t pb_q8_layout_scale_bytes(int N, int K, int sdt) {
+  const int n = pb_q8_stream_chunks(K, nullptr);
+  return (size_t)N * (n ? n * 64 : K / 32) * (sdt == PB_DT_F32 ? 4 : 2);
 }
 inline size_t pb_q8_scale_bytes(int N, int K, int sdt) {
   return (size_t)N * (K / 32) * (sdt == PB_DT_F32 ? 4 : 2);

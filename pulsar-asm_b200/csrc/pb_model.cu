@@ -71,6 +71,26 @@ PB_DEV float s_dot16(const uint4 g, const float* xr, float dot) {
   }
   return dot;
 }
+PB_DEV void s_dots(const uint4 (&q)[4], const float (&xr)[64], float& d0, float& d1) {
+  d0 = s_dot16(q[0], xr, 0.0f);
+  d0 = s_dot16(q[1], xr + 16, d0);
+  d1 = s_dot16(q[2], xr + 32, 0.0f);
+  d1 = s_dot16(q[3], xr + 48, d1);
+}
+// one-chunk rows (K not a multiple of 2048): lane l's chain over blocks l,
+// l+32, l+64, ... runs on across the row's segments, then one tree; p holds
+// (dot_lo, dot_hi, s_lo, s_hi) per segment and lane
+template <int NCH>
+PB_DEV float s_one_chain(const float4* p, int lane) {
+  float acc = 0.0f;
+#pragma unroll
+  for (int c = 0; c < NCH; c++) {
+    const float4 v = p[c * 32 + lane];
+    acc = __fmaf_rn(v.z, v.x, acc);
+    acc = __fmaf_rn(v.w, v.y, acc);
+  }
+  return pb_warp_tree(acc);
+}
 PB_DEV float s_leaf(const uint4 (&q)[4], float slo, float shi, const float (&xr)[64]) {
   float d0 = s_dot16(q[0], xr, 0.0f);
   d0 = s_dot16(q[1], xr + 16, d0);
@@ -91,13 +111,15 @@ PB_DEV void l2_prefetch(const void* p, size_t bytes) {
   }
 }
 
-template <int NCH, bool F32S, int EPI>
+template <int NCH, bool F32S, int EPI, bool ONE>
 __global__ void __launch_bounds__(256, 2) k_step(StepArgs a) {
   constexpr int U = 2, G = 8 / NCH, RB = G * U;
+  static_assert(!ONE || (NCH > 1 && RB <= 8 && EPI == EPI_BF16), "one-chunk rows: a warp per row, bf16 out");
   extern __shared__ __align__(16) float smem[];
-  float* sx = smem;                          // K + K/32 (padded)
+  float* sx = smem;                          // padded K + K/32 (padded)
   __shared__ float red[16];
   __shared__ float part[2][RB][NCH];
+  __shared__ float4 partq[ONE ? 2 : 1][ONE ? RB : 1][ONE ? NCH * 32 : 1];
   __shared__ float bestv[8];
   __shared__ int besti[8];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -142,59 +164,74 @@ __global__ void __launch_bounds__(256, 2) k_step(StepArgs a) {
         slo[u] = shi[u] = 0.0f;
       }
     }
-    float v[U];
+    if constexpr (ONE) {
 #pragma unroll
-    for (int u = 0; u < U; u++) v[u] = pb_warp_tree(s_leaf(q[u], slo[u], shi[u], xr));
-    if (NCH == 1) {
-      if (lane == 0) {
-        if (EPI == EPI_SILU) {
-          // rows 2i (w1) and 2i+1 (w3): k_silu_mul_bf, lfm3_nanode.cu:821-829
-          if (row0 + 1 < a.N) {
-            const float av = pb_bf2f(pb_f2bf(__fadd_rn(0.0f, v[0])));
-            const float bw = pb_bf2f(pb_f2bf(__fadd_rn(0.0f, v[1])));
-            reinterpret_cast<bf16_t*>(a.y)[row0 >> 1] =
-                pb_f2bf(__fmul_rn(__fmul_rn(av, pb_sigmoid(av)), bw));
-          }
-        } else {
+      for (int u = 0; u < U; u++) {
+        float d0, d1;
+        s_dots(q[u], xr, d0, d1);
+        partq[it][g * U + u][c * 32 + lane] = make_float4(d0, d1, slo[u], shi[u]);
+      }
+      __syncthreads();
+      if (warp < RB) {
+        const int row = rb * RB + warp;
+        const float v = s_one_chain<NCH>(&partq[it][warp][0], lane);
+        if (lane == 0 && row < a.N) reinterpret_cast<bf16_t*>(a.y)[row] = pb_f2bf(__fadd_rn(0.0f, v));
+      }
+    } else {
+      float v[U];
 #pragma unroll
-          for (int u = 0; u < U; u++) {
-            const int row = row0 + u;
-            if (row < a.N) {
-              const float o = __fadd_rn(0.0f, v[u]);
-              if (EPI == EPI_ARGMAX) {
-                reinterpret_cast<float*>(a.y)[row] = o;
-                if (o > bv || (o == bv && row < bi)) { bv = o; bi = row; }
-              } else {
-                reinterpret_cast<bf16_t*>(a.y)[row] = pb_f2bf(o);
+      for (int u = 0; u < U; u++) v[u] = pb_warp_tree(s_leaf(q[u], slo[u], shi[u], xr));
+      if (NCH == 1) {
+        if (lane == 0) {
+          if (EPI == EPI_SILU) {
+            // rows 2i (w1) and 2i+1 (w3): k_silu_mul_bf, lfm3_nanode.cu:821-829
+            if (row0 + 1 < a.N) {
+              const float av = pb_bf2f(pb_f2bf(__fadd_rn(0.0f, v[0])));
+              const float bw = pb_bf2f(pb_f2bf(__fadd_rn(0.0f, v[1])));
+              reinterpret_cast<bf16_t*>(a.y)[row0 >> 1] =
+                  pb_f2bf(__fmul_rn(__fmul_rn(av, pb_sigmoid(av)), bw));
+            }
+          } else {
+#pragma unroll
+            for (int u = 0; u < U; u++) {
+              const int row = row0 + u;
+              if (row < a.N) {
+                const float o = __fadd_rn(0.0f, v[u]);
+                if (EPI == EPI_ARGMAX) {
+                  reinterpret_cast<float*>(a.y)[row] = o;
+                  if (o > bv || (o == bv && row < bi)) { bv = o; bi = row; }
+                } else {
+                  reinterpret_cast<bf16_t*>(a.y)[row] = pb_f2bf(o);
+                }
               }
             }
           }
         }
-      }
-    } else {
-      if (lane == 0)
+      } else {
+        if (lane == 0)
 #pragma unroll
-        for (int u = 0; u < U; u++) part[it][g * U + u][c] = v[u];
-      __syncthreads();
-      if (threadIdx.x < RB) {
-        const int row = rb * RB + threadIdx.x;
-        float acc = 0.0f;
+          for (int u = 0; u < U; u++) part[it][g * U + u][c] = v[u];
+        __syncthreads();
+        if (threadIdx.x < RB) {
+          const int row = rb * RB + threadIdx.x;
+          float acc = 0.0f;
 #pragma unroll
-        for (int cc = 0; cc < NCH; cc++) acc = __fadd_rn(acc, part[it][threadIdx.x][cc]);
-        if (EPI == EPI_SILU) {
-          if ((threadIdx.x & 1) == 0 && row + 1 < a.N) {
-            float acc1 = 0.0f;
+          for (int cc = 0; cc < NCH; cc++) acc = __fadd_rn(acc, part[it][threadIdx.x][cc]);
+          if (EPI == EPI_SILU) {
+            if ((threadIdx.x & 1) == 0 && row + 1 < a.N) {
+              float acc1 = 0.0f;
 #pragma unroll
-            for (int cc = 0; cc < NCH; cc++) acc1 = __fadd_rn(acc1, part[it][threadIdx.x + 1][cc]);
-            const float av = pb_bf2f(pb_f2bf(acc)), bw = pb_bf2f(pb_f2bf(acc1));
-            reinterpret_cast<bf16_t*>(a.y)[row >> 1] = pb_f2bf(__fmul_rn(__fmul_rn(av, pb_sigmoid(av)), bw));
-          }
-        } else if (row < a.N) {
-          if (EPI == EPI_ARGMAX) {
-            reinterpret_cast<float*>(a.y)[row] = acc;
-            if (acc > bv || (acc == bv && row < bi)) { bv = acc; bi = row; }
-          } else {
-            reinterpret_cast<bf16_t*>(a.y)[row] = pb_f2bf(acc);
+              for (int cc = 0; cc < NCH; cc++) acc1 = __fadd_rn(acc1, part[it][threadIdx.x + 1][cc]);
+              const float av = pb_bf2f(pb_f2bf(acc)), bw = pb_bf2f(pb_f2bf(acc1));
+              reinterpret_cast<bf16_t*>(a.y)[row >> 1] = pb_f2bf(__fmul_rn(__fmul_rn(av, pb_sigmoid(av)), bw));
+            }
+          } else if (row < a.N) {
+            if (EPI == EPI_ARGMAX) {
+              reinterpret_cast<float*>(a.y)[row] = acc;
+              if (acc > bv || (acc == bv && row < bi)) { bv = acc; bi = row; }
+            } else {
+              reinterpret_cast<bf16_t*>(a.y)[row] = pb_f2bf(acc);
+            }
           }
         }
       }
@@ -406,14 +443,17 @@ int max_span(const pb_model* m, int max_ctx) {
 }
 
 // ---- launches ---------------------------------------------------------------
-size_t step_smem(int K, int H) { return (size_t)(K + K / 32 + 2 * H) * sizeof(float); }
+size_t step_smem(int K, int H) {
+  const int kp = pb_kpad(K);
+  return (size_t)(kp + kp / 32 + 2 * H) * sizeof(float);
+}
 
-template <int NCH, bool F32S, int EPI>
+template <int NCH, bool F32S, int EPI, bool ONE = false>
 int launch_step_t(const StepArgs& a, cudaStream_t st, bool pdl) {
   const size_t smem = step_smem(a.K, a.H);
   static bool set = false;
   if (!set) {
-    cudaFuncSetAttribute(k_step<NCH, F32S, EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize, 96 * 1024);
+    cudaFuncSetAttribute(k_step<NCH, F32S, EPI, ONE>, cudaFuncAttributeMaxDynamicSharedMemorySize, 96 * 1024);
     set = true;
   }
   if (smem > 96 * 1024) return pb_set_error(PB_ENOTSUP, "step: K=%d H=%d needs too much shared memory", a.K, a.H);
@@ -432,14 +472,23 @@ int launch_step_t(const StepArgs& a, cudaStream_t st, bool pdl) {
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = pdl ? 1 : 0;
-  cudaError_t e = cudaLaunchKernelEx(&cfg, k_step<NCH, F32S, EPI>, a);
+  cudaError_t e = cudaLaunchKernelEx(&cfg, k_step<NCH, F32S, EPI, ONE>, a);
   if (e != cudaSuccess) return pb_set_error(PB_ECUDA, "launch k_step: %s", cudaGetErrorString(e));
   pb_count_launch();
   return PB_OK;
 }
 
 template <bool F32S, int EPI>
-int launch_step_n(int nch, const StepArgs& a, cudaStream_t st, bool pdl) {
+int launch_step_n(int nch, int one, const StepArgs& a, cudaStream_t st, bool pdl) {
+  if (one && nch > 1) {
+    if (EPI != EPI_BF16) return pb_set_error(PB_ENOTSUP, "step: one-chunk rows (K %d) feed a bf16 output only", a.K);
+    switch (nch) {
+      case 2: return launch_step_t<2, F32S, EPI_BF16, true>(a, st, pdl);
+      case 4: return launch_step_t<4, F32S, EPI_BF16, true>(a, st, pdl);
+      case 8: return launch_step_t<8, F32S, EPI_BF16, true>(a, st, pdl);
+    }
+    return pb_set_error(PB_ENOTSUP, "step: %d chunks", nch);
+  }
   switch (nch) {
     case 1: return launch_step_t<1, F32S, EPI>(a, st, pdl);
     case 2: return launch_step_t<2, F32S, EPI>(a, st, pdl);
@@ -455,9 +504,9 @@ int launch_step(const pb_q8& w, int epi, StepArgs a, cudaStream_t st, bool pdl) 
   a.N = w.N;
   a.K = w.K;
   const bool f = w.sdt == PB_DT_F32;
-  if (epi == EPI_BF16) return f ? launch_step_n<true, EPI_BF16>(w.nch, a, st, pdl) : launch_step_n<false, EPI_BF16>(w.nch, a, st, pdl);
-  if (epi == EPI_SILU) return f ? launch_step_n<true, EPI_SILU>(w.nch, a, st, pdl) : launch_step_n<false, EPI_SILU>(w.nch, a, st, pdl);
-  return f ? launch_step_n<true, EPI_ARGMAX>(w.nch, a, st, pdl) : launch_step_n<false, EPI_ARGMAX>(w.nch, a, st, pdl);
+  if (epi == EPI_BF16) return f ? launch_step_n<true, EPI_BF16>(w.nch, w.one, a, st, pdl) : launch_step_n<false, EPI_BF16>(w.nch, w.one, a, st, pdl);
+  if (epi == EPI_SILU) return f ? launch_step_n<true, EPI_SILU>(w.nch, w.one, a, st, pdl) : launch_step_n<false, EPI_SILU>(w.nch, w.one, a, st, pdl);
+  return f ? launch_step_n<true, EPI_ARGMAX>(w.nch, w.one, a, st, pdl) : launch_step_n<false, EPI_ARGMAX>(w.nch, w.one, a, st, pdl);
 }
 
 int launch_attn(const pb_model* m, pb_state* s, int layer, cudaStream_t st, bool pdl) {
@@ -716,16 +765,25 @@ int build_graph(pb_state* s) {
 }
 
 // ---- persistent decode ---------------------------------------------------
-// The persistent kernel is compiled for the shapes listed here (head_dim 64,
-// hidden 2048, conv width 3: the LFM3 2B-class backbone); other models decode
-// on the per-kernel CUDA-graph path, with the same results.
+// The persistent kernel is compiled for the shapes listed here: hidden 2048
+// with head_dim 64 and conv width 3 (the LFM3 2B-class backbone) or head_dim
+// 128 and conv width 7 (the reference engine's own model, lfm3_nanode.cu:76-
+// 101); other models decode on the per-kernel CUDA-graph path, with the same
+// results.
 bool persistent_shape(const pb_model* m) {
-  if (m->HD != 64 || m->H != 2048 || m->W != 3) return false;
-  // PRO_PLAIN inputs (w2: K = F; o_proj: K = NH*HD) take 256*{8,16,32} values;
-  // the P.V phase runs on 4 NH CTAs
-  const int kf = m->F >> 8, ka = (m->NH * m->HD) >> 8;
-  return m->F % 256 == 0 && (kf == 8 || kf == 16 || kf == 32) && (m->NH * m->HD) % 256 == 0 &&
-         (ka == 8 || ka == 16 || ka == 32) && 4 * m->NH <= pb_num_sms();
+  if (m->H != 2048 || !((m->HD == 64 && m->W == 3) || (m->HD == 128 && m->W == 7))) return false;
+  // PRO_PLAIN inputs (w2: K = F; o_proj: K = NH*HD) stage 256*{8,16,32}
+  // values (K padded to whole segments); the P.V phase runs on 4 NH CTAs
+  const int kf = pb_kpad(m->F) >> 8, ka = pb_kpad(m->NH * m->HD) >> 8;
+  return (kf == 8 || kf == 16 || kf == 32) && (ka == 8 || ka == 16 || ka == 32) && 4 * m->NH <= pb_num_sms();
+}
+
+// shapes the integer-path chunk kernels (prefill, batched decode) are compiled
+// for: hidden 2048, head_dim 64 with conv width 3 or head_dim 128 with conv
+// width 7, the attention output 2048 wide, F a multiple of 32 up to 8192
+bool chunk_shape(const pb_model* m) {
+  return m->H == 2048 && ((m->HD == 64 && m->W == 3) || (m->HD == 128 && m->W == 7)) && m->F % 32 == 0 &&
+         m->F <= 8192 && m->F % 256 == 0 && m->NH * m->HD == 2048;
 }
 
 AttnArgs attn_args(const pb_model* m, pb_state* s, int layer) {
@@ -759,6 +817,7 @@ DPhase dgemv(const pb_model* m, const pb_q8& w, int pro, int epi, const uint32_t
   ph.N = w.N;
   ph.K = w.K;
   ph.nch = w.nch;
+  ph.one = w.one && w.nch > 1;
   ph.H = m->H;
   ph.eps = m->eps;
   ph.tin = tin;
@@ -835,8 +894,11 @@ int build_phases(pb_state* s) {
     if (p.kind == PH_GEMV) {
       const int RB = DSEGS / p.nch;
       const int nrb = (p.N + RB - 1) / RB;
-      p.rowoff = (p.K + p.K / 32 + 3) & ~3;
-      xr = std::max(xr, p.rowoff + ((nrb + G - 1) / G) * DSEGS);
+      const int kp = pb_kpad(p.K);
+      p.rowoff = (kp + kp / 32 + 3) & ~3;
+      // row values: one float per (row, segment); one-chunk rows park four
+      // per (row, segment, lane)
+      xr = std::max(xr, p.rowoff + ((nrb + G - 1) / G) * DSEGS * (p.one ? 128 : 1));
     }
   // weight-stream schedule: per CTA and GEMV its rows and first stage within
   // the token, and one descriptor per stage
@@ -1008,8 +1070,11 @@ int launch_decode(pb_state* s, int ntok, cudaStream_t st) {
   int rc = build_phases(s);
   if (rc) return rc;
   const bool f = s->m->sdt == PB_DT_F32;
-  if (persistent_shape(s->m))
+  if (persistent_shape(s->m)) {
+    if (s->m->HD == 128)
+      return f ? launch_decode_t<true, 4, 8, 7>(s, ntok, st) : launch_decode_t<false, 4, 8, 7>(s, ntok, st);
     return f ? launch_decode_t<true, 2, 8, 3>(s, ntok, st) : launch_decode_t<false, 2, 8, 3>(s, ntok, st);
+  }
   return pb_set_error(PB_ENOTSUP, "persistent decode: shape not compiled");
 }
 
@@ -1178,10 +1243,11 @@ extern "C" int pb_open(const char* path, int device, pb_model** out) {
   size_t need = 0;
   auto plan_q8 = [&](pb_q8& w, int N, int K) {
     w.N = N; w.K = K; w.owner = false;
-    w.layout = pb_q8_stream_ok(K) ? PB_Q8_STREAM : PB_Q8_ROWMAJOR;
-    w.nch = w.layout == PB_Q8_STREAM ? K / 2048 : 1;
-    need += align256((size_t)N * K);
-    need += align256((size_t)N * (K / 32) * 4);
+    const int nch = pb_q8_stream_chunks(K, &w.one);
+    w.layout = nch ? PB_Q8_STREAM : PB_Q8_ROWMAJOR;
+    w.nch = nch ? nch : 1;
+    need += align256(pb_q8_code_bytes(N, K));
+    need += align256(pb_q8_layout_scale_bytes(N, K, PB_DT_F32));   // room for fp32 scales
     if (w.layout != PB_Q8_STREAM) m->decode_ok = false;
   };
   const int H = m->H, F = m->F, NH = m->NH, NKV = m->NKV, HD = m->HD, W = m->W;
@@ -1268,9 +1334,9 @@ extern "C" int pb_open(const char* path, int device, pb_model** out) {
     for (auto* p : assigned) if (p == w) return;
     w->sdt = m->sdt;
     w->codes = reinterpret_cast<int8_t*>(m->arena + cursor);
-    cursor += align256((size_t)w->N * w->K);
+    cursor += align256(pb_q8_code_bytes(w->N, w->K));
     w->scales = m->arena + cursor;
-    cursor += align256((size_t)w->N * (w->K / 32) * 4);
+    cursor += align256(pb_q8_layout_scale_bytes(w->N, w->K, PB_DT_F32));
     assigned.push_back(w);
   };
   for (auto& p : q8pieces) assign(p.dst);
@@ -1361,7 +1427,7 @@ extern "C" int pb_tensor_id(const pb_model* m, const char* name) {
 extern "C" int pb_state_create(pb_model* m, int max_ctx, pb_state** out) {
   if (!m || !out || max_ctx <= 0) return pb_set_error(PB_EINVAL, "pb_state_create: bad argument");
   *out = nullptr;
-  if (!m->decode_ok) return pb_set_error(PB_ENOTSUP, "decode needs every matrix K to be a multiple of 2048");
+  if (!m->decode_ok) return pb_set_error(PB_ENOTSUP, "decode needs every matrix in the streaming layout (K up to 16384)");
   if ((size_t)max_ctx * 4 > 160 * 1024) return pb_set_error(PB_ENOTSUP, "max_ctx %d too large", max_ctx);
   PB_TRY_CUDA(cudaSetDevice(m->device));
   pb_state* s = new pb_state();
@@ -1967,9 +2033,8 @@ extern "C" int pb_prefill_chunk(pb_model* m, pb_state* s, const int* d_tokens, i
   if (!m || !s || !d_tokens || T <= 0) return pb_set_error(PB_EINVAL, "pb_prefill_chunk: bad argument");
   if (T % 16 || T > 256) return pb_set_error(PB_ENOTSUP, "pb_prefill_chunk: T=%d (a multiple of 16, at most 256)", T);
   if (pos0 < 0 || pos0 + T > s->max_ctx) return pb_set_error(PB_EINVAL, "pb_prefill_chunk: positions beyond max_ctx");
-  if (m->H != 2048 || m->HD != 64 || m->W != 3 || m->F % 256 || m->F / 256 > 32 || (m->NH * m->HD) != 2048)
-    return pb_set_error(PB_ENOTSUP, "pb_prefill_chunk: shape not compiled");
-  if (!m->decode_ok) return pb_set_error(PB_ENOTSUP, "pb_prefill_chunk: needs every K a multiple of 2048");
+  if (!chunk_shape(m)) return pb_set_error(PB_ENOTSUP, "pb_prefill_chunk: shape not compiled");
+  if (!m->decode_ok) return pb_set_error(PB_ENOTSUP, "pb_prefill_chunk: needs every matrix in the streaming layout");
   PB_TRY_CUDA(cudaSetDevice(m->device));
   cudaStream_t st = (cudaStream_t)stream;
   int rc = prefill_prepare(m, s, T, st);
@@ -1994,13 +2059,20 @@ extern "C" int pb_prefill_chunk(pb_model* m, pb_state* s, const int* d_tokens, i
       q.kc = s->kv + (size_t)Ly.attn_idx * 2 * per;
       q.vc = q.kc + per;
       q.nq = nq; q.nh = m->NH; q.nkv = m->NKV; q.half = layer_half(m, L); q.pos0 = pos0; q.eps = m->eps;
-      k_pf_qkv<2><<<T, 256, 0, st>>>(q);
+      if (m->HD == 128) k_pf_qkv<4><<<T, 256, 0, st>>>(q);
+      else k_pf_qkv<2><<<T, 256, 0, st>>>(q);
       PB_LAUNCHED("k_pf_qkv");
       AttnArgs a = attn_args(m, s, L);
       a.qkvg = s->pf_qkvg;
       a.out = s->pf_att;
-      PB_TRY_CUDA(cudaFuncSetAttribute(k_pf_attn<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, 160 * 1024));
-      k_pf_attn<2><<<dim3(m->NH, T), 256, (size_t)s->max_ctx * sizeof(float), st>>>(a, pos0, nq, m->NH * m->HD);
+      const size_t asm_b = (size_t)s->max_ctx * sizeof(float);
+      if (m->HD == 128) {
+        PB_TRY_CUDA(cudaFuncSetAttribute(k_pf_attn<4>, cudaFuncAttributeMaxDynamicSharedMemorySize, 160 * 1024));
+        k_pf_attn<4><<<dim3(m->NH, T), 256, asm_b, st>>>(a, pos0, nq, m->NH * m->HD);
+      } else {
+        PB_TRY_CUDA(cudaFuncSetAttribute(k_pf_attn<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, 160 * 1024));
+        k_pf_attn<2><<<dim3(m->NH, T), 256, asm_b, st>>>(a, pos0, nq, m->NH * m->HD);
+      }
       PB_LAUNCHED("k_pf_attn");
       k_pf_quant<8><<<T, 256, 0, st>>>(s->pf_att, m->NH * m->HD, s->pf_qx, s->pf_dx);
       PB_LAUNCHED("k_pf_quant");
@@ -2013,7 +2085,8 @@ extern "C" int pb_prefill_chunk(pb_model* m, pb_state* s, const int* d_tokens, i
       c.dx = s->pf_dx;
       c.H = H;
       c.pos0 = pos0;
-      k_pf_conv_quant<8, 3><<<T, 256, 0, st>>>(c);
+      if (m->W == 7) k_pf_conv_quant<8, 7><<<T, 256, 0, st>>>(c);
+      else k_pf_conv_quant<8, 3><<<T, 256, 0, st>>>(c);
       PB_LAUNCHED("k_pf_conv_quant");
       k_pf_ring<<<dim3((H + 255) / 256, m->W), 256, 0, st>>>(s->pf_y, s->ring + (size_t)Ly.conv_idx * m->W * H,
                                                              H, m->W, T, pos0);
@@ -2064,9 +2137,8 @@ extern "C" int pb_decode_batch(pb_model* m, pb_state* const* states, int B, cons
                                int* d_ids, float* d_logits, void* stream) {
   if (!m || !states || !d_tokens || !d_pos || !d_ids || B <= 0) return pb_set_error(PB_EINVAL, "pb_decode_batch: bad argument");
   if (B % 16 || B > 256) return pb_set_error(PB_ENOTSUP, "pb_decode_batch: B=%d (a multiple of 16, at most 256)", B);
-  if (m->H != 2048 || m->HD != 64 || m->W != 3 || m->F % 256 || m->F / 256 > 32 || (m->NH * m->HD) != 2048)
-    return pb_set_error(PB_ENOTSUP, "pb_decode_batch: shape not compiled");
-  if (!m->decode_ok) return pb_set_error(PB_ENOTSUP, "pb_decode_batch: needs every K a multiple of 2048");
+  if (!chunk_shape(m)) return pb_set_error(PB_ENOTSUP, "pb_decode_batch: shape not compiled");
+  if (!m->decode_ok) return pb_set_error(PB_ENOTSUP, "pb_decode_batch: needs every matrix in the streaming layout");
   int max_ctx = 0;
   for (int b = 0; b < B; b++) {
     if (!states[b] || states[b]->m != m) return pb_set_error(PB_EINVAL, "pb_decode_batch: state %d is not of this model", b);
@@ -2130,10 +2202,16 @@ extern "C" int pb_decode_batch(pb_model* m, pb_state* const* states, int B, cons
       a.slide = Ly.slide ? 1 : 0;
       a.eps = m->eps;
       a.scaling = 1.0f / sqrtf((float)m->HD);
-      k_bd_qkv<2><<<B, 256, 0, st>>>(a);
+      if (m->HD == 128) k_bd_qkv<4><<<B, 256, 0, st>>>(a);
+      else k_bd_qkv<2><<<B, 256, 0, st>>>(a);
       PB_LAUNCHED("k_bd_qkv");
-      PB_TRY_CUDA(cudaFuncSetAttribute(k_bd_attn<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, 160 * 1024));
-      k_bd_attn<2><<<dim3(m->NH, B), 256, (size_t)max_ctx * sizeof(float), st>>>(a);
+      if (m->HD == 128) {
+        PB_TRY_CUDA(cudaFuncSetAttribute(k_bd_attn<4>, cudaFuncAttributeMaxDynamicSharedMemorySize, 160 * 1024));
+        k_bd_attn<4><<<dim3(m->NH, B), 256, (size_t)max_ctx * sizeof(float), st>>>(a);
+      } else {
+        PB_TRY_CUDA(cudaFuncSetAttribute(k_bd_attn<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, 160 * 1024));
+        k_bd_attn<2><<<dim3(m->NH, B), 256, (size_t)max_ctx * sizeof(float), st>>>(a);
+      }
       PB_LAUNCHED("k_bd_attn");
       k_pf_quant<8><<<B, 256, 0, st>>>(ws->pf_att, m->NH * m->HD, ws->pf_qx, ws->pf_dx);
       PB_LAUNCHED("k_pf_quant");
@@ -2147,7 +2225,8 @@ extern "C" int pb_decode_batch(pb_model* m, pb_state* const* states, int B, cons
       c.H = H;
       c.qx = ws->pf_qx;
       c.dx = ws->pf_dx;
-      k_bd_conv_quant<8, 3><<<B, 256, 0, st>>>(c);
+      if (m->W == 7) k_bd_conv_quant<8, 7><<<B, 256, 0, st>>>(c);
+      else k_bd_conv_quant<8, 3><<<B, 256, 0, st>>>(c);
       PB_LAUNCHED("k_bd_conv_quant");
     }
     if ((rc = pb_q80_gemm(&tc[1], B, ws->pf_qx, ws->pf_dx, ws->pf_y, nullptr, st))) return rc;

@@ -209,10 +209,13 @@ __global__ void __launch_bounds__(256) k_pf_quant(const bf16_t* __restrict__ x, 
 
 // SwiGLU on the interleaved w1|w3 outputs (k_silu_mul_bf, lfm3_nanode.cu:821-829),
 // then quantised (the w2 input)
+// (F = 256 E, or with E = 32 any multiple of 32 up to 8192: a thread then
+// holds one whole 32-block, and threads past F have none)
 template <int E>
 __global__ void __launch_bounds__(256) k_pf_silu_quant(const float* __restrict__ y, int F, int8_t* __restrict__ qx,
                                                        uint16_t* __restrict__ dx) {
   const int t = blockIdx.x, th = threadIdx.x;
+  if (E == 32 && th * E >= F) return;
   float u[E];
 #pragma unroll
   for (int j = 0; j < E; j++) {

@@ -9,12 +9,16 @@
 // the 32 leaves combine by the shuffle-down tree (16, 8, 4, 2, 1); chunk
 // partials are summed ascending from 0; the Linear output is bf16(that sum).
 //
-// Streaming layout (PB_Q8_STREAM, K % 2048 == 0): the codes of (row, chunk)
+// Streaming layout (PB_Q8_STREAM): the codes of (row, chunk)
 // form one 2048-byte segment of 128 16-byte granules; granule h*32 + l holds
 // codes [16(h&1), 16(h&1)+16) of block l + 32(h>>1). Lane l of a warp reads
 // granules l, 32+l, 64+l, 96+l -- each warp load instruction is one contiguous
 // 512-byte run -- and owns exactly leaf l. Scales of a segment are 32 pairs
-// (s_l, s_{l+32}), one 4-byte (fp16) or 8-byte (fp32) load per lane.
+// (s_l, s_{l+32}), one 4-byte (fp16) or 8-byte (fp32) load per lane. A K that
+// 2048 does not divide is reduced as one chunk (pick(), lfm3_nanode.cu:
+// 1763-1768): its rows are padded with zero blocks (codes and scales) to whole
+// segments, and lane l's chain runs on from segment to segment before the one
+// tree (a zero block adds fma(0, 0, acc) = acc exactly).
 #include "pb_common.cuh"
 #include "pb_internal.h"
 #include <cstdio>
@@ -27,7 +31,7 @@
 __global__ void k_q8_pack_codes(const uint4* __restrict__ src, uint4* __restrict__ dst,
                                 int R, int K, int rmul, int radd) {
   // one thread per source granule of the destination order
-  const int nch = K / 2048;
+  const int nch = (K + 2047) / 2048;
   const size_t total = (size_t)R * nch * 128;
   const size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
   if (i >= total) return;
@@ -37,12 +41,13 @@ __global__ void k_q8_pack_codes(const uint4* __restrict__ src, uint4* __restrict
   const int c = (int)(seg - row * nch);
   const int blk = c * 64 + l + 32 * (h >> 1);
   const size_t drow = row * rmul + radd;
-  dst[(drow * nch + c) * 128 + gi] = src[(row * (size_t)K + (size_t)blk * 32 + 16 * (h & 1)) >> 4];
+  dst[(drow * nch + c) * 128 + gi] =
+      blk < K / 32 ? src[(row * (size_t)K + (size_t)blk * 32 + 16 * (h & 1)) >> 4] : make_uint4(0, 0, 0, 0);
 }
 template <typename ST>
 __global__ void k_q8_pack_scales(const ST* __restrict__ src, ST* __restrict__ dst, int R, int K,
                                  int rmul, int radd) {
-  const int nch = K / 2048, nb = K / 32;
+  const int nch = (K + 2047) / 2048, nb = K / 32;
   const size_t total = (size_t)R * nch * 32;
   const size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
   if (i >= total) return;
@@ -51,8 +56,8 @@ __global__ void k_q8_pack_scales(const ST* __restrict__ src, ST* __restrict__ ds
   const size_t row = seg / nch;
   const int c = (int)(seg - row * nch);
   const size_t d = ((row * rmul + radd) * nch + c) * 32 + l;
-  dst[2 * d] = src[row * nb + c * 64 + l];
-  dst[2 * d + 1] = src[row * nb + c * 64 + l + 32];
+  dst[2 * d] = c * 64 + l < nb ? src[row * nb + c * 64 + l] : (ST)0;
+  dst[2 * d + 1] = c * 64 + l + 32 < nb ? src[row * nb + c * 64 + l + 32] : (ST)0;
 }
 
 // ------------------------------------------------------ fast streaming GEMV
@@ -80,10 +85,16 @@ struct ScalePair<true> {
   }
 };
 
-PB_DEV void pb_load_x64(const bf16_t* __restrict__ xc, int lane, float (&xr)[64]) {
-  // xr[0..31] = x[32*lane .. +31], xr[32..63] = x[1024 + 32*lane .. +31]
+PB_DEV void pb_load_x64(const bf16_t* __restrict__ xc, int lane, float (&xr)[64], int nvalid = 2048) {
+  // xr[0..31] = x[32*lane .. +31], xr[32..63] = x[1024 + 32*lane .. +31];
+  // blocks at or past nvalid (a one-chunk tensor's padding) read as zero
 #pragma unroll
   for (int half = 0; half < 2; half++) {
+    if (half * 1024 + lane * 32 >= nvalid) {
+#pragma unroll
+      for (int j = 0; j < 32; j++) xr[half * 32 + j] = 0.0f;
+      continue;
+    }
     const uint4* p = reinterpret_cast<const uint4*>(xc + half * 1024 + lane * 32);
 #pragma unroll
     for (int v = 0; v < 4; v++) {
@@ -110,6 +121,29 @@ PB_DEV float pb_dot16(const uint4 g, const float* xr, float dot) {
   return dot;
 }
 
+// the dots of this lane's two blocks (l and l+32 of the segment)
+PB_DEV void pb_dots(const uint4 (&q)[4], const float (&xr)[64], float& d0, float& d1) {
+  d0 = pb_dot16(q[0], xr, 0.0f);
+  d0 = pb_dot16(q[1], xr + 16, d0);
+  d1 = pb_dot16(q[2], xr + 32, 0.0f);
+  d1 = pb_dot16(q[3], xr + 48, d1);
+}
+
+// one-chunk rows: segment c's (dot_lo, dot_hi, s_lo, s_hi) of every lane,
+// chained in segment order (acc = fma(s, dot, acc), blocks l, l+32, l+64, ...)
+// then one tree; lane 0 holds the row's chunk value
+template <int NCH>
+PB_DEV float pb_one_chain(const float4* p, int lane) {
+  float acc = 0.0f;
+#pragma unroll
+  for (int c = 0; c < NCH; c++) {
+    const float4 v = p[c * 32 + lane];
+    acc = __fmaf_rn(v.z, v.x, acc);
+    acc = __fmaf_rn(v.w, v.y, acc);
+  }
+  return pb_warp_tree(acc);
+}
+
 // one row's leaf value for this lane: blocks l and l+32 of the chunk
 PB_DEV float pb_leaf(const uint4 (&q)[4], float slo, float shi, const float (&xr)[64]) {
   float d0 = pb_dot16(q[0], xr, 0.0f);
@@ -120,16 +154,18 @@ PB_DEV float pb_leaf(const uint4 (&q)[4], float slo, float shi, const float (&xr
   return __fmaf_rn(shi, d1, acc);
 }
 
-template <int NCH, int U, bool F32S, bool OUTF32>
+template <int NCH, int U, bool F32S, bool OUTF32, bool ONE>
 __global__ void __launch_bounds__(256, 2)
 k_q8f_stream(const uint4* __restrict__ codes, const void* __restrict__ scales,
-             const bf16_t* __restrict__ x, void* __restrict__ y, int N) {
+             const bf16_t* __restrict__ x, void* __restrict__ y, int N, int K) {
   constexpr int G = 8 / NCH, RB = G * U;
+  static_assert(!ONE || (NCH > 1 && RB <= 8), "one-chunk rows: a warp per row");
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int c = warp % NCH, g = warp / NCH;
   __shared__ float part[2][RB][NCH];
+  __shared__ float4 partq[ONE ? 2 : 1][ONE ? RB : 1][ONE ? NCH * 32 : 1];
   float xr[64];
-  pb_load_x64(x + c * 2048, lane, xr);
+  pb_load_x64(x + c * 2048, lane, xr, K - c * 2048);
   int it = 0;
   for (int rb = blockIdx.x; rb * RB < N; rb += gridDim.x, it ^= 1) {
     const int row0 = rb * RB + g * U;
@@ -150,29 +186,47 @@ k_q8f_stream(const uint4* __restrict__ codes, const void* __restrict__ scales,
         slo[u] = shi[u] = 0.0f;
       }
     }
+    if constexpr (ONE) {
 #pragma unroll
-    for (int u = 0; u < U; u++) {
-      const float v = pb_warp_tree(pb_leaf(q[u], slo[u], shi[u], xr));
-      const int row = row0 + u;
-      if (NCH == 1) {
+      for (int u = 0; u < U; u++) {
+        float d0, d1;
+        pb_dots(q[u], xr, d0, d1);
+        partq[it][g * U + u][c * 32 + lane] = make_float4(d0, d1, slo[u], shi[u]);
+      }
+      __syncthreads();
+      if (warp < RB) {
+        const int row = rb * RB + warp;
+        const float v = pb_one_chain<NCH>(&partq[it][warp][0], lane);
         if (lane == 0 && row < N) {
           if (OUTF32) reinterpret_cast<float*>(y)[row] = __fadd_rn(0.0f, v);
           else reinterpret_cast<bf16_t*>(y)[row] = pb_f2bf(__fadd_rn(0.0f, v));
         }
-      } else if (lane == 0) {
-        part[it][g * U + u][c] = v;
       }
-    }
-    if (NCH > 1) {
-      __syncthreads();
-      if (threadIdx.x < RB) {
-        const int row = rb * RB + threadIdx.x;
-        if (row < N) {
-          float acc = 0.0f;
+    } else {
 #pragma unroll
-          for (int cc = 0; cc < NCH; cc++) acc = __fadd_rn(acc, part[it][threadIdx.x][cc]);
-          if (OUTF32) reinterpret_cast<float*>(y)[row] = acc;
-          else reinterpret_cast<bf16_t*>(y)[row] = pb_f2bf(acc);
+      for (int u = 0; u < U; u++) {
+        const float v = pb_warp_tree(pb_leaf(q[u], slo[u], shi[u], xr));
+        const int row = row0 + u;
+        if (NCH == 1) {
+          if (lane == 0 && row < N) {
+            if (OUTF32) reinterpret_cast<float*>(y)[row] = __fadd_rn(0.0f, v);
+            else reinterpret_cast<bf16_t*>(y)[row] = pb_f2bf(__fadd_rn(0.0f, v));
+          }
+        } else if (lane == 0) {
+          part[it][g * U + u][c] = v;
+        }
+      }
+      if (NCH > 1) {
+        __syncthreads();
+        if (threadIdx.x < RB) {
+          const int row = rb * RB + threadIdx.x;
+          if (row < N) {
+            float acc = 0.0f;
+#pragma unroll
+            for (int cc = 0; cc < NCH; cc++) acc = __fadd_rn(acc, part[it][threadIdx.x][cc]);
+            if (OUTF32) reinterpret_cast<float*>(y)[row] = acc;
+            else reinterpret_cast<bf16_t*>(y)[row] = pb_f2bf(acc);
+          }
         }
       }
     }
@@ -337,11 +391,11 @@ int pb_q8_pack_into(pb_q8* w, const int8_t* d_codes, const void* d_scales, cudaS
     }
     return PB_OK;
   }
-  const size_t ng = (size_t)R * (K / 2048) * 128;
+  const size_t ng = (size_t)R * w->nch * 128;
   k_q8_pack_codes<<<(unsigned)((ng + 255) / 256), 256, 0, st>>>(
       reinterpret_cast<const uint4*>(d_codes), reinterpret_cast<uint4*>(w->codes), R, K, rmul, radd);
   PB_LAUNCHED("k_q8_pack_codes");
-  const size_t ns = (size_t)R * (K / 2048) * 32;
+  const size_t ns = (size_t)R * w->nch * 32;
   if (w->sdt == PB_DT_F32)
     k_q8_pack_scales<float><<<(unsigned)((ns + 255) / 256), 256, 0, st>>>(
         reinterpret_cast<const float*>(d_scales), reinterpret_cast<float*>(w->scales), R, K, rmul, radd);
@@ -353,7 +407,7 @@ int pb_q8_pack_into(pb_q8* w, const int8_t* d_codes, const void* d_scales, cudaS
   return PB_OK;
 }
 
-template <int NCH, int U>
+template <int NCH, int U, bool ONE>
 static int launch_stream(const pb_q8* w, const uint16_t* x, void* y, int outf32, cudaStream_t st) {
   constexpr int RB = (8 / NCH) * U;
   const int nrb = (w->N + RB - 1) / RB;
@@ -361,10 +415,10 @@ static int launch_stream(const pb_q8* w, const uint16_t* x, void* y, int outf32,
   if (grid > nrb) grid = nrb;
   const uint4* q = reinterpret_cast<const uint4*>(w->codes);
   const bool f32s = w->sdt == PB_DT_F32;
-  if (f32s && outf32) k_q8f_stream<NCH, U, true, true><<<grid, 256, 0, st>>>(q, w->scales, x, y, w->N);
-  else if (f32s) k_q8f_stream<NCH, U, true, false><<<grid, 256, 0, st>>>(q, w->scales, x, y, w->N);
-  else if (outf32) k_q8f_stream<NCH, U, false, true><<<grid, 256, 0, st>>>(q, w->scales, x, y, w->N);
-  else k_q8f_stream<NCH, U, false, false><<<grid, 256, 0, st>>>(q, w->scales, x, y, w->N);
+  if (f32s && outf32) k_q8f_stream<NCH, U, true, true, ONE><<<grid, 256, 0, st>>>(q, w->scales, x, y, w->N, w->K);
+  else if (f32s) k_q8f_stream<NCH, U, true, false, ONE><<<grid, 256, 0, st>>>(q, w->scales, x, y, w->N, w->K);
+  else if (outf32) k_q8f_stream<NCH, U, false, true, ONE><<<grid, 256, 0, st>>>(q, w->scales, x, y, w->N, w->K);
+  else k_q8f_stream<NCH, U, false, false, ONE><<<grid, 256, 0, st>>>(q, w->scales, x, y, w->N, w->K);
   PB_LAUNCHED("k_q8f_stream");
   return PB_OK;
 }
@@ -373,10 +427,10 @@ int pb_q8_gemv_launch(const pb_q8* w, const uint16_t* d_x, void* d_y, int y_dtyp
   const int outf32 = y_dtype == PB_DT_F32;
   if (w->layout == PB_Q8_STREAM) {
     switch (w->nch) {
-      case 1: return launch_stream<1, 2>(w, d_x, d_y, outf32, st);
-      case 2: return launch_stream<2, 2>(w, d_x, d_y, outf32, st);
-      case 4: return launch_stream<4, 2>(w, d_x, d_y, outf32, st);
-      case 8: return launch_stream<8, 2>(w, d_x, d_y, outf32, st);
+      case 1: return launch_stream<1, 2, false>(w, d_x, d_y, outf32, st);   // one chunk either way
+      case 2: return w->one ? launch_stream<2, 2, true>(w, d_x, d_y, outf32, st) : launch_stream<2, 2, false>(w, d_x, d_y, outf32, st);
+      case 4: return w->one ? launch_stream<4, 2, true>(w, d_x, d_y, outf32, st) : launch_stream<4, 2, false>(w, d_x, d_y, outf32, st);
+      case 8: return w->one ? launch_stream<8, 2, true>(w, d_x, d_y, outf32, st) : launch_stream<8, 2, false>(w, d_x, d_y, outf32, st);
       default: return pb_set_error(PB_EINVAL, "stream layout with %d chunks", w->nch);
     }
   }
@@ -397,13 +451,16 @@ extern "C" int pb_q8_pack(const int8_t* codes, const void* scales, int scale_dty
   cudaStream_t st = (cudaStream_t)stream;
   pb_q8* w = new pb_q8();
   w->N = N; w->K = K; w->sdt = scale_dtype;
-  w->layout = pb_q8_stream_ok(K) ? PB_Q8_STREAM : PB_Q8_ROWMAJOR;
-  w->nch = w->layout == PB_Q8_STREAM ? K / 2048 : 1;
+  const int nch = pb_q8_stream_chunks(K, &w->one);
+  w->layout = nch ? PB_Q8_STREAM : PB_Q8_ROWMAJOR;
+  w->nch = nch ? nch : 1;
+  // source sizes (row-major) and device sizes (the tensor's layout)
   const size_t cb = (size_t)N * K, sb = pb_q8_scale_bytes(N, K, scale_dtype);
-  if (cudaMalloc(&w->codes, cb) != cudaSuccess || cudaMalloc(&w->scales, sb) != cudaSuccess) {
+  const size_t dcb = pb_q8_code_bytes(N, K), dsb = pb_q8_layout_scale_bytes(N, K, scale_dtype);
+  if (cudaMalloc(&w->codes, dcb) != cudaSuccess || cudaMalloc(&w->scales, dsb) != cudaSuccess) {
     cudaGetLastError();
     cudaFree(w->codes); cudaFree(w->scales); delete w;
-    return pb_set_error(PB_ENOMEM, "pb_q8_pack: cannot allocate %zu bytes", cb + sb);
+    return pb_set_error(PB_ENOMEM, "pb_q8_pack: cannot allocate %zu bytes", dcb + dsb);
   }
   int rc = PB_OK;
   int8_t* tc = nullptr; void* ts = nullptr;

@@ -471,11 +471,13 @@ __global__ void k_q80tc_pack(const int8_t* __restrict__ codes, const S* __restri
 
 // the same tiles from a tensor in the streaming layout (pb_q8.cu): granule
 // h*32 + l of segment (row, chunk) holds codes [16(h&1), +16) of block
-// l + 32(h>>1) of the chunk; scales are pairs (s_l, s_{l+32}) per segment
+// l + 32(h>>1) of the chunk; scales are pairs (s_l, s_{l+32}) per segment;
+// only the K / 32 real blocks are copied (the integer fold is block-serial,
+// whatever the float path's chunking)
 template <typename S>
 __global__ void k_q80tc_from_stream(const uint4* __restrict__ codes, const S* __restrict__ scales, int N, int K,
                                     int ntile, int8_t* __restrict__ a, S* __restrict__ dw) {
-  const int nblk = K / 32, nch = K / 2048;
+  const int nblk = K / 32, nch = (K + 2047) / 2048;   // segments per row (a one-chunk row is padded)
   const size_t total = (size_t)ntile * TC_M * nblk * 2;
   for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (size_t)gridDim.x * blockDim.x) {
     const int kh = (int)(i & 1);

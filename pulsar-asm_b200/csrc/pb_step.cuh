@@ -219,14 +219,25 @@ __device__ void rms_reg(const float (&v)[E], const float (&wv)[E], float (&out)[
 // plain GEMV input: K = 256 EK values, EK consecutive per thread
 template <int EK, int SYNC>
 __device__ void pro_plain(const StepArgs& a, float* sx, const GridWait* gw) {
+  // 256 EK values staged: K of them from the input, zeros after it (a
+  // one-chunk tensor's padding; K is a multiple of 32, so a thread's EK
+  // values are all inside or all past it)
   const int t = threadIdx.x;
   const bf16_t* xin = a.xin;
   gw_pass<SYNC>(gw);
   float x[EK];
-  ld_bf<EK, SYNC>(xin + (size_t)t * EK, x);
+  if (t * EK < a.K) {
+    ld_bf<EK, SYNC>(xin + (size_t)t * EK, x);
+  } else {
+#pragma unroll
+    for (int j = 0; j < EK; j++) x[j] = 0.0f;
+  }
 #pragma unroll
   for (int j = 0; j < EK; j++) sx[padx(t * EK + j)] = x[j];
 }
+// staged length of a GEMV input: K rounded up to whole 2048-code segments
+// (the streaming layout; K itself when 2048 divides it)
+__host__ __device__ __forceinline__ int pb_kpad(int K) { return (K + 2047) / 2048 * 2048; }
 
 // gated short conv (lfm3_nanode.cu:3790-3818): bx = bf16(B*x) enters the ring
 // as the newest slot; y = sum_k taps[i][k] * ring_k (oldest first), one fp32
@@ -377,7 +388,7 @@ template <int SYNC>
 __device__ __noinline__ void step_prologue(const StepArgs& a, float* sx, float* red, const GridWait* gw, int pos) {
   const int pro = a.pro;
   if (pro == PRO_PLAIN) {
-    switch (a.K >> 8) {
+    switch (pb_kpad(a.K) >> 8) {
       case 1: pro_plain<1, SYNC>(a, sx, gw); break;
       case 2: pro_plain<2, SYNC>(a, sx, gw); break;
       case 4: pro_plain<4, SYNC>(a, sx, gw); break;
@@ -424,7 +435,7 @@ __device__ __forceinline__ void step_prologue_fixed(const StepArgs& a, float* sx
                                                     int pos) {
   const int pro = a.pro;
   if (pro == PRO_PLAIN) {
-    switch (a.K >> 8) {
+    switch (pb_kpad(a.K) >> 8) {
       case 8: pro_plain<8, SYNC>(a, sx, gw); break;
       case 16: pro_plain<16, SYNC>(a, sx, gw); break;
       case 32: pro_plain<32, SYNC>(a, sx, gw); break;
