@@ -54,7 +54,8 @@ int pb_q8_pack(const int8_t* codes, const void* scales, int scale_dtype, int N, 
 int pb_q8_free(pb_q8* w);
 int pb_q8_shape(const pb_q8* w, int* N, int* K);
 /* y = W x, REF_FLOAT numerics: bf16 x, fp32 FMA chains in the reference's
- * 32-leaf tree order, K-chunks of 2048 summed ascending, output rounded to
+ * 32-leaf tree order, K-chunks of 2048 summed ascending (a K that 2048 does
+ * not divide is one chunk, pick() :1763-1768), output rounded to
  * bf16 (y_dtype PB_DT_BF16, the Linear) or kept fp32 (PB_DT_F32, the head).
  * Replaces gemv() lfm3_nanode.cu:1916-1966 (q8_partial + k_combine_bf) and
  * gemv_f() :3634-3664 (q8_partial + k_combine_f).                            */
@@ -63,6 +64,17 @@ int pb_q8_gemv(const pb_q8* w, const uint16_t* d_x, void* d_y, int y_dtype, void
  * prefill pf_gemv_T (lfm3_nanode.cu:4840-4968), bit-identical per position.  */
 int pb_q8_gemm(const pb_q8* w, int T, const uint16_t* d_x, void* d_y, int y_dtype,
                void* stream);
+
+/* The certified arm's head over the bf16 tied table (blob dtype 3): logits[n]
+ * = the 32 lane chains s = s + bf16(W[n][k]) * x[k] (k = l, l+32, ...;
+ * product and sum rounded apart) combined by the shuffle-down tree, fp32 as
+ * is. Replaces k_gemv_bf16 / lm_head_bf16, lfm3_nanode.cu:3517-3560. The table
+ * is first re-laid (d_src [N][K] row-major bf16 -> d_dst, 16-byte aligned,
+ * N*K*2 bytes; K a multiple of 256); pb_bf16_gemv takes the re-laid table,
+ * K = 1024, 2048 or 4096. A .lfm3q8 model with a dtype-3 embedding uses the
+ * same head inside every decode path.                                        */
+int pb_bf16_relayout(const uint16_t* d_src, uint16_t* d_dst, int N, int K, void* stream);
+int pb_bf16_gemv(const uint16_t* d_w, int N, int K, const uint16_t* d_x, float* d_y, void* stream);
 
 /* Q8_0 x Q8_0 integer path. x (fp32) is quantised per 32-block to int8 codes
  * and fp16 scales (fwd35_ref.c:332-343); y[n] = sum_b (dw*dx)*(float)isum_b in

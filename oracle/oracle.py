@@ -79,6 +79,8 @@ def lib():
         L.pbo_model_set_q8.argtypes = [vp, i, i, vp, vp, i, i]
         L.pbo_model_set_f32.argtypes = [vp, i, i, vp]
         L.pbo_model_set_int.argtypes = [vp, i]
+        L.pbo_model_set_emb_bf16.argtypes = [vp, vp]
+        L.pbo_gemv_bf16.argtypes = [vp, i, i, vp, vp]
         L.pbo_state_new.restype = vp; L.pbo_state_new.argtypes = [vp]
         L.pbo_state_free.argtypes = [vp]
         L.pbo_decode.restype = i; L.pbo_decode.argtypes = [vp, vp, i, i, vp, vp]
@@ -149,6 +151,15 @@ def q8f_gemv(codes, scales_f32, x_bf16):
     y = np.zeros((T, N), np.float32)
     lib().pbo_q8f_gemm(_p(codes), _p(scales_f32), N, K, T, _p(np.ascontiguousarray(x_bf16)), _p(y))
     return y[0] if x_bf16.ndim == 1 else y
+
+
+def gemv_bf16(w_bf16, x_bf16):
+    """k_gemv_bf16 (the bf16 head): w [N][K] bf16 bits, x [K] bf16 bits -> fp32 [N]"""
+    N, K = w_bf16.shape
+    y = np.zeros(N, np.float32)
+    lib().pbo_gemv_bf16(_p(np.ascontiguousarray(w_bf16, np.uint16)), N, K,
+                        _p(np.ascontiguousarray(x_bf16, np.uint16)), _p(y))
+    return y
 
 
 def q80_quant_act(x):
@@ -234,10 +245,15 @@ class Model:
                     a = np.ascontiguousarray(lw[name], np.float32)
                     self._keep.append(a)
                     L.pbo_model_set_f32(self.m, li, slot, _p(a))
-        codes, sc16 = weights["embed"]
-        s32 = np.ascontiguousarray(h2f_vec(sc16))
-        self._keep += [codes, s32]
-        L.pbo_model_set_q8(self.m, -1, 0, _p(codes), _p(s32), codes.shape[0], codes.shape[1])
+        if "embed_bf16" in weights:
+            e16 = np.ascontiguousarray(weights["embed_bf16"], np.uint16)
+            self._keep.append(e16)
+            L.pbo_model_set_emb_bf16(self.m, _p(e16))
+        else:
+            codes, sc16 = weights["embed"]
+            s32 = np.ascontiguousarray(h2f_vec(sc16))
+            self._keep += [codes, s32]
+            L.pbo_model_set_q8(self.m, -1, 0, _p(codes), _p(s32), codes.shape[0], codes.shape[1])
         fn = np.ascontiguousarray(weights["final_norm"], np.float32)
         self._keep.append(fn)
         L.pbo_model_set_f32(self.m, -1, 0, _p(fn))

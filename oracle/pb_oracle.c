@@ -435,6 +435,24 @@ int pbo_argmax(const float* v, int n) {
   return bi;
 }
 
+/* k_gemv_bf16, lfm3_nanode.cu:3517-3534 (the certified arm's lm_head over the
+ * bf16 embedding, blob dtype 3): row n, lane l chains k = l, l+32, ... of
+ * s = s + bf16(W[n][k]) * x[k] (product and sum rounded apart), then the
+ * shuffle-down tree with rounded adds; the fp32 result is the logit as is. */
+void pbo_gemv_bf16(const uint16_t* w, int N, int K, const uint16_t* x_bf16, float* y) {
+#pragma omp parallel for schedule(static)
+  for (int n = 0; n < N; n++) {
+    float v[32];
+    const uint16_t* wr = w + (size_t)n * K;
+    for (int l = 0; l < 32; l++) {
+      float acc = 0.0f;
+      for (int k = l; k < K; k += 32) acc = acc + pbo_bf2f(wr[k]) * pbo_bf2f(x_bf16[k]);
+      v[l] = acc;
+    }
+    y[n] = tree_down(v, 32);
+  }
+}
+
 /* ------------------------------------------------------- decode step ---- */
 typedef struct { const int8_t* c; const float* s; int N, K; } q8t;
 struct pbo_model {
@@ -444,6 +462,7 @@ struct pbo_model {
   q8t (*q)[PBO_NQ8];
   const float* (*f)[PBO_NF32];
   q8t emb;
+  const uint16_t* emb16;   /* bf16 tied embedding (dtype 3) instead of emb */
   const float* final_norm;
   float* invf;           /* full-attention layers */
   float* invf_slide;     /* sliding-attention layers */
@@ -476,6 +495,7 @@ void pbo_model_set_q8(pbo_model* m, int layer, int slot, const int8_t* codes,
   q8t t = {codes, scales, N, K};
   if (layer < 0) m->emb = t; else m->q[layer][slot] = t;
 }
+void pbo_model_set_emb_bf16(pbo_model* m, const uint16_t* e) { m->emb16 = e; }
 void pbo_model_set_f32(pbo_model* m, int layer, int slot, const float* p) {
   if (layer < 0) m->final_norm = p; else m->f[layer][slot] = p;
 }
@@ -565,9 +585,11 @@ int pbo_decode(const pbo_model* m, pbo_state* s, int token, int pos, float* logi
   const int half_full = (int)((double)c->rope_partial * HD) / 2;
   const int half_slide = (int)((double)c->slide_partial * HD) / 2;
   float* cs = malloc(sizeof(float) * (HD / 2 + 1)); float* sn = malloc(sizeof(float) * (HD / 2 + 1));
-  /* embedding row: bf16(code * scale), k_dequant_row (:138-142) */
+  /* embedding row: bf16(code * scale), k_dequant_row (:138-142); a bf16
+   * embedding's row as it is (lfm3_nanode.cu:6062-6070) */
   for (int i = 0; i < H; i++)
-    x[i] = pbo_f2bf((float)m->emb.c[(size_t)token * H + i] * m->emb.s[(size_t)token * (H / 32) + i / 32]);
+    x[i] = m->emb16 ? m->emb16[(size_t)token * H + i]
+                    : pbo_f2bf((float)m->emb.c[(size_t)token * H + i] * m->emb.s[(size_t)token * (H / 32) + i / 32]);
   for (int L = 0; L < c->n_layers; L++) {
     const q8t* T = m->q[L];
     const float* const* fw = m->f[L];
@@ -617,7 +639,9 @@ int pbo_decode(const pbo_model* m, pbo_state* s, int token, int pos, float* logi
   /* embedding_norm, then the tied head in fp32 (gemv_f + k_combine_f) */
   pbo_rmsnorm(x, m->final_norm, h1, H, c->norm_eps);
   float* lg = logits ? logits : (float*)malloc(sizeof(float) * c->vocab);
-  if (m->int_mode) {
+  if (m->emb16) {
+    pbo_gemv_bf16(m->emb16, c->vocab, H, h1, lg);     /* lm_head_bf16 in either mode (:5172-5175) */
+  } else if (m->int_mode) {
     const q8t head = {m->emb.c, m->emb.s, c->vocab, H};
     gemv_int(&head, h1, lg);
   } else {

@@ -100,6 +100,10 @@ void pbo_model_set_f32(pbo_model* m, int layer, int slot, const float* p);
  * prefill's tensor-core form); 0: the reference's float path (default) */
 void pbo_model_set_int(pbo_model* m, int on);
 /* layer -1: the tied embedding / head (Q8) and the final norm (fp32). */
+/* the tied embedding as bf16 (blob dtype 3): the embedding row is copied and
+ * the head is k_gemv_bf16 (lfm3_nanode.cu:3517-3534) */
+void pbo_model_set_emb_bf16(pbo_model* m, const uint16_t* e);
+void pbo_gemv_bf16(const uint16_t* w, int N, int K, const uint16_t* x_bf16, float* y);
 pbo_state* pbo_state_new(const pbo_model* m);
 void pbo_state_free(pbo_state* s);
 /* one token at position pos; returns the greedy id. logits (fp32 [vocab])

@@ -15,6 +15,7 @@
 #include <cuda_fp16.h>
 
 #define PB_DEV __device__ __forceinline__
+#define PB_HD_INL __host__ __device__ __forceinline__
 
 typedef unsigned short bf16_t;
 

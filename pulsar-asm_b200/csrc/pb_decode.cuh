@@ -82,6 +82,8 @@ struct DPhase {
   const uint4* emb_codes;   // EMBED: tied table, streaming layout
   const void* emb_scales;
   int emb_nch, emb_f32;
+  const uint16_t* emb16;    // EMBED: the bf16 table (head layout) instead
+  int b16;             // GEMV over the bf16 table (the dtype-3 head): 8 rows per stage
   AttnArgs at;         // SCORE, PV
 };
 
@@ -330,7 +332,7 @@ PB_DEV void issue_stage(unsigned k, unsigned slot, unsigned S, unsigned char* ri
   const uint64_t pol = ic->pol;
   mbar_expect_tx(&full[slot], dsc.z + dsc.w);
   bulk_g2s(ring + (size_t)slot * Gm::STAGE, arena + (size_t)dsc.x * 16, dsc.z, &full[slot], pol);
-  bulk_g2s(ring + (size_t)slot * Gm::STAGE + STAGE_CODES, arena + (size_t)dsc.y * 16, dsc.w, &full[slot], pol);
+  if (dsc.w) bulk_g2s(ring + (size_t)slot * Gm::STAGE + STAGE_CODES, arena + (size_t)dsc.y * 16, dsc.w, &full[slot], pol);
   ic->issued[slot] = S + 1;
 }
 // arrival of a warp that finished reading a slot; true for the last of the 8
@@ -367,20 +369,10 @@ PB_DEV void dpro_residual(const DPhase& ph, float* sx, bf16_t* res_s, float* red
   if (!embed) ld_f32<E>(ph.wpost + (size_t)t * E, wp);
   ld_f32<E>(ph.wnorm + (size_t)t * E, wn);
   if (embed) {
-    // k_dequant_row (lfm3_nanode.cu:138-142): bf16(code * scale), row = token;
-    // the row is read from the tied table's streaming layout
-    const int8_t* cb = reinterpret_cast<const int8_t*>(ph.emb_codes);
+    // the token's row of the tied table
 #pragma unroll
-    for (int j = 0; j < E; j++) {
-      const int i = t * E + j;
-      const int b = i >> 5, jj = i & 31, c = b >> 6, bb = b & 63, l = bb & 31, half = bb >> 5;
-      const size_t seg = (size_t)tok_id * ph.emb_nch + c;
-      const int gi = (half * 2 + (jj >> 4)) * 32 + l;
-      const float code = (float)cb[(seg * 128 + gi) * 16 + (jj & 15)];
-      const float s = ph.emb_f32 ? reinterpret_cast<const float*>(ph.emb_scales)[(seg * 32 + l) * 2 + half]
-                                 : pb_h2f(reinterpret_cast<const unsigned short*>(ph.emb_scales)[(seg * 32 + l) * 2 + half]);
-      R[j] = pb_bf2f(pb_f2bf(__fmul_rn(code, s)));
-    }
+    for (int j = 0; j < E; j++)
+      R[j] = emb_value(ph.emb_codes, ph.emb_scales, ph.emb_nch, ph.emb_f32, ph.emb16, H, tok_id, t * E + j);
   } else {
     uint32_t w[E];
     if (!poll_words<E>(ph.tin + (size_t)t * E, tw, w, pc)) poll_fail(pc, 4);
@@ -496,7 +488,11 @@ __device__ __forceinline__ unsigned gemv_phase(const DecodeArgs& d, const DPhase
   const int c = warp % nch, g = warp / nch;
   const unsigned ds = (unsigned)d.ds;
   f2x xr[32];
-  {
+  if (ph.b16) {
+    // the bf16 head's lane chain: x[l + 32 m], m = 0..63, in pairs
+#pragma unroll
+    for (int j = 0; j < 32; j++) xr[j] = pk(sx[lane + 33 * (2 * j)], sx[lane + 33 * (2 * j + 1)]);
+  } else {
     const float* x0 = sx + (c * 64 + lane) * 33;
     const float* x1 = sx + (c * 64 + 32 + lane) * 33;
 #pragma unroll
@@ -526,6 +522,42 @@ __device__ __forceinline__ unsigned gemv_phase(const DecodeArgs& d, const DPhase
     if (tm2 && threadIdx.x == 0) tm2[4] += gtime() - tw0;
 #endif
     const unsigned char* st = ring + (size_t)slot * Gm::STAGE;
+    if (ph.b16) {
+      // bf16 head (k_gemv_bf16, lfm3_nanode.cu:3517-3534): warp w takes row
+      // r + w of the stage's 8 (4 KB each, head layout); lane l's chain over
+      // k = l + 32 m is s = s + bf16(W[k]) * x[k], products and sums rounded
+      // apart; the shuffle-down tree gives the logit as is
+      const bool live = r + warp < r1;
+      const uint4* gp = reinterpret_cast<const uint4*>(st + (size_t)warp * 4096) + lane;
+      uint4 qb[8];
+#pragma unroll
+      for (int h = 0; h < 8; h++) qb[h] = live ? gp[32 * h] : make_uint4(0, 0, 0, 0);
+#pragma unroll
+      for (int h = 0; h < 8; h++) asm volatile("" ::"r"(qb[h].x), "r"(qb[h].y), "r"(qb[h].z), "r"(qb[h].w));
+      __syncwarp();
+      if (lane == 0 && slot_release(slot)) {
+        issue_ctx()->cnt[slot] = 0;
+        if (it + ds < total) issue_stage<F32S>(kn, slot, it + ds, ring, full);
+      }
+      float acc = 0.0f;
+#pragma unroll
+      for (int h = 0; h < 8; h++) {
+        const unsigned ws[4] = {qb[h].x, qb[h].y, qb[h].z, qb[h].w};
+#pragma unroll
+        for (int i = 0; i < 4; i++) {
+          float xa, xb;
+          upk(xr[4 * h + i], xa, xb);
+          acc = __fadd_rn(acc, __fmul_rn(pb_lo2f(ws[i]), xa));
+          acc = __fadd_rn(acc, __fmul_rn(pb_hi2f(ws[i]), xb));
+        }
+      }
+      const float v = pb_warp_tree(acc);
+      if (lane == 0 && live) rowv[(r - r0 + warp) * nch] = v;
+      it++;
+      if (++slot == ds) { slot = 0; par ^= 1; }
+      if (++kn == spt) kn = 0;
+      continue;
+    }
     uint4 q[2][4];
     float slo[2], shi[2];
 #pragma unroll
@@ -648,7 +680,9 @@ __device__ __forceinline__ unsigned gemv_phase(const DecodeArgs& d, const DPhase
     float* out = ph.fout;
     for (int i = threadIdx.x; i < nr; i += DTHREADS) {
       float o = 0.0f;
-      for (int cc = 0; cc < nch; cc++) o = __fadd_rn(o, rowv[i * nch + cc]);
+      if (ph.b16) o = rowv[i * nch];    // the bf16 head's logit is the tree's value
+      else
+        for (int cc = 0; cc < nch; cc++) o = __fadd_rn(o, rowv[i * nch + cc]);
       out[r0 + i] = o;
       if (o > bv || (o == bv && r0 + i < bi)) { bv = o; bi = r0 + i; }
     }

@@ -32,7 +32,10 @@ void pb_set_capturing(bool on);
 // Q8 tensor layouts
 // PB_Q8_UMMA: 128-row tiles in the tensor cores' K-major 128-byte-swizzle order,
 // fp32 scales [tile][block][128] (pb_q80tc_pack; only pb_q80_gemm reads it)
-enum { PB_Q8_ROWMAJOR = 0, PB_Q8_STREAM = 1, PB_Q8_UMMA = 2 };
+// PB_Q8_B16: the bf16 tied table (blob dtype 3) in the head layout
+// (b16_index); codes points at it, no scales, nch = K / 1024 (2048-byte
+// segments per row)
+enum { PB_Q8_ROWMAJOR = 0, PB_Q8_STREAM = 1, PB_Q8_UMMA = 2, PB_Q8_B16 = 3 };
 
 struct pb_q8 {
   int N = 0, K = 0;
@@ -84,6 +87,9 @@ inline size_t pb_q8_scale_bytes(int N, int K, int sdt) {
 // rows r*rmul + radd (the model arena merges and interleaves tensors this way)
 int pb_q8_pack_into(pb_q8* w, const int8_t* d_codes, const void* d_scales, cudaStream_t st,
                     int src_rows, int rmul, int radd);
+
+// the bf16 tied table (blob dtype 3) re-laid for the head GEMV (pb_q8.cu)
+int pb_b16_pack(const uint16_t* d_src, uint16_t* d_dst, int N, int K, cudaStream_t st);
 
 // launch helpers used by the model's step (pdl: programmatic dependent launch)
 int pb_q8_gemv_launch(const pb_q8* w, const uint16_t* d_x, void* d_y, int y_dtype,

@@ -111,6 +111,49 @@ PB_DEV void l2_prefetch(const void* p, size_t bytes) {
   }
 }
 
+// greedy argmax of the logits a CTA wrote, ties to the lowest index: per-thread
+// best -> warp -> CTA slot; the last CTA to finish reduces the slots and
+// publishes the id (and the step's bookkeeping)
+PB_DEV void step_argmax_publish(const StepArgs& a, float bv, int bi, float* bestv, int* besti) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const float ov = __shfl_down_sync(0xffffffffu, bv, o);
+    const int oi = __shfl_down_sync(0xffffffffu, bi, o);
+    if (ov > bv || (ov == bv && oi < bi)) { bv = ov; bi = oi; }
+  }
+  if (lane == 0) { bestv[warp] = bv; besti[warp] = bi; }
+  __syncthreads();
+  __shared__ int am_last;
+  if (threadIdx.x == 0) {
+    float b = bestv[0]; int ix = besti[0];
+    for (int w = 1; w < 8; w++)
+      if (bestv[w] > b || (bestv[w] == b && besti[w] < ix)) { b = bestv[w]; ix = besti[w]; }
+    a.ctl->slot_val[blockIdx.x] = b;
+    a.ctl->slot_idx[blockIdx.x] = ix;
+    __threadfence();
+    const unsigned prev = atomicAdd(&a.ctl->counter, 1u);
+    am_last = prev == gridDim.x - 1;
+  }
+  __syncthreads();
+  if (am_last && threadIdx.x == 0) {
+    __threadfence();
+    volatile float* sv = a.ctl->slot_val;
+    volatile int* si = a.ctl->slot_idx;
+    float b = sv[0]; int ix = si[0];
+    for (int k = 1; k < (int)gridDim.x; k++) {
+      const float ov = sv[k]; const int oi = si[k];
+      if (ov > b || (ov == b && oi < ix)) { b = ov; ix = oi; }
+    }
+    const int step = a.ctl->step;
+    a.ctl->token = (step + 1 < a.ctl->n_prompt) ? a.ctl->prompt[step + 1] : ix;
+    if (a.ctl->ids) a.ctl->ids[step] = ix;
+    a.ctl->step = step + 1;
+    a.ctl->pos += 1;
+    a.ctl->counter = 0;
+  }
+}
+
 template <int NCH, bool F32S, int EPI, bool ONE>
 __global__ void __launch_bounds__(256, 2) k_step(StepArgs a) {
   constexpr int U = 2, G = 8 / NCH, RB = G * U;
@@ -237,46 +280,51 @@ __global__ void __launch_bounds__(256, 2) k_step(StepArgs a) {
       }
     }
   }
-  if (EPI == EPI_ARGMAX && !a.no_publish) {
-    // greedy argmax, ties to the lowest index: per-thread best -> warp -> CTA
-    // slot; the last CTA to finish reduces the slots and publishes the id.
+  if (EPI == EPI_ARGMAX && !a.no_publish) step_argmax_publish(a, bv, bi, bestv, besti);
+}
+
+// the head over the bf16 tied table (blob dtype 3): the same prologue as
+// k_step, then k_gemv_bf16 (lfm3_nanode.cu:3517-3534) per row -- lane l chains
+// s = s + bf16(W[k]) * x[k] over k = l, l+32, ... -- the shuffle-down tree, and
+// the fp32 logit as is; then the greedy argmax. a.codes: the table in the head
+// layout (b16_index); KG = K / 256.
+template <int KG>
+__global__ void __launch_bounds__(256, 2) k_step16(StepArgs a) {
+  constexpr int K = KG * 256;
+  extern __shared__ __align__(16) float smem[];
+  float* sx = smem;
+  __shared__ float red[16];
+  __shared__ float bestv[8];
+  __shared__ int besti[8];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  pb_grid_launch_dependents();
+  step_prologue<0>(a, sx, red, nullptr, -1);
+  float xr[K / 32];
 #pragma unroll
-    for (int o = 16; o > 0; o >>= 1) {
-      const float ov = __shfl_down_sync(0xffffffffu, bv, o);
-      const int oi = __shfl_down_sync(0xffffffffu, bi, o);
-      if (ov > bv || (ov == bv && oi < bi)) { bv = ov; bi = oi; }
-    }
-    if (lane == 0) { bestv[warp] = bv; besti[warp] = bi; }
-    __syncthreads();
-    __shared__ int am_last;
-    if (threadIdx.x == 0) {
-      float b = bestv[0]; int ix = besti[0];
-      for (int w = 1; w < 8; w++)
-        if (bestv[w] > b || (bestv[w] == b && besti[w] < ix)) { b = bestv[w]; ix = besti[w]; }
-      a.ctl->slot_val[blockIdx.x] = b;
-      a.ctl->slot_idx[blockIdx.x] = ix;
-      __threadfence();
-      const unsigned prev = atomicAdd(&a.ctl->counter, 1u);
-      am_last = prev == gridDim.x - 1;
-    }
-    __syncthreads();
-    if (am_last && threadIdx.x == 0) {
-      __threadfence();
-      volatile float* sv = a.ctl->slot_val;
-      volatile int* si = a.ctl->slot_idx;
-      float b = sv[0]; int ix = si[0];
-      for (int k = 1; k < (int)gridDim.x; k++) {
-        const float ov = sv[k]; const int oi = si[k];
-        if (ov > b || (ov == b && oi < ix)) { b = ov; ix = oi; }
+  for (int m = 0; m < K / 32; m++) xr[m] = sx[padx(lane + 32 * m)];
+  float bv = -INFINITY;
+  int bi = 0x7fffffff;
+  const uint16_t* w = reinterpret_cast<const uint16_t*>(a.codes);
+  for (int row = blockIdx.x * 8 + warp; row < a.N; row += gridDim.x * 8) {
+    const uint4* g = reinterpret_cast<const uint4*>(w + (size_t)row * K) + lane;
+    float acc = 0.0f;
+#pragma unroll
+    for (int h = 0; h < KG; h++) {
+      const uint4 q = pb_ldg_stream(g + 32 * h);
+      const unsigned ws[4] = {q.x, q.y, q.z, q.w};
+#pragma unroll
+      for (int i = 0; i < 4; i++) {
+        acc = __fadd_rn(acc, __fmul_rn(pb_lo2f(ws[i]), xr[8 * h + 2 * i]));
+        acc = __fadd_rn(acc, __fmul_rn(pb_hi2f(ws[i]), xr[8 * h + 2 * i + 1]));
       }
-      const int step = a.ctl->step;
-      a.ctl->token = (step + 1 < a.ctl->n_prompt) ? a.ctl->prompt[step + 1] : ix;
-      if (a.ctl->ids) a.ctl->ids[step] = ix;
-      a.ctl->step = step + 1;
-      a.ctl->pos += 1;
-      a.ctl->counter = 0;
+    }
+    const float v = pb_warp_tree(acc);
+    if (lane == 0) {
+      reinterpret_cast<float*>(a.y)[row] = v;
+      if (v > bv || (v == bv && row < bi)) { bv = v; bi = row; }
     }
   }
+  if (!a.no_publish) step_argmax_publish(a, bv, bi, bestv, besti);
 }
 
 // ------------------------------------------------------------- attention
@@ -336,7 +384,8 @@ struct pb_model {
   bool any_slide = false;
   int sdt = PB_DT_F16;
   std::vector<Layer> layers;
-  pb_q8 head;
+  pb_q8 head;                // the tied table (Q8); N, K also describe a bf16 table
+  uint16_t* head16 = nullptr;   // the tied table as bf16 (blob dtype 3), head layout (b16_index)
   float* final_norm = nullptr;
   char* arena = nullptr;
   size_t arena_bytes = 0;
@@ -414,6 +463,7 @@ struct pb_state {
   bf16_t* pf_att = nullptr;       // [T][NH*HD] gated attention output
   float* pf_logits = nullptr;     // [T][V]
   int* pf_tok = nullptr;          // [T]
+  bf16_t* pf_R2 = nullptr;        // [T][H] x of the bf16 head (a dtype-3 table)
   // row sharding over tp_world ranks (pb_state_shard): every GEMV computes its
   // rank's rows, an in-place NCCL all-gather completes the output vector
   int tp_rank = 0, tp_world = 1;
@@ -498,11 +548,47 @@ int launch_step_n(int nch, int one, const StepArgs& a, cudaStream_t st, bool pdl
   return pb_set_error(PB_ENOTSUP, "step: %d chunks", nch);
 }
 
+template <int KG>
+int launch_step16_t(const StepArgs& a, cudaStream_t st, bool pdl) {
+  const size_t smem = step_smem(a.K, a.H);
+  static bool set = false;
+  if (!set) {
+    cudaFuncSetAttribute(k_step16<KG>, cudaFuncAttributeMaxDynamicSharedMemorySize, 96 * 1024);
+    set = true;
+  }
+  int grid = 2 * pb_num_sms();
+  if (grid > (a.N + 7) / 8) grid = (a.N + 7) / 8;
+  if (grid > MAX_CTA) grid = MAX_CTA;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(256);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl ? 1 : 0;
+  cudaError_t e = cudaLaunchKernelEx(&cfg, k_step16<KG>, a);
+  if (e != cudaSuccess) return pb_set_error(PB_ECUDA, "launch k_step16: %s", cudaGetErrorString(e));
+  pb_count_launch();
+  return PB_OK;
+}
+
 int launch_step(const pb_q8& w, int epi, StepArgs a, cudaStream_t st, bool pdl) {
   a.codes = reinterpret_cast<const uint4*>(w.codes);
   a.scales = w.scales;
   a.N = w.N;
   a.K = w.K;
+  if (w.layout == PB_Q8_B16) {
+    if (epi != EPI_ARGMAX) return pb_set_error(PB_ENOTSUP, "step: the bf16 table is the head only");
+    switch (w.K) {
+      case 1024: return launch_step16_t<4>(a, st, pdl);
+      case 2048: return launch_step16_t<8>(a, st, pdl);
+      case 4096: return launch_step16_t<16>(a, st, pdl);
+    }
+    return pb_set_error(PB_ENOTSUP, "step: bf16 head with K=%d", w.K);
+  }
   const bool f = w.sdt == PB_DT_F32;
   if (epi == EPI_BF16) return f ? launch_step_n<true, EPI_BF16>(w.nch, w.one, a, st, pdl) : launch_step_n<false, EPI_BF16>(w.nch, w.one, a, st, pdl);
   if (epi == EPI_SILU) return f ? launch_step_n<true, EPI_SILU>(w.nch, w.one, a, st, pdl) : launch_step_n<false, EPI_SILU>(w.nch, w.one, a, st, pdl);
@@ -624,8 +710,9 @@ int launch_gemv(pb_state* s, const pb_q8& w, int epi, StepArgs a, cudaStream_t s
   pb_q8 part = w;
   part.N = rows;
   part.owner = false;
-  part.codes = w.codes + (size_t)r0 * w.nch * 2048;
-  part.scales = static_cast<char*>(w.scales) + (size_t)r0 * w.nch * 32 * (w.sdt == PB_DT_F32 ? 8 : 4);
+  part.codes = w.codes + (size_t)r0 * w.nch * 2048;   // (a bf16 row is nch 2048-byte segments too)
+  if (w.layout != PB_Q8_B16)
+    part.scales = static_cast<char*>(w.scales) + (size_t)r0 * w.nch * 32 * (w.sdt == PB_DT_F32 ? 8 : 4);
   size_t elem = 2, per_rank = rows, first = r0;
   if (epi == EPI_SILU) { per_rank = rows / 2; first = r0 / 2; }
   else if (epi == EPI_ARGMAX) { elem = 4; a.no_publish = 1; }
@@ -668,6 +755,7 @@ int enqueue_layer(const pb_model* m, pb_state* s, int L, int& cur, int first_mod
     a.emb_scales = m->head.scales;
     a.emb_nch = m->head.nch;
     a.emb_f32 = m->head.sdt == PB_DT_F32;
+    a.emb16 = m->head.layout == PB_Q8_B16 ? m->head16 : nullptr;
     a.rout = s->res[cur];
   } else {
     a.xin = x_in ? x_in : s->res[cur];
@@ -818,6 +906,7 @@ DPhase dgemv(const pb_model* m, const pb_q8& w, int pro, int epi, const uint32_t
   ph.K = w.K;
   ph.nch = w.nch;
   ph.one = w.one && w.nch > 1;
+  ph.b16 = w.layout == PB_Q8_B16;
   ph.H = m->H;
   ph.eps = m->eps;
   ph.tin = tin;
@@ -846,6 +935,7 @@ int build_phases(pb_state* s) {
       a.emb_scales = m->head.scales;
       a.emb_nch = m->head.nch;
       a.emb_f32 = m->head.sdt == PB_DT_F32;
+      a.emb16 = m->head.layout == PB_Q8_B16 ? m->head16 : nullptr;
     } else {
       a.wpost = m->layers[L - 1].post_ffn_norm;
     }
@@ -925,7 +1015,7 @@ int build_phases(pb_state* s) {
       const int rb0 = (int)(((long long)b * nrb) / G), rb1 = (int)(((long long)(b + 1) * nrb) / G);
       GemvSched& g = sched[(size_t)b * ngemv + p.gidx];
       g.codes = reinterpret_cast<const char*>(w.codes);
-      g.scales = reinterpret_cast<const char*>(w.scales);
+      g.scales = reinterpret_cast<const char*>(p.b16 ? w.codes : w.scales);   // (a bf16 table has none)
       g.r0 = rb0 * RB;
       g.r1 = std::min(rb1 * RB, p.N);
       g.base = base;
@@ -936,7 +1026,7 @@ int build_phases(pb_state* s) {
         sd.codes16 = (unsigned)(((size_t)(g.codes - m->arena) + (size_t)r * p.nch * 2048) / 16);
         sd.scales16 = (unsigned)(((size_t)(g.scales - m->arena) + (size_t)r * p.nch * 32 * q8s) / 16);
         sd.bc = (unsigned)(nr * p.nch * 2048);
-        sd.bs = (unsigned)(nr * p.nch * 32 * q8s);
+        sd.bs = p.b16 ? 0u : (unsigned)(nr * p.nch * 32 * q8s);
         sdesc[b].push_back(sd);
       }
       base += rb1 - rb0;
@@ -1207,6 +1297,11 @@ extern "C" int pb_open(const char* path, int device, pb_model** out) {
       size_t n = 1;
       for (auto d : t.ne) n *= (size_t)d;
       if (t.nc != n * 4) return bad(PB_EFORMAT, ("f32 tensor with inconsistent size: " + t.name).c_str());
+    } else if (t.dtype == 3) {
+      // bf16 payload, verbatim (export_lfm3_q8.py:96-110): ncodes = N K 2, nscales = 0
+      if (t.ne.size() != 2 || t.ne[0] <= 0 || t.ne[1] <= 0 || t.ne[1] % 256 ||
+          t.nc != (size_t)t.ne[0] * t.ne[1] * 2 || t.ns != 0)
+        return bad(PB_EFORMAT, ("bf16 tensor with inconsistent sizes: " + t.name).c_str());
     } else {
       return bad(PB_ENOTSUP, ("tensor dtype not supported by this build: " + t.name).c_str());
     }
@@ -1291,11 +1386,22 @@ extern "C" int pb_open(const char* path, int device, pb_model** out) {
     fpieces.push_back({lname(L, "ffn_norm.weight"), &Ly.ffn_norm, (size_t)H});
     fpieces.push_back({lname(L, "post_ffn_norm.weight"), &Ly.post_ffn_norm, (size_t)H});
   }
+  bool emb16 = false;
   {
     int N, K;
-    if (!q8shape("lfm.model.embed_tokens.weight", N, K) || N != m->V || K != H) return bad(PB_EFORMAT, "embed_tokens missing or misshapen");
-    plan_q8(m->head, m->V, H);
-    q8pieces.push_back({"lfm.model.embed_tokens.weight", &m->head, 1, 0});
+    const Tensor* et = find(m, "lfm.model.embed_tokens.weight");
+    if (et && et->dtype == 3) {
+      // the certified arm's bf16 table (lfm3_nanode.cu:3505-3534): embedding
+      // rows copied, the head as k_gemv_bf16
+      if (et->ne[0] != m->V || et->ne[1] != H) return bad(PB_EFORMAT, "embed_tokens misshapen");
+      emb16 = true;
+      m->head.N = m->V; m->head.K = H; m->head.owner = false;
+      need += align256(et->nc);
+    } else {
+      if (!q8shape("lfm.model.embed_tokens.weight", N, K) || N != m->V || K != H) return bad(PB_EFORMAT, "embed_tokens missing or misshapen");
+      plan_q8(m->head, m->V, H);
+      q8pieces.push_back({"lfm.model.embed_tokens.weight", &m->head, 1, 0});
+    }
     fpieces.push_back({"lfm.model.embedding_norm.weight", &m->final_norm, (size_t)H});
   }
   for (auto& fp : fpieces) {
@@ -1340,6 +1446,14 @@ extern "C" int pb_open(const char* path, int device, pb_model** out) {
     assigned.push_back(w);
   };
   for (auto& p : q8pieces) assign(p.dst);
+  if (emb16) {
+    m->head16 = reinterpret_cast<uint16_t*>(m->arena + cursor);
+    cursor += align256((size_t)m->V * H * 2);
+    m->head.layout = PB_Q8_B16;
+    m->head.codes = reinterpret_cast<int8_t*>(m->head16);
+    m->head.scales = nullptr;
+    m->head.nch = H / 1024;
+  }
   for (auto& fp : fpieces) {
     *fp.dst = reinterpret_cast<float*>(m->arena + cursor);
     cursor += align256(fp.n * 4);
@@ -1371,6 +1485,13 @@ extern "C" int pb_open(const char* path, int device, pb_model** out) {
     rc = pb_q8_pack_into(q8pieces[i].dst, reinterpret_cast<int8_t*>(stage), stage + t->nc, st,
                          (int)t->ne[0], q8pieces[i].rmul, q8pieces[i].radd);
     m->weight_bytes += t->nc + (size_t)t->ne[0] * (t->ne[1] / 32) * (m->sdt == PB_DT_F32 ? 4 : 2);
+  }
+  if (rc == PB_OK && emb16) {
+    const Tensor* t = find(m, "lfm.model.embed_tokens.weight");
+    if ((rc = load(t)) == PB_OK) {
+      rc = pb_b16_pack(reinterpret_cast<const uint16_t*>(stage), m->head16, m->V, H, st);
+      m->weight_bytes += t->nc;
+    }
   }
   for (size_t i = 0; rc == PB_OK && i < fpieces.size(); i++) {
     const Tensor* t = find(m, fpieces[i].name);
@@ -1952,11 +2073,31 @@ extern "C" int pb_layer_step_noalloc(pb_model* m, pb_state* s, int layer, int po
 // ------------------------------------------------------------ chunked prefill
 namespace {
 
+int launch_b16_head_T(const pb_model* m, const bf16_t* x, float* lg, int T, cudaStream_t st) {
+  const size_t smem = (size_t)32 * m->H * 2;
+  int grid = pb_num_sms();
+  if (grid > (m->V + 7) / 8) grid = (m->V + 7) / 8;
+  const uint16_t* w = m->head16;
+  switch (m->H) {
+    case 1024:
+      PB_TRY_CUDA(cudaFuncSetAttribute(k_b16_head_T<4>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+      k_b16_head_T<4><<<grid, 256, smem, st>>>(w, x, lg, m->V, T);
+      break;
+    case 2048:
+      PB_TRY_CUDA(cudaFuncSetAttribute(k_b16_head_T<8>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+      k_b16_head_T<8><<<grid, 256, smem, st>>>(w, x, lg, m->V, T);
+      break;
+    default: return pb_set_error(PB_ENOTSUP, "bf16 head with hidden %d", m->H);
+  }
+  PB_LAUNCHED("k_b16_head_T");
+  return PB_OK;
+}
+
 int prefill_prepare(pb_model* m, pb_state* s, int T, cudaStream_t st) {
   if (!m->tc_arena) {
     std::vector<const pb_q8*> src;
     for (auto& Ly : m->layers) { src.push_back(&Ly.first); src.push_back(&Ly.mix); src.push_back(&Ly.w13); src.push_back(&Ly.w2); }
-    src.push_back(&m->head);
+    if (m->head.layout != PB_Q8_B16) src.push_back(&m->head);   // (a bf16 table is read as it is)
     size_t tot = 0;
     for (auto* w : src) tot += align256(pb_q80tc_bytes(w->N, w->K));
     if (cudaMalloc(&m->tc_arena, tot) != cudaSuccess) {
@@ -1981,7 +2122,8 @@ int prefill_prepare(pb_model* m, pb_state* s, int T, cudaStream_t st) {
     const int kmax = std::max(H, std::max(F, m->NH * m->HD));
     int nmax = std::max(std::max(3 * H, nq), std::max(2 * F, H));
     const size_t sizes[] = {(size_t)T * H * 2, (size_t)T * kmax, (size_t)T * (kmax / 32) * 2, (size_t)T * nmax * 4,
-                            (size_t)T * nq * 2, (size_t)T * m->NH * m->HD * 2, (size_t)T * m->V * 4, (size_t)T * 4};
+                            (size_t)T * nq * 2, (size_t)T * m->NH * m->HD * 2, (size_t)T * m->V * 4, (size_t)T * 4,
+                            (size_t)T * H * 2};
     size_t tot = 0;
     for (size_t x : sizes) tot += align256(x);
     if (cudaMalloc(&s->pf_mem, tot) != cudaSuccess) {
@@ -1990,7 +2132,7 @@ int prefill_prepare(pb_model* m, pb_state* s, int T, cudaStream_t st) {
       return pb_set_error(PB_ENOMEM, "prefill: buffers");
     }
     void** slots[] = {(void**)&s->pf_R, (void**)&s->pf_qx, (void**)&s->pf_dx, (void**)&s->pf_y, (void**)&s->pf_qkvg,
-                      (void**)&s->pf_att, (void**)&s->pf_logits, (void**)&s->pf_tok};
+                      (void**)&s->pf_att, (void**)&s->pf_logits, (void**)&s->pf_tok, (void**)&s->pf_R2};
     char* p = s->pf_mem;
     for (size_t i = 0; i < sizeof(sizes) / sizeof(sizes[0]); i++) { *slots[i] = p; p += align256(sizes[i]); }
     s->pf_cap = T;
@@ -1999,13 +2141,15 @@ int prefill_prepare(pb_model* m, pb_state* s, int T, cudaStream_t st) {
 }
 
 int pf_norm(const pb_model* m, pb_state* s, int T, const int* tokens, const float* hin, const float* wpost,
-            const float* wnorm, cudaStream_t st) {
+            const float* wnorm, cudaStream_t st, bf16_t* xout = nullptr) {
   PfNormArgs a = {};
+  a.xout = xout;
   a.tokens = tokens;
   a.emb_codes = reinterpret_cast<const uint4*>(m->head.codes);
   a.emb_scales = m->head.scales;
   a.emb_nch = m->head.nch;
   a.emb_f32 = m->head.sdt == PB_DT_F32;
+  a.emb16 = m->head.layout == PB_Q8_B16 ? m->head16 : nullptr;
   a.rin = s->pf_R;
   a.hin = hin;
   a.wpost = wpost;
@@ -2103,9 +2247,16 @@ extern "C" int pb_prefill_chunk(pb_model* m, pb_state* s, const int* d_tokens, i
     PB_LAUNCHED("k_pf_silu_quant");
     if ((rc = pb_q80_gemm(&tc[3], T, s->pf_qx, s->pf_dx, s->pf_y, nullptr, st))) return rc;
   }
-  if ((rc = pf_norm(m, s, T, nullptr, s->pf_y, m->layers[m->L - 1].post_ffn_norm, m->final_norm, st))) return rc;
   float* lg = d_logits ? d_logits : s->pf_logits;
-  if ((rc = pb_q80_gemm(&m->tc.back(), T, s->pf_qx, s->pf_dx, lg, nullptr, st))) return rc;
+  if (m->head.layout == PB_Q8_B16) {
+    // the bf16 head on each position's x (the float path's head: there is no
+    // integer form of k_gemv_bf16)
+    if ((rc = pf_norm(m, s, T, nullptr, s->pf_y, m->layers[m->L - 1].post_ffn_norm, m->final_norm, st, s->pf_R2))) return rc;
+    if ((rc = launch_b16_head_T(m, s->pf_R2, lg, T, st))) return rc;
+  } else {
+    if ((rc = pf_norm(m, s, T, nullptr, s->pf_y, m->layers[m->L - 1].post_ffn_norm, m->final_norm, st))) return rc;
+    if ((rc = pb_q80_gemm(&m->tc.back(), T, s->pf_qx, s->pf_dx, lg, nullptr, st))) return rc;
+  }
   if (d_ids) {
     k_pf_argmax<<<T, 256, 0, st>>>(lg, m->V, d_ids);
     PB_LAUNCHED("k_pf_argmax");
@@ -2240,9 +2391,17 @@ extern "C" int pb_decode_batch(pb_model* m, pb_state* const* states, int B, cons
     PB_LAUNCHED("k_pf_silu_quant");
     if ((rc = pb_q80_gemm(&tc[3], B, ws->pf_qx, ws->pf_dx, ws->pf_y, nullptr, st))) return rc;
   }
-  if ((rc = pf_norm(m, ws, B, nullptr, ws->pf_y, m->layers[m->L - 1].post_ffn_norm, m->final_norm, st))) return rc;
+  if (m->head.layout == PB_Q8_B16) {
+    if ((rc = pf_norm(m, ws, B, nullptr, ws->pf_y, m->layers[m->L - 1].post_ffn_norm, m->final_norm, st, ws->pf_R2))) return rc;
+  } else if ((rc = pf_norm(m, ws, B, nullptr, ws->pf_y, m->layers[m->L - 1].post_ffn_norm, m->final_norm, st))) {
+    return rc;
+  }
   float* lg = d_logits ? d_logits : ws->pf_logits;
-  if ((rc = pb_q80_gemm(&m->tc.back(), B, ws->pf_qx, ws->pf_dx, lg, nullptr, st))) return rc;
+  if (m->head.layout == PB_Q8_B16) {
+    if ((rc = launch_b16_head_T(m, ws->pf_R2, lg, B, st))) return rc;
+  } else if ((rc = pb_q80_gemm(&m->tc.back(), B, ws->pf_qx, ws->pf_dx, lg, nullptr, st))) {
+    return rc;
+  }
   k_pf_argmax<<<B, 256, 0, st>>>(lg, m->V, d_ids);
   PB_LAUNCHED("k_pf_argmax");
   return PB_OK;

@@ -38,6 +38,7 @@ struct PfNormArgs {
   const uint4* emb_codes;   // tied table, streaming layout
   const void* emb_scales;
   int emb_nch, emb_f32;
+  const uint16_t* emb16;    // the bf16 table (head layout) instead
   const bf16_t* rin;        // [T][H] residual (unless EMBED)
   const float* hin;         // [T][H] fp32 projection output to post-normalise and add (null: none)
   const float* wpost;
@@ -45,6 +46,7 @@ struct PfNormArgs {
   bf16_t* rout;             // [T][H] new residual
   int8_t* qx;               // [T][H]
   uint16_t* dx;             // [T][H/32]
+  bf16_t* xout;             // optional [T][H]: x itself (the bf16 head's input)
   int H;
   float eps;
 };
@@ -57,20 +59,11 @@ __global__ void __launch_bounds__(256) k_pf_norm_quant(PfNormArgs p) {
   const int t = blockIdx.x, th = threadIdx.x, H = p.H;
   float R[E];
   if (p.tokens) {
-    // k_dequant_row (lfm3_nanode.cu:138-142) from the tied table's streaming layout
+    // the token's row of the tied table
     const int tok = p.tokens[t];
-    const int8_t* cb = reinterpret_cast<const int8_t*>(p.emb_codes);
 #pragma unroll
-    for (int j = 0; j < E; j++) {
-      const int i = th * E + j;
-      const int b = i >> 5, jj = i & 31, c = b >> 6, bb = b & 63, l = bb & 31, half = bb >> 5;
-      const size_t seg = (size_t)tok * p.emb_nch + c;
-      const int gi = (half * 2 + (jj >> 4)) * 32 + l;
-      const float code = (float)cb[(seg * 128 + gi) * 16 + (jj & 15)];
-      const float s = p.emb_f32 ? reinterpret_cast<const float*>(p.emb_scales)[(seg * 32 + l) * 2 + half]
-                                : pb_h2f(reinterpret_cast<const unsigned short*>(p.emb_scales)[(seg * 32 + l) * 2 + half]);
-      R[j] = pb_bf2f(pb_f2bf(__fmul_rn(code, s)));
-    }
+    for (int j = 0; j < E; j++)
+      R[j] = emb_value(p.emb_codes, p.emb_scales, p.emb_nch, p.emb_f32, p.emb16, H, tok, th * E + j);
   } else {
     ld_bf<E, 0>(p.rin + (size_t)t * H + (size_t)th * E, R);
     if (p.hin) {
@@ -87,7 +80,49 @@ __global__ void __launch_bounds__(256) k_pf_norm_quant(PfNormArgs p) {
   float wn[E], X[E];
   ld_f32<E>(p.wnorm + (size_t)th * E, wn);
   rms_reg<E, 0>(R, wn, X, H, p.eps, red + 8);
+  if (p.xout) st_bf<E>(p.xout + (size_t)t * H + (size_t)th * E, X);
   pf_quant_store<E>(X, p.qx + (size_t)t * H, p.dx + (size_t)t * (H / 32), th);
+}
+
+// the head over the bf16 tied table for T positions (k_gemv_bf16,
+// lfm3_nanode.cu:3517-3534, per position): a warp per row holds lane l's 64
+// weights (k = l + 32 m) and runs each position's chain s = s + bf16(W[k]) *
+// x[k] from the positions' x (bf16, up to 32 positions in shared memory at a
+// time), then the shuffle-down tree; lg [T][N] fp32 as is. KG = K / 256.
+template <int KG>
+__global__ void __launch_bounds__(256) k_b16_head_T(const uint16_t* __restrict__ w, const bf16_t* __restrict__ x,
+                                                    float* __restrict__ lg, int N, int T) {
+  constexpr int K = KG * 256, TG = 32;
+  extern __shared__ __align__(16) bf16_t xs[];     // [TG][K]
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  for (int t0 = 0; t0 < T; t0 += TG) {
+    const int nt = T - t0 < TG ? T - t0 : TG;
+    __syncthreads();
+    for (int i = threadIdx.x; i < nt * K / 8; i += blockDim.x)
+      reinterpret_cast<uint4*>(xs)[i] = reinterpret_cast<const uint4*>(x + (size_t)t0 * K)[i];
+    __syncthreads();
+    for (int row = blockIdx.x * 8 + warp; row < N; row += gridDim.x * 8) {
+      const uint4* g = reinterpret_cast<const uint4*>(w + (size_t)row * K) + lane;
+      uint4 q[KG];
+#pragma unroll
+      for (int h = 0; h < KG; h++) q[h] = pb_ldg_stream(g + 32 * h);
+      for (int t = 0; t < nt; t++) {
+        const bf16_t* xt = xs + (size_t)t * K + lane;
+        float acc = 0.0f;
+#pragma unroll
+        for (int h = 0; h < KG; h++) {
+          const unsigned ws[4] = {q[h].x, q[h].y, q[h].z, q[h].w};
+#pragma unroll
+          for (int i = 0; i < 4; i++) {
+            acc = __fadd_rn(acc, __fmul_rn(pb_lo2f(ws[i]), pb_bf2f(xt[32 * (8 * h + 2 * i)])));
+            acc = __fadd_rn(acc, __fmul_rn(pb_hi2f(ws[i]), pb_bf2f(xt[32 * (8 * h + 2 * i + 1)])));
+          }
+        }
+        const float v = pb_warp_tree(acc);
+        if (lane == 0) lg[(size_t)(t0 + t) * N + row] = v;
+      }
+    }
+  }
 }
 
 struct PfConvArgs {

@@ -24,6 +24,7 @@
 #include <cstdio>
 #include <cstdlib>
 #include <cstring>
+#include <algorithm>
 
 // ------------------------------------------------------------------ packing
 // Source rows r = 0..R-1 (row-major) land at destination row r*rmul + radd,
@@ -360,6 +361,53 @@ k_q80_stream(const uint4* __restrict__ codes, const void* __restrict__ scales,
   }
 }
 
+// ----------------------------------------------------- bf16 table (dtype 3)
+// The certified arm's tied table (lfm3_nanode.cu:3505-3534): row-major bf16
+// -> the head layout (b16_index: granule h*32 + l of a row holds elements
+// l + 32 (8h + m), m = 0..7); one thread per destination granule
+__global__ void k_b16_pack(const uint16_t* __restrict__ src, uint16_t* __restrict__ dst, int N, int K) {
+  const size_t ng = (size_t)N * (K / 8);
+  for (size_t g = (size_t)blockIdx.x * blockDim.x + threadIdx.x; g < ng; g += (size_t)gridDim.x * blockDim.x) {
+    const size_t row = g / (K / 8);
+    const int gi = (int)(g - row * (K / 8)), h = gi >> 5, l = gi & 31;
+    const uint16_t* r = src + row * K;
+    unsigned w[4];
+#pragma unroll
+    for (int m = 0; m < 8; m += 2)
+      w[m / 2] = (unsigned)r[l + 32 * (8 * h + m)] | ((unsigned)r[l + 32 * (8 * h + m + 1)] << 16);
+    reinterpret_cast<uint4*>(dst + row * K)[gi] = make_uint4(w[0], w[1], w[2], w[3]);
+  }
+}
+
+// k_gemv_bf16: a warp per row, lane l chains s = s + bf16(W[k]) * x[k] over
+// k = l, l+32, ... (product and sum rounded apart), then the shuffle-down
+// tree; y fp32 as is. KG = K / 256: 8 granules per 256 elements and lane.
+template <int KG>
+__global__ void __launch_bounds__(256) k_b16_gemv(const uint16_t* __restrict__ w, const bf16_t* __restrict__ x,
+                                                  float* __restrict__ y, int N) {
+  constexpr int K = KG * 256;
+  const int lane = threadIdx.x & 31;
+  float xr[K / 32];
+#pragma unroll
+  for (int m = 0; m < K / 32; m++) xr[m] = pb_bf2f(x[lane + 32 * m]);
+  for (int row = blockIdx.x * 8 + (threadIdx.x >> 5); row < N; row += gridDim.x * 8) {
+    const uint4* g = reinterpret_cast<const uint4*>(w + (size_t)row * K) + lane;
+    float s = 0.0f;
+#pragma unroll
+    for (int h = 0; h < KG; h++) {
+      const uint4 q = pb_ldg_stream(g + 32 * h);
+      const unsigned ws[4] = {q.x, q.y, q.z, q.w};
+#pragma unroll
+      for (int i = 0; i < 4; i++) {
+        s = __fadd_rn(s, __fmul_rn(pb_lo2f(ws[i]), xr[8 * h + 2 * i]));
+        s = __fadd_rn(s, __fmul_rn(pb_hi2f(ws[i]), xr[8 * h + 2 * i + 1]));
+      }
+    }
+    const float v = pb_warp_tree(s);
+    if (lane == 0) y[row] = v;
+  }
+}
+
 // =============================================================== host side
 static int g_nsm = 0;
 int pb_num_sms() {
@@ -440,7 +488,36 @@ int pb_q8_gemv_launch(const pb_q8* w, const uint16_t* d_x, void* d_y, int y_dtyp
   return PB_OK;
 }
 
+int pb_b16_pack(const uint16_t* d_src, uint16_t* d_dst, int N, int K, cudaStream_t st) {
+  if (N <= 0 || K <= 0 || K % 256) return pb_set_error(PB_EINVAL, "bf16 table: shape %dx%d (K %% 256)", N, K);
+  const size_t ng = (size_t)N * (K / 8);
+  const int grid = (int)std::min<size_t>((ng + 255) / 256, (size_t)pb_num_sms() * 16);
+  k_b16_pack<<<grid, 256, 0, st>>>(d_src, d_dst, N, K);
+  PB_LAUNCHED("k_b16_pack");
+  return PB_OK;
+}
+
 // ---------------------------------------------------------------- C ABI
+extern "C" int pb_bf16_relayout(const uint16_t* d_src, uint16_t* d_dst, int N, int K, void* stream) {
+  if (!d_src || !d_dst) return pb_set_error(PB_EINVAL, "pb_bf16_relayout: null argument");
+  if (((uintptr_t)d_dst & 15) != 0) return pb_set_error(PB_EINVAL, "pb_bf16_relayout: dst must be 16-byte aligned");
+  return pb_b16_pack(d_src, d_dst, N, K, (cudaStream_t)stream);
+}
+
+extern "C" int pb_bf16_gemv(const uint16_t* d_w, int N, int K, const uint16_t* d_x, float* d_y, void* stream) {
+  if (!d_w || !d_x || !d_y || N <= 0) return pb_set_error(PB_EINVAL, "pb_bf16_gemv: bad argument");
+  if (((uintptr_t)d_w & 15) != 0) return pb_set_error(PB_EINVAL, "pb_bf16_gemv: w must be 16-byte aligned");
+  cudaStream_t st = (cudaStream_t)stream;
+  const int grid = (int)std::min<long>((N + 7) / 8, (long)pb_num_sms() * 8);
+  switch (K) {
+    case 1024: k_b16_gemv<4><<<grid, 256, 0, st>>>(d_w, d_x, d_y, N); break;
+    case 2048: k_b16_gemv<8><<<grid, 256, 0, st>>>(d_w, d_x, d_y, N); break;
+    case 4096: k_b16_gemv<16><<<grid, 256, 0, st>>>(d_w, d_x, d_y, N); break;
+    default: return pb_set_error(PB_ENOTSUP, "pb_bf16_gemv: K=%d (1024, 2048 or 4096)", K);
+  }
+  PB_LAUNCHED("k_b16_gemv");
+  return PB_OK;
+}
 extern "C" int pb_q8_pack(const int8_t* codes, const void* scales, int scale_dtype, int N, int K,
                           int src_on_device, void* stream, pb_q8** out) {
   if (!out || !codes || !scales) return pb_set_error(PB_EINVAL, "pb_q8_pack: null argument");

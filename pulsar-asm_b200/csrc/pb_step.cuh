@@ -47,6 +47,7 @@ struct StepArgs {
   const void* emb_scales;
   int emb_nch;
   int emb_f32;         // EMBED: scales are fp32 pairs (else fp16 pairs)
+  const uint16_t* emb16;    // EMBED: the bf16 table (blob dtype 3) instead, head layout
   bf16_t* ring;        // CONV: [W][H], slot = position mod W
   const float* taps;   // CONV: [H][W]
   int convw;
@@ -134,6 +135,26 @@ PB_DEV void gw_pass(const GridWait* g) {
 // sx (the GEMV input) is stored padded, one spare float per 32, so that lane
 // l reading its 32 consecutive values (index 32 l + j) hits bank (l + j) % 32.
 PB_DEV int padx(int i) { return i + (i >> 5); }
+
+// The bf16 tied table (blob dtype 3) in its head layout: per row, 16-byte
+// granule h*32 + l holds elements l + 32 (8h + m), m = 0..7, so that lane l of
+// the head GEMV reads its chain k = l, l+32, ... as 8 conflict-free vector loads.
+PB_HD_INL size_t b16_index(int i) { return (size_t)((((i >> 8) * 32 + (i & 31)) << 3) + ((i >> 5) & 7)); }
+
+// element i of row tok of the tied table: bf16(code * scale) from the Q8
+// streaming layout (k_dequant_row, lfm3_nanode.cu:138-142), or the bf16
+// table's value itself (lfm3_nanode.cu:6062-6070)
+PB_DEV float emb_value(const uint4* codes, const void* scales, int nch, int f32s, const uint16_t* e16, int H, int tok,
+                       int i) {
+  if (e16) return pb_bf2f(e16[(size_t)tok * H + b16_index(i)]);
+  const int b = i >> 5, jj = i & 31, c = b >> 6, bb = b & 63, l = bb & 31, half = bb >> 5;
+  const size_t seg = (size_t)tok * nch + c;
+  const int gi = (half * 2 + (jj >> 4)) * 32 + l;
+  const float code = (float)reinterpret_cast<const int8_t*>(codes)[(seg * 128 + gi) * 16 + (jj & 15)];
+  const float s = f32s ? reinterpret_cast<const float*>(scales)[(seg * 32 + l) * 2 + half]
+                       : pb_h2f(reinterpret_cast<const unsigned short*>(scales)[(seg * 32 + l) * 2 + half]);
+  return pb_bf2f(pb_f2bf(__fmul_rn(code, s)));
+}
 
 // ---- vector helpers: thread t owns N consecutive elements ---------------
 template <int N, int SYNC>
@@ -305,21 +326,11 @@ __device__ void pro_residual(const StepArgs& a, float* sx, float* red, const Gri
   gw_pass<SYNC>(gw);
   float R[E];
   if (embed) {
-    // k_dequant_row (lfm3_nanode.cu:138-142): bf16(code * scale), row = token;
-    // the row is read from the tied table's streaming layout
+    // the token's row of the tied table
     const int tok = ldi<SYNC>(&a.ctl->token);
-    const int8_t* cb = reinterpret_cast<const int8_t*>(a.emb_codes);
 #pragma unroll
-    for (int j = 0; j < E; j++) {
-      const int i = t * E + j;
-      const int b = i >> 5, jj = i & 31, c = b >> 6, bb = b & 63, l = bb & 31, half = bb >> 5;
-      const size_t seg = (size_t)tok * a.emb_nch + c;
-      const int gi = (half * 2 + (jj >> 4)) * 32 + l;
-      const float code = (float)cb[(seg * 128 + gi) * 16 + (jj & 15)];
-      const float s = a.emb_f32 ? reinterpret_cast<const float*>(a.emb_scales)[(seg * 32 + l) * 2 + half]
-                                : pb_h2f(reinterpret_cast<const unsigned short*>(a.emb_scales)[(seg * 32 + l) * 2 + half]);
-      R[j] = pb_bf2f(pb_f2bf(__fmul_rn(code, s)));
-    }
+    for (int j = 0; j < E; j++)
+      R[j] = emb_value(a.emb_codes, a.emb_scales, a.emb_nch, a.emb_f32, a.emb16, H, tok, t * E + j);
   } else {
     ld_bf<E, SYNC>(xin + (size_t)t * E, R);
     if (hin) {

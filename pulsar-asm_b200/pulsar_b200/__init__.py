@@ -74,6 +74,8 @@ def lib():
     L.pb_q80_quantize.argtypes = [vp, i, vp, vp, vp]
     L.pb_q80_gemv.argtypes = [vp, vp, vp, vp, vp, vp]
     L.pb_q80tc_pack.argtypes = [vp, vp, i, i, i, i, vp, pvp]
+    L.pb_bf16_relayout.argtypes = [vp, vp, i, i, vp]
+    L.pb_bf16_gemv.argtypes = [vp, i, i, vp, vp, vp]
     L.pb_q80_gemm.argtypes = [vp, i, vp, vp, vp, vp, vp]
     L.pb_q80_gemm_status.argtypes = [vp]
     L.pb_q1_pack.argtypes = [vp, i, i, i, vp, pvp]

@@ -25,7 +25,7 @@ T_Q8_F32S, T_F32, T_BF16, T_Q8_F16S = 1, 2, 3, 8
 
 def write_blob(path, cfg, tensors):
     """tensors: list of (name, kind, payload) with kind "q8" -> (codes int8 [N,K],
-    scales fp16/fp32 [N,K/32]) or "f32" -> ndarray."""
+    scales fp16/fp32 [N,K/32]), "bf16" -> uint16 bf16 bits, or "f32" -> ndarray."""
     table, blobs, off = [], [], 0
     for name, kind, payload in tensors:
         if kind == "q8":
@@ -43,6 +43,15 @@ def write_blob(path, cfg, tensors):
                               ncodes=len(cb), nscales=len(sb), crc=crc))
             blobs += [cb, sb]
             off += len(cb) + len(sb)
+        elif kind == "bf16":
+            # the certified arm's embedding: bf16 bits verbatim, no scales
+            # (export_lfm3_q8.py:96-110)
+            a = np.ascontiguousarray(payload, np.uint16)
+            b = a.tobytes()
+            table.append(dict(name=name, dtype=T_BF16, ne=list(a.shape), off=off, ncodes=len(b),
+                              nscales=0, crc=zlib.crc32(b) & 0xFFFFFFFF))
+            blobs.append(b)
+            off += len(b)
         elif kind == "f32":
             a = np.ascontiguousarray(payload, np.float32)
             b = a.tobytes()

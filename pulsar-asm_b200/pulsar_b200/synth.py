@@ -80,6 +80,12 @@ def make_weights(c, seed=1234):
         for k in ("op_norm", "post_op_norm", "ffn_norm", "post_ffn_norm"):
             d[k] = norm(H)
         layers.append(d)
+    if c.get("emb_bf16"):
+        # the certified arm's bf16 table (blob dtype 3): N(0, 1) values as bf16 bits
+        e = rng.standard_normal((c["vocab"], H), dtype=np.float32)
+        u = e.view(np.uint32)
+        e16 = ((u + np.uint32(0x7FFF) + ((u >> 16) & 1)) >> 16).astype(np.uint16)
+        return dict(layers=layers, embed_bf16=e16, final_norm=norm(H))
     return dict(layers=layers, embed=q8(rng, c["vocab"], H), final_norm=norm(H))
 
 
@@ -105,8 +111,11 @@ def write_model(path, c, w, fp32_scales=False):
                 ts.append((p + nm + ".weight", "f32", d[k]))
         if "taps" in d:
             ts.append((p + "conv.conv.weight", "f32", d["taps"].reshape(c["hidden"], 1, c["conv_w"])))
-    codes, sc = w["embed"]
-    ts.append(("lfm.model.embed_tokens.weight", "q8", (codes, sc.astype(np.float32) if fp32_scales else sc)))
+    if "embed_bf16" in w:
+        ts.append(("lfm.model.embed_tokens.weight", "bf16", w["embed_bf16"]))
+    else:
+        codes, sc = w["embed"]
+        ts.append(("lfm.model.embed_tokens.weight", "q8", (codes, sc.astype(np.float32) if fp32_scales else sc)))
     ts.append(("lfm.model.embedding_norm.weight", "f32", w["final_norm"]))
     return blob.write_blob(path, hf_cfg(c), ts)
 
@@ -127,7 +136,10 @@ def weight_bytes_per_token(c, fp32_scales=False):
         else:
             tot += q(3 * H, H) + q(H, H) + H * W * 4
         tot += 2 * q(F, H) + q(H, F) + 4 * H * 4
-    tot += q(V, H) + H * 4 + H + (H // 32) * sb
+    if c.get("emb_bf16"):
+        tot += V * H * 2 + H * 4 + H * 2          # bf16 head, final norm, one embedding row
+    else:
+        tot += q(V, H) + H * 4 + H + (H // 32) * sb
     return tot
 
 

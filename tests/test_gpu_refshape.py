@@ -122,3 +122,59 @@ def test_refshape_prefill_and_batch_integer_path(refm, oracle, pb, cuda):
         want, lg, _ = oms[b].decode(last[b], 16, want_logits=True)
         assert np.array_equal(_bits32(lg_dev[b]), _bits32(lg)), "batched logits differ for sequence %d" % b
         assert int(id_dev[b]) == want
+
+
+def test_bf16_head_kernel(oracle, pb, cuda):
+    """k_gemv_bf16 over the re-laid table (pb_bf16_relayout + pb_bf16_gemv)
+    bit for bit against the oracle's restatement, including a row of -0
+    weights and the largest finite bf16"""
+    torch = cuda
+    import ctypes as C
+    rng = np.random.default_rng(9)
+    N, K = 1000, 2048
+    w = oracle.f2bf((rng.standard_normal((N, K)) * 3).astype(np.float32))
+    w[5] = 0x8000                 # a row of -0 weights
+    w[7, :8] = 0x7F7F             # the largest finite bf16
+    x = oracle.f2bf(rng.standard_normal(K).astype(np.float32))
+    want = oracle.gemv_bf16(w, x)
+    src = torch.from_numpy(w.view(np.int16)).cuda()
+    dst = torch.empty_like(src)
+    L = pb.lib()
+    stream = C.c_void_p(torch.cuda.current_stream().cuda_stream)
+    assert L.pb_bf16_relayout(C.c_void_p(src.data_ptr()), C.c_void_p(dst.data_ptr()), N, K, stream) == 0
+    xd = torch.from_numpy(x.view(np.int16)).cuda()
+    y = torch.empty(N, dtype=torch.float32, device="cuda")
+    assert L.pb_bf16_gemv(C.c_void_p(dst.data_ptr()), N, K, C.c_void_p(xd.data_ptr()), C.c_void_p(y.data_ptr()),
+                          stream) == 0
+    torch.cuda.synchronize()
+    assert np.array_equal(_bits32(y.cpu().numpy()), _bits32(want))
+
+
+def test_bf16_embedding_model(tmp_path, oracle, pb, cuda, monkeypatch):
+    """the certified arm (blob dtype 3): embedding rows copied from the bf16
+    table and the k_gemv_bf16 head, at the reference shape; persistent kernel,
+    graph path and the chunked prefill, bit-exact"""
+    torch = cuda
+    from pulsar_b200 import synth
+    c = dict(REF_SHAPE, emb_bf16=True, n_layers=2, attn_layers=(1,), slide_layers=())
+    w = synth.make_weights(c, seed=3)
+    path = str(tmp_path / "b16.lfm3q8")
+    synth.write_model(path, c, w)
+    monkeypatch.delenv("PB_DECODE_MODE", raising=False)
+    _decode_and_check(pb, torch, oracle, c, w, path, 20)
+    monkeypatch.setenv("PB_DECODE_MODE", "graph")
+    _decode_and_check(pb, torch, oracle, c, w, path, 12)
+    m = pb.Model(path)
+    s = m.new_state(64)
+    om = oracle.Model(synth.oracle_cfg(c, 64), w, int_path=True)
+    T = 16
+    tokens = np.random.default_rng(4).integers(0, c["vocab"], T).astype(np.int32)
+    ids = torch.empty(T, dtype=torch.int32, device="cuda")
+    logits = torch.empty((T, c["vocab"]), dtype=torch.float32, device="cuda")
+    s.prefill_chunk(torch.from_numpy(tokens).cuda(), 0, ids, logits)
+    torch.cuda.synchronize()
+    lg_dev, id_dev = logits.cpu().numpy(), ids.cpu().numpy()
+    for t in range(T):
+        want, lg, _ = om.decode(int(tokens[t]), t, want_logits=True)
+        assert np.array_equal(_bits32(lg_dev[t]), _bits32(lg)), "prefill logits differ at position %d" % t
+        assert int(id_dev[t]) == want
