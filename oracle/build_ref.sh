@@ -153,6 +153,10 @@ echo "build_ref: built $out/libpb_refpins.so"
 #   lfm3_nanode.cu:852-859       k_sigmoid_gate
 #   lfm3_nanode.cu:892-911       k_shift_in, k_conv7
 #   lfm3_nanode.cu:942-964       k_argmax
+#   lfm3_nanode.cu:164-167       k_bf2f
+#   lfm3_nanode.cu:175-176       lfm_stage
+#   lfm3_nanode.cu:222-343       q8_partial (the Q8 GEMV leaf) and k_combine_bf
+#   lfm3_nanode.cu:3517-3534     k_gemv_bf16 (the certified arm's bf16 head)
 # followed by host wrappers written here (host buffers in and out) and probes
 # that return CUDA's own expf / rsqrtf / cosf / sinf for given arguments. The
 # library runs on the GPU box only (tests/golden/make_golden_lfm3.py).
@@ -171,6 +175,10 @@ if [ -x "$NVCC" ]; then
     sed -n '852,859p' "$A"
     sed -n '892,911p' "$A"
     sed -n '942,964p' "$A"
+    sed -n '164,167p' "$A"
+    sed -n '175,176p' "$A"
+    sed -n '222,343p' "$A"
+    sed -n '3517,3534p' "$A"
     cat <<'WRAP'
 /* ---- host wrappers and probes (this repository's code) ---- */
 namespace {
@@ -236,6 +244,29 @@ int pbref_gpu_argmax(const float* lg, int n, int* out) {
   float* dl = up(lg, n); int* di = up((const int*)nullptr, 1);
   k_argmax<<<1, 256>>>(dl, di, n);
   int rc = down(out, di, 1); cudaFree(dl); cudaFree(di); return rc;
+}
+/* y = bf16(gemv): q8_partial<bf16, FMA=true> with pick()'s KCHUNK (2048 when
+   it divides K, else K) and R (256 from N 1024, else 64), then k_combine_bf */
+int pbref_gpu_q8_gemv(const int8_t* q, const float* s, const uint16_t* x, uint16_t* y, int N, int K) {
+  const int KC = (K >= 2048 && K % 2048 == 0) ? 2048 : K, nch = K / KC, R = N >= 1024 ? 256 : 64;
+  int8_t* dq = up(q, (size_t)N * K); float* ds = up(s, (size_t)N * (K / 32));
+  bf16* dx = up((const bf16*)x, K); float* dp = up((const float*)nullptr, (size_t)N * nch);
+  bf16* dy = up((const bf16*)nullptr, N);
+  const size_t shm = (size_t)(KC / 32) * 33 * sizeof(float);
+  cudaFuncSetAttribute(q8_partial<bf16, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)shm);
+  q8_partial<bf16, true><<<((N + R - 1) / R) * nch, 256, shm>>>(dq, ds, dx, dp, N, K, KC, R, KC / 32);
+  k_combine_bf<<<(N + 255) / 256, 256>>>(dp, dy, N, nch);
+  int rc = down((bf16*)y, dy, N);
+  cudaFree(dq); cudaFree(ds); cudaFree(dx); cudaFree(dp); cudaFree(dy); return rc;
+}
+/* logits = lm_head_bf16: k_bf2f of x, k_gemv_bf16 with R = 32 rows per block */
+int pbref_gpu_gemv_bf16(const uint16_t* w, const uint16_t* x, float* y, int N, int K) {
+  bf16* dw = up((const bf16*)w, (size_t)N * K); bf16* dx = up((const bf16*)x, K);
+  float* dxf = up((const float*)nullptr, K); float* dy = up((const float*)nullptr, N);
+  k_bf2f<<<(K + 255) / 256, 256>>>(dx, dxf, K);
+  k_gemv_bf16<<<(N + 31) / 32, 256, (size_t)K * sizeof(float)>>>(dw, dxf, dy, N, K, 32);
+  int rc = down(y, dy, N);
+  cudaFree(dw); cudaFree(dx); cudaFree(dxf); cudaFree(dy); return rc;
 }
 int pbref_gpu_expf(const float* x, float* y, int n) {
   float* dx = up(x, n); float* dy = up((const float*)nullptr, n);

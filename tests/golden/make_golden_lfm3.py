@@ -4,6 +4,9 @@ k_silu_mul_bf, k_sigmoid_gate, k_mul_bf, k_shift_in + k_conv7, k_argmax),
 compiled for sm_100a by oracle/build_ref.sh into oracle/_ref/libpb_refgpu.so
 and run on a B200. TEST INFRASTRUCTURE ONLY.
 
+It also holds the Q8 GEMV leaf (q8_partial + k_combine_bf, one-chunk and
+chunked K) and the bf16 head (k_gemv_bf16) on seeded inputs.
+
 Besides each kernel's seeded inputs and outputs, the file records the values
 CUDA's rsqrtf / expf / cosf / sinf give for the arguments the kernels form
 (the arguments are found by replaying the kernels' arithmetic in numpy,
@@ -55,7 +58,8 @@ def main(path):
                        ("pbref_gpu_mul_bf", [vp, vp, vp, i]), ("pbref_gpu_sigmoid_gate", [vp, vp, i]),
                        ("pbref_gpu_conv", [vp, vp, vp, vp]), ("pbref_gpu_argmax", [vp, i, vp]),
                        ("pbref_gpu_expf", [vp, vp, i]), ("pbref_gpu_rsqrtf", [vp, vp, i]),
-                       ("pbref_gpu_cossin", [vp, vp, vp, i])]:
+                       ("pbref_gpu_cossin", [vp, vp, vp, i]), ("pbref_gpu_q8_gemv", [vp, vp, vp, vp, i, i]),
+                       ("pbref_gpu_gemv_bf16", [vp, vp, vp, i, i])]:
         getattr(L, name).argtypes = args
         getattr(L, name).restype = i
     sh = np.zeros(5, np.int32)
@@ -173,6 +177,25 @@ def main(path):
     for j, (lg, o) in enumerate(am):
         g["argmax%d_lg" % j] = lg
         g["argmax%d_id" % j] = np.array(o, np.int32)
+    # the Q8 GEMV leaf (q8_partial + k_combine_bf) with pick()'s chunking:
+    # one 7680-code chunk (the reference model's w2), 2048-code chunks, and a
+    # short one-chunk row; fp32 scales, bf16 input and output
+    for j, (N, K) in enumerate(((24, 7680), (16, 8192), (40, 1024))):
+        q = rng.integers(-127, 128, (N, K), dtype=np.int8)
+        q[0, :32] = -128
+        sc = (np.abs(rng.standard_normal((N, K // 32))) * 0.01).astype(np.float32)
+        x = bf16(rng.standard_normal(K))
+        y = np.zeros(N, np.uint16)
+        assert L.pbref_gpu_q8_gemv(p(q), p(sc), p(x), p(y), N, K) == 0
+        g.update({"q8g%d_q" % j: q, "q8g%d_s" % j: sc, "q8g%d_x" % j: x, "q8g%d_y" % j: y})
+    g["q8g_n"] = np.array(3, np.int32)
+    # the certified arm's bf16 head (k_gemv_bf16 via lm_head_bf16)
+    wb = bf16(rng.standard_normal((64, 2048)) * 2.0)
+    wb[3] = 0x8000
+    xb = bf16(rng.standard_normal(2048))
+    yb = np.zeros(64, np.float32)
+    assert L.pbref_gpu_gemv_bf16(p(wb), p(xb), p(yb), 64, 2048) == 0
+    g.update(b16_w=wb, b16_x=xb, b16_y=yb)
     np.savez_compressed(path, **g)
     print("wrote", path, "(%d arrays)" % len(g))
 

@@ -167,3 +167,23 @@ def test_oracle_conv_mul_argmax_bitexact(oracle, g):
     for j in range(3):
         lg = g["argmax%d_lg" % j]
         assert L.pbo_argmax(_p(lg), lg.size) == int(g["argmax%d_id" % j])
+
+
+def test_oracle_q8_gemv_leaf_bitexact(oracle, g):
+    """q8_partial + k_combine_bf with pick()'s chunking, the reference's own
+    kernels: one 7680-code chunk (lane chains over blocks l, l+32, ... of the
+    whole row, one tree), 2048-code chunks summed ascending, a short row"""
+    if "q8g_n" not in g:
+        pytest.skip("fixture predates the GEMV cases")
+    for j in range(int(g["q8g_n"])):
+        q, sc, x, y = g["q8g%d_q" % j], g["q8g%d_s" % j], g["q8g%d_x" % j], g["q8g%d_y" % j]
+        want = oracle.f2bf(np.float32(0) + oracle.q8f_gemv(q, sc, x))
+        assert np.array_equal(want, y), "case %d (K %d)" % (j, q.shape[1])
+
+
+def test_oracle_bf16_head_bitexact(oracle, g):
+    """k_gemv_bf16 (lm_head_bf16) of the reference against the oracle"""
+    if "b16_w" not in g:
+        pytest.skip("fixture predates the bf16 head")
+    got = oracle.gemv_bf16(g["b16_w"], g["b16_x"])
+    assert np.array_equal(got.view(np.uint32), np.ascontiguousarray(g["b16_y"]).view(np.uint32))
