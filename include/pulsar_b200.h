@@ -293,6 +293,29 @@ int pb_bonsai_decode(pb_bonsai* m, pb_bonsai_state* s, int token, int pos, const
 int pb_bonsai_decode_greedy(pb_bonsai* m, pb_bonsai_state* s, int token, int pos, int n, int* d_ids,
                             void* stream);
 
+/* ---- the Bonsai host hooks of pulsar_arm/bonsai2/pq1_fwd8_shim.h:24-60 ----
+ * (the reference implements them in pq1_fwd8_glue.c:235-246, :1483-1760):
+ * fwd8.c built with that shim and linked against this library runs each
+ * token on the device in one call. Weights and norms are fwd8's host arrays
+ * (wt: q k v o gate up down per layer, then output.weight; nw: attn ffn q k
+ * norms per layer, then output_norm), uploaded on first use and keyed by
+ * their pointers; x is the token's fp32 embedding row, rcc/rcs the 64 cos /
+ * sin values of position npos; head (fp32 [vocab]) receives the logits unless
+ * pq1_head_need(0). pq1_token_fused returns 0 when the step ran and -1 when it
+ * declines (the caller then runs its own path): no pq1_kv_shape, a shape the
+ * decoder does not take, or npos not the next position of the session's
+ * cache. pq1_head_top: the last step's greedy id and its logit, or -1.
+ * pq1_sess_init(n) (before the first step, 1 <= n <= 64) gives n sessions
+ * with their own caches and positions; pq1_sess_select picks the current one. */
+void pq1_kv_shape(int nl, int nkv, int ctx);
+int pq1_token_fused(int nl, const unsigned char* const* wt, const float* const* nw, int nh, int nkv, int hid,
+                    int inter, int vocab, int ctx, int npos, const float* rcc, const float* rcs, const float* x,
+                    float* head);
+void pq1_head_need(int need);
+int pq1_head_top(float* val);
+int pq1_sess_init(int n);
+void pq1_sess_select(int s);
+
 #ifdef __cplusplus
 }
 #endif

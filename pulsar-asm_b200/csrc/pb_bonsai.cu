@@ -1021,6 +1021,17 @@ extern "C" int pb_bonsai_state_residual(pb_bonsai_state* s, float* d_x, void* st
   return PB_OK;
 }
 
+// the caller's rope row for position pos ([cos 64 | sin 64], as fwd8.c's
+// host table holds it), for the host hooks; and the device logits
+int pb_bonsai_state_set_rope_row(pb_bonsai_state* s, int pos, const float* h_cos, const float* h_sin,
+                                 cudaStream_t st) {
+  if (!s || pos < 0 || pos >= s->max_ctx) return pb_set_error(PB_EINVAL, "rope row %d", pos);
+  PB_TRY_CUDA(cudaMemcpyAsync(s->rope + (size_t)pos * BS_HD, h_cos, 64 * 4, cudaMemcpyHostToDevice, st));
+  PB_TRY_CUDA(cudaMemcpyAsync(s->rope + (size_t)pos * BS_HD + 64, h_sin, 64 * 4, cudaMemcpyHostToDevice, st));
+  return PB_OK;
+}
+const float* pb_bonsai_state_logits(const pb_bonsai_state* s) { return s ? s->logits : nullptr; }
+
 extern "C" int pb_bonsai_decode(pb_bonsai* m, pb_bonsai_state* s, int token, int pos, const float* d_x,
                                 float* d_logits, int* out_id, void* stream) {
   if (!m || !s || s->m != m) return pb_set_error(PB_EINVAL, "pb_bonsai_decode: bad argument");

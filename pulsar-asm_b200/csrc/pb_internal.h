@@ -88,6 +88,11 @@ inline size_t pb_q8_scale_bytes(int N, int K, int sdt) {
 int pb_q8_pack_into(pb_q8* w, const int8_t* d_codes, const void* d_scales, cudaStream_t st,
                     int src_rows, int rmul, int radd);
 
+// Bonsai state access for the host hooks (pb_pq1hooks.cpp)
+int pb_bonsai_state_set_rope_row(pb_bonsai_state* s, int pos, const float* h_cos, const float* h_sin,
+                                 cudaStream_t st);
+const float* pb_bonsai_state_logits(const pb_bonsai_state* s);
+
 // the bf16 tied table (blob dtype 3) re-laid for the head GEMV (pb_q8.cu)
 int pb_b16_pack(const uint16_t* d_src, uint16_t* d_dst, int N, int K, cudaStream_t st);
 
