@@ -388,6 +388,26 @@ def kernel_suite(torch, pb, peak, stream):
             out[key] = {"layer_gemms": shapes, "T": T, "us_per_layer": ms * 1e3, "bytes": nbytes,
                         "GB/s": gbs, "frac": gbs / peak, "int8_TOPS": ops / (ms / 1e3) / 1e12, "copies": ncp}
         del layers
+        # cfg2, float path (the reference's REF_FLOAT numerics, pf_gemv_T): the
+        # same layer's projections at T = 32 through the position-tiled
+        # streaming kernel, bf16 in and out
+        T = 32
+        layers = [[pb.Q8Tensor(*q8_dev(n, k), stream=stream) for n, k in shapes] for _ in range(ncp)]
+        xs = {k: torch.randn((T, k), device="cuda", generator=g).to(torch.bfloat16).view(torch.int16)
+              for _, k in shapes}
+        ys = {n: torch.empty((T, n), dtype=torch.int16, device="cuda") for n, _ in shapes}
+
+        def flayer(ws=None):
+            for w, (n, k) in zip(ws, shapes):
+                w.gemm(xs[k], ys[n], stream=stream)
+        ms = _time_rotating(torch, stream, [lambda ws=ws: flayer(ws) for ws in layers], 10)
+        nbytes = lay_bytes + sum(T * k * 2 + T * n * 2 for n, k in shapes)
+        flops = sum(2 * n * k * T for n, k in shapes)
+        gbs = nbytes / (ms / 1e3) / 1e9
+        out["cfg2_q8f_gemm_T32"] = {"layer_gemms": shapes, "T": T, "us_per_layer": ms * 1e3, "bytes": nbytes,
+                                    "GB/s": gbs, "frac": gbs / peak, "fp32_TFLOPS": flops / (ms / 1e3) / 1e12,
+                                    "copies": ncp, "path": "float (REF_FLOAT leaf per position, k_q8f_tiled)"}
+        del layers
     torch.cuda.synchronize()
     return out
 

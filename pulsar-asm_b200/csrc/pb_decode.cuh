@@ -47,6 +47,7 @@
 // error.
 #pragma once
 #include "pb_step.cuh"
+#include <type_traits>
 
 namespace {
 
@@ -455,7 +456,9 @@ PB_DEV void dpro_plain(const DPhase& ph, float* sx, uint32_t tw, const PollCtx& 
 // and run the epilogue for all of the CTA's rows at once. A wait that gives up
 // breaks out of the loop and the phase still ends with the same barriers as
 // on the other warps.
-template <bool F32S, int EH, int W>
+// EXT: the build that also takes one-chunk rows and the bf16 head (a model
+// without them runs the build that compiles them out)
+template <bool F32S, int EH, int W, bool EXT>
 __device__ __forceinline__ unsigned gemv_phase(const DecodeArgs& d, const DPhase& ph, unsigned char* ring,
                                                float* xreg, bf16_t* res_s, uint64_t* full, unsigned it,
                                                float* red, float* bestv, int* besti, volatile int* abort_flag,
@@ -488,7 +491,7 @@ __device__ __forceinline__ unsigned gemv_phase(const DecodeArgs& d, const DPhase
   const int c = warp % nch, g = warp / nch;
   const unsigned ds = (unsigned)d.ds;
   f2x xr[32];
-  if (ph.b16) {
+  if (EXT && ph.b16) {
     // the bf16 head's lane chain: x[l + 32 m], m = 0..63, in pairs
 #pragma unroll
     for (int j = 0; j < 32; j++) xr[j] = pk(sx[lane + 33 * (2 * j)], sx[lane + 33 * (2 * j + 1)]);
@@ -509,139 +512,151 @@ __device__ __forceinline__ unsigned gemv_phase(const DecodeArgs& d, const DPhase
   const unsigned spt = issue_ctx()->spt, total = issue_ctx()->total;
   unsigned kn = it % spt + ds;
   while (kn >= spt) kn -= spt;
-  for (int r = r0; r < r1; r += RB) {
+  // the stage loop, compiled once per row kind so that the common one carries
+  // no per-stage test: 0 chunked rows, 1 one-chunk rows, 2 the bf16 head
+  auto stage_loop = [&](auto mode) {
+    constexpr int MODE = decltype(mode)::value;
+    for (int r = r0; r < r1; r += RB) {
 #ifdef PB_TRACE_STAGE_LOOP
-    const unsigned long long tw0 = (tm2 && threadIdx.x == 0) ? gtime() : 0;
+      const unsigned long long tw0 = (tm2 && threadIdx.x == 0) ? gtime() : 0;
 #endif
-    if (!mbar_wait(&full[slot], par, abort_flag)) {
-      *abort_flag = 1;
-      atomicCAS(d.err, 0, 2);
-      break;
-    }
+      if (!mbar_wait(&full[slot], par, abort_flag)) {
+        *abort_flag = 1;
+        atomicCAS(d.err, 0, 2);
+        break;
+      }
 #ifdef PB_TRACE_STAGE_LOOP
-    if (tm2 && threadIdx.x == 0) tm2[4] += gtime() - tw0;
+      if (tm2 && threadIdx.x == 0) tm2[4] += gtime() - tw0;
 #endif
-    const unsigned char* st = ring + (size_t)slot * Gm::STAGE;
-    if (ph.b16) {
-      // bf16 head (k_gemv_bf16, lfm3_nanode.cu:3517-3534): warp w takes row
-      // r + w of the stage's 8 (4 KB each, head layout); lane l's chain over
-      // k = l + 32 m is s = s + bf16(W[k]) * x[k], products and sums rounded
-      // apart; the shuffle-down tree gives the logit as is
-      const bool live = r + warp < r1;
-      const uint4* gp = reinterpret_cast<const uint4*>(st + (size_t)warp * 4096) + lane;
-      uint4 qb[8];
+      const unsigned char* st = ring + (size_t)slot * Gm::STAGE;
+      if constexpr (MODE == 2) {
+        // bf16 head (k_gemv_bf16, lfm3_nanode.cu:3517-3534): warp w takes row
+        // r + w of the stage's 8 (4 KB each, head layout); lane l's chain over
+        // k = l + 32 m is s = s + bf16(W[k]) * x[k], products and sums rounded
+        // apart; the shuffle-down tree gives the logit as is
+        const bool live = r + warp < r1;
+        const uint4* gp = reinterpret_cast<const uint4*>(st + (size_t)warp * 4096) + lane;
+        uint4 qb[8];
 #pragma unroll
-      for (int h = 0; h < 8; h++) qb[h] = live ? gp[32 * h] : make_uint4(0, 0, 0, 0);
+        for (int h = 0; h < 8; h++) qb[h] = live ? gp[32 * h] : make_uint4(0, 0, 0, 0);
 #pragma unroll
-      for (int h = 0; h < 8; h++) asm volatile("" ::"r"(qb[h].x), "r"(qb[h].y), "r"(qb[h].z), "r"(qb[h].w));
+        for (int h = 0; h < 8; h++) asm volatile("" ::"r"(qb[h].x), "r"(qb[h].y), "r"(qb[h].z), "r"(qb[h].w));
+        __syncwarp();
+        if (lane == 0 && slot_release(slot)) {
+          issue_ctx()->cnt[slot] = 0;
+          if (it + ds < total) issue_stage<F32S>(kn, slot, it + ds, ring, full);
+        }
+        float acc = 0.0f;
+#pragma unroll
+        for (int h = 0; h < 8; h++) {
+          const unsigned ws[4] = {qb[h].x, qb[h].y, qb[h].z, qb[h].w};
+#pragma unroll
+          for (int i = 0; i < 4; i++) {
+            float xa, xb;
+            upk(xr[4 * h + i], xa, xb);
+            acc = __fadd_rn(acc, __fmul_rn(pb_lo2f(ws[i]), xa));
+            acc = __fadd_rn(acc, __fmul_rn(pb_hi2f(ws[i]), xb));
+          }
+        }
+        const float v = pb_warp_tree(acc);
+        if (lane == 0 && live) rowv[(r - r0 + warp) * nch] = v;
+        it++;
+        if (++slot == ds) { slot = 0; par ^= 1; }
+        if (++kn == spt) kn = 0;
+        continue;
+      }
+      uint4 q[2][4];
+      float slo[2], shi[2];
+#pragma unroll
+      for (int u = 0; u < 2; u++) {
+        const int rel = g * 2 + u;
+        const int seg = rel * nch + c;
+        if (r + rel < r1) {
+          const uint4* gp = reinterpret_cast<const uint4*>(st + (size_t)seg * 2048) + lane;
+#pragma unroll
+          for (int h = 0; h < 4; h++) q[u][h] = gp[32 * h];
+          if (F32S) {
+            const float2 s2 = reinterpret_cast<const float2*>(st + STAGE_CODES)[seg * 32 + lane];
+            slo[u] = s2.x; shi[u] = s2.y;
+          } else {
+            const unsigned w = reinterpret_cast<const unsigned*>(st + STAGE_CODES)[seg * 32 + lane];
+            slo[u] = pb_h2f((unsigned short)(w & 0xffffu));
+            shi[u] = pb_h2f((unsigned short)(w >> 16));
+          }
+        } else {
+#pragma unroll
+          for (int h = 0; h < 4; h++) q[u][h] = make_uint4(0, 0, 0, 0);
+          slo[u] = shi[u] = 0.0f;
+        }
+      }
+      // release the slot as soon as its data sit in registers (the empty asm
+      // makes every load complete first), so the refill of the stage DS ahead
+      // overlaps this stage's arithmetic; the last warp to release issues it
+      asm volatile("" ::"r"(q[0][0].x), "r"(q[0][0].y), "r"(q[0][0].z), "r"(q[0][0].w), "r"(q[0][1].x),
+                   "r"(q[0][1].y), "r"(q[0][1].z), "r"(q[0][1].w), "r"(q[0][2].x), "r"(q[0][2].y),
+                   "r"(q[0][2].z), "r"(q[0][2].w), "r"(q[0][3].x), "r"(q[0][3].y), "r"(q[0][3].z),
+                   "r"(q[0][3].w), "f"(slo[0]), "f"(shi[0]));
+      asm volatile("" ::"r"(q[1][0].x), "r"(q[1][0].y), "r"(q[1][0].z), "r"(q[1][0].w), "r"(q[1][1].x),
+                   "r"(q[1][1].y), "r"(q[1][1].z), "r"(q[1][1].w), "r"(q[1][2].x), "r"(q[1][2].y),
+                   "r"(q[1][2].z), "r"(q[1][2].w), "r"(q[1][3].x), "r"(q[1][3].y), "r"(q[1][3].z),
+                   "r"(q[1][3].w), "f"(slo[1]), "f"(shi[1]));
       __syncwarp();
+#ifdef PB_TRACE_STAGE_LOOP
+      const unsigned long long tr0 = (tm2 && threadIdx.x == 0) ? gtime() : 0;
+#endif
       if (lane == 0 && slot_release(slot)) {
         issue_ctx()->cnt[slot] = 0;
         if (it + ds < total) issue_stage<F32S>(kn, slot, it + ds, ring, full);
       }
-      float acc = 0.0f;
-#pragma unroll
-      for (int h = 0; h < 8; h++) {
-        const unsigned ws[4] = {qb[h].x, qb[h].y, qb[h].z, qb[h].w};
-#pragma unroll
-        for (int i = 0; i < 4; i++) {
-          float xa, xb;
-          upk(xr[4 * h + i], xa, xb);
-          acc = __fadd_rn(acc, __fmul_rn(pb_lo2f(ws[i]), xa));
-          acc = __fadd_rn(acc, __fmul_rn(pb_hi2f(ws[i]), xb));
-        }
-      }
-      const float v = pb_warp_tree(acc);
-      if (lane == 0 && live) rowv[(r - r0 + warp) * nch] = v;
-      it++;
-      if (++slot == ds) { slot = 0; par ^= 1; }
-      if (++kn == spt) kn = 0;
-      continue;
-    }
-    uint4 q[2][4];
-    float slo[2], shi[2];
-#pragma unroll
-    for (int u = 0; u < 2; u++) {
-      const int rel = g * 2 + u;
-      const int seg = rel * nch + c;
-      if (r + rel < r1) {
-        const uint4* gp = reinterpret_cast<const uint4*>(st + (size_t)seg * 2048) + lane;
-#pragma unroll
-        for (int h = 0; h < 4; h++) q[u][h] = gp[32 * h];
-        if (F32S) {
-          const float2 s2 = reinterpret_cast<const float2*>(st + STAGE_CODES)[seg * 32 + lane];
-          slo[u] = s2.x; shi[u] = s2.y;
-        } else {
-          const unsigned w = reinterpret_cast<const unsigned*>(st + STAGE_CODES)[seg * 32 + lane];
-          slo[u] = pb_h2f((unsigned short)(w & 0xffffu));
-          shi[u] = pb_h2f((unsigned short)(w >> 16));
-        }
-      } else {
-#pragma unroll
-        for (int h = 0; h < 4; h++) q[u][h] = make_uint4(0, 0, 0, 0);
-        slo[u] = shi[u] = 0.0f;
-      }
-    }
-    // release the slot as soon as its data sit in registers (the empty asm
-    // makes every load complete first), so the refill of the stage DS ahead
-    // overlaps this stage's arithmetic; the last warp to release issues it
-    asm volatile("" ::"r"(q[0][0].x), "r"(q[0][0].y), "r"(q[0][0].z), "r"(q[0][0].w), "r"(q[0][1].x),
-                 "r"(q[0][1].y), "r"(q[0][1].z), "r"(q[0][1].w), "r"(q[0][2].x), "r"(q[0][2].y),
-                 "r"(q[0][2].z), "r"(q[0][2].w), "r"(q[0][3].x), "r"(q[0][3].y), "r"(q[0][3].z),
-                 "r"(q[0][3].w), "f"(slo[0]), "f"(shi[0]));
-    asm volatile("" ::"r"(q[1][0].x), "r"(q[1][0].y), "r"(q[1][0].z), "r"(q[1][0].w), "r"(q[1][1].x),
-                 "r"(q[1][1].y), "r"(q[1][1].z), "r"(q[1][1].w), "r"(q[1][2].x), "r"(q[1][2].y),
-                 "r"(q[1][2].z), "r"(q[1][2].w), "r"(q[1][3].x), "r"(q[1][3].y), "r"(q[1][3].z),
-                 "r"(q[1][3].w), "f"(slo[1]), "f"(shi[1]));
-    __syncwarp();
 #ifdef PB_TRACE_STAGE_LOOP
-    const unsigned long long tr0 = (tm2 && threadIdx.x == 0) ? gtime() : 0;
+      const unsigned long long tr1 = (tm2 && threadIdx.x == 0) ? gtime() : 0;
 #endif
-    if (lane == 0 && slot_release(slot)) {
-      issue_ctx()->cnt[slot] = 0;
-      if (it + ds < total) issue_stage<F32S>(kn, slot, it + ds, ring, full);
-    }
-#ifdef PB_TRACE_STAGE_LOOP
-    const unsigned long long tr1 = (tm2 && threadIdx.x == 0) ? gtime() : 0;
-#endif
-    if (ph.one) {
-      // park this lane's two block dots and scales per (row, segment)
-      float4* rq = reinterpret_cast<float4*>(rowv);
+      if constexpr (MODE == 1) {
+        // park this lane's two block dots and scales per (row, segment)
+        float4* rq = reinterpret_cast<float4*>(rowv);
 #pragma unroll
-      for (int u = 0; u < 2; u++) {
-        float d0, d1;
-        dots2(q[u], xr, d0, d1);
-        const int lr = r - r0 + g * 2 + u;
-        if (r + g * 2 + u < r1) rq[(lr * nch + c) * 32 + lane] = make_float4(d0, d1, slo[u], shi[u]);
+        for (int u = 0; u < 2; u++) {
+          float d0, d1;
+          dots2(q[u], xr, d0, d1);
+          const int lr = r - r0 + g * 2 + u;
+          if (r + g * 2 + u < r1) rq[(lr * nch + c) * 32 + lane] = make_float4(d0, d1, slo[u], shi[u]);
+        }
+        it++;
+        if (++slot == ds) { slot = 0; par ^= 1; }
+        if (++kn == spt) kn = 0;
+        continue;
+      }
+      float v[2];
+#pragma unroll
+      for (int u = 0; u < 2; u++) v[u] = pb_warp_tree(leaf2(q[u], slo[u], shi[u], xr));
+#ifdef PB_TRACE_STAGE_LOOP
+      if (tm2 && threadIdx.x == 0) {
+        asm volatile("" ::"f"(v[0]), "f"(v[1]));
+        tm2[3] += tr1 - tr0;            // slot 5: release (+ refill issue) of warp 0
+        tm2[5] += gtime() - tr1;        // slot 7: chains and trees of warp 0
+      }
+#endif
+      if (lane == 0) {
+        const int lr = r - r0 + g * 2;
+        rowv[lr * nch + c] = v[0];
+        if (r + g * 2 + 1 < r1) rowv[(lr + 1) * nch + c] = v[1];
       }
       it++;
       if (++slot == ds) { slot = 0; par ^= 1; }
       if (++kn == spt) kn = 0;
-      continue;
     }
-    float v[2];
-#pragma unroll
-    for (int u = 0; u < 2; u++) v[u] = pb_warp_tree(leaf2(q[u], slo[u], shi[u], xr));
-#ifdef PB_TRACE_STAGE_LOOP
-    if (tm2 && threadIdx.x == 0) {
-      asm volatile("" ::"f"(v[0]), "f"(v[1]));
-      tm2[3] += tr1 - tr0;            // slot 5: release (+ refill issue) of warp 0
-      tm2[5] += gtime() - tr1;        // slot 7: chains and trees of warp 0
-    }
-#endif
-    if (lane == 0) {
-      const int lr = r - r0 + g * 2;
-      rowv[lr * nch + c] = v[0];
-      if (r + g * 2 + 1 < r1) rowv[(lr + 1) * nch + c] = v[1];
-    }
-    it++;
-    if (++slot == ds) { slot = 0; par ^= 1; }
-    if (++kn == spt) kn = 0;
+  };
+  if constexpr (EXT) {
+    if (ph.b16) stage_loop(std::integral_constant<int, 2>{});
+    else if (ph.one) stage_loop(std::integral_constant<int, 1>{});
+    else stage_loop(std::integral_constant<int, 0>{});
+  } else {
+    stage_loop(std::integral_constant<int, 0>{});
   }
   dsync();
   // epilogue over the CTA's rows: chunk values added in chunk order from 0
   const int nr = r1 - r0;
-  if (ph.one) {
+  if (EXT && ph.one) {
     // one-chunk rows (bf16 output only): a warp per row chains every lane's
     // blocks l, l+32, l+64, ... in order, then the tree; the chunk sum is 0 + v
     const float4* rq = reinterpret_cast<const float4*>(rowv);
@@ -680,7 +695,7 @@ __device__ __forceinline__ unsigned gemv_phase(const DecodeArgs& d, const DPhase
     float* out = ph.fout;
     for (int i = threadIdx.x; i < nr; i += DTHREADS) {
       float o = 0.0f;
-      if (ph.b16) o = rowv[i * nch];    // the bf16 head's logit is the tree's value
+      if (EXT && ph.b16) o = rowv[i * nch];    // the bf16 head's logit is the tree's value
       else
         for (int cc = 0; cc < nch; cc++) o = __fadd_rn(o, rowv[i * nch + cc]);
       out[r0 + i] = o;
@@ -1019,7 +1034,7 @@ PB_DEV int argmax_slots(const Ctl* ctl) {
   return __shfl_sync(0xffffffffu, ix, 0);
 }
 
-template <bool F32S, int E, int EH, int W>
+template <bool F32S, int E, int EH, int W, bool EXT>
 __global__ void __launch_bounds__(DTHREADS, 1) k_decode(DecodeArgs d) {
   typedef DGeo<F32S> Gm;
   IssueCtx* ic = issue_ctx();
@@ -1079,7 +1094,7 @@ __global__ void __launch_bounds__(DTHREADS, 1) k_decode(DecodeArgs d) {
       const DPhase& ph = d.phases[p];
       unsigned long long* tm2 = (d.trace && tok == 0) ? d.trace + ((size_t)blockIdx.x * d.nphase + p) * 8 + 2 : nullptr;
       if (ph.kind == PH_GEMV) {
-        it = gemv_phase<F32S, EH, W>(d, ph, ring, xreg, res_s, full, it, red, bestv, besti, &abort_flag, tm2,
+        it = gemv_phase<F32S, EH, W, EXT>(d, ph, ring, xreg, res_s, full, it, red, bestv, besti, &abort_flag, tm2,
                                      tw_in, tw_out, pos, tok_id);
       } else if (ph.kind == PH_SCORE) {
         score_phase<E>(ph, pos, xreg, tw_in, (unsigned long long)q << 32, &abort_flag, d.err);

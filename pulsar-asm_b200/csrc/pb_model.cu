@@ -1098,7 +1098,7 @@ int build_phases(pb_state* s) {
   return PB_OK;
 }
 
-template <bool F32S, int E, int EH, int W>
+template <bool F32S, int E, int EH, int W, bool EXT>
 int launch_decode_t(pb_state* s, int ntok, cudaStream_t st) {
   DecodeArgs d;
   d.phases = s->d_phases;
@@ -1131,13 +1131,13 @@ int launch_decode_t(pb_state* s, int ntok, cudaStream_t st) {
     {
       std::lock_guard<std::mutex> lk(mu);
       if (dev < 0 || dev >= 64 || s->dsmem > attr_max[dev]) {
-        PB_TRY_CUDA(cudaFuncSetAttribute(k_decode<F32S, E, EH, W>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+        PB_TRY_CUDA(cudaFuncSetAttribute(k_decode<F32S, E, EH, W, EXT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          (int)s->dsmem));
         if (dev >= 0 && dev < 64) attr_max[dev] = s->dsmem;
       }
     }
     int per_sm = 0;
-    PB_TRY_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k_decode<F32S, E, EH, W>, DTHREADS, s->dsmem));
+    PB_TRY_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k_decode<F32S, E, EH, W, EXT>, DTHREADS, s->dsmem));
     if (per_sm < 1) return pb_set_error(PB_ENOTSUP, "persistent decode does not fit on an SM");
     s->decode_checked = true;
   }
@@ -1146,7 +1146,7 @@ int launch_decode_t(pb_state* s, int ntok, cudaStream_t st) {
   PB_TRY_CUDA(cudaMemsetAsync(s->d_bar, 0, sizeof(unsigned), st));
   if (s->d_trace) PB_TRY_CUDA(cudaMemsetAsync(s->d_trace, 0, (size_t)pb_num_sms() * s->nphase * 8 * 8, st));
   void* args[] = {&d};
-  cudaError_t e = cudaLaunchCooperativeKernel((const void*)k_decode<F32S, E, EH, W>, dim3(grid), dim3(DTHREADS), args,
+  cudaError_t e = cudaLaunchCooperativeKernel((const void*)k_decode<F32S, E, EH, W, EXT>, dim3(grid), dim3(DTHREADS), args,
                                               s->dsmem, st);
   // the tags of the next launch continue after this one's, whether or not it
   // ran to the end (a launch that gave up leaves words of its own tag range)
@@ -1156,14 +1156,26 @@ int launch_decode_t(pb_state* s, int ntok, cudaStream_t st) {
   return PB_OK;
 }
 
+// a model with one-chunk rows (K not a multiple of 2048) or the bf16 head
+bool model_ext(const pb_model* m) {
+  if (m->head.layout == PB_Q8_B16) return true;
+  for (const auto& Ly : m->layers)
+    if ((Ly.first.one && Ly.first.nch > 1) || (Ly.mix.one && Ly.mix.nch > 1) || (Ly.w13.one && Ly.w13.nch > 1) ||
+        (Ly.w2.one && Ly.w2.nch > 1))
+      return true;
+  return false;
+}
+
 int launch_decode(pb_state* s, int ntok, cudaStream_t st) {
   int rc = build_phases(s);
   if (rc) return rc;
   const bool f = s->m->sdt == PB_DT_F32;
   if (persistent_shape(s->m)) {
     if (s->m->HD == 128)
-      return f ? launch_decode_t<true, 4, 8, 7>(s, ntok, st) : launch_decode_t<false, 4, 8, 7>(s, ntok, st);
-    return f ? launch_decode_t<true, 2, 8, 3>(s, ntok, st) : launch_decode_t<false, 2, 8, 3>(s, ntok, st);
+      return f ? launch_decode_t<true, 4, 8, 7, true>(s, ntok, st) : launch_decode_t<false, 4, 8, 7, true>(s, ntok, st);
+    if (model_ext(s->m))
+      return f ? launch_decode_t<true, 2, 8, 3, true>(s, ntok, st) : launch_decode_t<false, 2, 8, 3, true>(s, ntok, st);
+    return f ? launch_decode_t<true, 2, 8, 3, false>(s, ntok, st) : launch_decode_t<false, 2, 8, 3, false>(s, ntok, st);
   }
   return pb_set_error(PB_ENOTSUP, "persistent decode: shape not compiled");
 }

@@ -234,6 +234,114 @@ k_q8f_stream(const uint4* __restrict__ codes, const void* __restrict__ scales,
   }
 }
 
+// ------------------------------------------------ T positions (float path)
+// pf_gemv_T's values (lfm3_nanode.cu:4840-4968: per position, the GEMV leaf
+// and chunk order of q8_partial + k_combine) for a tensor in the streaming
+// layout: each row's codes and scales are read once per tile of TT positions.
+// A warp takes a whole row: per segment (in chunk order) its lane converts
+// the 64 codes of blocks l and l+32 once, then for every position of the tile
+// runs the two dot chains as one packed fma.rn.f32x2 chain against the
+// positions' x in shared memory (x of blocks l and l+32 side by side). Chunked
+// rows: the chunk's leaf (s_lo, s_hi FMAs from 0), the tree, and the chunk
+// values summed ascending from 0; one-chunk rows: the lane chain runs on over
+// the segments, one tree, 0 + v.
+constexpr int Q8T_X2 = 32 * 33;   // float2 per (segment, position): lane-major, padded
+typedef unsigned long long q8t_f2;
+PB_DEV q8t_f2 q8t_pk(float a, float b) {
+  q8t_f2 r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(a), "f"(b));
+  return r;
+}
+PB_DEV void q8t_upk(q8t_f2 v, float& a, float& b) { asm("mov.b64 {%0, %1}, %2;" : "=f"(a), "=f"(b) : "l"(v)); }
+PB_DEV q8t_f2 q8t_fma2(q8t_f2 a, q8t_f2 b, q8t_f2 c) {
+  q8t_f2 d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+  return d;
+}
+
+template <int NCH, bool ONE, bool F32S, bool OUTF32>
+__global__ void __launch_bounds__(256, 1)
+k_q8f_tiled(const uint4* __restrict__ codes, const void* __restrict__ scales, const bf16_t* __restrict__ x,
+            void* __restrict__ y, int N, int K, int T) {
+  constexpr int TT = 16 / NCH;
+  extern __shared__ __align__(16) float2 xs[];     // [NCH][TT][Q8T_X2]
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  for (int t0 = 0; t0 < T; t0 += TT) {
+    const int nt = T - t0 < TT ? T - t0 : TT;
+    __syncthreads();
+    // stage the tile's x: (segment c, position t, lane l, j) = (x[c 2048 + 32 l + j],
+    // x[c 2048 + 32 (l + 32) + j]); blocks past K (one-chunk padding) and
+    // positions past T are zero
+    for (int i = threadIdx.x; i < NCH * TT * 1024; i += blockDim.x) {
+      const int j = i & 31, l = (i >> 5) & 31, t = (i >> 10) % TT, c = i / (TT * 1024);
+      const int k0 = c * 2048 + 32 * l + j, k1 = k0 + 1024;
+      float a = 0.0f, b = 0.0f;
+      if (t < nt) {
+        const bf16_t* xr = x + (size_t)(t0 + t) * K;
+        if (k0 < K) a = pb_bf2f(xr[k0]);
+        if (k1 < K) b = pb_bf2f(xr[k1]);
+      }
+      xs[(c * TT + t) * Q8T_X2 + l * 33 + j] = make_float2(a, b);
+    }
+    __syncthreads();
+    for (int row = blockIdx.x * 8 + warp; row < N; row += gridDim.x * 8) {
+      float acc[TT], tot[TT];
+#pragma unroll
+      for (int t = 0; t < TT; t++) { acc[t] = 0.0f; tot[t] = 0.0f; }
+#pragma unroll 1
+      for (int c = 0; c < NCH; c++) {
+        const size_t seg = (size_t)row * NCH + c;
+        const uint4* base = codes + seg * 128 + lane;
+        uint4 q[4];
+#pragma unroll
+        for (int h = 0; h < 4; h++) q[h] = pb_ldg_stream(base + 32 * h);
+        float slo, shi;
+        ScalePair<F32S>::load(scales, seg * 32 + lane, slo, shi);
+        // codes of block l (granules 0, 1) and block l+32 (granules 2, 3), paired
+        q8t_f2 cw[32];
+#pragma unroll
+        for (int g = 0; g < 2; g++) {
+          const unsigned wa[4] = {q[g].x, q[g].y, q[g].z, q[g].w}, wb[4] = {q[g + 2].x, q[g + 2].y, q[g + 2].z, q[g + 2].w};
+#pragma unroll
+          for (int k = 0; k < 4; k++) {
+            const unsigned ua = wa[k] ^ 0x80808080u, ub = wb[k] ^ 0x80808080u;
+#pragma unroll
+            for (int jj = 0; jj < 4; jj++) cw[g * 16 + 4 * k + jj] = q8t_pk(pb_code(ua, jj), pb_code(ub, jj));
+          }
+        }
+        const float2* xc = xs + (size_t)c * TT * Q8T_X2 + lane * 33;
+#pragma unroll
+        for (int t = 0; t < TT; t++) {
+          const float2* xt = xc + t * Q8T_X2;
+          q8t_f2 d = q8t_pk(0.0f, 0.0f);
+#pragma unroll
+          for (int j = 0; j < 32; j++) {
+            const float2 xv = xt[j];
+            d = q8t_fma2(cw[j], q8t_pk(xv.x, xv.y), d);
+          }
+          float d0, d1;
+          q8t_upk(d, d0, d1);
+          if (ONE) {
+            acc[t] = __fmaf_rn(slo, d0, acc[t]);
+            acc[t] = __fmaf_rn(shi, d1, acc[t]);
+          } else {
+            const float v = pb_warp_tree(__fmaf_rn(shi, d1, __fmaf_rn(slo, d0, 0.0f)));
+            tot[t] = __fadd_rn(tot[t], v);
+          }
+        }
+      }
+#pragma unroll
+      for (int t = 0; t < TT; t++) {
+        const float o = ONE ? __fadd_rn(0.0f, pb_warp_tree(acc[t])) : tot[t];
+        if (lane == 0 && t < nt) {
+          if (OUTF32) reinterpret_cast<float*>(y)[(size_t)(t0 + t) * N + row] = o;
+          else reinterpret_cast<bf16_t*>(y)[(size_t)(t0 + t) * N + row] = pb_f2bf(o);
+        }
+      }
+    }
+  }
+}
+
 // ---------------------------------------------------- general (row-major) path
 // Any K % 32 == 0 and T positions: one warp per row, positions in groups of 4,
 // the same leaf chains and trees, chunks per pick(). x is read through L2.
@@ -471,6 +579,42 @@ static int launch_stream(const pb_q8* w, const uint16_t* x, void* y, int outf32,
   return PB_OK;
 }
 
+template <int NCH, bool ONE, bool F32S, bool OUTF32>
+static int launch_tiled_t(const pb_q8* w, int T, const uint16_t* x, void* y, cudaStream_t st) {
+  constexpr int TT = 16 / NCH;
+  const size_t smem = (size_t)NCH * TT * Q8T_X2 * sizeof(float2);
+  static bool set[64] = {};
+  int dev = 0;
+  PB_TRY_CUDA(cudaGetDevice(&dev));
+  if (dev >= 0 && dev < 64 && !set[dev]) {
+    PB_TRY_CUDA(cudaFuncSetAttribute(k_q8f_tiled<NCH, ONE, F32S, OUTF32>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     (int)smem));
+    set[dev] = true;
+  }
+  int grid = pb_num_sms();
+  if (grid > (w->N + 7) / 8) grid = (w->N + 7) / 8;
+  k_q8f_tiled<NCH, ONE, F32S, OUTF32><<<grid, 256, smem, st>>>(reinterpret_cast<const uint4*>(w->codes), w->scales,
+                                                              x, y, w->N, w->K, T);
+  PB_LAUNCHED("k_q8f_tiled");
+  return PB_OK;
+}
+template <int NCH, bool ONE>
+static int launch_tiled_n(const pb_q8* w, int T, const uint16_t* x, void* y, bool outf32, cudaStream_t st) {
+  const bool f = w->sdt == PB_DT_F32;
+  if (f) return outf32 ? launch_tiled_t<NCH, ONE, true, true>(w, T, x, y, st) : launch_tiled_t<NCH, ONE, true, false>(w, T, x, y, st);
+  return outf32 ? launch_tiled_t<NCH, ONE, false, true>(w, T, x, y, st) : launch_tiled_t<NCH, ONE, false, false>(w, T, x, y, st);
+}
+// T positions of a streaming-layout tensor (pb_q8_gemm, the prefill's float path)
+static int launch_tiled(const pb_q8* w, int T, const uint16_t* x, void* y, bool outf32, cudaStream_t st) {
+  switch (w->nch) {
+    case 1: return launch_tiled_n<1, false>(w, T, x, y, outf32, st);   // one chunk either way
+    case 2: return w->one ? launch_tiled_n<2, true>(w, T, x, y, outf32, st) : launch_tiled_n<2, false>(w, T, x, y, outf32, st);
+    case 4: return w->one ? launch_tiled_n<4, true>(w, T, x, y, outf32, st) : launch_tiled_n<4, false>(w, T, x, y, outf32, st);
+    case 8: return w->one ? launch_tiled_n<8, true>(w, T, x, y, outf32, st) : launch_tiled_n<8, false>(w, T, x, y, outf32, st);
+  }
+  return pb_set_error(PB_EINVAL, "stream layout with %d chunks", w->nch);
+}
+
 int pb_q8_gemv_launch(const pb_q8* w, const uint16_t* d_x, void* d_y, int y_dtype, cudaStream_t st) {
   const int outf32 = y_dtype == PB_DT_F32;
   if (w->layout == PB_Q8_STREAM) {
@@ -590,15 +734,7 @@ extern "C" int pb_q8_gemm(const pb_q8* w, int T, const uint16_t* d_x, void* d_y,
   if (w->layout == PB_Q8_UMMA) return pb_set_error(PB_EINVAL, "pb_q8_gemm: tensor packed for pb_q80_gemm");
   if (y_dtype != PB_DT_BF16 && y_dtype != PB_DT_F32) return pb_set_error(PB_EINVAL, "pb_q8_gemm: y dtype");
   cudaStream_t st = (cudaStream_t)stream;
-  if (w->layout == PB_Q8_STREAM) {
-    // positions one at a time through the streaming kernel: same values
-    for (int t = 0; t < T; t++) {
-      const size_t ob = (size_t)t * w->N * (y_dtype == PB_DT_F32 ? 4 : 2);
-      int rc = pb_q8_gemv_launch(w, d_x + (size_t)t * w->K, (char*)d_y + ob, y_dtype, st);
-      if (rc) return rc;
-    }
-    return PB_OK;
-  }
+  if (w->layout == PB_Q8_STREAM) return launch_tiled(w, T, d_x, d_y, y_dtype == PB_DT_F32, st);
   const int KC = w->K >= 2048 && w->K % 2048 == 0 ? 2048 : (w->K == 512 ? 512 : w->K);
   k_q8f_general<<<(w->N + 7) / 8, 256, 0, st>>>(w->codes, w->scales, w->sdt == PB_DT_F32, d_x, d_y,
                                                 y_dtype == PB_DT_F32, w->N, w->K, T, KC);

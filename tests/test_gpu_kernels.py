@@ -41,8 +41,11 @@ def test_q8_gemv_bitexact(cuda, oracle, pb, N, K, scales):
     assert np.array_equal(_bits(yf.cpu().numpy()), _bits(np.float32(0) + want))
 
 
-@pytest.mark.parametrize("N,K,T", [(256, 2048, 4), (128, 1024, 5), (64, 8192, 3)])
+@pytest.mark.parametrize("N,K,T", [(256, 2048, 4), (128, 1024, 5), (64, 8192, 3), (96, 7680, 21), (300, 2048, 40),
+                                   (40, 16384, 3), (70, 4096, 9)])
 def test_q8_gemm_positions(cuda, oracle, pb, N, K, T):
+    """T positions of a streaming tensor in one position-tiled launch: every
+    position's output equals the single-position GEMV's (pf_gemv_T)"""
     torch = cuda
     rng = np.random.default_rng(T)
     codes = rng.integers(-127, 128, (N, K), dtype=np.int8)
