@@ -306,7 +306,11 @@ int pb_bonsai_decode_greedy(pb_bonsai* m, pb_bonsai_state* s, int token, int pos
  * decoder does not take, or npos not the next position of the session's
  * cache. pq1_head_top: the last step's greedy id and its logit, or -1.
  * pq1_sess_init(n) (before the first step, 1 <= n <= 64) gives n sessions
- * with their own caches and positions; pq1_sess_select picks the current one. */
+ * with their own caches and positions; pq1_sess_select picks the current one.
+ * pq1_attn_kv_put: the K / V rows ([nkv][128] f16, post-rope) of layer il at
+ * position npos that fwd8 computed on the host (it runs a sequence's first
+ * token there), mirrored into the current session's cache; 0, or -1 when npos
+ * is not that layer's next position. */
 void pq1_kv_shape(int nl, int nkv, int ctx);
 int pq1_token_fused(int nl, const unsigned char* const* wt, const float* const* nw, int nh, int nkv, int hid,
                     int inter, int vocab, int ctx, int npos, const float* rcc, const float* rcs, const float* x,
@@ -315,6 +319,7 @@ void pq1_head_need(int need);
 int pq1_head_top(float* val);
 int pq1_sess_init(int n);
 void pq1_sess_select(int s);
+int pq1_attn_kv_put(int il, int nl, int nkv, int ctx, int npos, const uint16_t* k16, const uint16_t* v16);
 
 #ifdef __cplusplus
 }

@@ -11,12 +11,18 @@
 //                                key), the caller's fp32 embedding row and
 //                                this position's rope row; logits written to
 //                                the host unless pq1_head_need(0);
-//   pq1_head_top(&val)           the device argmax of the last token, or -1.
+//   pq1_head_top(&val)           the device argmax of the last token, or -1;
+//   pq1_attn_kv_put(il, ...)     a layer's K/V rows of a position fwd8 ran on
+//                                the host (it always runs a sequence's first
+//                                token there, fwd8.c:780-787), mirrored into
+//                                the session's cache (held on the host until
+//                                the cache exists).
 // As in the reference, pq1_token_fused declines (returns -1, the caller runs
 // its own path) when it cannot run the step exactly: a shape it does not
 // support, no cache shape announced, or a position that is not the next one
-// its cache holds (the caller ran earlier positions itself). Errors print
-// nothing; pb_last_error keeps the reason.
+// every layer's cache holds (the caller ran earlier positions itself without
+// mirroring their K/V rows). Errors print nothing; pb_last_error keeps the
+// reason.
 #include "pb_internal.h"
 
 #include <cstdio>
@@ -26,9 +32,15 @@
 
 namespace {
 
+struct PendingKV {
+  int il, pos;
+  std::vector<uint16_t> k, v;   // [nkv][128] f16 each
+};
 struct HookSession {
   pb_bonsai_state* st = nullptr;
-  int next = 0;          // the position the cache is ready to take
+  int mc = 0;                       // the cache's positions (ctx rounded up to 32)
+  std::vector<int> next;            // per layer: the position its cache takes next
+  std::vector<PendingKV> pending;   // rows put before the cache existed
 };
 
 struct Hooks {
@@ -48,8 +60,16 @@ struct Hooks {
 };
 Hooks g_h;
 
+// a new weight set: the caches built for the old one go (rows mirrored
+// before any model existed stay, they belong to the first one)
 void drop_model() {
-  for (auto& s : g_h.sess) { pb_bonsai_state_destroy(s.st); s.st = nullptr; s.next = 0; }
+  if (!g_h.m) return;
+  for (auto& s : g_h.sess) {
+    pb_bonsai_state_destroy(s.st);
+    s.st = nullptr;
+    s.next.assign(s.next.size(), 0);
+    s.pending.clear();
+  }
   pb_bonsai_destroy(g_h.m);
   g_h.m = nullptr;
   g_h.key.clear();
@@ -95,6 +115,30 @@ bool ensure_model(int nl, const unsigned char* const* wt, const float* const* nw
   g_h.key = key;
   g_h.hid = hid; g_h.inter = inter; g_h.nh = nh; g_h.vocab = vocab;
   return true;
+}
+
+// one layer's K and V rows of position pos ([n_kv][128] f16 each) into the
+// session's cache ([n_kv][max_ctx][128] per layer, K and V)
+bool put_rows(HookSession& S, int il, int pos, const uint16_t* k16, const uint16_t* v16, cudaStream_t st) {
+  for (int which = 0; which < 2; which++) {
+    void* d = nullptr;
+    if (pb_bonsai_state_kv(S.st, il, which, &d) != PB_OK) return false;
+    uint16_t* dst = static_cast<uint16_t*>(d) + (size_t)pos * 128;
+    if (cudaMemcpy2DAsync(dst, (size_t)S.mc * 128 * 2, which ? v16 : k16, 256, 256, (size_t)g_h.nkv,
+                          cudaMemcpyHostToDevice, st) != cudaSuccess) {
+      cudaGetLastError();
+      pb_set_error(PB_ECUDA, "pq1 hooks: K/V rows");
+      return false;
+    }
+  }
+  return true;
+}
+
+HookSession& session() {
+  if ((int)g_h.sess.size() != g_h.nsess) g_h.sess.resize(g_h.nsess);
+  HookSession& S = g_h.sess[g_h.cur];
+  if ((int)S.next.size() != g_h.nl) S.next.assign(g_h.nl, 0);
+  return S;
 }
 
 }  // namespace
@@ -146,12 +190,17 @@ int pq1_token_fused(int nl, const unsigned char* const* wt, const float* const* 
     return -1;
   g_h.sess_fixed = true;
   if (!ensure_model(nl, wt, nw, nh, nkv, hid, inter, vocab)) return -1;
-  if ((int)g_h.sess.size() != g_h.nsess) g_h.sess.resize(g_h.nsess);
-  HookSession& S = g_h.sess[g_h.cur];
-  if (npos != S.next) return -1;               // the cache lacks earlier positions
+  HookSession& S = session();
+  for (int il = 0; il < nl; il++)
+    if (S.next[il] != npos) return -1;         // a layer's cache lacks earlier positions
   if (!S.st) {
     const int mc = (ctx + 31) / 32 * 32;
     if (mc > 8192 || pb_bonsai_state_create(g_h.m, mc, &S.st) != PB_OK) { S.st = nullptr; return -1; }
+    S.mc = mc;
+    for (const auto& pk : S.pending)
+      if (!put_rows(S, pk.il, pk.pos, pk.k.data(), pk.v.data(), g_h.stream)) return -1;
+    if (cudaStreamSynchronize(g_h.stream) != cudaSuccess) { cudaGetLastError(); return -1; }
+    S.pending.clear();
   }
   if (!g_h.d_x && cudaMalloc(&g_h.d_x, (size_t)8192 * 4) != cudaSuccess) {
     cudaGetLastError();
@@ -166,8 +215,8 @@ int pq1_token_fused(int nl, const unsigned char* const* wt, const float* const* 
   }
   int id = -1;
   if (pb_bonsai_decode(g_h.m, S.st, 0, npos, g_h.d_x, nullptr, &id, st) != PB_OK) return -1;
-  // from here the step has run: the cache holds npos
-  S.next = npos + 1;
+  // from here the step has run: every layer's cache holds npos
+  for (int il = 0; il < nl; il++) S.next[il] = npos + 1;
   const float* lg = pb_bonsai_state_logits(S.st);
   float v = 0.0f;
   if (cudaMemcpyAsync(&v, lg + id, 4, cudaMemcpyDeviceToHost, st) != cudaSuccess ||
@@ -180,6 +229,31 @@ int pq1_token_fused(int nl, const unsigned char* const* wt, const float* const* 
   g_h.top_id = id;
   g_h.top_val = v;
   g_h.top_valid = 1;
+  return 0;
+}
+
+int pq1_attn_kv_put(int il, int nl, int nkv, int ctx, int npos, const uint16_t* k16, const uint16_t* v16) {
+  std::lock_guard<std::mutex> lk(g_h.mu);
+  if (!k16 || !v16 || nl != g_h.nl || nkv != g_h.nkv || ctx != g_h.ctx || il < 0 || il >= nl || npos < 0 ||
+      npos >= ctx)
+    return -1;
+  g_h.sess_fixed = true;
+  HookSession& S = session();
+  if (S.next[il] != npos) return -1;
+  if (S.st) {
+    if (!put_rows(S, il, npos, k16, v16, g_h.stream) || cudaStreamSynchronize(g_h.stream) != cudaSuccess) {
+      cudaGetLastError();
+      return -1;
+    }
+  } else {
+    PendingKV pk;
+    pk.il = il;
+    pk.pos = npos;
+    pk.k.assign(k16, k16 + (size_t)nkv * 128);
+    pk.v.assign(v16, v16 + (size_t)nkv * 128);
+    S.pending.push_back(std::move(pk));
+  }
+  S.next[il] = npos + 1;
   return 0;
 }
 

@@ -2,7 +2,9 @@
 the way fwd8.c drives them (host Q1_0 weights and norms, the token's fp32
 embedding row, the position's rope row), bit for bit against the oracle's
 fwd8 token step: the logits each step writes to the host, pq1_head_top after
-pq1_head_need(0), two interleaved sessions, and the calls that must decline."""
+pq1_head_need(0), two interleaved sessions, the first token run on the host
+with its K/V rows mirrored by pq1_attn_kv_put (fwd8.c's own flow), and the
+calls that must decline."""
 import ctypes as C
 
 import numpy as np
@@ -40,6 +42,8 @@ def test_pq1_token_fused_sessions(oracle, pb, cuda):
     L.pq1_sess_init.argtypes = [i]
     L.pq1_sess_init.restype = i
     L.pq1_sess_select.argtypes = [i]
+    L.pq1_attn_kv_put.argtypes = [i, i, i, i, i, vp, vp]
+    L.pq1_attn_kv_put.restype = i
     O = oracle.lib()
     O.pbo_bs_rope_table.argtypes = [i, C.c_float, i, C.c_float, vp, vp]
     keep = []
@@ -86,7 +90,7 @@ def test_pq1_token_fused_sessions(oracle, pb, cuda):
             tok = int(toks[sess][pos])
             head = np.full(V, np.nan, np.float32)
             rc, x = step(tok, pos, head)
-            assert rc == 0, "session %d position %d declined" % (sess, pos)
+            assert rc == 0, "session %d position %d declined: %s" % (sess, pos, pb.last_error())
             want, lg, _ = oms[sess].decode(tok, pos, x_in=x, want_logits=True)
             if need:
                 assert np.array_equal(_bits(head), _bits(lg)), "session %d position %d" % (sess, pos)
@@ -98,6 +102,17 @@ def test_pq1_token_fused_sessions(oracle, pb, cuda):
             assert L.pq1_head_top(C.byref(v)) == -1      # consumed
             nxt[sess] += 1
 
+    # session 0 as fwd8.c runs a sequence: the first token on the host (here
+    # the oracle), its K/V rows mirrored layer by layer, the fused path after
+    L.pq1_sess_select(0)
+    tok0 = int(toks[0][0])
+    oms[0].decode(tok0, 0, x_in=_embed_row(emb[tok0]))
+    for il in range(nl):
+        k0 = np.ascontiguousarray(oms[0].kv(il, 0)[:, 0, :])
+        v0 = np.ascontiguousarray(oms[0].kv(il, 1)[:, 0, :])
+        assert L.pq1_attn_kv_put(il, nl, NKV, ctx, 1, k0.ctypes.data, v0.ctypes.data) == -1   # not its next position
+        assert L.pq1_attn_kv_put(il, nl, NKV, ctx, 0, k0.ctypes.data, v0.ctypes.data) == 0
+    nxt[0] = 1
     run(0, 6)
     run(1, 4)
     run(0, 3, need=False)
