@@ -71,7 +71,7 @@ int pb_q8_gemm(const pb_q8* w, int T, const uint16_t* d_x, void* d_y, int y_dtyp
  * is. Replaces k_gemv_bf16 / lm_head_bf16, lfm3_nanode.cu:3517-3560. The table
  * is first re-laid (d_src [N][K] row-major bf16 -> d_dst, 16-byte aligned,
  * N*K*2 bytes; K a multiple of 256); pb_bf16_gemv takes the re-laid table,
- * K = 1024, 2048 or 4096. A .lfm3q8 model with a dtype-3 embedding uses the
+ * K = 256, 512, 1024, 2048 or 4096. A .lfm3q8 model with a dtype-3 embedding uses the
  * same head inside every decode path.                                        */
 int pb_bf16_relayout(const uint16_t* d_src, uint16_t* d_dst, int N, int K, void* stream);
 int pb_bf16_gemv(const uint16_t* d_w, int N, int K, const uint16_t* d_x, float* d_y, void* stream);

@@ -310,3 +310,24 @@ WRAP
   } | "$CC" -O3 -fPIC -fopenmp -ffp-contract=off -w $extra -shared -x c -o "$out/libpb_q8cpu_$arm.so" - -lm
   echo "build_ref: built $out/libpb_q8cpu_$arm.so"
 done
+
+# --- H: fwd8.c's GGUF table reader (pulsar_arm/bonsai2/fwd8.c:205-245:
+#        the table statics and gguf_table), unmodified, with a lookup wrapper
+#        written here; tests/test_export.py compares pulsar_b200.gguf's
+#        tensor offsets with it.
+F8="$REF/pulsar_arm/bonsai2/fwd8.c"
+{
+  printf '#include <stdio.h>\n#include <stdint.h>\n#include <stdlib.h>\n#include <string.h>\n#include <fcntl.h>\n#include <sys/mman.h>\n#include <sys/stat.h>\n#include <unistd.h>\n'
+  sed -n '205,245p' "$F8"
+  cat <<'WRAP'
+/* ---- lookup wrapper (this repository's code) ---- */
+int pbref_gguf_offset(const char* path, const char* name, unsigned long long* off) {
+  static char opened[4096];
+  if (strcmp(opened, path)) { gguf_table(path); strncpy(opened, path, sizeof opened - 1); }
+  for (int i = 0; i < NT; i++)
+    if (!strcmp(TN[i], name)) { *off = (unsigned long long)TO[i]; return 0; }
+  return -1;
+}
+WRAP
+} | "$CC" -O2 -fPIC -shared -w -x c -o "$out/libpb_gguf.so" -
+echo "build_ref: built $out/libpb_gguf.so"

@@ -583,6 +583,8 @@ int launch_step(const pb_q8& w, int epi, StepArgs a, cudaStream_t st, bool pdl) 
   if (w.layout == PB_Q8_B16) {
     if (epi != EPI_ARGMAX) return pb_set_error(PB_ENOTSUP, "step: the bf16 table is the head only");
     switch (w.K) {
+      case 256: return launch_step16_t<1>(a, st, pdl);
+      case 512: return launch_step16_t<2>(a, st, pdl);
       case 1024: return launch_step16_t<4>(a, st, pdl);
       case 2048: return launch_step16_t<8>(a, st, pdl);
       case 4096: return launch_step16_t<16>(a, st, pdl);
@@ -710,7 +712,7 @@ int launch_gemv(pb_state* s, const pb_q8& w, int epi, StepArgs a, cudaStream_t s
   pb_q8 part = w;
   part.N = rows;
   part.owner = false;
-  part.codes = w.codes + (size_t)r0 * w.nch * 2048;   // (a bf16 row is nch 2048-byte segments too)
+  part.codes = w.codes + (size_t)r0 * (w.layout == PB_Q8_B16 ? (size_t)w.K * 2 : (size_t)w.nch * 2048);
   if (w.layout != PB_Q8_B16)
     part.scales = static_cast<char*>(w.scales) + (size_t)r0 * w.nch * 32 * (w.sdt == PB_DT_F32 ? 8 : 4);
   size_t elem = 2, per_rank = rows, first = r0;
@@ -1464,7 +1466,7 @@ extern "C" int pb_open(const char* path, int device, pb_model** out) {
     m->head.layout = PB_Q8_B16;
     m->head.codes = reinterpret_cast<int8_t*>(m->head16);
     m->head.scales = nullptr;
-    m->head.nch = H / 1024;
+    m->head.nch = H >= 1024 ? H / 1024 : 1;   // 2048-byte segments per row (the persistent kernel takes H 2048)
   }
   for (auto& fp : fpieces) {
     *fp.dst = reinterpret_cast<float*>(m->arena + cursor);
@@ -2091,6 +2093,14 @@ int launch_b16_head_T(const pb_model* m, const bf16_t* x, float* lg, int T, cuda
   if (grid > (m->V + 7) / 8) grid = (m->V + 7) / 8;
   const uint16_t* w = m->head16;
   switch (m->H) {
+    case 256:
+      PB_TRY_CUDA(cudaFuncSetAttribute(k_b16_head_T<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+      k_b16_head_T<1><<<grid, 256, smem, st>>>(w, x, lg, m->V, T);
+      break;
+    case 512:
+      PB_TRY_CUDA(cudaFuncSetAttribute(k_b16_head_T<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+      k_b16_head_T<2><<<grid, 256, smem, st>>>(w, x, lg, m->V, T);
+      break;
     case 1024:
       PB_TRY_CUDA(cudaFuncSetAttribute(k_b16_head_T<4>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
       k_b16_head_T<4><<<grid, 256, smem, st>>>(w, x, lg, m->V, T);

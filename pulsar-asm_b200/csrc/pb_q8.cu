@@ -654,10 +654,12 @@ extern "C" int pb_bf16_gemv(const uint16_t* d_w, int N, int K, const uint16_t* d
   cudaStream_t st = (cudaStream_t)stream;
   const int grid = (int)std::min<long>((N + 7) / 8, (long)pb_num_sms() * 8);
   switch (K) {
+    case 256: k_b16_gemv<1><<<grid, 256, 0, st>>>(d_w, d_x, d_y, N); break;
+    case 512: k_b16_gemv<2><<<grid, 256, 0, st>>>(d_w, d_x, d_y, N); break;
     case 1024: k_b16_gemv<4><<<grid, 256, 0, st>>>(d_w, d_x, d_y, N); break;
     case 2048: k_b16_gemv<8><<<grid, 256, 0, st>>>(d_w, d_x, d_y, N); break;
     case 4096: k_b16_gemv<16><<<grid, 256, 0, st>>>(d_w, d_x, d_y, N); break;
-    default: return pb_set_error(PB_ENOTSUP, "pb_bf16_gemv: K=%d (1024, 2048 or 4096)", K);
+    default: return pb_set_error(PB_ENOTSUP, "pb_bf16_gemv: K=%d (256, 512, 1024, 2048 or 4096)", K);
   }
   PB_LAUNCHED("k_b16_gemv");
   return PB_OK;
