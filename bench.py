@@ -813,6 +813,17 @@ def main():
             "clocks": clk.summary()}
     if world > 1 and not args.no_tp:
         line["tp_decode"] = tp_bench(torch, pb, model, prompt, stream, rank, world)
+    if world > 1 and not args.no_kernels:
+        # cfg4 over the ranks: each rank decodes its own share of the sequences
+        # (a multiple of 16, the batched step's granule), no data-path
+        # collective; the step time is the maximum over ranks
+        br = max(16, (64 // world + 15) // 16 * 16)
+        b = batch_bench(torch, model, c, stream, B=br)
+        msb = dist.max_over_ranks(b["ms_per_step"], device="cuda")
+        line["cfg4_batched_decode_split"] = {
+            "ranks": world, "sequences_per_rank": br, "sequences": br * world, "steps": b["steps"],
+            "ms_per_step": msb, "tok/s": br * world / (msb / 1e3), "scaling": "sequence split, weak",
+            "path": b["path"]}
     if rank == 0 and world == 1 and not args.no_kernels:
         line["kernels"] = kernel_suite(torch, pb, peak, stream)
         line["kernels"]["cfg2_prefill"] = prefill_bench(torch, model, prompt, stream)
