@@ -17,6 +17,8 @@ whose type number is not vendored here; like fwd8.c, the reader does not rely
 on it: a weight tensor is accepted when its bytes up to the next tensor (or
 the file's end) hold rows x K/128 blocks. Norms are F32 (type 0).
 """
+import mmap
+import os
 import struct
 
 import numpy as np
@@ -34,7 +36,8 @@ class GGUF:
     def __init__(self, path):
         self.path = path
         with open(path, "rb") as f:
-            self.buf = f.read()
+            # mapped, not read: an 8B model's file is over a gigabyte
+            self.buf = mmap.mmap(f.fileno(), 0, access=mmap.ACCESS_READ) if os.fstat(f.fileno()).st_size else b""
         b = self.buf
         if b[:4] != GGUF_MAGIC:
             raise ValueError("%s: not a GGUF file" % path)
