@@ -310,7 +310,20 @@ int pb_bonsai_decode_greedy(pb_bonsai* m, pb_bonsai_state* s, int token, int pos
  * pq1_attn_kv_put: the K / V rows ([nkv][128] f16, post-rope) of layer il at
  * position npos that fwd8 computed on the host (it runs a sequence's first
  * token there), mirrored into the current session's cache; 0, or -1 when npos
- * is not that layer's next position. */
+ * is not that layer's next position.
+ * pq1_attn_fused (layer il's attention block: q|k|v, head norms, rope, the
+ * K/V rows stored at npos in the current session's cache, f16 attention over
+ * positions 0..npos, attn_output; xq is fwd8's host Q8_K of attn_norm(x), ao
+ * the host fp32 output) and pq1_ffn_fused (the FFN tail: gate|up, silu(g)*u,
+ * its Q8_K, down; fo the host output): 0 when the block ran, -1 when it
+ * declines (for attention: no pq1_kv_shape, or npos not the layer's next
+ * position). Tensors are fwd8's host arrays, uploaded on first use and keyed
+ * by pointer (pq1_fwd8_glue.c:1156-1235, :1376-1470). pq1_attn_dbg and
+ * pq1_ffn_dbg_xq return the device's K/V rows, post-rope q and attention
+ * output of the last attention block, and the Q8_K down activation of the
+ * last FFN tail (fwd8's PQ1_ATT_CHECK / PQ1_FFN_CHECK). pb_pq1_hooks_reset
+ * (no reference counterpart) frees every device object the hooks hold and
+ * returns them to their initial state (no shape, one session). */
 void pq1_kv_shape(int nl, int nkv, int ctx);
 int pq1_token_fused(int nl, const unsigned char* const* wt, const float* const* nw, int nh, int nkv, int hid,
                     int inter, int vocab, int ctx, int npos, const float* rcc, const float* rcs, const float* x,
@@ -320,6 +333,14 @@ int pq1_head_top(float* val);
 int pq1_sess_init(int n);
 void pq1_sess_select(int s);
 int pq1_attn_kv_put(int il, int nl, int nkv, int ctx, int npos, const uint16_t* k16, const uint16_t* v16);
+int pq1_attn_fused(int il, const unsigned char* wq, const unsigned char* wk, const unsigned char* wv,
+                   const unsigned char* wo, const float* qnw, const float* knw, int nh, int nkv, int hid, int ctx,
+                   int npos, const float* rcc, const float* rcs, const unsigned char* xq, float* ao);
+int pq1_ffn_fused(const unsigned char* wg, const unsigned char* wu, const unsigned char* wd, int inter, int hid,
+                  const unsigned char* xq, float* fo);
+void pq1_attn_dbg(int il, int npos, uint16_t* k16, uint16_t* v16, float* q, float* atto, int nh);
+void pq1_ffn_dbg_xq(unsigned char* dst, unsigned long n);
+int pb_pq1_hooks_reset(void);
 
 #ifdef __cplusplus
 }

@@ -157,6 +157,7 @@ struct BsPreArgs {
   uint16_t* vc;         // layer's V cache
   int NH, NKV, max_ctx;
   BsCtl* ctl;
+  float* qf;            // optional: post-rope q as fp32 [NH][128] (the per-layer hooks' debug copy)
 };
 // one warp per head: q heads, k heads (rms, rope), then v heads (copied)
 __global__ void __launch_bounds__(32) k_bs_attn_pre(BsPreArgs a) {
@@ -215,6 +216,10 @@ __global__ void __launch_bounds__(32) k_bs_attn_pre(BsPreArgs a) {
     const float c = rc[l + 32 * k], s = rc[64 + l + 32 * k], av = y[k], bv = y[k + 2];
     o[k] = __fmaf_rn(av, c, -__fmul_rn(bv, s));
     o[k + 2] = __fmaf_rn(av, s, __fmul_rn(bv, c));
+  }
+  if (a.qf && hh < a.NH) {
+#pragma unroll
+    for (int k = 0; k < 4; k++) a.qf[(size_t)hh * BS_HD + l + 32 * k] = o[k];
   }
   uint16_t* dst = hh < a.NH ? a.qh + (size_t)hh * BS_HD
                             : a.kc + ((size_t)(hh - a.NH) * a.max_ctx + pos) * BS_HD;
@@ -728,7 +733,8 @@ int bs_record(pb_bonsai* m, pb_bonsai_state* s, cudaStream_t st) {
     }
     if ((rc = pb_q1_gemv_launch(&m->qkv[L], s->xq, s->qkv, nullptr, st, true))) return rc;
     {
-      BsPreArgs a{s->qkv, nw + 2 * H, nw + 2 * H + BS_HD, s->rope, s->qh, kc, vc, NH, NKV, s->max_ctx, s->ctl};
+      BsPreArgs a{s->qkv, nw + 2 * H, nw + 2 * H + BS_HD, s->rope, s->qh, kc, vc, NH, NKV, s->max_ctx, s->ctl,
+                  nullptr};
       if ((rc = bs_launch(k_bs_attn_pre, dim3(NH + 2 * NKV), 32, 0, st, a, "k_bs_attn_pre"))) return rc;
     }
     {
@@ -937,7 +943,8 @@ extern "C" int pb_bonsai_set_norm(pb_bonsai* m, int layer, int slot, const float
   return PB_OK;
 }
 
-extern "C" int pb_bonsai_state_create(pb_bonsai* m, int max_ctx, pb_bonsai_state** out) {
+namespace {
+int bs_state_create(pb_bonsai* m, int max_ctx, uint16_t* kv_ext, pb_bonsai_state** out) {
   if (!m || !out || max_ctx <= 0 || max_ctx % 32) return pb_set_error(PB_EINVAL, "pb_bonsai_state_create: bad argument (max_ctx a positive multiple of 32)");
   *out = nullptr;
   if (pv_smem(max_ctx) > 200 * 1024) return pb_set_error(PB_ENOTSUP, "pb_bonsai_state_create: max_ctx %d too large for the attention kernel (<= 8192)", max_ctx);
@@ -947,7 +954,7 @@ extern "C" int pb_bonsai_state_create(pb_bonsai* m, int max_ctx, pb_bonsai_state
   pb_bonsai_state* s = new pb_bonsai_state();
   s->m = m;
   s->max_ctx = max_ctx;
-  const size_t kvb = (size_t)c.n_layers * 2 * NKV * max_ctx * BS_HD * 2;
+  const size_t kvb = kv_ext ? 0 : (size_t)c.n_layers * 2 * NKV * max_ctx * BS_HD * 2;
   const int kmax = std::max(std::max(H, F), m->QD);
   const size_t sizes[] = {kvb, (size_t)max_ctx * BS_HD * 4, (size_t)H * 4, (size_t)H * 4, (size_t)H * 4,
                           (size_t)(m->QD + 2 * m->KD) * 4, (size_t)NH * BS_HD * 2, (size_t)NH * max_ctx * 4,
@@ -964,6 +971,7 @@ extern "C" int pb_bonsai_state_create(pb_bonsai* m, int max_ctx, pb_bonsai_state
   size_t k = 0;
   auto take = [&]() { char* r = p; p += a256(sizes[k++]); return r; };
   s->kv = reinterpret_cast<uint16_t*>(take());
+  if (kv_ext) s->kv = kv_ext;
   s->rope = reinterpret_cast<float*>(take());
   s->x[0] = reinterpret_cast<float*>(take());
   s->x[1] = reinterpret_cast<float*>(take());
@@ -995,6 +1003,15 @@ extern "C" int pb_bonsai_state_create(pb_bonsai* m, int max_ctx, pb_bonsai_state
   }
   *out = s;
   return PB_OK;
+}
+}  // namespace
+
+extern "C" int pb_bonsai_state_create(pb_bonsai* m, int max_ctx, pb_bonsai_state** out) {
+  return bs_state_create(m, max_ctx, nullptr, out);
+}
+int pb_bonsai_state_create_kv(pb_bonsai* m, int max_ctx, uint16_t* d_kv, pb_bonsai_state** out) {
+  if (!d_kv) return pb_set_error(PB_EINVAL, "pb_bonsai_state_create_kv: null cache");
+  return bs_state_create(m, max_ctx, d_kv, out);
 }
 
 extern "C" int pb_bonsai_state_destroy(pb_bonsai_state* s) {
@@ -1082,5 +1099,193 @@ extern "C" int pb_bonsai_state_status(pb_bonsai_state* s, void* stream) {
 extern "C" int pb_bonsai_state_fallbacks(pb_bonsai_state* s, int* out) {
   if (!s || !out) return pb_set_error(PB_EINVAL, "pb_bonsai_state_fallbacks: null argument");
   PB_TRY_CUDA(cudaMemcpy(out, &s->ctl->fallbacks, sizeof(int), cudaMemcpyDeviceToHost));
+  return PB_OK;
+}
+
+// ====================================================== per-layer blocks
+// The attention block and the FFN tail of one layer as fwd8.c's per-layer
+// hooks run them (pq1_attn_fused / pq1_ffn_fused, pq1_fwd8_shim.h:24-40; the
+// reference's glue: pq1_fwd8_glue.c:1156-1235, :1376-1470): the caller's host
+// Q8_K activation of the normed residual in, the block's fp32 output back to
+// the host. The kernels are the token step's, so every value equals the one
+// the whole-token path computes for that layer.
+struct pb_bs_blocks {
+  int device = 0;
+  // attention: shapes the buffers were sized for
+  int H = 0, NH = 0, NKV = 0, max_ctx = 0;
+  char* amem = nullptr;
+  float *rope = nullptr, *qkv = nullptr, *qf = nullptr, *scores = nullptr, *atto = nullptr, *ao = nullptr;
+  uint16_t* qh = nullptr;
+  uint8_t* xq = nullptr;   // Q8_K of the block input, then of the attention output
+  BsCtl* ctl = nullptr;
+  // FFN tail
+  int fH = 0, F = 0;
+  char* fmem = nullptr;
+  float *gu = nullptr, *fo = nullptr;
+  uint8_t *fxq = nullptr, *dxq = nullptr;   // Q8_K of the input; of silu(g)*u (the down activation)
+};
+
+namespace {
+
+int bs_carve(const size_t* sizes, int n, char** mem, char** parts) {
+  size_t tot = 0;
+  for (int i = 0; i < n; i++) tot += a256(sizes[i]);
+  if (cudaMalloc(mem, tot) != cudaSuccess) {
+    cudaGetLastError();
+    *mem = nullptr;
+    return pb_set_error(PB_ENOMEM, "bonsai blocks: %zu bytes", tot);
+  }
+  if (cudaMemset(*mem, 0, tot) != cudaSuccess) {
+    cudaFree(*mem);
+    *mem = nullptr;
+    return pb_set_error(PB_ECUDA, "bonsai blocks: memset");
+  }
+  char* p = *mem;
+  for (int i = 0; i < n; i++) { parts[i] = p; p += a256(sizes[i]); }
+  return PB_OK;
+}
+
+int bs_blocks_attn_alloc(pb_bs_blocks* b, int H, int NH, int NKV, int max_ctx) {
+  if (b->amem && b->H == H && b->NH == NH && b->NKV == NKV && b->max_ctx == max_ctx) return PB_OK;
+  cudaFree(b->amem);
+  b->amem = nullptr;
+  b->H = 0;
+  const int QD = NH * BS_HD, KD = NKV * BS_HD;
+  const size_t sizes[] = {(size_t)max_ctx * BS_HD * 4, (size_t)(QD + 2 * KD) * 4, (size_t)QD * 4,
+                          (size_t)NH * max_ctx * 4, (size_t)QD * 4, (size_t)H * 4, (size_t)QD * 2,
+                          (size_t)(std::max(H, QD) / 256) * 292, sizeof(BsCtl)};
+  char* parts[9];
+  int rc = bs_carve(sizes, 9, &b->amem, parts);
+  if (rc) return rc;
+  b->rope = reinterpret_cast<float*>(parts[0]);
+  b->qkv = reinterpret_cast<float*>(parts[1]);
+  b->qf = reinterpret_cast<float*>(parts[2]);
+  b->scores = reinterpret_cast<float*>(parts[3]);
+  b->atto = reinterpret_cast<float*>(parts[4]);
+  b->ao = reinterpret_cast<float*>(parts[5]);
+  b->qh = reinterpret_cast<uint16_t*>(parts[6]);
+  b->xq = reinterpret_cast<uint8_t*>(parts[7]);
+  b->ctl = reinterpret_cast<BsCtl*>(parts[8]);
+  b->H = H; b->NH = NH; b->NKV = NKV; b->max_ctx = max_ctx;
+  return PB_OK;
+}
+
+int bs_blocks_ffn_alloc(pb_bs_blocks* b, int H, int F) {
+  if (b->fmem && b->fH == H && b->F == F) return PB_OK;
+  cudaFree(b->fmem);
+  b->fmem = nullptr;
+  b->fH = 0;
+  const size_t sizes[] = {(size_t)2 * F * 4, (size_t)H * 4, (size_t)(H / 256) * 292, (size_t)(F / 256) * 292};
+  char* parts[4];
+  int rc = bs_carve(sizes, 4, &b->fmem, parts);
+  if (rc) return rc;
+  b->gu = reinterpret_cast<float*>(parts[0]);
+  b->fo = reinterpret_cast<float*>(parts[1]);
+  b->fxq = reinterpret_cast<uint8_t*>(parts[2]);
+  b->dxq = reinterpret_cast<uint8_t*>(parts[3]);
+  b->fH = H; b->F = F;
+  return PB_OK;
+}
+
+}  // namespace
+
+int pb_bs_blocks_create(int device, pb_bs_blocks** out) {
+  if (!out) return pb_set_error(PB_EINVAL, "pb_bs_blocks_create: null argument");
+  *out = new pb_bs_blocks();
+  (*out)->device = device;
+  return PB_OK;
+}
+
+void pb_bs_blocks_destroy(pb_bs_blocks* b) {
+  if (!b) return;
+  cudaSetDevice(b->device);
+  cudaFree(b->amem);
+  cudaFree(b->fmem);
+  delete b;
+}
+
+int pb_bs_attn_block(pb_bs_blocks* b, const pb_q1* wq, const pb_q1* wk, const pb_q1* wv, const pb_q1* wo,
+                     const float* d_qn, const float* d_kn, uint16_t* kc, uint16_t* vc, int max_ctx, int npos,
+                     float attn_scale, const float* h_cos, const float* h_sin, const uint8_t* h_xq, float* h_ao,
+                     cudaStream_t st) {
+  if (!b || !wq || !wk || !wv || !wo || !d_qn || !d_kn || !kc || !vc || !h_cos || !h_sin || !h_xq || !h_ao)
+    return pb_set_error(PB_EINVAL, "pb_bs_attn_block: null argument");
+  const int H = wq->K, QD = wq->rows, KD = wk->rows, NH = QD / BS_HD, NKV = KD / BS_HD;
+  if (H % 256 || H > 8192 || QD % 256 || KD % BS_HD || NKV <= 0 || NH % NKV || NH / NKV > 8 || NH > 128 ||
+      wk->K != H || wv->K != H || wv->rows != KD || wo->rows != H || wo->K != QD)
+    return pb_set_error(PB_EINVAL, "pb_bs_attn_block: shapes q %dx%d k %dx%d v %dx%d o %dx%d", wq->rows, wq->K,
+                        wk->rows, wk->K, wv->rows, wv->K, wo->rows, wo->K);
+  if (max_ctx <= 0 || max_ctx % 32 || pv_smem(max_ctx) > 200 * 1024 || npos < 0 || npos >= max_ctx)
+    return pb_set_error(PB_EINVAL, "pb_bs_attn_block: position %d, cache of %d", npos, max_ctx);
+  PB_TRY_CUDA(cudaSetDevice(b->device));
+  int rc;
+  if ((rc = bs_blocks_attn_alloc(b, H, NH, NKV, max_ctx))) return rc;
+  PB_TRY_CUDA(cudaFuncSetAttribute(k_bs_fa_pv, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)pv_smem(max_ctx)));
+  const int hdr[4] = {0, npos, 0, 0};
+  PB_TRY_CUDA(cudaMemcpyAsync(b->ctl, hdr, sizeof hdr, cudaMemcpyHostToDevice, st));
+  PB_TRY_CUDA(cudaMemcpyAsync(b->rope + (size_t)npos * BS_HD, h_cos, 64 * 4, cudaMemcpyHostToDevice, st));
+  PB_TRY_CUDA(cudaMemcpyAsync(b->rope + (size_t)npos * BS_HD + 64, h_sin, 64 * 4, cudaMemcpyHostToDevice, st));
+  PB_TRY_CUDA(cudaMemcpyAsync(b->xq, h_xq, (size_t)(H / 256) * 292, cudaMemcpyHostToDevice, st));
+  // q, k and v into one [NH + 2 NKV][128] vector, as the merged tensor writes it
+  if ((rc = pb_q1_gemv_launch(wq, b->xq, b->qkv, nullptr, st, true))) return rc;
+  if ((rc = pb_q1_gemv_launch(wk, b->xq, b->qkv + QD, nullptr, st, true))) return rc;
+  if ((rc = pb_q1_gemv_launch(wv, b->xq, b->qkv + QD + KD, nullptr, st, true))) return rc;
+  {
+    BsPreArgs a{b->qkv, d_qn, d_kn, b->rope, b->qh, kc, vc, NH, NKV, max_ctx, b->ctl, b->qf};
+    if ((rc = bs_launch(k_bs_attn_pre, dim3(NH + 2 * NKV), 32, 0, st, a, "k_bs_attn_pre"))) return rc;
+  }
+  {
+    BsQkArgs a{b->qh, kc, b->scores, NH, NKV, max_ctx, attn_scale, b->ctl};
+    if ((rc = bs_launch(k_bs_fa_qk, dim3(max_ctx / 32, NKV), 32 * (NH / NKV), 0, st, a, "k_bs_fa_qk"))) return rc;
+  }
+  {
+    BsPvArgs a{b->scores, vc, b->atto, b->xq, NH, NKV, max_ctx, b->ctl};
+    if ((rc = bs_launch(k_bs_fa_pv, dim3(NH), 256, pv_smem(max_ctx), st, a, "k_bs_fa_pv"))) return rc;
+  }
+  if ((rc = pb_q1_gemv_launch(wo, b->xq, b->ao, nullptr, st, true))) return rc;
+  int err = 0;
+  PB_TRY_CUDA(cudaMemcpyAsync(h_ao, b->ao, (size_t)H * 4, cudaMemcpyDeviceToHost, st));
+  PB_TRY_CUDA(cudaMemcpyAsync(&err, &b->ctl->err, sizeof(int), cudaMemcpyDeviceToHost, st));
+  PB_TRY_CUDA(cudaStreamSynchronize(st));
+  if (err) return pb_set_error(PB_ECUDA, "pb_bs_attn_block: a bounded wait in the attention kernel gave up");
+  return PB_OK;
+}
+
+int pb_bs_ffn_block(pb_bs_blocks* b, const pb_q1* wg, const pb_q1* wu, const pb_q1* wd, const uint8_t* h_xq,
+                    float* h_fo, cudaStream_t st) {
+  if (!b || !wg || !wu || !wd || !h_xq || !h_fo) return pb_set_error(PB_EINVAL, "pb_bs_ffn_block: null argument");
+  const int H = wg->K, F = wg->rows;
+  if (H % 256 || F % 256 || wu->K != H || wu->rows != F || wd->K != F || wd->rows != H)
+    return pb_set_error(PB_EINVAL, "pb_bs_ffn_block: shapes gate %dx%d up %dx%d down %dx%d", wg->rows, wg->K,
+                        wu->rows, wu->K, wd->rows, wd->K);
+  PB_TRY_CUDA(cudaSetDevice(b->device));
+  int rc;
+  if ((rc = bs_blocks_ffn_alloc(b, H, F))) return rc;
+  PB_TRY_CUDA(cudaMemcpyAsync(b->fxq, h_xq, (size_t)(H / 256) * 292, cudaMemcpyHostToDevice, st));
+  if ((rc = pb_q1_gemv_launch(wg, b->fxq, b->gu, nullptr, st, true))) return rc;
+  if ((rc = pb_q1_gemv_launch(wu, b->fxq, b->gu + F, nullptr, st, true))) return rc;
+  {
+    BsSiluArgs a{b->gu, b->dxq, F};
+    if ((rc = bs_launch(k_bs_silu_q8k, dim3(F / 256), 256, 0, st, a, "k_bs_silu_q8k"))) return rc;
+  }
+  if ((rc = pb_q1_gemv_launch(wd, b->dxq, b->fo, nullptr, st, true))) return rc;
+  PB_TRY_CUDA(cudaMemcpyAsync(h_fo, b->fo, (size_t)H * 4, cudaMemcpyDeviceToHost, st));
+  PB_TRY_CUDA(cudaStreamSynchronize(st));
+  return PB_OK;
+}
+
+int pb_bs_blocks_attn_debug(pb_bs_blocks* b, float* h_q, float* h_atto, int nh) {
+  if (!b || !b->amem || nh != b->NH) return pb_set_error(PB_EINVAL, "pb_bs_blocks_attn_debug: no attention block ran");
+  PB_TRY_CUDA(cudaSetDevice(b->device));
+  if (h_q) PB_TRY_CUDA(cudaMemcpy(h_q, b->qf, (size_t)nh * BS_HD * 4, cudaMemcpyDeviceToHost));
+  if (h_atto) PB_TRY_CUDA(cudaMemcpy(h_atto, b->atto, (size_t)nh * BS_HD * 4, cudaMemcpyDeviceToHost));
+  return PB_OK;
+}
+
+int pb_bs_blocks_ffn_xq(pb_bs_blocks* b, uint8_t* h_dst, size_t n) {
+  if (!b || !b->fmem || !h_dst) return pb_set_error(PB_EINVAL, "pb_bs_blocks_ffn_xq: no FFN block ran");
+  PB_TRY_CUDA(cudaSetDevice(b->device));
+  const size_t have = (size_t)(b->F / 256) * 292;
+  PB_TRY_CUDA(cudaMemcpy(h_dst, b->dxq, n < have ? n : have, cudaMemcpyDeviceToHost));
   return PB_OK;
 }

@@ -92,6 +92,25 @@ int pb_q8_pack_into(pb_q8* w, const int8_t* d_codes, const void* d_scales, cudaS
 int pb_bonsai_state_set_rope_row(pb_bonsai_state* s, int pos, const float* h_cos, const float* h_sin,
                                  cudaStream_t st);
 const float* pb_bonsai_state_logits(const pb_bonsai_state* s);
+// a state over a K/V cache the caller owns ([layer][2][n_kv][max_ctx][128]
+// f16, not freed with the state)
+int pb_bonsai_state_create_kv(pb_bonsai* m, int max_ctx, uint16_t* d_kv, pb_bonsai_state** out);
+
+// one layer's attention block / FFN tail from the caller's host Q8_K
+// activation, for fwd8.c's per-layer hooks (pb_bonsai.cu); blocking
+struct pb_bs_blocks;
+int pb_bs_blocks_create(int device, pb_bs_blocks** out);
+void pb_bs_blocks_destroy(pb_bs_blocks* b);
+int pb_bs_attn_block(pb_bs_blocks* b, const pb_q1* wq, const pb_q1* wk, const pb_q1* wv, const pb_q1* wo,
+                     const float* d_qn, const float* d_kn, uint16_t* kc, uint16_t* vc, int max_ctx, int npos,
+                     float attn_scale, const float* h_cos, const float* h_sin, const uint8_t* h_xq, float* h_ao,
+                     cudaStream_t st);
+int pb_bs_ffn_block(pb_bs_blocks* b, const pb_q1* wg, const pb_q1* wu, const pb_q1* wd, const uint8_t* h_xq,
+                    float* h_fo, cudaStream_t st);
+// the last attention block's post-rope q and attention output (fp32 [nh][128]);
+// the last FFN tail's down activation (Q8_K blocks, at most n bytes)
+int pb_bs_blocks_attn_debug(pb_bs_blocks* b, float* h_q, float* h_atto, int nh);
+int pb_bs_blocks_ffn_xq(pb_bs_blocks* b, uint8_t* h_dst, size_t n);
 
 // the bf16 tied table (blob dtype 3) re-laid for the head GEMV (pb_q8.cu)
 int pb_b16_pack(const uint16_t* d_src, uint16_t* d_dst, int N, int K, cudaStream_t st);

@@ -1,8 +1,9 @@
 // pb_pq1hooks.cpp -- the Bonsai host hooks fwd8.c calls through
 // pulsar_arm/bonsai2/pq1_fwd8_shim.h:24-60 (implemented by the reference in
-// pq1_fwd8_glue.c:235-246, :1483-1760), here over this library's Bonsai
+// pq1_fwd8_glue.c:1156-1470, :1483-1760), here over this library's Bonsai
 // decoder (pb_bonsai_*). A fwd8.c built with that shim and linked against this
-// library runs every token on the B200 in one call:
+// library runs every token on the B200 in one call, or a layer's attention
+// block and FFN tail in one call each:
 //   pq1_kv_shape(nl, nkv, ctx)   the K/V cache shape, before the first call;
 //   pq1_sess_init(n) / pq1_sess_select(s)   n time-sliced sessions, each with
 //                                its own K/V cache and position, one model;
@@ -12,35 +13,51 @@
 //                                this position's rope row; logits written to
 //                                the host unless pq1_head_need(0);
 //   pq1_head_top(&val)           the device argmax of the last token, or -1;
+//   pq1_attn_fused(il, ...)      layer il's attention block from the host Q8_K
+//                                of attn_norm(x): q|k|v, head norms, rope, the
+//                                K/V rows stored at npos in the session's
+//                                cache, attention, attn_output -> ao (host);
+//   pq1_ffn_fused(...)           the FFN tail from the host Q8_K of
+//                                ffn_norm(x): gate|up, silu(g)*u, its Q8_K,
+//                                down -> fo (host);
 //   pq1_attn_kv_put(il, ...)     a layer's K/V rows of a position fwd8 ran on
 //                                the host (it always runs a sequence's first
 //                                token there, fwd8.c:780-787), mirrored into
-//                                the session's cache (held on the host until
-//                                the cache exists).
-// As in the reference, pq1_token_fused declines (returns -1, the caller runs
-// its own path) when it cannot run the step exactly: a shape it does not
-// support, no cache shape announced, or a position that is not the next one
-// every layer's cache holds (the caller ran earlier positions itself without
-// mirroring their K/V rows). Errors print nothing; pb_last_error keeps the
-// reason.
+//                                the session's cache;
+//   pq1_attn_dbg / pq1_ffn_dbg_xq   the device's values of the last block for
+//                                fwd8's PQ1_ATT_CHECK / PQ1_FFN_CHECK.
+// Per-layer tensors are keyed by their host pointers, as the reference's glue
+// keys them; the whole-token path keeps its own copy of the weight set. A
+// session's K/V cache belongs to the session, so the per-layer hooks, the
+// mirrored rows and the whole-token path all continue one cache.
+// As in the reference, a hook declines (returns -1, the caller runs its own
+// path) when it cannot run the step exactly: a shape it does not support, no
+// cache shape announced, or a position that is not the next one the layer's
+// cache holds (the caller ran earlier positions itself without mirroring
+// their K/V rows). Errors print nothing; pb_last_error keeps the reason.
 #include "pb_internal.h"
 
 #include <cstdio>
 #include <cstring>
+#include <map>
 #include <mutex>
 #include <vector>
 
 namespace {
 
-struct PendingKV {
-  int il, pos;
-  std::vector<uint16_t> k, v;   // [nkv][128] f16 each
-};
+// fwd8.c:566: the attention scale 1/sqrt(128)
+constexpr float kAttnScale = 0.0883883476f;
+
 struct HookSession {
-  pb_bonsai_state* st = nullptr;
-  int mc = 0;                       // the cache's positions (ctx rounded up to 32)
-  std::vector<int> next;            // per layer: the position its cache takes next
-  std::vector<PendingKV> pending;   // rows put before the cache existed
+  pb_bonsai_state* st = nullptr;   // the whole-token path's state, over kv
+  uint16_t* kv = nullptr;          // [nl][2][nkv][mc][128] f16
+  int nl = 0, nkv = 0, mc = 0;     // the cache's shape
+  std::vector<int> next;           // per layer: the position its cache takes next
+};
+
+struct Q1Entry {
+  pb_q1* t = nullptr;
+  int rows = 0, K = 0;
 };
 
 struct Hooks {
@@ -57,18 +74,35 @@ struct Hooks {
   std::vector<HookSession> sess;
   float* d_x = nullptr;                  // the caller's row on the device
   cudaStream_t stream = nullptr;
+  // per-layer hooks: device copies of host tensors and head-norm weights
+  std::map<const void*, Q1Entry> q1;
+  std::map<const void*, float*> hnorm;
+  pb_bs_blocks* blk = nullptr;
 };
 Hooks g_h;
 
-// a new weight set: the caches built for the old one go (rows mirrored
-// before any model existed stay, they belong to the first one)
+int cache_len(int ctx) { return (ctx + 31) / 32 * 32; }
+
+bool ensure_stream() {
+  if (g_h.stream) return true;
+  if (cudaStreamCreateWithFlags(&g_h.stream, cudaStreamNonBlocking) != cudaSuccess) {
+    cudaGetLastError();
+    g_h.stream = nullptr;
+    pb_set_error(PB_ECUDA, "pq1 hooks: stream");
+    return false;
+  }
+  return true;
+}
+
+// a new weight set: the whole-token states built for the old one go and every
+// cache starts again from position 0. Rows mirrored or computed before the
+// first model existed stay: they belong to it.
 void drop_model() {
   if (!g_h.m) return;
   for (auto& s : g_h.sess) {
     pb_bonsai_state_destroy(s.st);
     s.st = nullptr;
     s.next.assign(s.next.size(), 0);
-    s.pending.clear();
   }
   pb_bonsai_destroy(g_h.m);
   g_h.m = nullptr;
@@ -85,15 +119,11 @@ bool ensure_model(int nl, const unsigned char* const* wt, const float* const* nw
   if (g_h.m && key == g_h.key && hid == g_h.hid && inter == g_h.inter && nh == g_h.nh && vocab == g_h.vocab)
     return true;
   drop_model();
-  if (!g_h.stream && cudaStreamCreateWithFlags(&g_h.stream, cudaStreamNonBlocking) != cudaSuccess) {
-    cudaGetLastError();
-    pb_set_error(PB_ECUDA, "pq1 hooks: stream");
-    return false;
-  }
+  if (!ensure_stream()) return false;
   // fwd8.c's Bonsai-8B constants: YaRN factor 4 over 16384 positions, base
   // 1e6 (fwd8.c:51-57; the table itself comes from the caller per call), and
-  // attention scale 1/sqrt(128) (fwd8.c:566)
-  pb_bonsai_cfg c = {hid, inter, nl, nh, nkv, vocab, 4.0f, 16384, 1e6f, 0.0883883476f};
+  // the attention scale
+  pb_bonsai_cfg c = {hid, inter, nl, nh, nkv, vocab, 4.0f, 16384, 1e6f, kAttnScale};
   int dev = 0;
   cudaGetDevice(&dev);
   if (pb_bonsai_create(&c, dev, &g_h.m) != PB_OK) { g_h.m = nullptr; return false; }
@@ -117,14 +147,49 @@ bool ensure_model(int nl, const unsigned char* const* wt, const float* const* nw
   return true;
 }
 
+HookSession& session() {
+  if ((int)g_h.sess.size() != g_h.nsess) g_h.sess.resize(g_h.nsess);
+  HookSession& S = g_h.sess[g_h.cur];
+  if ((int)S.next.size() != g_h.nl) S.next.assign(g_h.nl, 0);
+  return S;
+}
+
+// the session's K/V cache for the announced shape; false: decline (the
+// shape changed after the cache was made, or is too long for the attention
+// kernel)
+bool ensure_kv(HookSession& S) {
+  const int mc = cache_len(g_h.ctx);
+  if (S.kv) {
+    if (S.nl == g_h.nl && S.nkv == g_h.nkv && S.mc == mc) return true;
+    pb_set_error(PB_EINVAL, "pq1 hooks: the cache shape changed after the cache was made");
+    return false;
+  }
+  if (g_h.nl <= 0 || g_h.nkv <= 0 || mc <= 0 || mc > 8192) {
+    pb_set_error(PB_EINVAL, "pq1 hooks: cache shape %d x %d x %d", g_h.nl, g_h.nkv, g_h.ctx);
+    return false;
+  }
+  const size_t bytes = (size_t)g_h.nl * 2 * g_h.nkv * mc * 128 * 2;
+  if (cudaMalloc(&S.kv, bytes) != cudaSuccess || cudaMemset(S.kv, 0, bytes) != cudaSuccess) {
+    cudaGetLastError();
+    if (S.kv) cudaFree(S.kv);
+    S.kv = nullptr;
+    pb_set_error(PB_ENOMEM, "pq1 hooks: K/V cache of %zu bytes", bytes);
+    return false;
+  }
+  S.nl = g_h.nl; S.nkv = g_h.nkv; S.mc = mc;
+  return true;
+}
+
+uint16_t* kv_layer(HookSession& S, int il, int which) {
+  return S.kv + ((size_t)il * 2 + which) * S.nkv * S.mc * 128;
+}
+
 // one layer's K and V rows of position pos ([n_kv][128] f16 each) into the
-// session's cache ([n_kv][max_ctx][128] per layer, K and V)
+// session's cache ([n_kv][mc][128] per layer, K and V)
 bool put_rows(HookSession& S, int il, int pos, const uint16_t* k16, const uint16_t* v16, cudaStream_t st) {
   for (int which = 0; which < 2; which++) {
-    void* d = nullptr;
-    if (pb_bonsai_state_kv(S.st, il, which, &d) != PB_OK) return false;
-    uint16_t* dst = static_cast<uint16_t*>(d) + (size_t)pos * 128;
-    if (cudaMemcpy2DAsync(dst, (size_t)S.mc * 128 * 2, which ? v16 : k16, 256, 256, (size_t)g_h.nkv,
+    uint16_t* dst = kv_layer(S, il, which) + (size_t)pos * 128;
+    if (cudaMemcpy2DAsync(dst, (size_t)S.mc * 128 * 2, which ? v16 : k16, 256, 256, (size_t)S.nkv,
                           cudaMemcpyHostToDevice, st) != cudaSuccess) {
       cudaGetLastError();
       pb_set_error(PB_ECUDA, "pq1 hooks: K/V rows");
@@ -134,11 +199,54 @@ bool put_rows(HookSession& S, int il, int pos, const uint16_t* k16, const uint16
   return true;
 }
 
-HookSession& session() {
-  if ((int)g_h.sess.size() != g_h.nsess) g_h.sess.resize(g_h.nsess);
-  HookSession& S = g_h.sess[g_h.cur];
-  if ((int)S.next.size() != g_h.nl) S.next.assign(g_h.nl, 0);
-  return S;
+// the device copy of a host Q1_0 tensor [rows][K/128 blocks], made on first use
+const pb_q1* q1_of(const void* w, int rows, int K) {
+  auto it = g_h.q1.find(w);
+  if (it != g_h.q1.end()) {
+    if (it->second.rows == rows && it->second.K == K) return it->second.t;
+    pb_q1_free(it->second.t);
+    g_h.q1.erase(it);
+  }
+  Q1Entry e;
+  if (pb_q1_pack(static_cast<const uint8_t*>(w), rows, K, 0, g_h.stream, &e.t) != PB_OK) return nullptr;
+  if (cudaStreamSynchronize(g_h.stream) != cudaSuccess) {
+    cudaGetLastError();
+    pb_q1_free(e.t);
+    pb_set_error(PB_ECUDA, "pq1 hooks: tensor upload");
+    return nullptr;
+  }
+  e.rows = rows;
+  e.K = K;
+  g_h.q1[w] = e;
+  return e.t;
+}
+
+// the device copy of a head-norm weight (128 floats)
+const float* hnorm_of(const float* w) {
+  auto it = g_h.hnorm.find(w);
+  if (it != g_h.hnorm.end()) return it->second;
+  float* d = nullptr;
+  if (cudaMalloc(&d, 128 * 4) != cudaSuccess || cudaMemcpy(d, w, 128 * 4, cudaMemcpyHostToDevice) != cudaSuccess) {
+    cudaGetLastError();
+    if (d) cudaFree(d);
+    pb_set_error(PB_ECUDA, "pq1 hooks: head-norm weights");
+    return nullptr;
+  }
+  g_h.hnorm[w] = d;
+  return d;
+}
+
+bool ensure_blocks() {
+  if (g_h.blk) return true;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  return pb_bs_blocks_create(dev, &g_h.blk) == PB_OK;
+}
+
+// shapes the device decoder takes (pb_bonsai_create's limits)
+bool shape_ok(int nh, int nkv, int hid) {
+  return hid > 0 && hid % 256 == 0 && hid <= 8192 && nh > 0 && nh <= 128 && nh % 2 == 0 && nkv > 0 &&
+         nh % nkv == 0 && nh / nkv <= 8;
 }
 
 }  // namespace
@@ -185,23 +293,14 @@ int pq1_token_fused(int nl, const unsigned char* const* wt, const float* const* 
   g_h.top_valid = 0;
   if (!wt || !nw || !rcc || !rcs || !x) return -1;
   if (nl != g_h.nl || nkv != g_h.nkv || ctx != g_h.ctx || npos < 0 || npos >= ctx) return -1;
-  if ((hid & 255) || hid > 8192 || (inter & 255) || nh <= 0 || nh > 128 || (nh & 1) || nkv <= 0 || nh % nkv ||
-      nh / nkv > 8 || vocab <= 0)
-    return -1;
+  if (!shape_ok(nh, nkv, hid) || (inter & 255) || inter <= 0 || vocab <= 0) return -1;
   g_h.sess_fixed = true;
   if (!ensure_model(nl, wt, nw, nh, nkv, hid, inter, vocab)) return -1;
   HookSession& S = session();
   for (int il = 0; il < nl; il++)
     if (S.next[il] != npos) return -1;         // a layer's cache lacks earlier positions
-  if (!S.st) {
-    const int mc = (ctx + 31) / 32 * 32;
-    if (mc > 8192 || pb_bonsai_state_create(g_h.m, mc, &S.st) != PB_OK) { S.st = nullptr; return -1; }
-    S.mc = mc;
-    for (const auto& pk : S.pending)
-      if (!put_rows(S, pk.il, pk.pos, pk.k.data(), pk.v.data(), g_h.stream)) return -1;
-    if (cudaStreamSynchronize(g_h.stream) != cudaSuccess) { cudaGetLastError(); return -1; }
-    S.pending.clear();
-  }
+  if (!ensure_kv(S)) return -1;
+  if (!S.st && pb_bonsai_state_create_kv(g_h.m, S.mc, S.kv, &S.st) != PB_OK) { S.st = nullptr; return -1; }
   if (!g_h.d_x && cudaMalloc(&g_h.d_x, (size_t)8192 * 4) != cudaSuccess) {
     cudaGetLastError();
     g_h.d_x = nullptr;
@@ -240,21 +339,103 @@ int pq1_attn_kv_put(int il, int nl, int nkv, int ctx, int npos, const uint16_t* 
   g_h.sess_fixed = true;
   HookSession& S = session();
   if (S.next[il] != npos) return -1;
-  if (S.st) {
-    if (!put_rows(S, il, npos, k16, v16, g_h.stream) || cudaStreamSynchronize(g_h.stream) != cudaSuccess) {
-      cudaGetLastError();
-      return -1;
-    }
-  } else {
-    PendingKV pk;
-    pk.il = il;
-    pk.pos = npos;
-    pk.k.assign(k16, k16 + (size_t)nkv * 128);
-    pk.v.assign(v16, v16 + (size_t)nkv * 128);
-    S.pending.push_back(std::move(pk));
+  if (!ensure_stream() || !ensure_kv(S)) return -1;
+  if (!put_rows(S, il, npos, k16, v16, g_h.stream) || cudaStreamSynchronize(g_h.stream) != cudaSuccess) {
+    cudaGetLastError();
+    return -1;
   }
   S.next[il] = npos + 1;
   return 0;
+}
+
+int pq1_attn_fused(int il, const unsigned char* wq, const unsigned char* wk, const unsigned char* wv,
+                   const unsigned char* wo, const float* qnw, const float* knw, int nh, int nkv, int hid, int ctx,
+                   int npos, const float* rcc, const float* rcs, const unsigned char* xq, float* ao) {
+  std::lock_guard<std::mutex> lk(g_h.mu);
+  if (!wq || !wk || !wv || !wo || !qnw || !knw || !rcc || !rcs || !xq || !ao) return -1;
+  if (g_h.nl <= 0 || nkv != g_h.nkv || ctx != g_h.ctx || il < 0 || il >= g_h.nl || npos < 0 || npos >= ctx)
+    return -1;
+  if (!shape_ok(nh, nkv, hid)) return -1;
+  g_h.sess_fixed = true;
+  HookSession& S = session();
+  if (S.next[il] != npos) return -1;
+  if (!ensure_stream() || !ensure_kv(S) || !ensure_blocks()) return -1;
+  const pb_q1* tq = q1_of(wq, nh * 128, hid);
+  const pb_q1* tk = tq ? q1_of(wk, nkv * 128, hid) : nullptr;
+  const pb_q1* tv = tk ? q1_of(wv, nkv * 128, hid) : nullptr;
+  const pb_q1* to = tv ? q1_of(wo, hid, nh * 128) : nullptr;
+  const float* dq = to ? hnorm_of(qnw) : nullptr;
+  const float* dk = dq ? hnorm_of(knw) : nullptr;
+  if (!dk) return -1;
+  if (pb_bs_attn_block(g_h.blk, tq, tk, tv, to, dq, dk, kv_layer(S, il, 0), kv_layer(S, il, 1), S.mc, npos,
+                       kAttnScale, rcc, rcs, xq, ao, g_h.stream) != PB_OK) {
+    cudaGetLastError();
+    return -1;
+  }
+  S.next[il] = npos + 1;
+  return 0;
+}
+
+int pq1_ffn_fused(const unsigned char* wg, const unsigned char* wu, const unsigned char* wd, int inter, int hid,
+                  const unsigned char* xq, float* fo) {
+  std::lock_guard<std::mutex> lk(g_h.mu);
+  if (!wg || !wu || !wd || !xq || !fo) return -1;
+  if (hid <= 0 || hid % 256 || hid > 8192 || inter <= 0 || inter % 256) return -1;
+  if (!ensure_stream() || !ensure_blocks()) return -1;
+  const pb_q1* tg = q1_of(wg, inter, hid);
+  const pb_q1* tu = tg ? q1_of(wu, inter, hid) : nullptr;
+  const pb_q1* td = tu ? q1_of(wd, hid, inter) : nullptr;
+  if (!td) return -1;
+  if (pb_bs_ffn_block(g_h.blk, tg, tu, td, xq, fo, g_h.stream) != PB_OK) {
+    cudaGetLastError();
+    return -1;
+  }
+  return 0;
+}
+
+void pq1_ffn_dbg_xq(unsigned char* dst, unsigned long n) {
+  std::lock_guard<std::mutex> lk(g_h.mu);
+  if (g_h.blk && dst) pb_bs_blocks_ffn_xq(g_h.blk, dst, (size_t)n);
+}
+
+void pq1_attn_dbg(int il, int npos, uint16_t* k16, uint16_t* v16, float* q, float* atto, int nh) {
+  std::lock_guard<std::mutex> lk(g_h.mu);
+  if (g_h.sess.empty() || g_h.cur >= (int)g_h.sess.size()) return;
+  HookSession& S = g_h.sess[g_h.cur];
+  if (!S.kv || il < 0 || il >= S.nl || npos < 0 || npos >= S.mc) return;
+  const size_t pitch = (size_t)S.mc * 128 * 2;
+  if (k16) cudaMemcpy2D(k16, 256, kv_layer(S, il, 0) + (size_t)npos * 128, pitch, 256, S.nkv, cudaMemcpyDeviceToHost);
+  if (v16) cudaMemcpy2D(v16, 256, kv_layer(S, il, 1) + (size_t)npos * 128, pitch, 256, S.nkv, cudaMemcpyDeviceToHost);
+  if (g_h.blk && (q || atto)) pb_bs_blocks_attn_debug(g_h.blk, q, atto, nh);
+  cudaGetLastError();
+}
+
+int pb_pq1_hooks_reset(void) {
+  std::lock_guard<std::mutex> lk(g_h.mu);
+  drop_model();
+  for (auto& s : g_h.sess) {
+    pb_bonsai_state_destroy(s.st);
+    if (s.kv) cudaFree(s.kv);
+  }
+  g_h.sess.clear();
+  for (auto& e : g_h.q1) pb_q1_free(e.second.t);
+  g_h.q1.clear();
+  for (auto& e : g_h.hnorm) cudaFree(e.second);
+  g_h.hnorm.clear();
+  pb_bs_blocks_destroy(g_h.blk);
+  g_h.blk = nullptr;
+  if (g_h.d_x) cudaFree(g_h.d_x);
+  g_h.d_x = nullptr;
+  if (g_h.stream) cudaStreamDestroy(g_h.stream);
+  g_h.stream = nullptr;
+  g_h.nl = g_h.nkv = g_h.ctx = 0;
+  g_h.nsess = 1;
+  g_h.cur = 0;
+  g_h.sess_fixed = false;
+  g_h.head_need = true;
+  g_h.top_valid = 0;
+  g_h.top_id = -1;
+  return PB_OK;
 }
 
 }  // extern "C"
