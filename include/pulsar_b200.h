@@ -341,6 +341,12 @@ int pq1_ffn_fused(const unsigned char* wg, const unsigned char* wu, const unsign
 void pq1_attn_dbg(int il, int npos, uint16_t* k16, uint16_t* v16, float* q, float* atto, int nh);
 void pq1_ffn_dbg_xq(unsigned char* dst, unsigned long n);
 int pb_pq1_hooks_reset(void);
+/* the shim's host helpers (pq1_fwd8_shim.h:21-22, :64): silu(g)*u in place
+ * on the host, lu[i] = (g * (1/(1+expf(-g)))) * lu[i] with the C library's
+ * expf, every operation rounded (pq1_host.c:196-227); and the GPU memory
+ * report fwd8 prints under PQ1_STATS=1 */
+void pq1_silu_mul(float* lu, const float* lg, int n);
+const char* pq1_gpu_stats_mb(char* buf, int n);
 
 #ifdef __cplusplus
 }

@@ -25,7 +25,8 @@
 //                                token there, fwd8.c:780-787), mirrored into
 //                                the session's cache;
 //   pq1_attn_dbg / pq1_ffn_dbg_xq   the device's values of the last block for
-//                                fwd8's PQ1_ATT_CHECK / PQ1_FFN_CHECK.
+//                                fwd8's PQ1_ATT_CHECK / PQ1_FFN_CHECK;
+//   pq1_silu_mul, pq1_gpu_stats_mb   the shim's two host helpers.
 // Per-layer tensors are keyed by their host pointers, as the reference's glue
 // keys them; the whole-token path keeps its own copy of the weight set. A
 // session's K/V cache belongs to the session, so the per-layer hooks, the
@@ -37,6 +38,7 @@
 // their K/V rows). Errors print nothing; pb_last_error keeps the reason.
 #include "pb_internal.h"
 
+#include <cmath>
 #include <cstdio>
 #include <cstring>
 #include <map>
@@ -408,6 +410,36 @@ void pq1_attn_dbg(int il, int npos, uint16_t* k16, uint16_t* v16, float* q, floa
   if (v16) cudaMemcpy2D(v16, 256, kv_layer(S, il, 1) + (size_t)npos * 128, pitch, 256, S.nkv, cudaMemcpyDeviceToHost);
   if (g_h.blk && (q || atto)) pb_bs_blocks_attn_debug(g_h.blk, q, atto, nh);
   cudaGetLastError();
+}
+
+// pq1_host.c:196-227: lu[i] = (g * (1 / (1 + expf(-g)))) * lu[i], the host
+// helper fwd8.c calls when its FFN tail runs on the host. expf is the host
+// C library's (glibc's expf on the reference's targets); the operations are
+// rounded one by one, as the reference's -ffp-contract=off build does.
+__attribute__((optimize("fp-contract=off"))) void pq1_silu_mul(float* lu, const float* lg, int n) {
+  for (int i = 0; i < n; i++) {
+    const float g = lg[i];
+    const float e = expf(-g);
+    const float d = 1.0f + e;
+    const float sg = 1.0f / d;
+    const float gs = g * sg;
+    lu[i] = gs * lu[i];
+  }
+}
+
+// the GPU memory report fwd8.c prints at exit under PQ1_STATS=1
+// (pq1_fwd8_shim.h:64-77): device memory in use and total, in MB
+const char* pq1_gpu_stats_mb(char* buf, int n) {
+  if (!buf || n <= 0) return buf;
+  size_t fr = 0, tot = 0;
+  if (cudaMemGetInfo(&fr, &tot) != cudaSuccess) {
+    cudaGetLastError();
+    snprintf(buf, (size_t)n, "pq1: GPU memory unavailable");
+    return buf;
+  }
+  snprintf(buf, (size_t)n, "pq1: GPU memory %.1f MB used of %.1f MB", (double)(tot - fr) / 1048576.0,
+           (double)tot / 1048576.0);
+  return buf;
 }
 
 int pb_pq1_hooks_reset(void) {

@@ -105,3 +105,23 @@ def test_misshapen_tensor_is_format_error(pb, tmp_path):
     path = str(tmp_path / "m.lfm3q8")
     synth.write_model(path, c, w)
     assert _open_validate(pb, path) == -6
+
+
+def test_shim_host_silu_mul(pb):
+    """pq1_silu_mul (the shim's host helper, pq1_host.c:196-227) runs without a
+    GPU: lu = (g * (1/(1+expf(-g)))) * lu, each operation rounded to fp32, with
+    the C library's expf, on edge values (0, -0, large magnitudes, subnormal)"""
+    L = pb.lib()
+    L.pq1_silu_mul.argtypes = [C.c_void_p, C.c_void_p, C.c_int]
+    libm = C.CDLL("libm.so.6")
+    libm.expf.argtypes = [C.c_float]
+    libm.expf.restype = C.c_float
+    rng = np.random.default_rng(5)
+    g = np.concatenate([rng.standard_normal(4093).astype(np.float32) * 6,
+                        np.array([0.0, -0.0, 88.0, -88.0, 103.0, -103.0, 1e-40], np.float32)])
+    u = rng.standard_normal(g.size).astype(np.float32)
+    out = u.copy()
+    L.pq1_silu_mul(out.ctypes.data, g.ctypes.data, g.size)
+    f = np.float32
+    want = np.array([f(f(gi * f(f(1.0) / f(f(1.0) + f(libm.expf(f(-gi)))))) * ui) for gi, ui in zip(g, u)], np.float32)
+    assert np.array_equal(out.view(np.uint32), want.view(np.uint32))
