@@ -293,6 +293,19 @@ int pb_bonsai_decode(pb_bonsai* m, pb_bonsai_state* s, int token, int pos, const
 int pb_bonsai_decode_greedy(pb_bonsai* m, pb_bonsai_state* s, int token, int pos, int n, int* d_ids,
                             void* stream);
 
+/* ---- sampler: sample_topkpp + frand01 (pulsar_arm/bonsai2/fwd8.c:465-521) ----
+ * for each of B rows of fp32 logits (row b at d_logits + b*ld, n values):
+ * top-k (topk <= 0 or > 1024 means 1024; ties in the reference's order,
+ * value descending then index ascending), min-p and top-p on the raw logits,
+ * temperature last, softmax draw with the row's 64-bit LCG state d_rng[b]
+ * (advanced once per draw). temp <= 0 is greedy (the first maximum, the state
+ * untouched; d_rng may be null). d_ids[b] receives the id, or -1 for a row
+ * holding a NaN. One launch for all rows; asynchronous on `stream`. The
+ * exponentials are this library's expf (within about 1 ulp of the C
+ * library's, which the reference uses); logf(minp) is the host's. */
+int pb_sample_topkpp(const float* d_logits, int B, int n, long long ld, float temp, float topp, int topk,
+                     float minp, unsigned long long* d_rng, int* d_ids, void* stream);
+
 /* ---- the Bonsai host hooks of pulsar_arm/bonsai2/pq1_fwd8_shim.h:24-60 ----
  * (the reference implements them in pq1_fwd8_glue.c:235-246, :1483-1760):
  * fwd8.c built with that shim and linked against this library runs each

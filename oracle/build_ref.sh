@@ -16,6 +16,7 @@
 #   lfm3_nanode.cu:4598-4603    cpu_f2bf / cpu_bf2f
 #   lfm3_nanode.cu:4658-4684    cpuchk_run's scalar leaf-order transcription
 #   fwd8.c:312-317, 320-369     rms, YaRN rope table and rotation (8B constants)
+#   fwd8.c:465-521              argmax, RS, frand01, sample_topkpp (libpb_sample.so)
 #   pq1_host.c:373-434, 226     pq1_fa16_head (f16 flash-attention decode), silu tail
 #
 # Needs the reference checkout (default /root/reference, override with
@@ -331,3 +332,23 @@ int pbref_gguf_offset(const char* path, const char* name, unsigned long long* of
 WRAP
 } | "$CC" -O2 -fPIC -shared -w -x c -o "$out/libpb_gguf.so" -
 echo "build_ref: built $out/libpb_gguf.so"
+
+# --- I: fwd8.c's sampler (pulsar_arm/bonsai2/fwd8.c:465-521: argmax, the
+#        generator state RS, frand01 and sample_topkpp), unmodified, built with
+#        gcc's default contraction as D is, with a wrapper written here that
+#        loads and returns the generator state; tests/test_sample.py compares
+#        the oracle's restatement with it.
+{
+  printf '#include <stdint.h>\n#include <math.h>\n'
+  sed -n '465,521p' "$F8"
+  cat <<'WRAP'
+/* ---- wrapper (this repository's code) ---- */
+int pbref_sample_topkpp(const float* lg, int n, float temp, float topp, int topk, float minp, uint64_t* rs) {
+  RS = *rs;
+  const int id = sample_topkpp(lg, n, temp, topp, topk, minp);
+  *rs = RS;
+  return id;
+}
+WRAP
+} | "$CC" -O2 -fPIC -shared -ffp-contract=fast -mfma -w -x c -o "$out/libpb_sample.so" - -lm
+echo "build_ref: built $out/libpb_sample.so"

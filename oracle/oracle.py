@@ -71,6 +71,8 @@ def lib():
         L.pbo_rope.argtypes = [vp, i, i, i, vp, vp]
         L.pbo_attn_head.argtypes = [vp, vp, vp, i, i, i, i, i, f, C.c_uint16, i, vp]
         L.pbo_argmax.restype = i; L.pbo_argmax.argtypes = [vp, i]
+        L.pbo_sample_topkpp.restype = i
+        L.pbo_sample_topkpp.argtypes = [vp, i, f, f, i, f, C.POINTER(C.c_uint64), i]
         L.pbo_conv_step.argtypes = [vp, vp, vp, i, i, vp]
         L.pbo_silu_mul_bf.argtypes = [vp, vp, vp, i]
         L.pbo_sigmoid_gate.argtypes = [vp, vp, i, i]
@@ -413,3 +415,12 @@ class BsModel:
             lib().pbo_bs_model_free(self.m)
         except Exception:
             pass
+
+
+def sample_topkpp(logits, temp, topp, topk, minp, rs, libm_exp=False):
+    """fwd8.c:465-521 on one row: -> (id, the advanced generator state)"""
+    lg = np.ascontiguousarray(logits, np.float32)
+    st = C.c_uint64(int(rs))
+    tid = lib().pbo_sample_topkpp(_p(lg), lg.shape[0], float(temp), float(topp), int(topk), float(minp),
+                                  C.byref(st), 1 if libm_exp else 0)
+    return tid, int(st.value)

@@ -886,3 +886,57 @@ int pbo_bs_decode(const pbo_bs_model* m, pbo_bs_state* s, int token, int pos, co
   free(xn); free(qf); free(kf); free(vf); free(at); free(ao); free(lg); free(lu); free(xq);
   return id;
 }
+
+/* ---- sampler ------------------------------------------------------------------
+ * sample_topkpp + frand01, pulsar_arm/bonsai2/fwd8.c:465-521. The reference
+ * keeps a descending insertion list of at most k entries; a later value equal
+ * to an entry goes after it and a full list drops it, so the list is the
+ * first k of all (value, index) pairs ordered by value descending, then index
+ * ascending. That order is produced here by a sort. */
+typedef struct { float v; int i; } pbo_vi;
+static int pbo_vi_cmp(const void* pa, const void* pb) {
+  const pbo_vi* a = (const pbo_vi*)pa;
+  const pbo_vi* b = (const pbo_vi*)pb;
+  if (a->v > b->v) return -1;
+  if (a->v < b->v) return 1;
+  return (a->i > b->i) - (a->i < b->i);
+}
+int pbo_sample_topkpp(const float* lg, int n, float temp, float topp, int topk, float minp, uint64_t* rs,
+                      int libm_exp) {
+  float (*ex)(float) = libm_exp ? expf : pbo_expf;
+  for (int i = 0; i < n; i++)
+    if (lg[i] != lg[i]) return -1;
+  if (temp <= 0.0f) return pbo_argmax(lg, n);
+  int k = (topk <= 0 || topk > 1024) ? 1024 : topk;
+  if (k > n) k = n;
+  pbo_vi* all = malloc(sizeof(pbo_vi) * (size_t)n);
+  for (int i = 0; i < n; i++) { all[i].v = lg[i]; all[i].i = i; }
+  qsort(all, (size_t)n, sizeof(pbo_vi), pbo_vi_cmp);
+  const float mx = all[0].v;
+  int m = k;
+  if (minp > 0.0f) {   /* min-p on the raw logits */
+    const float thr = mx + logf(minp);
+    while (m > 1 && all[m - 1].v < thr) m--;
+  }
+  double es = 0.0;     /* top-p on the raw logits */
+  for (int j = 0; j < m; j++) es += (double)ex(all[j].v - mx);
+  double acc = 0.0;
+  int keep = m;
+  for (int j = 0; j < m; j++) {
+    acc += (double)ex(all[j].v - mx) / es;
+    if (acc >= (double)topp) { keep = j + 1; break; }
+  }
+  double es2 = 0.0;    /* temperature last, softmax, draw */
+  for (int j = 0; j < keep; j++) es2 += (double)ex((all[j].v - mx) / temp);
+  *rs = *rs * 6364136223846793005ull + 1442695040888963407ull;
+  const float r01 = (float)((double)(*rs >> 11) * (1.0 / 9007199254740992.0));
+  const double r = (double)r01 * es2;
+  double a2 = 0.0;
+  int id = all[keep - 1].i;
+  for (int j = 0; j < keep; j++) {
+    a2 += (double)ex((all[j].v - mx) / temp);
+    if (r < a2 || j == keep - 1) { id = all[j].i; break; }
+  }
+  free(all);
+  return id;
+}

@@ -145,6 +145,14 @@ const uint16_t* pbo_bs_state_kv(const pbo_bs_state* s, int layer, int which);
 int pbo_bs_decode(const pbo_bs_model* m, pbo_bs_state* s, int token, int pos, const float* x_in,
                   float* logits, float* x_out);
 
+/* sample_topkpp + frand01 (fwd8.c:465-521): top-k (k <= 1024; <= 0 means
+ * 1024), min-p and top-p on the raw logits, temperature last, softmax draw
+ * from the LCG state *rs (advanced only when temp > 0). libm_exp selects the
+ * C library's expf (the reference's) instead of pbo_expf (the device's).
+ * Rows holding a NaN return -1. */
+int pbo_sample_topkpp(const float* lg, int n, float temp, float topp, int topk, float minp, uint64_t* rs,
+                      int libm_exp);
+
 int pbo_threads(void);
 
 #ifdef __cplusplus

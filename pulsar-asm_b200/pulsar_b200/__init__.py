@@ -81,6 +81,7 @@ def lib():
     L.pb_q1_pack.argtypes = [vp, i, i, i, vp, pvp]
     L.pb_q1_free.argtypes = [vp]
     L.pb_q8k_quantize.argtypes = [vp, i, vp, vp]
+    L.pb_sample_topkpp.argtypes = [vp, i, i, C.c_longlong, C.c_float, C.c_float, i, C.c_float, vp, vp, vp]
     L.pb_q1_gemv.argtypes = [vp, vp, vp, vp, vp]
     L.pq1_pq1_compat_gemv.restype = None
     L.pq1_pq1_compat_gemv.argtypes = [i, i, vp, vp, vp, vp]
@@ -242,6 +243,17 @@ def q80_quantize(x, qx, dx, stream=None):
 
 def q8k_quantize(x, xq, stream=None):
     check(lib().pb_q8k_quantize(_ptr(x), x.shape[0], _ptr(xq), _stream(stream)))
+
+
+def sample_topkpp(logits, temp, topp, topk, minp, rng, ids, stream=None):
+    """fwd8.c's sampler on the device for every row of logits (fp32 [B][n]):
+    top-k, min-p, top-p on the raw logits, temperature last, softmax draw;
+    rng (uint64 as int64 [B]) holds each row's generator state and advances
+    when temp > 0; ids (int32 [B]) receives the ids (-1 for a row with a NaN)"""
+    lg = logits if logits.dim() == 2 else logits.view(1, -1)
+    check(lib().pb_sample_topkpp(_ptr(lg), lg.shape[0], lg.shape[1], lg.stride(0), float(temp), float(topp),
+                                 int(topk), float(minp), _ptr(rng) if rng is not None else None, _ptr(ids),
+                                 _stream(stream)))
 
 
 class Q1Tensor:
