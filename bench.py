@@ -342,6 +342,51 @@ def kernel_suite(torch, pb, peak, stream):
         out["cfg0_q80_gemv"] = {"shape": [N, K], "us": ms * 1e3, "bytes": nbytes, "GB/s": gbs,
                                 "frac": gbs / peak, "copies": ncp}
         del ws
+        # cfg0 shape on the low-bit formats (blob dtypes 6 / 7): Q4 and Q5, bf16
+        # x and y; and one conv layer's four projections at T = 32 in Q4
+        from pulsar_b200 import synth as _synth
+        for bits in (4, 5):
+            N, K = 8192, 2048
+            nbytes = N * K // 32 * (20 if bits == 5 else 16) + N * K // 32 * 4 + K * 2 + N * 2
+            ncp = int(2 * L2 // nbytes) + 1
+            rng = np.random.default_rng(bits)
+            qc, qs = _synth.qlow_payload(rng, N, K, bits)
+            qls = [pb.QlowTensor(torch.from_numpy(qc).cuda(), torch.from_numpy(qs.view(np.int16)).cuda(), bits, N, K,
+                                 stream=stream) for _ in range(ncp)]
+            xb = torch.randn(K, device="cuda", generator=g).to(torch.bfloat16).view(torch.int16)
+            yb = torch.empty(N, dtype=torch.int16, device="cuda")
+            ms = _time_rotating(torch, stream, [lambda w=w: w.gemv(xb, yb, stream=stream) for w in qls], 20)
+            gbs = nbytes / (ms / 1e3) / 1e9
+            out["cfg0_q%d_gemv" % bits] = {"shape": [N, K], "us": ms * 1e3, "bytes": nbytes, "GB/s": gbs,
+                                           "frac": gbs / peak, "copies": ncp,
+                                           "path": "k_qlow_tile (lfm3_qlow.cuh arithmetic, blob dtype %d)" % (
+                                               7 if bits == 5 else 6)}
+            del qls
+        shapes = [(6144, 2048), (2048, 2048), (16384, 2048), (2048, 8192)]
+        T = 32
+        lay_bytes = sum(n * k // 32 * 16 + n * k // 32 * 4 + T * (k + n) * 2 for n, k in shapes)
+        ncp = int(2 * L2 // lay_bytes) + 1
+        rng = np.random.default_rng(7)
+        lays = []
+        for _ in range(ncp):
+            lay = []
+            for n, k in shapes:
+                qc, qs = _synth.qlow_payload(rng, n, k, 4)
+                lay.append(pb.QlowTensor(qc, qs, 4, n, k, stream=stream))
+            lays.append(lay)
+        xs = {k: torch.randn((T, k), device="cuda", generator=g).to(torch.bfloat16).view(torch.int16)
+              for k in (2048, 8192)}
+        ys = {n: torch.empty((T, n), dtype=torch.int16, device="cuda") for n, _ in shapes}
+
+        def q4_layer(lay):
+            for (n, k), w in zip(shapes, lay):
+                w.gemm(xs[k], ys[n], stream=stream)
+        ms = _time_rotating(torch, stream, [lambda lay=lay: q4_layer(lay) for lay in lays], 10)
+        out["cfg2_q4_gemm_T32"] = {"layer_gemms": [list(x) for x in shapes], "T": T, "us_per_layer": ms * 1e3,
+                                   "bytes": lay_bytes, "GB/s": lay_bytes / (ms / 1e3) / 1e9,
+                                   "frac": lay_bytes / (ms / 1e3) / 1e9 / peak, "copies": ncp,
+                                   "path": "k_qlow_tile, 4 positions per tile read (blob dtype 6)"}
+        del lays
         # cfg3: Q1_0 gate|up 24576x4096, Q8_K activation, y fp32
         N, K = 24576, 4096
         nbytes = N * K // 8 + N * (K // 128) * 2 + (K // 256) * 292 + N * 4

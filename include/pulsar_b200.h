@@ -293,6 +293,28 @@ int pb_bonsai_decode(pb_bonsai* m, pb_bonsai_state* s, int token, int pos, const
 int pb_bonsai_decode_greedy(pb_bonsai* m, pb_bonsai_state* s, int token, int pos, int n, int* d_ids,
                             void* stream);
 
+/* ---- low-bit backbone GEMV: Q4 / Q5 (blob dtypes 6 / 7) ------------------
+ * pulsar_arm/asm/lfm3_qlow.cuh:1-113 (k_qlow + k_qlow_combine, dispatched by
+ * qlow_gemv, lfm3_nanode.cu:1894-1915). codes / scales are the exporter's
+ * tiled payload as the blob stores it (32-row tiles; per tile and 32-weight
+ * group 32 x 16 bytes of nibbles, for Q5 then 32 x 4 bytes of high-bit
+ * planes; scales 32 x half2 (128 d, mn) per tile and group): N*K/32*16 (Q4)
+ * or *20 (Q5) code bytes and N*K/32*4 scale bytes; N % 32 == 0, K % 256 ==
+ * 0. pb_qlow_gemv: y (bf16 [N]) = W x (x bf16 [K]) with the reference's
+ * arithmetic bit for bit (K slices of 2, 4 from K = 4096, added in order).
+ * pb_qlow_gemm: T positions (x [T][K], y [T][N]), each position's values
+ * those of pb_qlow_gemv (the prefill's per-position loop, :4847). x must be
+ * 16-byte aligned, and x and y must not overlap. */
+typedef struct pb_qlow pb_qlow;
+int pb_qlow_pack(const void* codes, const void* scales, int bits, int N, int K, int src_on_device, void* stream,
+                 pb_qlow** out);
+int pb_qlow_free(pb_qlow* w);
+int pb_qlow_gemv(const pb_qlow* w, const uint16_t* d_x, uint16_t* d_y, void* stream);
+int pb_qlow_gemm(const pb_qlow* w, int T, const uint16_t* d_x, uint16_t* d_y, void* stream);
+/* synchronise `stream` and report a failure recorded on the device (a
+ * bounded wait for the streamed weights that gave up): PB_OK or PB_ECUDA */
+int pb_qlow_status(const pb_qlow* w, void* stream);
+
 /* ---- sampler: sample_topkpp + frand01 (pulsar_arm/bonsai2/fwd8.c:465-521) ----
  * for each of B rows of fp32 logits (row b at d_logits + b*ld, n values):
  * top-k (topk <= 0 or > 1024 means 1024; ties in the reference's order,

@@ -293,6 +293,72 @@ WRAP
   echo "build_ref: built $out/libpb_refgpu.so"
 fi
 
+# --- F2: the reference's low-bit GEMV kernels (pulsar_arm/asm/lfm3_qlow.cuh,
+#         included where it lies: k_qlow + k_qlow_combine), with a wrapper
+#         written here that launches them as qlow_gemv does
+#         (lfm3_nanode.cu:1898-1915: KS 2, 4 from K = 4096; PD 2 at 4 blocks per
+#         SM, the default) on host buffers. GPU box only
+#         (tests/golden/make_golden_qlow.py).
+if [ -x "$NVCC" ]; then
+  {
+    printf '#include <cstdint>\n#include <cuda_runtime.h>\n#include "%s"\n' "$REF/pulsar_arm/asm/lfm3_qlow.cuh"
+    cat <<'WRAP'
+/* ---- host wrapper (this repository's code) ---- */
+extern "C" int pbref_gpu_qlow(const void* q, const void* s, int bits, const uint16_t* x, uint16_t* y, int N, int K) {
+  const size_t nc = (size_t)N * K / 32 * (bits == 5 ? 20 : 16), ns = (size_t)N * K / 32 * 4;
+  const int KS = K >= 4096 ? 4 : 2;
+  const size_t sm = (size_t)(K / KS + K / 32 / KS) * 4;
+  void *dq, *ds, *dx, *dy, *dp;
+  cudaMalloc(&dq, nc); cudaMalloc(&ds, ns); cudaMalloc(&dx, (size_t)K * 2); cudaMalloc(&dy, (size_t)N * 2);
+  cudaMalloc(&dp, (size_t)KS * N * 4);
+  cudaMemcpy(dq, q, nc, cudaMemcpyHostToDevice); cudaMemcpy(ds, s, ns, cudaMemcpyHostToDevice);
+  cudaMemcpy(dx, x, (size_t)K * 2, cudaMemcpyHostToDevice);
+  const dim3 gr((unsigned)((N + 255) / 256), (unsigned)KS);
+  const uint4* cq = (const uint4*)dq; const __half2* cs = (const __half2*)ds;
+  if (bits == 4) k_qlow<4, 256, 2, 4><<<gr, 256, sm>>>(cq, cs, (const unsigned short*)dx, (float*)dp, (unsigned short*)dy, N, K);
+  else           k_qlow<5, 256, 2, 4><<<gr, 256, sm>>>(cq, cs, (const unsigned short*)dx, (float*)dp, (unsigned short*)dy, N, K);
+  k_qlow_combine<<<(N + 255) / 256, 256>>>((const float*)dp, (unsigned short*)dy, N, KS);
+  cudaMemcpy(y, dy, (size_t)N * 2, cudaMemcpyDeviceToHost);
+  const int rc = cudaDeviceSynchronize() == cudaSuccess && cudaGetLastError() == cudaSuccess ? 0 : -1;
+  cudaFree(dq); cudaFree(ds); cudaFree(dx); cudaFree(dy); cudaFree(dp);
+  return rc;
+}
+/* mean microseconds of qlow_gemv's two launches over `reps` calls, cycling
+   over `ncopy` device copies of the tensor (together larger than L2), timed
+   with CUDA events after one warm pass */
+extern "C" float pbref_gpu_qlow_time(const void* q, const void* s, int bits, int N, int K, int ncopy, int reps) {
+  const size_t nc = (size_t)N * K / 32 * (bits == 5 ? 20 : 16), ns = (size_t)N * K / 32 * 4;
+  const int KS = K >= 4096 ? 4 : 2;
+  const size_t sm = (size_t)(K / KS + K / 32 / KS) * 4;
+  char *dq, *ds; void *dx, *dy, *dp;
+  cudaMalloc(&dq, nc * ncopy); cudaMalloc(&ds, ns * ncopy); cudaMalloc(&dx, (size_t)K * 2); cudaMalloc(&dy, (size_t)N * 2);
+  cudaMalloc(&dp, (size_t)KS * N * 4); cudaMemset(dx, 0, (size_t)K * 2);
+  for (int c = 0; c < ncopy; c++) { cudaMemcpy(dq + nc * c, q, nc, cudaMemcpyHostToDevice); cudaMemcpy(ds + ns * c, s, ns, cudaMemcpyHostToDevice); }
+  const dim3 gr((unsigned)((N + 255) / 256), (unsigned)KS);
+  auto run = [&](int c) {
+    const uint4* cq = (const uint4*)(dq + nc * c); const __half2* cs = (const __half2*)(ds + ns * c);
+    if (bits == 4) k_qlow<4, 256, 2, 4><<<gr, 256, sm>>>(cq, cs, (const unsigned short*)dx, (float*)dp, (unsigned short*)dy, N, K);
+    else           k_qlow<5, 256, 2, 4><<<gr, 256, sm>>>(cq, cs, (const unsigned short*)dx, (float*)dp, (unsigned short*)dy, N, K);
+    k_qlow_combine<<<(N + 255) / 256, 256>>>((const float*)dp, (unsigned short*)dy, N, KS);
+  };
+  for (int c = 0; c < ncopy; c++) run(c);
+  cudaEvent_t e0, e1; cudaEventCreate(&e0); cudaEventCreate(&e1);
+  cudaEventRecord(e0);
+  for (int r = 0; r < reps; r++) for (int c = 0; c < ncopy; c++) run(c);
+  cudaEventRecord(e1); cudaEventSynchronize(e1);
+  float ms = 0.f; cudaEventElapsedTime(&ms, e0, e1);
+  const int ok = cudaGetLastError() == cudaSuccess;
+  cudaFree(dq); cudaFree(ds); cudaFree(dx); cudaFree(dy); cudaFree(dp); cudaEventDestroy(e0); cudaEventDestroy(e1);
+  return ok ? ms * 1e3f / (reps * ncopy) : -1.0f;
+}
+WRAP
+  } > "$out/refqlow.cu"
+  "$NVCC" -gencode arch=compute_100a,code=sm_100a -O3 -std=c++17 -Xcompiler -fPIC -shared -w \
+      -o "$out/libpb_refqlow.so" "$out/refqlow.cu"
+  rm -f "$out/refqlow.cu"
+  echo "build_ref: built $out/libpb_refqlow.so"
+fi
+
 # --- G: the reference's x86/C CPU Q8 GEMV, unmodified, for timing: its own
 #        flags (.auto/lfm3/q8_gemv_cpu.c:16, -fopenmp -ffp-contract=off) at -O3,
 #        once for the baseline x86-64 ISA and once for x86-64-v3 (AVX2); the

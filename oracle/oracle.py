@@ -71,6 +71,7 @@ def lib():
         L.pbo_rope.argtypes = [vp, i, i, i, vp, vp]
         L.pbo_attn_head.argtypes = [vp, vp, vp, i, i, i, i, i, f, C.c_uint16, i, vp]
         L.pbo_argmax.restype = i; L.pbo_argmax.argtypes = [vp, i]
+        L.pbo_qlow_gemv.argtypes = [vp, vp, i, i, i, i, vp, vp]
         L.pbo_sample_topkpp.restype = i
         L.pbo_sample_topkpp.argtypes = [vp, i, f, f, i, f, C.POINTER(C.c_uint64), i]
         L.pbo_conv_step.argtypes = [vp, vp, vp, i, i, vp]
@@ -424,3 +425,13 @@ def sample_topkpp(logits, temp, topp, topk, minp, rs, libm_exp=False):
     tid = lib().pbo_sample_topkpp(_p(lg), lg.shape[0], float(temp), float(topp), int(topk), float(minp),
                                   C.byref(st), 1 if libm_exp else 0)
     return tid, int(st.value)
+
+
+def qlow_gemv(codes, scales, bits, N, K, x):
+    """lfm3_qlow.cuh's GEMV; x bf16 bits [T][K] (or [K]) -> y bf16 bits [T][N]"""
+    x = np.ascontiguousarray(x, np.uint16)
+    T = 1 if x.ndim == 1 else x.shape[0]
+    y = np.zeros((T, N), np.uint16)
+    lib().pbo_qlow_gemv(_p(np.ascontiguousarray(codes, np.uint8)), _p(np.ascontiguousarray(scales, np.uint16)),
+                        int(bits), int(N), int(K), T, _p(x), _p(y))
+    return y if x.ndim == 2 else y[0]

@@ -940,3 +940,67 @@ int pbo_sample_topkpp(const float* lg, int n, float temp, float topp, int topk, 
   free(all);
   return id;
 }
+
+/* ---- low-bit (Q4 / Q5) GEMV --------------------------------------------------
+ * pulsar_arm/asm/lfm3_qlow.cuh:20-113. Per row r (tile r/32, lane r%32): K is
+ * cut into KS slices (2, or 4 from K = 4096, lfm3_nanode.cu:1899); per slice
+ * y = 0 and, group by group in order, the codes q of the group become
+ * f = 1 + q/128, four fma chains a_b run over weights b, b+4, ..., b+28,
+ * acc = (a0 + a1) + (a2 + a3), sx = the group's x summed in order from 0,
+ * y = fma(d', acc - sx, fma(mn, sx, y)); out = bf16(((0 + y_0) + y_1) ...)
+ * (k_qlow_combine, :104-110; its rounding has no inf / NaN case). */
+static inline uint32_t qlow_code(const uint8_t* grp, int bits, int lane, int k) {
+  /* grp: the (tile, group) record; lane's uint4 at grp + 16*lane; weight k =
+   * 8i + 4hf + b sits in word i, byte b, nibble hf */
+  const int i = k >> 3, hf = (k >> 2) & 1, b = k & 3;
+  const uint8_t byte = grp[16 * lane + 4 * i + b];
+  uint32_t q = hf ? (uint32_t)(byte >> 4) : (uint32_t)(byte & 15u);
+  if (bits == 5) {
+    const uint8_t* pl = grp + 512 + 4 * lane;   /* the lane's high-bit plane word */
+    const int p = 2 * i + hf;                   /* quad; bit 8b + p of the word */
+    const uint32_t word = (uint32_t)pl[0] | (uint32_t)pl[1] << 8 | (uint32_t)pl[2] << 16 | (uint32_t)pl[3] << 24;
+    q |= ((word >> (8 * b + p)) & 1u) << 4;
+  }
+  return q;
+}
+void pbo_qlow_gemv(const uint8_t* codes, const uint16_t* scales, int bits, int N, int K, int T,
+                   const uint16_t* x, uint16_t* y) {
+  const int G = K / 32, KS = K >= 4096 ? 4 : 2, GL = G / KS;
+  const size_t rec = bits == 5 ? 640 : 512;   /* bytes per (tile, group) */
+  float* xf = malloc(sizeof(float) * (size_t)K);
+  float* sx = malloc(sizeof(float) * (size_t)G);
+  for (int t = 0; t < T; t++) {
+    for (int k = 0; k < K; k++) xf[k] = pbo_bf2f(x[(size_t)t * K + k]);
+    for (int g = 0; g < G; g++) {
+      float s = 0.0f;
+      for (int k = 0; k < 32; k++) s = s + xf[g * 32 + k];
+      sx[g] = s;
+    }
+#pragma omp parallel for schedule(static)
+    for (int r = 0; r < N; r++) {
+      const int tile = r / 32, lane = r % 32;
+      float out = 0.0f;
+      for (int sl = 0; sl < KS; sl++) {
+        float yv = 0.0f;
+        for (int g = sl * GL; g < (sl + 1) * GL; g++) {
+          const uint8_t* grp = codes + ((size_t)tile * G + g) * rec;
+          float a[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+          for (int k = 0; k < 32; k++) {   /* chain b = k % 4, in k order */
+            const uint32_t q = qlow_code(grp, bits, lane, k);
+            const float f = bitsf(0x3F800000u | (q << 16));   /* 1 + q/128 */
+            a[k & 3] = fmaf(f, xf[g * 32 + k], a[k & 3]);
+          }
+          const float acc = (a[0] + a[1]) + (a[2] + a[3]);
+          const size_t si = (((size_t)tile * G + g) * 32 + lane) * 2;
+          const float dp = pbo_h2f(scales[si]), mn = pbo_h2f(scales[si + 1]);
+          yv = fmaf(dp, acc - sx[g], fmaf(mn, sx[g], yv));
+        }
+        out = out + yv;
+      }
+      const uint32_t u = fbits(out);
+      y[(size_t)t * N + r] = (uint16_t)((u + 0x7fffu + ((u >> 16) & 1u)) >> 16);
+    }
+  }
+  free(xf);
+  free(sx);
+}

@@ -145,6 +145,12 @@ const uint16_t* pbo_bs_state_kv(const pbo_bs_state* s, int layer, int which);
 int pbo_bs_decode(const pbo_bs_model* m, pbo_bs_state* s, int token, int pos, const float* x_in,
                   float* logits, float* x_out);
 
+/* the low-bit GEMV (lfm3_qlow.cuh: k_qlow + k_qlow_combine, launched by
+ * qlow_gemv, lfm3_nanode.cu:1894-1915): codes / scales in the exporter's
+ * tiled payload, bits 4 or 5; T positions x [T][K] bf16 -> y [T][N] bf16 */
+void pbo_qlow_gemv(const uint8_t* codes, const uint16_t* scales, int bits, int N, int K, int T,
+                   const uint16_t* x, uint16_t* y);
+
 /* sample_topkpp + frand01 (fwd8.c:465-521): top-k (k <= 1024; <= 0 means
  * 1024), min-p and top-p on the raw logits, temperature last, softmax draw
  * from the LCG state *rs (advanced only when temp > 0). libm_exp selects the

@@ -81,6 +81,11 @@ def lib():
     L.pb_q1_pack.argtypes = [vp, i, i, i, vp, pvp]
     L.pb_q1_free.argtypes = [vp]
     L.pb_q8k_quantize.argtypes = [vp, i, vp, vp]
+    L.pb_qlow_pack.argtypes = [vp, vp, i, i, i, i, vp, pvp]
+    L.pb_qlow_free.argtypes = [vp]
+    L.pb_qlow_gemv.argtypes = [vp, vp, vp, vp]
+    L.pb_qlow_gemm.argtypes = [vp, i, vp, vp, vp]
+    L.pb_qlow_status.argtypes = [vp, vp]
     L.pb_sample_topkpp.argtypes = [vp, i, i, C.c_longlong, C.c_float, C.c_float, i, C.c_float, vp, vp, vp]
     L.pb_q1_gemv.argtypes = [vp, vp, vp, vp, vp]
     L.pq1_pq1_compat_gemv.restype = None
@@ -243,6 +248,44 @@ def q80_quantize(x, qx, dx, stream=None):
 
 def q8k_quantize(x, xq, stream=None):
     check(lib().pb_q8k_quantize(_ptr(x), x.shape[0], _ptr(xq), _stream(stream)))
+
+
+class QlowTensor:
+    """A Q4 / Q5 matrix (blob dtypes 6 / 7, the exporter's tiled payload) on
+    the device; gemv / gemm take and give bf16 bits (int16 tensors)."""
+
+    def __init__(self, codes, scales, bits, N, K, stream=None):
+        self.N, self.K, self.bits = N, K, bits
+        h = C.c_void_p()
+        on_dev = hasattr(codes, "is_cuda") and codes.is_cuda
+        if on_dev:
+            _produced(codes)
+            _produced(scales)
+            cp, sp = _ptr(codes), _ptr(scales)
+        else:
+            import numpy as np
+            codes = np.ascontiguousarray(codes, np.uint8)
+            scales = np.ascontiguousarray(scales, np.uint16)
+            cp, sp = codes.ctypes.data, scales.ctypes.data
+        check(lib().pb_qlow_pack(cp, sp, bits, N, K, 1 if on_dev else 0, _stream(stream), C.byref(h)))
+        self.h = h
+
+    def gemv(self, x, y, stream=None):
+        check(lib().pb_qlow_gemv(self.h, _ptr(x), _ptr(y), _stream(stream)))
+
+    def gemm(self, x, y, stream=None):
+        check(lib().pb_qlow_gemm(self.h, x.shape[0], _ptr(x), _ptr(y), _stream(stream)))
+
+    def status(self, stream=None):
+        check(lib().pb_qlow_status(self.h, _stream(stream)))
+
+    def __del__(self):
+        try:
+            if self.h:
+                lib().pb_qlow_free(self.h)
+                self.h = None
+        except Exception:
+            pass
 
 
 def sample_topkpp(logits, temp, topp, topk, minp, rng, ids, stream=None):

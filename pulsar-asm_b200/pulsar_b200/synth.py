@@ -159,6 +159,20 @@ BONSAI_TINY = dict(hidden=1024, inter=2048, n_layers=2, n_heads=8, n_kv=2, vocab
                    rope_factor=4.0, rope_orig_ctx=16384, rope_base=1e6, attn_scale=0.0883883476)
 
 
+def qlow_payload(rng, N, K, bits):
+    """a seeded Q4 / Q5 tensor [N, K] in the exporter's tiled payload
+    (lfm3_qlow.cuh:5-13): (codes uint8 [N*K/32*(16|20)], scales uint16
+    [N*K/32*2] = fp16 (d' = 128 d, mn) per row and group). Every code pattern
+    is a valid tensor, so the codes and planes are uniform random bytes; d' is
+    positive and mn about -d' q_mid / 128, so w = d q + mn is centred."""
+    G = K // 32
+    codes = rng.integers(0, 256, N * K // 32 * (20 if bits == 5 else 16), dtype=np.uint8)
+    dp = rng.uniform(0.02, 0.25, (N // 32, G, 32)).astype(np.float32)
+    mn = (-dp * (2 ** (bits - 1)) / 128 + rng.normal(0, 0.002, dp.shape)).astype(np.float32)
+    sc = np.stack([dp.astype(np.float16), mn.astype(np.float16)], axis=-1).view(np.uint16).reshape(-1)
+    return codes, np.ascontiguousarray(sc)
+
+
 def q1_blocks(rng, rows, K, scale=0.02):
     """Q1_0 18-byte blocks [rows][K/128]: fp16 scale |N(0,1)|*scale, then 16
     bytes of uniform sign bits"""
