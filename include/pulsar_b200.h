@@ -315,6 +315,27 @@ int pb_qlow_gemm(const pb_qlow* w, int T, const uint16_t* d_x, uint16_t* d_y, vo
  * bounded wait for the streamed weights that gave up): PB_OK or PB_ECUDA */
 int pb_qlow_status(const pb_qlow* w, void* stream);
 
+/* ---- TurboQuant K/V cache (pulsar_arm/bonsai2/pq1_swar_sm53.cu:3264-3990;
+ * PQ1_KVTQ, pq1_fwd8_glue.c:211-232, 4 bits by default there) ---------------
+ * bits: 3 or 4 for K and V alike, 43 for 4-bit K with 3-bit V. A 128-value
+ * f16 row becomes 12 (3-bit) or 16 (4-bit) uint32 code words and one fp32
+ * scale (random-sign Hadamard rotation, Lloyd-Max levels of the d = 128
+ * sphere marginal, s = |x| / |c|). Layout per layer: K codes
+ * [n_kv][ctx][CW], K scales [n_kv][ctx], V alike; ctx is the position stride.
+ * pb_tq_store: rows [2 n_kv][128] f16 (the n_kv K rows, then the V rows, post
+ * rope) encoded at position npos (pq1_tq_store). pb_tq_attention: the query
+ * heads q [4 n_kv][128] fp32 (post rope, 4 per KV head as in the reference)
+ * over positions 0..T-1 -> atto [4 n_kv][128] fp32 (pq1_tq_qk2, pq1_tq_sm,
+ * pq1_tq_pv2, pq1_tq_out: the same reductions, in the same orders; rsqrtf and
+ * expf replaced by 1/sqrt and this library's expf); scratch of
+ * pb_tq_scratch_bytes(n_kv, ctx) bytes, 16-byte aligned. Asynchronous. */
+long long pb_tq_scratch_bytes(int nkv, int ctx);
+int pb_tq_store(int bits, const uint16_t* d_rows, int npos, uint32_t* d_kcode, float* d_kscale, uint32_t* d_vcode,
+                float* d_vscale, int nkv, int ctx, void* stream);
+int pb_tq_attention(int bits, const float* d_q, const uint32_t* d_kcode, const float* d_kscale,
+                    const uint32_t* d_vcode, const float* d_vscale, int nkv, int ctx, int T, float* d_atto,
+                    void* d_scratch, void* stream);
+
 /* ---- sampler: sample_topkpp + frand01 (pulsar_arm/bonsai2/fwd8.c:465-521) ----
  * for each of B rows of fp32 logits (row b at d_logits + b*ld, n values):
  * top-k (topk <= 0 or > 1024 means 1024; ties in the reference's order,

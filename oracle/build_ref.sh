@@ -359,6 +359,103 @@ WRAP
   echo "build_ref: built $out/libpb_refqlow.so"
 fi
 
+# --- F3: the reference's TurboQuant K/V kernels (pulsar_arm/bonsai2/
+#         pq1_swar_sm53.cu, cut by line range and compiled where they lie):
+#   :2164        PQ1_APAR_NPOS (the parameter block's position slot)
+#   :2187-2191   pq1_h2f
+#   :3264-3376   codebook, thresholds, sign pattern, pq1_fwht128, pq1_tq_row,
+#                pq1_tq_store
+#   :3447-3550   pq1_tq_qk2, pq1_tq_sm
+#   :3619-3689   pq1_tq_pv2
+#   :3698-3715   pq1_tq_out
+#   :3716-3906   pq1_tq_qks, pq1_tq_tail (the short pair)
+# with host wrappers written here (host buffers in and out). GPU box only
+# (tests/golden/make_golden_tq.py).
+if [ -x "$NVCC" ]; then
+  S="$REF/pulsar_arm/bonsai2/pq1_swar_sm53.cu"
+  {
+    printf '#include <cstdint>\n#include <cmath>\n#include <cuda_runtime.h>\n#include <cuda_fp16.h>\n'
+    sed -n '2164p' "$S"
+    sed -n '2187,2191p' "$S"
+    sed -n '3264,3376p' "$S"
+    sed -n '3447,3550p' "$S"
+    sed -n '3619,3689p' "$S"
+    sed -n '3698,3715p' "$S"
+    sed -n '3716,3906p' "$S"
+    cat <<'WRAP'
+/* ---- host wrappers (this repository's code) ---- */
+namespace {
+template <class T> T* tup(const T* h, size_t n) { T* d = nullptr; cudaMalloc(&d, n * sizeof(T) + 16); if (h) cudaMemcpy(d, h, n * sizeof(T), cudaMemcpyHostToDevice); else cudaMemset(d, 0, n * sizeof(T) + 16); return d; }
+template <class T> int tdown(T* h, const T* d, size_t n) { cudaMemcpy(h, d, n * sizeof(T), cudaMemcpyDeviceToHost); return cudaDeviceSynchronize() == cudaSuccess && cudaGetLastError() == cudaSuccess ? 0 : -1; }
+int cwof(int b) { return b == 3 ? 12 : 16; }
+}
+extern "C" {
+/* encode 2 nkv f16 rows (nkv K rows, then nkv V rows) with pq1_tq_store at
+   bits bk (K) / bv (V): K codes [nkv][CW(bk)], scales [nkv]; V alike */
+int pbref_gpu_tq_store(const uint16_t* rows, int nkv, int bk, int bv, uint32_t* kcw, float* ksc, uint32_t* vcw, float* vsc) {
+  unsigned short* ds = tup((const unsigned short*)rows, (size_t)2 * nkv * 128);
+  uint32_t* dk = tup((const uint32_t*)nullptr, (size_t)nkv * cwof(bk)); float* dks = tup((const float*)nullptr, nkv);
+  uint32_t* dv = tup((const uint32_t*)nullptr, (size_t)nkv * cwof(bv)); float* dvs = tup((const float*)nullptr, nkv);
+  if (bk == 3 && bv == 3) pq1_tq_store<3, 3><<<1, 64 * nkv>>>(ds, nullptr, 0, dk, dks, dv, dvs, nkv, 1);
+  else if (bk == 4 && bv == 4) pq1_tq_store<4, 4><<<1, 64 * nkv>>>(ds, nullptr, 0, dk, dks, dv, dvs, nkv, 1);
+  else pq1_tq_store<4, 3><<<1, 64 * nkv>>>(ds, nullptr, 0, dk, dks, dv, dvs, nkv, 1);
+  int rc = tdown(kcw, dk, (size_t)nkv * cwof(bk)); if (!rc) rc = tdown(ksc, dks, nkv);
+  if (!rc) rc = tdown(vcw, dv, (size_t)nkv * cwof(bv)); if (!rc) rc = tdown(vsc, dvs, nkv);
+  cudaFree(ds); cudaFree(dk); cudaFree(dks); cudaFree(dv); cudaFree(dvs); return rc;
+}
+/* the long chain (pq1_tq_qk2, pq1_tq_sm, pq1_tq_pv2, pq1_tq_out) over
+   positions 0..T-1 of caches with position stride ctx: q [4 nkv][128] fp32,
+   K codes [nkv][ctx][CW], scales [nkv][ctx], V alike; atto [4 nkv][128] */
+int pbref_gpu_tq_attn(const float* q, int bk, int bv, const uint32_t* kcw, const float* ksc, const uint32_t* vcw,
+                      const float* vsc, int nkv, int ctx, int T, float* atto) {
+  const int nh = 4 * nkv, npos = T - 1;
+  uint8_t par[1024] = {0}; *reinterpret_cast<int*>(par + PQ1_APAR_NPOS) = npos;
+  uint8_t* dp = tup(par, sizeof par); float* dq = tup(q, (size_t)nh * 128);
+  uint32_t* dk = tup(kcw, (size_t)nkv * ctx * cwof(bk)); float* dks = tup(ksc, (size_t)nkv * ctx);
+  uint32_t* dv = tup(vcw, (size_t)nkv * ctx * cwof(bv)); float* dvs = tup(vsc, (size_t)nkv * ctx);
+  float* dsc = tup((const float*)nullptr, (size_t)nh * ctx); float* dinv = tup((const float*)nullptr, nh);
+  const int nch = (ctx + PQ1_TQ_CH - 1) / PQ1_TQ_CH;
+  float* dpart = tup((const float*)nullptr, (size_t)nch * nh * 128); float* dat = tup((const float*)nullptr, (size_t)nh * 128);
+  const dim3 gq(nkv, (ctx + 511) / 512 < PQ1_TQ_QB ? (ctx + 511) / 512 : PQ1_TQ_QB), gp(nkv, nch);
+  if (bk == 3) pq1_tq_qk2<3><<<gq, 256>>>(dq, dk, dks, dp, dsc, ctx); else pq1_tq_qk2<4><<<gq, 256>>>(dq, dk, dks, dp, dsc, ctx);
+  pq1_tq_sm<<<nh, 256>>>(dsc, dp, dinv, ctx);
+  if (bv == 3) pq1_tq_pv2<3><<<gp, 128>>>(dsc, dv, dvs, dp, dpart, nh, ctx); else pq1_tq_pv2<4><<<gp, 128>>>(dsc, dv, dvs, dp, dpart, nh, ctx);
+  pq1_tq_out<<<nh, 32>>>(dpart, dinv, dp, dat, nh);
+  int rc = tdown(atto, dat, (size_t)nh * 128);
+  cudaFree(dp); cudaFree(dq); cudaFree(dk); cudaFree(dks); cudaFree(dv); cudaFree(dvs); cudaFree(dsc); cudaFree(dinv);
+  cudaFree(dpart); cudaFree(dat); return rc;
+}
+/* the short pair (pq1_tq_qks encodes the staged rows of position T-1 into the
+   caches, pq1_tq_tail) for T <= 256: stage [2 nkv][128] f16; the caches are
+   read and updated; atto as above */
+int pbref_gpu_tq_short(const float* q, const uint16_t* stage, int bk, int bv, uint32_t* kcw, float* ksc, uint32_t* vcw,
+                       float* vsc, int nkv, int ctx, int T, float* atto) {
+  const int nh = 4 * nkv, npos = T - 1;
+  uint8_t par[1024] = {0}; *reinterpret_cast<int*>(par + PQ1_APAR_NPOS) = npos;
+  uint8_t* dp = tup(par, sizeof par); float* dq = tup(q, (size_t)nh * 128);
+  unsigned short* dst = tup((const unsigned short*)stage, (size_t)2 * nkv * 128);
+  uint32_t* dk = tup(kcw, (size_t)nkv * ctx * cwof(bk)); float* dks = tup(ksc, (size_t)nkv * ctx);
+  uint32_t* dv = tup(vcw, (size_t)nkv * ctx * cwof(bv)); float* dvs = tup(vsc, (size_t)nkv * ctx);
+  float* dsc = tup((const float*)nullptr, (size_t)nh * ctx); float* dat = tup((const float*)nullptr, (size_t)nh * 128);
+  const dim3 g(nkv, ((ctx < PQ1_TQ_CH ? ctx : PQ1_TQ_CH) + PQ1_TQ_SB - 1) / PQ1_TQ_SB);
+  if (bk == 3 && bv == 3) { pq1_tq_qks<3, 3><<<g, PQ1_TQ_SB>>>(dq, dst, dp, dk, dks, dv, dvs, dsc, nkv, ctx); pq1_tq_tail<3><<<nkv, 256>>>(dsc, dv, dvs, dp, dat, ctx); }
+  else if (bk == 4 && bv == 4) { pq1_tq_qks<4, 4><<<g, PQ1_TQ_SB>>>(dq, dst, dp, dk, dks, dv, dvs, dsc, nkv, ctx); pq1_tq_tail<4><<<nkv, 256>>>(dsc, dv, dvs, dp, dat, ctx); }
+  else { pq1_tq_qks<4, 3><<<g, PQ1_TQ_SB>>>(dq, dst, dp, dk, dks, dv, dvs, dsc, nkv, ctx); pq1_tq_tail<3><<<nkv, 256>>>(dsc, dv, dvs, dp, dat, ctx); }
+  int rc = tdown(atto, dat, (size_t)nh * 128);
+  if (!rc) rc = tdown(kcw, dk, (size_t)nkv * ctx * cwof(bk)); if (!rc) rc = tdown(ksc, dks, (size_t)nkv * ctx);
+  if (!rc) rc = tdown(vcw, dv, (size_t)nkv * ctx * cwof(bv)); if (!rc) rc = tdown(vsc, dvs, (size_t)nkv * ctx);
+  cudaFree(dp); cudaFree(dq); cudaFree(dst); cudaFree(dk); cudaFree(dks); cudaFree(dv); cudaFree(dvs); cudaFree(dsc); cudaFree(dat);
+  return rc;
+}
+}
+WRAP
+  } > "$out/reftq.cu"
+  "$NVCC" -gencode arch=compute_100a,code=sm_100a -O3 -std=c++17 -Xcompiler -fPIC -shared -w \
+      -o "$out/libpb_reftq.so" "$out/reftq.cu"
+  rm -f "$out/reftq.cu"
+  echo "build_ref: built $out/libpb_reftq.so"
+fi
+
 # --- G: the reference's x86/C CPU Q8 GEMV, unmodified, for timing: its own
 #        flags (.auto/lfm3/q8_gemv_cpu.c:16, -fopenmp -ffp-contract=off) at -O3,
 #        once for the baseline x86-64 ISA and once for x86-64-v3 (AVX2); the

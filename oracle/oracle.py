@@ -72,6 +72,8 @@ def lib():
         L.pbo_attn_head.argtypes = [vp, vp, vp, i, i, i, i, i, f, C.c_uint16, i, vp]
         L.pbo_argmax.restype = i; L.pbo_argmax.argtypes = [vp, i]
         L.pbo_qlow_gemv.argtypes = [vp, vp, i, i, i, i, vp, vp]
+        L.pbo_tq_row.argtypes = [vp, i, vp, vp]
+        L.pbo_tq_attn.argtypes = [vp, i, i, vp, vp, vp, vp, i, vp]
         L.pbo_sample_topkpp.restype = i
         L.pbo_sample_topkpp.argtypes = [vp, i, f, f, i, f, C.POINTER(C.c_uint64), i]
         L.pbo_conv_step.argtypes = [vp, vp, vp, i, i, vp]
@@ -435,3 +437,30 @@ def qlow_gemv(codes, scales, bits, N, K, x):
     lib().pbo_qlow_gemv(_p(np.ascontiguousarray(codes, np.uint8)), _p(np.ascontiguousarray(scales, np.uint16)),
                         int(bits), int(N), int(K), T, _p(x), _p(y))
     return y if x.ndim == 2 else y[0]
+
+
+def tq_cw(bits):
+    return 12 if bits == 3 else 16
+
+
+def tq_rows(rows16, bits):
+    """TurboQuant encode of f16 rows [n][128] (bits) -> (codes uint32 [n][CW], scales fp32 [n])"""
+    rows16 = np.ascontiguousarray(rows16, np.uint16).reshape(-1, 128)
+    n = rows16.shape[0]
+    cw = np.zeros((n, tq_cw(bits)), np.uint32)
+    sc = np.zeros(n, np.float32)
+    L = lib()
+    for r in range(n):
+        L.pbo_tq_row(_p(rows16[r]), int(bits), _p(cw[r]), C.cast(C.c_void_p(sc.ctypes.data + 4 * r), C.c_void_p))
+    return cw, sc
+
+
+def tq_attn(q4, bk, bv, kcw, ksc, vcw, vsc, T):
+    """the 4 query heads q4 [4][128] of one KV head over positions 0..T-1 of a
+    TurboQuant cache (codes [>=T][CW], scales [>=T]) -> atto [4][128]"""
+    out = np.zeros((4, 128), np.float32)
+    lib().pbo_tq_attn(_p(np.ascontiguousarray(q4, np.float32)), int(bk), int(bv),
+                      _p(np.ascontiguousarray(kcw, np.uint32)), _p(np.ascontiguousarray(ksc, np.float32)),
+                      _p(np.ascontiguousarray(vcw, np.uint32)), _p(np.ascontiguousarray(vsc, np.float32)), int(T),
+                      _p(out))
+    return out

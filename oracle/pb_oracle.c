@@ -1004,3 +1004,185 @@ void pbo_qlow_gemv(const uint8_t* codes, const uint16_t* scales, int bits, int N
   free(xf);
   free(sx);
 }
+
+/* ---- TurboQuant K/V cache ----------------------------------------------------
+ * pulsar_arm/bonsai2/pq1_swar_sm53.cu:3264-3990 (Zandieh et al., TurboQuant,
+ * the MSE variant): a 128-value row x is rotated, y = H D x (H the Sylvester
+ * Hadamard matrix, unnormalised, D the fixed sign pattern below), each
+ * coordinate of y / |x| is replaced by the index of its Lloyd-Max level for
+ * the sphere marginal at d = 128 (sign + magnitude), and the row keeps
+ * s = |x| / |c|. The codebook, its thresholds and D define the stored format
+ * and are the reference's (:3282-3288). The warp orders of the reference's
+ * kernels are emulated: lane l holds elements 4l..4l+3; a butterfly over lanes
+ * is the xor-shuffle loop the kernels run. */
+static const float TQC3[4] = {0.24444127f, 0.75336427f, 1.33664119f, 2.13151002f};
+static const float TQT3[3] = {0.49890277f, 1.04500270f, 1.73407555f};
+static const float TQC4[8] = {0.12788960f, 0.38643676f, 0.65370631f, 0.93720949f,
+                              1.24789774f, 1.60447431f, 2.04605246f, 2.68896675f};
+static const float TQT4[7] = {0.25716320f, 0.52007151f, 0.79545790f, 1.09255362f,
+                              1.42618608f, 1.82526338f, 2.36750960f};
+static const uint32_t TQD[4] = {0xb5297a4du, 0x68e31da4u, 0x1b56c4e9u, 0xf3c2a581u};
+
+static float tq_dsign(float v, int j) { return (TQD[j >> 5] >> (j & 31)) & 1u ? -v : v; }
+static float tq_cent(int bits, int v) {   /* signed level of code v */
+  const float m = bits == 3 ? TQC3[v & 3] : TQC4[v & 7];
+  return (v >> (bits - 1)) & 1 ? -m : m;
+}
+/* xs[128] (lane l holds 4l..4l+3) <- H xs: the pairs within a lane, then the
+ * xor butterflies over lanes m = 1, 2, ..., 16 (:3297-3307) */
+static void tq_fwht(float* xs) {
+  for (int l = 0; l < 32; l++) {
+    float* x = xs + 4 * l;
+    const float a = x[0] + x[1], b = x[0] - x[1], c = x[2] + x[3], d = x[2] - x[3];
+    x[0] = a + c; x[1] = b + d; x[2] = a - c; x[3] = b - d;
+  }
+  for (int m = 1; m < 32; m <<= 1) {
+    float y[128];
+    for (int l = 0; l < 32; l++)
+      for (int i = 0; i < 4; i++) {
+        const float own = xs[4 * l + i], p = xs[4 * (l ^ m) + i];
+        y[4 * l + i] = (l & m) ? p - own : own + p;
+      }
+    memcpy(xs, y, sizeof y);
+  }
+}
+/* the xor-shuffle sum of one value per lane (o = 16, 8, 4, 2, 1); every lane
+ * ends with the same total, returned */
+static float tq_xor_sum(const float* v) {
+  float a[32];
+  memcpy(a, v, sizeof a);
+  for (int o = 16; o; o >>= 1) {
+    float b[32];
+    for (int l = 0; l < 32; l++) b[l] = a[l] + a[l ^ o];
+    memcpy(a, b, sizeof a);
+  }
+  return a[0];
+}
+/* pq1_tq_row (:3312-3366) */
+void pbo_tq_row(const uint16_t* row, int bits, uint32_t* cw, float* scale) {
+  float x[128], n2l[32], c2l[32];
+  int v[128];
+  for (int l = 0; l < 32; l++) {
+    float n2 = 0.0f;
+    for (int i = 0; i < 4; i++) {
+      const float e = pbo_h2f(row[4 * l + i]);
+      n2 = fmaf(e, e, n2);
+      x[4 * l + i] = tq_dsign(e, 4 * l + i);
+    }
+    n2l[l] = n2;
+  }
+  const float n2 = tq_xor_sum(n2l);
+  tq_fwht(x);
+  const float nrm = sqrtf(n2), inv = nrm > 0.0f ? 1.0f / nrm : 0.0f;
+  for (int l = 0; l < 32; l++) {
+    float c2 = 0.0f;
+    for (int i = 0; i < 4; i++) {
+      const float z = x[4 * l + i] * inv, a = fabsf(z);
+      int m = 0;
+      if (bits == 3) m = (a > TQT3[0]) + (a > TQT3[1]) + (a > TQT3[2]);
+      else for (int k = 0; k < 7; k++) m += a > TQT4[k];
+      const float c = bits == 3 ? TQC3[m] : TQC4[m];
+      c2 = fmaf(c, c, c2);
+      v[4 * l + i] = m | ((z < 0.0f) << (bits - 1));
+    }
+    c2l[l] = c2;
+  }
+  const float c2 = tq_xor_sum(c2l);
+  if (bits == 3) {   /* 8 words of 2-bit magnitudes (16 per word), 4 words of sign bits */
+    for (int k = 0; k < 12; k++) cw[k] = 0u;
+    for (int j = 0; j < 128; j++) {
+      cw[j >> 4] |= (uint32_t)(v[j] & 3) << (2 * (j & 15));
+      cw[8 + (j >> 5)] |= (uint32_t)(v[j] >> 2) << (j & 31);
+    }
+  } else {           /* 16 words of nibbles (magnitude | sign << 3) */
+    for (int k = 0; k < 16; k++) cw[k] = 0u;
+    for (int j = 0; j < 128; j++) cw[j >> 3] |= (uint32_t)v[j] << (4 * (j & 7));
+  }
+  *scale = c2 > 0.0f ? nrm * (1.0f / sqrtf(c2)) : 0.0f;
+}
+static int tq_code(const uint32_t* cw, int bits, int j) {
+  if (bits == 3) return (int)((cw[j >> 4] >> (2 * (j & 15))) & 3u) | (int)(((cw[8 + (j >> 5)] >> (j & 31)) & 1u) << 2);
+  return (int)((cw[j >> 3] >> (4 * (j & 7))) & 15u);
+}
+/* pq1_tq_qk2 / pq1_tq_sm / pq1_tq_pv2 / pq1_tq_out (:3447-3714, the long
+ * chain; the short pair, :3722-3905, is the same arithmetic) */
+void pbo_tq_attn(const float* q, int bk, int bv, const uint32_t* kcode, const float* ksc, const uint32_t* vcode,
+                 const float* vsc, int T, float* atto) {
+  const int cwk = bk == 3 ? 12 : 16, cwv = bv == 3 ? 12 : 16;
+  float qr[4][128];
+  for (int h = 0; h < 4; h++) {   /* R q with R's 1/sqrt(128) and the score scale: 2^-7 */
+    float x[128];
+    for (int j = 0; j < 128; j++) x[j] = tq_dsign(q[h * 128 + j], j);
+    tq_fwht(x);
+    for (int j = 0; j < 128; j++) qr[h][j] = x[j] * 0.0078125f;
+  }
+  float* sc = malloc(sizeof(float) * 4 * (size_t)T);
+  for (int t = 0; t < T; t++) {   /* scores: a + fl(q_r c) over j in order, then the row scale */
+    const uint32_t* cw = kcode + (size_t)t * cwk;
+    for (int h = 0; h < 4; h++) {
+      float a = 0.0f;
+      for (int j = 0; j < 128; j++) a = a + qr[h][j] * tq_cent(bk, tq_code(cw, bk, j));
+      sc[h * T + t] = a * ksc[t];
+    }
+  }
+  float inv[4];
+  for (int h = 0; h < 4; h++) {   /* 256 threads: strided per-thread max and sum, warp xor tree, 8 warps in order */
+    float* s = sc + (size_t)h * T;
+    float tm[256], ts[256], wm[8], wsum[8];
+    for (int th = 0; th < 256; th++) {
+      float m = -INFINITY;
+      for (int t = th; t < T; t += 256) m = fmaxf(m, s[t]);
+      tm[th] = m;
+    }
+    for (int w = 0; w < 8; w++) {
+      float a[32];
+      memcpy(a, tm + 32 * w, sizeof a);
+      for (int o = 16; o; o >>= 1) {
+        float b[32];
+        for (int l = 0; l < 32; l++) b[l] = fmaxf(a[l], a[l ^ o]);
+        memcpy(a, b, sizeof a);
+      }
+      wm[w] = a[0];
+    }
+    float m = wm[0];
+    for (int k = 1; k < 8; k++) m = fmaxf(m, wm[k]);
+    for (int th = 0; th < 256; th++) {
+      float sum = 0.0f;
+      for (int t = th; t < T; t += 256) { const float p = pbo_expf(s[t] - m); s[t] = p; sum += p; }
+      ts[th] = sum;
+    }
+    for (int w = 0; w < 8; w++) wsum[w] = tq_xor_sum(ts + 32 * w);
+    float z = 0.0f;
+    for (int k = 0; k < 8; k++) z += wsum[k];
+    inv[h] = 1.0f / z;
+  }
+  const int nc = (T + 255) / 256;   /* P.V in the rotated domain, 256-position chunks */
+  float acc[4][128];
+  for (int h = 0; h < 4; h++) for (int d = 0; d < 128; d++) acc[h][d] = 0.0f;
+  for (int c = 0; c < nc; c++) {
+    const int t0 = c * 256, n = T - t0 < 256 ? T - t0 : 256;
+    float part[4][4][128];   /* [warp][head][dim]: warp w takes positions w, w+4, ... of the chunk */
+    for (int w = 0; w < 4; w++)
+      for (int h = 0; h < 4; h++) {
+        for (int d = 0; d < 128; d++) part[w][h][d] = 0.0f;
+        for (int t = w; t < n; t += 4) {
+          const float g = sc[h * T + t0 + t] * vsc[t0 + t];
+          const uint32_t* cw = vcode + (size_t)(t0 + t) * cwv;
+          for (int d = 0; d < 128; d++) part[w][h][d] = fmaf(g, tq_cent(bv, tq_code(cw, bv, d)), part[w][h][d]);
+        }
+      }
+    for (int h = 0; h < 4; h++)
+      for (int d = 0; d < 128; d++) {
+        const float cs = ((part[0][h][d] + part[1][h][d]) + part[2][h][d]) + part[3][h][d];
+        acc[h][d] = acc[h][d] + cs;
+      }
+  }
+  for (int h = 0; h < 4; h++) {   /* R^T: H, the 1/sqrt(128), 1/sum, then D */
+    float x[128];
+    memcpy(x, acc[h], sizeof x);
+    tq_fwht(x);
+    const float k = inv[h] * 0.0883883476f;
+    for (int j = 0; j < 128; j++) atto[h * 128 + j] = tq_dsign(x[j] * k, j);
+  }
+  free(sc);
+}

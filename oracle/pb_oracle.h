@@ -151,6 +151,16 @@ int pbo_bs_decode(const pbo_bs_model* m, pbo_bs_state* s, int token, int pos, co
 void pbo_qlow_gemv(const uint8_t* codes, const uint16_t* scales, int bits, int N, int K, int T,
                    const uint16_t* x, uint16_t* y);
 
+/* TurboQuant K/V cache (pulsar_arm/bonsai2/pq1_swar_sm53.cu:3264-3990): bits
+ * 3 or 4 per coordinate; a row is CW = 12 (3-bit) or 16 (4-bit) code words and
+ * one f32 scale. pbo_tq_row encodes one f16 row of 128 values. pbo_tq_attn is
+ * the attention of the 4 query heads of one KV head (post-rope fp32 q [4][128])
+ * over positions 0..T-1 of a TurboQuant cache (codes [ctx][CW], scales [ctx])
+ * into atto [4][128]. rsqrtf -> 1/sqrt and expf -> pbo_expf, as everywhere. */
+void pbo_tq_row(const uint16_t* row, int bits, uint32_t* cw, float* scale);
+void pbo_tq_attn(const float* q, int bk, int bv, const uint32_t* kcode, const float* ksc, const uint32_t* vcode,
+                 const float* vsc, int T, float* atto);
+
 /* sample_topkpp + frand01 (fwd8.c:465-521): top-k (k <= 1024; <= 0 means
  * 1024), min-p and top-p on the raw logits, temperature last, softmax draw
  * from the LCG state *rs (advanced only when temp > 0). libm_exp selects the

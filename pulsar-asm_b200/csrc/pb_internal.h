@@ -96,6 +96,14 @@ const float* pb_bonsai_state_logits(const pb_bonsai_state* s);
 // f16, not freed with the state)
 int pb_bonsai_state_create_kv(pb_bonsai* m, int max_ctx, uint16_t* d_kv, pb_bonsai_state** out);
 
+// TurboQuant K/V cache (pb_tq.cu): bits 3, 4 or 43 (4-bit K, 3-bit V); the
+// store takes the position from d_npos when it is non-null (graph replays)
+size_t pb_tq_scratch_floats(int nkv, int ctx);
+int pb_tq_store_launch(int bits, const uint16_t* d_rows, const int* d_npos, int npos, uint32_t* kc, float* ks,
+                       uint32_t* vc, float* vs, int nkv, int ctx, cudaStream_t st);
+int pb_tq_attention_launch(int bits, const float* d_q, const uint32_t* kc, const float* ks, const uint32_t* vc,
+                           const float* vs, int nkv, int ctx, int T, float* d_atto, float* d_scratch, cudaStream_t st);
+
 // one layer's attention block / FFN tail from the caller's host Q8_K
 // activation, for fwd8.c's per-layer hooks (pb_bonsai.cu); blocking
 struct pb_bs_blocks;

@@ -86,6 +86,10 @@ def lib():
     L.pb_qlow_gemv.argtypes = [vp, vp, vp, vp]
     L.pb_qlow_gemm.argtypes = [vp, i, vp, vp, vp]
     L.pb_qlow_status.argtypes = [vp, vp]
+    L.pb_tq_scratch_bytes.argtypes = [i, i]
+    L.pb_tq_scratch_bytes.restype = C.c_longlong
+    L.pb_tq_store.argtypes = [i, vp, i, vp, vp, vp, vp, i, i, vp]
+    L.pb_tq_attention.argtypes = [i, vp, vp, vp, vp, vp, i, i, i, vp, vp, vp]
     L.pb_sample_topkpp.argtypes = [vp, i, i, C.c_longlong, C.c_float, C.c_float, i, C.c_float, vp, vp, vp]
     L.pb_q1_gemv.argtypes = [vp, vp, vp, vp, vp]
     L.pq1_pq1_compat_gemv.restype = None
@@ -286,6 +290,21 @@ class QlowTensor:
                 self.h = None
         except Exception:
             pass
+
+
+def tq_store(bits, rows, npos, kcode, kscale, vcode, vscale, nkv, ctx, stream=None):
+    """TurboQuant encode of rows (f16 bits [2 nkv][128]) at position npos"""
+    check(lib().pb_tq_store(int(bits), _ptr(rows), int(npos), _ptr(kcode), _ptr(kscale), _ptr(vcode), _ptr(vscale),
+                            int(nkv), int(ctx), _stream(stream)))
+
+
+def tq_attention(bits, q, kcode, kscale, vcode, vscale, nkv, ctx, T, atto, scratch=None, stream=None):
+    """attention of q (fp32 [4 nkv][128]) over positions 0..T-1 of a TurboQuant cache"""
+    import torch
+    if scratch is None:
+        scratch = torch.empty(int(lib().pb_tq_scratch_bytes(nkv, ctx)) // 4, dtype=torch.float32, device=q.device)
+    check(lib().pb_tq_attention(int(bits), _ptr(q), _ptr(kcode), _ptr(kscale), _ptr(vcode), _ptr(vscale), int(nkv),
+                                int(ctx), int(T), _ptr(atto), _ptr(scratch), _stream(stream)))
 
 
 def sample_topkpp(logits, temp, topp, topk, minp, rng, ids, stream=None):
