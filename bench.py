@@ -523,18 +523,21 @@ def batch_bench(torch, model, c, stream, B=64, steps=10):
             "tok/s": B * steps / (ms / 1e3), "path": "integer (Q8_0 activations, tcgen05 kind::i8 GEMMs, N = 64)"}
 
 
-def bonsai_bench(torch, pb, peak, stream, steps=20, warmup=3):
+def bonsai_bench(torch, pb, peak, stream, steps=20, warmup=3, kv_bits=0):
     """cfg3: the Bonsai-8B-shaped Q1_0 decoder (36 layers, hidden 4096, 32/8
     heads x 128, FFN 12288, vocab 151936, tied head) over an f16 K/V cache
     filled to just below 2048 positions; `warmup` + `steps` greedy tokens end
     at position 2047 (each step's CUDA graph: 364 kernels). Weights are
     seeded on the device (uniform sign bits, fp16 scales |N(0,1)|*0.02), the
     cache with N(0,1) f16 rows. Also timed end to end through the public
-    call with a host token in and the host id out per step."""
+    call with a host token in and the host id out per step. kv_bits 4: the
+    same with the TurboQuant cache the reference's glue uses by default (its
+    positions below pos0 hold zero codes: the kernels' work does not depend on
+    the code values)."""
     from pulsar_b200 import synth
     max_ctx = 2048
     pos0 = max_ctx - (warmup + steps)
-    c, m, s = bonsai_setup(torch, pb, stream, max_ctx, pos0)
+    c, m, s = bonsai_setup(torch, pb, stream, max_ctx, pos0, kv_bits=kv_bits)
     ids = torch.empty(warmup + steps, dtype=torch.int32, device="cuda")
     with torch.cuda.stream(stream):
         s.decode_greedy(7, pos0, warmup, ids[:warmup], stream=stream)
@@ -556,7 +559,7 @@ def bonsai_bench(torch, pb, peak, stream, steps=20, warmup=3):
         ms_e2e = e2.elapsed_time(e3)
     fb = s.fallbacks()
     ctx_mean = pos0 + warmup + (steps + 1) / 2.0
-    nbytes = synth.bonsai_bytes_per_token(c, ctx_mean)
+    nbytes = synth.bonsai_bytes_per_token(c, ctx_mean, kv_bits=kv_bits)
     step_s = ms / 1e3 / steps
     s.destroy()
     m.close()
@@ -565,11 +568,13 @@ def bonsai_bench(torch, pb, peak, stream, steps=20, warmup=3):
             "ms_per_token": ms / steps, "tok/s": steps / (ms / 1e3),
             "e2e_tok/s": steps / (ms_e2e / 1e3), "bytes_per_token": nbytes,
             "GB/s": nbytes / step_s / 1e9, "frac": nbytes / step_s / 1e9 / peak,
-            "kernels_per_token": 36 * 10 + 4, "rms_serial_fallbacks": fb,
-            "path": "CUDA graph of PDL launches: Q1_0 x Q8_K GEMVs, f16 flash-attention decode in fork order"}
+            "kernels_per_token": 36 * (14 if kv_bits else 10) + 4, "rms_serial_fallbacks": fb,
+            "path": ("CUDA graph of PDL launches: Q1_0 x Q8_K GEMVs, TurboQuant %d-bit K/V cache "
+                     "(store, scores, softmax, chunked rotated-domain P.V, inverse rotation)" % kv_bits) if kv_bits else
+                    "CUDA graph of PDL launches: Q1_0 x Q8_K GEMVs, f16 flash-attention decode in fork order"}
 
 
-def bonsai_setup(torch, pb, stream, max_ctx, pos0, n_layers=None):
+def bonsai_setup(torch, pb, stream, max_ctx, pos0, n_layers=None, kv_bits=0):
     """the cfg3 model with seeded device weights and a state whose K/V cache
     holds N(0,1) f16 rows at positions < pos0"""
     from pulsar_b200 import synth
@@ -598,12 +603,13 @@ def bonsai_setup(torch, pb, stream, max_ctx, pos0, n_layers=None):
             m.set_norm(L, slot, norm(n), st)
     m.set_q1(-1, 16, q1(c["vocab"], H), st)
     m.set_norm(-1, 16, norm(H), st)
-    s = m.new_state(max_ctx)
-    for L in range(c["n_layers"]):
-        for which in (0, 1):
-            kv = s.kv(L, which)
-            kv.copy_(torch.randn(kv.shape, device="cuda", generator=g).half().view(torch.int16))
-            kv[:, pos0:].zero_()
+    s = m.new_state(max_ctx, kv_bits=kv_bits)
+    if not kv_bits:
+        for L in range(c["n_layers"]):
+            for which in (0, 1):
+                kv = s.kv(L, which)
+                kv.copy_(torch.randn(kv.shape, device="cuda", generator=g).half().view(torch.int16))
+                kv[:, pos0:].zero_()
     torch.cuda.synchronize()
     return c, m, s
 
@@ -874,6 +880,7 @@ def main():
         line["kernels"]["cfg2_prefill"] = prefill_bench(torch, model, prompt, stream)
         line["kernels"]["cfg4_batched_decode"] = batch_bench(torch, model, c, stream)
         line["kernels"]["cfg3_decode"] = bonsai_bench(torch, pb, peak, stream)
+        line["kernels"]["cfg3_decode_tq4"] = bonsai_bench(torch, pb, peak, stream, kv_bits=4)
     if rank == 0 and world == 1 and not args.no_cpu:
         tps, cores, n, _ = cpu_baseline(c, weights, args.ctx, args.cpu_seconds)
         line["cpu_baseline"] = {"value": tps, "unit": "tok/s", "cores": cores, "kind": "port", "cpu": cpu_model(),

@@ -273,6 +273,13 @@ int pb_bonsai_set_norm(pb_bonsai* m, int layer, int slot, const float* w, int sr
 /* per sequence: K/V cache [layer][K|V][n_kv][max_ctx][128] f16 and the rope
  * table of every position (max_ctx a multiple of 32, <= 8192) */
 int pb_bonsai_state_create(pb_bonsai* m, int max_ctx, pb_bonsai_state** out);
+/* a state whose K/V cache is TurboQuant-coded (kv_bits 3, 4 or 43; 0 is the
+ * f16 cache of pb_bonsai_state_create): every position's post-rope K/V rows
+ * are coded as they are stored and the attention runs over the codes
+ * (pb_tq_store / pb_tq_attention inside the token's graph). The reference's
+ * glue does this by default (PQ1_KVTQ=4, pq1_fwd8_glue.c:211-232). Needs
+ * n_heads = 4 n_kv (PB_ENOTSUP otherwise). */
+int pb_bonsai_state_create_tq(pb_bonsai* m, int max_ctx, int kv_bits, pb_bonsai_state** out);
 int pb_bonsai_state_destroy(pb_bonsai_state* s);
 /* device address of one layer's K (which 0) or V (which 1) cache [n_kv][max_ctx][128] */
 int pb_bonsai_state_kv(pb_bonsai_state* s, int layer, int which, void** d_ptr);

@@ -102,6 +102,7 @@ def lib():
         L.pbo_bs_model_set_q1.argtypes = [vp, i, i, vp, i, i]
         L.pbo_bs_model_set_f32.argtypes = [vp, i, i, vp]
         L.pbo_bs_state_new.restype = vp; L.pbo_bs_state_new.argtypes = [vp]
+        L.pbo_bs_state_new_tq.restype = vp; L.pbo_bs_state_new_tq.argtypes = [vp, i]
         L.pbo_bs_state_free.argtypes = [vp]
         L.pbo_bs_state_kv.restype = vp; L.pbo_bs_state_kv.argtypes = [vp, i, i]
         L.pbo_bs_decode.restype = i; L.pbo_bs_decode.argtypes = [vp, vp, i, i, vp, vp, vp]
@@ -362,7 +363,7 @@ class BsModel:
     SLOTS = {"q": 0, "k": 1, "v": 2, "o": 3, "gate": 4, "up": 5, "down": 6}
     NORMS = {"attn_norm": 0, "ffn_norm": 1, "q_norm": 2, "k_norm": 3}
 
-    def __init__(self, cfg, weights, max_ctx):
+    def __init__(self, cfg, weights, max_ctx, kv_bits=0):
         L = lib()
         self.cfg = dict(cfg)
         self.max_ctx = max_ctx
@@ -386,7 +387,7 @@ class BsModel:
         on = np.ascontiguousarray(weights["out_norm"], np.float32)
         self._keep.append(on)
         L.pbo_bs_model_set_f32(self.m, -1, 0, _p(on))
-        self.s = L.pbo_bs_state_new(self.m)
+        self.s = L.pbo_bs_state_new_tq(self.m, int(kv_bits)) if kv_bits else L.pbo_bs_state_new(self.m)
 
     def decode(self, token, pos, x_in=None, want_logits=False):
         """-> (greedy id, logits or None, final residual fp32 [hidden])"""

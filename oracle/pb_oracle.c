@@ -757,6 +757,9 @@ struct pbo_bs_state {
   int n_layers;
   uint16_t **kc, **vc;   /* [layer] -> [n_kv][max_ctx][128] f16 */
   float* x;
+  int tq;                /* 0: f16 cache; 3, 4, 43: TurboQuant (pbo_bs_state_new_tq) */
+  uint32_t **tkc, **tvc; /* [layer] -> codes [n_kv][max_ctx][CW] */
+  float **tks, **tvs;    /* [layer] -> scales [n_kv][max_ctx] */
 };
 pbo_bs_model* pbo_bs_model_new(const pbo_bs_cfg* cfg) {
   pbo_bs_model* m = (pbo_bs_model*)calloc(1, sizeof *m);
@@ -798,8 +801,31 @@ pbo_bs_state* pbo_bs_state_new(const pbo_bs_model* m) {
   s->x = calloc((size_t)c->hidden, 4);
   return s;
 }
+/* a state whose K/V cache is TurboQuant-coded (bits 3, 4 or 43, pq1_fwd8_glue.c:
+ * 211-232); needs n_heads = 4 n_kv */
+pbo_bs_state* pbo_bs_state_new_tq(const pbo_bs_model* m, int bits) {
+  pbo_bs_state* s = pbo_bs_state_new(m);
+  const pbo_bs_cfg* c = &m->cfg;
+  const int bk = bits == 43 ? 4 : bits, bv = bits == 43 ? 3 : bits;
+  s->tq = bits;
+  s->tkc = calloc((size_t)c->n_layers, sizeof(uint32_t*));
+  s->tvc = calloc((size_t)c->n_layers, sizeof(uint32_t*));
+  s->tks = calloc((size_t)c->n_layers, sizeof(float*));
+  s->tvs = calloc((size_t)c->n_layers, sizeof(float*));
+  for (int L = 0; L < c->n_layers; L++) {
+    s->tkc[L] = calloc((size_t)c->n_kv * c->max_ctx * (bk == 3 ? 12 : 16), 4);
+    s->tvc[L] = calloc((size_t)c->n_kv * c->max_ctx * (bv == 3 ? 12 : 16), 4);
+    s->tks[L] = calloc((size_t)c->n_kv * c->max_ctx, 4);
+    s->tvs[L] = calloc((size_t)c->n_kv * c->max_ctx, 4);
+  }
+  return s;
+}
 void pbo_bs_state_free(pbo_bs_state* s) {
   if (!s) return;
+  if (s->tq) {
+    for (int L = 0; L < s->n_layers; L++) { free(s->tkc[L]); free(s->tvc[L]); free(s->tks[L]); free(s->tvs[L]); }
+    free(s->tkc); free(s->tvc); free(s->tks); free(s->tvs);
+  }
   for (int L = 0; L < s->n_layers; L++) { free(s->kc[L]); free(s->vc[L]); }
   free(s->kc); free(s->vc); free(s->x); free(s);
 }
@@ -861,10 +887,25 @@ int pbo_bs_decode(const pbo_bs_model* m, pbo_bs_state* s, int token, int pos, co
         s->kc[L][o] = pbo_f2h(kf[kh * 128 + d]);
         s->vc[L][o] = pbo_f2h(vf[kh * 128 + d]);
       }
-    for (int h = 0; h < NH; h++) {
-      const size_t base = (size_t)(h / G) * c->max_ctx * 128;
-      pbo_bs_fa16_head(qf + h * 128, s->kc[L] + base, s->vc[L] + base, pos + 1, c->attn_scale,
-                       at + h * 128);
+    if (s->tq) {   /* the f16 rows of pos, coded (pq1_tq_store), then the TurboQuant attention */
+      const int bk = s->tq == 43 ? 4 : s->tq, bv = s->tq == 43 ? 3 : s->tq;
+      const int cwk = bk == 3 ? 12 : 16, cwv = bv == 3 ? 12 : 16;
+      for (int kh = 0; kh < NKV; kh++) {
+        const size_t r = (size_t)kh * c->max_ctx + pos;
+        pbo_tq_row(s->kc[L] + r * 128, bk, s->tkc[L] + r * cwk, s->tks[L] + r);
+        pbo_tq_row(s->vc[L] + r * 128, bv, s->tvc[L] + r * cwv, s->tvs[L] + r);
+      }
+      for (int kh = 0; kh < NKV; kh++) {
+        const size_t r = (size_t)kh * c->max_ctx;
+        pbo_tq_attn(qf + (size_t)kh * 4 * 128, bk, bv, s->tkc[L] + r * cwk, s->tks[L] + r, s->tvc[L] + r * cwv,
+                    s->tvs[L] + r, pos + 1, at + (size_t)kh * 4 * 128);
+      }
+    } else {
+      for (int h = 0; h < NH; h++) {
+        const size_t base = (size_t)(h / G) * c->max_ctx * 128;
+        pbo_bs_fa16_head(qf + h * 128, s->kc[L] + base, s->vc[L] + base, pos + 1, c->attn_scale,
+                         at + h * 128);
+      }
     }
     bs_gemv(&T[PBO_BS_O], at, xq, ao);
     for (int i = 0; i < H; i++) x[i] = x[i] + ao[i];

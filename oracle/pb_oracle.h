@@ -140,6 +140,10 @@ void pbo_bs_model_set_q1(pbo_bs_model* m, int layer, int slot, const uint8_t* bl
 /* fp32 norm weights (kept by pointer); layer -1: output_norm */
 void pbo_bs_model_set_f32(pbo_bs_model* m, int layer, int slot, const float* p);
 pbo_bs_state* pbo_bs_state_new(const pbo_bs_model* m);
+/* the same with a TurboQuant K/V cache (bits 3, 4 or 43; n_heads = 4 n_kv):
+ * each position's f16 K/V rows are coded at their store, and attention runs
+ * over the codes (pbo_tq_attn) */
+pbo_bs_state* pbo_bs_state_new_tq(const pbo_bs_model* m, int bits);
 void pbo_bs_state_free(pbo_bs_state* s);
 const uint16_t* pbo_bs_state_kv(const pbo_bs_state* s, int layer, int which);
 int pbo_bs_decode(const pbo_bs_model* m, pbo_bs_state* s, int token, int pos, const float* x_in,

@@ -157,7 +157,8 @@ struct BsPreArgs {
   uint16_t* vc;         // layer's V cache
   int NH, NKV, max_ctx;
   BsCtl* ctl;
-  float* qf;            // optional: post-rope q as fp32 [NH][128] (the per-layer hooks' debug copy)
+  float* qf;            // optional: post-rope q as fp32 [NH][128] (TurboQuant attention; the hooks' debug copy)
+  uint16_t* stage;      // optional: the K and V rows go here ([2 NKV][128] f16, K heads first), not to the cache
 };
 // one warp per head: q heads, k heads (rms, rope), then v heads (copied)
 __global__ void __launch_bounds__(32) k_bs_attn_pre(BsPreArgs a) {
@@ -178,7 +179,8 @@ __global__ void __launch_bounds__(32) k_bs_attn_pre(BsPreArgs a) {
 #pragma unroll
   for (int k = 0; k < 4; k++) x[k] = src[l + 32 * k];
   if (hh >= a.NH + a.NKV) {
-    uint16_t* dst = a.vc + ((size_t)(hh - a.NH - a.NKV) * a.max_ctx + pos) * BS_HD;
+    uint16_t* dst = a.stage ? a.stage + (size_t)(hh - a.NH) * BS_HD
+                            : a.vc + ((size_t)(hh - a.NH - a.NKV) * a.max_ctx + pos) * BS_HD;
 #pragma unroll
     for (int k = 0; k < 4; k++) dst[l + 32 * k] = pb_f2h(x[k]);
     return;
@@ -222,7 +224,8 @@ __global__ void __launch_bounds__(32) k_bs_attn_pre(BsPreArgs a) {
     for (int k = 0; k < 4; k++) a.qf[(size_t)hh * BS_HD + l + 32 * k] = o[k];
   }
   uint16_t* dst = hh < a.NH ? a.qh + (size_t)hh * BS_HD
-                            : a.kc + ((size_t)(hh - a.NH) * a.max_ctx + pos) * BS_HD;
+                 : a.stage ? a.stage + (size_t)(hh - a.NH) * BS_HD
+                           : a.kc + ((size_t)(hh - a.NH) * a.max_ctx + pos) * BS_HD;
 #pragma unroll
   for (int k = 0; k < 4; k++) dst[l + 32 * k] = pb_f2h(o[k]);
 }
@@ -536,6 +539,19 @@ __global__ void __launch_bounds__(256) k_bs_silu_q8k(BsSiluArgs a) {
   pb_q8k_block256(v, a.xq + (size_t)blockIdx.x * 292, q8s);
 }
 
+// ------------------------------------------------- Q8_K of a vector
+// the TurboQuant attention's output (fp32 [QD]) for the o projection
+struct BsQ8kArgs {
+  const float* x;
+  uint8_t* xq;   // [n / 256][292]
+};
+__global__ void __launch_bounds__(256) k_bs_q8k(BsQ8kArgs a) {
+  __shared__ Q8kScratch q8s;
+  pb_grid_wait();
+  pb_grid_launch_dependents();
+  pb_q8k_block256(a.x[blockIdx.x * 256 + threadIdx.x], a.xq + (size_t)blockIdx.x * 292, q8s);
+}
+
 // ------------------------------------------------------------- argmax
 struct BsArgmaxArgs {
   const float* lg;
@@ -653,6 +669,7 @@ struct pb_bonsai_state {
   pb_bonsai* m = nullptr;
   int max_ctx = 0;
   char* mem = nullptr;
+  char* tq_mem = nullptr;   // the TurboQuant cache's allocation
   uint16_t* kv = nullptr;   // [layer][2][NKV][max_ctx][128]
   float* rope = nullptr;    // [max_ctx][128]
   float* x[2] = {nullptr, nullptr};
@@ -668,6 +685,15 @@ struct pb_bonsai_state {
   float* logits = nullptr;
   BsCtl* ctl = nullptr;
   BsCtl* h_ctl = nullptr;   // pinned mirror for uploads
+  // TurboQuant K/V cache (kv_bits 3, 4 or 43; 0: the f16 cache `kv`)
+  int kv_bits = 0;
+  uint32_t* tq_kc = nullptr;   // [layer][n_kv][max_ctx][CW(bk)]
+  uint32_t* tq_vc = nullptr;   // [layer][n_kv][max_ctx][CW(bv)]
+  float* tq_ks = nullptr;      // [layer][n_kv][max_ctx]
+  float* tq_vs = nullptr;
+  uint16_t* tq_stage = nullptr;   // [2 n_kv][128] f16: the rows of the current position
+  float* tq_qf = nullptr;         // [n_heads][128] post-rope q
+  float* tq_scratch = nullptr;
   cudaGraphExec_t graph = nullptr;
   uint64_t graph_launches = 0;   // kernels per graph launch
   int final_x = 0;          // which x buffer holds the residual after a step
@@ -734,16 +760,33 @@ int bs_record(pb_bonsai* m, pb_bonsai_state* s, cudaStream_t st) {
     if ((rc = pb_q1_gemv_launch(&m->qkv[L], s->xq, s->qkv, nullptr, st, true))) return rc;
     {
       BsPreArgs a{s->qkv, nw + 2 * H, nw + 2 * H + BS_HD, s->rope, s->qh, kc, vc, NH, NKV, s->max_ctx, s->ctl,
-                  nullptr};
+                  s->tq_qf, s->tq_stage};
       if ((rc = bs_launch(k_bs_attn_pre, dim3(NH + 2 * NKV), 32, 0, st, a, "k_bs_attn_pre"))) return rc;
     }
-    {
-      BsQkArgs a{s->qh, kc, s->scores, NH, NKV, s->max_ctx, c.attn_scale, s->ctl};
-      if ((rc = bs_launch(k_bs_fa_qk, dim3(s->max_ctx / 32, NKV), 32 * (NH / NKV), 0, st, a, "k_bs_fa_qk"))) return rc;
-    }
-    {
-      BsPvArgs a{s->scores, vc, s->atto, s->xq, NH, NKV, s->max_ctx, s->ctl};
-      if ((rc = bs_launch(k_bs_fa_pv, dim3(NH), 256, pv_smem(s->max_ctx), st, a, "k_bs_fa_pv"))) return rc;
+    if (s->kv_bits) {   // TurboQuant: code the rows of this position, attend over the codes
+      const int bk = pb_tq_bk(s->kv_bits), bv = pb_tq_bv(s->kv_bits);
+      const size_t rows = (size_t)NKV * s->max_ctx;
+      uint32_t* tkc = s->tq_kc + (size_t)L * rows * pb_tq_cw(bk);
+      uint32_t* tvc = s->tq_vc + (size_t)L * rows * pb_tq_cw(bv);
+      float* tks = s->tq_ks + (size_t)L * rows;
+      float* tvs = s->tq_vs + (size_t)L * rows;
+      if ((rc = pb_tq_store_launch(s->kv_bits, s->tq_stage, &s->ctl->pos, 0, tkc, tks, tvc, tvs, NKV, s->max_ctx, st,
+                                   true)))
+        return rc;
+      if ((rc = pb_tq_attention_launch(s->kv_bits, s->tq_qf, tkc, tks, tvc, tvs, NKV, s->max_ctx, 0, &s->ctl->pos,
+                                       s->atto, s->tq_scratch, st, true)))
+        return rc;
+      BsQ8kArgs a{s->atto, s->xq};
+      if ((rc = bs_launch(k_bs_q8k, dim3(m->QD / 256), 256, 0, st, a, "k_bs_q8k"))) return rc;
+    } else {
+      {
+        BsQkArgs a{s->qh, kc, s->scores, NH, NKV, s->max_ctx, c.attn_scale, s->ctl};
+        if ((rc = bs_launch(k_bs_fa_qk, dim3(s->max_ctx / 32, NKV), 32 * (NH / NKV), 0, st, a, "k_bs_fa_qk"))) return rc;
+      }
+      {
+        BsPvArgs a{s->scores, vc, s->atto, s->xq, NH, NKV, s->max_ctx, s->ctl};
+        if ((rc = bs_launch(k_bs_fa_pv, dim3(NH), 256, pv_smem(s->max_ctx), st, a, "k_bs_fa_pv"))) return rc;
+      }
     }
     if ((rc = pb_q1_gemv_launch(&m->o[L], s->xq, s->ao, nullptr, st, true))) return rc;
     {   // x += attention output ; rms(ffn_norm) ; Q8_K
@@ -782,7 +825,7 @@ int bs_graph(pb_bonsai* m, pb_bonsai_state* s, cudaStream_t st) {
   pb_set_capturing(true);
   cudaGraph_t g = nullptr;
   const int L = m->c.n_layers;
-  s->graph_launches = (uint64_t)L * 10 + 4;
+  s->graph_launches = (uint64_t)L * (s->kv_bits ? 14 : 10) + 4;
   int rc = PB_OK;
   if (cudaStreamBeginCapture(cap, cudaStreamCaptureModeThreadLocal) != cudaSuccess) {
     rc = pb_set_error(PB_ECUDA, "bonsai: begin capture");
@@ -944,7 +987,7 @@ extern "C" int pb_bonsai_set_norm(pb_bonsai* m, int layer, int slot, const float
 }
 
 namespace {
-int bs_state_create(pb_bonsai* m, int max_ctx, uint16_t* kv_ext, pb_bonsai_state** out) {
+int bs_state_create(pb_bonsai* m, int max_ctx, uint16_t* kv_ext, int kv_bits, pb_bonsai_state** out) {
   if (!m || !out || max_ctx <= 0 || max_ctx % 32) return pb_set_error(PB_EINVAL, "pb_bonsai_state_create: bad argument (max_ctx a positive multiple of 32)");
   *out = nullptr;
   if (pv_smem(max_ctx) > 200 * 1024) return pb_set_error(PB_ENOTSUP, "pb_bonsai_state_create: max_ctx %d too large for the attention kernel (<= 8192)", max_ctx);
@@ -954,7 +997,11 @@ int bs_state_create(pb_bonsai* m, int max_ctx, uint16_t* kv_ext, pb_bonsai_state
   pb_bonsai_state* s = new pb_bonsai_state();
   s->m = m;
   s->max_ctx = max_ctx;
-  const size_t kvb = kv_ext ? 0 : (size_t)c.n_layers * 2 * NKV * max_ctx * BS_HD * 2;
+  if (kv_bits && !(kv_bits == 3 || kv_bits == 4 || kv_bits == 43))
+    return pb_set_error(PB_EINVAL, "pb_bonsai_state_create: K/V bits %d (0, 3, 4 or 43)", kv_bits);
+  if (kv_bits && (NH != 4 * NKV || NKV > 16))
+    return pb_set_error(PB_ENOTSUP, "pb_bonsai_state_create: the TurboQuant cache needs n_heads = 4 n_kv <= 64");
+  const size_t kvb = (kv_ext || kv_bits) ? 0 : (size_t)c.n_layers * 2 * NKV * max_ctx * BS_HD * 2;
   const int kmax = std::max(std::max(H, F), m->QD);
   const size_t sizes[] = {kvb, (size_t)max_ctx * BS_HD * 4, (size_t)H * 4, (size_t)H * 4, (size_t)H * 4,
                           (size_t)(m->QD + 2 * m->KD) * 4, (size_t)NH * BS_HD * 2, (size_t)NH * max_ctx * 4,
@@ -988,6 +1035,30 @@ int bs_state_create(pb_bonsai* m, int max_ctx, uint16_t* kv_ext, pb_bonsai_state
   s->ctl = reinterpret_cast<BsCtl*>(take());
   int rc = PB_OK;
   if (cudaMemset(s->mem, 0, tot) != cudaSuccess) rc = pb_set_error(PB_ECUDA, "pb_bonsai_state_create: memset");
+  if (rc == PB_OK && kv_bits) {   // the TurboQuant cache and its scratch, in a second allocation
+    const size_t rows = (size_t)c.n_layers * NKV * max_ctx;
+    const size_t tsz[] = {rows * pb_tq_cw(pb_tq_bk(kv_bits)) * 4, rows * pb_tq_cw(pb_tq_bv(kv_bits)) * 4, rows * 4,
+                          rows * 4, (size_t)2 * NKV * BS_HD * 2, (size_t)m->QD * 4,
+                          pb_tq_scratch_floats(NKV, max_ctx) * 4};
+    size_t ttot = 0;
+    for (size_t x : tsz) ttot += a256(x);
+    if (cudaMalloc(&s->tq_mem, ttot) != cudaSuccess || cudaMemset(s->tq_mem, 0, ttot) != cudaSuccess) {
+      cudaGetLastError();
+      rc = pb_set_error(PB_ENOMEM, "pb_bonsai_state_create: TurboQuant cache of %zu bytes", ttot);
+    } else {
+      char* q = s->tq_mem;
+      int k2 = 0;
+      auto tk = [&]() { char* r = q; q += a256(tsz[k2++]); return r; };
+      s->tq_kc = reinterpret_cast<uint32_t*>(tk());
+      s->tq_vc = reinterpret_cast<uint32_t*>(tk());
+      s->tq_ks = reinterpret_cast<float*>(tk());
+      s->tq_vs = reinterpret_cast<float*>(tk());
+      s->tq_stage = reinterpret_cast<uint16_t*>(tk());
+      s->tq_qf = reinterpret_cast<float*>(tk());
+      s->tq_scratch = reinterpret_cast<float*>(tk());
+      s->kv_bits = kv_bits;
+    }
+  }
   if (rc == PB_OK && cudaMallocHost(&s->h_ctl, sizeof(BsCtl)) != cudaSuccess) rc = pb_set_error(PB_ENOMEM, "pb_bonsai_state_create: pinned");
   if (rc == PB_OK) {
     memset(s->h_ctl, 0, sizeof(BsCtl));
@@ -997,7 +1068,7 @@ int bs_state_create(pb_bonsai* m, int max_ctx, uint16_t* kv_ext, pb_bonsai_state
       rc = pb_set_error(PB_ECUDA, "pb_bonsai_state_create: rope table");
   }
   if (rc != PB_OK) {
-    cudaFree(s->mem); if (s->h_ctl) cudaFreeHost(s->h_ctl);
+    cudaFree(s->mem); if (s->h_ctl) cudaFreeHost(s->h_ctl); cudaFree(s->tq_mem);
     delete s;
     return rc;
   }
@@ -1007,11 +1078,14 @@ int bs_state_create(pb_bonsai* m, int max_ctx, uint16_t* kv_ext, pb_bonsai_state
 }  // namespace
 
 extern "C" int pb_bonsai_state_create(pb_bonsai* m, int max_ctx, pb_bonsai_state** out) {
-  return bs_state_create(m, max_ctx, nullptr, out);
+  return bs_state_create(m, max_ctx, nullptr, 0, out);
+}
+extern "C" int pb_bonsai_state_create_tq(pb_bonsai* m, int max_ctx, int kv_bits, pb_bonsai_state** out) {
+  return bs_state_create(m, max_ctx, nullptr, kv_bits, out);
 }
 int pb_bonsai_state_create_kv(pb_bonsai* m, int max_ctx, uint16_t* d_kv, pb_bonsai_state** out) {
   if (!d_kv) return pb_set_error(PB_EINVAL, "pb_bonsai_state_create_kv: null cache");
-  return bs_state_create(m, max_ctx, d_kv, out);
+  return bs_state_create(m, max_ctx, d_kv, 0, out);
 }
 
 extern "C" int pb_bonsai_state_destroy(pb_bonsai_state* s) {
@@ -1019,6 +1093,7 @@ extern "C" int pb_bonsai_state_destroy(pb_bonsai_state* s) {
   cudaSetDevice(s->m->device);
   if (s->graph) cudaGraphExecDestroy(s->graph);
   cudaFree(s->mem);
+  cudaFree(s->tq_mem);
   cudaFreeHost(s->h_ctl);
   delete s;
   return PB_OK;
@@ -1027,6 +1102,7 @@ extern "C" int pb_bonsai_state_destroy(pb_bonsai_state* s) {
 extern "C" int pb_bonsai_state_kv(pb_bonsai_state* s, int layer, int which, void** d_ptr) {
   if (!s || !d_ptr || layer < 0 || layer >= s->m->c.n_layers || which < 0 || which > 1)
     return pb_set_error(PB_EINVAL, "pb_bonsai_state_kv: bad argument");
+  if (s->kv_bits) return pb_set_error(PB_ENOTSUP, "pb_bonsai_state_kv: the state's cache is TurboQuant-coded");
   *d_ptr = s->kv + ((size_t)layer * 2 + which) * s->m->c.n_kv * s->max_ctx * BS_HD;
   return PB_OK;
 }
@@ -1231,7 +1307,7 @@ int pb_bs_attn_block(pb_bs_blocks* b, const pb_q1* wq, const pb_q1* wk, const pb
   if ((rc = pb_q1_gemv_launch(wk, b->xq, b->qkv + QD, nullptr, st, true))) return rc;
   if ((rc = pb_q1_gemv_launch(wv, b->xq, b->qkv + QD + KD, nullptr, st, true))) return rc;
   {
-    BsPreArgs a{b->qkv, d_qn, d_kn, b->rope, b->qh, kc, vc, NH, NKV, max_ctx, b->ctl, b->qf};
+    BsPreArgs a{b->qkv, d_qn, d_kn, b->rope, b->qh, kc, vc, NH, NKV, max_ctx, b->ctl, b->qf, nullptr};
     if ((rc = bs_launch(k_bs_attn_pre, dim3(NH + 2 * NKV), 32, 0, st, a, "k_bs_attn_pre"))) return rc;
   }
   {

@@ -100,9 +100,15 @@ int pb_bonsai_state_create_kv(pb_bonsai* m, int max_ctx, uint16_t* d_kv, pb_bons
 // store takes the position from d_npos when it is non-null (graph replays)
 size_t pb_tq_scratch_floats(int nkv, int ctx);
 int pb_tq_store_launch(int bits, const uint16_t* d_rows, const int* d_npos, int npos, uint32_t* kc, float* ks,
-                       uint32_t* vc, float* vs, int nkv, int ctx, cudaStream_t st);
+                       uint32_t* vc, float* vs, int nkv, int ctx, cudaStream_t st, bool pdl);
+// T positions, or (d_npos non-null) *d_npos + 1 read on the device
 int pb_tq_attention_launch(int bits, const float* d_q, const uint32_t* kc, const float* ks, const uint32_t* vc,
-                           const float* vs, int nkv, int ctx, int T, float* d_atto, float* d_scratch, cudaStream_t st);
+                           const float* vs, int nkv, int ctx, int T, const int* d_npos, float* d_atto, float* d_scratch,
+                           cudaStream_t st, bool pdl);
+// per-layer TurboQuant cache sizes: code words per row and bytes per layer
+inline int pb_tq_cw(int b) { return b == 3 ? 12 : 16; }
+inline int pb_tq_bk(int bits) { return bits == 43 ? 4 : bits; }
+inline int pb_tq_bv(int bits) { return bits == 43 ? 3 : bits; }
 
 // one layer's attention block / FFN tail from the caller's host Q8_K
 // activation, for fwd8.c's per-layer hooks (pb_bonsai.cu); blocking

@@ -126,6 +126,8 @@ __global__ void __launch_bounds__(1024) k_tq_store(const uint16_t* __restrict__ 
                                                    int npos_h, uint32_t* __restrict__ kc, float* __restrict__ ks,
                                                    uint32_t* __restrict__ vc, float* __restrict__ vs, int nkv, int ctx) {
   const int w = threadIdx.x >> 5, l = threadIdx.x & 31;
+  pb_grid_wait();
+  pb_grid_launch_dependents();
   if (w >= 2 * nkv) return;
   const int npos = d_npos ? *d_npos : npos_h;
   const uint16_t* row = rows + (size_t)w * 128;
@@ -142,11 +144,16 @@ __global__ void __launch_bounds__(1024) k_tq_store(const uint16_t* __restrict__ 
 // per head a = a + fl(q_r[j] c) over j in order, then the row scale
 template <int B>
 __global__ void __launch_bounds__(256) k_tq_qk(const float* __restrict__ q, const uint32_t* __restrict__ kc,
-                                               const float* __restrict__ ks, float* __restrict__ sc, int ctx, int T) {
+                                               const float* __restrict__ ks, float* __restrict__ sc, int ctx, int T_h,
+                                               const int* __restrict__ d_npos) {
   constexpr int CW = tq_cw(B), NV = 1 << B;
   __shared__ __align__(16) float4 qr[128];   // [j] = the 4 heads' rotated q
   __shared__ float cm[NV];
   const int kh = blockIdx.x, tid = threadIdx.x, w = tid >> 5, l = tid & 31;
+  pb_grid_wait();
+  pb_grid_launch_dependents();
+  const int T = d_npos ? *d_npos + 1 : T_h;
+  if ((int)blockIdx.y * 256 >= T) return;   // block-uniform
   if (w < 4) {   // R q with R's 1/sqrt(128) and the score scale 1/sqrt(128): 2^-7
     const float4 q4 = reinterpret_cast<const float4*>(q + (size_t)(kh * 4 + w) * 128)[l];
     float x[4] = {tq_dsign(q4.x, 4 * l), tq_dsign(q4.y, 4 * l + 1), tq_dsign(q4.z, 4 * l + 2), tq_dsign(q4.w, 4 * l + 3)};
@@ -186,9 +193,13 @@ __global__ void __launch_bounds__(256) k_tq_qk(const float* __restrict__ q, cons
 // per query head (256 threads): the max and the sum of exp(s - max) over
 // thread-strided positions, the warp xor tree, the 8 warps in order; p in
 // place, inv = 1 / sum
-__global__ void __launch_bounds__(256) k_tq_softmax(float* __restrict__ sc, float* __restrict__ inv, int ctx, int T) {
+__global__ void __launch_bounds__(256) k_tq_softmax(float* __restrict__ sc, float* __restrict__ inv, int ctx, int T_h,
+                                                    const int* __restrict__ d_npos) {
   __shared__ float red[8];
   const int h = blockIdx.x, tid = threadIdx.x, l = tid & 31, w = tid >> 5;
+  pb_grid_wait();
+  pb_grid_launch_dependents();
+  const int T = d_npos ? *d_npos + 1 : T_h;
   float* s = sc + (size_t)h * ctx;
   float m = -INFINITY;
   for (int t = tid; t < T; t += 256) m = fmaxf(m, s[t]);
@@ -222,12 +233,15 @@ __global__ void __launch_bounds__(256) k_tq_softmax(float* __restrict__ sc, floa
 template <int B>
 __global__ void __launch_bounds__(128) k_tq_pv(const float* __restrict__ p, const uint32_t* __restrict__ vc,
                                                const float* __restrict__ vs, float* __restrict__ part, int nh, int ctx,
-                                               int T) {
+                                               int T_h, const int* __restrict__ d_npos) {
   constexpr int CW = tq_cw(B), NV = 1 << B;
   __shared__ __align__(16) float4 wt[TQ_CH];
   __shared__ float cent[NV];
   __shared__ __align__(16) float red[3][4][128];
   const int kh = blockIdx.x, c = blockIdx.y, tid = threadIdx.x, w = tid >> 5, l = tid & 31;
+  pb_grid_wait();
+  pb_grid_launch_dependents();
+  const int T = d_npos ? *d_npos + 1 : T_h;
   const int t0 = c * TQ_CH, n = min(TQ_CH, T - t0);
   if (n <= 0) return;   // block-uniform
   if (tid < NV) cent[tid] = tq_cent(B, tid);
@@ -288,8 +302,11 @@ __global__ void __launch_bounds__(128) k_tq_pv(const float* __restrict__ p, cons
 // per query head (one warp): the chunks summed in order from 0, R^T (H, the
 // 1/sqrt(128) and 1/sum, then D)
 __global__ void __launch_bounds__(32) k_tq_out(const float* __restrict__ part, const float* __restrict__ inv,
-                                               float* __restrict__ atto, int nh, int T) {
+                                               float* __restrict__ atto, int nh, int T_h, const int* __restrict__ d_npos) {
   const int h = blockIdx.x, l = threadIdx.x;
+  pb_grid_wait();
+  pb_grid_launch_dependents();
+  const int T = d_npos ? *d_npos + 1 : T_h;
   const int nc = (T + TQ_CH - 1) / TQ_CH;
   float x[4] = {0.0f, 0.0f, 0.0f, 0.0f};
   for (int c = 0; c < nc; c++) {
@@ -308,8 +325,18 @@ int tq_bk(int bits) { return bits == 43 ? 4 : bits; }
 int tq_bv(int bits) { return bits == 43 ? 3 : bits; }
 bool tq_bits_ok(int bits) { return bits == 3 || bits == 4 || bits == 43; }
 
-int tq_launched(const char* name) {
-  cudaError_t e = cudaGetLastError();
+template <typename... KArgs, typename... Args>
+int tq_launch(void (*k)(KArgs...), dim3 grid, int block, cudaStream_t st, bool pdl, const char* name, Args... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = dim3(block);
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl ? 1 : 0;
+  cudaError_t e = cudaLaunchKernelEx(&cfg, k, args...);
   if (e != cudaSuccess) return pb_set_error(PB_ECUDA, "%s: %s", name, cudaGetErrorString(e));
   pb_count_launch();
   return PB_OK;
@@ -322,47 +349,48 @@ size_t pb_tq_scratch_floats(int nkv, int ctx) {
   return (size_t)nh * ctx + (size_t)nch * nh * 128 + nh;
 }
 
-// device npos (d_npos, when non-null) lets a captured graph store at the
-// position of each replay
+// device npos (d_npos, when non-null) lets a captured graph store at, and
+// attend up to, the position of each replay; pdl: programmatic dependent
+// launch (every kernel waits for its predecessor before touching its data)
 int pb_tq_store_launch(int bits, const uint16_t* d_rows, const int* d_npos, int npos, uint32_t* kc, float* ks,
-                       uint32_t* vc, float* vs, int nkv, int ctx, cudaStream_t st) {
+                       uint32_t* vc, float* vs, int nkv, int ctx, cudaStream_t st, bool pdl) {
   if (!tq_bits_ok(bits) || nkv <= 0 || nkv > 16 || ctx <= 0 || (!d_npos && (npos < 0 || npos >= ctx)))
     return pb_set_error(PB_EINVAL, "pb_tq_store: bits %d (3, 4 or 43), n_kv %d (1..16), position %d of %d", bits, nkv,
                         npos, ctx);
-  if (bits == 3) k_tq_store<3, 3><<<1, 64 * nkv, 0, st>>>(d_rows, d_npos, npos, kc, ks, vc, vs, nkv, ctx);
-  else if (bits == 4) k_tq_store<4, 4><<<1, 64 * nkv, 0, st>>>(d_rows, d_npos, npos, kc, ks, vc, vs, nkv, ctx);
-  else k_tq_store<4, 3><<<1, 64 * nkv, 0, st>>>(d_rows, d_npos, npos, kc, ks, vc, vs, nkv, ctx);
-  return tq_launched("k_tq_store");
+  const dim3 g(1);
+  if (bits == 3) return tq_launch(k_tq_store<3, 3>, g, 64 * nkv, st, pdl, "k_tq_store", d_rows, d_npos, npos, kc, ks, vc, vs, nkv, ctx);
+  if (bits == 4) return tq_launch(k_tq_store<4, 4>, g, 64 * nkv, st, pdl, "k_tq_store", d_rows, d_npos, npos, kc, ks, vc, vs, nkv, ctx);
+  return tq_launch(k_tq_store<4, 3>, g, 64 * nkv, st, pdl, "k_tq_store", d_rows, d_npos, npos, kc, ks, vc, vs, nkv, ctx);
 }
 
+// T positions (host), or d_npos + 1 (device, grids sized for ctx)
 int pb_tq_attention_launch(int bits, const float* d_q, const uint32_t* kc, const float* ks, const uint32_t* vc,
-                           const float* vs, int nkv, int ctx, int T, float* d_atto, float* d_scratch, cudaStream_t st) {
-  if (!tq_bits_ok(bits) || nkv <= 0 || ctx <= 0 || T <= 0 || T > ctx || !d_q || !d_atto || !d_scratch)
+                           const float* vs, int nkv, int ctx, int T, const int* d_npos, float* d_atto, float* d_scratch,
+                           cudaStream_t st, bool pdl) {
+  if (!tq_bits_ok(bits) || nkv <= 0 || ctx <= 0 || (!d_npos && (T <= 0 || T > ctx)) || !d_q || !d_atto || !d_scratch)
     return pb_set_error(PB_EINVAL, "pb_tq_attention: bits %d, n_kv %d, T %d of %d", bits, nkv, T, ctx);
-  const int nh = 4 * nkv, bk = tq_bk(bits), bv = tq_bv(bits), nch = (T + TQ_CH - 1) / TQ_CH;
+  const int nh = 4 * nkv, bk = tq_bk(bits), bv = tq_bv(bits);
+  const int span = d_npos ? ctx : T, nch = (span + TQ_CH - 1) / TQ_CH;
   float* sc = d_scratch;
   float* part = sc + (size_t)nh * ctx;
   float* inv = part + (size_t)((ctx + TQ_CH - 1) / TQ_CH) * nh * 128;
-  const dim3 gq((unsigned)nkv, (unsigned)((T + 255) / 256));
-  if (bk == 3) k_tq_qk<3><<<gq, 256, 0, st>>>(d_q, kc, ks, sc, ctx, T);
-  else k_tq_qk<4><<<gq, 256, 0, st>>>(d_q, kc, ks, sc, ctx, T);
-  int rc;
-  if ((rc = tq_launched("k_tq_qk"))) return rc;
-  k_tq_softmax<<<nh, 256, 0, st>>>(sc, inv, ctx, T);
-  if ((rc = tq_launched("k_tq_softmax"))) return rc;
+  const dim3 gq((unsigned)nkv, (unsigned)((span + 255) / 256));
+  int rc = bk == 3 ? tq_launch(k_tq_qk<3>, gq, 256, st, pdl, "k_tq_qk", d_q, (const uint32_t*)kc, ks, sc, ctx, T, d_npos)
+                   : tq_launch(k_tq_qk<4>, gq, 256, st, pdl, "k_tq_qk", d_q, (const uint32_t*)kc, ks, sc, ctx, T, d_npos);
+  if (rc) return rc;
+  if ((rc = tq_launch(k_tq_softmax, dim3(nh), 256, st, pdl, "k_tq_softmax", sc, inv, ctx, T, d_npos))) return rc;
   const dim3 gp((unsigned)nkv, (unsigned)nch);
-  if (bv == 3) k_tq_pv<3><<<gp, 128, 0, st>>>(sc, vc, vs, part, nh, ctx, T);
-  else k_tq_pv<4><<<gp, 128, 0, st>>>(sc, vc, vs, part, nh, ctx, T);
-  if ((rc = tq_launched("k_tq_pv"))) return rc;
-  k_tq_out<<<nh, 32, 0, st>>>(part, inv, d_atto, nh, T);
-  return tq_launched("k_tq_out");
+  rc = bv == 3 ? tq_launch(k_tq_pv<3>, gp, 128, st, pdl, "k_tq_pv", (const float*)sc, (const uint32_t*)vc, vs, part, nh, ctx, T, d_npos)
+               : tq_launch(k_tq_pv<4>, gp, 128, st, pdl, "k_tq_pv", (const float*)sc, (const uint32_t*)vc, vs, part, nh, ctx, T, d_npos);
+  if (rc) return rc;
+  return tq_launch(k_tq_out, dim3(nh), 32, st, pdl, "k_tq_out", (const float*)part, (const float*)inv, d_atto, nh, T, d_npos);
 }
 
 extern "C" int pb_tq_store(int bits, const uint16_t* d_rows, int npos, uint32_t* d_kcode, float* d_kscale,
                            uint32_t* d_vcode, float* d_vscale, int nkv, int ctx, void* stream) {
   if (!d_rows || !d_kcode || !d_kscale || !d_vcode || !d_vscale) return pb_set_error(PB_EINVAL, "pb_tq_store: null argument");
   return pb_tq_store_launch(bits, d_rows, nullptr, npos, d_kcode, d_kscale, d_vcode, d_vscale, nkv, ctx,
-                            (cudaStream_t)stream);
+                            (cudaStream_t)stream, false);
 }
 
 extern "C" long long pb_tq_scratch_bytes(int nkv, int ctx) {
@@ -373,6 +401,6 @@ extern "C" int pb_tq_attention(int bits, const float* d_q, const uint32_t* d_kco
                                const uint32_t* d_vcode, const float* d_vscale, int nkv, int ctx, int T, float* d_atto,
                                void* d_scratch, void* stream) {
   if (!d_kcode || !d_kscale || !d_vcode || !d_vscale) return pb_set_error(PB_EINVAL, "pb_tq_attention: null argument");
-  return pb_tq_attention_launch(bits, d_q, d_kcode, d_kscale, d_vcode, d_vscale, nkv, ctx, T, d_atto,
-                                static_cast<float*>(d_scratch), (cudaStream_t)stream);
+  return pb_tq_attention_launch(bits, d_q, d_kcode, d_kscale, d_vcode, d_vscale, nkv, ctx, T, nullptr, d_atto,
+                                static_cast<float*>(d_scratch), (cudaStream_t)stream, false);
 }

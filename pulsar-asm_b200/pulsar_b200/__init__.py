@@ -122,6 +122,7 @@ def lib():
     L.pb_bonsai_set_q1.argtypes = [vp, i, i, vp, i, vp]
     L.pb_bonsai_set_norm.argtypes = [vp, i, i, vp, i, vp]
     L.pb_bonsai_state_create.argtypes = [vp, i, pvp]
+    L.pb_bonsai_state_create_tq.argtypes = [vp, i, i, pvp]
     L.pb_bonsai_state_destroy.argtypes = [vp]
     L.pb_bonsai_state_kv.argtypes = [vp, i, i, pvp]
     L.pb_bonsai_state_residual.argtypes = [vp, vp, vp]
@@ -559,8 +560,8 @@ class Bonsai:
         check(lib().pb_bonsai_set_norm(self.h, layer, slot, a.ctypes.data_as(C.c_void_p), 0,
                                        st if st is not None else _stream()))
 
-    def new_state(self, max_ctx):
-        return BonsaiState(self, max_ctx)
+    def new_state(self, max_ctx, kv_bits=0):
+        return BonsaiState(self, max_ctx, kv_bits)
 
     def close(self):
         if self.h:
@@ -575,12 +576,16 @@ class Bonsai:
 
 
 class BonsaiState:
-    """One sequence: f16 K/V cache and rope table (pb_bonsai_state)."""
+    """One sequence: K/V cache (f16, or TurboQuant-coded when kv_bits is 3, 4
+    or 43) and rope table (pb_bonsai_state)."""
 
-    def __init__(self, model, max_ctx):
+    def __init__(self, model, max_ctx, kv_bits=0):
         h = C.c_void_p()
-        check(lib().pb_bonsai_state_create(model.h, max_ctx, C.byref(h)))
-        self.h, self.model, self.max_ctx = h, model, max_ctx
+        if kv_bits:
+            check(lib().pb_bonsai_state_create_tq(model.h, max_ctx, int(kv_bits), C.byref(h)))
+        else:
+            check(lib().pb_bonsai_state_create(model.h, max_ctx, C.byref(h)))
+        self.h, self.model, self.max_ctx, self.kv_bits = h, model, max_ctx, kv_bits
 
     def decode(self, token, pos, x=None, logits=None, want_id=True, stream=None):
         """one token; returns the greedy id (synchronises) when want_id."""

@@ -200,14 +200,19 @@ def make_bonsai_weights(c, seed=4321, tied=True):
                 out_norm=norm(H))
 
 
-def bonsai_bytes_per_token(c, ctx):
+def bonsai_bytes_per_token(c, ctx, kv_bits=0):
     """algorithmic bytes of one decode token at context ctx: every Q1_0 tensor
-    (18 B per 128 weights), the norm vectors, the head once, and the f16 K and
-    V rows the attention reads"""
+    (18 B per 128 weights), the norm vectors, the head once, and the K and V
+    rows the attention reads (f16: 256 B per row; TurboQuant: 48 or 64 B of
+    codes and a 4 B scale)"""
     H, F, NH, NKV, L = c["hidden"], c["inter"], c["n_heads"], c["n_kv"], c["n_layers"]
 
     def q(rows, K):
         return rows * (K // 128) * 18
     layer = q((NH + 2 * NKV) * 128, H) + q(H, NH * 128) + 2 * q(F, H) + q(H, F) + (2 * H + 256) * 4
-    kv = 2 * NKV * ctx * 128 * 2
+    if kv_bits:
+        bk, bv = (4, 3) if kv_bits == 43 else (kv_bits, kv_bits)
+        kv = NKV * ctx * ((12 if bk == 3 else 16) * 4 + 4 + (12 if bv == 3 else 16) * 4 + 4)
+    else:
+        kv = 2 * NKV * ctx * 128 * 2
     return L * (layer + kv) + q(c["vocab"], H) + H * 4

@@ -110,3 +110,30 @@ def test_bonsai_greedy_and_caller_row(oracle, pb, cuda):
     assert s2.fallbacks() > before
     assert np.array_equal(_bits(lg.cpu().numpy()), _bits(lw))
     assert got == want_id
+
+
+@pytest.mark.parametrize("bits", [4, 3, 43])
+def test_bonsai_turboquant_cache(oracle, pb, cuda, bits):
+    """the decoder with a TurboQuant K/V cache (pb_bonsai_state_create_tq, the
+    reference glue's default PQ1_KVTQ=4) against the oracle's token step with
+    the same cache, bit for bit: logits and greedy ids over 300 positions
+    (beyond one 256-position chunk of the V sum)"""
+    torch = cuda
+    from pulsar_b200 import synth
+    c = dict(synth.BONSAI_TINY)
+    max_ctx = 320
+    w = synth.make_bonsai_weights(c, seed=77)
+    m, om = pb.Bonsai(c, w), oracle.BsModel(c, w, max_ctx, kv_bits=bits)
+    s = m.new_state(max_ctx, kv_bits=bits)
+    rng = np.random.default_rng(bits)
+    toks = rng.integers(0, c["vocab"], 300)
+    lg = torch.empty(c["vocab"], dtype=torch.float32, device="cuda")
+    for pos, tok in enumerate(toks):
+        got = s.decode(int(tok), pos, logits=lg)
+        want, lw, _ = om.decode(int(tok), pos, want_logits=True)
+        torch.cuda.synchronize()
+        assert np.array_equal(_bits(lg.cpu().numpy()), _bits(lw)), "logits differ at position %d" % pos
+        assert got == want
+    s.status()
+    with pytest.raises(pb.PBError):
+        s.kv(0, 0)     # no f16 cache to view
