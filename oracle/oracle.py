@@ -103,6 +103,7 @@ def lib():
         L.pbo_bs_model_set_f32.argtypes = [vp, i, i, vp]
         L.pbo_bs_state_new.restype = vp; L.pbo_bs_state_new.argtypes = [vp]
         L.pbo_bs_state_new_tq.restype = vp; L.pbo_bs_state_new_tq.argtypes = [vp, i]
+        L.pbo_bs_state_tq_recode.argtypes = [vp, vp, i]
         L.pbo_bs_state_free.argtypes = [vp]
         L.pbo_bs_state_kv.restype = vp; L.pbo_bs_state_kv.argtypes = [vp, i, i]
         L.pbo_bs_decode.restype = i; L.pbo_bs_decode.argtypes = [vp, vp, i, i, vp, vp, vp]
@@ -412,6 +413,10 @@ class BsModel:
         a = np.ascontiguousarray(a, np.uint16)
         assert a.size == c["n_kv"] * self.max_ctx * 128
         C.memmove(lib().pbo_bs_state_kv(self.s, layer, which), a.ctypes.data, a.nbytes)
+
+    def tq_recode(self, n):
+        """a TurboQuant state: code positions < n again from the f16 rows (after set_kv)"""
+        lib().pbo_bs_state_tq_recode(self.s, self.m, int(n))
 
     def __del__(self):
         try:

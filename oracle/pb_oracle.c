@@ -820,6 +820,21 @@ pbo_bs_state* pbo_bs_state_new_tq(const pbo_bs_model* m, int bits) {
   }
   return s;
 }
+/* a TurboQuant state's codes of positions < n recoded from its f16 rows (for
+ * a cache loaded with pbo_bs_state_kv's arrays) */
+void pbo_bs_state_tq_recode(pbo_bs_state* s, const pbo_bs_model* m, int n) {
+  if (!s->tq) return;
+  const pbo_bs_cfg* c = &m->cfg;
+  const int bk = s->tq == 43 ? 4 : s->tq, bv = s->tq == 43 ? 3 : s->tq;
+  const int cwk = bk == 3 ? 12 : 16, cwv = bv == 3 ? 12 : 16;
+  for (int L = 0; L < c->n_layers; L++)
+    for (int kh = 0; kh < c->n_kv; kh++)
+      for (int t = 0; t < n; t++) {
+        const size_t r = (size_t)kh * c->max_ctx + t;
+        pbo_tq_row(s->kc[L] + r * 128, bk, s->tkc[L] + r * cwk, s->tks[L] + r);
+        pbo_tq_row(s->vc[L] + r * 128, bv, s->tvc[L] + r * cwv, s->tvs[L] + r);
+      }
+}
 void pbo_bs_state_free(pbo_bs_state* s) {
   if (!s) return;
   if (s->tq) {

@@ -144,6 +144,7 @@ pbo_bs_state* pbo_bs_state_new(const pbo_bs_model* m);
  * each position's f16 K/V rows are coded at their store, and attention runs
  * over the codes (pbo_tq_attn) */
 pbo_bs_state* pbo_bs_state_new_tq(const pbo_bs_model* m, int bits);
+void pbo_bs_state_tq_recode(pbo_bs_state* s, const pbo_bs_model* m, int n);
 void pbo_bs_state_free(pbo_bs_state* s);
 const uint16_t* pbo_bs_state_kv(const pbo_bs_state* s, int layer, int which);
 int pbo_bs_decode(const pbo_bs_model* m, pbo_bs_state* s, int token, int pos, const float* x_in,

@@ -987,7 +987,8 @@ extern "C" int pb_bonsai_set_norm(pb_bonsai* m, int layer, int slot, const float
 }
 
 namespace {
-int bs_state_create(pb_bonsai* m, int max_ctx, uint16_t* kv_ext, int kv_bits, pb_bonsai_state** out) {
+int bs_state_create(pb_bonsai* m, int max_ctx, uint16_t* kv_ext, int kv_bits, const PbTqCache* tq_ext,
+                    pb_bonsai_state** out) {
   if (!m || !out || max_ctx <= 0 || max_ctx % 32) return pb_set_error(PB_EINVAL, "pb_bonsai_state_create: bad argument (max_ctx a positive multiple of 32)");
   *out = nullptr;
   if (pv_smem(max_ctx) > 200 * 1024) return pb_set_error(PB_ENOTSUP, "pb_bonsai_state_create: max_ctx %d too large for the attention kernel (<= 8192)", max_ctx);
@@ -1035,8 +1036,8 @@ int bs_state_create(pb_bonsai* m, int max_ctx, uint16_t* kv_ext, int kv_bits, pb
   s->ctl = reinterpret_cast<BsCtl*>(take());
   int rc = PB_OK;
   if (cudaMemset(s->mem, 0, tot) != cudaSuccess) rc = pb_set_error(PB_ECUDA, "pb_bonsai_state_create: memset");
-  if (rc == PB_OK && kv_bits) {   // the TurboQuant cache and its scratch, in a second allocation
-    const size_t rows = (size_t)c.n_layers * NKV * max_ctx;
+  if (rc == PB_OK && kv_bits) {   // the TurboQuant cache (unless the caller's) and its scratch, in a second allocation
+    const size_t rows = tq_ext ? 0 : (size_t)c.n_layers * NKV * max_ctx;
     const size_t tsz[] = {rows * pb_tq_cw(pb_tq_bk(kv_bits)) * 4, rows * pb_tq_cw(pb_tq_bv(kv_bits)) * 4, rows * 4,
                           rows * 4, (size_t)2 * NKV * BS_HD * 2, (size_t)m->QD * 4,
                           pb_tq_scratch_floats(NKV, max_ctx) * 4};
@@ -1056,6 +1057,7 @@ int bs_state_create(pb_bonsai* m, int max_ctx, uint16_t* kv_ext, int kv_bits, pb
       s->tq_stage = reinterpret_cast<uint16_t*>(tk());
       s->tq_qf = reinterpret_cast<float*>(tk());
       s->tq_scratch = reinterpret_cast<float*>(tk());
+      if (tq_ext) { s->tq_kc = tq_ext->kc; s->tq_vc = tq_ext->vc; s->tq_ks = tq_ext->ks; s->tq_vs = tq_ext->vs; }
       s->kv_bits = kv_bits;
     }
   }
@@ -1078,14 +1080,20 @@ int bs_state_create(pb_bonsai* m, int max_ctx, uint16_t* kv_ext, int kv_bits, pb
 }  // namespace
 
 extern "C" int pb_bonsai_state_create(pb_bonsai* m, int max_ctx, pb_bonsai_state** out) {
-  return bs_state_create(m, max_ctx, nullptr, 0, out);
+  return bs_state_create(m, max_ctx, nullptr, 0, nullptr, out);
 }
 extern "C" int pb_bonsai_state_create_tq(pb_bonsai* m, int max_ctx, int kv_bits, pb_bonsai_state** out) {
-  return bs_state_create(m, max_ctx, nullptr, kv_bits, out);
+  return bs_state_create(m, max_ctx, nullptr, kv_bits, nullptr, out);
 }
 int pb_bonsai_state_create_kv(pb_bonsai* m, int max_ctx, uint16_t* d_kv, pb_bonsai_state** out) {
   if (!d_kv) return pb_set_error(PB_EINVAL, "pb_bonsai_state_create_kv: null cache");
-  return bs_state_create(m, max_ctx, d_kv, 0, out);
+  return bs_state_create(m, max_ctx, d_kv, 0, nullptr, out);
+}
+int pb_bonsai_state_create_tq_ext(pb_bonsai* m, int max_ctx, int kv_bits, const PbTqCache* cache,
+                                  pb_bonsai_state** out) {
+  if (!cache || !cache->kc || !cache->vc || !cache->ks || !cache->vs || !kv_bits)
+    return pb_set_error(PB_EINVAL, "pb_bonsai_state_create_tq_ext: bad cache");
+  return bs_state_create(m, max_ctx, nullptr, kv_bits, cache, out);
 }
 
 extern "C" int pb_bonsai_state_destroy(pb_bonsai_state* s) {
@@ -1194,6 +1202,11 @@ struct pb_bs_blocks {
   uint16_t* qh = nullptr;
   uint8_t* xq = nullptr;   // Q8_K of the block input, then of the attention output
   BsCtl* ctl = nullptr;
+  // TurboQuant attention (tq_bits != 0): the current rows, scratch
+  int tq_bits = 0, tq_ctx = 0, tq_nkv = 0;
+  char* tmem = nullptr;
+  uint16_t* stage = nullptr;
+  float* tq_scratch = nullptr;
   // FFN tail
   int fH = 0, F = 0;
   char* fmem = nullptr;
@@ -1276,6 +1289,7 @@ void pb_bs_blocks_destroy(pb_bs_blocks* b) {
   if (!b) return;
   cudaSetDevice(b->device);
   cudaFree(b->amem);
+  cudaFree(b->tmem);
   cudaFree(b->fmem);
   delete b;
 }
@@ -1324,6 +1338,63 @@ int pb_bs_attn_block(pb_bs_blocks* b, const pb_q1* wq, const pb_q1* wk, const pb
   PB_TRY_CUDA(cudaMemcpyAsync(&err, &b->ctl->err, sizeof(int), cudaMemcpyDeviceToHost, st));
   PB_TRY_CUDA(cudaStreamSynchronize(st));
   if (err) return pb_set_error(PB_ECUDA, "pb_bs_attn_block: a bounded wait in the attention kernel gave up");
+  return PB_OK;
+}
+
+// the attention block over a TurboQuant cache: the layer's K/V rows of npos are
+// coded into it, then the attention runs over the codes (the reference's
+// pq1_attn_tq_launch inside pq1_attn_fused)
+int pb_bs_attn_block_tq(pb_bs_blocks* b, int bits, const pb_q1* wq, const pb_q1* wk, const pb_q1* wv, const pb_q1* wo,
+                        const float* d_qn, const float* d_kn, const PbTqCache* layer, int max_ctx, int npos,
+                        const float* h_cos, const float* h_sin, const uint8_t* h_xq, float* h_ao, cudaStream_t st) {
+  if (!b || !wq || !wk || !wv || !wo || !d_qn || !d_kn || !layer || !h_cos || !h_sin || !h_xq || !h_ao)
+    return pb_set_error(PB_EINVAL, "pb_bs_attn_block_tq: null argument");
+  const int H = wq->K, QD = wq->rows, KD = wk->rows, NH = QD / BS_HD, NKV = KD / BS_HD;
+  if (H % 256 || H > 8192 || QD % 256 || KD % BS_HD || NKV <= 0 || NKV > 16 || NH != 4 * NKV || wk->K != H ||
+      wv->K != H || wv->rows != KD || wo->rows != H || wo->K != QD)
+    return pb_set_error(PB_EINVAL, "pb_bs_attn_block_tq: shapes q %dx%d k %dx%d (n_heads = 4 n_kv)", wq->rows, wq->K,
+                        wk->rows, wk->K);
+  if (max_ctx <= 0 || max_ctx % 32 || npos < 0 || npos >= max_ctx)
+    return pb_set_error(PB_EINVAL, "pb_bs_attn_block_tq: position %d, cache of %d", npos, max_ctx);
+  PB_TRY_CUDA(cudaSetDevice(b->device));
+  int rc;
+  if ((rc = bs_blocks_attn_alloc(b, H, NH, NKV, max_ctx))) return rc;
+  if (!b->tmem || b->tq_ctx != max_ctx || b->tq_nkv != NKV) {
+    cudaFree(b->tmem);
+    b->tmem = nullptr;
+    const size_t sz[] = {(size_t)2 * NKV * BS_HD * 2, pb_tq_scratch_floats(NKV, max_ctx) * 4};
+    char* parts[2];
+    if ((rc = bs_carve(sz, 2, &b->tmem, parts))) return rc;
+    b->stage = reinterpret_cast<uint16_t*>(parts[0]);
+    b->tq_scratch = reinterpret_cast<float*>(parts[1]);
+    b->tq_ctx = max_ctx;
+    b->tq_nkv = NKV;
+  }
+  const int hdr[4] = {0, npos, 0, 0};
+  PB_TRY_CUDA(cudaMemcpyAsync(b->ctl, hdr, sizeof hdr, cudaMemcpyHostToDevice, st));
+  PB_TRY_CUDA(cudaMemcpyAsync(b->rope + (size_t)npos * BS_HD, h_cos, 64 * 4, cudaMemcpyHostToDevice, st));
+  PB_TRY_CUDA(cudaMemcpyAsync(b->rope + (size_t)npos * BS_HD + 64, h_sin, 64 * 4, cudaMemcpyHostToDevice, st));
+  PB_TRY_CUDA(cudaMemcpyAsync(b->xq, h_xq, (size_t)(H / 256) * 292, cudaMemcpyHostToDevice, st));
+  if ((rc = pb_q1_gemv_launch(wq, b->xq, b->qkv, nullptr, st, true))) return rc;
+  if ((rc = pb_q1_gemv_launch(wk, b->xq, b->qkv + QD, nullptr, st, true))) return rc;
+  if ((rc = pb_q1_gemv_launch(wv, b->xq, b->qkv + QD + KD, nullptr, st, true))) return rc;
+  {
+    BsPreArgs a{b->qkv, d_qn, d_kn, b->rope, b->qh, nullptr, nullptr, NH, NKV, max_ctx, b->ctl, b->qf, b->stage};
+    if ((rc = bs_launch(k_bs_attn_pre, dim3(NH + 2 * NKV), 32, 0, st, a, "k_bs_attn_pre"))) return rc;
+  }
+  if ((rc = pb_tq_store_launch(bits, b->stage, nullptr, npos, layer->kc, layer->ks, layer->vc, layer->vs, NKV, max_ctx,
+                               st, true)))
+    return rc;
+  if ((rc = pb_tq_attention_launch(bits, b->qf, layer->kc, layer->ks, layer->vc, layer->vs, NKV, max_ctx, npos + 1,
+                                   nullptr, b->atto, b->tq_scratch, st, true)))
+    return rc;
+  {
+    BsQ8kArgs a{b->atto, b->xq};
+    if ((rc = bs_launch(k_bs_q8k, dim3(QD / 256), 256, 0, st, a, "k_bs_q8k"))) return rc;
+  }
+  if ((rc = pb_q1_gemv_launch(wo, b->xq, b->ao, nullptr, st, true))) return rc;
+  PB_TRY_CUDA(cudaMemcpyAsync(h_ao, b->ao, (size_t)H * 4, cudaMemcpyDeviceToHost, st));
+  PB_TRY_CUDA(cudaStreamSynchronize(st));
   return PB_OK;
 }
 

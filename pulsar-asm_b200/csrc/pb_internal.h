@@ -95,6 +95,15 @@ const float* pb_bonsai_state_logits(const pb_bonsai_state* s);
 // a state over a K/V cache the caller owns ([layer][2][n_kv][max_ctx][128]
 // f16, not freed with the state)
 int pb_bonsai_state_create_kv(pb_bonsai* m, int max_ctx, uint16_t* d_kv, pb_bonsai_state** out);
+// a TurboQuant cache the caller owns: all layers' code words and scales
+// ([layer][n_kv][max_ctx][CW], [layer][n_kv][max_ctx]); per layer, the same
+// four pointers advanced to that layer
+struct PbTqCache {
+  uint32_t *kc = nullptr, *vc = nullptr;
+  float *ks = nullptr, *vs = nullptr;
+};
+int pb_bonsai_state_create_tq_ext(pb_bonsai* m, int max_ctx, int kv_bits, const PbTqCache* cache,
+                                  pb_bonsai_state** out);
 
 // TurboQuant K/V cache (pb_tq.cu): bits 3, 4 or 43 (4-bit K, 3-bit V); the
 // store takes the position from d_npos when it is non-null (graph replays)
@@ -119,6 +128,9 @@ int pb_bs_attn_block(pb_bs_blocks* b, const pb_q1* wq, const pb_q1* wk, const pb
                      const float* d_qn, const float* d_kn, uint16_t* kc, uint16_t* vc, int max_ctx, int npos,
                      float attn_scale, const float* h_cos, const float* h_sin, const uint8_t* h_xq, float* h_ao,
                      cudaStream_t st);
+int pb_bs_attn_block_tq(pb_bs_blocks* b, int bits, const pb_q1* wq, const pb_q1* wk, const pb_q1* wv, const pb_q1* wo,
+                        const float* d_qn, const float* d_kn, const PbTqCache* layer, int max_ctx, int npos,
+                        const float* h_cos, const float* h_sin, const uint8_t* h_xq, float* h_ao, cudaStream_t st);
 int pb_bs_ffn_block(pb_bs_blocks* b, const pb_q1* wg, const pb_q1* wu, const pb_q1* wd, const uint8_t* h_xq,
                     float* h_fo, cudaStream_t st);
 // the last attention block's post-rope q and attention output (fp32 [nh][128]);

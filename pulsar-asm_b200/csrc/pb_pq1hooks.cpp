@@ -27,8 +27,10 @@
 //   pq1_attn_dbg / pq1_ffn_dbg_xq   the device's values of the last block for
 //                                fwd8's PQ1_ATT_CHECK / PQ1_FFN_CHECK;
 //   pq1_silu_mul, pq1_gpu_stats_mb   the shim's two host helpers.
-// Per-layer tensors are keyed by their host pointers, as the reference's glue
-// keys them; the whole-token path keeps its own copy of the weight set. A
+// The cache is f16, or TurboQuant-coded when PQ1_KVTQ is 3, 4 or 43 (unset:
+// 4, the reference glue's default; 0: the exact f16 cache), read when a
+// session's cache is made. Per-layer tensors are keyed by their host
+// pointers, as the reference's glue keys them; the whole-token path keeps its own copy of the weight set. A
 // session's K/V cache belongs to the session, so the per-layer hooks, the
 // mirrored rows and the whole-token path all continue one cache.
 // As in the reference, a hook declines (returns -1, the caller runs its own
@@ -40,6 +42,7 @@
 
 #include <cmath>
 #include <cstdio>
+#include <cstdlib>
 #include <cstring>
 #include <map>
 #include <mutex>
@@ -51,9 +54,13 @@ namespace {
 constexpr float kAttnScale = 0.0883883476f;
 
 struct HookSession {
-  pb_bonsai_state* st = nullptr;   // the whole-token path's state, over kv
-  uint16_t* kv = nullptr;          // [nl][2][nkv][mc][128] f16
+  pb_bonsai_state* st = nullptr;   // the whole-token path's state, over the session's cache
+  uint16_t* kv = nullptr;          // f16 cache: [nl][2][nkv][mc][128]
   int nl = 0, nkv = 0, mc = 0;     // the cache's shape
+  int tq = 0;                      // TurboQuant bits (3, 4, 43), 0 for the f16 cache
+  char* tq_mem = nullptr;          // TurboQuant cache: codes and scales of every layer, then 2 nkv staged rows
+  PbTqCache tqc;                   // its layer-0 pointers ([layer][nkv][mc][CW], [layer][nkv][mc])
+  uint16_t* stage = nullptr;       // [2 nkv][128] f16 rows put by the host
   std::vector<int> next;           // per layer: the position its cache takes next
 };
 
@@ -84,6 +91,26 @@ struct Hooks {
 Hooks g_h;
 
 int cache_len(int ctx) { return (ctx + 31) / 32 * 32; }
+
+// PQ1_KVTQ as the reference's glue reads it (pq1_fwd8_glue.c:219-229): 3, 4
+// or 43 codes the cache with TurboQuant, anything else is the f16 cache; unset
+// is 4, the reference's default. Read when a session's cache is made.
+int kv_mode() {
+  const char* e = getenv("PQ1_KVTQ");
+  const int v = e ? atoi(e) : 4;
+  return (v == 3 || v == 4 || v == 43) ? v : 0;
+}
+
+// layer il's TurboQuant code and scale arrays
+PbTqCache tq_layer(const HookSession& S, int il) {
+  const size_t rows = (size_t)S.nkv * S.mc;
+  PbTqCache c;
+  c.kc = S.tqc.kc + (size_t)il * rows * pb_tq_cw(pb_tq_bk(S.tq));
+  c.vc = S.tqc.vc + (size_t)il * rows * pb_tq_cw(pb_tq_bv(S.tq));
+  c.ks = S.tqc.ks + (size_t)il * rows;
+  c.vs = S.tqc.vs + (size_t)il * rows;
+  return c;
+}
 
 bool ensure_stream() {
   if (g_h.stream) return true;
@@ -166,17 +193,43 @@ bool ensure_kv(HookSession& S) {
     pb_set_error(PB_EINVAL, "pq1 hooks: the cache shape changed after the cache was made");
     return false;
   }
+  if (S.tq_mem) {
+    if (S.nl == g_h.nl && S.nkv == g_h.nkv && S.mc == mc) return true;
+    pb_set_error(PB_EINVAL, "pq1 hooks: the cache shape changed after the cache was made");
+    return false;
+  }
   if (g_h.nl <= 0 || g_h.nkv <= 0 || mc <= 0 || mc > 8192) {
     pb_set_error(PB_EINVAL, "pq1 hooks: cache shape %d x %d x %d", g_h.nl, g_h.nkv, g_h.ctx);
     return false;
   }
-  const size_t bytes = (size_t)g_h.nl * 2 * g_h.nkv * mc * 128 * 2;
-  if (cudaMalloc(&S.kv, bytes) != cudaSuccess || cudaMemset(S.kv, 0, bytes) != cudaSuccess) {
-    cudaGetLastError();
-    if (S.kv) cudaFree(S.kv);
-    S.kv = nullptr;
-    pb_set_error(PB_ENOMEM, "pq1 hooks: K/V cache of %zu bytes", bytes);
-    return false;
+  const int tq = g_h.nkv <= 16 ? kv_mode() : 0;
+  if (tq) {   // codes and scales of every layer, then the staged rows
+    const size_t rows = (size_t)g_h.nl * g_h.nkv * mc;
+    const size_t kcb = rows * pb_tq_cw(pb_tq_bk(tq)) * 4, vcb = rows * pb_tq_cw(pb_tq_bv(tq)) * 4;
+    const size_t bytes = kcb + vcb + 2 * rows * 4 + (size_t)2 * g_h.nkv * 128 * 2;
+    if (cudaMalloc(&S.tq_mem, bytes) != cudaSuccess || cudaMemset(S.tq_mem, 0, bytes) != cudaSuccess) {
+      cudaGetLastError();
+      if (S.tq_mem) cudaFree(S.tq_mem);
+      S.tq_mem = nullptr;
+      pb_set_error(PB_ENOMEM, "pq1 hooks: TurboQuant cache of %zu bytes", bytes);
+      return false;
+    }
+    char* p = S.tq_mem;
+    S.tqc.kc = reinterpret_cast<uint32_t*>(p); p += kcb;
+    S.tqc.vc = reinterpret_cast<uint32_t*>(p); p += vcb;
+    S.tqc.ks = reinterpret_cast<float*>(p); p += rows * 4;
+    S.tqc.vs = reinterpret_cast<float*>(p); p += rows * 4;
+    S.stage = reinterpret_cast<uint16_t*>(p);
+    S.tq = tq;
+  } else {
+    const size_t bytes = (size_t)g_h.nl * 2 * g_h.nkv * mc * 128 * 2;
+    if (cudaMalloc(&S.kv, bytes) != cudaSuccess || cudaMemset(S.kv, 0, bytes) != cudaSuccess) {
+      cudaGetLastError();
+      if (S.kv) cudaFree(S.kv);
+      S.kv = nullptr;
+      pb_set_error(PB_ENOMEM, "pq1 hooks: K/V cache of %zu bytes", bytes);
+      return false;
+    }
   }
   S.nl = g_h.nl; S.nkv = g_h.nkv; S.mc = mc;
   return true;
@@ -189,6 +242,17 @@ uint16_t* kv_layer(HookSession& S, int il, int which) {
 // one layer's K and V rows of position pos ([n_kv][128] f16 each) into the
 // session's cache ([n_kv][mc][128] per layer, K and V)
 bool put_rows(HookSession& S, int il, int pos, const uint16_t* k16, const uint16_t* v16, cudaStream_t st) {
+  if (S.tq) {   // stage the rows, code them at pos (the glue's pq1_tq_store_launch)
+    const PbTqCache c = tq_layer(S, il);
+    if (cudaMemcpyAsync(S.stage, k16, (size_t)S.nkv * 256, cudaMemcpyHostToDevice, st) != cudaSuccess ||
+        cudaMemcpyAsync(S.stage + (size_t)S.nkv * 128, v16, (size_t)S.nkv * 256, cudaMemcpyHostToDevice, st) !=
+            cudaSuccess) {
+      cudaGetLastError();
+      pb_set_error(PB_ECUDA, "pq1 hooks: K/V rows");
+      return false;
+    }
+    return pb_tq_store_launch(S.tq, S.stage, nullptr, pos, c.kc, c.ks, c.vc, c.vs, S.nkv, S.mc, st, false) == PB_OK;
+  }
   for (int which = 0; which < 2; which++) {
     uint16_t* dst = kv_layer(S, il, which) + (size_t)pos * 128;
     if (cudaMemcpy2DAsync(dst, (size_t)S.mc * 128 * 2, which ? v16 : k16, 256, 256, (size_t)S.nkv,
@@ -302,7 +366,12 @@ int pq1_token_fused(int nl, const unsigned char* const* wt, const float* const* 
   for (int il = 0; il < nl; il++)
     if (S.next[il] != npos) return -1;         // a layer's cache lacks earlier positions
   if (!ensure_kv(S)) return -1;
-  if (!S.st && pb_bonsai_state_create_kv(g_h.m, S.mc, S.kv, &S.st) != PB_OK) { S.st = nullptr; return -1; }
+  if (S.tq && nh != 4 * nkv) return -1;   // the TurboQuant attention takes 4 query heads per KV head
+  if (!S.st) {
+    const int rc = S.tq ? pb_bonsai_state_create_tq_ext(g_h.m, S.mc, S.tq, &S.tqc, &S.st)
+                        : pb_bonsai_state_create_kv(g_h.m, S.mc, S.kv, &S.st);
+    if (rc != PB_OK) { S.st = nullptr; return -1; }
+  }
   if (!g_h.d_x && cudaMalloc(&g_h.d_x, (size_t)8192 * 4) != cudaSuccess) {
     cudaGetLastError();
     g_h.d_x = nullptr;
@@ -369,8 +438,16 @@ int pq1_attn_fused(int il, const unsigned char* wq, const unsigned char* wk, con
   const float* dq = to ? hnorm_of(qnw) : nullptr;
   const float* dk = dq ? hnorm_of(knw) : nullptr;
   if (!dk) return -1;
-  if (pb_bs_attn_block(g_h.blk, tq, tk, tv, to, dq, dk, kv_layer(S, il, 0), kv_layer(S, il, 1), S.mc, npos,
-                       kAttnScale, rcc, rcs, xq, ao, g_h.stream) != PB_OK) {
+  int rc;
+  if (S.tq) {
+    if (nh != 4 * nkv) return -1;
+    const PbTqCache c = tq_layer(S, il);
+    rc = pb_bs_attn_block_tq(g_h.blk, S.tq, tq, tk, tv, to, dq, dk, &c, S.mc, npos, rcc, rcs, xq, ao, g_h.stream);
+  } else {
+    rc = pb_bs_attn_block(g_h.blk, tq, tk, tv, to, dq, dk, kv_layer(S, il, 0), kv_layer(S, il, 1), S.mc, npos,
+                          kAttnScale, rcc, rcs, xq, ao, g_h.stream);
+  }
+  if (rc != PB_OK) {
     cudaGetLastError();
     return -1;
   }
@@ -404,7 +481,8 @@ void pq1_attn_dbg(int il, int npos, uint16_t* k16, uint16_t* v16, float* q, floa
   std::lock_guard<std::mutex> lk(g_h.mu);
   if (g_h.sess.empty() || g_h.cur >= (int)g_h.sess.size()) return;
   HookSession& S = g_h.sess[g_h.cur];
-  if (!S.kv || il < 0 || il >= S.nl || npos < 0 || npos >= S.mc) return;
+  // no f16 rows under TurboQuant (the glue returns nothing there either)
+  if (!S.kv || S.tq || il < 0 || il >= S.nl || npos < 0 || npos >= S.mc) return;
   const size_t pitch = (size_t)S.mc * 128 * 2;
   if (k16) cudaMemcpy2D(k16, 256, kv_layer(S, il, 0) + (size_t)npos * 128, pitch, 256, S.nkv, cudaMemcpyDeviceToHost);
   if (v16) cudaMemcpy2D(v16, 256, kv_layer(S, il, 1) + (size_t)npos * 128, pitch, 256, S.nkv, cudaMemcpyDeviceToHost);
@@ -448,6 +526,7 @@ int pb_pq1_hooks_reset(void) {
   for (auto& s : g_h.sess) {
     pb_bonsai_state_destroy(s.st);
     if (s.kv) cudaFree(s.kv);
+    if (s.tq_mem) cudaFree(s.tq_mem);
   }
   g_h.sess.clear();
   for (auto& e : g_h.q1) pb_q1_free(e.second.t);

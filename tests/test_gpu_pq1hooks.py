@@ -27,7 +27,11 @@ def _embed_row(blocks):
     return np.where(bits, sc[:, None], -sc[:, None]).reshape(-1).astype(np.float32)
 
 
-def test_pq1_token_fused_sessions(oracle, pb, cuda):
+@pytest.mark.parametrize("kvtq", [0, 4])
+def test_pq1_token_fused_sessions(oracle, pb, cuda, monkeypatch, kvtq):
+    """PQ1_KVTQ=0: the f16 cache; 4: the TurboQuant cache (the reference's
+    default), the host-run first token's rows coded by pq1_attn_kv_put"""
+    monkeypatch.setenv("PQ1_KVTQ", str(kvtq))
     from pulsar_b200 import synth
     c = dict(synth.BONSAI_TINY)
     w = synth.make_bonsai_weights(c, seed=31)
@@ -81,7 +85,7 @@ def test_pq1_token_fused_sessions(oracle, pb, cuda):
     assert step(5, 0, head)[0] == -1
     L.pq1_kv_shape(nl, NKV, ctx)
     assert L.pq1_sess_init(2) == 0
-    oms = [oracle.BsModel(c, w, ctx), oracle.BsModel(c, w, ctx)]
+    oms = [oracle.BsModel(c, w, ctx, kv_bits=kvtq), oracle.BsModel(c, w, ctx, kv_bits=kvtq)]
     rng = np.random.default_rng(8)
     toks = [rng.integers(0, V, 16), rng.integers(0, V, 16)]
     nxt = [0, 0]
@@ -141,13 +145,17 @@ def _f16(a):
     return np.ascontiguousarray(a, np.float32).astype(np.float16).view(np.uint16)
 
 
-def test_pq1_layer_hooks(oracle, pb, cuda):
+@pytest.mark.parametrize("kvtq", [0, 4])
+def test_pq1_layer_hooks(oracle, pb, cuda, monkeypatch, kvtq):
     """fwd8.c's per-layer flow (fwd8.c:812-883): host RMS norm and Q8_K, then
     pq1_attn_fused and pq1_ffn_fused per layer (the first token's attention
     on the host with its rows mirrored, as fwd8 runs it), each output and the
     PQ1_ATT_CHECK / PQ1_FFN_CHECK debug values bit for bit against the
     oracle's restatement of attn_cpu and the FFN tail; then pq1_token_fused
-    continues the same cache."""
+    continues the same cache. PQ1_KVTQ=0: the f16 cache; 4: the TurboQuant
+    cache (rows coded at their store, attention over the codes; no f16 rows
+    for pq1_attn_dbg, as in the reference)."""
+    monkeypatch.setenv("PQ1_KVTQ", str(kvtq))
     from pulsar_b200 import synth
     c = dict(synth.BONSAI_TINY)
     w = synth.make_bonsai_weights(c, seed=47)
@@ -189,8 +197,17 @@ def test_pq1_layer_hooks(oracle, pb, cuda):
         qf, kf = oracle.bs_rope(qf, rc_, rs_), oracle.bs_rope(kf, rc_, rs_)
         kr, vr = _f16(kf).reshape(NKV, 128), _f16(vf).reshape(NKV, 128)
         kc[il][:, pos], vc[il][:, pos] = kr, vr
-        at = np.concatenate([oracle.bs_fa16_head(qf[h * 128:(h + 1) * 128], kc[il][h // G, :pos + 1],
-                                                 vc[il][h // G, :pos + 1]) for h in range(NH)])
+        if kvtq:
+            tkc, tks = oracle.tq_rows(kc[il][:, :pos + 1].reshape(-1, 128), kvtq)
+            tvc, tvs = oracle.tq_rows(vc[il][:, :pos + 1].reshape(-1, 128), kvtq)
+            tkc, tvc = tkc.reshape(NKV, pos + 1, -1), tvc.reshape(NKV, pos + 1, -1)
+            tks, tvs = tks.reshape(NKV, pos + 1), tvs.reshape(NKV, pos + 1)
+            at = np.concatenate([oracle.tq_attn(qf[kh * 512:(kh + 1) * 512].reshape(4, 128), kvtq, kvtq, tkc[kh],
+                                                tks[kh], tvc[kh], tvs[kh], pos + 1).reshape(-1)
+                                 for kh in range(NKV)])
+        else:
+            at = np.concatenate([oracle.bs_fa16_head(qf[h * 128:(h + 1) * 128], kc[il][h // G, :pos + 1],
+                                                     vc[il][h // G, :pos + 1]) for h in range(NH)])
         ao = _q1_ref(d["o"], H, QD, oracle.q8k_quant(at), oracle)
         if not on_device:
             assert L.pq1_attn_kv_put(il, nl, NKV, ctx, pos, np.ascontiguousarray(kr).ctypes.data,
@@ -202,6 +219,8 @@ def test_pq1_layer_hooks(oracle, pb, cuda):
                                 rc_.ctypes.data, rs_.ctypes.data, xq.ctypes.data, got.ctypes.data) == 0, \
             pb.last_error()
         assert np.array_equal(_bits(got), _bits(ao)), "attention output, layer %d position %d" % (il, pos)
+        if kvtq:
+            return got
         kd, vd = np.zeros((NKV, 128), np.uint16), np.zeros((NKV, 128), np.uint16)
         qd, od = np.zeros(QD, np.float32), np.zeros(QD, np.float32)
         L.pq1_attn_dbg(il, pos, kd.ctypes.data, vd.ctypes.data, qd.ctypes.data, od.ctypes.data, NH)
@@ -253,10 +272,11 @@ def test_pq1_layer_hooks(oracle, pb, cuda):
             x = x + attn(il, x, pos, rc_, rs_, on_device=pos > 0)
             x = x + ffn(il, x)
     # the whole-token hook continues the cache the per-layer hooks wrote
-    om = oracle.BsModel(c, w, ctx)
+    om = oracle.BsModel(c, w, ctx, kv_bits=kvtq)
     for il in range(nl):
         om.set_kv(il, 0, kc[il])
         om.set_kv(il, 1, vc[il])
+    om.tq_recode(npos_layer)
     wt = (vp * (7 * nl + 1))()
     nw = (vp * (4 * nl + 1))()
     for il, d in enumerate(lw):
