@@ -260,6 +260,33 @@ int pbref_gpu_q8_gemv(const int8_t* q, const float* s, const uint16_t* x, uint16
   int rc = down((bf16*)y, dy, N);
   cudaFree(dq); cudaFree(ds); cudaFree(dx); cudaFree(dp); cudaFree(dy); return rc;
 }
+/* mean microseconds of pbref_gpu_q8_gemv's two launches over `reps` calls,
+   cycling over `ncopy` device copies of the tensor (together larger than L2),
+   CUDA events after one warm pass */
+float pbref_gpu_q8_gemv_time(const int8_t* q, const float* s, int N, int K, int ncopy, int reps) {
+  const int KC = (K >= 2048 && K % 2048 == 0) ? 2048 : K, nch = K / KC, R = N >= 1024 ? 256 : 64;
+  const size_t nq = (size_t)N * K, nsc = (size_t)N * (K / 32);
+  int8_t* dq = up((const int8_t*)nullptr, nq * ncopy); float* ds = up((const float*)nullptr, nsc * ncopy);
+  for (int c = 0; c < ncopy; c++) { cudaMemcpy(dq + nq * c, q, nq, cudaMemcpyHostToDevice); cudaMemcpy(ds + nsc * c, s, nsc * 4, cudaMemcpyHostToDevice); }
+  bf16* dx = up((const bf16*)nullptr, K); float* dp = up((const float*)nullptr, (size_t)N * nch);
+  bf16* dy = up((const bf16*)nullptr, N);
+  cudaMemset(dx, 0, (size_t)K * 2);
+  const size_t shm = (size_t)(KC / 32) * 33 * sizeof(float);
+  cudaFuncSetAttribute(q8_partial<bf16, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)shm);
+  auto run = [&](int c) {
+    q8_partial<bf16, true><<<((N + R - 1) / R) * nch, 256, shm>>>(dq + nq * c, ds + nsc * c, dx, dp, N, K, KC, R, KC / 32);
+    k_combine_bf<<<(N + 255) / 256, 256>>>(dp, dy, N, nch);
+  };
+  for (int c = 0; c < ncopy; c++) run(c);
+  cudaEvent_t e0, e1; cudaEventCreate(&e0); cudaEventCreate(&e1);
+  cudaEventRecord(e0);
+  for (int r = 0; r < reps; r++) for (int c = 0; c < ncopy; c++) run(c);
+  cudaEventRecord(e1); cudaEventSynchronize(e1);
+  float ms = 0.f; cudaEventElapsedTime(&ms, e0, e1);
+  const int ok = cudaGetLastError() == cudaSuccess;
+  cudaFree(dq); cudaFree(ds); cudaFree(dx); cudaFree(dp); cudaFree(dy); cudaEventDestroy(e0); cudaEventDestroy(e1);
+  return ok ? ms * 1e3f / (reps * ncopy) : -1.0f;
+}
 /* logits = lm_head_bf16: k_bf2f of x, k_gemv_bf16 with R = 32 rows per block */
 int pbref_gpu_gemv_bf16(const uint16_t* w, const uint16_t* x, float* y, int N, int K) {
   bf16* dw = up((const bf16*)w, (size_t)N * K); bf16* dx = up((const bf16*)x, K);
