@@ -148,6 +148,14 @@ int pb_close(pb_model* m);
 int pb_model_get_info(const pb_model* m, pb_model_info* info);
 /* index of a tensor by its blob name, or PB_EINVAL */
 int pb_tensor_id(const pb_model* m, const char* name);
+/* gemv(model, name, x, y) for a model holding Q4 / Q5 records (blob dtypes 6
+ * / 7, lfm3_nanode.cu:1494-1501): pb_open then loads every 2-D Q8 / Q4 / Q5
+ * matrix by itself (no fused decode arena; pb_state_create returns
+ * PB_ENOTSUP), and this dispatches one by dtype as the reference's gemv()
+ * does (lfm3_nanode.cu:1916-1922): y (bf16 [N]) = W x (x bf16 [K], 16-byte
+ * aligned). PB_ENOTSUP for an all-Q8 model (its projections are fused for
+ * the decode entry points). */
+int pb_model_gemv(pb_model* m, int tensor_id, const uint16_t* d_x, uint16_t* d_y, void* stream);
 /* KV cache (fp16, [layer][max_ctx][n_kv][head_dim]) and conv rings, zeroed */
 int pb_state_create(pb_model* m, int max_ctx, pb_state** out);
 int pb_state_destroy(pb_state* s);

@@ -375,6 +375,13 @@ struct Tensor {
 
 struct pb_model {
   int device = 0;
+  // per-tensor mode (a model holding Q4 / Q5 records, blob dtypes 6 / 7): every
+  // 2-D Q8 / Q4 / Q5 tensor on the device by itself for pb_model_gemv, as the
+  // reference's gemv() dispatches by record (lfm3_nanode.cu:1916-1922); the
+  // fused decode paths decline such a model
+  bool per_tensor = false;
+  std::vector<pb_q8*> pt_q8;      // [tensor id], null where not a Q8 record
+  std::vector<pb_qlow*> pt_qlow;  // [tensor id], null where not a Q4 / Q5 record
   int H = 0, F = 0, L = 0, NH = 0, NKV = 0, HD = 0, V = 0, W = 3, n_attn = 0, win = 0;
   float theta = 1e6f, partial = 1.0f, eps = 1e-5f;
   // sliding-attention layers (lfm3_nanode.cu:3753-3785, :5402-5420): their
@@ -1316,6 +1323,12 @@ extern "C" int pb_open(const char* path, int device, pb_model** out) {
       if (t.ne.size() != 2 || t.ne[0] <= 0 || t.ne[1] <= 0 || t.ne[1] % 256 ||
           t.nc != (size_t)t.ne[0] * t.ne[1] * 2 || t.ns != 0)
         return bad(PB_EFORMAT, ("bf16 tensor with inconsistent sizes: " + t.name).c_str());
+    } else if (t.dtype == 6 || t.dtype == 7) {
+      // low-bit Q4 / Q5 payload, pre-tiled by the exporter (lfm3_nanode.cu:1494-1501)
+      if (t.ne.size() != 2 || t.ne[0] <= 0 || t.ne[1] <= 0 || t.ne[0] % 32 || t.ne[1] % 256 ||
+          t.nc != (size_t)t.ne[0] * t.ne[1] / 32 * (t.dtype == 6 ? 16 : 20) ||
+          t.ns != (size_t)t.ne[0] * t.ne[1] / 32 * 4)
+        return bad(PB_EFORMAT, ("bad low-bit record: " + t.name).c_str());
     } else {
       return bad(PB_ENOTSUP, ("tensor dtype not supported by this build: " + t.name).c_str());
     }
@@ -1344,6 +1357,51 @@ extern "C" int pb_open(const char* path, int device, pb_model** out) {
     else m->layers[L].conv_idx = n_conv++;
   }
   m->n_attn = n_attn;
+  bool lowbit = false;
+  for (auto& t : m->table) lowbit = lowbit || t.dtype == 6 || t.dtype == 7;
+  if (lowbit) {   // per-tensor mode: every projection on the device by itself
+    m->per_tensor = true;
+    m->decode_ok = false;
+    std::vector<char> buf;
+    auto read_tensor = [&](const Tensor& t) -> int {
+      buf.resize(t.nc + t.ns);
+      if (fseeko(f, (off_t)(base + t.off), SEEK_SET) != 0 || read_all(f, buf.data(), buf.size()))
+        return pb_set_error(PB_EIO, "pb_open: short read in %s", t.name.c_str());
+      const uint32_t c = (uint32_t)crc32(0L, reinterpret_cast<const Bytef*>(buf.data()), (uInt)buf.size());
+      if (c != t.crc) return pb_set_error(PB_ECRC, "pb_open: CRC mismatch in %s", t.name.c_str());
+      return PB_OK;
+    };
+    int rc = PB_OK;
+    if (device < 0) {   // validate only
+      for (auto& t : m->table)
+        if ((rc = read_tensor(t)) != PB_OK) break;
+      fclose(f);
+      delete m;
+      return rc;
+    }
+    if (cudaSetDevice(device) != cudaSuccess) {
+      cudaGetLastError();
+      return bad(PB_ECUDA, "cudaSetDevice failed");
+    }
+    m->pt_q8.assign(m->table.size(), nullptr);
+    m->pt_qlow.assign(m->table.size(), nullptr);
+    for (size_t i = 0; rc == PB_OK && i < m->table.size(); i++) {
+      const Tensor& t = m->table[i];
+      if (t.dtype != 1 && t.dtype != 8 && t.dtype != 6 && t.dtype != 7) continue;
+      if ((rc = read_tensor(t)) != PB_OK) break;
+      const int N = (int)t.ne[0], K = (int)t.ne[1];
+      if (t.dtype == 6 || t.dtype == 7)
+        rc = pb_qlow_pack(buf.data(), buf.data() + t.nc, t.dtype == 6 ? 4 : 5, N, K, 0, nullptr, &m->pt_qlow[i]);
+      else
+        rc = pb_q8_pack(reinterpret_cast<const int8_t*>(buf.data()), buf.data() + t.nc,
+                        t.dtype == 1 ? PB_DT_F32 : PB_DT_F16, N, K, 0, nullptr, &m->pt_q8[i]);
+      m->weight_bytes += t.nc + t.ns;
+    }
+    fclose(f);
+    if (rc != PB_OK) { pb_close(m); return rc; }
+    *out = m;
+    return PB_OK;
+  }
   // arena plan
   struct Piece { std::string name; pb_q8* dst; int rmul, radd; };
   std::vector<Piece> q8pieces;
@@ -1536,6 +1594,8 @@ extern "C" int pb_open(const char* path, int device, pb_model** out) {
 
 extern "C" int pb_close(pb_model* m) {
   if (!m) return PB_OK;
+  for (auto* q : m->pt_q8) pb_q8_free(q);
+  for (auto* q : m->pt_qlow) pb_qlow_free(q);
   cudaFree(m->arena);
   cudaFree(m->tc_arena);
   delete m;
@@ -1559,9 +1619,23 @@ extern "C" int pb_tensor_id(const pb_model* m, const char* name) {
   return pb_set_error(PB_EINVAL, "pb_tensor_id: no tensor %s", name);
 }
 
+extern "C" int pb_model_gemv(pb_model* m, int tensor_id, const uint16_t* d_x, uint16_t* d_y, void* stream) {
+  if (!m || !d_x || !d_y) return pb_set_error(PB_EINVAL, "pb_model_gemv: null argument");
+  if (!m->per_tensor)
+    return pb_set_error(PB_ENOTSUP, "pb_model_gemv: the model's projections are fused for decoding "
+                                    "(per-tensor GEMVs are for models holding Q4 / Q5 records)");
+  if (tensor_id < 0 || tensor_id >= (int)m->table.size())
+    return pb_set_error(PB_EINVAL, "pb_model_gemv: tensor id %d", tensor_id);
+  PB_TRY_CUDA(cudaSetDevice(m->device));
+  if (m->pt_qlow[tensor_id]) return pb_qlow_gemv(m->pt_qlow[tensor_id], d_x, d_y, stream);
+  if (m->pt_q8[tensor_id]) return pb_q8_gemv(m->pt_q8[tensor_id], d_x, d_y, PB_DT_BF16, stream);
+  return pb_set_error(PB_EINVAL, "pb_model_gemv: %s is not a Q8 / Q4 / Q5 matrix", m->table[tensor_id].name.c_str());
+}
+
 extern "C" int pb_state_create(pb_model* m, int max_ctx, pb_state** out) {
   if (!m || !out || max_ctx <= 0) return pb_set_error(PB_EINVAL, "pb_state_create: bad argument");
   *out = nullptr;
+  if (m->per_tensor) return pb_set_error(PB_ENOTSUP, "pb_state_create: a model holding Q4 / Q5 records runs per-tensor GEMVs only (pb_model_gemv)");
   if (!m->decode_ok) return pb_set_error(PB_ENOTSUP, "decode needs every matrix in the streaming layout (K up to 16384)");
   if ((size_t)max_ctx * 4 > 160 * 1024) return pb_set_error(PB_ENOTSUP, "max_ctx %d too large", max_ctx);
   PB_TRY_CUDA(cudaSetDevice(m->device));

@@ -99,6 +99,7 @@ def lib():
     L.pb_close.argtypes = [vp]
     L.pb_model_get_info.argtypes = [vp, C.POINTER(_Info)]
     L.pb_tensor_id.argtypes = [vp, C.c_char_p]
+    L.pb_model_gemv.argtypes = [vp, i, vp, vp, vp]
     L.pb_state_create.argtypes = [vp, i, pvp]
     L.pb_state_destroy.argtypes = [vp]
     L.pb_state_reset.argtypes = [vp, vp]
@@ -386,6 +387,11 @@ class Model:
         if r < 0:
             raise PBError(r, last_error())
         return r
+
+    def gemv(self, name, x, y, stream=None):
+        """y (bf16 bits [N]) = the named matrix x (bf16 bits [K]); models holding
+        Q4 / Q5 records (pb_model_gemv)"""
+        check(lib().pb_model_gemv(self.h, self.tensor_id(name), _ptr(x), _ptr(y), _stream(stream)))
 
     def decode_batch(self, states, tokens, pos, ids, logits=None, stream=None):
         """one integer-path decode step of len(states) sequences: device int32

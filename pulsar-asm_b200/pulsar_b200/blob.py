@@ -20,12 +20,13 @@ import zlib
 import numpy as np
 
 MAGIC = b"LFM3Q8\x01\x00"
-T_Q8_F32S, T_F32, T_BF16, T_Q8_F16S = 1, 2, 3, 8
+T_Q8_F32S, T_F32, T_BF16, T_Q4, T_Q5, T_Q8_F16S = 1, 2, 3, 6, 7, 8
 
 
 def write_blob(path, cfg, tensors):
     """tensors: list of (name, kind, payload) with kind "q8" -> (codes int8 [N,K],
-    scales fp16/fp32 [N,K/32]), "bf16" -> uint16 bf16 bits, or "f32" -> ndarray."""
+    scales fp16/fp32 [N,K/32]), "bf16" -> uint16 bf16 bits, "q4" / "q5" ->
+    ((N, K), tiled codes uint8, half2 scales as uint16), or "f32" -> ndarray."""
     table, blobs, off = [], [], 0
     for name, kind, payload in tensors:
         if kind == "q8":
@@ -52,6 +53,16 @@ def write_blob(path, cfg, tensors):
                               nscales=0, crc=zlib.crc32(b) & 0xFFFFFFFF))
             blobs.append(b)
             off += len(b)
+        elif kind in ("q4", "q5"):
+            # the low-bit records (lfm3_nanode.cu:1494-1501): the exporter's
+            # tiled codes, then the half2 (128 d, mn) scales; ne = [N, K]
+            (N, K), codes, scales = payload
+            cb = np.ascontiguousarray(codes, np.uint8).tobytes()
+            sb = np.ascontiguousarray(scales, np.uint16).tobytes()
+            table.append(dict(name=name, dtype=T_Q4 if kind == "q4" else T_Q5, ne=[int(N), int(K)], off=off,
+                              ncodes=len(cb), nscales=len(sb), crc=zlib.crc32(sb, zlib.crc32(cb)) & 0xFFFFFFFF))
+            blobs += [cb, sb]
+            off += len(cb) + len(sb)
         elif kind == "f32":
             a = np.ascontiguousarray(payload, np.float32)
             b = a.tobytes()

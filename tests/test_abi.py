@@ -125,3 +125,40 @@ def test_shim_host_silu_mul(pb):
     f = np.float32
     want = np.array([f(f(gi * f(f(1.0) / f(f(1.0) + f(libm.expf(f(-gi)))))) * ui) for gi, ui in zip(g, u)], np.float32)
     assert np.array_equal(out.view(np.uint32), want.view(np.uint32))
+
+
+def _lowbit_blob(tmp_path, corrupt=None):
+    """a model holding Q4 / Q5 records next to a Q8 one (the speech server's
+    low-bit backbone, lfm3_nanode.cu:1494-1501)"""
+    from pulsar_b200 import synth
+    c = dict(synth.LFM3_TINY)
+    rng = np.random.default_rng(3)
+    q4c, q4s = synth.qlow_payload(rng, 256, 512, 4)
+    q5c, q5s = synth.qlow_payload(rng, 64, 256, 5)
+    if corrupt == "size":
+        q5s = q5s[:-2]
+    q8 = (rng.integers(-127, 128, (128, 256), dtype=np.int8), (rng.random((128, 8)) * 0.01).astype(np.float32))
+    tensors = [("lfm.model.layers.0.feed_forward.w1.weight", "q4", ((256, 512), q4c, q4s)),
+               ("lfm.model.layers.0.feed_forward.w2.weight", "q5", ((64, 256), q5c, q5s)),
+               ("lfm.model.layers.0.conv.out_proj.weight", "q8", q8),
+               ("lfm.model.embedding_norm.weight", "f32", np.ones(c["hidden"], np.float32))]
+    return tensors
+
+
+def test_lowbit_records(pb, tmp_path):
+    """pb_open takes Q4 / Q5 records (the reference's record checks) into its
+    per-tensor mode; a record with inconsistent sizes is a format error, a
+    corrupt payload a CRC error"""
+    from pulsar_b200 import blob, synth
+    c = dict(synth.LFM3_TINY)
+    cfg = synth.hf_cfg(c)
+    path = str(tmp_path / "low.lfm3q8")
+    blob.write_blob(path, cfg, _lowbit_blob(tmp_path))
+    assert _open_validate(pb, path) == 0
+    bad = str(tmp_path / "bad.lfm3q8")
+    blob.write_blob(bad, cfg, _lowbit_blob(tmp_path, corrupt="size"))
+    assert _open_validate(pb, bad) == -6          # PB_EFORMAT
+    raw = bytearray(open(path, "rb").read())
+    raw[-40] ^= 0xFF
+    open(bad, "wb").write(bytes(raw))
+    assert _open_validate(pb, bad) == -5          # PB_ECRC

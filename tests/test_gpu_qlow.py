@@ -60,3 +60,43 @@ def test_qlow_rejects_overlap_and_bad_shapes(pb, cuda):
         pb.QlowTensor(codes, scales, 4, 250, 256)   # N not a multiple of 32
     with pytest.raises(pb.PBError):
         pb.QlowTensor(codes, scales, 6, 256, 256)   # 4 or 5 bits only
+
+
+def test_model_with_lowbit_records(oracle, pb, cuda, tmp_path):
+    """a model holding Q4 / Q5 records loads in per-tensor mode: pb_model_gemv
+    dispatches each named matrix by its record (the reference's gemv(),
+    lfm3_nanode.cu:1916-1922), bit for bit; the fused decode declines it"""
+    torch = cuda
+    import importlib.util
+    import os
+    from conftest import ROOT
+    from pulsar_b200 import blob, synth
+    spec = importlib.util.spec_from_file_location("t_abi", os.path.join(ROOT, "tests", "test_abi.py"))
+    t_abi = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(t_abi)
+    tensors = t_abi._lowbit_blob(tmp_path)
+    path = str(tmp_path / "low.lfm3q8")
+    blob.write_blob(path, synth.hf_cfg(dict(synth.LFM3_TINY)), tensors)
+    m = pb.Model(path)
+    rng = np.random.default_rng(5)
+    for name, kind, payload in tensors:
+        if kind == "f32":
+            continue
+        if kind == "q8":
+            N, K = payload[0].shape
+        else:
+            N, K = payload[0]
+        xf = rng.standard_normal(K).astype(np.float32)
+        u = xf.view(np.uint32)
+        x = ((u + np.uint32(0x7FFF) + ((u >> 16) & 1)) >> 16).astype(np.uint16)
+        y = torch.empty(N, dtype=torch.int16, device="cuda")
+        m.gemv(name, torch.from_numpy(x.view(np.int16)).cuda(), y)
+        torch.cuda.synchronize()
+        got = y.cpu().numpy().view(np.uint16)
+        if kind == "q8":
+            want = oracle.f2bf(oracle.q8f_gemv(payload[0], payload[1], x))
+        else:
+            want = oracle.qlow_gemv(payload[1], payload[2], 4 if kind == "q4" else 5, N, K, x)
+        assert np.array_equal(got, want), name
+    with pytest.raises(pb.PBError):
+        m.new_state(64)
