@@ -515,12 +515,34 @@ def batch_bench(torch, model, c, stream, B=64, steps=10):
             tokens.copy_(ids)
         e1.record(stream)
         e1.synchronize()
+        ms = e0.elapsed_time(e1)
+        # the same steps with each sequence's next id drawn on the device by
+        # fwd8.c's sampler (temperature 0.7, top-p 0.9, top-k 40, one LCG state
+        # per sequence) from the step's logits, instead of the greedy id
+        import pulsar_b200 as pbm
+        logits = torch.empty((B, c["vocab"]), dtype=torch.float32, device="cuda")
+        rs = torch.arange(1, B + 1, dtype=torch.int64, device="cuda") * 7919
+        marks = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(steps)]
+        e2 = torch.cuda.Event(enable_timing=True)
+        e2.record(stream)
+        for k in range(steps):
+            model.decode_batch(states, tokens, pos, ids, logits, stream=stream)
+            marks[k][0].record(stream)
+            pbm.sample_topkpp(logits, 0.7, 0.9, 40, 0.0, rs, tokens, stream=stream)
+            marks[k][1].record(stream)
+            pos += 1
+        marks[-1][1].synchronize()
+        ms_sampled = e2.elapsed_time(marks[-1][1])
+        ms_sample = sum(a.elapsed_time(b) for a, b in marks)
     for st in states:
         st.status(stream)
         st.destroy()
-    ms = e0.elapsed_time(e1)
     return {"sequences": B, "steps": steps, "mean_ctx": float(ctx.mean()), "ms_per_step": ms / steps,
-            "tok/s": B * steps / (ms / 1e3), "path": "integer (Q8_0 activations, tcgen05 kind::i8 GEMMs, N = 64)"}
+            "tok/s": B * steps / (ms / 1e3), "path": "integer (Q8_0 activations, tcgen05 kind::i8 GEMMs, N = 64)",
+            "sampled": {"ms_per_step": ms_sampled / steps, "tok/s": B * steps / (ms_sampled / 1e3),
+                        "sampler_us_per_step": ms_sample * 1e3 / steps,
+                        "path": "logits [64][vocab] from the batched step, pb_sample_topkpp (fwd8.c:465-521) "
+                                "on the device"}}
 
 
 def bonsai_bench(torch, pb, peak, stream, steps=20, warmup=3, kv_bits=0):
