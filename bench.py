@@ -45,6 +45,9 @@ def parse():
     ap.add_argument("--blob", default=os.environ.get("PB_BENCH_BLOB", "/tmp/pb_cfg1.lfm3q8"))
     ap.add_argument("--phase-trace", action="store_true",
                     help="print the persistent decode kernel's per-phase time breakdown (one GPU) and exit")
+    ap.add_argument("--bonsai-only", type=int, default=-1, metavar="KV_BITS",
+                    help="profiling only: run just the cfg3 Bonsai decode (K/V cache 0 = f16, 3, 4, 43 = TurboQuant) "
+                         "for --warmup + --steps tokens, print its line and exit")
     ap.add_argument("--layers", type=int, default=0,
                     help="profiling only: a shallower model of the same shapes (0 = the 24-layer cfg1)")
     return ap.parse_args()
@@ -771,6 +774,13 @@ def main():
     dist.init(timeout_s=900)
     if not os.path.exists(pb.LIB_PATH):
         pb.build()
+    if args.bonsai_only >= 0:
+        if rank == 0:
+            peak, _ = measured_peaks()
+            print(json.dumps({"cfg3_decode": bonsai_bench(torch, pb, peak, torch.cuda.Stream(), steps=args.steps,
+                                                          warmup=args.warmup, kv_bits=args.bonsai_only)}))
+        dist.finish()
+        return
     c = bench_cfg(args.layers)
     blob = args.blob if not args.layers else args.blob.replace(".lfm3q8", "_L%d.lfm3q8" % args.layers)
     weights = None

@@ -236,6 +236,7 @@ __global__ void __launch_bounds__(128) k_tq_pv(const float* __restrict__ p, cons
                                                int T_h, const int* __restrict__ d_npos) {
   constexpr int CW = tq_cw(B), NV = 1 << B;
   __shared__ __align__(16) float4 wt[TQ_CH];
+  __shared__ __align__(16) uint32_t cs[TQ_CH * CW];   // the chunk's code words
   __shared__ float cent[NV];
   __shared__ __align__(16) float red[3][4][128];
   const int kh = blockIdx.x, c = blockIdx.y, tid = threadIdx.x, w = tid >> 5, l = tid & 31;
@@ -245,6 +246,10 @@ __global__ void __launch_bounds__(128) k_tq_pv(const float* __restrict__ p, cons
   const int t0 = c * TQ_CH, n = min(TQ_CH, T - t0);
   if (n <= 0) return;   // block-uniform
   if (tid < NV) cent[tid] = tq_cent(B, tid);
+  {   // every thread's 16-byte loads of the chunk's codes in flight at once
+    const uint4* src = reinterpret_cast<const uint4*>(vc + ((size_t)kh * ctx + t0) * CW);
+    for (int i = tid; i < n * CW / 4; i += 128) reinterpret_cast<uint4*>(cs)[i] = src[i];
+  }
   for (int t = tid; t < n; t += 128) {
     const float s = vs[(size_t)kh * ctx + t0 + t];
     const float* pp = p + (size_t)kh * 4 * ctx + t0 + t;
@@ -257,11 +262,10 @@ __global__ void __launch_bounds__(128) k_tq_pv(const float* __restrict__ p, cons
   for (int h = 0; h < 4; h++)
 #pragma unroll
     for (int i = 0; i < 4; i++) a[h][i] = 0.0f;
-  const uint32_t* vb = vc + ((size_t)kh * ctx + t0) * CW;
   const int wa = B == 3 ? l >> 2 : l >> 1, wb = 8 + (l >> 3);
 #pragma unroll 4
   for (int t = w; t < n; t += 4) {
-    const uint32_t* cw = vb + (size_t)t * CW;
+    const uint32_t* cw = cs + t * CW;
     int v[4];
     if (B == 3) {
       const uint32_t mb = cw[wa] >> (8 * (l & 3)), sb = cw[wb] >> (4 * (l & 7));
