@@ -90,10 +90,16 @@ __global__ void __launch_bounds__(ST) k_sample(SampleArgs a) {
   if (a.temp <= 0.0f) {   // greedy: the first maximum
     float bv = -INFINITY;
     int bi = -1;
-    for (int i = t; i < n; i += ST) {
-      const float v = lg[i];
-      if (v != v) nan = 1;
-      if (bi < 0 || v > bv) { bv = v; bi = i; }
+    for (int i0 = t; i0 < n; i0 += 8 * ST) {
+      float v[8];
+#pragma unroll
+      for (int u = 0; u < 8; u++) v[u] = i0 + u * ST < n ? lg[i0 + u * ST] : 0.0f;
+#pragma unroll
+      for (int u = 0; u < 8; u++) {   // increasing index: the first maximum stays
+        if (i0 + u * ST >= n) break;
+        if (v[u] != v[u]) nan = 1;
+        if (bi < 0 || v[u] > bv) { bv = v[u]; bi = i0 + u * ST; }
+      }
     }
 #pragma unroll
     for (int o = 16; o; o >>= 1) {
@@ -121,11 +127,18 @@ __global__ void __launch_bounds__(ST) k_sample(SampleArgs a) {
     const int shift = 24 - 8 * pass;
     if (t < 256) hist[t] = 0u;
     __syncthreads();
-    for (int i = t; i < n; i += ST) {
-      const float v = lg[i];
-      if (pass == 0 && v != v) nan = 1;
-      const uint32_t key = skey(v);
-      if ((key & mask) == prefix) atomicAdd(&hist[(key >> shift) & 255u], 1u);
+    // 8 loads issued before any is used: the row is read from L2 in flight
+    for (int i0 = t; i0 < n; i0 += 8 * ST) {
+      float v[8];
+#pragma unroll
+      for (int u = 0; u < 8; u++) v[u] = i0 + u * ST < n ? lg[i0 + u * ST] : 0.0f;
+#pragma unroll
+      for (int u = 0; u < 8; u++) {
+        if (i0 + u * ST >= n) break;
+        if (pass == 0 && v[u] != v[u]) nan = 1;
+        const uint32_t key = skey(v[u]);
+        if ((key & mask) == prefix) atomicAdd(&hist[(key >> shift) & 255u], 1u);
+      }
     }
     if (pass == 0) {
       nan = __syncthreads_or(nan);
@@ -136,14 +149,35 @@ __global__ void __launch_bounds__(ST) k_sample(SampleArgs a) {
     } else {
       __syncthreads();
     }
-    if (t == 0) {
-      int cum = 0, d = 255;
-      for (; d > 0; d--) {
-        if (cum + (int)hist[d] >= rem) break;
-        cum += (int)hist[d];
+    // the highest bin d whose count, with every bin above it, reaches rem
+    // (bin 0 when none does): warp 0, lane l holding bins 255-8l down to
+    // 248-8l, scans the lanes' sums, and the first lane to reach rem walks
+    // its own eight bins
+    if (w == 0) {
+      int c8[8], sum = 0;
+#pragma unroll
+      for (int j = 0; j < 8; j++) {
+        c8[j] = (int)hist[255 - 8 * lane - j];
+        sum += c8[j];
       }
-      s_prefix = prefix | ((uint32_t)d << shift);
-      s_rem = rem - cum;
+      int inc = sum;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const int up = __shfl_up_sync(0xffffffffu, inc, o);
+        if (lane >= o) inc += up;
+      }
+      const unsigned hit = __ballot_sync(0xffffffffu, inc >= rem);
+      if (lane == (hit ? __ffs(hit) - 1 : 31)) {
+        int cum = inc - sum, d = 255 - 8 * lane;
+#pragma unroll
+        for (int j = 0; j < 8; j++) {
+          if (d == 0 || cum + c8[j] >= rem) break;
+          cum += c8[j];
+          d--;
+        }
+        s_prefix = prefix | ((uint32_t)d << shift);
+        s_rem = rem - cum;
+      }
     }
     __syncthreads();
     prefix = s_prefix;
@@ -151,33 +185,72 @@ __global__ void __launch_bounds__(ST) k_sample(SampleArgs a) {
     mask |= 0xFFu << shift;
   }
   // 2. compaction: keys above T anywhere, the first `rem` keys equal to T in
-  // index order (each thread walks a contiguous run of indices)
+  // index order. Warp w walks the contiguous segment [w S, (w + 1) S) in
+  // coalesced 32-key steps; ballots give each key its place among the warp's
+  // keys, a block scan of the warps' counts places the segments
   const uint32_t T = prefix;
-  const int C = (n + ST - 1) / ST, i0 = t * C, i1 = min(n, i0 + C);
+  const int S = (n + 32 * 32 - 1) / (32 * 32) * 32;
+  const int s0 = w * S, s1 = min(n, s0 + S);
+  const unsigned lt = (1u << lane) - 1u;
   int ngt = 0, neq = 0;
-  for (int i = i0; i < i1; i++) {
-    const uint32_t key = skey(lg[i]);
-    ngt += key > T;
-    neq += key == T;
+  for (int j0 = s0; j0 < s1; j0 += 8 * 32) {
+    float v[8];
+#pragma unroll
+    for (int u = 0; u < 8; u++) {
+      const int i = j0 + u * 32 + lane;
+      v[u] = i < s1 ? lg[i] : 0.0f;
+    }
+#pragma unroll
+    for (int u = 0; u < 8; u++) {
+      const bool in = j0 + u * 32 + lane < s1;
+      const uint32_t key = skey(v[u]);
+      ngt += __popc(__ballot_sync(0xffffffffu, in && key > T));
+      neq += __popc(__ballot_sync(0xffffffffu, in && key == T));
+    }
   }
   int pgt, peq;
-  scan2(ngt, neq, pgt, peq, ws);
+  scan2(lane ? 0 : ngt, lane ? 0 : neq, pgt, peq, ws);
+  pgt = __shfl_sync(0xffffffffu, pgt, 0);
+  peq = __shfl_sync(0xffffffffu, peq, 0);
   const int base_eq = k - rem;   // the number of keys above T
-  for (int i = i0; i < i1; i++) {
-    const uint32_t key = skey(lg[i]);
-    const unsigned long long e = ((unsigned long long)key << 32) | (uint32_t)~(uint32_t)i;
-    // the counts make pgt < k - rem and base_eq + peq < k; the guards keep the
-    // writes inside the list whatever the input
-    if (key > T) { if (pgt < base_eq) cand[pgt] = e; pgt++; }
-    else if (key == T && peq < rem) { if (base_eq + peq < KMAX) cand[base_eq + peq] = e; peq++; }
+  for (int j0 = s0; j0 < s1; j0 += 8 * 32) {
+    float v[8];
+#pragma unroll
+    for (int u = 0; u < 8; u++) {
+      const int i = j0 + u * 32 + lane;
+      v[u] = i < s1 ? lg[i] : 0.0f;
+    }
+#pragma unroll
+    for (int u = 0; u < 8; u++) {
+      const int i = j0 + u * 32 + lane;
+      const uint32_t key = skey(v[u]);
+      const bool gt = i < s1 && key > T, eq = i < s1 && key == T;
+      const unsigned bg = __ballot_sync(0xffffffffu, gt), be = __ballot_sync(0xffffffffu, eq);
+      const unsigned long long e = ((unsigned long long)key << 32) | (uint32_t)~(uint32_t)i;
+      // the counts keep every place of a key above T below k - rem, and
+      // rem equal keys are taken; the guards keep the writes inside the list
+      // whatever the input
+      if (gt) {
+        const int p = pgt + __popc(bg & lt);
+        if (p < base_eq) cand[p] = e;
+      }
+      if (eq) {
+        const int p = peq + __popc(be & lt);
+        if (p < rem && base_eq + p < KMAX) cand[base_eq + p] = e;
+      }
+      pgt += __popc(bg);
+      peq += __popc(be);
+    }
   }
   if (t >= k) cand[t] = 0ull;   // below every real entry (no key is 0 once NaN is excluded)
-  // 3. bitonic sort, descending
-  for (int size = 2; size <= KMAX; size <<= 1) {
+  // 3. bitonic sort, descending, of the first kp2 >= k entries (a power of two)
+  int kp2 = 2;
+  while (kp2 < k) kp2 <<= 1;
+  for (int size = 2; size <= kp2; size <<= 1) {
     for (int stride = size >> 1; stride > 0; stride >>= 1) {
       __syncthreads();
       const int j = t ^ stride;
-      if (j > t) {
+      if (t < kp2 && j > t) {
         const unsigned long long x = cand[t], y = cand[j];
         const bool desc = (t & size) == 0;
         if (desc ? (x < y) : (x > y)) { cand[t] = y; cand[j] = x; }
