@@ -2354,7 +2354,7 @@ extern "C" int pb_prefill_chunk(pb_model* m, pb_state* s, const int* d_tokens, i
     if ((rc = pb_q80_gemm(&m->tc.back(), T, s->pf_qx, s->pf_dx, lg, nullptr, st))) return rc;
   }
   if (d_ids) {
-    k_pf_argmax<<<T, 256, 0, st>>>(lg, m->V, d_ids);
+    k_pf_argmax<<<T, PF_AM_T, 0, st>>>(lg, m->V, d_ids);
     PB_LAUNCHED("k_pf_argmax");
   }
   return PB_OK;
@@ -2498,7 +2498,7 @@ extern "C" int pb_decode_batch(pb_model* m, pb_state* const* states, int B, cons
   } else if ((rc = pb_q80_gemm(&m->tc.back(), B, ws->pf_qx, ws->pf_dx, lg, nullptr, st))) {
     return rc;
   }
-  k_pf_argmax<<<B, 256, 0, st>>>(lg, m->V, d_ids);
+  k_pf_argmax<<<B, PF_AM_T, 0, st>>>(lg, m->V, d_ids);
   PB_LAUNCHED("k_pf_argmax");
   return PB_OK;
 }

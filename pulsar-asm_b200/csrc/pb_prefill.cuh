@@ -262,16 +262,30 @@ __global__ void __launch_bounds__(256) k_pf_silu_quant(const float* __restrict__
   pf_quant_store<E>(u, qx + (size_t)t * F, dx + (size_t)t * (F / 32), th);
 }
 
-// greedy id of each position's logits (ties to the lowest index)
-__global__ void __launch_bounds__(256) k_pf_argmax(const float* __restrict__ lg, int V, int* __restrict__ ids) {
-  __shared__ float bv[8];
-  __shared__ int bi[8];
+// greedy id of each position's logits (ties to the lowest index; a NaN is
+// never taken), one CTA per position. Each thread keeps 8 loads in flight:
+// the row is read from L2 at its latency once per 8 keys, not once per key.
+// The rule does not depend on the order keys are visited in.
+constexpr int PF_AM_T = 1024;
+__global__ void __launch_bounds__(PF_AM_T) k_pf_argmax(const float* __restrict__ lg, int V, int* __restrict__ ids) {
+  __shared__ float bv[PF_AM_T / 32];
+  __shared__ int bi[PF_AM_T / 32];
   const int t = blockIdx.x, lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const float* row = lg + (size_t)t * V;
   float b = -INFINITY;
   int ix = 0x7fffffff;
-  for (int i = threadIdx.x; i < V; i += blockDim.x) {
-    const float v = lg[(size_t)t * V + i];
-    if (v > b || (v == b && i < ix)) { b = v; ix = i; }
+  for (int base = 0; base < V; base += 8 * PF_AM_T) {
+    float v[8];
+#pragma unroll
+    for (int u = 0; u < 8; u++) {
+      const int i = base + u * PF_AM_T + threadIdx.x;
+      v[u] = i < V ? row[i] : 0.0f;
+    }
+#pragma unroll
+    for (int u = 0; u < 8; u++) {
+      const int i = base + u * PF_AM_T + threadIdx.x;
+      if (i < V && (v[u] > b || (v[u] == b && i < ix))) { b = v[u]; ix = i; }
+    }
   }
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) {
@@ -282,7 +296,7 @@ __global__ void __launch_bounds__(256) k_pf_argmax(const float* __restrict__ lg,
   if (lane == 0) { bv[warp] = b; bi[warp] = ix; }
   __syncthreads();
   if (threadIdx.x == 0) {
-    for (int w = 1; w < 8; w++)
+    for (int w = 1; w < PF_AM_T / 32; w++)
       if (bv[w] > bv[0] || (bv[w] == bv[0] && bi[w] < bi[0])) { bv[0] = bv[w]; bi[0] = bi[w]; }
     ids[t] = bi[0];
   }
